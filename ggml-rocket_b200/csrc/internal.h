@@ -1,0 +1,20 @@
+// Declarations shared between the backend's translation units (not part of the C ABI).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace b200 {
+
+int device_sm_count();
+bool make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+                      uint32_t box_rows, uint32_t box_cols);
+size_t packed_weight_bytes(int type, int64_t N, int64_t K, size_t* plane_d_off);
+bool weight_type_supported(int type, int64_t K);
+int mul_mat_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const float* src1, int64_t lda, int64_t M,
+                 float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t st);
+size_t mul_mat_workspace(int64_t M, int64_t N, int64_t K);
+
+}  // namespace b200

@@ -1,0 +1,459 @@
+// MUL_MAT on sm_100a: the activation pre-pass, the weight decode / re-layout kernels, the
+// tcgen05 GEMM launches (gemm.cuh) and the split-K reduction, behind the C ABI declared in
+// include/ggml-b200-kernels.h.
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "ggml-b200-kernels.h"
+#include "gemm.cuh"
+#include "internal.h"
+#include "ptx.cuh"
+#include "quant.cuh"
+
+namespace b200 {
+
+// ------------------------------------------------------------------------------------------
+// Activation "sandwich" pre-pass (the reference's rk_pack_act_row, ggml-rocket.cpp:1451-1475):
+// per row s = max|A[m,:]| (1 when 0), A16 = fp16(A * (1/s)). One warp per row.
+// ------------------------------------------------------------------------------------------
+__global__ void act_pack_kernel(const float* __restrict__ A, int64_t lda, int M, int K,
+                                __half* __restrict__ A16, float* __restrict__ scales) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= M) return;
+    const float* row = A + (size_t)warp * lda;
+    __half* out = A16 + (size_t)warp * K;
+    const bool vec = ((reinterpret_cast<uintptr_t>(row) & 15u) == 0) && (K % 4 == 0);
+    float amax = 0.0f;
+    if (vec) {
+        const float4* r4 = reinterpret_cast<const float4*>(row);
+        for (int i = lane; i < K / 4; i += 32) {
+            const float4 v = __ldg(r4 + i);
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+    } else {
+        for (int i = lane; i < K; i += 32) amax = fmaxf(amax, fabsf(__ldg(row + i)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float s = amax > 0.0f ? amax : 1.0f;
+    const float inv = __frcp_rn(s);
+    if (lane == 0) scales[warp] = s;
+    if (vec) {
+        const float4* r4 = reinterpret_cast<const float4*>(row);
+        uint2* o2 = reinterpret_cast<uint2*>(out);
+        for (int i = lane; i < K / 4; i += 32) {
+            const float4 v = __ldg(r4 + i);
+            uint2 w;
+            w.x = pack_half2(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv));
+            w.y = pack_half2(__fmul_rn(v.z, inv), __fmul_rn(v.w, inv));
+            o2[i] = w;
+        }
+    } else {
+        for (int i = lane; i < K; i += 32) out[i] = __float2half_rn(__fmul_rn(__ldg(row + i), inv));
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Split-K reduction: out[t, n] = s[t] * sum_s P[s][t, n].
+// ------------------------------------------------------------------------------------------
+__global__ void splitk_reduce_kernel(const float* __restrict__ P, int splits, int64_t split_stride,
+                                     const float* __restrict__ scales, float* __restrict__ out,
+                                     int64_t ldo, int M, int N) {
+    const int64_t total = (int64_t)M * N;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / N), n = (int)(i % N);
+        float acc = 0.0f;
+        for (int s = 0; s < splits; s++) acc += P[(size_t)s * split_stride + i];
+        out[(size_t)t * ldo + n] = acc * __ldg(scales + t);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Standalone dequant of native ggml rows (the K2d check kernel): one thread per element.
+// ------------------------------------------------------------------------------------------
+template <int WT, bool F16OUT>
+__global__ void dequant_native_kernel(const uint8_t* __restrict__ src, int64_t row_bytes, int64_t N,
+                                      int64_t K, void* __restrict__ dst) {
+    const int64_t total = N * K;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = i / K;
+        const int k = (int)(i % K);
+        const uint8_t* row = src + n * row_bytes;
+        float v;
+        if constexpr (WT == WT_Q8_0) v = decode_native_elem_q8_0(row, k);
+        else if constexpr (WT == WT_Q4_K) v = decode_native_elem_q4k(row, k);
+        else if constexpr (WT == WT_Q6_K) v = decode_native_elem_q6k(row, k);
+        else if constexpr (WT == WT_F16) v = __half2float(reinterpret_cast<const __half*>(row)[k]);
+        else if constexpr (WT == WT_BF16) v = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(row)[k] << 16);
+        else v = reinterpret_cast<const float*>(row)[k];
+        if constexpr (F16OUT) reinterpret_cast<__half*>(dst)[i] = __float2half_rn(v);
+        else reinterpret_cast<float*>(dst)[i] = v;
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Native -> packed re-layout (the weight cache's device-resident format, quant.cuh).
+// One thread per (row, 256-weight super-block).
+// ------------------------------------------------------------------------------------------
+__global__ void pack_q6k_kernel(const uint8_t* __restrict__ src, int64_t N, int64_t nsb,
+                                uint8_t* __restrict__ dstA, uint16_t* __restrict__ dstD) {
+    const int64_t total = N * nsb;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const uint8_t* b = src + i * 210;
+        uint8_t* o = dstA + i * 208;
+        for (int j = 0; j < 208; j++) o[j] = b[j];
+        dstD[i] = (uint16_t)(b[208] | (b[209] << 8));
+    }
+}
+
+__global__ void pack_q8_0_kernel(const uint8_t* __restrict__ src, int64_t N, int64_t nblk, int64_t ngrp,
+                                 uint8_t* __restrict__ dstA, uint16_t* __restrict__ dstD) {
+    // nblk native 32-weight blocks per row, packed into ngrp groups of 8 (zero-padded).
+    const int64_t total = N * ngrp * 8;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = i / (ngrp * 8);
+        const int64_t j = i % (ngrp * 8);
+        uint8_t* o = dstA + n * ngrp * 256 + j * 32;
+        uint16_t* od = dstD + n * ngrp * 8 + j;
+        if (j < nblk) {
+            const uint8_t* b = src + (n * nblk + j) * 34;
+            *od = (uint16_t)(b[0] | (b[1] << 8));
+            for (int q = 0; q < 32; q++) o[q] = b[2 + q];
+        } else {
+            *od = 0;
+            for (int q = 0; q < 32; q++) o[q] = 0;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Host side
+// ------------------------------------------------------------------------------------------
+
+int device_sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cached[dev] == 0) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        cached[dev] = v;
+    }
+    return cached[dev];
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// A 2-D fp16 tensor map [rows, cols] (cols innermost), row pitch in elements, box
+// [box_rows, box_cols] with the 128-byte swizzle (box_cols * 2 == 128).
+bool make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+                      uint32_t box_rows, uint32_t box_cols) {
+    EncodeTiledFn fn = get_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {pitch_elems * 2};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+static inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// The launch plan for one MUL_MAT: token tile, split-K factor and unit count.
+struct GemmPlan {
+    int bt, splits, kb_per_split, nkb, ntn, ntt, units, grid;
+};
+
+static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms) {
+    GemmPlan p{};
+    p.nkb = (int)((K + GEMM_BK - 1) / GEMM_BK);
+    p.ntn = (int)((N + GEMM_BN - 1) / GEMM_BN);
+    p.bt = M <= 32 ? 32 : M <= 64 ? 64 : M <= 1024 ? 128 : 256;
+    p.ntt = (int)((M + p.bt - 1) / p.bt);
+    const int tiles = p.ntn * p.ntt;
+    int splits = 1;
+    if (tiles < sms) {
+        splits = sms / tiles;
+        const int max_by_k = p.nkb / 4 > 0 ? p.nkb / 4 : 1;
+        if (splits > max_by_k) splits = max_by_k;
+        if (splits > 16) splits = 16;
+        if (splits < 1) splits = 1;
+    }
+    p.kb_per_split = (p.nkb + splits - 1) / splits;
+    p.splits = (p.nkb + p.kb_per_split - 1) / p.kb_per_split;   // no empty split
+    p.units = tiles * p.splits;
+    p.grid = p.units < sms ? p.units : sms;
+    return p;
+}
+
+struct MulMatWorkspace {
+    size_t a16_off, scales_off, part_off, total;
+};
+
+static MulMatWorkspace mm_workspace_layout(int64_t M, int64_t N, int64_t K, const GemmPlan& p) {
+    MulMatWorkspace w{};
+    w.a16_off = 0;
+    w.scales_off = align_up((size_t)M * K * 2, 256);
+    w.part_off = align_up(w.scales_off + (size_t)M * 4, 256);
+    w.total = w.part_off + (p.splits > 1 ? (size_t)p.splits * M * N * 4 : 0);
+    return w;
+}
+
+template <int BT, int WT>
+static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& a, int grid,
+                                 cudaStream_t st) {
+    using C = GemmCfg<BT, WT>;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BT, WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    gemm_kernel<BT, WT><<<grid, C::THREADS, C::SMEM, st>>>(tmA, tmW, a);
+    return cudaGetLastError();
+}
+
+template <int WT>
+static cudaError_t launch_gemm_bt(int bt, const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& a,
+                                  int grid, cudaStream_t st) {
+    switch (bt) {
+        case 32: return launch_gemm_t<32, WT>(tmA, tmW, a, grid, st);
+        case 64: return launch_gemm_t<64, WT>(tmA, tmW, a, grid, st);
+        case 128: return launch_gemm_t<128, WT>(tmA, tmW, a, grid, st);
+        default: return launch_gemm_t<256, WT>(tmA, tmW, a, grid, st);
+    }
+}
+
+size_t packed_weight_bytes(int type, int64_t N, int64_t K, size_t* plane_d_off) {
+    size_t off = 0, total = 0;
+    switch (type) {
+        case WT_F16: total = (size_t)N * K * 2; break;
+        case WT_Q4_K: total = (size_t)N * (K / 256) * 144; break;
+        case WT_Q6_K:
+            off = align_up((size_t)N * (K / 256) * 208, 256);
+            total = off + (size_t)N * (K / 256) * 2;
+            break;
+        case WT_Q8_0: {
+            const int64_t ngrp = (K + 255) / 256;
+            off = align_up((size_t)N * ngrp * 256, 256);
+            total = off + (size_t)N * ngrp * 8 * 2;
+            break;
+        }
+        default: return 0;
+    }
+    if (plane_d_off) *plane_d_off = off;
+    return total;
+}
+
+bool weight_type_supported(int type, int64_t K) {
+    switch (type) {
+        case WT_F16: return K % 8 == 0;
+        case WT_Q8_0: return K % 32 == 0;
+        case WT_Q4_K:
+        case WT_Q6_K: return K % 256 == 0;
+        default: return false;
+    }
+}
+
+int mul_mat_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const float* src1, int64_t lda, int64_t M,
+                 float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t st) {
+    if (!w_packed || !src1 || !dst || !dev_err || M <= 0 || N <= 0 || K <= 0) return B200_E_INVALID;
+    if (!weight_type_supported(wtype, K) || K % 32 != 0 || N % 16 != 0) return B200_E_UNSUPPORTED;
+    if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return B200_E_UNSUPPORTED;
+    const int sms = device_sm_count();
+    const GemmPlan p = plan_gemm(M, N, K, sms);
+    const MulMatWorkspace wl = mm_workspace_layout(M, N, K, p);
+    if (!workspace || workspace_bytes < wl.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+        return B200_E_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    __half* a16 = reinterpret_cast<__half*>(ws + wl.a16_off);
+    float* scales = reinterpret_cast<float*>(ws + wl.scales_off);
+    float* part = reinterpret_cast<float*>(ws + wl.part_off);
+
+    {
+        const int threads = 256;
+        const int blocks = (int)((M * 32 + threads - 1) / threads);
+        act_pack_kernel<<<blocks, threads, 0, st>>>(src1, lda, (int)M, (int)K, a16, scales);
+        if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
+    }
+
+    CUtensorMap tmA, tmW;
+    std::memset(&tmW, 0, sizeof(tmW));
+    if (!make_tmap_2d_f16(&tmA, a16, (uint64_t)M, (uint64_t)K, (uint64_t)K, (uint32_t)p.bt, GEMM_BK))
+        return B200_E_CUDA;
+    GemmArgs a{};
+    size_t d_off = 0;
+    packed_weight_bytes(wtype, N, K, &d_off);
+    if (wtype == WT_F16) {
+        if (!make_tmap_2d_f16(&tmW, w_packed, (uint64_t)N, (uint64_t)K, (uint64_t)K, GEMM_BN, GEMM_BK))
+            return B200_E_CUDA;
+    } else {
+        tmW = tmA;   // unused by the quantized kernels
+        a.w = static_cast<const uint8_t*>(w_packed);
+        if (wtype == WT_Q4_K) {
+            a.w_row_bytes = (K / 256) * 144;
+        } else if (wtype == WT_Q6_K) {
+            a.w_row_bytes = (K / 256) * 208;
+            a.wd = reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(w_packed) + d_off);
+            a.wd_row_elems = K / 256;
+        } else {
+            const int64_t ngrp = (K + 255) / 256;
+            a.w_row_bytes = ngrp * 256;
+            a.wd = reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(w_packed) + d_off);
+            a.wd_row_elems = ngrp * 8;
+        }
+    }
+    a.scales = scales;
+    a.M = (int)M;
+    a.N = (int)N;
+    a.K = (int)K;
+    a.n_tiles_n = p.ntn;
+    a.n_tiles_t = p.ntt;
+    a.splits = p.splits;
+    a.kb_per_split = p.kb_per_split;
+    a.nkb = p.nkb;
+    a.num_units = p.units;
+    a.err = dev_err;
+    if (p.splits > 1) {
+        a.out = part;
+        a.ldo = N;
+        a.split_stride = (int64_t)M * N;
+    } else {
+        a.out = dst;
+        a.ldo = ldd;
+        a.split_stride = 0;
+    }
+    cudaError_t e;
+    switch (wtype) {
+        case WT_F16: e = launch_gemm_bt<WT_F16>(p.bt, tmA, tmW, a, p.grid, st); break;
+        case WT_Q4_K: e = launch_gemm_bt<WT_Q4_K>(p.bt, tmA, tmW, a, p.grid, st); break;
+        case WT_Q6_K: e = launch_gemm_bt<WT_Q6_K>(p.bt, tmA, tmW, a, p.grid, st); break;
+        case WT_Q8_0: e = launch_gemm_bt<WT_Q8_0>(p.bt, tmA, tmW, a, p.grid, st); break;
+        default: return B200_E_UNSUPPORTED;
+    }
+    if (e != cudaSuccess) return B200_E_CUDA;
+    if (p.splits > 1) {
+        const int64_t total = M * N;
+        int blocks = (int)((total + 255) / 256);
+        if (blocks > sms * 8) blocks = sms * 8;
+        splitk_reduce_kernel<<<blocks, 256, 0, st>>>(part, p.splits, (int64_t)M * N, scales, dst, ldd, (int)M, (int)N);
+        if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
+    }
+    return B200_OK;
+}
+
+size_t mul_mat_workspace(int64_t M, int64_t N, int64_t K) {
+    const GemmPlan p = plan_gemm(M, N, K, device_sm_count());
+    return mm_workspace_layout(M, N, K, p).total;
+}
+
+int weight_pack_impl(int type, const void* src, int64_t N, int64_t K, void* dst, cudaStream_t st) {
+    if (!src || !dst || N <= 0 || K <= 0) return B200_E_INVALID;
+    if (!weight_type_supported(type, K)) return B200_E_UNSUPPORTED;
+    size_t d_off = 0;
+    const size_t bytes = packed_weight_bytes(type, N, K, &d_off);
+    if (type == WT_F16 || type == WT_Q4_K) {
+        if (cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st) != cudaSuccess) return B200_E_CUDA;
+        return B200_OK;
+    }
+    uint8_t* dA = static_cast<uint8_t*>(dst);
+    uint16_t* dD = reinterpret_cast<uint16_t*>(dA + d_off);
+    if (type == WT_Q6_K) {
+        const int64_t nsb = K / 256;
+        const int64_t total = N * nsb;
+        int blocks = (int)((total + 255) / 256);
+        if (blocks > 65535) blocks = 65535;
+        pack_q6k_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint8_t*>(src), N, nsb, dA, dD);
+    } else {
+        const int64_t nblk = K / 32, ngrp = (K + 255) / 256;
+        const int64_t total = N * ngrp * 8;
+        int blocks = (int)((total + 255) / 256);
+        if (blocks > 65535) blocks = 65535;
+        pack_q8_0_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint8_t*>(src), N, nblk, ngrp, dA, dD);
+    }
+    return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
+int dequantize_impl(int type, const void* src, int64_t N, int64_t K, int f16_out, void* dst, cudaStream_t st) {
+    if (!src || !dst || N <= 0 || K <= 0) return B200_E_INVALID;
+    if (K % wt_block_elems(type)) return B200_E_UNSUPPORTED;
+    const int64_t row_bytes = (K / wt_block_elems(type)) * wt_block_bytes(type);
+    const int64_t total = N * K;
+    int blocks = (int)((total + 255) / 256);
+    if (blocks > device_sm_count() * 16) blocks = device_sm_count() * 16;
+    const uint8_t* s = static_cast<const uint8_t*>(src);
+#define B200_DQ(T)                                                                                 \
+    if (f16_out) dequant_native_kernel<T, true><<<blocks, 256, 0, st>>>(s, row_bytes, N, K, dst); \
+    else dequant_native_kernel<T, false><<<blocks, 256, 0, st>>>(s, row_bytes, N, K, dst);
+    switch (type) {
+        case WT_Q8_0: B200_DQ(WT_Q8_0); break;
+        case WT_Q4_K: B200_DQ(WT_Q4_K); break;
+        case WT_Q6_K: B200_DQ(WT_Q6_K); break;
+        case WT_F16: B200_DQ(WT_F16); break;
+        case WT_BF16: B200_DQ(WT_BF16); break;
+        case WT_F32: B200_DQ(WT_F32); break;
+        default: return B200_E_UNSUPPORTED;
+    }
+#undef B200_DQ
+    return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
+}  // namespace b200
+
+// ------------------------------------------------------------------------------------------
+// C ABI
+// ------------------------------------------------------------------------------------------
+extern "C" {
+
+size_t b200_weight_packed_size(int type, int64_t N, int64_t K) {
+    if (!b200::weight_type_supported(type, K) || N <= 0) return 0;
+    return b200::packed_weight_bytes(type, N, K, nullptr);
+}
+
+int b200_weight_pack(int type, const void* src_native, int64_t N, int64_t K, void* dst_packed, void* stream) {
+    return b200::weight_pack_impl(type, src_native, N, K, dst_packed, static_cast<cudaStream_t>(stream));
+}
+
+int b200_dequantize(int type, const void* src_native, int64_t N, int64_t K, int f16_out, void* dst, void* stream) {
+    return b200::dequantize_impl(type, src_native, N, K, f16_out, dst, static_cast<cudaStream_t>(stream));
+}
+
+size_t b200_mul_mat_workspace_size(int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    return b200::mul_mat_workspace(M, N, K);
+}
+
+int b200_mul_mat(int wtype, const void* w_packed, int64_t N, int64_t K, const float* src1, int64_t lda, int64_t M,
+                 float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err, void* stream) {
+    return b200::mul_mat_impl(wtype, w_packed, N, K, src1, lda, M, dst, ldd, workspace, workspace_bytes, dev_err,
+                              static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

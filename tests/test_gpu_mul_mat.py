@@ -1,0 +1,170 @@
+"""MUL_MAT parity on the GPU, through the C ABI (b200_dequantize / b200_weight_pack /
+b200_mul_mat), against the CPU oracle and the golden dequant vectors.
+
+Mirrors test-rocket-matmul.cpp: its F16 shapes and pad cases (:123-132), the outlier-row
+case (:181-221) and the quantized shapes (:316-330), plus the BASELINE sweep's (K, N) at
+small M. Tolerance: max |err| / max |ref| <= 1e-2 against the fp64 oracle (the north
+star's bound), and the reference's element rule.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from conftest import rel_err, rk_compare
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+def _lib():
+    import ggml_b200
+    return ggml_b200
+
+
+def _dev(torch, arr):
+    return torch.from_numpy(np.ascontiguousarray(arr)).cuda()
+
+
+def _err_word(torch):
+    return torch.zeros(1, dtype=torch.int32, device="cuda")
+
+
+def _check_err(err):
+    assert int(err.item()) == 0, f"device error word {int(err.item())}"
+
+
+def run_mul_mat(torch, wtype, w_raw, N, K, a):
+    """Upload native weight bytes, pack them, run b200_mul_mat; returns dst [M, N] f32."""
+    g = _lib()
+    M = a.shape[0]
+    w_dev = _dev(torch, w_raw.reshape(-1))
+    packed = torch.empty(g.weight_packed_size(wtype, N, K), dtype=torch.uint8, device="cuda")
+    g.weight_pack(wtype, w_dev, N, K, packed)
+    a_dev = _dev(torch, a.astype(np.float32))
+    out = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    ws = torch.empty(g.mul_mat_workspace_size(M, N, K), dtype=torch.uint8, device="cuda")
+    err = _err_word(torch)
+    g.mul_mat(wtype, packed, N, K, a_dev, M, out, ws, err)
+    torch.cuda.synchronize()
+    _check_err(err)
+    return out.cpu().numpy()
+
+
+def _weights(rng, N, K, wtype):
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    if wtype == 1:
+        return oracle.fp16_bits(w).view(np.uint8).reshape(N, K * 2)
+    return oracle.quantize(wtype, w)
+
+
+@pytest.mark.parametrize("name", ["q8_0", "q4_k", "q6_k"])
+def test_dequant_golden_bitexact(cuda, name):
+    import os
+    import torch
+    g = _lib()
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", f"dequant_{name}.npz"))
+    raw, deq, t = z["raw"], z["deq"], int(z["type_id"])
+    elems = deq.shape[1]
+    per_row = 8 if elems == 32 else 4
+    N = raw.shape[0] // per_row
+    K = per_row * elems
+    src = _dev(torch, raw[: N * per_row].reshape(-1))
+    out = torch.empty((N, K), dtype=torch.float32, device="cuda")
+    g.dequantize(t, src, N, K, out)
+    out16 = torch.empty((N, K), dtype=torch.float16, device="cuda")
+    g.dequantize(t, src, N, K, out16, f16_out=True)
+    torch.cuda.synchronize()
+    want = deq[: N * per_row].reshape(N, K)
+    got = out.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert np.array_equal(out16.cpu().numpy().view(np.uint16), want.astype(np.float16).view(np.uint16))
+
+
+# (K, N, M) from test-rocket-matmul.cpp:123-132, N raised to the claim rule's minimum where
+# the reference used a smaller one.
+F16_SHAPES = [(64, 64, 8), (384, 256, 256), (3840, 4096, 512), (64, 64, 7), (384, 256, 130), (3840, 4096, 250),
+              (4096, 512, 33), (4096, 256, 1100), (1024, 272, 64)]
+
+
+@pytest.mark.parametrize("K,N,M", F16_SHAPES)
+def test_mul_mat_f16(cuda, K, N, M):
+    import torch
+    rng = np.random.default_rng(0xB200 ^ (K * 7 + N * 13 + M))
+    w = _weights(rng, N, K, 1)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    got = run_mul_mat(torch, 1, w, N, K, a)
+    ref = oracle.mul_mat(1, w, N, K, a)
+    assert np.all(np.isfinite(got))
+    assert rel_err(got, ref) <= TOL
+    cos, bad = rk_compare(ref, got)
+    assert bad == 0 and cos > 0.9999
+
+
+@pytest.mark.parametrize("K,N,M", [(384, 256, 130), (4096, 512, 512), (1024, 128, 40)])
+def test_mul_mat_f16_matches_exact_operands(cuda, K, N, M):
+    """The kernel against fp64 over its own fp16 operands (the packed activation and the fp16
+    weight): only the fp32 accumulation order differs, so the bound is tight."""
+    import torch
+    rng = np.random.default_rng(K + N + M)
+    w = _weights(rng, N, K, 1)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    got = run_mul_mat(torch, 1, w, N, K, a)
+    a16, s = oracle.pack_act(a)
+    a16f = a16.view(np.float16).astype(np.float64)
+    wf = w.view(np.float16).reshape(N, K).astype(np.float64)
+    ref = (a16f @ wf.T) * s[:, None].astype(np.float64)
+    assert rel_err(got, ref) <= 2e-6
+
+
+def test_mul_mat_outlier_row(cuda):
+    """test-rocket-matmul.cpp:181-221: one token ~3000x the others must not crush the small rows."""
+    import torch
+    K, N, M = 256, 64, 8
+    wf = ((np.arange(K * N) * 7 % 13) - 6).astype(np.float32).reshape(N, K) * 0.05
+    x = ((np.arange(K * M) * 5 % 11) - 5).astype(np.float32).reshape(M, K) * 0.02
+    x[3] = ((np.arange(K) % 7) - 3).astype(np.float32) * 300.0
+    w = oracle.fp16_bits(wf).view(np.uint8).reshape(N, K * 2)
+    got = run_mul_mat(torch, 1, w, N, K, x)
+    ref = oracle.mul_mat(1, w, N, K, x)
+    small = [m for m in range(M) if m != 3]
+    assert rel_err(got[small], ref[small]) <= TOL
+    assert rel_err(got[3], ref[3]) <= TOL
+
+
+# test-rocket-matmul.cpp:320-326 plus the BASELINE sweep shapes at small M
+Q_SHAPES = [(256, 128, 64, 8), (3840, 256, 128, 8), (256, 128, 64, 12), (3840, 256, 128, 12), (512, 256, 128, 14),
+            (4096, 256, 32, 12), (4096, 256, 32, 14), (4096, 256, 32, 8), (14336, 128, 48, 12), (768, 2048, 200, 12),
+            (2080, 64, 16, 8)]
+
+
+@pytest.mark.parametrize("K,N,M,wtype", Q_SHAPES)
+def test_mul_mat_quant(cuda, K, N, M, wtype):
+    import torch
+    rng = np.random.default_rng(0xB200 ^ (K + N * 3 + M * 5 + wtype))
+    w = _weights(rng, N, K, wtype)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    got = run_mul_mat(torch, wtype, w, N, K, a)
+    ref = oracle.mul_mat(wtype, w, N, K, a)
+    assert np.all(np.isfinite(got))
+    assert rel_err(got, ref) <= TOL
+    cos, bad = rk_compare(ref, got)
+    assert bad == 0 and cos > 0.9999
+
+
+@pytest.mark.parametrize("K,N,M,wtype", [(3840, 256, 128, 12), (512, 256, 128, 14), (3840, 256, 96, 8)])
+def test_mul_mat_quant_equals_dequant_then_f16(cuda, K, N, M, wtype):
+    """The fused dequant GEMM decodes each weight to exactly the fp16 value the standalone
+    dequant produces, so it must equal the F16 GEMM over that fp16 weight bit for bit."""
+    import torch
+    g = _lib()
+    rng = np.random.default_rng(99 + wtype)
+    w = _weights(rng, N, K, wtype)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    got_q = run_mul_mat(torch, wtype, w, N, K, a)
+    w16 = torch.empty((N, K), dtype=torch.float16, device="cuda")
+    g.dequantize(wtype, _dev(torch, w.reshape(-1)), N, K, w16, f16_out=True)
+    torch.cuda.synchronize()
+    w16_bytes = w16.cpu().numpy().view(np.uint8).reshape(N, K * 2)
+    got_f = run_mul_mat(torch, 1, w16_bytes, N, K, a)
+    assert np.array_equal(got_q.view(np.uint32), got_f.view(np.uint32))
