@@ -1,0 +1,368 @@
+#!/usr/bin/env python
+"""Prefill MUL_MAT throughput of the ggml B200 backend (the headline of BASELINE.json).
+
+Workload (one "step"): the quantized prefill GEMM sweep's three (K, N) weight shapes,
+(4096, 4096), (4096, 14336) and (14336, 4096), in Q4_K, each multiplied by a 512-token F32
+activation ubatch -- three MUL_MAT ops, 137.4 GFLOP. Weights are N(0, 0.02) quantized to
+Q4_K on the host, activations N(0, 1), seeded; all synthetic.
+
+  value     TFLOP/s of the step on the device, inputs resident in HBM, L2 flushed (a 256 MiB
+            memset) before every timed step, device time from CUDA events.
+  e2e       the same metric through the public C ABI with host buffers: every step copies the
+            activations H2D from pinned memory, runs b200_mul_mat, and copies dst D2H.
+  roofline  the tcgen05 GEMM kernel alone (its CUDA-event time per launch) against the
+            measured bf16/fp16 dense peak.
+
+--gpus N (under torchrun): every rank runs its own ubatch against its own copy of the
+weights (replicas; weak scaling); the timed region is bracketed by barriers and the max over
+ranks is reported.
+
+--impl reference: the CPU restatement of the reference's MUL_MAT (the oracle, fp64 over the
+ggml-decoded weight, rocket_cpu_matmul_slice) on all host cores, on a bounded token sample of
+the same workload per step.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "ggml-rocket_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "prefill GEMM TFLOP/s (F16/Q4_K) and prompt tokens/sec at 512-token ubatch"
+SHAPES = [(4096, 4096), (4096, 14336), (14336, 4096)]   # (K, N)
+M_TOKENS = 512
+WTYPE = 12   # Q4_K
+WORKLOAD = ("Q4_K MUL_MAT sweep (BASELINE configs[1]) at M=512: (K,N) in {(4096,4096),(4096,14336),"
+            "(14336,4096)}, one op per shape per step")
+CPU_SAMPLE_ROWS = 64
+
+
+def step_flops(m=M_TOKENS):
+    return sum(2.0 * m * n * k for (k, n) in SHAPES)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    return ap.parse_args()
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def profile_traffic():
+    """Per-launch DRAM bytes of the GEMM kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "gemm_q4k_m512_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get("traffic_bytes_per_launch")
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.out.flush()
+        self.out.seek(0)
+        rows = [r.strip().split(",") for r in self.out.read().strip().splitlines() if r.strip()]
+        os.unlink(self.out.name)
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax = max(smax, float(r[2]))
+                for i, nm in enumerate(names):
+                    if r[5 + i].strip().lower() == "active":
+                        reasons.add(nm)
+            except Exception:
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------------
+# reference arm: the CPU restatement timed on the host
+# ------------------------------------------------------------------------------------------------
+
+def make_host_inputs(seed, m_rows):
+    import numpy as np
+    from ggml_b200 import quants
+    rng = np.random.default_rng(seed)
+    ws, acts = [], []
+    for (k, n) in SHAPES:
+        w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02))
+        ws.append(quants.quantize(WTYPE, w))
+        acts.append(rng.standard_normal((m_rows, k), dtype=np.float32))
+    return ws, acts
+
+
+def cpu_oracle_step(ws, acts):
+    import oracle
+    for (k, n), w, a in zip(SHAPES, ws, acts):
+        oracle.mul_mat(WTYPE, w, n, k, a, nthreads=0)
+
+
+def run_reference(args):
+    ws_, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    import oracle
+    oracle.build()
+    ws, acts = make_host_inputs(0xB200, CPU_SAMPLE_ROWS)
+    for _ in range(args.warmup):
+        cpu_oracle_step(ws, acts)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_oracle_step(ws, acts)
+    dt = (time.perf_counter() - t0) / args.steps
+    val = step_flops(CPU_SAMPLE_ROWS) / dt / 1e12
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": f"{CPU_SAMPLE_ROWS} of the 512 tokens per step",
+                   "global_batch": M_TOKENS, "parallelism": "host threads"},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": f"{CPU_SAMPLE_ROWS} token rows x 3 shapes per step"},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------------
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import ggml_b200 as g
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    g.lib()
+
+    ws_host, acts_host = make_host_inputs(0xB200 + rank, M_TOKENS)
+    stream = torch.cuda.current_stream()
+    weights, acts, a16s, scales, outs, gws = [], [], [], [], [], []
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    for (k, n), w, a in zip(SHAPES, ws_host, acts_host):
+        raw = torch.from_numpy(w.reshape(-1)).to(dev)
+        packed = torch.empty(g.weight_packed_size(WTYPE, n, k), dtype=torch.uint8, device=dev)
+        g.weight_pack(WTYPE, raw, n, k, packed)
+        del raw
+        weights.append(packed)
+        acts.append(torch.from_numpy(a).to(dev))
+        a16s.append(torch.empty((M_TOKENS, k), dtype=torch.float16, device=dev))
+        scales.append(torch.empty(M_TOKENS, dtype=torch.float32, device=dev))
+        outs.append(torch.empty((M_TOKENS, n), dtype=torch.float32, device=dev))
+        wsz = g.gemm_packed_workspace_size(M_TOKENS, n, k)
+        gws.append(torch.empty(max(wsz, 256), dtype=torch.uint8, device=dev))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    launches_per_step = sum(g.mul_mat_plan(M_TOKENS, n, k)["launches"] for (k, n) in SHAPES)
+
+    def step(ev):
+        # ev: list of events [start, after pack0, after gemm0, after pack1, ...]
+        ev[0].record(stream)
+        for i, (k, n) in enumerate(SHAPES):
+            g.act_pack(acts[i], M_TOKENS, k, a16s[i], scales[i], stream=stream)
+            ev[1 + 2 * i].record(stream)
+            g.gemm_packed(WTYPE, weights[i], n, k, a16s[i], scales[i], M_TOKENS, outs[i], gws[i], err,
+                          stream=stream)
+            ev[2 + 2 * i].record(stream)
+
+    def new_events():
+        return [torch.cuda.Event(enable_timing=True) for _ in range(1 + 2 * len(SHAPES))]
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step(new_events())
+    torch.cuda.synchronize()
+    if int(err.item()) != 0:
+        raise SystemExit(f"device error {int(err.item())} during warm-up")
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+    evs = []
+    for _ in range(args.steps):
+        flush.zero_()
+        e = new_events()
+        step(e)
+        evs.append(e)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = sampler.stop() if sampler else None
+    if int(err.item()) != 0:
+        raise SystemExit(f"device error {int(err.item())} in the timed region")
+
+    step_ms = [e[0].elapsed_time(e[-1]) for e in evs]
+    gemm_ms = [sum(e[1 + 2 * i].elapsed_time(e[2 + 2 * i]) for i in range(len(SHAPES))) for e in evs]
+    ms_local = sum(step_ms) / len(step_ms)
+    gemm_local = sum(gemm_ms) / len(gemm_ms)
+
+    # ---- e2e: host buffers through the public C ABI ----
+    pin_in = [torch.from_numpy(a).pin_memory() for a in acts_host]
+    pin_out = [torch.empty((M_TOKENS, n), dtype=torch.float32).pin_memory() for (k, n) in SHAPES]
+    mm_ws = [torch.empty(g.mul_mat_workspace_size(M_TOKENS, n, k), dtype=torch.uint8, device=dev)
+             for (k, n) in SHAPES]
+    h2d = sum(a.numel() * 4 for a in pin_in)
+    d2h = sum(o.numel() * 4 for o in pin_out)
+
+    def e2e_step():
+        for i, (k, n) in enumerate(SHAPES):
+            acts[i].copy_(pin_in[i], non_blocking=True)
+            g.mul_mat(WTYPE, weights[i], n, k, acts[i], M_TOKENS, outs[i], mm_ws[i], err, stream=stream)
+            pin_out[i].copy_(outs[i], non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        flush.zero_()
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    flush_ms = 0.0
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        flush.zero_()
+    f1.record(stream)
+    torch.cuda.synchronize()
+    flush_ms = f0.elapsed_time(f1)
+    e2e_local = (e0.elapsed_time(e1) - flush_ms) / args.steps
+    if world > 1:
+        torch.distributed.barrier()
+
+    vals = torch.tensor([ms_local, gemm_local, e2e_local], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+    ms, gms, e2e_ms = [float(x) for x in vals.tolist()]
+
+    if rank == 0:
+        peaks, peak_src = measured_peaks()
+        flops = step_flops()
+        value = flops * world / (ms / 1e3) / 1e12
+        achieved = flops / (gms / 1e3) / 1e12
+        peak = float(peaks.get("bf16_tflops", 1590.0))
+        # the CPU baseline: the oracle on a bounded sample, this host's cores
+        import oracle
+        oracle.build()
+        ws_c, acts_c = make_host_inputs(0xB200, CPU_SAMPLE_ROWS)
+        cpu_oracle_step(ws_c, acts_c)
+        t0 = time.perf_counter()
+        reps = 3
+        for _ in range(reps):
+            cpu_oracle_step(ws_c, acts_c)
+        cpu_dt = (time.perf_counter() - t0) / reps
+        cpu_val = step_flops(CPU_SAMPLE_ROWS) / cpu_dt / 1e12
+        plans = {f"{k}x{n}": g.mul_mat_plan(M_TOKENS, n, k) for (k, n) in SHAPES}
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "weight_type": "Q4_K", "global_batch": M_TOKENS * world,
+                       "seq_len": M_TOKENS, "parallelism": f"replicas x{world}",
+                       "l2": "flushed before every timed step (256 MiB memset)",
+                       "tokens_per_s": M_TOKENS * world / (ms / 1e3), "plans": plans},
+            "e2e": {"value": flops * world / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "b200_mul_mat with pinned-host activations copied in and dst copied out"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": profile_traffic(),
+                         "kernel": "gemm_kernel<BT,Q4_K> (tcgen05, fused Q4_K dequant)",
+                         "peak_source": f"{peak_src} bf16_tflops (burst)",
+                         "algorithmic": "2*M*N*K FLOP per launch, summed over the 3 launches of a step"},
+            "cpu_baseline": {"value": cpu_val, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"{CPU_SAMPLE_ROWS} token rows x 3 shapes (oracle fp64 GEMM over "
+                                       f"ggml-decoded Q4_K weights)"},
+            "clocks": clocks,
+            "gpu_launches": launches_per_step * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

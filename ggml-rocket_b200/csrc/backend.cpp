@@ -1,0 +1,1020 @@
+// The ggml B200 backend's host layer: what ggml-rocket decides on the host, re-implemented
+// over plain b200_tensor descriptors (include/ggml-b200.h) and driving the sm_100a kernels
+// (include/ggml-b200-kernels.h).
+//
+//   knobs          B200_* environment variables, read once; set-but-empty reads as unset
+//                  (ggml-rocket.cpp:698-724)
+//   claim rules    supports_op / offload_op (ggml-rocket.cpp:7334-7827)
+//   breaker        the device-route circuit breaker (ggml-rocket.cpp:263-307)
+//   weight cache   device-resident packed weights keyed by name + content fingerprint
+//                  (ggml-rocket.cpp:4124-4222), so a weight crosses the host link once
+//   graph_compute  the serial node walk with shared-src1 grouping (ggml-rocket.cpp:7088-7200)
+//
+// There is no CPU fallback: a claimed op that fails on the device fails the graph.
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <list>
+#include <map>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "ggml-b200-kernels.h"
+#include "ggml-b200.h"
+
+namespace {
+
+// ------------------------------------------------------------------------------------------------
+// logging and knobs
+// ------------------------------------------------------------------------------------------------
+
+void logf(const char* level, const char* fmt, ...) {
+    static const bool quiet = [] {
+        const char* e = getenv("B200_LOG");
+        return e && *e && atoi(e) == 0;
+    }();
+    if (quiet && strcmp(level, "E") != 0) return;
+    va_list ap;
+    va_start(ap, fmt);
+    fprintf(stderr, "[ggml-b200 %s] ", level);
+    vfprintf(stderr, fmt, ap);
+    va_end(ap);
+}
+
+int knob_int(const char* name, int dflt) {
+    const char* e = getenv(name);
+    return (e && *e) ? atoi(e) : dflt;
+}
+bool knob_on(const char* name, bool dflt) {
+    const char* e = getenv(name);
+    return (e && *e) ? (atoi(e) > 0) : dflt;
+}
+
+// Minimum rows a dense MUL_MAT must carry to be claimed (ggml-rocket.cpp:868-876). Below it
+// the op's fixed cost -- here the host<->device copies of the activation and the result --
+// outweighs the device's throughput advantage; decode (M = 1) and batched-beam decode stay on
+// the CPU. Floor 4, as in the reference.
+int min_m() {
+    static const int m = [] { const int x = knob_int("B200_MIN_M", 32); return x < 4 ? 4 : x; }();
+    return m;
+}
+// The floor for quantized weights (ggml-rocket.cpp:887-894). The reference's 512 pays for a
+// per-call host dequant; the fused device dequant has no such cost, so the default equals
+// min_m(). Never below min_m().
+int min_m_quant() {
+    static const int m = [] {
+        const int x = knob_int("B200_MIN_M_QUANT", 32);
+        return x < min_m() ? min_m() : x;
+    }();
+    return m;
+}
+
+enum MoeMode { MOE_OFF = 0, MOE_AUTO = 1, MOE_FORCED = 2 };
+int moe_mode() {
+    static const int v = [] {
+        const char* e = getenv("B200_MOE");
+        if (!e || !*e) return (int)MOE_AUTO;
+        return atoi(e) > 0 ? (int)MOE_FORCED : (int)MOE_OFF;
+    }();
+    return v;
+}
+int moe_min_tokens() {
+    static const int m = [] { const int x = knob_int("B200_MOE_MIN_TOKENS", 32); return x < min_m() ? min_m() : x; }();
+    return m;
+}
+// AUTO's first floor: rows an expert receives on average (n_tokens * n_used / n_expert),
+// rounded up to a power of two (ggml-rocket.cpp:952-961).
+int moe_m_bucket() {
+    static const int p = [] {
+        int g = knob_int("B200_MOE_M_BUCKET", 8);
+        if (g < 1) g = 1;
+        int q = 1;
+        while (q < g && q < (1 << 20)) q <<= 1;
+        return q;
+    }();
+    return p;
+}
+// AUTO's second floor: MACs one expert GEMM carries, in millions (0 disables).
+int moe_min_work_mmac() {
+    static const int w = [] { int v = knob_int("B200_MOE_MIN_WORK", 0); return v < 0 ? 0 : v; }();
+    return w;
+}
+bool flash_attn_on() {
+    static const bool v = knob_int("B200_FLASH_ATTN", 1) > 0;
+    return v;
+}
+int flash_attn_min_t() {
+    static const int t = [] { const int x = knob_int("B200_FLASH_ATTN_MIN_T", 16); return x < 1 ? 1 : x; }();
+    return t;
+}
+int flash_attn_min_kv() {
+    static const int kv = [] { const int x = knob_int("B200_FLASH_ATTN_MIN_KV", 1024); return x < 1 ? 1 : x; }();
+    return kv;
+}
+bool flash_attn_unmasked() {
+    static const bool v = knob_int("B200_FLASH_ATTN_UNMASKED", 0) > 0;
+    return v;
+}
+bool fuse_on() {
+    static const bool v = knob_on("B200_FUSE", true);
+    return v;
+}
+size_t weight_budget_bytes(int device) {
+    const int mb = knob_int("B200_WEIGHT_BUDGET_MB", 0);
+    if (mb > 0) return (size_t)mb << 20;
+    size_t fr = 0, tot = 0;
+    if (ggml_backend_b200_device_memory(device, &fr, &tot) != 0 || tot == 0) return (size_t)64 << 30;
+    return tot / 10 * 8;   // 80 % of the device
+}
+
+// ------------------------------------------------------------------------------------------------
+// tensor helpers (ggml semantics)
+// ------------------------------------------------------------------------------------------------
+
+enum : int { T_F32 = 0, T_F16 = 1, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14, T_I32 = 26, T_BF16 = 30 };
+
+int64_t blck_size(int t) { return t == T_Q8_0 ? 32 : (t == T_Q4_K || t == T_Q6_K) ? 256 : 1; }
+size_t type_size(int t) {
+    switch (t) {
+        case T_F32: case T_I32: return 4;
+        case T_F16: case T_BF16: return 2;
+        case T_Q8_0: return 34;
+        case T_Q4_K: return 144;
+        case T_Q6_K: return 210;
+        default: return 0;
+    }
+}
+bool is_quantized(int t) { return t == T_Q8_0 || t == T_Q4_K || t == T_Q6_K; }
+// Weight types the kernels read: F16 and the three GGUF formats natively; F32 and BF16 are
+// converted to fp16 once, when the weight enters the cache (the reference decodes both to fp16,
+// ggml-rocket.cpp:3853-3890).
+bool weight_type_ok(int t) { return t == T_F16 || t == T_F32 || t == T_BF16 || is_quantized(t); }
+int kernel_wtype(int t) { return (t == T_F32 || t == T_BF16) ? T_F16 : t; }
+
+size_t row_bytes(int t, int64_t k) { return type_size(t) * (size_t)(k / blck_size(t)); }
+size_t nbytes(const b200_tensor* t) {
+    size_t n = row_bytes(t->type, t->ne[0]);
+    for (int i = 1; i < 4; i++) n += (size_t)(t->ne[i] - 1) * t->nb[i];
+    return t->ne[1] && t->ne[2] && t->ne[3] ? n : 0;
+}
+bool is_contiguous(const b200_tensor* t) {
+    size_t next = type_size(t->type);
+    if (t->nb[0] != next) return false;
+    next = row_bytes(t->type, t->ne[0]);
+    for (int i = 1; i < 4; i++) {
+        if (t->ne[i] != 1 && t->nb[i] != next) return false;
+        next *= (size_t)t->ne[i];
+    }
+    return true;
+}
+int32_t op_param_i32(const b200_tensor* op, int i) { return op->op_params[i]; }
+float op_param_f32(const b200_tensor* op, int i) {
+    float f;
+    memcpy(&f, &op->op_params[i], 4);
+    return f;
+}
+
+// ------------------------------------------------------------------------------------------------
+// precision contract (ggml-rocket.cpp:7334-7404)
+// ------------------------------------------------------------------------------------------------
+
+// The accumulator of every route here is fp32 (tcgen05 accumulates in TMEM), which meets any
+// declaration. The activation is rounded to fp16, so a src1 declaration above F16 (F32, BF16)
+// is declined. A Hadamard-tagged MUL_MAT is declined: the CPU evaluates it as an exact
+// O(n log n) transform, here it would be a dense fp16 GEMM.
+bool prec_declines(const b200_tensor* op) {
+    const int32_t src1 = op_param_i32(op, 3);
+    if (src1 != B200_PREC_UNDECLARED && src1 < B200_PREC_F16) return true;
+    if (op->op == B200_OP_MUL_MAT && op_param_i32(op, 1) == B200_HINT_SRC0_IS_HADAMARD) return true;
+    return false;
+}
+
+bool sources_readable(const b200_tensor* op) {
+    for (int i = 0; i < B200_MAX_SRC; i++)
+        if (op->src[i] && !op->src[i]->readable) return false;
+    return true;
+}
+
+// ------------------------------------------------------------------------------------------------
+// MoE placement ledger (the reference's pre-flight, ggml-rocket.cpp:6131-6375): a process-wide
+// reservation of whole expert stacks against the device budget, decided once per stack.
+// ------------------------------------------------------------------------------------------------
+
+struct MoeLedger {
+    std::mutex mu;
+    std::map<std::string, bool> decided;
+    size_t reserved = 0;
+};
+MoeLedger& moe_ledger() {
+    static MoeLedger l;
+    return l;
+}
+
+}  // namespace
+
+// ================================================================================================
+// weight identity
+// ================================================================================================
+
+namespace {
+
+uint64_t fingerprint(const b200_tensor* t, const void* host_bytes) {
+    const size_t n = nbytes(t);
+    const unsigned char* p = static_cast<const unsigned char*>(host_bytes);
+    uint64_t h = 1469598103934665603ull ^ ((uint64_t)n * 0x100000001b3ull) ^ ((uint64_t)t->type << 48);
+    auto eat = [&](size_t off, size_t len) {
+        for (size_t i = 0; i < len; i++) {
+            h ^= p[off + i];
+            h *= 1099511628211ull;
+        }
+    };
+    const int NS = 16;
+    const size_t W = 64;
+    if (n <= NS * W) eat(0, n);
+    else
+        for (int s = 0; s < NS; s++) eat((n - W) / (NS - 1) * (size_t)s, W);
+    return h;
+}
+
+std::string weight_key(const b200_tensor* t) {
+    const char* n = t->name;
+    if (!n[0]) return std::string();
+    std::string key(n, strnlen(n, B200_MAX_NAME));
+    static const char PREFIX[] = "B200#";   // the scheduler's copy name: "<backend>#<tensor>#<copy>"
+    const size_t pl = sizeof(PREFIX) - 1;
+    if (key.compare(0, pl, PREFIX) == 0 && key.size() > pl) {
+        key = key.substr(pl);
+        const size_t h = key.rfind('#');
+        if (h != std::string::npos && h > 0 && h + 1 < key.size() &&
+            key.find_first_not_of("0123456789", h + 1) == std::string::npos)
+            key.resize(h);
+    }
+    auto autoname = [](const std::string& s) {
+        if (s.compare(0, 5, "leaf_") != 0 && s.compare(0, 5, "node_") != 0) return false;
+        if (s.size() == 5) return false;
+        return s.find_first_not_of("0123456789", 5) == std::string::npos;
+    };
+    if (autoname(key)) return std::string();
+    char buf[96];
+    snprintf(buf, sizeof buf, ":t%d:%lldx%lldx%lld", t->type, (long long)t->ne[0], (long long)t->ne[1],
+             (long long)t->ne[2]);
+    key += buf;
+    if (t->data && !t->on_device) {
+        snprintf(buf, sizeof buf, "@%016llx", (unsigned long long)fingerprint(t, t->data));
+        key += buf;
+    }
+    return key;
+}
+
+// ------------------------------------------------------------------------------------------------
+// the breaker (ggml-rocket.cpp:263-307): three consecutive device failures open a route for 64
+// calls, doubling per failed probe up to 4096; structural declines do not count.
+// ------------------------------------------------------------------------------------------------
+
+struct Breaker {
+    int fails = 0;
+    long skip = 0;
+    long open_len = 0;
+};
+bool device_failure(int rc) { return rc < 0 && rc != B200_E_UNSUPPORTED && rc != B200_E_WORKSPACE; }
+bool breaker_allow(Breaker& b) {
+    if (b.skip > 0) {
+        b.skip--;
+        return false;
+    }
+    return true;
+}
+void breaker_note(Breaker& b, int rc, const char* route) {
+    if (!device_failure(rc)) {
+        if (rc == 0) {
+            b.fails = 0;
+            b.open_len = 0;
+        }
+        return;
+    }
+    if (++b.fails < 3) return;
+    const long OPEN0 = 64, OPEN_MAX = 4096;
+    b.open_len = b.open_len ? std::min(b.open_len * 2, OPEN_MAX) : OPEN0;
+    b.skip = b.open_len;
+    logf("W", "%s: %d consecutive device failures (last rc=%d); bypassed for the next %ld calls\n", route, b.fails, rc,
+         b.skip);
+}
+
+}  // namespace
+
+// ================================================================================================
+// the backend context
+// ================================================================================================
+
+struct CachedWeight {
+    void* dev = nullptr;
+    size_t bytes = 0;
+    int ktype = 0;            // the type the kernels read
+    std::list<std::string>::iterator lru;
+};
+
+struct b200_backend {
+    uint32_t magic = 0xB2000B20u;
+    int device = 0;
+    int n_gpus = 1;
+    bool dev_ready = false;
+    cudaStream_t stream = nullptr;
+    int* dev_err = nullptr;
+    // grow-only device scratch arenas
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    void* io = nullptr;       // staging for host activations / outputs / attention inputs
+    size_t io_bytes = 0;
+    // weight cache
+    std::unordered_map<std::string, CachedWeight> cache;
+    std::list<std::string> lru;
+    size_t cache_bytes = 0;
+    size_t cache_budget = 0;
+    // transient (unkeyed) weight uploads of the current graph
+    std::vector<void*> transient;
+    // counters
+    std::map<std::string, long> route_ops;
+    long device_errors = 0;
+    long moe_resident = 0, moe_streamed = 0;
+    std::map<std::string, bool> moe_seen;
+    Breaker brk_fused;
+    std::mutex mu;            // graph_compute is serial per instance
+};
+
+namespace {
+
+bool cuda_ok(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return true;
+    logf("E", "%s: %s\n", what, cudaGetErrorString(e));
+    return false;
+}
+
+bool ensure_device(b200_backend* b) {
+    if (b->dev_ready) return true;
+    if (!cuda_ok(cudaSetDevice(b->device), "cudaSetDevice")) return false;
+    if (!cuda_ok(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking), "cudaStreamCreate")) return false;
+    if (!cuda_ok(cudaMalloc(&b->dev_err, 256), "cudaMalloc(err)")) return false;
+    if (!cuda_ok(cudaMemsetAsync(b->dev_err, 0, 256, b->stream), "cudaMemset(err)")) return false;
+    b->cache_budget = weight_budget_bytes(b->device);
+    b->dev_ready = true;
+    return true;
+}
+
+bool grow(void** p, size_t* have, size_t need, cudaStream_t st) {
+    if (*have >= need) return true;
+    if (*p) {
+        cudaStreamSynchronize(st);
+        cudaFree(*p);
+        *p = nullptr;
+        *have = 0;
+    }
+    size_t sz = std::max(need, (size_t)1 << 20);
+    sz = (sz + 4095) & ~(size_t)4095;
+    if (cudaMalloc(p, sz) != cudaSuccess) return false;
+    *have = sz;
+    return true;
+}
+
+void evict_until(b200_backend* b, size_t need) {
+    while (b->cache_bytes + need > b->cache_budget && !b->lru.empty()) {
+        const std::string k = b->lru.back();
+        b->lru.pop_back();
+        auto it = b->cache.find(k);
+        if (it != b->cache.end()) {
+            cudaStreamSynchronize(b->stream);
+            cudaFree(it->second.dev);
+            b->cache_bytes -= it->second.bytes;
+            b->cache.erase(it);
+        }
+    }
+}
+
+// Upload one [N, K] weight slab (native ggml bytes, host or device) into packed device form.
+// Returns the packed device pointer (cached under `key` when non-empty).
+void* pack_weight(b200_backend* b, const std::string& key, int type, const void* src, bool src_on_device, int64_t N,
+                  int64_t K, int* ktype_out) {
+    const int kt = kernel_wtype(type);
+    *ktype_out = kt;
+    if (!key.empty()) {
+        auto it = b->cache.find(key);
+        if (it != b->cache.end()) {
+            b->lru.erase(it->second.lru);
+            b->lru.push_front(key);
+            it->second.lru = b->lru.begin();
+            return it->second.dev;
+        }
+    }
+    const size_t packed = b200_weight_packed_size(kt, N, K);
+    const size_t native = row_bytes(type, K) * (size_t)N;
+    if (packed == 0) return nullptr;
+    if (!key.empty()) evict_until(b, packed);
+    void* dst = nullptr;
+    if (cudaMalloc(&dst, packed) != cudaSuccess) return nullptr;
+    // stage the native bytes on the device
+    const void* dsrc = src;
+    void* stage = nullptr;
+    if (!src_on_device) {
+        if (cudaMalloc(&stage, native) != cudaSuccess) {
+            cudaFree(dst);
+            return nullptr;
+        }
+        if (cudaMemcpyAsync(stage, src, native, cudaMemcpyHostToDevice, b->stream) != cudaSuccess) {
+            cudaFree(stage);
+            cudaFree(dst);
+            return nullptr;
+        }
+        dsrc = stage;
+    }
+    int rc;
+    if (type == T_F32 || type == T_BF16) rc = b200_dequantize(type, dsrc, N, K, 1, dst, b->stream);
+    else rc = b200_weight_pack(kt, dsrc, N, K, dst, b->stream);
+    if (stage) {
+        cudaStreamSynchronize(b->stream);
+        cudaFree(stage);
+    }
+    if (rc != B200_OK) {
+        cudaFree(dst);
+        return nullptr;
+    }
+    if (key.empty()) {
+        b->transient.push_back(dst);
+    } else {
+        b->lru.push_front(key);
+        CachedWeight cw;
+        cw.dev = dst;
+        cw.bytes = packed;
+        cw.ktype = kt;
+        cw.lru = b->lru.begin();
+        b->cache[key] = cw;
+        b->cache_bytes += packed;
+    }
+    return dst;
+}
+
+// Device pointer holding a tensor's bytes: its own when on the device, else a staged copy in
+// the io arena at *io_off (advanced).
+const void* stage_in(b200_backend* b, const b200_tensor* t, size_t* io_off, bool* ok) {
+    if (t->on_device) return t->data;
+    const size_t n = nbytes(t);
+    const size_t off = (*io_off + 255) & ~(size_t)255;
+    if (off + n > b->io_bytes) {
+        *ok = false;
+        return nullptr;
+    }
+    void* d = static_cast<char*>(b->io) + off;
+    if (cudaMemcpyAsync(d, t->data, n, cudaMemcpyHostToDevice, b->stream) != cudaSuccess) *ok = false;
+    *io_off = off + n;
+    return d;
+}
+
+size_t staged_size(const b200_tensor* t) { return t->on_device ? 0 : ((nbytes(t) + 255) & ~(size_t)255); }
+
+}  // namespace
+
+// ================================================================================================
+// claim rules
+// ================================================================================================
+
+extern "C" bool ggml_backend_b200_supports_op(const b200_tensor* op) {
+    if (!op) return false;
+    if (!sources_readable(op)) return false;
+    switch (op->op) {
+        case B200_OP_NONE:
+        case B200_OP_RESHAPE:
+        case B200_OP_VIEW:
+        case B200_OP_PERMUTE:
+        case B200_OP_TRANSPOSE:
+            return true;
+        case B200_OP_MUL_MAT: {
+            const b200_tensor* a = op->src[0];
+            const b200_tensor* bb = op->src[1];
+            if (!a || !bb) return false;
+            if (prec_declines(op)) return false;
+            const int64_t K = a->ne[0], N = a->ne[1], M = bb->ne[1];
+            const bool aq = is_quantized(a->type);
+            return a->op == B200_OP_NONE && weight_type_ok(a->type) && bb->type == T_F32 && op->type == T_F32 &&
+                   is_contiguous(a) && is_contiguous(bb) && is_contiguous(op) && a->ne[0] == bb->ne[0] &&
+                   a->ne[2] == 1 && a->ne[3] == 1 && (!aq || K % blck_size(a->type) == 0) && K % 32 == 0 &&
+                   N % 16 == 0 && K >= 64 && N >= 64 && M >= (aq ? min_m_quant() : min_m());
+        }
+        case B200_OP_MUL_MAT_ID: {
+            const int mode = moe_mode();
+            if (mode == MOE_OFF) return false;
+            const b200_tensor* a = op->src[0];
+            const b200_tensor* bb = op->src[1];
+            const b200_tensor* ids = op->src[2];
+            if (!a || !bb || !ids) return false;
+            if (prec_declines(op)) return false;
+            const int64_t K = a->ne[0], N = a->ne[1], n_tokens = ids->ne[1];
+            const bool aq = is_quantized(a->type);
+            const bool computable = a->op == B200_OP_NONE && weight_type_ok(a->type) && bb->type == T_F32 &&
+                                    ids->type == T_I32 && op->type == T_F32 && is_contiguous(a) &&
+                                    is_contiguous(bb) && is_contiguous(op) && a->ne[0] == bb->ne[0] &&
+                                    a->ne[3] == 1 && (!aq || K % blck_size(a->type) == 0) && K % 32 == 0 &&
+                                    N % 16 == 0 && K >= 64 && N >= 64 && n_tokens >= moe_min_tokens() &&
+                                    a->ne[2] > 0;
+            if (!computable) return false;
+            if (mode == MOE_FORCED) return true;
+            // AUTO: the rows an expert receives on average and the work one expert GEMM
+            // carries, each against its floor; then the whole stack reserved on the device.
+            const int64_t n_used = ids->ne[0], n_expert = a->ne[2];
+            const int64_t m_e = n_tokens * n_used / n_expert;
+            if (m_e < moe_m_bucket()) return false;
+            if (m_e * K * N < (int64_t)moe_min_work_mmac() * 1000000) return false;
+            const std::string key = weight_key(a);
+            const size_t stack = b200_weight_packed_size(kernel_wtype(a->type), N, K) * (size_t)n_expert;
+            MoeLedger& L = moe_ledger();
+            std::lock_guard<std::mutex> lk(L.mu);
+            if (!key.empty()) {
+                auto it = L.decided.find(key);
+                if (it != L.decided.end()) return it->second;
+            }
+            const size_t budget = weight_budget_bytes(0);
+            const bool fits = L.reserved + stack <= budget;
+            if (fits) L.reserved += stack;
+            if (!key.empty()) L.decided[key] = fits;
+            return fits;
+        }
+        case B200_OP_FLASH_ATTN_EXT: {
+            const b200_tensor* q = op->src[0];
+            const b200_tensor* k = op->src[1];
+            const b200_tensor* v = op->src[2];
+            const b200_tensor* m = op->src[3];
+            if (!flash_attn_on() || !q || !k || !v) return false;
+            if (!m && !flash_attn_unmasked()) return false;
+            if (op->src[4]) return false;   // attention sinks: a different softmax (ggml-rocket.cpp:7703-7721)
+            const float max_bias = op_param_f32(op, 1);
+            const int64_t D = q->ne[0], T = q->ne[1], H = q->ne[2], DV = v->ne[0];
+            const int64_t KV = k->ne[1], HK = k->ne[2];
+            auto aligned16 = [](const b200_tensor* t) {
+                return (t->nb[1] % 16 == 0) && (t->nb[2] % 16 == 0) && (t->on_device ? ((uintptr_t)t->data % 16 == 0) : true);
+            };
+            return max_bias == 0.0f && q->type == T_F32 && k->type == T_F16 && v->type == T_F16 &&
+                   (!m || (m->type == T_F16 && is_contiguous(m))) && op->type == T_F32 && is_contiguous(op) &&
+                   q->ne[3] == 1 && k->ne[3] == 1 && v->ne[3] == 1 && k->ne[0] == D && op->ne[0] == DV &&
+                   v->ne[1] == KV && v->ne[2] == HK && q->nb[0] == 4 && k->nb[0] == 2 && v->nb[0] == 2 &&
+                   (D == 64 || D == 128) && (DV == 64 || DV == 128) && HK > 0 && H % HK == 0 &&
+                   aligned16(k) && aligned16(v) && (!m || (m->ne[0] >= KV && m->ne[1] >= T)) &&
+                   T >= flash_attn_min_t() && KV >= flash_attn_min_kv();
+        }
+        default:
+            return false;
+    }
+}
+
+extern "C" bool ggml_backend_b200_offload_op(const b200_tensor* op) {
+    return op && (op->op == B200_OP_MUL_MAT || op->op == B200_OP_MUL_MAT_ID) && ggml_backend_b200_supports_op(op);
+}
+
+// ================================================================================================
+// handlers
+// ================================================================================================
+
+namespace {
+
+const char* route_name(int ktype) {
+    switch (ktype) {
+        case T_F16: return "f16";
+        case T_Q8_0: return "q8_0";
+        case T_Q4_K: return "q4_K";
+        case T_Q6_K: return "q6_K";
+        default: return "other";
+    }
+}
+
+bool check_dev_err(b200_backend* b, const char* what) {
+    int h = 0;
+    if (cudaMemcpyAsync(&h, b->dev_err, sizeof(int), cudaMemcpyDeviceToHost, b->stream) != cudaSuccess ||
+        cudaStreamSynchronize(b->stream) != cudaSuccess) {
+        logf("E", "%s: CUDA error %s\n", what, cudaGetErrorString(cudaGetLastError()));
+        b->device_errors++;
+        return false;
+    }
+    if (h != 0) {
+        logf("E", "%s: device error word %d\n", what, h);
+        b->device_errors++;
+        cudaMemsetAsync(b->dev_err, 0, sizeof(int), b->stream);
+        return false;
+    }
+    return true;
+}
+
+// MUL_MAT, including ggml's batch broadcast over dims 2/3 (ggml-rocket.cpp:4725-4750), and a
+// group of MUL_MATs sharing src1 (fused: one activation pack, one GEMM per member).
+int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
+    const b200_tensor* node0 = nodes[0];
+    const b200_tensor* src1 = node0->src[1];
+    const int64_t K = src1->ne[0], M = src1->ne[1];
+    const int64_t ne12 = src1->ne[2], ne13 = src1->ne[3];
+    // weights
+    std::vector<void*> wdev(ng);
+    std::vector<int> kt(ng);
+    for (int g = 0; g < ng; g++) {
+        const b200_tensor* a = nodes[g]->src[0];
+        const std::string key = weight_key(a);
+        const int64_t N = a->ne[1];
+        wdev[g] = pack_weight(b, key, a->type, a->data, a->on_device != 0, N * a->ne[2] * a->ne[3], K, &kt[g]);
+        if (!wdev[g]) return B200_E_CUDA;
+    }
+    // staging: src1 (if host), A16 + scales, per-member dst (if host), GEMM workspace
+    size_t need_io = staged_size(src1);
+    size_t need_out = 0, need_ws = 0;
+    for (int g = 0; g < ng; g++) {
+        const b200_tensor* d = nodes[g];
+        if (!d->on_device) need_out += (nbytes(d) + 255) & ~(size_t)255;
+        need_ws = std::max(need_ws, b200_gemm_packed_workspace_size(M, d->src[0]->ne[1], K));
+    }
+    const size_t a16_bytes = ((size_t)M * K * 2 + 255) & ~(size_t)255;
+    const size_t sc_bytes = ((size_t)M * 4 + 255) & ~(size_t)255;
+    need_ws = ((need_ws + 255) & ~(size_t)255) + a16_bytes + sc_bytes;
+    if (!grow(&b->io, &b->io_bytes, need_io + need_out, b->stream)) return B200_E_CUDA;
+    if (!grow(&b->ws, &b->ws_bytes, need_ws, b->stream)) return B200_E_CUDA;
+    size_t io_off = 0;
+    bool ok = true;
+    const char* a_base = static_cast<const char*>(stage_in(b, src1, &io_off, &ok));
+    if (!ok) return B200_E_CUDA;
+    std::vector<char*> d_base(ng);
+    for (int g = 0; g < ng; g++) {
+        if (nodes[g]->on_device) {
+            d_base[g] = static_cast<char*>(nodes[g]->data);
+        } else {
+            io_off = (io_off + 255) & ~(size_t)255;
+            d_base[g] = static_cast<char*>(b->io) + io_off;
+            io_off += nbytes(nodes[g]);
+        }
+    }
+    char* ws = static_cast<char*>(b->ws);
+    void* a16 = ws;
+    float* scales = reinterpret_cast<float*>(ws + a16_bytes);
+    void* gws = ws + a16_bytes + sc_bytes;
+    const size_t gws_bytes = b->ws_bytes - a16_bytes - sc_bytes;
+    for (int64_t i3 = 0; i3 < ne13; i3++) {
+        for (int64_t i2 = 0; i2 < ne12; i2++) {
+            const float* A = reinterpret_cast<const float*>(a_base + i3 * src1->nb[3] + i2 * src1->nb[2]);
+            int rc = b200_act_pack(A, (int64_t)(src1->nb[1] / 4), M, K, a16, scales, b->stream);
+            if (rc != B200_OK) return rc;
+            for (int g = 0; g < ng; g++) {
+                const b200_tensor* d = nodes[g];
+                const b200_tensor* a = d->src[0];
+                const int64_t N = a->ne[1];
+                const int64_t r2 = ne12 / a->ne[2], r3 = ne13 / a->ne[3];
+                const size_t wslab = b200_weight_packed_size(kt[g], N, K);
+                const char* W = static_cast<const char*>(wdev[g]) + ((i3 / r3) * a->ne[2] + (i2 / r2)) * wslab;
+                float* C = reinterpret_cast<float*>(d_base[g] + i3 * d->nb[3] + i2 * d->nb[2]);
+                rc = b200_gemm_packed(kt[g], W, N, K, a16, scales, M, C, (int64_t)(d->nb[1] / 4), gws, gws_bytes,
+                                      b->dev_err, b->stream);
+                if (rc != B200_OK) return rc;
+            }
+        }
+    }
+    for (int g = 0; g < ng; g++) {
+        if (!nodes[g]->on_device &&
+            cudaMemcpyAsync(nodes[g]->data, d_base[g], nbytes(nodes[g]), cudaMemcpyDeviceToHost, b->stream) != cudaSuccess)
+            return B200_E_CUDA;
+    }
+    if (!check_dev_err(b, "MUL_MAT")) return B200_E_DEVICE;
+    if (ng > 1) b->route_ops["fused"]++;
+    else b->route_ops[route_name(kt[0])]++;
+    return B200_OK;
+}
+
+// Fusable: a static 2-D weight of a kernel-native type feeding off a shared src1
+// (ggml-rocket.cpp:4928-4944). Quantized weights fuse too: the shared pack is free here.
+bool node_fusable(const b200_tensor* op) {
+    if (op->op != B200_OP_MUL_MAT) return false;
+    const b200_tensor* a = op->src[0];
+    const b200_tensor* bb = op->src[1];
+    return a->ne[2] == 1 && a->ne[3] == 1 && bb->ne[2] == 1 && bb->ne[3] == 1 && ggml_backend_b200_supports_op(op);
+}
+
+int do_mul_mat_id(b200_backend* b, b200_tensor* op) {
+    const b200_tensor* as = op->src[0];
+    const b200_tensor* bb = op->src[1];
+    const b200_tensor* ids = op->src[2];
+    const int64_t K = as->ne[0], N = as->ne[1], n_expert = as->ne[2];
+    const int64_t ne11 = bb->ne[1], n_used = ids->ne[0], n_tokens = ids->ne[1];
+    int kt = 0;
+    const std::string key = weight_key(as);
+    void* w = pack_weight(b, key, as->type, as->data, as->on_device != 0, N * n_expert, K, &kt);
+    if (!w) return B200_E_CUDA;
+    if (!key.empty() && !b->moe_seen[key]) {
+        b->moe_seen[key] = true;
+        b->moe_resident++;
+    } else if (key.empty()) {
+        b->moe_streamed++;
+    }
+    const size_t need_ws = b200_mul_mat_id_workspace_size(K, N, n_expert, n_used, n_tokens);
+    size_t need_io = staged_size(bb) + staged_size(ids) + (op->on_device ? 0 : ((nbytes(op) + 255) & ~(size_t)255));
+    if (!grow(&b->io, &b->io_bytes, need_io, b->stream)) return B200_E_CUDA;
+    if (!grow(&b->ws, &b->ws_bytes, need_ws, b->stream)) return B200_E_CUDA;
+    size_t io_off = 0;
+    bool ok = true;
+    const void* bd = stage_in(b, bb, &io_off, &ok);
+    const void* idd = stage_in(b, ids, &io_off, &ok);
+    if (!ok) return B200_E_CUDA;
+    char* dd;
+    if (op->on_device) {
+        dd = static_cast<char*>(op->data);
+    } else {
+        io_off = (io_off + 255) & ~(size_t)255;
+        dd = static_cast<char*>(b->io) + io_off;
+    }
+    int rc = b200_mul_mat_id(kt, w, K, N, n_expert, static_cast<const float*>(bd), (int64_t)bb->nb[1],
+                             (int64_t)bb->nb[2], ne11, static_cast<const int32_t*>(idd), (int64_t)ids->nb[0],
+                             (int64_t)ids->nb[1], n_used, n_tokens, reinterpret_cast<float*>(dd), (int64_t)op->nb[1],
+                             (int64_t)op->nb[2], b->ws, b->ws_bytes, b->dev_err, b->stream);
+    if (rc != B200_OK) return rc;
+    if (!op->on_device && cudaMemcpyAsync(op->data, dd, nbytes(op), cudaMemcpyDeviceToHost, b->stream) != cudaSuccess)
+        return B200_E_CUDA;
+    int h = 0;
+    cudaMemcpyAsync(&h, b->dev_err, sizeof(int), cudaMemcpyDeviceToHost, b->stream);
+    if (cudaStreamSynchronize(b->stream) != cudaSuccess) {
+        b->device_errors++;
+        return B200_E_CUDA;
+    }
+    if (h == B200_DEV_BAD_IDS) {
+        cudaMemsetAsync(b->dev_err, 0, sizeof(int), b->stream);
+        logf("E", "MUL_MAT_ID: an expert id outside [0, %lld)\n", (long long)n_expert);
+        return B200_E_BAD_IDS;
+    }
+    if (h != 0) {
+        cudaMemsetAsync(b->dev_err, 0, sizeof(int), b->stream);
+        b->device_errors++;
+        logf("E", "MUL_MAT_ID: device error word %d\n", h);
+        return B200_E_DEVICE;
+    }
+    b->route_ops["moe"]++;
+    return B200_OK;
+}
+
+int do_flash_attn(b200_backend* b, b200_tensor* op) {
+    const b200_tensor* q = op->src[0];
+    const b200_tensor* k = op->src[1];
+    const b200_tensor* v = op->src[2];
+    const b200_tensor* m = op->src[3];
+    const int D = (int)q->ne[0], T = (int)q->ne[1], H = (int)q->ne[2];
+    const int DV = (int)v->ne[0], KV = (int)k->ne[1], HK = (int)k->ne[2];
+    const float scale = op_param_f32(op, 0), max_bias = op_param_f32(op, 1), softcap = op_param_f32(op, 2);
+    size_t need_io = staged_size(q) + staged_size(k) + staged_size(v) + (m ? staged_size(m) : 0) +
+                     (op->on_device ? 0 : ((nbytes(op) + 255) & ~(size_t)255));
+    const size_t need_ws = b200_flash_attn_workspace_size(D, DV, T, H, KV, HK);
+    if (!grow(&b->io, &b->io_bytes, need_io, b->stream)) return B200_E_CUDA;
+    if (!grow(&b->ws, &b->ws_bytes, need_ws, b->stream)) return B200_E_CUDA;
+    size_t io_off = 0;
+    bool ok = true;
+    const void* qd = stage_in(b, q, &io_off, &ok);
+    const void* kd = stage_in(b, k, &io_off, &ok);
+    const void* vd = stage_in(b, v, &io_off, &ok);
+    const void* md = m ? stage_in(b, m, &io_off, &ok) : nullptr;
+    if (!ok) return B200_E_CUDA;
+    char* dd;
+    if (op->on_device) {
+        dd = static_cast<char*>(op->data);
+    } else {
+        io_off = (io_off + 255) & ~(size_t)255;
+        dd = static_cast<char*>(b->io) + io_off;
+    }
+    int rc = b200_flash_attn_ext(static_cast<const float*>(qd), (int64_t)q->nb[1], (int64_t)q->nb[2], kd,
+                                 (int64_t)k->nb[1], (int64_t)k->nb[2], vd, (int64_t)v->nb[1], (int64_t)v->nb[2], md,
+                                 m ? (int64_t)m->nb[1] : 0, reinterpret_cast<float*>(dd), D, DV, T, H, KV, HK, scale,
+                                 max_bias, softcap, b->ws, b->ws_bytes, b->dev_err, b->stream);
+    if (rc != B200_OK) return rc;
+    if (!op->on_device && cudaMemcpyAsync(op->data, dd, nbytes(op), cudaMemcpyDeviceToHost, b->stream) != cudaSuccess)
+        return B200_E_CUDA;
+    if (!check_dev_err(b, "FLASH_ATTN_EXT")) return B200_E_DEVICE;
+    b->route_ops["fa"]++;
+    return B200_OK;
+}
+
+}  // namespace
+
+// ================================================================================================
+// public C API
+// ================================================================================================
+
+extern "C" {
+
+const char* ggml_backend_b200_reg_name(void) { return "B200"; }
+
+int ggml_backend_b200_reg_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+int ggml_backend_b200_op_from_name(const char* name) {
+    if (!name) return B200_OP_OTHER;
+    static const struct { const char* n; int op; } map[] = {
+        {"NONE", B200_OP_NONE},         {"RESHAPE", B200_OP_RESHAPE},       {"VIEW", B200_OP_VIEW},
+        {"PERMUTE", B200_OP_PERMUTE},   {"TRANSPOSE", B200_OP_TRANSPOSE},   {"MUL_MAT", B200_OP_MUL_MAT},
+        {"MUL_MAT_ID", B200_OP_MUL_MAT_ID}, {"FLASH_ATTN_EXT", B200_OP_FLASH_ATTN_EXT},
+    };
+    for (const auto& e : map)
+        if (strcmp(name, e.n) == 0) return e.op;
+    return B200_OP_OTHER;
+}
+
+const char* ggml_backend_b200_device_name(int device) {
+    static char names[16][16];
+    if (device < 0 || device >= 16) return "B200";
+    snprintf(names[device], sizeof names[device], "B200_%d", device);
+    return names[device];
+}
+
+int ggml_backend_b200_device_description(int device, char* buf, size_t n) {
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, device) != cudaSuccess) return -1;
+    snprintf(buf, n, "%s (sm_%d%d, %d SMs)", p.name, p.major, p.minor, p.multiProcessorCount);
+    return 0;
+}
+
+int ggml_backend_b200_device_memory(int device, size_t* free_bytes, size_t* total_bytes) {
+    int cur = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess) return -1;
+    if (cur != device && cudaSetDevice(device) != cudaSuccess) return -1;
+    size_t f = 0, t = 0;
+    const cudaError_t e = cudaMemGetInfo(&f, &t);
+    if (cur != device) cudaSetDevice(cur);
+    if (e != cudaSuccess) return -1;
+    if (free_bytes) *free_bytes = f;
+    if (total_bytes) *total_bytes = t;
+    return 0;
+}
+
+b200_backend_t ggml_backend_b200_init(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) return nullptr;
+    auto* b = new b200_backend();
+    cudaGetDevice(&b->device);
+    return b;
+}
+
+void ggml_backend_b200_free(b200_backend_t b) {
+    if (!b) return;
+    if (b->dev_ready) {
+        cudaSetDevice(b->device);
+        cudaStreamSynchronize(b->stream);
+        for (auto& kv : b->cache) cudaFree(kv.second.dev);
+        for (void* p : b->transient) cudaFree(p);
+        cudaFree(b->ws);
+        cudaFree(b->io);
+        cudaFree(b->dev_err);
+        cudaStreamDestroy(b->stream);
+    }
+    b->magic = 0;
+    delete b;
+}
+
+bool ggml_backend_is_b200(const void* backend) {
+    return backend && static_cast<const b200_backend*>(backend)->magic == 0xB2000B20u;
+}
+
+void ggml_backend_b200_set_n_gpus(b200_backend_t b, int n) {
+    if (!b) return;
+    int c = n < 1 ? 1 : (n > 8 ? 8 : n);
+    if (c != n) logf("W", "set_n_gpus(%d) clamped to %d\n", n, c);
+    b->n_gpus = c;
+}
+
+void ggml_backend_b200_moe_stats(b200_backend_t b, long* n_resident, long* n_streamed) {
+    if (n_resident) *n_resident = b ? b->moe_resident : 0;
+    if (n_streamed) *n_streamed = b ? b->moe_streamed : 0;
+}
+
+long ggml_backend_b200_route_ops(b200_backend_t b, const char* route) {
+    if (!b) return 0;
+    std::lock_guard<std::mutex> lk(b->mu);
+    if (!route) {
+        long t = 0;
+        for (auto& kv : b->route_ops) t += kv.second;
+        return t;
+    }
+    auto it = b->route_ops.find(route);
+    return it == b->route_ops.end() ? 0 : it->second;
+}
+
+long ggml_backend_b200_cpu_fallbacks(b200_backend_t b) {
+    (void)b;
+    return 0;
+}
+
+long ggml_backend_b200_device_errors(b200_backend_t b) { return b ? b->device_errors : 0; }
+
+size_t ggml_backend_b200_weight_cache_bytes(b200_backend_t b, long* n_entries) {
+    if (!b) return 0;
+    if (n_entries) *n_entries = (long)b->cache.size();
+    return b->cache_bytes;
+}
+
+size_t ggml_backend_b200_weight_key(const b200_tensor* w, char* buf, size_t n) {
+    if (!w) return 0;
+    const std::string k = weight_key(w);
+    if (buf && n) {
+        const size_t c = std::min(n - 1, k.size());
+        memcpy(buf, k.data(), c);
+        buf[c] = 0;
+    }
+    return k.size();
+}
+
+void ggml_backend_b200_breaker_replay(const int* rcs, int n, int* attempted) {
+    Breaker br;
+    for (int i = 0; i < n; i++) {
+        const bool go = breaker_allow(br);
+        attempted[i] = go ? 1 : 0;
+        if (go) breaker_note(br, rcs[i], "replay");
+    }
+}
+
+int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes, int n) {
+    if (!b || (n > 0 && !nodes)) return B200_STATUS_FAILED;
+    std::lock_guard<std::mutex> lk(b->mu);
+    if (!ensure_device(b)) return B200_STATUS_FAILED;
+    cudaSetDevice(b->device);
+    const bool fuse = fuse_on();
+    std::vector<bool> done(n, false);
+    int status = B200_STATUS_SUCCESS;
+    for (int i = 0; i < n && status == B200_STATUS_SUCCESS; i++) {
+        b200_tensor* node = nodes[i];
+        if (done[i]) continue;
+        switch (node->op) {
+            case B200_OP_MUL_MAT: {
+                if (!ggml_backend_b200_supports_op(node)) {
+                    logf("E", "graph_compute: MUL_MAT %s was not claimed\n", node->name);
+                    status = B200_STATUS_FAILED;
+                    break;
+                }
+                std::vector<b200_tensor*> group{node};
+                std::vector<int> gidx{i};
+                if (fuse && node_fusable(node) && breaker_allow(b->brk_fused)) {
+                    for (int j = i + 1; j < n && group.size() < 8; j++) {
+                        b200_tensor* nj = nodes[j];
+                        if (!done[j] && nj->op == B200_OP_MUL_MAT && nj->src[1] == node->src[1] && node_fusable(nj)) {
+                            group.push_back(nj);
+                            gidx.push_back(j);
+                        }
+                    }
+                }
+                int rc = do_mul_mat_group(b, group.data(), (int)group.size());
+                if (group.size() > 1) breaker_note(b->brk_fused, rc, "fused MUL_MAT group");
+                if (rc != B200_OK && group.size() > 1) {
+                    // the fused group's optional route failed: run the members one by one
+                    rc = B200_OK;
+                    for (size_t g = 0; g < group.size() && rc == B200_OK; g++) rc = do_mul_mat_group(b, &group[g], 1);
+                }
+                if (rc != B200_OK) {
+                    logf("E", "graph_compute: MUL_MAT %s failed (%d)\n", node->name, rc);
+                    status = B200_STATUS_FAILED;
+                }
+                for (int g : gidx) done[g] = true;
+                break;
+            }
+            case B200_OP_MUL_MAT_ID: {
+                if (!ggml_backend_b200_supports_op(node)) {
+                    status = B200_STATUS_FAILED;
+                    break;
+                }
+                const int rc = do_mul_mat_id(b, node);
+                if (rc != B200_OK) {
+                    logf("E", "graph_compute: MUL_MAT_ID handler failed (%d)\n", rc);
+                    status = B200_STATUS_FAILED;
+                }
+                break;
+            }
+            case B200_OP_FLASH_ATTN_EXT: {
+                if (!ggml_backend_b200_supports_op(node)) {
+                    status = B200_STATUS_FAILED;
+                    break;
+                }
+                const int rc = do_flash_attn(b, node);
+                if (rc != B200_OK) {
+                    logf("E", "graph_compute: FLASH_ATTN_EXT handler failed (%d)\n", rc);
+                    status = B200_STATUS_FAILED;
+                }
+                break;
+            }
+            case B200_OP_NONE:
+            case B200_OP_RESHAPE:
+            case B200_OP_VIEW:
+            case B200_OP_PERMUTE:
+            case B200_OP_TRANSPOSE:
+                break;
+            default:
+                logf("E", "graph_compute: unsupported op in node %s\n", node->name);
+                status = B200_STATUS_FAILED;
+        }
+    }
+    if (cudaStreamSynchronize(b->stream) != cudaSuccess) status = B200_STATUS_FAILED;
+    for (void* p : b->transient) cudaFree(p);
+    b->transient.clear();
+    return status;
+}
+
+}  // extern "C"

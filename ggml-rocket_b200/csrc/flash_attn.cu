@@ -1,0 +1,629 @@
+// FLASH_ATTN_EXT prefill on sm_100a (the reference's ggml_backend_rocket_flash_attn,
+// ggml-rocket.cpp:5444-5691, without its gathers, host softmax or range fallback).
+//
+// Three kernels:
+//   q_pack     Q F32 [D, T, H] (strided) -> Q16 [H][T][D] fp16 holding scale*q, with a per-row
+//              power-of-two divisor for rows whose scaled values leave fp16's range; the
+//              divisor is multiplied back into that row's scores.
+//   mask_flags per (token block, 128-key block) of the F16 mask: all -inf (skipped), all zero
+//              (no mask loads), or mixed. Causal prefill skips ~half the key blocks.
+//   fa_kernel  one CTA per (group of GP query heads that share a KV head, TQ tokens) = 128 query
+//              rows. Per key block: S = Q.K^T by tcgen05 into one of two TMEM buffers; the 128
+//              softmax threads (one per row) read S from TMEM, keep the online max / sum in
+//              fp32, write P (fp16) to shared memory; O_blk = P.V by tcgen05 into TMEM, which
+//              the same threads fold into their fp32 output registers. K and V tiles arrive by
+//              TMA straight from the op's strided cache views, two stages deep.
+#include <cstdint>
+#include <cstring>
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "ggml-b200-kernels.h"
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace b200 {
+
+constexpr int FA_ROWS = 128;      // query rows per CTA (tcgen05 M)
+constexpr int FA_KB = 128;        // keys per block (tcgen05 N of Q.K^T, K of P.V)
+constexpr int FA_THREADS = 192;   // warp 0 TMA, warp 1 MMA, warps 2..5 softmax
+enum : uint8_t { MF_MIXED = 0, MF_ZERO = 1, MF_MASKED = 2 };
+
+struct FaArgs {
+    const float* qscale;       // [H*T] per-row divisor (1 unless out of fp16 range)
+    const uint16_t* mask;      // F16 mask or nullptr
+    int64_t m_stride;          // mask row stride, elements
+    bool mask_vec;             // rows 16-byte aligned: 16-byte loads
+    const uint8_t* flags;      // [n_tb][n_kvb]
+    float* dst;                // [T][H][DV]
+    int T, H, KV, HK, GP, TQ, n_hg, n_tb, n_kvb;
+    float softcap;
+    int* err;
+};
+
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// 32 columns of one TMEM lane per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
+// Shared-memory descriptor of an MN-major operand in 128-byte-swizzled rows: 64 MN elements per
+// 128-byte row, rows (K) 128 B apart, 8-row groups 1024 B apart, 64-element MN groups `lbo` apart.
+__device__ __forceinline__ uint64_t sdesc_mn_sw128(uint32_t addr, uint32_t lbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(2) << 61;
+    return d;
+}
+
+__host__ __device__ constexpr uint32_t idesc_f16_f32_bmn(int M, int N) {
+    return idesc_f16_f32(M, N) | (1u << 16);   // B operand MN-major
+}
+
+// 32 mask values (fp16 bits) of one row starting at key k0; keys at or past KV read as 0
+// (the score of such a key is forced to -inf separately).
+__device__ __forceinline__ void load_mask32(const uint16_t* mrow, int k0, int KV, bool vec, uint4 (&mv)[4]) {
+    if (vec && k0 + 32 <= KV) {
+        const uint4* mp = reinterpret_cast<const uint4*>(mrow + k0);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; q4++) mv[q4] = __ldg(mp + q4);
+    } else {
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+            const uint32_t lo = (k0 + e < KV) ? (uint32_t)__ldg(mrow + k0 + e) : 0u;
+            const uint32_t hi = (k0 + e + 1 < KV) ? (uint32_t)__ldg(mrow + k0 + e + 1) : 0u;
+            w[e >> 1] = lo | (hi << 16);
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 4; q4++) mv[q4] = make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Q pre-pass: one warp per (h, t) row.
+// ---------------------------------------------------------------------------------------------
+template <int D>
+__global__ void fa_q_pack_kernel(const float* __restrict__ q, int64_t q_nb1, int64_t q_nb2, int T, int H,
+                                 float scale, __half* __restrict__ q16, float* __restrict__ qscale) {
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= H * T) return;
+    const int h = row / T, t = row % T;
+    const float* src = reinterpret_cast<const float*>(reinterpret_cast<const char*>(q) + (int64_t)t * q_nb1 +
+                                                      (int64_t)h * q_nb2);
+    constexpr int PER = D / 32;
+    float x[PER];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        x[i] = scale * __ldg(src + lane * PER + i);
+        amax = fmaxf(amax, fabsf(x[i]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    float div = 1.0f, inv = 1.0f;
+    if (amax > 65504.0f && amax <= 3.0e38f) {
+        int e;
+        frexpf(amax / 65504.0f, &e);        // amax / 2^e <= 65504
+        div = ldexpf(1.0f, e);
+        inv = ldexpf(1.0f, -e);
+    }
+    __half* dst = q16 + ((int64_t)h * T + t) * D + lane * PER;
+#pragma unroll
+    for (int i = 0; i < PER; i += 2) {
+        const uint32_t w = pack_half2(x[i] * inv, x[i + 1] * inv);
+        *reinterpret_cast<uint32_t*>(dst + i) = w;
+    }
+    if (lane == 0) qscale[row] = div;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Mask flags: one 256-thread CTA per (token block, key block).
+// ---------------------------------------------------------------------------------------------
+__global__ void fa_mask_flags_kernel(const uint16_t* __restrict__ mask, int64_t m_stride, int T, int KV, int TQ,
+                                     int n_kvb, uint8_t* __restrict__ flags) {
+    const int tb = blockIdx.y, j = blockIdx.x;
+    const int key_seg = threadIdx.x & 7;          // 16 keys each
+    const int trow = threadIdx.x >> 3;            // 32 token rows per pass
+    bool all_masked = true, all_zero = true;
+    for (int tr = trow; tr < TQ; tr += 32) {
+        const int t = tb * TQ + tr;
+        if (t >= T) continue;
+        const uint16_t* mrow = mask + (int64_t)t * m_stride + (int64_t)j * FA_KB + key_seg * 16;
+        for (int i = 0; i < 16; i++) {
+            const int key = j * FA_KB + key_seg * 16 + i;
+            if (key >= KV) {
+                all_zero = false;
+                continue;
+            }
+            const uint16_t v = __ldg(mrow + i);
+            if (v != 0xFC00u) all_masked = false;                 // -inf
+            if ((v & 0x7FFFu) != 0) all_zero = false;            // +-0
+        }
+    }
+    const int am = __syncthreads_and(all_masked ? 1 : 0);
+    const int az = __syncthreads_and(all_zero ? 1 : 0);
+    if (threadIdx.x == 0) flags[(int64_t)tb * n_kvb + j] = am ? MF_MASKED : (az ? MF_ZERO : MF_MIXED);
+}
+
+// ---------------------------------------------------------------------------------------------
+// The attention kernel.
+// ---------------------------------------------------------------------------------------------
+template <int D, int DV>
+struct FaCfg {
+    static constexpr int Q_BYTES = FA_ROWS * D * 2;
+    static constexpr int K_BYTES = FA_KB * D * 2;
+    static constexpr int V_BYTES = FA_KB * DV * 2;
+    static constexpr int P_BYTES = FA_ROWS * FA_KB * 2;
+    static constexpr int OFF_Q = 0;
+    static constexpr int OFF_K = OFF_Q + Q_BYTES;
+    static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
+    static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
+    static constexpr int OFF_BAR = OFF_P + P_BYTES;
+    static constexpr int SMEM = OFF_BAR + 256 + 1024;
+    static constexpr uint32_t TMEM_COLS = 512;      // S0 | S1 | O
+    static constexpr uint32_t IDESC_S = idesc_f16_f32(FA_ROWS, FA_KB);
+    static constexpr uint32_t IDESC_O = idesc_f16_f32_bmn(FA_ROWS, DV);
+};
+
+template <int D, int DV>
+__global__ void __launch_bounds__(FA_THREADS, 1)
+fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+          const __grid_constant__ CUtensorMap tmV, const FaArgs args) {
+    using C = FaCfg<D, DV>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+    const uint32_t sb = smem_u32(smem);
+    const uint32_t bar = sb + C::OFF_BAR;
+    const uint32_t q_full = bar;
+    auto k_full = [&](int s) { return bar + 8u * (1 + s); };
+    auto k_empty = [&](int s) { return bar + 8u * (3 + s); };
+    auto v_full = [&](int s) { return bar + 8u * (5 + s); };
+    auto v_empty = [&](int s) { return bar + 8u * (7 + s); };
+    auto s_full = [&](int s) { return bar + 8u * (9 + s); };
+    auto s_empty = [&](int s) { return bar + 8u * (11 + s); };
+    const uint32_t p_full = bar + 8u * 13;
+    const uint32_t o_full = bar + 8u * 14;
+    const uint32_t o_empty = bar + 8u * 15;
+    const uint32_t drain = bar + 8u * 16;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 8 * 17);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 8 * 17 + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // heavier (later) token blocks first
+    const int tb = args.n_tb - 1 - (int)(blockIdx.x / args.n_hg);
+    const int hg = (int)(blockIdx.x % args.n_hg);
+    const int G = args.H / args.HK;
+    const int hk = (hg * args.GP) / G;
+    const uint8_t* flags = args.flags + (int64_t)tb * args.n_kvb;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < 2; s++) {
+            mbar_init(k_full(s), 1);
+            mbar_init(k_empty(s), 1);
+            mbar_init(v_full(s), 1);
+            mbar_init(v_empty(s), 1);
+            mbar_init(s_full(s), 1);
+            mbar_init(s_empty(s), 4);
+        }
+        mbar_init(p_full, 4);
+        mbar_init(o_full, 1);
+        mbar_init(o_empty, 4);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+            for (int c = 0; c < D / 64; c++)
+                tma_load_3d(sb + C::OFF_Q + c * (FA_ROWS * 128), &tmQ, q_full, c * 64, tb * args.TQ, hg * args.GP);
+            int i = 0;
+            bool ok = true;
+            int k_issued[2] = {-1, -1}, v_issued[2] = {-1, -1};
+            for (int j = 0; j < args.n_kvb && ok; j++) {
+                if (flags[j] == MF_MASKED) continue;
+                const int s = i & 1;
+                const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+                if (!mbar_wait(k_empty(s), ph ^ 1u, args.err, ERR_WAIT_PRODUCER, abort_flag)) { ok = false; break; }
+                k_issued[s] = (int)ph;
+                mbar_arrive_expect_tx(k_full(s), C::K_BYTES);
+                for (int c = 0; c < D / 64; c++)
+                    tma_load_3d(sb + C::OFF_K + s * C::K_BYTES + c * (FA_KB * 128), &tmK, k_full(s), c * 64, j * FA_KB, hk);
+                if (!mbar_wait(v_empty(s), ph ^ 1u, args.err, ERR_WAIT_PRODUCER, abort_flag)) { ok = false; break; }
+                v_issued[s] = (int)ph;
+                mbar_arrive_expect_tx(v_full(s), C::V_BYTES);
+                for (int c = 0; c < DV / 64; c++)
+                    tma_load_3d(sb + C::OFF_V + s * C::V_BYTES + c * (FA_KB * 128), &tmV, v_full(s), c * 64, j * FA_KB, hk);
+                i++;
+            }
+            if (!ok) {   // let every copy already issued land before the CTA exits
+                bool drained = mbar_drain(q_full, 0);
+                for (int s = 0; s < 2; s++) {
+                    if (k_issued[s] >= 0) drained &= mbar_drain(k_full(s), (uint32_t)k_issued[s]);
+                    if (v_issued[s] >= 0) drained &= mbar_drain(v_full(s), (uint32_t)v_issued[s]);
+                }
+                if (!drained) atomicCAS(args.err, 0, ERR_WAIT_DRAIN);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            bool ok = mbar_wait(q_full, 0, args.err, ERR_WAIT_MMA, abort_flag);
+            tc_fence_after();
+            int n_active = 0;
+            auto issue_pv = [&](int i) -> bool {
+                const int s = i & 1;
+                const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+                if (!mbar_wait(p_full, (uint32_t)i & 1u, args.err, ERR_WAIT_MMA, abort_flag)) return false;
+                if (!mbar_wait(v_full(s), ph, args.err, ERR_WAIT_MMA, abort_flag)) return false;
+                if (i > 0 && !mbar_wait(o_empty, (uint32_t)(i - 1) & 1u, args.err, ERR_WAIT_MMA, abort_flag)) return false;
+                tc_fence_after();
+                const uint32_t vb = sb + C::OFF_V + s * C::V_BYTES;
+#pragma unroll
+                for (int ks = 0; ks < FA_KB / 16; ks++) {
+                    const uint64_t a = sdesc_k_sw128(sb + C::OFF_P + (ks >> 2) * (FA_ROWS * 128) + (ks & 3) * 32);
+                    const uint64_t bdesc = sdesc_mn_sw128(vb + ks * 2048, FA_KB * 128);
+                    mma_f16(tmem + 256, a, bdesc, C::IDESC_O, ks > 0 ? 1u : 0u);
+                }
+                mma_commit(o_full);
+                mma_commit(v_empty(s));
+                return true;
+            };
+            for (int j = 0; j < args.n_kvb && ok; j++) {
+                if (flags[j] == MF_MASKED) continue;
+                const int i = n_active;
+                const int s = i & 1;
+                const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+                if (!mbar_wait(k_full(s), ph, args.err, ERR_WAIT_MMA, abort_flag)) { ok = false; break; }
+                if (!mbar_wait(s_empty(s), ph ^ 1u, args.err, ERR_WAIT_MMA, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t kb = sb + C::OFF_K + s * C::K_BYTES;
+#pragma unroll
+                for (int ks = 0; ks < D / 16; ks++) {
+                    const uint64_t a = sdesc_k_sw128(sb + C::OFF_Q + (ks >> 2) * (FA_ROWS * 128) + (ks & 3) * 32);
+                    const uint64_t bdesc = sdesc_k_sw128(kb + (ks >> 2) * (FA_KB * 128) + (ks & 3) * 32);
+                    mma_f16(tmem + (uint32_t)(s * FA_KB), a, bdesc, C::IDESC_S, ks > 0 ? 1u : 0u);
+                }
+                mma_commit(s_full(s));
+                mma_commit(k_empty(s));
+                n_active++;
+                if (i > 0 && !issue_pv(i - 1)) { ok = false; break; }
+            }
+            if (ok && n_active > 0) issue_pv(n_active - 1);
+            mma_commit(drain);
+            if (!mbar_drain(drain, 0)) atomicCAS(args.err, 0, ERR_WAIT_DRAIN);
+        }
+    } else {
+        // ---------------- softmax / output (128 threads, one query row each) ----------------
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const int g = r / args.TQ, tq = r % args.TQ;
+        const int h = hg * args.GP + g;
+        const int t = tb * args.TQ + tq;
+        const bool row_valid = t < args.T;
+        const float qs = row_valid ? __ldg(args.qscale + (int64_t)h * args.T + t) : 1.0f;
+        const uint16_t* mrow = (args.mask && row_valid) ? args.mask + (int64_t)t * args.m_stride : nullptr;
+        const float LOG2E = 1.4426950408889634f;
+        const float softcap = args.softcap;
+        const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+        float o[DV];
+#pragma unroll
+        for (int c = 0; c < DV; c++) o[c] = 0.0f;
+        float m = -INFINITY, l = 0.0f;
+        int i = 0;
+        bool ok = true;
+        auto score = [&](float raw, int key, uint16_t mbits, bool use_mask) -> float {
+            float s = raw * qs;
+            if (softcap != 0.0f) s = softcap * tanhf(s / softcap);
+            if (key >= args.KV) return -INFINITY;
+            if (use_mask) s += __half2float(__ushort_as_half(mbits));
+            return s;
+        };
+        for (int j = 0; j < args.n_kvb && ok; j++) {
+            const uint8_t fl = flags[j];
+            if (fl == MF_MASKED) continue;
+            const bool use_mask = (fl == MF_MIXED) && (mrow != nullptr);
+            const int s = i & 1;
+            const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+            if (!mbar_wait(s_full(s), ph, args.err, ERR_WAIT_EPILOGUE, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sbase = tmem + lane_base + (uint32_t)(s * FA_KB);
+            // pass 1: the block's row max
+            float bmax = -INFINITY;
+#pragma unroll 1
+            for (int c0 = 0; c0 < FA_KB; c0 += 32) {
+                uint32_t rv[32];
+                tmem_ld32(sbase + c0, rv);
+                tmem_ld_wait();
+                uint4 mv[4];
+                if (use_mask) load_mask32(mrow, j * FA_KB + c0, args.KV, args.mask_vec, mv);
+#pragma unroll
+                for (int e = 0; e < 32; e++) {
+                    const uint32_t mw = use_mask ? (&mv[e >> 3].x)[(e & 7) >> 1] : 0u;
+                    const uint16_t mb = (uint16_t)((e & 1) ? (mw >> 16) : (mw & 0xFFFFu));
+                    bmax = fmaxf(bmax, score(__uint_as_float(rv[e]), j * FA_KB + c0 + e, mb, use_mask));
+                }
+            }
+            const float m_new = fmaxf(m, bmax);
+            const float m_use = (m_new == -INFINITY) ? 0.0f : m_new;
+            const float alpha = (m == -INFINITY) ? 0.0f : ex2_approx((m - m_use) * LOG2E);
+            // fold the previous block's P.V into the registers, then rescale
+            if (i > 0) {
+                if (!mbar_wait(o_full, (uint32_t)(i - 1) & 1u, args.err, ERR_WAIT_EPILOGUE, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int c0 = 0; c0 < DV; c0 += 32) {
+                    uint32_t ov[32];
+                    tmem_ld32(tmem + lane_base + 256u + (uint32_t)c0, ov);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 32; e++) o[c0 + e] += __uint_as_float(ov[e]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(o_empty);
+            }
+#pragma unroll
+            for (int c = 0; c < DV; c++) o[c] *= alpha;
+            l *= alpha;
+            // pass 2: P = exp(S - m) to shared memory (fp16, 128-byte swizzled, K-major)
+            const float mb2 = m_use * LOG2E;
+#pragma unroll 1
+            for (int c0 = 0; c0 < FA_KB; c0 += 32) {
+                uint32_t rv[32];
+                tmem_ld32(sbase + c0, rv);
+                tmem_ld_wait();
+                uint4 mv[4];
+                if (use_mask) load_mask32(mrow, j * FA_KB + c0, args.KV, args.mask_vec, mv);
+                uint32_t pw[16];
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    float p2[2];
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        const int ee = e + u;
+                        const uint32_t mw = use_mask ? (&mv[ee >> 3].x)[(ee & 7) >> 1] : 0u;
+                        const uint16_t mbits = (uint16_t)((ee & 1) ? (mw >> 16) : (mw & 0xFFFFu));
+                        const float sc = score(__uint_as_float(rv[ee]), j * FA_KB + c0 + ee, mbits, use_mask);
+                        p2[u] = (sc == -INFINITY) ? 0.0f : ex2_approx(fmaf(sc, LOG2E, -mb2));
+                        l += p2[u];
+                    }
+                    pw[e >> 1] = pack_half2(p2[0], p2[1]);
+                }
+                // keys c0..c0+31 -> P chunk (c0 / 64), 16-byte units ((c0 % 64) / 8) .. +3
+                const uint32_t pchunk = sb + C::OFF_P + (uint32_t)(c0 >> 6) * (FA_ROWS * 128);
+                const uint32_t u0 = (uint32_t)((c0 & 63) >> 3);
+#pragma unroll
+                for (int u = 0; u < 4; u++)
+                    st_shared_v4(pchunk + sw128_offset((uint32_t)r, u0 + u), pw[4 * u], pw[4 * u + 1], pw[4 * u + 2],
+                                 pw[4 * u + 3]);
+            }
+            tc_fence_before();
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(s_empty(s));
+                mbar_arrive(p_full);
+            }
+            m = m_new;
+            i++;
+        }
+        if (ok && i > 0) {
+            if (mbar_wait(o_full, (uint32_t)(i - 1) & 1u, args.err, ERR_WAIT_EPILOGUE, abort_flag)) {
+                tc_fence_after();
+#pragma unroll
+                for (int c0 = 0; c0 < DV; c0 += 32) {
+                    uint32_t ov[32];
+                    tmem_ld32(tmem + lane_base + 256u + (uint32_t)c0, ov);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 32; e++) o[c0 + e] += __uint_as_float(ov[e]);
+                }
+            }
+        }
+        if (row_valid) {
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            float4* out = reinterpret_cast<float4*>(args.dst + ((int64_t)t * args.H + h) * DV);
+#pragma unroll
+            for (int c = 0; c < DV; c += 4) out[c >> 2] = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------------------------
+
+static bool make_tmap_3d_f16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t nb1,
+                             uint64_t nb2, uint32_t b0, uint32_t b1, uint32_t b2);
+
+struct FaLayout {
+    int GP, TQ, n_hg, n_tb, n_kvb;
+    size_t q16_off, qs_off, flags_off, total;
+};
+
+static FaLayout fa_layout(int D, int T, int H, int KV, int HK) {
+    FaLayout L{};
+    const int G = H / HK;
+    int gp = 1;
+    while (gp * 2 <= 16 && G % (gp * 2) == 0) gp *= 2;
+    L.GP = gp;
+    L.TQ = FA_ROWS / gp;
+    L.n_hg = H / gp;
+    L.n_tb = (T + L.TQ - 1) / L.TQ;
+    L.n_kvb = (KV + FA_KB - 1) / FA_KB;
+    auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    L.q16_off = 0;
+    L.qs_off = al((size_t)H * T * D * 2);
+    L.flags_off = L.qs_off + al((size_t)H * T * 4);
+    L.total = L.flags_off + al((size_t)L.n_tb * L.n_kvb);
+    return L;
+}
+
+template <int D, int DV>
+static cudaError_t launch_fa(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const FaArgs& a,
+                             int grid, cudaStream_t st) {
+    using C = FaCfg<D, DV>;
+    static bool set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(fa_kernel<D, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) return e;
+        set[dev] = true;
+    }
+    fa_kernel<D, DV><<<grid, FA_THREADS, C::SMEM, st>>>(tq, tk, tv, a);
+    return cudaGetLastError();
+}
+
+int flash_attn_impl(const float* q, int64_t q_nb1, int64_t q_nb2, const void* k, int64_t k_nb1, int64_t k_nb2,
+                    const void* v, int64_t v_nb1, int64_t v_nb2, const void* mask, int64_t m_nb1, float* dst, int D,
+                    int DV, int T, int H, int KV, int HK, float scale, float max_bias, float softcap, void* workspace,
+                    size_t ws_bytes, int* dev_err, cudaStream_t st) {
+    if (!q || !k || !v || !dst || !dev_err || T <= 0 || H <= 0 || KV <= 0 || HK <= 0) return B200_E_INVALID;
+    if (H % HK != 0 || max_bias != 0.0f) return B200_E_UNSUPPORTED;
+    if (!((D == 64 || D == 128) && (DV == 64 || DV == 128))) return B200_E_UNSUPPORTED;
+    if ((k_nb1 | k_nb2 | v_nb1 | v_nb2) % 16 != 0) return B200_E_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(dst)) & 15u)
+        return B200_E_UNSUPPORTED;
+    if (mask && ((m_nb1 % 2) != 0 || (reinterpret_cast<uintptr_t>(mask) & 1u))) return B200_E_UNSUPPORTED;
+    const FaLayout L = fa_layout(D, T, H, KV, HK);
+    if (!workspace || ws_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255u)) return B200_E_WORKSPACE;
+    char* ws = static_cast<char*>(workspace);
+    __half* q16 = reinterpret_cast<__half*>(ws + L.q16_off);
+    float* qs = reinterpret_cast<float*>(ws + L.qs_off);
+    uint8_t* flags = reinterpret_cast<uint8_t*>(ws + L.flags_off);
+
+    {
+        const int rows = H * T;
+        const int blocks = (rows * 32 + 255) / 256;
+        if (D == 64) fa_q_pack_kernel<64><<<blocks, 256, 0, st>>>(q, q_nb1, q_nb2, T, H, scale, q16, qs);
+        else fa_q_pack_kernel<128><<<blocks, 256, 0, st>>>(q, q_nb1, q_nb2, T, H, scale, q16, qs);
+        if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
+    }
+    if (mask) {
+        dim3 grid(L.n_kvb, L.n_tb);
+        fa_mask_flags_kernel<<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(mask), m_nb1 / 2, T, KV, L.TQ, L.n_kvb,
+                                                   flags);
+    } else {
+        cudaMemsetAsync(flags, MF_ZERO, (size_t)L.n_tb * L.n_kvb, st);
+    }
+    if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
+
+    CUtensorMap tq, tk, tv;
+    if (!make_tmap_3d_f16(&tq, q16, D, T, H, (uint64_t)D * 2, (uint64_t)T * D * 2, 64, L.TQ, L.GP)) return B200_E_CUDA;
+    if (!make_tmap_3d_f16(&tk, k, D, KV, HK, k_nb1, k_nb2, 64, FA_KB, 1)) return B200_E_CUDA;
+    if (!make_tmap_3d_f16(&tv, v, DV, KV, HK, v_nb1, v_nb2, 64, FA_KB, 1)) return B200_E_CUDA;
+    FaArgs a{};
+    a.qscale = qs;
+    a.mask = static_cast<const uint16_t*>(mask);
+    a.m_stride = m_nb1 / 2;
+    a.mask_vec = mask && (m_nb1 % 16) == 0 && (reinterpret_cast<uintptr_t>(mask) & 15u) == 0;
+    a.flags = flags;
+    a.dst = dst;
+    a.T = T;
+    a.H = H;
+    a.KV = KV;
+    a.HK = HK;
+    a.GP = L.GP;
+    a.TQ = L.TQ;
+    a.n_hg = L.n_hg;
+    a.n_tb = L.n_tb;
+    a.n_kvb = L.n_kvb;
+    a.softcap = softcap;
+    a.err = dev_err;
+    const int grid = L.n_hg * L.n_tb;
+    cudaError_t e;
+    if (D == 128 && DV == 128) e = launch_fa<128, 128>(tq, tk, tv, a, grid, st);
+    else if (D == 64 && DV == 64) e = launch_fa<64, 64>(tq, tk, tv, a, grid, st);
+    else if (D == 128 && DV == 64) e = launch_fa<128, 64>(tq, tk, tv, a, grid, st);
+    else e = launch_fa<64, 128>(tq, tk, tv, a, grid, st);
+    return e == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
+}  // namespace b200
+
+// The 3-D fp16 tensor map [d2][d1][d0] with byte strides nb1, nb2 and a 128-byte-swizzled box.
+namespace b200 {
+using EncodeTiledFn3 = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static bool make_tmap_3d_f16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t nb1,
+                             uint64_t nb2, uint32_t b0, uint32_t b1, uint32_t b2) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    static EncodeTiledFn3 fn = nullptr;
+    if (!fn) {
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) != cudaSuccess ||
+            qr != cudaDriverEntryPointSuccess)
+            return false;
+        fn = reinterpret_cast<EncodeTiledFn3>(p);
+    }
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {nb1, nb2};
+    cuuint32_t box[3] = {b0, b1, b2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace b200
+
+extern "C" {
+
+size_t b200_flash_attn_workspace_size(int D, int DV, int T, int H, int KV, int HK) {
+    (void)DV;
+    if (T <= 0 || H <= 0 || KV <= 0 || HK <= 0 || H % HK) return 0;
+    return b200::fa_layout(D, T, H, KV, HK).total;
+}
+
+int b200_flash_attn_ext(const float* q, int64_t q_nb1, int64_t q_nb2, const void* k, int64_t k_nb1, int64_t k_nb2,
+                        const void* v, int64_t v_nb1, int64_t v_nb2, const void* mask, int64_t m_nb1, float* dst,
+                        int D, int DV, int T, int H, int KV, int HK, float scale, float max_bias, float softcap,
+                        void* workspace, size_t workspace_bytes, int* dev_err, void* stream) {
+    return b200::flash_attn_impl(q, q_nb1, q_nb2, k, k_nb1, k_nb2, v, v_nb1, v_nb2, mask, m_nb1, dst, D, DV, T, H, KV,
+                                 HK, scale, max_bias, softcap, workspace, workspace_bytes, dev_err,
+                                 static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

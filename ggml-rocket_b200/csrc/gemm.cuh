@@ -42,6 +42,18 @@ struct GemmArgs {
     int M, N, K;
     int n_tiles_n, n_tiles_t, splits, kb_per_split, nkb, num_units;
     int* err;                  // device error word
+    // grouped (MUL_MAT_ID) mode: the token rows are sorted by expert; expert e owns rows
+    // [g_off[e], g_off[e+1]) of A16 and weight rows [e*N, (e+1)*N) of the packed stack.
+    const int32_t* g_off;          // [n_expert + 1]
+    const int32_t* g_tile_start;   // [n_expert + 1] prefix of ceil(rows_e / BT)
+    const int32_t* g_slot;         // sorted row -> expert slot
+    const int32_t* g_tok;          // sorted row -> token
+    int n_expert;
+    int64_t d_nb1, d_nb2;          // dst strides over (slot, token), bytes
+};
+
+struct UnitCoords {
+    int t0, t_end, n0, wrow0, ks, kb0, kb1;
 };
 
 template <int BT, int WT>
@@ -58,15 +70,7 @@ struct GemmCfg {
     static constexpr uint32_t IDESC = idesc_f16_f32(GEMM_BN, BT);
 };
 
-__device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity) {
-    const uint64_t t0 = globaltimer();
-    while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer() - t0 > B200_WAIT_LIMIT_NS) return false;
-    }
-    return true;
-}
-
-template <int BT, int WT>
+template <int BT, int WT, bool GROUPED>
 __global__ void __launch_bounds__(GemmCfg<BT, WT>::THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
             const GemmArgs args) {
@@ -114,15 +118,40 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     const uint32_t tmem_base = *tmem_slot;
 
     const int ntt = args.n_tiles_t, ntn = args.n_tiles_n;
-    auto unit_coords = [&](int u, int& t0, int& n0, int& ks, int& kb0, int& kb1) {
-        const int tt = u % ntt;
-        const int rest = u / ntt;
-        const int nt = rest % ntn;
-        ks = rest / ntn;
-        t0 = tt * BT;
-        n0 = nt * GEMM_BN;
-        kb0 = ks * args.kb_per_split;
-        kb1 = min(args.nkb, kb0 + args.kb_per_split);
+    int num_units = args.num_units;
+    if constexpr (GROUPED) num_units = __ldg(args.g_tile_start + args.n_expert) * ntn;
+    auto unit_coords = [&](int u) {
+        UnitCoords c;
+        if constexpr (GROUPED) {
+            const int tg = u / ntn;
+            const int nt = u % ntn;
+            int lo = 0, hi = args.n_expert;            // last e with tile_start[e] <= tg
+            while (hi - lo > 1) {
+                const int mid = (lo + hi) >> 1;
+                if (__ldg(args.g_tile_start + mid) <= tg) lo = mid;
+                else hi = mid;
+            }
+            const int e = lo;
+            c.t0 = __ldg(args.g_off + e) + (tg - __ldg(args.g_tile_start + e)) * BT;
+            c.t_end = __ldg(args.g_off + e + 1);
+            c.n0 = nt * GEMM_BN;
+            c.wrow0 = e * args.N + c.n0;
+            c.ks = 0;
+            c.kb0 = 0;
+            c.kb1 = args.nkb;
+        } else {
+            const int tt = u % ntt;
+            const int rest = u / ntt;
+            const int nt = rest % ntn;
+            c.ks = rest / ntn;
+            c.t0 = tt * BT;
+            c.t_end = args.M;
+            c.n0 = nt * GEMM_BN;
+            c.wrow0 = c.n0;
+            c.kb0 = c.ks * args.kb_per_split;
+            c.kb1 = min(args.nkb, c.kb0 + args.kb_per_split);
+        }
+        return c;
     };
 
     if (warp == 0) {
@@ -134,15 +163,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 #pragma unroll
             for (int s = 0; s < STAGES; s++) issued_phase[s] = -1;
             bool ok = true;
-            for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x) {
-                int t0, n0, ks, kb0, kb1;
-                unit_coords(u, t0, n0, ks, kb0, kb1);
-                for (int kb = kb0; kb < kb1; kb++) {
+            for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+                const UnitCoords uc = unit_coords(u);
+                for (int kb = uc.kb0; kb < uc.kb1; kb++) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u, args.err, ERR_WAIT_PRODUCER, abort_flag)) { ok = false; break; }
                     const uint32_t sa = sbase + stage * C::STAGE_BYTES;
                     mbar_arrive_expect_tx(full_bar(stage), C::QUANT ? C::A_BYTES : C::A_BYTES + C::W_BYTES);
-                    tma_load_2d(sa, &tmA, full_bar(stage), kb * GEMM_BK, t0);
-                    if (!C::QUANT) tma_load_2d(sa + C::A_BYTES, &tmW, full_bar(stage), kb * GEMM_BK, n0);
+                    tma_load_2d(sa, &tmA, full_bar(stage), kb * GEMM_BK, uc.t0);
+                    if (!C::QUANT) tma_load_2d(sa + C::A_BYTES, &tmW, full_bar(stage), kb * GEMM_BK, uc.wrow0);
                     issued_phase[stage] = (int)phase;
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
@@ -161,9 +189,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             uint32_t phase = 0;
             int lt = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x, lt++) {
-                int t0, n0, ks, kb0, kb1;
-                unit_coords(u, t0, n0, ks, kb0, kb1);
+            for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, lt++) {
+                const UnitCoords uc = unit_coords(u);
+                const int kb0 = uc.kb0, kb1 = uc.kb1;
                 const int acc = lt & 1;
                 const uint32_t aphase = (uint32_t)(lt >> 1) & 1u;
                 if (!mbar_wait(tempty_bar(acc), aphase ^ 1u, args.err, ERR_WAIT_MMA, abort_flag)) { ok = false; break; }
@@ -193,29 +221,34 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         // ---------------- epilogue ----------------
         const int q = warp & 3;                       // TMEM lane quadrant this warp may read
         int lt = 0;
-        for (int u = blockIdx.x; u < args.num_units; u += gridDim.x, lt++) {
-            int t0, n0, ks, kb0, kb1;
-            unit_coords(u, t0, n0, ks, kb0, kb1);
+        for (int u = blockIdx.x; u < num_units; u += gridDim.x, lt++) {
+            const UnitCoords uc = unit_coords(u);
             const int acc = lt & 1;
             const uint32_t aphase = (uint32_t)(lt >> 1) & 1u;
             if (!mbar_wait(tfull_bar(acc), aphase, args.err, ERR_WAIT_EPILOGUE, abort_flag)) break;
             tc_fence_after();
-            const int n = n0 + 32 * q + lane;
-            float* obase = args.out + (size_t)ks * args.split_stride;
+            const int n = uc.n0 + 32 * q + lane;
+            float* obase = args.out + (size_t)uc.ks * args.split_stride;
             const bool scaled = args.splits == 1;
             for (int c0 = 0; c0 < BT; c0 += 16) {
-                if (t0 + c0 >= args.M) break;
+                if (uc.t0 + c0 >= uc.t_end) break;
                 uint32_t r[16];
                 tmem_ld16(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BT + c0), r);
                 tmem_ld_wait();
                 if (n < args.N) {
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
-                        const int t = t0 + c0 + j;
-                        if (t < args.M) {
+                        const int t = uc.t0 + c0 + j;
+                        if (t < uc.t_end) {
                             float v = __uint_as_float(r[j]);
                             if (scaled) v *= __ldg(args.scales + t);
-                            obase[(size_t)t * args.ldo + n] = v;
+                            if constexpr (GROUPED) {
+                                char* drow = reinterpret_cast<char*>(args.out) + (int64_t)__ldg(args.g_tok + t) * args.d_nb2 +
+                                             (int64_t)__ldg(args.g_slot + t) * args.d_nb1;
+                                reinterpret_cast<float*>(drow)[n] = v;
+                            } else {
+                                obase[(size_t)t * args.ldo + n] = v;
+                            }
                         }
                     }
                 }
@@ -231,13 +264,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x) {
-                int t0, n0, ks, kb0, kb1;
-                unit_coords(u, t0, n0, ks, kb0, kb1);
-                const int n = n0 + r;
-                const uint8_t* wrow = args.w + (size_t)n * args.w_row_bytes;
-                const uint16_t* drow = args.wd ? args.wd + (size_t)n * args.wd_row_elems : nullptr;
-                for (int kb = kb0; kb < kb1; kb++) {
+            for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+                const UnitCoords uc = unit_coords(u);
+                const int n = uc.n0 + r;
+                const int64_t wr = (int64_t)uc.wrow0 + r;
+                const uint8_t* wrow = args.w + (size_t)wr * args.w_row_bytes;
+                const uint16_t* drow = args.wd ? args.wd + (size_t)wr * args.wd_row_elems : nullptr;
+                for (int kb = uc.kb0; kb < uc.kb1; kb++) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u, args.err, ERR_WAIT_DEQUANT, abort_flag)) { ok = false; break; }
                     uint32_t h[32];
                     if (n < args.N) {

@@ -4,6 +4,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace b200 {
@@ -16,5 +17,10 @@ bool weight_type_supported(int type, int64_t K);
 int mul_mat_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const float* src1, int64_t lda, int64_t M,
                  float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t st);
 size_t mul_mat_workspace(int64_t M, int64_t N, int64_t K);
+int act_pack_impl(const float* src1, int64_t lda, int64_t M, int64_t K, __half* a16, float* scales, cudaStream_t st);
+int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int64_t n_expert, const __half* a16,
+                      const float* scales, int64_t rows, int bt, const int32_t* off, const int32_t* tile_start,
+                      const int32_t* slot, const int32_t* tok, float* dst, int64_t d_nb1, int64_t d_nb2, int* dev_err,
+                      cudaStream_t st);
 
 }  // namespace b200

@@ -1,0 +1,246 @@
+// MUL_MAT_ID on sm_100a (the reference's ggml_backend_rocket_mul_mat_id,
+// ggml-rocket.cpp:6692-6944), with no host round trip:
+//   route      the counting sort of (slot, token) rows by expert id (ggml-rocket.cpp:6706-6732),
+//              stable in token-major order like the reference's, plus the grouped GEMM's tile
+//              table (per-expert prefix of ceil(rows / token tile)); a bad id aborts the op
+//   gather     row r of the sorted order -> b[:, slot % ne11, tok], packed to fp16 with its
+//              per-row scale (the reference's gather + pack, :6790-6800 / :1451-1475)
+//   grouped    the tcgen05 GEMM of gemm.cuh over every (expert, token tile, weight tile) unit the
+//              table lists, whose epilogue scatters each row straight to dst[:, slot, tok]
+#include <cstdint>
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "ggml-b200-kernels.h"
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace b200 {
+
+constexpr int ROUTE_THREADS = 1024;
+
+// One CTA. Dynamic shared memory: cnt[E], base[E], wcnt[32][E] (ints).
+__global__ void __launch_bounds__(ROUTE_THREADS) moe_route_kernel(const int32_t* __restrict__ ids, int64_t ids_nb0,
+                                                                 int64_t ids_nb1, int n_used, int n_tokens, int E,
+                                                                 int bt, int32_t* __restrict__ off,
+                                                                 int32_t* __restrict__ tile_start,
+                                                                 int32_t* __restrict__ slot, int32_t* __restrict__ tok,
+                                                                 int* err) {
+    extern __shared__ int sm[];
+    int* cnt = sm;
+    int* base = sm + E;
+    int* wcnt = sm + 2 * E;
+    const int R = n_used * n_tokens;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int e = threadIdx.x; e < E; e += ROUTE_THREADS) cnt[e] = 0;
+    for (int i = threadIdx.x; i < 32 * E; i += ROUTE_THREADS) wcnt[i] = 0;
+    __syncthreads();
+    auto id_at = [&](int r) {
+        const int t = r / n_used, e = r % n_used;
+        return __ldg(reinterpret_cast<const int32_t*>(reinterpret_cast<const char*>(ids) + (int64_t)t * ids_nb1 +
+                                                      (int64_t)e * ids_nb0));
+    };
+    int bad = 0;
+    for (int r = threadIdx.x; r < R; r += ROUTE_THREADS) {
+        const int x = id_at(r);
+        if (x < 0 || x >= E) bad = 1;
+        else atomicAdd(&cnt[x], 1);
+    }
+    if (__syncthreads_or(bad)) {
+        if (threadIdx.x == 0) atomicCAS(err, 0, B200_DEV_BAD_IDS);
+        for (int e = threadIdx.x; e <= E; e += ROUTE_THREADS) {
+            off[e] = 0;
+            tile_start[e] = 0;
+        }
+        return;
+    }
+    if (threadIdx.x == 0) {
+        int acc = 0, tacc = 0;
+        for (int e = 0; e < E; e++) {
+            off[e] = acc;
+            base[e] = acc;
+            tile_start[e] = tacc;
+            acc += cnt[e];
+            tacc += (cnt[e] + bt - 1) / bt;
+        }
+        off[E] = acc;
+        tile_start[E] = tacc;
+    }
+    __syncthreads();
+    const unsigned lt_mask = (1u << lane) - 1u;
+    for (int r0 = 0; r0 < R; r0 += ROUTE_THREADS) {
+        const int r = r0 + threadIdx.x;
+        const int x = r < R ? id_at(r) : -1;
+        const unsigned same = __match_any_sync(0xffffffffu, x);
+        const int rank = __popc(same & lt_mask);
+        if (x >= 0 && rank == 0) wcnt[warp * E + x] = __popc(same);
+        __syncthreads();
+        if (x >= 0) {
+            int prefix = 0;
+            for (int w = 0; w < warp; w++) prefix += wcnt[w * E + x];
+            const int p = base[x] + prefix + rank;
+            slot[p] = r % n_used;
+            tok[p] = r / n_used;
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < E; e += ROUTE_THREADS) {
+            int s = 0;
+            for (int w = 0; w < 32; w++) {
+                s += wcnt[w * E + e];
+                wcnt[w * E + e] = 0;
+            }
+            base[e] += s;
+        }
+        __syncthreads();
+    }
+}
+
+// Row r of the sorted order: gather b[:, slot % ne11, tok] and pack it like act_pack_kernel.
+template <int V>
+__global__ void __launch_bounds__(256) moe_gather_pack_kernel(const float* __restrict__ b, int64_t b_nb1,
+                                                              int64_t b_nb2, int ne11, int K,
+                                                              const int32_t* __restrict__ slot,
+                                                              const int32_t* __restrict__ tok,
+                                                              const int32_t* __restrict__ off_total,
+                                                              __half* __restrict__ a16, float* __restrict__ scales) {
+    __shared__ float red[8];
+    const int r = blockIdx.x;
+    if (r >= __ldg(off_total)) return;   // a bad-id op has no rows
+    const int s = __ldg(slot + r), t = __ldg(tok + r);
+    const float4* row = reinterpret_cast<const float4*>(reinterpret_cast<const char*>(b) + (int64_t)t * b_nb2 +
+                                                        (int64_t)(s % ne11) * b_nb1);
+    uint2* out = reinterpret_cast<uint2*>(a16 + (int64_t)r * K);
+    const int n4 = K / 4;
+    float4 v[V];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; i++) {
+        const int idx = threadIdx.x + i * 256;
+        v[i] = idx < n4 ? __ldg(row + idx) : make_float4(0.f, 0.f, 0.f, 0.f);
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; w++) amax = fmaxf(amax, red[w]);
+    const float sc = amax > 0.0f ? amax : 1.0f;
+    const float inv = __frcp_rn(sc);
+    if (threadIdx.x == 0) scales[r] = sc;
+#pragma unroll
+    for (int i = 0; i < V; i++) {
+        const int idx = threadIdx.x + i * 256;
+        if (idx < n4) {
+            uint2 w;
+            w.x = pack_half2(__fmul_rn(v[i].x, inv), __fmul_rn(v[i].y, inv));
+            w.y = pack_half2(__fmul_rn(v[i].z, inv), __fmul_rn(v[i].w, inv));
+            out[idx] = w;
+        }
+    }
+}
+
+struct MoeLayout {
+    size_t off, tiles, slot, tok, a16, scales, total;
+};
+
+static MoeLayout moe_layout(int64_t K, int64_t n_expert, int64_t n_used, int64_t n_tokens) {
+    auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    const size_t R = (size_t)(n_used * n_tokens);
+    MoeLayout L{};
+    L.off = 0;
+    L.tiles = al((size_t)(n_expert + 1) * 4);
+    L.slot = L.tiles + al((size_t)(n_expert + 1) * 4);
+    L.tok = L.slot + al(R * 4);
+    L.a16 = L.tok + al(R * 4);
+    L.scales = L.a16 + al(R * (size_t)K * 2);
+    L.total = L.scales + al(R * 4);
+    return L;
+}
+
+static int moe_token_tile(int64_t R, int64_t n_expert) {
+    const int64_t avg = n_expert > 0 ? R / n_expert : R;
+    return avg <= 32 ? 32 : avg <= 64 ? 64 : 128;
+}
+
+int mul_mat_id_impl(int wtype, const void* as_packed, int64_t K, int64_t N, int64_t n_expert, const float* b,
+                    int64_t b_nb1, int64_t b_nb2, int64_t ne11, const int32_t* ids, int64_t ids_nb0, int64_t ids_nb1,
+                    int64_t n_used, int64_t n_tokens, float* dst, int64_t d_nb1, int64_t d_nb2, void* workspace,
+                    size_t ws_bytes, int* dev_err, cudaStream_t st) {
+    if (!as_packed || !b || !ids || !dst || !dev_err || K <= 0 || N <= 0 || n_expert <= 0 || n_used <= 0 ||
+        n_tokens <= 0 || ne11 <= 0)
+        return B200_E_INVALID;
+    if (!weight_type_supported(wtype, K) || K % 32 != 0 || N % 16 != 0 || K % 4 != 0) return B200_E_UNSUPPORTED;
+    if (n_expert > 4096 || n_used * n_tokens > (1 << 28)) return B200_E_UNSUPPORTED;
+    if ((b_nb1 % 16) || (b_nb2 % 16) || (reinterpret_cast<uintptr_t>(b) & 15u)) return B200_E_UNSUPPORTED;
+    const MoeLayout L = moe_layout(K, n_expert, n_used, n_tokens);
+    if (!workspace || ws_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255u)) return B200_E_WORKSPACE;
+    char* ws = static_cast<char*>(workspace);
+    int32_t* off = reinterpret_cast<int32_t*>(ws + L.off);
+    int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
+    int32_t* slot = reinterpret_cast<int32_t*>(ws + L.slot);
+    int32_t* tok = reinterpret_cast<int32_t*>(ws + L.tok);
+    __half* a16 = reinterpret_cast<__half*>(ws + L.a16);
+    float* scales = reinterpret_cast<float*>(ws + L.scales);
+    const int64_t R = n_used * n_tokens;
+    const int bt = moe_token_tile(R, n_expert);
+
+    const size_t route_smem = (size_t)(2 + 32) * n_expert * sizeof(int);
+    if (route_smem > 48 * 1024) {
+        if (cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)route_smem) !=
+            cudaSuccess)
+            return B200_E_UNSUPPORTED;
+    }
+    moe_route_kernel<<<1, ROUTE_THREADS, route_smem, st>>>(ids, ids_nb0, ids_nb1, (int)n_used, (int)n_tokens,
+                                                           (int)n_expert, bt, off, tiles, slot, tok, dev_err);
+    if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
+
+    const int64_t per = (K / 4 + 255) / 256;
+    const dim3 grid((unsigned)R);
+#define B200_GATHER(V) \
+    moe_gather_pack_kernel<V><<<grid, 256, 0, st>>>(b, b_nb1, b_nb2, (int)ne11, (int)K, slot, tok, off + n_expert, a16, scales)
+    if (per <= 1) B200_GATHER(1);
+    else if (per <= 2) B200_GATHER(2);
+    else if (per <= 4) B200_GATHER(4);
+    else if (per <= 8) B200_GATHER(8);
+    else if (per <= 16) B200_GATHER(16);
+    else return B200_E_UNSUPPORTED;
+#undef B200_GATHER
+    if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
+
+    return gemm_grouped_impl(wtype, as_packed, N, K, n_expert, a16, scales, R, bt, off, tiles, slot, tok, dst, d_nb1,
+                             d_nb2, dev_err, st);
+}
+
+}  // namespace b200
+
+extern "C" {
+
+size_t b200_mul_mat_id_workspace_size(int64_t K, int64_t N, int64_t n_expert, int64_t n_used, int64_t n_tokens) {
+    (void)N;
+    if (K <= 0 || n_expert <= 0 || n_used <= 0 || n_tokens <= 0) return 0;
+    return b200::moe_layout(K, n_expert, n_used, n_tokens).total;
+}
+
+int b200_mul_mat_id(int wtype, const void* as_packed, int64_t K, int64_t N, int64_t n_expert, const float* b,
+                    int64_t b_nb1, int64_t b_nb2, int64_t ne11, const int32_t* ids, int64_t ids_nb0, int64_t ids_nb1,
+                    int64_t n_used, int64_t n_tokens, float* dst, int64_t d_nb1, int64_t d_nb2, void* workspace,
+                    size_t workspace_bytes, int* dev_err, void* stream) {
+    return b200::mul_mat_id_impl(wtype, as_packed, K, N, n_expert, b, b_nb1, b_nb2, ne11, ids, ids_nb0, ids_nb1, n_used,
+                                 n_tokens, dst, d_nb1, d_nb2, workspace, workspace_bytes, dev_err,
+                                 static_cast<cudaStream_t>(stream));
+}
+
+int b200_mul_mat_id_route_view(int64_t K, int64_t n_expert, int64_t n_used, int64_t n_tokens, size_t* off_offset,
+                               size_t* slot_offset, size_t* tok_offset) {
+    if (K <= 0 || n_expert <= 0 || n_used <= 0 || n_tokens <= 0) return B200_E_INVALID;
+    const b200::MoeLayout L = b200::moe_layout(K, n_expert, n_used, n_tokens);
+    if (off_offset) *off_offset = L.off;
+    if (slot_offset) *slot_offset = L.slot;
+    if (tok_offset) *tok_offset = L.tok;
+    return B200_OK;
+}
+
+}  // extern "C"

@@ -20,44 +20,83 @@ namespace b200 {
 
 // ------------------------------------------------------------------------------------------
 // Activation "sandwich" pre-pass (the reference's rk_pack_act_row, ggml-rocket.cpp:1451-1475):
-// per row s = max|A[m,:]| (1 when 0), A16 = fp16(A * (1/s)). One warp per row.
+// per row s = max|A[m,:]| (1 when 0), A16 = fp16(A * (1/s)).
+// One 256-thread CTA per row; the row is read from HBM once into registers (V float4 per
+// thread), reduced across the CTA, then scaled and written from registers.
 // ------------------------------------------------------------------------------------------
-__global__ void act_pack_kernel(const float* __restrict__ A, int64_t lda, int M, int K,
-                                __half* __restrict__ A16, float* __restrict__ scales) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (warp >= M) return;
-    const float* row = A + (size_t)warp * lda;
-    __half* out = A16 + (size_t)warp * K;
-    const bool vec = ((reinterpret_cast<uintptr_t>(row) & 15u) == 0) && (K % 4 == 0);
+constexpr int ACT_THREADS = 256;
+
+template <int V>
+__global__ void __launch_bounds__(ACT_THREADS) act_pack_kernel(const float* __restrict__ A, int64_t lda, int K,
+                                                               __half* __restrict__ A16, float* __restrict__ scales) {
+    __shared__ float red[ACT_THREADS / 32];
+    const int m = blockIdx.x;
+    const float4* row = reinterpret_cast<const float4*>(A + (size_t)m * lda);
+    uint2* out = reinterpret_cast<uint2*>(A16 + (size_t)m * K);
+    const int n4 = K / 4;
+    float4 v[V];
     float amax = 0.0f;
-    if (vec) {
-        const float4* r4 = reinterpret_cast<const float4*>(row);
-        for (int i = lane; i < K / 4; i += 32) {
-            const float4 v = __ldg(r4 + i);
-            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-        }
-    } else {
-        for (int i = lane; i < K; i += 32) amax = fmaxf(amax, fabsf(__ldg(row + i)));
+#pragma unroll
+    for (int i = 0; i < V; i++) {
+        const int idx = threadIdx.x + i * ACT_THREADS;
+        v[i] = idx < n4 ? __ldg(row + idx) : make_float4(0.f, 0.f, 0.f, 0.f);
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = red[0];
+#pragma unroll
+    for (int w = 1; w < ACT_THREADS / 32; w++) amax = fmaxf(amax, red[w]);
     const float s = amax > 0.0f ? amax : 1.0f;
     const float inv = __frcp_rn(s);
-    if (lane == 0) scales[warp] = s;
-    if (vec) {
-        const float4* r4 = reinterpret_cast<const float4*>(row);
-        uint2* o2 = reinterpret_cast<uint2*>(out);
-        for (int i = lane; i < K / 4; i += 32) {
-            const float4 v = __ldg(r4 + i);
+    if (threadIdx.x == 0) scales[m] = s;
+#pragma unroll
+    for (int i = 0; i < V; i++) {
+        const int idx = threadIdx.x + i * ACT_THREADS;
+        if (idx < n4) {
             uint2 w;
-            w.x = pack_half2(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv));
-            w.y = pack_half2(__fmul_rn(v.z, inv), __fmul_rn(v.w, inv));
-            o2[i] = w;
+            w.x = pack_half2(__fmul_rn(v[i].x, inv), __fmul_rn(v[i].y, inv));
+            w.y = pack_half2(__fmul_rn(v[i].z, inv), __fmul_rn(v[i].w, inv));
+            out[idx] = w;
         }
-    } else {
-        for (int i = lane; i < K; i += 32) out[i] = __float2half_rn(__fmul_rn(__ldg(row + i), inv));
     }
+}
+
+// Rows too long (or too unaligned) for the register version: two passes with scalar loads.
+__global__ void __launch_bounds__(ACT_THREADS) act_pack_loop_kernel(const float* __restrict__ A, int64_t lda, int K,
+                                                                    __half* __restrict__ A16, float* __restrict__ scales) {
+    __shared__ float red[ACT_THREADS / 32];
+    const int m = blockIdx.x;
+    const float* row = A + (size_t)m * lda;
+    __half* out = A16 + (size_t)m * K;
+    float amax = 0.0f;
+    for (int i = threadIdx.x; i < K; i += ACT_THREADS) amax = fmaxf(amax, fabsf(__ldg(row + i)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = red[0];
+    for (int w = 1; w < ACT_THREADS / 32; w++) amax = fmaxf(amax, red[w]);
+    const float s = amax > 0.0f ? amax : 1.0f;
+    const float inv = __frcp_rn(s);
+    if (threadIdx.x == 0) scales[m] = s;
+    for (int i = threadIdx.x; i < K; i += ACT_THREADS) out[i] = __float2half_rn(__fmul_rn(__ldg(row + i), inv));
+}
+
+static cudaError_t launch_act_pack(const float* A, int64_t lda, int64_t M, int64_t K, __half* a16, float* scales,
+                                   cudaStream_t st) {
+    const bool vec = ((reinterpret_cast<uintptr_t>(A) & 15u) == 0) && (lda % 4 == 0) && (K % 4 == 0);
+    const int64_t per = (K / 4 + ACT_THREADS - 1) / ACT_THREADS;   // float4 per thread
+    const dim3 grid((unsigned)M);
+    if (!vec || per > 16) act_pack_loop_kernel<<<grid, ACT_THREADS, 0, st>>>(A, lda, (int)K, a16, scales);
+    else if (per <= 1) act_pack_kernel<1><<<grid, ACT_THREADS, 0, st>>>(A, lda, (int)K, a16, scales);
+    else if (per <= 2) act_pack_kernel<2><<<grid, ACT_THREADS, 0, st>>>(A, lda, (int)K, a16, scales);
+    else if (per <= 4) act_pack_kernel<4><<<grid, ACT_THREADS, 0, st>>>(A, lda, (int)K, a16, scales);
+    else if (per <= 8) act_pack_kernel<8><<<grid, ACT_THREADS, 0, st>>>(A, lda, (int)K, a16, scales);
+    else act_pack_kernel<16><<<grid, ACT_THREADS, 0, st>>>(A, lda, (int)K, a16, scales);
+    return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------------------------------
@@ -191,7 +230,8 @@ struct GemmPlan {
 
 static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms) {
     GemmPlan p{};
-    p.nkb = (int)((K + GEMM_BK - 1) / GEMM_BK);
+    p.nkb = (int)((K + GEMM_BK - 1) / GEMM_BK);   // Q8_0 rows are padded to 256 with zero blocks,
+                                                  // but the chunks past K need no MMA: A is zero there
     p.ntn = (int)((N + GEMM_BN - 1) / GEMM_BN);
     p.bt = M <= 32 ? 32 : M <= 64 ? 64 : M <= 1024 ? 128 : 256;
     p.ntt = (int)((M + p.bt - 1) / p.bt);
@@ -224,7 +264,7 @@ static MulMatWorkspace mm_workspace_layout(int64_t M, int64_t N, int64_t K, cons
     return w;
 }
 
-template <int BT, int WT>
+template <int BT, int WT, bool GROUPED>
 static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& a, int grid,
                                  cudaStream_t st) {
     using C = GemmCfg<BT, WT>;
@@ -232,23 +272,99 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW,
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BT, WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BT, WT, GROUPED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             C::SMEM);
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
-    gemm_kernel<BT, WT><<<grid, C::THREADS, C::SMEM, st>>>(tmA, tmW, a);
+    gemm_kernel<BT, WT, GROUPED><<<grid, C::THREADS, C::SMEM, st>>>(tmA, tmW, a);
     return cudaGetLastError();
 }
 
-template <int WT>
+template <int WT, bool GROUPED>
 static cudaError_t launch_gemm_bt(int bt, const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& a,
                                   int grid, cudaStream_t st) {
     switch (bt) {
-        case 32: return launch_gemm_t<32, WT>(tmA, tmW, a, grid, st);
-        case 64: return launch_gemm_t<64, WT>(tmA, tmW, a, grid, st);
-        case 128: return launch_gemm_t<128, WT>(tmA, tmW, a, grid, st);
-        default: return launch_gemm_t<256, WT>(tmA, tmW, a, grid, st);
+        case 32: return launch_gemm_t<32, WT, GROUPED>(tmA, tmW, a, grid, st);
+        case 64: return launch_gemm_t<64, WT, GROUPED>(tmA, tmW, a, grid, st);
+        case 128: return launch_gemm_t<128, WT, GROUPED>(tmA, tmW, a, grid, st);
+        default: return launch_gemm_t<256, WT, GROUPED>(tmA, tmW, a, grid, st);
     }
+}
+
+// Fill the weight-side fields of GemmArgs (and the F16 weight tensor map) for `wrows` packed
+// weight rows of K.
+static bool setup_weight_args(int wtype, const void* w_packed, int64_t wrows, int64_t K, GemmArgs& a, CUtensorMap& tmW,
+                              const CUtensorMap& tmA) {
+    size_t d_off = 0;
+    packed_weight_bytes(wtype, wrows, K, &d_off);
+    if (wtype == WT_F16) {
+        return make_tmap_2d_f16(&tmW, w_packed, (uint64_t)wrows, (uint64_t)K, (uint64_t)K, GEMM_BN, GEMM_BK);
+    }
+    tmW = tmA;   // unused by the quantized kernels
+    a.w = static_cast<const uint8_t*>(w_packed);
+    if (wtype == WT_Q4_K) {
+        a.w_row_bytes = (K / 256) * 144;
+    } else if (wtype == WT_Q6_K) {
+        a.w_row_bytes = (K / 256) * 208;
+        a.wd = reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(w_packed) + d_off);
+        a.wd_row_elems = K / 256;
+    } else {
+        const int64_t ngrp = (K + 255) / 256;
+        a.w_row_bytes = ngrp * 256;
+        a.wd = reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(w_packed) + d_off);
+        a.wd_row_elems = ngrp * 8;
+    }
+    return true;
+}
+
+template <bool GROUPED>
+cudaError_t launch_gemm_typed(int wtype, int bt, const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& a,
+                              int grid, cudaStream_t st) {
+    switch (wtype) {
+        case WT_F16: return launch_gemm_bt<WT_F16, GROUPED>(bt, tmA, tmW, a, grid, st);
+        case WT_Q4_K: return launch_gemm_bt<WT_Q4_K, GROUPED>(bt, tmA, tmW, a, grid, st);
+        case WT_Q6_K: return launch_gemm_bt<WT_Q6_K, GROUPED>(bt, tmA, tmW, a, grid, st);
+        case WT_Q8_0: return launch_gemm_bt<WT_Q8_0, GROUPED>(bt, tmA, tmW, a, grid, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// The grouped (MUL_MAT_ID) launch: A16 holds `rows` expert-sorted token rows; the route arrays
+// live on the device (see moe.cu).
+int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int64_t n_expert, const __half* a16,
+                      const float* scales, int64_t rows, int bt, const int32_t* off, const int32_t* tile_start,
+                      const int32_t* slot, const int32_t* tok, float* dst, int64_t d_nb1, int64_t d_nb2, int* dev_err,
+                      cudaStream_t st) {
+    CUtensorMap tmA, tmW;
+    if (!make_tmap_2d_f16(&tmA, a16, (uint64_t)rows, (uint64_t)K, (uint64_t)K, (uint32_t)bt, GEMM_BK)) return B200_E_CUDA;
+    GemmArgs a{};
+    if (!setup_weight_args(wtype, w_stack, N * n_expert, K, a, tmW, tmA)) return B200_E_CUDA;
+    a.scales = scales;
+    a.out = dst;
+    a.M = (int)rows;
+    a.N = (int)N;
+    a.K = (int)K;
+    a.n_tiles_n = (int)((N + GEMM_BN - 1) / GEMM_BN);
+    a.n_tiles_t = 1;
+    a.splits = 1;
+    a.nkb = (int)((K + GEMM_BK - 1) / GEMM_BK);
+    a.kb_per_split = a.nkb;
+    a.num_units = 0;
+    a.err = dev_err;
+    a.g_off = off;
+    a.g_tile_start = tile_start;
+    a.g_slot = slot;
+    a.g_tok = tok;
+    a.n_expert = (int)n_expert;
+    a.d_nb1 = d_nb1;
+    a.d_nb2 = d_nb2;
+    const int sms = device_sm_count();
+    const int64_t max_tiles = (rows + bt - 1) / bt + n_expert;
+    const int64_t max_units = max_tiles * a.n_tiles_n;
+    const int grid = (int)(max_units < sms ? max_units : sms);
+    if (grid <= 0) return B200_OK;
+    return launch_gemm_typed<true>(wtype, bt, tmA, tmW, a, grid, st) == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 
 size_t packed_weight_bytes(int type, int64_t N, int64_t K, size_t* plane_d_off) {
@@ -282,54 +398,25 @@ bool weight_type_supported(int type, int64_t K) {
     }
 }
 
-int mul_mat_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const float* src1, int64_t lda, int64_t M,
-                 float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t st) {
-    if (!w_packed || !src1 || !dst || !dev_err || M <= 0 || N <= 0 || K <= 0) return B200_E_INVALID;
+// The tcgen05 GEMM over an already packed activation (A16 [M,K] fp16 + per-row scales).
+int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const __half* a16, const float* scales,
+                     int64_t M, float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err,
+                     cudaStream_t st) {
+    if (!w_packed || !a16 || !scales || !dst || !dev_err || M <= 0 || N <= 0 || K <= 0) return B200_E_INVALID;
     if (!weight_type_supported(wtype, K) || K % 32 != 0 || N % 16 != 0) return B200_E_UNSUPPORTED;
     if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return B200_E_UNSUPPORTED;
     const int sms = device_sm_count();
     const GemmPlan p = plan_gemm(M, N, K, sms);
-    const MulMatWorkspace wl = mm_workspace_layout(M, N, K, p);
-    if (!workspace || workspace_bytes < wl.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    const size_t part_bytes = p.splits > 1 ? (size_t)p.splits * M * N * 4 : 0;
+    if (part_bytes && (!workspace || workspace_bytes < part_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
         return B200_E_WORKSPACE;
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    __half* a16 = reinterpret_cast<__half*>(ws + wl.a16_off);
-    float* scales = reinterpret_cast<float*>(ws + wl.scales_off);
-    float* part = reinterpret_cast<float*>(ws + wl.part_off);
-
-    {
-        const int threads = 256;
-        const int blocks = (int)((M * 32 + threads - 1) / threads);
-        act_pack_kernel<<<blocks, threads, 0, st>>>(src1, lda, (int)M, (int)K, a16, scales);
-        if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
-    }
-
+    float* part = static_cast<float*>(workspace);
     CUtensorMap tmA, tmW;
     std::memset(&tmW, 0, sizeof(tmW));
     if (!make_tmap_2d_f16(&tmA, a16, (uint64_t)M, (uint64_t)K, (uint64_t)K, (uint32_t)p.bt, GEMM_BK))
         return B200_E_CUDA;
     GemmArgs a{};
-    size_t d_off = 0;
-    packed_weight_bytes(wtype, N, K, &d_off);
-    if (wtype == WT_F16) {
-        if (!make_tmap_2d_f16(&tmW, w_packed, (uint64_t)N, (uint64_t)K, (uint64_t)K, GEMM_BN, GEMM_BK))
-            return B200_E_CUDA;
-    } else {
-        tmW = tmA;   // unused by the quantized kernels
-        a.w = static_cast<const uint8_t*>(w_packed);
-        if (wtype == WT_Q4_K) {
-            a.w_row_bytes = (K / 256) * 144;
-        } else if (wtype == WT_Q6_K) {
-            a.w_row_bytes = (K / 256) * 208;
-            a.wd = reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(w_packed) + d_off);
-            a.wd_row_elems = K / 256;
-        } else {
-            const int64_t ngrp = (K + 255) / 256;
-            a.w_row_bytes = ngrp * 256;
-            a.wd = reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(w_packed) + d_off);
-            a.wd_row_elems = ngrp * 8;
-        }
-    }
+    if (!setup_weight_args(wtype, w_packed, N, K, a, tmW, tmA)) return B200_E_CUDA;
     a.scales = scales;
     a.M = (int)M;
     a.N = (int)N;
@@ -350,14 +437,7 @@ int mul_mat_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const fl
         a.ldo = ldd;
         a.split_stride = 0;
     }
-    cudaError_t e;
-    switch (wtype) {
-        case WT_F16: e = launch_gemm_bt<WT_F16>(p.bt, tmA, tmW, a, p.grid, st); break;
-        case WT_Q4_K: e = launch_gemm_bt<WT_Q4_K>(p.bt, tmA, tmW, a, p.grid, st); break;
-        case WT_Q6_K: e = launch_gemm_bt<WT_Q6_K>(p.bt, tmA, tmW, a, p.grid, st); break;
-        case WT_Q8_0: e = launch_gemm_bt<WT_Q8_0>(p.bt, tmA, tmW, a, p.grid, st); break;
-        default: return B200_E_UNSUPPORTED;
-    }
+    const cudaError_t e = launch_gemm_typed<false>(wtype, p.bt, tmA, tmW, a, p.grid, st);
     if (e != cudaSuccess) return B200_E_CUDA;
     if (p.splits > 1) {
         const int64_t total = M * N;
@@ -367,6 +447,27 @@ int mul_mat_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const fl
         if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
     }
     return B200_OK;
+}
+
+int act_pack_impl(const float* src1, int64_t lda, int64_t M, int64_t K, __half* a16, float* scales, cudaStream_t st) {
+    if (!src1 || !a16 || !scales || M <= 0 || K <= 0 || lda < K) return B200_E_INVALID;
+    return launch_act_pack(src1, lda, M, K, a16, scales, st) == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
+int mul_mat_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const float* src1, int64_t lda, int64_t M,
+                 float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t st) {
+    if (!w_packed || !src1 || !dst || !dev_err || M <= 0 || N <= 0 || K <= 0) return B200_E_INVALID;
+    const GemmPlan p = plan_gemm(M, N, K, device_sm_count());
+    const MulMatWorkspace wl = mm_workspace_layout(M, N, K, p);
+    if (!workspace || workspace_bytes < wl.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+        return B200_E_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    __half* a16 = reinterpret_cast<__half*>(ws + wl.a16_off);
+    float* scales = reinterpret_cast<float*>(ws + wl.scales_off);
+    int rc = act_pack_impl(src1, lda, M, K, a16, scales, st);
+    if (rc != B200_OK) return rc;
+    return gemm_packed_impl(wtype, w_packed, N, K, a16, scales, M, dst, ldd, ws + wl.part_off, wl.total - wl.part_off,
+                            dev_err, st);
 }
 
 size_t mul_mat_workspace(int64_t M, int64_t N, int64_t K) {
@@ -443,6 +544,33 @@ int b200_weight_pack(int type, const void* src_native, int64_t N, int64_t K, voi
 
 int b200_dequantize(int type, const void* src_native, int64_t N, int64_t K, int f16_out, void* dst, void* stream) {
     return b200::dequantize_impl(type, src_native, N, K, f16_out, dst, static_cast<cudaStream_t>(stream));
+}
+
+int b200_act_pack(const float* src1, int64_t lda, int64_t M, int64_t K, void* a16, float* scales, void* stream) {
+    return b200::act_pack_impl(src1, lda, M, K, static_cast<__half*>(a16), scales, static_cast<cudaStream_t>(stream));
+}
+
+size_t b200_gemm_packed_workspace_size(int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    const b200::GemmPlan p = b200::plan_gemm(M, N, K, b200::device_sm_count());
+    return p.splits > 1 ? (size_t)p.splits * M * N * 4 : 0;
+}
+
+int b200_gemm_packed(int wtype, const void* w_packed, int64_t N, int64_t K, const void* a16, const float* scales,
+                     int64_t M, float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err,
+                     void* stream) {
+    return b200::gemm_packed_impl(wtype, w_packed, N, K, static_cast<const __half*>(a16), scales, M, dst, ldd,
+                                  workspace, workspace_bytes, dev_err, static_cast<cudaStream_t>(stream));
+}
+
+int b200_mul_mat_plan(int64_t M, int64_t N, int64_t K, int* token_tile, int* splits, int* grid, int* launches) {
+    if (M <= 0 || N <= 0 || K <= 0) return B200_E_INVALID;
+    const b200::GemmPlan p = b200::plan_gemm(M, N, K, b200::device_sm_count());
+    if (token_tile) *token_tile = p.bt;
+    if (splits) *splits = p.splits;
+    if (grid) *grid = p.grid;
+    if (launches) *launches = 2 + (p.splits > 1 ? 1 : 0);
+    return B200_OK;
 }
 
 size_t b200_mul_mat_workspace_size(int64_t M, int64_t N, int64_t K) {

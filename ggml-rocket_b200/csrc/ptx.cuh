@@ -88,6 +88,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
     }
 }
 
+// Wait without the abort short-cut (used after an abort, to let issued copies land), bounded.
+__device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() - t0 > B200_WAIT_LIMIT_NS) return false;
+    }
+    return true;
+}
+
 // ---- async-proxy fences and TMA ------------------------------------------------------------
 
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy

@@ -34,6 +34,7 @@ _lib = None
 
 _c = ctypes
 _vp, _i64, _int, _sz, _f = _c.c_void_p, _c.c_int64, _c.c_int, _c.c_size_t, _c.c_float
+_pint = _c.POINTER(_c.c_int)
 
 _SIGS = {
     "b200_weight_packed_size": (_sz, [_int, _i64, _i64]),
@@ -41,6 +42,10 @@ _SIGS = {
     "b200_dequantize": (_int, [_int, _vp, _i64, _i64, _int, _vp, _vp]),
     "b200_mul_mat_workspace_size": (_sz, [_i64, _i64, _i64]),
     "b200_mul_mat": (_int, [_int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _sz, _vp, _vp]),
+    "b200_act_pack": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
+    "b200_gemm_packed_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "b200_gemm_packed": (_int, [_int, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _sz, _vp, _vp]),
+    "b200_mul_mat_plan": (_int, [_i64, _i64, _i64, _pint, _pint, _pint, _pint]),
 }
 
 
@@ -104,3 +109,217 @@ def mul_mat(wtype, w_packed, N, K, a, M, out, workspace, dev_err, lda=None, ldd=
     check(lib().b200_mul_mat(wtype, _ptr(w_packed), N, K, _ptr(a), lda, M, _ptr(out), ldd,
                              _ptr(workspace), workspace.numel() * workspace.element_size(), _ptr(dev_err),
                              _stream(stream)), "mul_mat")
+
+
+def act_pack(a, M, K, a16, scales, lda=None, stream=None):
+    lda = K if lda is None else lda
+    check(lib().b200_act_pack(_ptr(a), lda, M, K, _ptr(a16), _ptr(scales), _stream(stream)), "act_pack")
+
+
+def gemm_packed_workspace_size(M, N, K):
+    return lib().b200_gemm_packed_workspace_size(M, N, K)
+
+
+def gemm_packed(wtype, w_packed, N, K, a16, scales, M, out, workspace, dev_err, ldd=None, stream=None):
+    ldd = N if ldd is None else ldd
+    wsb = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib().b200_gemm_packed(wtype, _ptr(w_packed), N, K, _ptr(a16), _ptr(scales), M, _ptr(out), ldd,
+                                 _ptr(workspace), wsb, _ptr(dev_err), _stream(stream)), "gemm_packed")
+
+
+def mul_mat_plan(M, N, K):
+    vals = [ctypes.c_int(0) for _ in range(4)]
+    check(lib().b200_mul_mat_plan(M, N, K, *[ctypes.byref(v) for v in vals]), "mul_mat_plan")
+    return dict(token_tile=vals[0].value, splits=vals[1].value, grid=vals[2].value, launches=vals[3].value)
+
+
+# ---- backend-level API (include/ggml-b200.h) -------------------------------------------------
+
+OP_NONE, OP_RESHAPE, OP_VIEW, OP_PERMUTE, OP_TRANSPOSE, OP_MUL_MAT, OP_MUL_MAT_ID, OP_FLASH_ATTN_EXT, OP_OTHER = range(9)
+STATUS_SUCCESS, STATUS_FAILED = 0, -1
+PREC_F32, PREC_BF16, PREC_F16, PREC_Q8, PREC_Q4 = 10, 15, 20, 30, 40
+HINT_SRC0_IS_HADAMARD = 1
+
+
+class Tensor(ctypes.Structure):
+    pass
+
+
+Tensor._fields_ = [
+    ("type", ctypes.c_int32),
+    ("op", ctypes.c_int32),
+    ("ne", ctypes.c_int64 * 4),
+    ("nb", ctypes.c_size_t * 4),
+    ("op_params", ctypes.c_int32 * 16),
+    ("src", ctypes.POINTER(Tensor) * 10),
+    ("data", ctypes.c_void_p),
+    ("on_device", ctypes.c_int32),
+    ("readable", ctypes.c_int32),
+    ("name", ctypes.c_char * 64),
+]
+
+_TP = ctypes.POINTER(Tensor)
+_BACKEND_SIGS = {
+    "ggml_backend_b200_reg_name": (ctypes.c_char_p, []),
+    "ggml_backend_b200_reg_device_count": (_int, []),
+    "ggml_backend_b200_op_from_name": (_int, [ctypes.c_char_p]),
+    "ggml_backend_b200_device_name": (ctypes.c_char_p, [_int]),
+    "ggml_backend_b200_device_description": (_int, [_int, ctypes.c_char_p, _sz]),
+    "ggml_backend_b200_device_memory": (_int, [_int, _c.POINTER(_sz), _c.POINTER(_sz)]),
+    "ggml_backend_b200_supports_op": (ctypes.c_bool, [_TP]),
+    "ggml_backend_b200_offload_op": (ctypes.c_bool, [_TP]),
+    "ggml_backend_b200_init": (_vp, []),
+    "ggml_backend_b200_free": (None, [_vp]),
+    "ggml_backend_is_b200": (ctypes.c_bool, [_vp]),
+    "ggml_backend_b200_set_n_gpus": (None, [_vp, _int]),
+    "ggml_backend_b200_moe_stats": (None, [_vp, _c.POINTER(_c.c_long), _c.POINTER(_c.c_long)]),
+    "ggml_backend_b200_route_ops": (_c.c_long, [_vp, ctypes.c_char_p]),
+    "ggml_backend_b200_cpu_fallbacks": (_c.c_long, [_vp]),
+    "ggml_backend_b200_device_errors": (_c.c_long, [_vp]),
+    "ggml_backend_b200_graph_compute": (_int, [_vp, _c.POINTER(_TP), _int]),
+    "ggml_backend_b200_weight_cache_bytes": (_sz, [_vp, _c.POINTER(_c.c_long)]),
+    "ggml_backend_b200_weight_key": (_sz, [_TP, ctypes.c_char_p, _sz]),
+    "ggml_backend_b200_breaker_replay": (None, [_c.POINTER(_int), _int, _c.POINTER(_int)]),
+    "b200_flash_attn_workspace_size": (_sz, [_int] * 6),
+    "b200_flash_attn_ext": (_int, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp,
+                                   _int, _int, _int, _int, _int, _int, _f, _f, _f, _vp, _sz, _vp, _vp]),
+    "b200_mul_mat_id_workspace_size": (_sz, [_i64] * 5),
+    "b200_mul_mat_id": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
+                               _vp, _i64, _i64, _vp, _sz, _vp, _vp]),
+    "b200_mul_mat_id_route_view": (_int, [_i64, _i64, _i64, _i64, _c.POINTER(_sz), _c.POINTER(_sz),
+                                          _c.POINTER(_sz)]),
+}
+_SIGS.update(_BACKEND_SIGS)
+
+
+def _elem_size(t):
+    be, bb = BLOCK.get(t, (1, 4 if t == I32 else 0))
+    return bb / be
+
+
+def make_tensor(t, ne, data=None, op=OP_NONE, srcs=(), name="", on_device=False, nb=None, readable=True,
+                op_params=None):
+    """A b200_tensor with ggml semantics: ne[0] innermost; contiguous strides unless nb is given."""
+    ne = list(ne) + [1] * (4 - len(ne))
+    x = Tensor()
+    x.type = t
+    x.op = op
+    for i in range(4):
+        x.ne[i] = int(ne[i])
+    if nb is None:
+        be, bb = BLOCK.get(t, (1, 4 if t == I32 else 4))
+        nb0 = bb if be == 1 else bb
+        nb1 = (ne[0] // be) * bb
+        nb = [nb0, nb1, nb1 * ne[1], nb1 * ne[1] * ne[2]]
+    for i in range(4):
+        x.nb[i] = int(nb[i])
+    for i, s in enumerate(srcs):
+        if s is not None:
+            x.src[i] = ctypes.pointer(s)
+    if data is not None:
+        x.data = data if isinstance(data, int) else data.ctypes.data
+    x.on_device = 1 if on_device else 0
+    x.readable = 1 if readable else 0
+    x.name = name.encode()[:63]
+    if op_params:
+        for i, v in enumerate(op_params):
+            if isinstance(v, float):
+                import struct
+                v = struct.unpack("<i", struct.pack("<f", v))[0]
+            x.op_params[i] = int(v)
+    return x
+
+
+def supports_op(op):
+    return bool(lib().ggml_backend_b200_supports_op(ctypes.byref(op)))
+
+
+def offload_op(op):
+    return bool(lib().ggml_backend_b200_offload_op(ctypes.byref(op)))
+
+
+class Backend:
+    """An owning wrapper of a b200_backend_t."""
+
+    def __init__(self):
+        self.h = lib().ggml_backend_b200_init()
+        if not self.h:
+            raise B200Error("ggml_backend_b200_init returned NULL (no CUDA device)")
+
+    def close(self):
+        if self.h:
+            lib().ggml_backend_b200_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def graph_compute(self, nodes):
+        arr = (_TP * len(nodes))(*[ctypes.pointer(n) for n in nodes])
+        return lib().ggml_backend_b200_graph_compute(self.h, arr, len(nodes))
+
+    def route_ops(self, route=None):
+        return lib().ggml_backend_b200_route_ops(self.h, route.encode() if route else None)
+
+    def cpu_fallbacks(self):
+        return lib().ggml_backend_b200_cpu_fallbacks(self.h)
+
+    def device_errors(self):
+        return lib().ggml_backend_b200_device_errors(self.h)
+
+    def moe_stats(self):
+        a, b = ctypes.c_long(0), ctypes.c_long(0)
+        lib().ggml_backend_b200_moe_stats(self.h, ctypes.byref(a), ctypes.byref(b))
+        return a.value, b.value
+
+    def weight_cache(self):
+        n = ctypes.c_long(0)
+        by = lib().ggml_backend_b200_weight_cache_bytes(self.h, ctypes.byref(n))
+        return by, n.value
+
+
+def weight_key(t):
+    buf = ctypes.create_string_buffer(256)
+    lib().ggml_backend_b200_weight_key(ctypes.byref(t), buf, 256)
+    return buf.value.decode()
+
+
+def breaker_replay(rcs):
+    n = len(rcs)
+    a = (ctypes.c_int * n)(*rcs)
+    out = (ctypes.c_int * n)()
+    lib().ggml_backend_b200_breaker_replay(a, n, out)
+    return list(out)
+
+
+def flash_attn_ext(q, q_nb1, q_nb2, k, k_nb1, k_nb2, v, v_nb1, v_nb2, mask, m_nb1, dst, D, DV, T, H, KV, HK,
+                   scale, softcap, workspace, dev_err, max_bias=0.0, stream=None):
+    check(lib().b200_flash_attn_ext(_ptr(q), q_nb1, q_nb2, _ptr(k), k_nb1, k_nb2, _ptr(v), v_nb1, v_nb2,
+                                    _ptr(mask), m_nb1, _ptr(dst), D, DV, T, H, KV, HK, scale, max_bias, softcap,
+                                    _ptr(workspace), workspace.numel() * workspace.element_size(), _ptr(dev_err),
+                                    _stream(stream)), "flash_attn_ext")
+
+
+def flash_attn_workspace_size(D, DV, T, H, KV, HK):
+    return lib().b200_flash_attn_workspace_size(D, DV, T, H, KV, HK)
+
+
+def mul_mat_id_workspace_size(K, N, n_expert, n_used, n_tokens):
+    return lib().b200_mul_mat_id_workspace_size(K, N, n_expert, n_used, n_tokens)
+
+
+def mul_mat_id(wtype, as_packed, K, N, n_expert, b, b_nb1, b_nb2, ne11, ids, ids_nb0, ids_nb1, n_used, n_tokens,
+               dst, d_nb1, d_nb2, workspace, dev_err, stream=None):
+    return lib().b200_mul_mat_id(wtype, _ptr(as_packed), K, N, n_expert, _ptr(b), b_nb1, b_nb2, ne11, _ptr(ids),
+                                 ids_nb0, ids_nb1, n_used, n_tokens, _ptr(dst), d_nb1, d_nb2, _ptr(workspace),
+                                 workspace.numel() * workspace.element_size(), _ptr(dev_err), _stream(stream))
+
+
+def mul_mat_id_route_view(K, n_expert, n_used, n_tokens):
+    a, b, c = ctypes.c_size_t(0), ctypes.c_size_t(0), ctypes.c_size_t(0)
+    check(lib().b200_mul_mat_id_route_view(K, n_expert, n_used, n_tokens, ctypes.byref(a), ctypes.byref(b),
+                                           ctypes.byref(c)), "route_view")
+    return a.value, b.value, c.value

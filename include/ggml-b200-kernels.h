@@ -70,6 +70,74 @@ int    b200_mul_mat(int wtype, const void * w_packed, int64_t N, int64_t K,
                     float * dst, int64_t ldd,
                     void * workspace, size_t workspace_bytes, int * dev_err, void * stream);
 
+/* The two halves of b200_mul_mat, for a caller that reuses one packed activation across
+ * several weights (the reference's fused QKV / gate-up group shares one pack,
+ * ggml-rocket.cpp:4956-5020) or times them apart:
+ *   b200_act_pack     src1 F32 [M, lda] -> a16 fp16 [M, K] (dense) + scales F32 [M]
+ *   b200_gemm_packed  dst = scales[m] * (a16 . W^T); the workspace is only needed when the
+ *                     plan splits K (b200_gemm_packed_workspace_size > 0). */
+int    b200_act_pack(const float * src1, int64_t lda, int64_t M, int64_t K, void * a16, float * scales, void * stream);
+size_t b200_gemm_packed_workspace_size(int64_t M, int64_t N, int64_t K);
+int    b200_gemm_packed(int wtype, const void * w_packed, int64_t N, int64_t K, const void * a16, const float * scales,
+                        int64_t M, float * dst, int64_t ldd, void * workspace, size_t workspace_bytes, int * dev_err,
+                        void * stream);
+
+/* The launch plan b200_mul_mat uses on the current device: the token tile (tcgen05 N), the
+ * split-K factor, the persistent grid and the number of kernel launches one call makes. */
+int    b200_mul_mat_plan(int64_t M, int64_t N, int64_t K, int * token_tile, int * splits, int * grid, int * launches);
+
+/* ---- FLASH_ATTN_EXT ------------------------------------------------------------------------
+ * Replaces ggml_backend_rocket_flash_attn (ggml-rocket.cpp:5444-5691): its gathers (:5487-5577),
+ * the NPU per-head QK -> mask -> softmax -> PV (rocket_flash_attn_fp16_ctx, :5590) and its
+ * scatter (:5644-5655), in one pass over the op's own strided tensors (ggml layouts, strides in
+ * bytes, innermost stride = element size):
+ *   q    F32 [D, T, H]        k F16 [D, KV, HK]       v F16 [DV, KV, HK]
+ *   mask F16 [KV, >=T] (row t at mask + t*m_nb1) or NULL for an unmasked op
+ *   dst  F32 [DV, H, T] contiguous
+ *   dst[c, h, t] = sum_j softmax_j(S[t,j]) v[c, j, h/(H/HK)],
+ *   S[t,j] = softcap*tanh(scale*q.k/softcap) (or scale*q.k when softcap == 0) + mask[t, j]
+ * Q is scaled and narrowed to fp16 (a row whose scaled values leave fp16's range is divided by a
+ * power of two that the score multiplies back, so no range fallback exists); q.k and P.v
+ * accumulate in fp32 in tensor memory, the softmax runs in fp32, P is fp16. A fully masked row
+ * is written as zeros. Requires D and DV in {64, 128}, H % HK == 0, 16-byte-aligned bases and
+ * row strides, max_bias == 0.
+ */
+size_t b200_flash_attn_workspace_size(int D, int DV, int T, int H, int KV, int HK);
+int    b200_flash_attn_ext(const float * q, int64_t q_nb1, int64_t q_nb2,
+                           const void * k, int64_t k_nb1, int64_t k_nb2,
+                           const void * v, int64_t v_nb1, int64_t v_nb2,
+                           const void * mask, int64_t m_nb1,
+                           float * dst, int D, int DV, int T, int H, int KV, int HK,
+                           float scale, float max_bias, float softcap,
+                           void * workspace, size_t workspace_bytes, int * dev_err, void * stream);
+
+/* ---- MUL_MAT_ID ----------------------------------------------------------------------------
+ * Replaces ggml_backend_rocket_mul_mat_id (ggml-rocket.cpp:6692-6944): the counting sort of
+ * (slot, token) rows by expert (:6706-6732), the per-expert gather (:6790-6800), the expert
+ * GEMMs and the scatter (:6742-6754), as three kernels with no host round trip:
+ *   as   [K, N, n_expert] expert weights, the whole stack packed by b200_weight_pack as one
+ *        [n_expert * N, K] matrix (expert e's row n is row e*N + n)
+ *   b    F32 [K, ne11, n_tokens]  (row (slot, t) at b + t*b_nb2 + (slot % ne11)*b_nb1)
+ *   ids  I32 [n_used, n_tokens]   (ids + t*ids_nb1 + slot*ids_nb0)
+ *   dst  F32 [N, n_used, n_tokens] (row (slot, t) at dst + t*d_nb2 + slot*d_nb1)
+ *   dst[:, slot, t] = as[:, :, ids[slot, t]] . b[:, slot % ne11, t]
+ * An id outside [0, n_expert) makes the kernels write nothing and set *dev_err to
+ * B200_DEV_BAD_IDS (the reference returns 1 there, ggml-rocket.cpp:6719). The per-expert row
+ * offsets, slots and tokens of the sort are left in the workspace
+ * (b200_mul_mat_id_route_view gives their offsets) so a test can compare them with the CPU sort.
+ */
+#define B200_DEV_BAD_IDS 100
+size_t b200_mul_mat_id_workspace_size(int64_t K, int64_t N, int64_t n_expert, int64_t n_used, int64_t n_tokens);
+int    b200_mul_mat_id(int wtype, const void * as_packed, int64_t K, int64_t N, int64_t n_expert,
+                       const float * b, int64_t b_nb1, int64_t b_nb2, int64_t ne11,
+                       const int32_t * ids, int64_t ids_nb0, int64_t ids_nb1, int64_t n_used, int64_t n_tokens,
+                       float * dst, int64_t d_nb1, int64_t d_nb2,
+                       void * workspace, size_t workspace_bytes, int * dev_err, void * stream);
+/* Byte offsets, inside the workspace, of the route arrays the last b200_mul_mat_id call wrote:
+ * off int32 [n_expert + 1], row_slot int32 [n_used*n_tokens], row_tok int32 [n_used*n_tokens]. */
+int    b200_mul_mat_id_route_view(int64_t K, int64_t n_expert, int64_t n_used, int64_t n_tokens,
+                                  size_t * off_offset, size_t * slot_offset, size_t * tok_offset);
+
 #ifdef __cplusplus
 }
 #endif

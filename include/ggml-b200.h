@@ -1,0 +1,130 @@
+/*
+ * ggml B200 backend -- the backend-level C ABI (the plugin surface).
+ *
+ * This mirrors the public API and the ggml vtable methods of gregordinary/ggml-rocket
+ * (ggml-rocket.h:24-93, device vtable ggml-rocket.cpp:7830-7842, backend vtable :7234-7238,
+ * registry :7875-7880) on plain C types: a ggml host links a thin adapter that copies the
+ * fields of each ggml_tensor it passes into a b200_tensor (INTEGRATION.md shows it), and
+ * everything the reference decides -- which ops to claim, how to walk a graph, which route
+ * computed what -- is decided here, in C++, over those descriptors. The three claimed ops run
+ * as sm_100a CUDA kernels (ggml-b200-kernels.h); nothing claimed ever runs on the CPU.
+ */
+#ifndef GGML_B200_H
+#define GGML_B200_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_MAX_DIMS      4
+#define B200_MAX_SRC       10
+#define B200_MAX_OP_PARAMS 16   /* int32 words, as ggml's GGML_MAX_OP_PARAMS / 4 */
+#define B200_MAX_NAME      64
+
+/* The ops the backend distinguishes. A ggml adapter maps ggml_op values by NAME
+ * (ggml_op_name), as the reference's op-ordinal check does (ggml-rocket.cpp:8231-8252). */
+typedef enum {
+    B200_OP_NONE = 0,
+    B200_OP_RESHAPE,
+    B200_OP_VIEW,
+    B200_OP_PERMUTE,
+    B200_OP_TRANSPOSE,
+    B200_OP_MUL_MAT,
+    B200_OP_MUL_MAT_ID,
+    B200_OP_FLASH_ATTN_EXT,
+    B200_OP_OTHER,
+} b200_op;
+
+/* Precision ranks of ggml's precision contract (op_params, ggml-rocket.cpp:7334-7355). */
+enum {
+    B200_PREC_UNDECLARED = 0,
+    B200_PREC_F32 = 10,
+    B200_PREC_BF16 = 15,
+    B200_PREC_F16 = 20,
+    B200_PREC_Q8 = 30,
+    B200_PREC_Q4 = 40,
+};
+
+/* op_params[1] of a MUL_MAT whose src0 is a Walsh-Hadamard matrix (ggml's
+ * GGML_HINT_SRC0_IS_HADAMARD; the adapter translates the host's value to this one). */
+#define B200_HINT_SRC0_IS_HADAMARD 1
+
+/* The fields of a ggml_tensor the backend reads. Strides nb[] are in bytes. `data` is host
+ * memory unless `on_device` is set, in which case it is device memory of the backend's GPU. */
+typedef struct b200_tensor {
+    int32_t type;                              /* ggml_type numbering */
+    int32_t op;                                /* b200_op */
+    int64_t ne[B200_MAX_DIMS];
+    size_t  nb[B200_MAX_DIMS];
+    int32_t op_params[B200_MAX_OP_PARAMS];
+    struct b200_tensor * src[B200_MAX_SRC];
+    void *  data;
+    int32_t on_device;
+    int32_t readable;                          /* 0: the bytes are in a layout the backend cannot read
+                                                  (a CPU_REPACK buffer, ggml-rocket.cpp:7773-7794) */
+    char    name[B200_MAX_NAME];
+} b200_tensor;
+
+typedef struct b200_backend * b200_backend_t;
+
+/* ggml_status values graph_compute returns. */
+enum { B200_STATUS_SUCCESS = 0, B200_STATUS_FAILED = -1, B200_STATUS_ALLOC_FAILED = -2 };
+
+/* ---- registry (ggml-rocket.cpp:7848-7880, 7918-7926) ------------------------------------ */
+const char * ggml_backend_b200_reg_name(void);                       /* "B200" */
+int          ggml_backend_b200_reg_device_count(void);               /* visible CUDA devices */
+/* Maps a ggml op name to a b200_op (B200_OP_OTHER when the backend has no use for it). */
+int          ggml_backend_b200_op_from_name(const char * ggml_op_name);
+
+/* ---- device (ggml-rocket.cpp:7830-7842) ---------------------------------------------------- */
+const char * ggml_backend_b200_device_name(int device);
+int          ggml_backend_b200_device_description(int device, char * buf, size_t n);
+int          ggml_backend_b200_device_memory(int device, size_t * free_bytes, size_t * total_bytes);
+/* The claim rules: supports_op (ggml-rocket.cpp:7410-7772) and offload_op (:7820-7827). */
+bool         ggml_backend_b200_supports_op(const b200_tensor * op);
+bool         ggml_backend_b200_offload_op(const b200_tensor * op);
+
+/* ---- backend (ggml-rocket.h:24-93, ggml-rocket.cpp:8024-8217) ------------------------------ */
+/* Creates an instance on the current CUDA device; NULL when there is none. Device state
+ * (stream, workspace, weight cache) is created lazily at the first graph_compute. */
+b200_backend_t ggml_backend_b200_init(void);
+void           ggml_backend_b200_free(b200_backend_t backend);
+bool           ggml_backend_is_b200(const void * backend);
+/* The number of GPUs an op may be spread over (the reference's set_n_threads, which spreads
+ * an op over NPU workers). Clamped to 1..8. */
+void           ggml_backend_b200_set_n_gpus(b200_backend_t backend, int n_gpus);
+/* Distinct MoE expert stacks held device-resident, and those streamed per call. */
+void           ggml_backend_b200_moe_stats(b200_backend_t backend, long * n_resident, long * n_streamed);
+/* Ops completed per route ("f16", "q8_0", "q4_K", "q6_K", "fused", "moe", "fa"); NULL: total. */
+long           ggml_backend_b200_route_ops(b200_backend_t backend, const char * route);
+/* Always 0: a claimed op is never computed on the CPU. Kept so a test can assert it. */
+long           ggml_backend_b200_cpu_fallbacks(b200_backend_t backend);
+/* Kernel launches and device faults reported through the device error word. */
+long           ggml_backend_b200_device_errors(b200_backend_t backend);
+/* Computes the claimed nodes of one graph split in order (views are no-ops); any other op, a
+ * malformed MUL_MAT_ID id, or a device error returns B200_STATUS_FAILED. */
+int            ggml_backend_b200_graph_compute(b200_backend_t backend, b200_tensor * const * nodes, int n_nodes);
+/* Bytes held by the device-resident weight cache, and its entry count. */
+size_t         ggml_backend_b200_weight_cache_bytes(b200_backend_t backend, long * n_entries);
+
+/* ---- the weight identity (ggml-rocket.cpp:4124-4222) ---------------------------------------- */
+/* The cache key of a weight: its name with the scheduler's copy prefixes stripped, the type and
+ * shape, and a 64-bit fingerprint of 16 evenly spaced 64-byte samples of its bytes. Writes at most
+ * n bytes (NUL-terminated) and returns the key length; 0 for a tensor the cache must not key
+ * (an unnamed or scheduler-generated "leaf_N" / "node_N" name). */
+size_t         ggml_backend_b200_weight_key(const b200_tensor * w, char * buf, size_t n);
+
+/* ---- the device-route circuit breaker (ggml-rocket.cpp:263-307) ----------------------------- */
+/* Replays a sequence of route outcomes through one breaker and writes, per call, whether the
+ * route was attempted (1) or bypassed (0); a bypassed call's rc is ignored. For tests. */
+void           ggml_backend_b200_breaker_replay(const int * rcs, int n, int * attempted);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GGML_B200_H */
