@@ -84,7 +84,8 @@ def build(verbose_ptxas=False, jobs=8):
     for p in procs:
         if p.wait() != 0:
             raise SystemExit("compile failed")
-    if cmds or not os.path.exists(LIB):
+    stale = not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs)
+    if cmds or stale:
         link = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart"]
         run(link)
     return LIB

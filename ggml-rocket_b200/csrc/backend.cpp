@@ -629,7 +629,7 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
     for (int g = 0; g < ng; g++) {
         const b200_tensor* d = nodes[g];
         if (!d->on_device) need_out += (nbytes(d) + 255) & ~(size_t)255;
-        need_ws = std::max(need_ws, b200_gemm_packed_workspace_size(M, d->src[0]->ne[1], K));
+        need_ws = std::max(need_ws, b200_gemm_packed_workspace_size(kernel_wtype(d->src[0]->type), M, d->src[0]->ne[1], K));
     }
     const size_t a16_bytes = ((size_t)M * K * 2 + 255) & ~(size_t)255;
     const size_t sc_bytes = ((size_t)M * 4 + 255) & ~(size_t)255;

@@ -8,12 +8,20 @@
 // contiguous). Small token counts (M = 32..64) keep the full 128-row weight tile.
 //
 // Warp roles in one CTA (persistent over work units):
-//   warp 0        TMA producer: the activation tile [BT x 64] (and the F16 weight tile)
+//   warp 0        TMA producer of the activation tile [BT x 64]
 //   warp 1        TMEM allocator and the single-thread tcgen05.mma issuer
-//   warps 2..5    epilogue: TMEM -> registers -> scaled f32 stores (or split-K partials)
-//   warps 6..9    (quantized weights only) dequant producers: each thread decodes one
-//                 weight row's 64-weight chunk to fp16 and writes it, 128-byte swizzled,
-//                 straight into the stage the MMA reads -- no fp16 weight copy in HBM.
+//   warps 2..5    epilogue: TMEM -> registers -> a 32x32 shared-memory transpose -> scaled
+//                 16-byte stores of whole 128-byte output lines (or split-K partials)
+//   warp 6        TMA producer of the F16 weight tile, or (quantized weights) of the raw
+//                 quantized super-block tile: 128 rows x 256 weights into a 2-3 deep ring,
+//                 with the TMA's L2 prefetch running 4 super-blocks further ahead
+//   (quantized weights only)
+//   8 dequant warps (7, 8, 10, 11, 12, 14, 15, 16 -- none shares a scheduler with warp 1):
+//                 thread (row r, half h) decodes 32 weights of row r's 64-weight chunk from
+//                 the ring to fp16 and writes them, 128-byte swizzled, straight into the
+//                 stage the MMA reads -- no fp16 weight copy in HBM.
+// Each producer thread only issues: one TMA or barrier operation costs it ~70-180 clocks, so
+// the two operands have separate producers.
 // Two TMEM accumulators alternate, so the epilogue of one unit overlaps the next unit's
 // main loop. Every wait is bounded (ptx.cuh).
 #pragma once
@@ -31,10 +39,6 @@ constexpr int GEMM_BN = 128;   // weight rows per tile (tcgen05 M)
 constexpr int GEMM_BK = 64;    // K per pipeline stage (one 128-byte swizzle row of fp16)
 
 struct GemmArgs {
-    const uint8_t* w;          // packed weight plane A (quantized types)
-    const uint16_t* wd;        // packed weight plane D (Q6_K / Q8_0 scales)
-    int64_t w_row_bytes;       // plane A row stride, bytes
-    int64_t wd_row_elems;      // plane D row stride, fp16 elements
     const float* scales;       // [M] per-token activation scale
     float* out;                // dst (splits == 1) or split-K partials
     int64_t ldo;               // row stride of out, floats
@@ -56,37 +60,78 @@ struct UnitCoords {
     int t0, t_end, n0, wrow0, ks, kb0, kb1;
 };
 
+// Raw quantized tile of one 256-weight super-block x 128 rows, as the TMA writes it.
+template <int WT>
+struct RawCfg {
+    static constexpr int ROW = WT == WT_Q4_K ? 144 : WT == WT_Q6_K ? 208 : WT == WT_Q8_0 ? 272 : 0;   // bytes
+    static constexpr int A_BYTES = ROW * GEMM_BN;
+    static constexpr int D_BYTES = WT == WT_Q6_K ? GEMM_BN * 2 : 0;    // transposed d plane box
+    static constexpr int STAGE = (A_BYTES + D_BYTES + 1023) / 1024 * 1024;
+    // the ring covers L2 latency; the L2 prefetch ahead of it covers HBM latency
+    static constexpr int STAGES = WT == WT_F16 ? 0 : WT == WT_Q4_K ? 3 : 2;
+    static constexpr int PREFETCH = 4;                                   // super-blocks ahead into L2
+    static constexpr int X_ELEMS = ROW / 2;                              // uint16 box width
+};
+
+// Warp roles. The dequant warps never share a scheduler (warp % 4) with the MMA warp.
+constexpr int W_APROD = 0, W_MMA = 1, W_EPI0 = 2, W_WPROD = 6;
+constexpr int DEQ_WARPS = 8;
+__device__ __forceinline__ int dequant_slot(int warp) {
+    switch (warp) {
+        case 7: return 0;
+        case 8: return 1;
+        case 10: return 2;
+        case 11: return 3;
+        case 12: return 4;
+        case 14: return 5;
+        case 15: return 6;
+        case 16: return 7;
+        default: return -1;
+    }
+}
+
 template <int BT, int WT>
 struct GemmCfg {
     static constexpr bool QUANT = (WT != WT_F16);
     static constexpr int A_BYTES = BT * GEMM_BK * 2;
     static constexpr int W_BYTES = GEMM_BN * GEMM_BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + W_BYTES;
-    static constexpr int STAGES = (196608 / STAGE_BYTES) > 8 ? 8 : (196608 / STAGE_BYTES);
-    static constexpr int THREADS = QUANT ? 320 : 192;
+    static constexpr int RAW_TOTAL = RawCfg<WT>::STAGE * RawCfg<WT>::STAGES;
+    static constexpr int EPI_BYTES = 4 * 32 * 32 * 4;          // a 32 x 32 f32 transpose tile per epilogue warp
+    static constexpr int BUDGET = 232448 - 1024 - 256 - RAW_TOTAL - EPI_BYTES;
+    static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
+    static constexpr int THREADS = QUANT ? 17 * 32 : 7 * 32;
+    static constexpr int DEQ_THREADS = DEQ_WARPS * 32;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    static constexpr int RAW_OFF = STAGES * STAGE_BYTES;
+    static constexpr int EPI_OFF = RAW_OFF + RAW_TOTAL;
+    static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
+    static constexpr int SMEM = BAR_OFF + BAR_BYTES + 1024;
     static constexpr uint32_t TMEM_COLS = 2 * BT;
     static constexpr uint32_t IDESC = idesc_f16_f32(GEMM_BN, BT);
+    static_assert(STAGES >= 2, "pipeline too shallow");
 };
 
 template <int BT, int WT, bool GROUPED>
 __global__ void __launch_bounds__(GemmCfg<BT, WT>::THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-            const GemmArgs args) {
+            const __grid_constant__ CUtensorMap tmD, const GemmArgs args) {
     using C = GemmCfg<BT, WT>;
+    using RC = RawCfg<WT>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t bar_base = sbase + STAGES * C::STAGE_BYTES;
+    const uint32_t bar_base = sbase + C::BAR_OFF;
     auto full_bar = [&](int s) { return bar_base + 8u * s; };
     auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
     auto tfull_bar = [&](int a) { return bar_base + 8u * (2 * STAGES + a); };
     auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * STAGES + 2 + a); };
     const uint32_t drain_bar = bar_base + 8u * (2 * STAGES + 4);
-    uint8_t* misc = smem + STAGES * C::STAGE_BYTES + 8 * (2 * STAGES + 5);
+    auto rfull_bar = [&](int s) { return bar_base + 8u * (2 * STAGES + 5 + s); };
+    auto rempty_bar = [&](int s) { return bar_base + 8u * (2 * STAGES + 8 + s); };
+    uint8_t* misc = smem + C::BAR_OFF + 8 * (2 * STAGES + 11);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
 
@@ -95,20 +140,25 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            mbar_init(full_bar(s), C::QUANT ? 5 : 1);
+            mbar_init(full_bar(s), C::QUANT ? 1 + DEQ_WARPS : 2);
             mbar_init(empty_bar(s), 1);
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(tfull_bar(a), 1);
             mbar_init(tempty_bar(a), 4);
         }
+        for (int s = 0; s < RC::STAGES; s++) {
+            mbar_init(rfull_bar(s), 1);
+            mbar_init(rempty_bar(s), DEQ_WARPS);
+        }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
-        if (!C::QUANT) tma_prefetch_desc(&tmW);
+        tma_prefetch_desc(&tmW);
+        if (WT == WT_Q6_K) tma_prefetch_desc(&tmD);
     }
-    if (warp == 1) {
+    if (warp == W_MMA) {
         tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
         tmem_relinquish();
     }
@@ -154,41 +204,84 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         return c;
     };
 
-    if (warp == 0) {
-        // ---------------- TMA producer ----------------
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            int issued_phase[STAGES];
-#pragma unroll
-            for (int s = 0; s < STAGES; s++) issued_phase[s] = -1;
-            bool ok = true;
-            for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-                const UnitCoords uc = unit_coords(u);
-                for (int kb = uc.kb0; kb < uc.kb1; kb++) {
-                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, args.err, ERR_WAIT_PRODUCER, abort_flag)) { ok = false; break; }
-                    const uint32_t sa = sbase + stage * C::STAGE_BYTES;
-                    mbar_arrive_expect_tx(full_bar(stage), C::QUANT ? C::A_BYTES : C::A_BYTES + C::W_BYTES);
+    // One operand's TMA producer over the A/W stage ring (W only for F16 weights).
+    auto produce_stages = [&](bool is_w) {
+        int stage = 0;
+        uint32_t phase = 0;
+        int issued = -1;                                 // phase of the last issue per stage, packed
+        uint32_t issued_mask = 0, issued_par = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+            const UnitCoords uc = unit_coords(u);
+            for (int kb = uc.kb0; kb < uc.kb1; kb++) {
+                if (!mbar_wait(empty_bar(stage), phase ^ 1u, args.err, ERR_WAIT_PRODUCER, abort_flag)) { ok = false; break; }
+                const uint32_t sa = sbase + stage * C::STAGE_BYTES;
+                if (is_w) {
+                    mbar_arrive_expect_tx(full_bar(stage), C::W_BYTES);
+                    tma_load_2d(sa + C::A_BYTES, &tmW, full_bar(stage), kb * GEMM_BK, uc.wrow0);
+                } else {
+                    mbar_arrive_expect_tx(full_bar(stage), C::A_BYTES);
                     tma_load_2d(sa, &tmA, full_bar(stage), kb * GEMM_BK, uc.t0);
-                    if (!C::QUANT) tma_load_2d(sa + C::A_BYTES, &tmW, full_bar(stage), kb * GEMM_BK, uc.wrow0);
-                    issued_phase[stage] = (int)phase;
-                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
-            }
-            if (!ok) {   // let every copy already issued land before the CTA exits
-#pragma unroll
-                for (int s = 0; s < STAGES; s++)
-                    if (issued_phase[s] >= 0 && !mbar_drain(full_bar(s), (uint32_t)issued_phase[s]))
-                        atomicCAS(args.err, 0, ERR_WAIT_DRAIN);
+                issued_mask |= 1u << stage;
+                issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
             }
         }
-    } else if (warp == 1) {
+        (void)issued;
+        if (!ok) {   // let every copy already issued land before the CTA exits
+            for (int s = 0; s < STAGES; s++)
+                if (((issued_mask >> s) & 1u) && !mbar_drain(full_bar(s), (issued_par >> s) & 1u))
+                    atomicCAS(args.err, 0, ERR_WAIT_DRAIN);
+        }
+    };
+
+    if (warp == W_APROD) {
+        if (lane == 0) produce_stages(false);
+    } else if (warp == W_WPROD) {
+        if (lane == 0) {
+            if constexpr (!C::QUANT) {
+                produce_stages(true);
+            } else {
+                // ---------------- raw quantized tiles ----------------
+                int rs = 0;
+                uint32_t rph = 0;
+                uint32_t issued_mask = 0, issued_par = 0;
+                bool ok = true;
+                for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+                    const UnitCoords uc = unit_coords(u);
+                    const int sb0 = uc.kb0 >> 2, sb_end = (uc.kb1 + 3) >> 2;
+                    for (int pf = sb0; pf < sb0 + RC::PREFETCH && pf < sb_end; pf++)
+                        tma_prefetch_l2_2d(&tmW, pf * RC::X_ELEMS, uc.wrow0);
+                    for (int sb = sb0; sb < sb_end; sb++) {
+                        if (sb + RC::PREFETCH < sb_end) tma_prefetch_l2_2d(&tmW, (sb + RC::PREFETCH) * RC::X_ELEMS, uc.wrow0);
+                        if (!mbar_wait(rempty_bar(rs), rph ^ 1u, args.err, ERR_WAIT_PRODUCER, abort_flag)) { ok = false; break; }
+                        const uint32_t dst = sbase + C::RAW_OFF + rs * RC::STAGE;
+                        mbar_arrive_expect_tx(rfull_bar(rs), RC::A_BYTES + RC::D_BYTES);
+                        tma_load_2d(dst, &tmW, rfull_bar(rs), sb * RC::X_ELEMS, uc.wrow0);
+                        if constexpr (WT == WT_Q6_K) tma_load_2d(dst + RC::A_BYTES, &tmD, rfull_bar(rs), uc.wrow0, sb);
+                        issued_mask |= 1u << rs;
+                        issued_par = (issued_par & ~(1u << rs)) | (rph << rs);
+                        if (++rs == RC::STAGES) { rs = 0; rph ^= 1u; }
+                    }
+                }
+                if (!ok) {
+                    for (int s2 = 0; s2 < RC::STAGES; s2++)
+                        if (((issued_mask >> s2) & 1u) && !mbar_drain(rfull_bar(s2), (issued_par >> s2) & 1u))
+                            atomicCAS(args.err, 0, ERR_WAIT_DRAIN);
+                }
+            }
+        }
+    } else if (warp == W_MMA) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
             int lt = 0;
             bool ok = true;
+            // descriptors of stage 0; a stage adds STAGE_BYTES, a 16-element K step 32 bytes (>> 4)
+            const uint64_t wdesc0 = sdesc_k_sw128(sbase + C::A_BYTES);
+            const uint64_t adesc0 = sdesc_k_sw128(sbase);
             for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, lt++) {
                 const UnitCoords uc = unit_coords(u);
                 const int kb0 = uc.kb0, kb1 = uc.kb1;
@@ -200,13 +293,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                 for (int kb = kb0; kb < kb1; kb++) {
                     if (!mbar_wait(full_bar(stage), phase, args.err, ERR_WAIT_MMA, abort_flag)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t sa = sbase + stage * C::STAGE_BYTES;
-                    const uint32_t sw = sa + C::A_BYTES;
+                    const uint64_t soff = (uint64_t)((stage * C::STAGE_BYTES) >> 4);
 #pragma unroll
-                    for (int k = 0; k < GEMM_BK / 16; k++) {
-                        mma_f16(d_tmem, sdesc_k_sw128(sw + 32u * k), sdesc_k_sw128(sa + 32u * k), C::IDESC,
+                    for (int k = 0; k < GEMM_BK / 16; k++)
+                        mma_f16(d_tmem, wdesc0 + soff + 2 * k, adesc0 + soff + 2 * k, C::IDESC,
                                 (kb > kb0 || k > 0) ? 1u : 0u);
-                    }
                     mma_commit(empty_bar(stage));
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
@@ -217,9 +308,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             mma_commit(drain_bar);
             if (!mbar_drain(drain_bar, 0)) atomicCAS(args.err, 0, ERR_WAIT_DRAIN);
         }
-    } else if (warp < 6) {
+    } else if (warp >= W_EPI0 && warp < W_EPI0 + 4) {
         // ---------------- epilogue ----------------
-        const int q = warp & 3;                       // TMEM lane quadrant this warp may read
+        const int q = warp & 3;                          // TMEM lane quadrant this warp may read
+        float* es = reinterpret_cast<float*>(smem + C::EPI_OFF) + (warp - W_EPI0) * 1024;
+        const float4* es4 = reinterpret_cast<const float4*>(es);
+        const int cc = lane & 7;                         // float4 column of the read-back
         int lt = 0;
         for (int u = blockIdx.x; u < num_units; u += gridDim.x, lt++) {
             const UnitCoords uc = unit_coords(u);
@@ -227,68 +321,80 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             const uint32_t aphase = (uint32_t)(lt >> 1) & 1u;
             if (!mbar_wait(tfull_bar(acc), aphase, args.err, ERR_WAIT_EPILOGUE, abort_flag)) break;
             tc_fence_after();
-            const int n = uc.n0 + 32 * q + lane;
+            const int nb = uc.n0 + 32 * q + 4 * cc;      // this lane's 4 output columns
             float* obase = args.out + (size_t)uc.ks * args.split_stride;
             const bool scaled = args.splits == 1;
-            for (int c0 = 0; c0 < BT; c0 += 16) {
+            for (int c0 = 0; c0 < BT; c0 += 32) {
                 if (uc.t0 + c0 >= uc.t_end) break;
-                uint32_t r[16];
-                tmem_ld16(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BT + c0), r);
+                uint32_t r[32];
+                tmem_ld32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BT + c0), r);
                 tmem_ld_wait();
-                if (n < args.N) {
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const int t = uc.t0 + c0 + j;
-                        if (t < uc.t_end) {
-                            float v = __uint_as_float(r[j]);
-                            if (scaled) v *= __ldg(args.scales + t);
-                            if constexpr (GROUPED) {
-                                char* drow = reinterpret_cast<char*>(args.out) + (int64_t)__ldg(args.g_tok + t) * args.d_nb2 +
-                                             (int64_t)__ldg(args.g_slot + t) * args.d_nb1;
-                                reinterpret_cast<float*>(drow)[n] = v;
-                            } else {
-                                obase[(size_t)t * args.ldo + n] = v;
-                            }
+                for (int j = 0; j < 32; j++) es[j * 32 + lane] = __uint_as_float(r[j]);
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int jr = (lane >> 3) + 4 * i;
+                    const int t = uc.t0 + c0 + jr;
+                    if (t < uc.t_end && nb < args.N) {
+                        float4 v = es4[jr * 8 + cc];
+                        if (scaled) {
+                            const float sc = __ldg(args.scales + t);
+                            v.x *= sc; v.y *= sc; v.z *= sc; v.w *= sc;
                         }
+                        float* dp;
+                        if constexpr (GROUPED)
+                            dp = reinterpret_cast<float*>(reinterpret_cast<char*>(args.out) +
+                                                          (int64_t)__ldg(args.g_tok + t) * args.d_nb2 +
+                                                          (int64_t)__ldg(args.g_slot + t) * args.d_nb1) + nb;
+                        else
+                            dp = obase + (size_t)t * args.ldo + nb;
+                        *reinterpret_cast<float4*>(dp) = v;
                     }
                 }
+                __syncwarp();
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty_bar(acc));
         }
-    } else {
-        // ---------------- dequant producers (quantized weights) ----------------
+    } else if (C::QUANT && dequant_slot(warp) >= 0) {
+        // ---------------- dequant (quantized weights) ----------------
         if constexpr (C::QUANT) {
-            const int r = threadIdx.x - 192;          // weight row within the tile, 0..127
-            int stage = 0;
-            uint32_t phase = 0;
+            const int dq = dequant_slot(warp);
+            const int r = (dq & 3) * 32 + lane;          // weight row within the tile
+            const int h = dq >> 2;                       // which 32 of the chunk's 64 weights
+            int stage = 0, rs = 0;
+            uint32_t phase = 0, rph = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
                 const UnitCoords uc = unit_coords(u);
-                const int n = uc.n0 + r;
-                const int64_t wr = (int64_t)uc.wrow0 + r;
-                const uint8_t* wrow = args.w + (size_t)wr * args.w_row_bytes;
-                const uint16_t* drow = args.wd ? args.wd + (size_t)wr * args.wd_row_elems : nullptr;
-                for (int kb = uc.kb0; kb < uc.kb1; kb++) {
-                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, args.err, ERR_WAIT_DEQUANT, abort_flag)) { ok = false; break; }
-                    uint32_t h[32];
-                    if (n < args.N) {
-                        if constexpr (WT == WT_Q4_K) decode_q4k_chunk(wrow, kb, h);
-                        else if constexpr (WT == WT_Q6_K) decode_q6k_chunk(wrow, drow, kb, h);
-                        else decode_q8_0_chunk(wrow, drow, kb, h);
-                    } else {
+                for (int sb = uc.kb0 >> 2; sb * 4 < uc.kb1 && ok; sb++) {
+                    if (!mbar_wait(rfull_bar(rs), rph, args.err, ERR_WAIT_DEQUANT, abort_flag)) { ok = false; break; }
+                    const uint8_t* raw = smem + C::RAW_OFF + rs * RC::STAGE;
+                    const uint8_t* rrow = raw + r * RC::ROW;
+                    float d6 = 0.0f;
+                    if constexpr (WT == WT_Q6_K) d6 = __half2float(reinterpret_cast<const __half*>(raw + RC::A_BYTES)[r]);
+                    const int k_lo = max(uc.kb0, 4 * sb), k_hi = min(uc.kb1, 4 * sb + 4);
+                    for (int kb = k_lo; kb < k_hi; kb++) {
+                        if (!mbar_wait(empty_bar(stage), phase ^ 1u, args.err, ERR_WAIT_DEQUANT, abort_flag)) { ok = false; break; }
+                        uint32_t o[16];
+                        if constexpr (WT == WT_Q4_K) decode_q4k_half(rrow, kb & 3, h, o);
+                        else if constexpr (WT == WT_Q6_K) decode_q6k_half(rrow, d6, kb & 3, h, o);
+                        else decode_q8_0_half(rrow, kb & 3, h, o);
+                        const uint32_t sw = sbase + stage * C::STAGE_BYTES + C::A_BYTES;
 #pragma unroll
-                        for (int i = 0; i < 32; i++) h[i] = 0u;
+                        for (int c = 0; c < 4; c++)
+                            st_shared_v4(sw + sw128_offset((uint32_t)r, (uint32_t)(4 * h + c)), o[4 * c], o[4 * c + 1],
+                                         o[4 * c + 2], o[4 * c + 3]);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(full_bar(stage));
+                        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                     }
-                    const uint32_t sw = sbase + stage * C::STAGE_BYTES + C::A_BYTES;
-#pragma unroll
-                    for (int c = 0; c < 8; c++)
-                        st_shared_v4(sw + sw128_offset((uint32_t)r, (uint32_t)c), h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
-                    fence_proxy_async_smem();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(full_bar(stage));
-                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                    if (lane == 0) mbar_arrive(rempty_bar(rs));
+                    if (++rs == RC::STAGES) { rs = 0; rph ^= 1u; }
                 }
             }
         }
@@ -296,7 +402,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == W_MMA) {
         tc_fence_after();
         tmem_dealloc(tmem_base, C::TMEM_COLS);
     }

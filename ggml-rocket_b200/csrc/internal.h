@@ -16,7 +16,7 @@ size_t packed_weight_bytes(int type, int64_t N, int64_t K, size_t* plane_d_off);
 bool weight_type_supported(int type, int64_t K);
 int mul_mat_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const float* src1, int64_t lda, int64_t M,
                  float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t st);
-size_t mul_mat_workspace(int64_t M, int64_t N, int64_t K);
+size_t mul_mat_workspace(int wtype, int64_t M, int64_t N, int64_t K);
 int act_pack_impl(const float* src1, int64_t lda, int64_t M, int64_t K, __half* a16, float* scales, cudaStream_t st);
 int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int64_t n_expert, const __half* a16,
                       const float* scales, int64_t rows, int bt, const int32_t* off, const int32_t* tile_start,

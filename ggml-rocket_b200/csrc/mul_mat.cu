@@ -145,29 +145,32 @@ __global__ void pack_q6k_kernel(const uint8_t* __restrict__ src, int64_t N, int6
                                 uint8_t* __restrict__ dstA, uint16_t* __restrict__ dstD) {
     const int64_t total = N * nsb;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = i / nsb, sb = i % nsb;
         const uint8_t* b = src + i * 210;
         uint8_t* o = dstA + i * 208;
         for (int j = 0; j < 208; j++) o[j] = b[j];
-        dstD[i] = (uint16_t)(b[208] | (b[209] << 8));
+        dstD[sb * N + n] = (uint16_t)(b[208] | (b[209] << 8));   // transposed: [sb][row]
     }
 }
 
 __global__ void pack_q8_0_kernel(const uint8_t* __restrict__ src, int64_t N, int64_t nblk, int64_t ngrp,
-                                 uint8_t* __restrict__ dstA, uint16_t* __restrict__ dstD) {
-    // nblk native 32-weight blocks per row, packed into ngrp groups of 8 (zero-padded).
+                                 uint8_t* __restrict__ dst) {
+    // nblk native 32-weight blocks per row -> ngrp groups of 8 as {d[8], qs[256]} (zero-padded).
     const int64_t total = N * ngrp * 8;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t n = i / (ngrp * 8);
         const int64_t j = i % (ngrp * 8);
-        uint8_t* o = dstA + n * ngrp * 256 + j * 32;
-        uint16_t* od = dstD + n * ngrp * 8 + j;
+        uint8_t* g = dst + (n * ngrp + j / 8) * 272;
+        uint8_t* od = g + 2 * (j % 8);
+        uint8_t* oq = g + 16 + 32 * (j % 8);
         if (j < nblk) {
             const uint8_t* b = src + (n * nblk + j) * 34;
-            *od = (uint16_t)(b[0] | (b[1] << 8));
-            for (int q = 0; q < 32; q++) o[q] = b[2 + q];
+            od[0] = b[0];
+            od[1] = b[1];
+            for (int q = 0; q < 32; q++) oq[q] = b[2 + q];
         } else {
-            *od = 0;
-            for (int q = 0; q < 32; q++) o[q] = 0;
+            od[0] = od[1] = 0;
+            for (int q = 0; q < 32; q++) oq[q] = 0;
         }
     }
 }
@@ -221,6 +224,21 @@ bool make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_
     return r == CUDA_SUCCESS;
 }
 
+// A 2-D uint16 tensor map [rows, cols] (cols innermost, row pitch in bytes), box [box_rows,
+// box_cols], no swizzle: the raw quantized tiles and the transposed d plane.
+static bool make_tmap_2d_u16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_bytes,
+                             uint32_t box_rows, uint32_t box_cols) {
+    EncodeTiledFn fn = get_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {pitch_bytes};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // The launch plan for one MUL_MAT: token tile, split-K factor and unit count.
@@ -228,27 +246,51 @@ struct GemmPlan {
     int bt, splits, kb_per_split, nkb, ntn, ntt, units, grid;
 };
 
-static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms) {
-    GemmPlan p{};
-    p.nkb = (int)((K + GEMM_BK - 1) / GEMM_BK);   // Q8_0 rows are padded to 256 with zero blocks,
-                                                  // but the chunks past K need no MMA: A is zero there
-    p.ntn = (int)((N + GEMM_BN - 1) / GEMM_BN);
-    p.bt = M <= 32 ? 32 : M <= 64 ? 64 : M <= 1024 ? 128 : 256;
-    p.ntt = (int)((M + p.bt - 1) / p.bt);
-    const int tiles = p.ntn * p.ntt;
-    int splits = 1;
-    if (tiles < sms) {
-        splits = sms / tiles;
-        const int max_by_k = p.nkb / 4 > 0 ? p.nkb / 4 : 1;
-        if (splits > max_by_k) splits = max_by_k;
-        if (splits > 16) splits = 16;
-        if (splits < 1) splits = 1;
+// Choose the token tile and the split-K factor from a cost model (SM clocks): a unit of
+// kb_per_split K-chunks costs per chunk the slowest of the tensor core (128 x BT x 64 MACs at
+// 4096 MAC/clk), the decode of 8192 quantized weights by 8 warps, and the L2 feed of its
+// operand tiles; units run in waves over the SMs; a split adds its partial-sum round trip.
+static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms, int wtype) {
+    const bool quant = wtype != WT_F16;
+    const int nkb = (int)((K + GEMM_BK - 1) / GEMM_BK);
+    const int ntn = (int)((N + GEMM_BN - 1) / GEMM_BN);
+    GemmPlan best{};
+    double best_t = 1e30;
+    const int bts[4] = {32, 64, 128, 256};
+    for (int bi = 0; bi < 4; bi++) {
+        const int bt = bts[bi];
+        if (bi > 0 && bts[bi - 1] >= M) break;          // a smaller tile already covers M
+        const int ntt = (int)((M + bt - 1) / bt);
+        const int tiles = ntn * ntt;
+        const double mma = bt < 64 ? 128.0 : 2.0 * bt;
+        const double decode = quant ? 300.0 : 0.0;
+        const double feed = (bt * 128.0 + (quant ? 4600.0 : 16384.0)) / 96.0;
+        const double per_kb = (mma > decode ? (mma > feed ? mma : feed) : (decode > feed ? decode : feed)) + 16.0;
+        for (int splits = 1; splits <= 16; splits++) {
+            int kbs = (nkb + splits - 1) / splits;
+            if (quant) kbs = (kbs + 3) / 4 * 4;
+            const int sp = (nkb + kbs - 1) / kbs;
+            if (sp != splits && splits > 1) continue;
+            const int units = tiles * sp;
+            const int grid = units < sms ? units : sms;
+            const int waves = (units + grid - 1) / grid;
+            double t = waves * (kbs * per_kb + 800.0);
+            if (sp > 1) t += 3000.0 + (double)(sp + 1) * M * N * 4.0 / 3200.0;
+            if (t < best_t * 0.97) {
+                best_t = t;
+                best.bt = bt;
+                best.splits = sp;
+                best.kb_per_split = kbs;
+                best.nkb = nkb;
+                best.ntn = ntn;
+                best.ntt = ntt;
+                best.units = units;
+                best.grid = grid;
+            }
+            if (units >= 4 * sms) break;
+        }
     }
-    p.kb_per_split = (p.nkb + splits - 1) / splits;
-    p.splits = (p.nkb + p.kb_per_split - 1) / p.kb_per_split;   // no empty split
-    p.units = tiles * p.splits;
-    p.grid = p.units < sms ? p.units : sms;
-    return p;
+    return best;
 }
 
 struct MulMatWorkspace {
@@ -265,8 +307,8 @@ static MulMatWorkspace mm_workspace_layout(int64_t M, int64_t N, int64_t K, cons
 }
 
 template <int BT, int WT, bool GROUPED>
-static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& a, int grid,
-                                 cudaStream_t st) {
+static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmD,
+                                 const GemmArgs& a, int grid, cudaStream_t st) {
     using C = GemmCfg<BT, WT>;
     static bool attr_set[64] = {false};
     int dev = 0;
@@ -277,55 +319,59 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW,
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
-    gemm_kernel<BT, WT, GROUPED><<<grid, C::THREADS, C::SMEM, st>>>(tmA, tmW, a);
+    gemm_kernel<BT, WT, GROUPED><<<grid, C::THREADS, C::SMEM, st>>>(tmA, tmW, tmD, a);
     return cudaGetLastError();
 }
 
 template <int WT, bool GROUPED>
-static cudaError_t launch_gemm_bt(int bt, const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& a,
-                                  int grid, cudaStream_t st) {
+static cudaError_t launch_gemm_bt(int bt, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmD,
+                                  const GemmArgs& a, int grid, cudaStream_t st) {
     switch (bt) {
-        case 32: return launch_gemm_t<32, WT, GROUPED>(tmA, tmW, a, grid, st);
-        case 64: return launch_gemm_t<64, WT, GROUPED>(tmA, tmW, a, grid, st);
-        case 128: return launch_gemm_t<128, WT, GROUPED>(tmA, tmW, a, grid, st);
-        default: return launch_gemm_t<256, WT, GROUPED>(tmA, tmW, a, grid, st);
+        case 32: return launch_gemm_t<32, WT, GROUPED>(tmA, tmW, tmD, a, grid, st);
+        case 64: return launch_gemm_t<64, WT, GROUPED>(tmA, tmW, tmD, a, grid, st);
+        case 128: return launch_gemm_t<128, WT, GROUPED>(tmA, tmW, tmD, a, grid, st);
+        default: return launch_gemm_t<256, WT, GROUPED>(tmA, tmW, tmD, a, grid, st);
     }
 }
 
-// Fill the weight-side fields of GemmArgs (and the F16 weight tensor map) for `wrows` packed
-// weight rows of K.
-static bool setup_weight_args(int wtype, const void* w_packed, int64_t wrows, int64_t K, GemmArgs& a, CUtensorMap& tmW,
-                              const CUtensorMap& tmA) {
+// Fill the weight-side tensor maps for `wrows` packed weight rows of K: the F16 weight tile
+// (128-byte swizzled), or the raw quantized super-block tile and, for Q6_K, the d plane.
+static bool setup_weight_maps(int wtype, const void* w_packed, int64_t wrows, int64_t K, CUtensorMap& tmW,
+                              CUtensorMap& tmD, const CUtensorMap& tmA) {
     size_t d_off = 0;
     packed_weight_bytes(wtype, wrows, K, &d_off);
-    if (wtype == WT_F16) {
-        return make_tmap_2d_f16(&tmW, w_packed, (uint64_t)wrows, (uint64_t)K, (uint64_t)K, GEMM_BN, GEMM_BK);
+    tmD = tmA;   // unused unless Q6_K
+    const uint8_t* base = static_cast<const uint8_t*>(w_packed);
+    switch (wtype) {
+        case WT_F16:
+            return make_tmap_2d_f16(&tmW, w_packed, (uint64_t)wrows, (uint64_t)K, (uint64_t)K, GEMM_BN, GEMM_BK);
+        case WT_Q4_K: {
+            const uint64_t rb = (uint64_t)(K / 256) * 144;
+            return make_tmap_2d_u16(&tmW, base, (uint64_t)wrows, rb / 2, rb, GEMM_BN, RawCfg<WT_Q4_K>::X_ELEMS);
+        }
+        case WT_Q6_K: {
+            const uint64_t rb = (uint64_t)(K / 256) * 208;
+            return make_tmap_2d_u16(&tmW, base, (uint64_t)wrows, rb / 2, rb, GEMM_BN, RawCfg<WT_Q6_K>::X_ELEMS) &&
+                   make_tmap_2d_u16(&tmD, base + d_off, (uint64_t)(K / 256), (uint64_t)wrows, (uint64_t)wrows * 2, 1,
+                                    GEMM_BN);
+        }
+        case WT_Q8_0: {
+            const uint64_t rb = (uint64_t)((K + 255) / 256) * 272;
+            return make_tmap_2d_u16(&tmW, base, (uint64_t)wrows, rb / 2, rb, GEMM_BN, RawCfg<WT_Q8_0>::X_ELEMS);
+        }
+        default:
+            return false;
     }
-    tmW = tmA;   // unused by the quantized kernels
-    a.w = static_cast<const uint8_t*>(w_packed);
-    if (wtype == WT_Q4_K) {
-        a.w_row_bytes = (K / 256) * 144;
-    } else if (wtype == WT_Q6_K) {
-        a.w_row_bytes = (K / 256) * 208;
-        a.wd = reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(w_packed) + d_off);
-        a.wd_row_elems = K / 256;
-    } else {
-        const int64_t ngrp = (K + 255) / 256;
-        a.w_row_bytes = ngrp * 256;
-        a.wd = reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(w_packed) + d_off);
-        a.wd_row_elems = ngrp * 8;
-    }
-    return true;
 }
 
 template <bool GROUPED>
-cudaError_t launch_gemm_typed(int wtype, int bt, const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmArgs& a,
-                              int grid, cudaStream_t st) {
+cudaError_t launch_gemm_typed(int wtype, int bt, const CUtensorMap& tmA, const CUtensorMap& tmW,
+                              const CUtensorMap& tmD, const GemmArgs& a, int grid, cudaStream_t st) {
     switch (wtype) {
-        case WT_F16: return launch_gemm_bt<WT_F16, GROUPED>(bt, tmA, tmW, a, grid, st);
-        case WT_Q4_K: return launch_gemm_bt<WT_Q4_K, GROUPED>(bt, tmA, tmW, a, grid, st);
-        case WT_Q6_K: return launch_gemm_bt<WT_Q6_K, GROUPED>(bt, tmA, tmW, a, grid, st);
-        case WT_Q8_0: return launch_gemm_bt<WT_Q8_0, GROUPED>(bt, tmA, tmW, a, grid, st);
+        case WT_F16: return launch_gemm_bt<WT_F16, GROUPED>(bt, tmA, tmW, tmD, a, grid, st);
+        case WT_Q4_K: return launch_gemm_bt<WT_Q4_K, GROUPED>(bt, tmA, tmW, tmD, a, grid, st);
+        case WT_Q6_K: return launch_gemm_bt<WT_Q6_K, GROUPED>(bt, tmA, tmW, tmD, a, grid, st);
+        case WT_Q8_0: return launch_gemm_bt<WT_Q8_0, GROUPED>(bt, tmA, tmW, tmD, a, grid, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -336,10 +382,11 @@ int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int6
                       const float* scales, int64_t rows, int bt, const int32_t* off, const int32_t* tile_start,
                       const int32_t* slot, const int32_t* tok, float* dst, int64_t d_nb1, int64_t d_nb2, int* dev_err,
                       cudaStream_t st) {
-    CUtensorMap tmA, tmW;
+    if ((d_nb1 % 16) || (d_nb2 % 16) || (reinterpret_cast<uintptr_t>(dst) & 15u)) return B200_E_UNSUPPORTED;
+    CUtensorMap tmA, tmW, tmD;
     if (!make_tmap_2d_f16(&tmA, a16, (uint64_t)rows, (uint64_t)K, (uint64_t)K, (uint32_t)bt, GEMM_BK)) return B200_E_CUDA;
     GemmArgs a{};
-    if (!setup_weight_args(wtype, w_stack, N * n_expert, K, a, tmW, tmA)) return B200_E_CUDA;
+    if (!setup_weight_maps(wtype, w_stack, N * n_expert, K, tmW, tmD, tmA)) return B200_E_CUDA;
     a.scales = scales;
     a.out = dst;
     a.M = (int)rows;
@@ -364,7 +411,7 @@ int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int6
     const int64_t max_units = max_tiles * a.n_tiles_n;
     const int grid = (int)(max_units < sms ? max_units : sms);
     if (grid <= 0) return B200_OK;
-    return launch_gemm_typed<true>(wtype, bt, tmA, tmW, a, grid, st) == cudaSuccess ? B200_OK : B200_E_CUDA;
+    return launch_gemm_typed<true>(wtype, bt, tmA, tmW, tmD, a, grid, st) == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 
 size_t packed_weight_bytes(int type, int64_t N, int64_t K, size_t* plane_d_off) {
@@ -376,12 +423,9 @@ size_t packed_weight_bytes(int type, int64_t N, int64_t K, size_t* plane_d_off) 
             off = align_up((size_t)N * (K / 256) * 208, 256);
             total = off + (size_t)N * (K / 256) * 2;
             break;
-        case WT_Q8_0: {
-            const int64_t ngrp = (K + 255) / 256;
-            off = align_up((size_t)N * ngrp * 256, 256);
-            total = off + (size_t)N * ngrp * 8 * 2;
+        case WT_Q8_0:
+            total = (size_t)N * ((K + 255) / 256) * 272;
             break;
-        }
         default: return 0;
     }
     if (plane_d_off) *plane_d_off = off;
@@ -404,19 +448,20 @@ int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, cons
                      cudaStream_t st) {
     if (!w_packed || !a16 || !scales || !dst || !dev_err || M <= 0 || N <= 0 || K <= 0) return B200_E_INVALID;
     if (!weight_type_supported(wtype, K) || K % 32 != 0 || N % 16 != 0) return B200_E_UNSUPPORTED;
+    // the epilogue writes 16-byte vectors of dst rows
+    if (ldd % 4 != 0 || (reinterpret_cast<uintptr_t>(dst) & 15u)) return B200_E_UNSUPPORTED;
     if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return B200_E_UNSUPPORTED;
     const int sms = device_sm_count();
-    const GemmPlan p = plan_gemm(M, N, K, sms);
+    const GemmPlan p = plan_gemm(M, N, K, sms, wtype);
     const size_t part_bytes = p.splits > 1 ? (size_t)p.splits * M * N * 4 : 0;
     if (part_bytes && (!workspace || workspace_bytes < part_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
         return B200_E_WORKSPACE;
     float* part = static_cast<float*>(workspace);
-    CUtensorMap tmA, tmW;
-    std::memset(&tmW, 0, sizeof(tmW));
+    CUtensorMap tmA, tmW, tmD;
     if (!make_tmap_2d_f16(&tmA, a16, (uint64_t)M, (uint64_t)K, (uint64_t)K, (uint32_t)p.bt, GEMM_BK))
         return B200_E_CUDA;
     GemmArgs a{};
-    if (!setup_weight_args(wtype, w_packed, N, K, a, tmW, tmA)) return B200_E_CUDA;
+    if (!setup_weight_maps(wtype, w_packed, N, K, tmW, tmD, tmA)) return B200_E_CUDA;
     a.scales = scales;
     a.M = (int)M;
     a.N = (int)N;
@@ -437,7 +482,7 @@ int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, cons
         a.ldo = ldd;
         a.split_stride = 0;
     }
-    const cudaError_t e = launch_gemm_typed<false>(wtype, p.bt, tmA, tmW, a, p.grid, st);
+    const cudaError_t e = launch_gemm_typed<false>(wtype, p.bt, tmA, tmW, tmD, a, p.grid, st);
     if (e != cudaSuccess) return B200_E_CUDA;
     if (p.splits > 1) {
         const int64_t total = M * N;
@@ -457,7 +502,7 @@ int act_pack_impl(const float* src1, int64_t lda, int64_t M, int64_t K, __half* 
 int mul_mat_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const float* src1, int64_t lda, int64_t M,
                  float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t st) {
     if (!w_packed || !src1 || !dst || !dev_err || M <= 0 || N <= 0 || K <= 0) return B200_E_INVALID;
-    const GemmPlan p = plan_gemm(M, N, K, device_sm_count());
+    const GemmPlan p = plan_gemm(M, N, K, device_sm_count(), wtype);
     const MulMatWorkspace wl = mm_workspace_layout(M, N, K, p);
     if (!workspace || workspace_bytes < wl.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
         return B200_E_WORKSPACE;
@@ -470,8 +515,8 @@ int mul_mat_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const fl
                             dev_err, st);
 }
 
-size_t mul_mat_workspace(int64_t M, int64_t N, int64_t K) {
-    const GemmPlan p = plan_gemm(M, N, K, device_sm_count());
+size_t mul_mat_workspace(int wtype, int64_t M, int64_t N, int64_t K) {
+    const GemmPlan p = plan_gemm(M, N, K, device_sm_count(), wtype);
     return mm_workspace_layout(M, N, K, p).total;
 }
 
@@ -497,7 +542,7 @@ int weight_pack_impl(int type, const void* src, int64_t N, int64_t K, void* dst,
         const int64_t total = N * ngrp * 8;
         int blocks = (int)((total + 255) / 256);
         if (blocks > 65535) blocks = 65535;
-        pack_q8_0_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint8_t*>(src), N, nblk, ngrp, dA, dD);
+        pack_q8_0_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint8_t*>(src), N, nblk, ngrp, dA);
     }
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
@@ -550,9 +595,9 @@ int b200_act_pack(const float* src1, int64_t lda, int64_t M, int64_t K, void* a1
     return b200::act_pack_impl(src1, lda, M, K, static_cast<__half*>(a16), scales, static_cast<cudaStream_t>(stream));
 }
 
-size_t b200_gemm_packed_workspace_size(int64_t M, int64_t N, int64_t K) {
+size_t b200_gemm_packed_workspace_size(int wtype, int64_t M, int64_t N, int64_t K) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
-    const b200::GemmPlan p = b200::plan_gemm(M, N, K, b200::device_sm_count());
+    const b200::GemmPlan p = b200::plan_gemm(M, N, K, b200::device_sm_count(), wtype);
     return p.splits > 1 ? (size_t)p.splits * M * N * 4 : 0;
 }
 
@@ -563,9 +608,10 @@ int b200_gemm_packed(int wtype, const void* w_packed, int64_t N, int64_t K, cons
                                   workspace, workspace_bytes, dev_err, static_cast<cudaStream_t>(stream));
 }
 
-int b200_mul_mat_plan(int64_t M, int64_t N, int64_t K, int* token_tile, int* splits, int* grid, int* launches) {
+int b200_mul_mat_plan(int wtype, int64_t M, int64_t N, int64_t K, int* token_tile, int* splits, int* grid,
+                      int* launches) {
     if (M <= 0 || N <= 0 || K <= 0) return B200_E_INVALID;
-    const b200::GemmPlan p = b200::plan_gemm(M, N, K, b200::device_sm_count());
+    const b200::GemmPlan p = b200::plan_gemm(M, N, K, b200::device_sm_count(), wtype);
     if (token_tile) *token_tile = p.bt;
     if (splits) *splits = p.splits;
     if (grid) *grid = p.grid;
@@ -573,9 +619,9 @@ int b200_mul_mat_plan(int64_t M, int64_t N, int64_t K, int* token_tile, int* spl
     return B200_OK;
 }
 
-size_t b200_mul_mat_workspace_size(int64_t M, int64_t N, int64_t K) {
+size_t b200_mul_mat_workspace_size(int wtype, int64_t M, int64_t N, int64_t K) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
-    return b200::mul_mat_workspace(M, N, K);
+    return b200::mul_mat_workspace(wtype, M, N, K);
 }
 
 int b200_mul_mat(int wtype, const void* w_packed, int64_t N, int64_t K, const float* src1, int64_t lda, int64_t M,

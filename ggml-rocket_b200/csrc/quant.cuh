@@ -12,11 +12,13 @@
 //
 // Two layouts are read:
 //   native  the GGUF block rows, as ggml stores them (row n at n * row_size(K));
-//   packed  the device-resident layout the weight cache keeps, with every load 16-byte
-//           aligned: Q4_K is native; Q6_K keeps {ql, qh, scales} (208 B per super-block)
-//           in one plane and d in a second plane of fp16; Q8_0 keeps the int8 codes of 256
-//           weights (256 B) in one plane and the 32-weight d values in a second plane, K
-//           padded to a multiple of 256 with zero blocks.
+//   packed  the device-resident layout the weight cache keeps, laid out for TMA tiles and
+//           conflict-free shared-memory reads; same bytes as native:
+//             Q4_K  native rows (144-byte super-blocks are already 16-byte multiples)
+//             Q6_K  plane A [rows][K/256][208 B] = {ql, qh, scales}; plane D [K/256][rows] fp16
+//                   d, transposed so that one 256-byte TMA box holds a 128-row tile's d values
+//             Q8_0  rows of 272-byte groups of 8 blocks {d[8], qs[256]}, K padded to 256 with
+//                   zero blocks
 #pragma once
 
 #include <cstdint>
@@ -51,99 +53,129 @@ __device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8
 // Q4_K (scale, min) pair of sub-block i (0..7) from the 12 scale bytes held in s0..s2.
 __device__ __forceinline__ void q4k_sm(int i, uint32_t s0, uint32_t s1, uint32_t s2,
                                        uint32_t& sc, uint32_t& m) {
-    const uint32_t w[3] = {s0, s1, s2};
-    auto B = [&](int b) { return byte_of(w[b >> 2], b & 3); };
+    const int sh = 8 * (i & 3);
+    const uint32_t a = (s0 >> sh) & 0xffu, b = (s1 >> sh) & 0xffu, c = (s2 >> sh) & 0xffu;
     if (i < 4) {
-        sc = B(i) & 63u;
-        m = B(i + 4) & 63u;
+        sc = a & 63u;
+        m = b & 63u;
     } else {
-        sc = (B(i + 4) & 0x0fu) | ((B(i - 4) >> 6) << 4);
-        m = (B(i + 4) >> 4) | ((B(i) >> 6) << 4);
+        sc = (c & 0x0fu) | ((a >> 6) << 4);
+        m = (c >> 4) | ((b >> 6) << 4);
     }
 }
 
-// ---- packed-layout decoders: one 64-weight chunk of one row -> 32 half2 words ------------
-// `row` points at the row's first byte in plane A; `drow` at its first fp16 in plane D.
+// ---- packed-layout decoders (fused GEMM): one 32-weight half of a 64-weight chunk of one
+// row, read from the raw tile the TMA placed in shared memory, -> 16 half2 words ----------
+//
+// Integer codes become floats without a conversion instruction: a code c in [0, 255] placed in
+// the low byte of 0x4B000000 is the float 2^23 + c, and one exact subtraction yields c. The
+// arithmetic after that is the scalar formula's, two floats at a time (sm_100 f32x2 ops).
 
-__device__ __forceinline__ void decode_q4k_chunk(const uint8_t* row, int kc, uint32_t (&h)[32]) {
-    const uint8_t* blk = row + (size_t)(kc >> 2) * 144;
-    const int j = kc & 3;
-    const uint4 hdr = ld_nc_v4(blk);
-    const uint4 qa = ld_nc_v4(blk + 16 + 32 * j);
-    const uint4 qb = ld_nc_v4(blk + 32 + 32 * j);
-    const float d = h2f_bits(hdr.x), dmin = h2f_bits(hdr.x >> 16);
-    uint32_t sc0, m0, sc1, m1;
-    q4k_sm(2 * j, hdr.y, hdr.z, hdr.w, sc0, m0);
-    q4k_sm(2 * j + 1, hdr.y, hdr.z, hdr.w, sc1, m1);
-    const float d1 = __fmul_rn(d, (float)sc0), mm1 = __fmul_rn(dmin, (float)m0);
-    const float d2 = __fmul_rn(d, (float)sc1), mm2 = __fmul_rn(dmin, (float)m1);
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+// Bytes 2i and 2i+1 of x as the floats 2^23 + byte.
+__device__ __forceinline__ uint64_t magic_pair(uint32_t x, int i) {
+    const uint32_t lo = __byte_perm(x, 0x4B000000u, 0x7540u + 2u * i);
+    const uint32_t hi = __byte_perm(x, 0x4B000000u, 0x7541u + 2u * i);
+    return f2_pack(__uint_as_float(lo), __uint_as_float(hi));
+}
+__device__ __forceinline__ uint32_t f2_to_half2(uint64_t v) {
+    float lo, hi;
+    f2_unpack(v, lo, hi);
+    return pack_half2(lo, hi);
+}
+
+// Q4_K: raw row = native 144-byte super-blocks. Chunk j of super-block sb, half h: the low (h=0)
+// or high (h=1) nibbles of qs[32j .. 32j+31], sub-block 2j+h: y = (d*sc)*q - dmin*m.
+__device__ __forceinline__ void decode_q4k_half(const uint8_t* blk, int j, int h, uint32_t (&o)[16]) {
+    const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+    const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * j);
+    const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * j);
+    uint32_t sc, m;
+    q4k_sm(2 * j + h, hdr.y, hdr.z, hdr.w, sc, m);
+    const float d1 = __fmul_rn(h2f_bits(hdr.x), (float)sc);
+    const float m1 = __fmul_rn(h2f_bits(hdr.x >> 16), (float)m);
+    const uint64_t D1 = f2_pack(d1, d1), NM1 = f2_pack(-m1, -m1);
+    const uint64_t MAG = f2_pack(-8388608.0f, -8388608.0f);
     const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-    for (int i = 0; i < 16; i++) {   // weights 2i, 2i+1: low nibbles of bytes 2i, 2i+1
-        const uint32_t b0 = byte_of(q[i >> 1], (2 * i) & 3), b1 = byte_of(q[i >> 1], (2 * i + 1) & 3);
-        h[i] = pack_half2(__fsub_rn(__fmul_rn(d1, (float)(b0 & 15u)), mm1),
-                          __fsub_rn(__fmul_rn(d1, (float)(b1 & 15u)), mm1));
-        h[16 + i] = pack_half2(__fsub_rn(__fmul_rn(d2, (float)(b0 >> 4)), mm2),
-                               __fsub_rn(__fmul_rn(d2, (float)(b1 >> 4)), mm2));
-    }
-}
-
-__device__ __forceinline__ void decode_q6k_chunk(const uint8_t* row, const uint16_t* drow, int kc,
-                                                 uint32_t (&h)[32]) {
-    const int sb = kc >> 2, j = kc & 3, hh = j >> 1, s = j & 1;
-    const uint8_t* blk = row + (size_t)sb * 208;
-    const float d = __half2float(__ushort_as_half(__ldg(drow + sb)));
-    const uint4 l0 = ld_nc_v4(blk + 64 * hh), l1 = ld_nc_v4(blk + 64 * hh + 16);
-    const uint4 l2 = ld_nc_v4(blk + 64 * hh + 32), l3 = ld_nc_v4(blk + 64 * hh + 48);
-    const uint4 g0 = ld_nc_v4(blk + 128 + 32 * hh), g1 = ld_nc_v4(blk + 128 + 32 * hh + 16);
-    const uint4 sv = ld_nc_v4(blk + 192);
-    const uint32_t ql[16] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w,
-                             l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
-    const uint32_t qh[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-    const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
-    const int sbase = 8 * hh + 4 * s;
-    float ds[4];
+    for (int w = 0; w < 8; w++) {
+        const uint32_t x = (h ? (q[w] >> 4) : q[w]) & 0x0F0F0F0Fu;
 #pragma unroll
-    for (int g = 0; g < 4; g++) {
-        const int si = sbase + g;
-        const int8_t scv = static_cast<int8_t>(byte_of(sw[si >> 2], si & 3));
-        ds[g] = __fmul_rn(d, (float)scv);
-    }
-    const int ns = 4 * s;
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-        float v[2];
-#pragma unroll
-        for (int e = 0; e < 2; e++) {
-            const int w = 2 * i + e;             // 0..63 within the chunk
-            const int second = w >> 5;           // 0: ql[l], 1: ql[l+32]
-            const int l = w & 31;
-            const uint32_t lb = byte_of(ql[(l + 32 * second) >> 2], (l + 32 * second) & 3);
-            const uint32_t hb = byte_of(qh[l >> 2], l & 3);
-            const int q = (int)(((lb >> ns) & 15u) | (((hb >> (ns + 2 * second)) & 3u) << 4)) - 32;
-            v[e] = __fmul_rn(ds[2 * second + (l >> 4)], (float)q);
+        for (int i = 0; i < 2; i++) {
+            const uint64_t qf = f2_add(magic_pair(x, i), MAG);          // exact codes
+            o[2 * w + i] = f2_to_half2(f2_fma(D1, qf, NM1));            // d1*q exact: one rounding
         }
-        h[i] = pack_half2(v[0], v[1]);
     }
 }
 
-__device__ __forceinline__ void decode_q8_0_chunk(const uint8_t* row, const uint16_t* drow, int kc,
-                                                  uint32_t (&h)[32]) {
-    const uint8_t* qs = row + (size_t)kc * 64;
-    const uint32_t dd = __ldg(reinterpret_cast<const uint32_t*>(drow) + kc);
-    const float d0 = h2f_bits(dd), d1 = h2f_bits(dd >> 16);
-    uint32_t q[16];
+// Q6_K: raw row = 208-byte {ql, qh, scales} super-blocks, d from the transposed d plane.
+// Chunk j (hh = j>>1 selects the 128-weight half, s = j&1 the nibble), half h selects
+// ql[l] (h=0) or ql[l+32] (h=1); y = (d*sc) * (q - 32).
+__device__ __forceinline__ void decode_q6k_half(const uint8_t* blk, float d, int j, int h, uint32_t (&o)[16]) {
+    const int hh = j >> 1, s = j & 1;
+    const uint4 la = *reinterpret_cast<const uint4*>(blk + 64 * hh + 32 * h);
+    const uint4 lb = *reinterpret_cast<const uint4*>(blk + 64 * hh + 32 * h + 16);
+    const uint4 ga = *reinterpret_cast<const uint4*>(blk + 128 + 32 * hh);
+    const uint4 gb = *reinterpret_cast<const uint4*>(blk + 128 + 32 * hh + 16);
+    const int si = 8 * hh + 4 * s + 2 * h;
+    const float ds0 = __fmul_rn(d, (float)(int8_t)blk[192 + si]);
+    const float ds1 = __fmul_rn(d, (float)(int8_t)blk[192 + si + 1]);
+    const uint64_t MAG = f2_pack(-8388640.0f, -8388640.0f);             // -(2^23 + 32)
+    const uint32_t ql[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+    const uint32_t qh[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+    const int hs = 4 * s + 2 * h;
 #pragma unroll
-    for (int c = 0; c < 4; c++) {
-        const uint4 v = ld_nc_v4(qs + 16 * c);
-        q[4 * c] = v.x; q[4 * c + 1] = v.y; q[4 * c + 2] = v.z; q[4 * c + 3] = v.w;
+    for (int w = 0; w < 8; w++) {
+        const uint32_t x = ((ql[w] >> (4 * s)) & 0x0F0F0F0Fu) | (((qh[w] >> hs) & 0x03030303u) << 4);
+        const uint64_t DS = w < 4 ? f2_pack(ds0, ds0) : f2_pack(ds1, ds1);
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const uint64_t qf = f2_add(magic_pair(x, i), MAG);          // exact q - 32
+            o[2 * w + i] = f2_to_half2(f2_mul(DS, qf));
+        }
     }
+}
+
+// Q8_0: raw row = 272-byte groups of 8 blocks {d[8] fp16, qs[256] int8}. Chunk c4 (0..3) of
+// the group, half h: block 2*c4 + h; y = q * d.
+__device__ __forceinline__ void decode_q8_0_half(const uint8_t* grp, int c4, int h, uint32_t (&o)[16]) {
+    const int blk = 2 * c4 + h;
+    const float d = __half2float(*reinterpret_cast<const __half*>(grp + 2 * blk));
+    const uint4 qa = *reinterpret_cast<const uint4*>(grp + 16 + 32 * blk);
+    const uint4 qb = *reinterpret_cast<const uint4*>(grp + 32 + 32 * blk);
+    const uint64_t D = f2_pack(d, d);
+    const uint64_t MAG = f2_pack(-8388736.0f, -8388736.0f);             // -(2^23 + 128)
+    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-    for (int i = 0; i < 32; i++) {
-        const float d = i < 16 ? d0 : d1;
-        const int8_t a = static_cast<int8_t>(byte_of(q[i >> 1], (2 * i) & 3));
-        const int8_t b = static_cast<int8_t>(byte_of(q[i >> 1], (2 * i + 1) & 3));
-        h[i] = pack_half2(__fmul_rn((float)a, d), __fmul_rn((float)b, d));
+    for (int w = 0; w < 8; w++) {
+        const uint32_t x = q[w] ^ 0x80808080u;                             // int8 -> q + 128
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const uint64_t qf = f2_add(magic_pair(x, i), MAG);
+            o[2 * w + i] = f2_to_half2(f2_mul(qf, D));
+        }
     }
 }
 

@@ -40,12 +40,12 @@ _SIGS = {
     "b200_weight_packed_size": (_sz, [_int, _i64, _i64]),
     "b200_weight_pack": (_int, [_int, _vp, _i64, _i64, _vp, _vp]),
     "b200_dequantize": (_int, [_int, _vp, _i64, _i64, _int, _vp, _vp]),
-    "b200_mul_mat_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "b200_mul_mat_workspace_size": (_sz, [_int, _i64, _i64, _i64]),
     "b200_mul_mat": (_int, [_int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _sz, _vp, _vp]),
     "b200_act_pack": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
-    "b200_gemm_packed_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "b200_gemm_packed_workspace_size": (_sz, [_int, _i64, _i64, _i64]),
     "b200_gemm_packed": (_int, [_int, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _sz, _vp, _vp]),
-    "b200_mul_mat_plan": (_int, [_i64, _i64, _i64, _pint, _pint, _pint, _pint]),
+    "b200_mul_mat_plan": (_int, [_int, _i64, _i64, _i64, _pint, _pint, _pint, _pint]),
 }
 
 
@@ -99,8 +99,8 @@ def dequantize(t, src, N, K, dst, f16_out=False, stream=None):
     check(lib().b200_dequantize(t, _ptr(src), N, K, 1 if f16_out else 0, _ptr(dst), _stream(stream)), "dequantize")
 
 
-def mul_mat_workspace_size(M, N, K):
-    return lib().b200_mul_mat_workspace_size(M, N, K)
+def mul_mat_workspace_size(M, N, K, wtype=F16):
+    return lib().b200_mul_mat_workspace_size(wtype, M, N, K)
 
 
 def mul_mat(wtype, w_packed, N, K, a, M, out, workspace, dev_err, lda=None, ldd=None, stream=None):
@@ -116,8 +116,8 @@ def act_pack(a, M, K, a16, scales, lda=None, stream=None):
     check(lib().b200_act_pack(_ptr(a), lda, M, K, _ptr(a16), _ptr(scales), _stream(stream)), "act_pack")
 
 
-def gemm_packed_workspace_size(M, N, K):
-    return lib().b200_gemm_packed_workspace_size(M, N, K)
+def gemm_packed_workspace_size(M, N, K, wtype=F16):
+    return lib().b200_gemm_packed_workspace_size(wtype, M, N, K)
 
 
 def gemm_packed(wtype, w_packed, N, K, a16, scales, M, out, workspace, dev_err, ldd=None, stream=None):
@@ -127,9 +127,9 @@ def gemm_packed(wtype, w_packed, N, K, a16, scales, M, out, workspace, dev_err, 
                                  _ptr(workspace), wsb, _ptr(dev_err), _stream(stream)), "gemm_packed")
 
 
-def mul_mat_plan(M, N, K):
+def mul_mat_plan(M, N, K, wtype=F16):
     vals = [ctypes.c_int(0) for _ in range(4)]
-    check(lib().b200_mul_mat_plan(M, N, K, *[ctypes.byref(v) for v in vals]), "mul_mat_plan")
+    check(lib().b200_mul_mat_plan(wtype, M, N, K, *[ctypes.byref(v) for v in vals]), "mul_mat_plan")
     return dict(token_tile=vals[0].value, splits=vals[1].value, grid=vals[2].value, launches=vals[3].value)
 
 

@@ -62,9 +62,9 @@ int    b200_dequantize(int type, const void * src_native, int64_t N, int64_t K, 
  * reference's "sandwich", :1451-1475); the products accumulate in fp32 in tensor memory and
  * the row scale is applied to the fp32 result. Requires K % 32 == 0, N % 16 == 0, and
  * K % 256 == 0 for Q4_K / Q6_K. The workspace (device, 256-byte aligned) must hold
- * b200_mul_mat_workspace_size(M, N, K) bytes.
+ * b200_mul_mat_workspace_size(wtype, M, N, K) bytes.
  */
-size_t b200_mul_mat_workspace_size(int64_t M, int64_t N, int64_t K);
+size_t b200_mul_mat_workspace_size(int wtype, int64_t M, int64_t N, int64_t K);
 int    b200_mul_mat(int wtype, const void * w_packed, int64_t N, int64_t K,
                     const float * src1, int64_t lda, int64_t M,
                     float * dst, int64_t ldd,
@@ -77,14 +77,15 @@ int    b200_mul_mat(int wtype, const void * w_packed, int64_t N, int64_t K,
  *   b200_gemm_packed  dst = scales[m] * (a16 . W^T); the workspace is only needed when the
  *                     plan splits K (b200_gemm_packed_workspace_size > 0). */
 int    b200_act_pack(const float * src1, int64_t lda, int64_t M, int64_t K, void * a16, float * scales, void * stream);
-size_t b200_gemm_packed_workspace_size(int64_t M, int64_t N, int64_t K);
+size_t b200_gemm_packed_workspace_size(int wtype, int64_t M, int64_t N, int64_t K);
 int    b200_gemm_packed(int wtype, const void * w_packed, int64_t N, int64_t K, const void * a16, const float * scales,
                         int64_t M, float * dst, int64_t ldd, void * workspace, size_t workspace_bytes, int * dev_err,
                         void * stream);
 
 /* The launch plan b200_mul_mat uses on the current device: the token tile (tcgen05 N), the
  * split-K factor, the persistent grid and the number of kernel launches one call makes. */
-int    b200_mul_mat_plan(int64_t M, int64_t N, int64_t K, int * token_tile, int * splits, int * grid, int * launches);
+int    b200_mul_mat_plan(int wtype, int64_t M, int64_t N, int64_t K, int * token_tile, int * splits, int * grid,
+                         int * launches);
 
 /* ---- FLASH_ATTN_EXT ------------------------------------------------------------------------
  * Replaces ggml_backend_rocket_flash_attn (ggml-rocket.cpp:5444-5691): its gathers (:5487-5577),

@@ -43,7 +43,7 @@ def run_mul_mat(torch, wtype, w_raw, N, K, a):
     g.weight_pack(wtype, w_dev, N, K, packed)
     a_dev = _dev(torch, a.astype(np.float32))
     out = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
-    ws = torch.empty(g.mul_mat_workspace_size(M, N, K), dtype=torch.uint8, device="cuda")
+    ws = torch.empty(g.mul_mat_workspace_size(M, N, K, wtype), dtype=torch.uint8, device="cuda")
     err = _err_word(torch)
     g.mul_mat(wtype, packed, N, K, a_dev, M, out, ws, err)
     torch.cuda.synchronize()
@@ -155,7 +155,8 @@ def test_mul_mat_quant(cuda, K, N, M, wtype):
 @pytest.mark.parametrize("K,N,M,wtype", [(3840, 256, 128, 12), (512, 256, 128, 14), (3840, 256, 96, 8)])
 def test_mul_mat_quant_equals_dequant_then_f16(cuda, K, N, M, wtype):
     """The fused dequant GEMM decodes each weight to exactly the fp16 value the standalone
-    dequant produces, so it must equal the F16 GEMM over that fp16 weight bit for bit."""
+    dequant produces, so it must equal the F16 GEMM over that fp16 weight bit for bit (when
+    both take the same tiling; otherwise up to the order of the fp32 sums)."""
     import torch
     g = _lib()
     rng = np.random.default_rng(99 + wtype)
@@ -167,4 +168,7 @@ def test_mul_mat_quant_equals_dequant_then_f16(cuda, K, N, M, wtype):
     torch.cuda.synchronize()
     w16_bytes = w16.cpu().numpy().view(np.uint8).reshape(N, K * 2)
     got_f = run_mul_mat(torch, 1, w16_bytes, N, K, a)
-    assert np.array_equal(got_q.view(np.uint32), got_f.view(np.uint32))
+    if g.mul_mat_plan(M, N, K, wtype) == g.mul_mat_plan(M, N, K, g.F16):
+        assert np.array_equal(got_q.view(np.uint32), got_f.view(np.uint32))
+    else:   # different tilings only reorder the fp32 sums
+        assert rel_err(got_q, got_f) <= 1e-5
