@@ -18,7 +18,8 @@ BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144
 
 B200_OK = 0
 STATUS = {0: "ok", -1: "invalid", -2: "unsupported", -3: "cuda", -4: "device", -5: "workspace",
-          -6: "bad_ids", -7: "no_device"}
+          -6: "bad_ids", -7: "no_device", -8: "too_large"}
+B200_E_TOO_LARGE = -8
 
 
 class B200Error(RuntimeError):
@@ -190,6 +191,11 @@ _BACKEND_SIGS = {
                                           _c.POINTER(_sz)]),
 }
 _SIGS.update(_BACKEND_SIGS)
+_SIGS.update({
+    "b200_mul_mat_noalloc_max_workspace": (_sz, []),
+    "b200_mul_mat_noalloc": (_int, [_int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp]),
+    "b200_mul_mat_noalloc_error": (_int, [_vp, _c.POINTER(_int)]),
+})
 
 
 def _elem_size(t):

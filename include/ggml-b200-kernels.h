@@ -32,6 +32,7 @@ typedef enum {
     B200_E_WORKSPACE = -5,     /* the workspace is missing, too small or not 256-byte aligned */
     B200_E_BAD_IDS = -6,       /* a MUL_MAT_ID expert id outside [0, n_expert) */
     B200_E_NO_DEVICE = -7,     /* no CUDA device */
+    B200_E_TOO_LARGE = -8,     /* the op needs more scratch than b200_mul_mat_noalloc's fixed array holds */
 } b200_status;
 
 /* ---- weights ------------------------------------------------------------------------------
@@ -86,6 +87,23 @@ int    b200_gemm_packed(int wtype, const void * w_packed, int64_t N, int64_t K, 
  * split-K factor, the persistent grid and the number of kernel launches one call makes. */
 int    b200_mul_mat_plan(int wtype, int64_t M, int64_t N, int64_t K, int * token_tile, int * splits, int * grid,
                          int * launches);
+
+/* ---- MUL_MAT without allocation ------------------------------------------------------------
+ * No counterpart in the reference. For callers that cannot call cudaMalloc (a plugin inside a
+ * process whose allocator owns the device, code that must not change the device memory map, a
+ * fixed memory budget): the same MUL_MAT as b200_mul_mat, with its workspace taken from a 32 MiB
+ * file-scope device array that every GPU loading this library holds until exit. The caller
+ * passes only inputs and outputs. An op whose workspace (b200_mul_mat_workspace_size) exceeds
+ * b200_mul_mat_noalloc_max_workspace() returns B200_E_TOO_LARGE. The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) and should come before any stream
+ * capture. dev_err may be NULL: the device error word then lives in the array and
+ * b200_mul_mat_noalloc_error() synchronises the stream, returns it and clears it. Calls share the
+ * array, so calls that overlap on the GPU race; the caller must order them. */
+size_t b200_mul_mat_noalloc_max_workspace(void);
+int    b200_mul_mat_noalloc(int wtype, const void * w_packed, int64_t N, int64_t K,
+                            const float * src1, int64_t lda, int64_t M, float * dst, int64_t ldd,
+                            int * dev_err, void * stream);
+int    b200_mul_mat_noalloc_error(void * stream, int * host_err);
 
 /* ---- FLASH_ATTN_EXT ------------------------------------------------------------------------
  * Replaces ggml_backend_rocket_flash_attn (ggml-rocket.cpp:5444-5691): its gathers (:5487-5577),
