@@ -1,0 +1,218 @@
+"""Host-only claim-rule tests (no GPU), mirroring test-rocket-placement.cpp:415-557.
+
+Differences from the reference are B200 facts, each stated at its case: the accumulator is
+fp32 in tensor memory, so F32/BF16 accumulator declarations are met; the quantized floor
+defaults to the dense one (the fused device dequant has no per-call host cost); attention needs
+head dims of 64 or 128. Knob states are read once per process (as the reference's statics are),
+so the knob cases run in child processes.
+"""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+import ggml_b200 as g
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def mm(K, N, M, wt, op_params=None, src0_op=g.OP_NONE, readable=True):
+    w = g.make_tensor(wt, [K, N], name="blk.0.attn_q.weight", op=src0_op, readable=readable)
+    x = g.make_tensor(g.F32, [K, M])
+    d = g.make_tensor(g.F32, [N, M], op=g.OP_MUL_MAT, srcs=[w, x], op_params=op_params)
+    return d, (w, x)
+
+
+def supported(*a, **k):
+    d, keep = mm(*a, **k)
+    return g.supports_op(d)
+
+
+K, N, M, MQ = 256, 128, 256, 512
+
+
+def test_mul_mat_weight_types():
+    assert supported(K, N, M, g.F16)
+    assert supported(K, N, M, g.F32)
+    assert supported(K, N, M, g.BF16)
+    assert supported(K, N, MQ, g.Q8_0)
+    assert supported(K, N, MQ, g.Q4_K)
+    assert supported(K, N, MQ, g.Q6_K)
+    # B200: the quant floor defaults to the dense one (32), so M=256 is claimed too
+    assert supported(K, N, M, g.Q4_K)
+    assert not supported(K, N, MQ, 2)          # Q4_0: no device decoder -> CPU
+
+
+def test_mul_mat_shape_gates():
+    assert not supported(80, N, M, g.F16)      # K % 32 != 0
+    assert not supported(K, 70, M, g.F16)      # N % 16 != 0
+    assert supported(K, 112, M, g.F16)         # N % 16 == 0
+    assert not supported(32, N, M, g.F16)      # K < 64
+    assert not supported(K, 48, M, g.F16)      # N < 64
+    assert not supported(K, N, 1, g.F16)       # decode GEMV stays on the CPU
+    assert not supported(K, N, 16, g.F16)      # below the default floor of 32
+    assert not supported(384, N, MQ, g.Q4_K)   # K % 256 != 0 for a K-quant
+
+
+def test_mul_mat_source_gates():
+    assert not supported(K, N, M, g.F16, src0_op=g.OP_OTHER)   # computed (non-leaf) weight
+    assert not supported(K, N, M, g.F16, readable=False)       # repacked bytes without a source
+    d, keep = mm(K, N, M, g.F16)
+    assert g.offload_op(d)
+    a = g.make_tensor(g.F32, [K, M])
+    add = g.make_tensor(g.F32, [K, M], op=g.OP_OTHER, srcs=[a, a])
+    assert not g.offload_op(add)
+
+
+def test_mul_mat_precision_declarations():
+    # accumulator declarations: fp32 accumulation meets all of them (the reference declines F32/BF16)
+    assert supported(K, N, M, g.F16, op_params=[10])
+    assert supported(K, N, M, g.F16, op_params=[15])
+    assert supported(K, N, M, g.F16, op_params=[20])
+    # activation declarations: the activation is rounded to fp16
+    assert not supported(K, N, M, g.F16, op_params=[0, 0, 0, 10])
+    assert not supported(K, N, M, g.F16, op_params=[0, 0, 0, 15])
+    assert supported(K, N, M, g.F16, op_params=[0, 0, 0, 20])
+    assert supported(K, N, M, g.F16, op_params=[0, 0, 0, 30])
+    # a Walsh-Hadamard src0 stays on the CPU's exact transform
+    assert supported(128, 128, M, g.F32)
+    assert not supported(128, 128, M, g.F32, op_params=[0, g.HINT_SRC0_IS_HADAMARD])
+
+
+def fa(D, T, H, KV, HK, kv_type=g.F16, max_bias=0.0, masked=True, sinks=False, acc=0, DV=None):
+    DV = D if DV is None else DV
+    q = g.make_tensor(g.F32, [D, T, H])
+    k = g.make_tensor(kv_type, [D, KV, HK])
+    v = g.make_tensor(kv_type, [DV, KV, HK])
+    m = g.make_tensor(g.F16, [KV, T + 3]) if masked else None
+    s = g.make_tensor(g.F32, [H]) if sinks else None
+    d = g.make_tensor(g.F32, [DV, H, T], op=g.OP_FLASH_ATTN_EXT, srcs=[q, k, v, m, s],
+                      op_params=[0.125, float(max_bias), 0.0, acc])
+    return g.supports_op(d)
+
+
+def test_flash_attn_gates():
+    assert fa(64, 256, 8, 1024, 2)
+    assert fa(64, 256, 8, 1024, 2, acc=10)     # F32 accumulator declared: met
+    assert fa(128, 512, 32, 4096, 8)           # the BASELINE shape
+    assert not fa(64, 1, 8, 1024, 2)           # decode
+    assert not fa(64, 256, 8, 512, 2)          # short context
+    assert not fa(48, 256, 8, 1024, 2)         # head_dim % 32 != 0
+    assert not fa(96, 256, 8, 1024, 2)         # B200: head dims 64 / 128 only
+    assert not fa(64, 256, 8, 1024, 2, kv_type=g.F32)
+    assert not fa(64, 256, 8, 1024, 2, max_bias=8.0)
+    assert not fa(64, 256, 8, 1024, 2, masked=False)   # unmasked needs B200_FLASH_ATTN_UNMASKED=1
+    assert not fa(64, 256, 8, 1024, 2, sinks=True)     # attention sinks: a different softmax
+    assert not fa(64, 256, 6, 1024, 4)                 # GQA does not divide
+
+
+def moe(n_tokens, n_used, n_expert, K=2048, N=768, wt=g.Q4_K, name="blk.0.ffn_up_exps.weight"):
+    a = g.make_tensor(wt, [K, N, n_expert], name=name)
+    b = g.make_tensor(g.F32, [K, 1, n_tokens])
+    ids = g.make_tensor(g.I32, [n_used, n_tokens])
+    d = g.make_tensor(g.F32, [N, n_used, n_tokens], op=g.OP_MUL_MAT_ID, srcs=[a, b, ids])
+    return g.supports_op(d)
+
+
+def test_moe_auto_defaults():
+    assert moe(2048, 8, 128)                   # M_e = 128
+    assert moe(512, 4, 32, K=2880, N=2880, wt=g.Q8_0)   # gpt-oss-like shape (K % 32)
+    assert not moe(16, 8, 128)                 # below the token floor
+    assert not moe(64, 1, 128)                 # M_e = 0 < bucket floor
+    assert not moe(2048, 8, 128, K=2000)       # K % 256 != 0 for Q4_K
+
+
+_CHILD = r"""
+import json, sys
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/ggml-rocket_b200"); sys.path.insert(0, sys.argv[1] + "/tests")
+import test_placement as t
+print(json.dumps({"q4k_m256": t.supported(256, 128, 256, 12), "q4k_m512": t.supported(256, 128, 512, 12),
+                  "f16_m16": t.supported(256, 128, 16, 1), "f16_m3": t.supported(256, 128, 3, 1),
+                  "moe": t.moe(2048, 8, 128), "fa_unmasked": t.fa(64, 256, 8, 1024, 2, masked=False),
+                  "fa": t.fa(64, 256, 8, 1024, 2)}))
+"""
+
+
+def child(env):
+    e = dict(os.environ)
+    for k in list(e):
+        if k.startswith("B200_"):
+            del e[k]
+    e.update(env)
+    out = subprocess.run([sys.executable, "-c", _CHILD, ROOT], env=e, capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    return json.loads(out.stdout.strip().splitlines()[-1])
+
+
+def test_knobs_in_children():
+    r = child({"B200_MIN_M_QUANT": "512"})
+    assert not r["q4k_m256"] and r["q4k_m512"]
+    r = child({"B200_MIN_M": "16"})
+    assert r["f16_m16"]
+    r = child({"B200_MIN_M": "1"})                 # floor of 4
+    assert not r["f16_m3"]
+    r = child({"B200_MIN_M": ""})                  # set-but-empty reads as unset (32)
+    assert not r["f16_m16"]
+    r = child({"B200_MOE": "0"})
+    assert not r["moe"]
+    r = child({"B200_MOE": "1"})
+    assert r["moe"]
+    r = child({"B200_MOE_MIN_WORK": "1000"})       # 128 * 2048 * 768 = 201 MMAC < 1000
+    assert not r["moe"]
+    r = child({"B200_FLASH_ATTN_UNMASKED": "1"})
+    assert r["fa_unmasked"]
+    r = child({"B200_FLASH_ATTN": "0"})
+    assert not r["fa"]
+    r = child({"B200_FLASH_ATTN_MIN_KV": "2048"})
+    assert not r["fa"]
+
+
+def test_moe_ledger_budget_in_child():
+    code = r"""
+import sys
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/ggml-rocket_b200"); sys.path.insert(0, sys.argv[1] + "/tests")
+import test_placement as t
+# four 113 MB Q4_K stacks against a 300 MB budget: two fit; each stack is decided once
+r = [t.moe(2048, 8, 128, name=f"blk.{i}.ffn_up_exps.weight") for i in range(4)]
+again = t.moe(2048, 8, 128, name="blk.0.ffn_up_exps.weight")
+print(sum(r), r[0], again)
+"""
+    e = dict(os.environ)
+    e["B200_WEIGHT_BUDGET_MB"] = "300"
+    out = subprocess.run([sys.executable, "-c", code, ROOT], env=e, capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    n, first, again = out.stdout.split()
+    assert n == "2" and first == "True" and again == "True"
+
+
+def test_weight_key_identity():
+    import numpy as np
+    a = np.arange(4096, dtype=np.uint8)
+    b = (a + 1).astype(np.uint8)               # new bytes throughout (the fingerprint samples 16 x 64 B)
+    w1 = g.make_tensor(g.F16, [64, 32], a, name="blk.3.ffn_down.weight")
+    w2 = g.make_tensor(g.F16, [64, 32], b, name="blk.3.ffn_down.weight")
+    w3 = g.make_tensor(g.F16, [64, 32], a, name="B200#blk.3.ffn_down.weight#1")
+    k1, k2, k3 = g.weight_key(w1), g.weight_key(w2), g.weight_key(w3)
+    assert k1 != k2                            # same name, new bytes -> a different key
+    assert k1 == k3                            # the scheduler's copy name maps to the weight
+    assert g.weight_key(g.make_tensor(g.F16, [64, 32], a, name="leaf_12")) == ""
+    assert g.weight_key(g.make_tensor(g.F16, [64, 32], a, name="")) == ""
+
+
+def test_breaker_semantics():
+    """ggml-rocket.cpp:263-307 / test-rocket-internals.cpp:535-561: three consecutive device
+    failures open the route for 64 calls; a failed probe doubles the interval (cap 4096); a
+    structural decline (unsupported) does not count; a success closes it."""
+    DEV, UNS = -4, -2
+    r = g.breaker_replay([DEV, DEV, DEV] + [0] * 64 + [DEV] + [0] * 130 + [0])
+    assert r[:3] == [1, 1, 1]
+    assert r[3:67] == [0] * 64                 # open for 64 calls
+    assert r[67] == 1                          # the probe (fails)
+    assert r[68:68 + 128] == [0] * 128         # reopened for twice as long
+    assert r[196] == 1
+    r = g.breaker_replay([UNS] * 10 + [0])
+    assert all(x == 1 for x in r)              # declines never open it
+    r = g.breaker_replay([DEV, DEV, 0, DEV, DEV, 0])
+    assert all(x == 1 for x in r)              # a success resets the count
