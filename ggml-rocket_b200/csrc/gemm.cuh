@@ -11,7 +11,7 @@
 //   warp 0        TMA producer of the activation tile [BT x 64]
 //   warp 1        TMEM allocator and the single-thread tcgen05.mma issuer
 //   warps 2..5    epilogue: TMEM -> registers -> a 32x32 shared-memory transpose -> scaled
-//                 16-byte stores of whole 128-byte output lines (or split-K partials)
+//                 16-byte stores of whole 128-byte output lines (or of a stream-K partial)
 //   warp 6        TMA producer of the F16 weight tile, or (quantized weights) of the raw
 //                 quantized super-block tile: 128 rows x 256 weights into a 2-3 deep ring,
 //                 with the TMA's L2 prefetch running 4 super-blocks further ahead
@@ -24,6 +24,15 @@
 // the two operands have separate producers.
 // Two TMEM accumulators alternate, so the epilogue of one unit overlaps the next unit's
 // main loop. Every wait is bounded (ptx.cuh).
+//
+// Scheduling (plain MUL_MAT): stream-K. The K range of every 128 x BT output tile is cut into
+// granules (one 64-wide K block for F16, one 256-weight super-block for quantized weights);
+// the grid (at most one CTA per SM, all resident: cooperative launch) takes equal contiguous
+// runs of the tile-after-tile granule sequence, so every SM gets the same number of K steps
+// whatever the tile count -- no partial last wave. A tile split between CTAs is finished by
+// the CTA holding its last granule, which adds the other CTAs' f32 partials in CTA order:
+// deterministic, with no atomics and no second kernel. The finisher gathers those partials
+// into its idle second TMEM accumulator while its own K range is still on the tensor core.
 #pragma once
 
 #include <cstdint>
@@ -40,12 +49,23 @@ constexpr int GEMM_BK = 64;    // K per pipeline stage (one 128-byte swizzle row
 
 struct GemmArgs {
     const float* scales;       // [M] per-token activation scale
-    float* out;                // dst (splits == 1) or split-K partials
+    float* out;                // dst
     int64_t ldo;               // row stride of out, floats
-    int64_t split_stride;      // floats between split-K partial planes
     int M, N, K;
-    int n_tiles_n, n_tiles_t, splits, kb_per_split, nkb, num_units;
+    int n_tiles_n, n_tiles_t, nkb;
     int* err;                  // device error word
+    // Stream-K schedule (plain MUL_MAT): the K-granules of all tiles, tile after tile, are
+    // split into gridDim.x contiguous ranges of equal length. A tile whose granules span
+    // several CTAs is finished by the CTA holding its last granule (the "finisher"); every
+    // other CTA holding part of it writes an unscaled f32 partial tile to its slot of
+    // `partials` and publishes `epoch` in its flags. The finisher adds the partials in CTA
+    // order, so the result does not depend on timing.
+    float* partials;           // [gridDim.x][BT][128] f32
+    uint32_t* flags;           // [gridDim.x][4] (one per epilogue warp)
+    uint32_t epoch;            // unique per launch
+    int gran;                  // K-blocks per granule (4 = one super-block for quantized weights)
+    int tile_g;                // granules per tile
+    int64_t total_g;           // n_tiles_n * n_tiles_t * tile_g
     // grouped (MUL_MAT_ID) mode: the token rows are sorted by expert; expert e owns rows
     // [g_off[e], g_off[e+1]) of A16 and weight rows [e*N, (e+1)*N) of the packed stack.
     const int32_t* g_off;          // [n_expert + 1]
@@ -56,8 +76,12 @@ struct GemmArgs {
     int64_t d_nb1, d_nb2;          // dst strides over (slot, token), bytes
 };
 
+// One work item of a CTA: a tile (or, in stream-K, the piece of a tile's K range this CTA owns).
 struct UnitCoords {
-    int t0, t_end, n0, wrow0, ks, kb0, kb1;
+    int t0, t_end, n0, wrow0, kb0, kb1;
+    bool finishes;             // this piece completes the tile: scale and store dst
+    int c_first;               // first CTA holding a piece of this tile (partials c_first..blockIdx.x-1)
+    int64_t next;              // cursor of the CTA's next item
 };
 
 // Raw quantized tile of one 256-weight super-block x 128 rows, as the TMA writes it.
@@ -168,13 +192,24 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     const uint32_t tmem_base = *tmem_slot;
 
     const int ntt = args.n_tiles_t, ntn = args.n_tiles_n;
-    int num_units = args.num_units;
-    if constexpr (GROUPED) num_units = __ldg(args.g_tile_start + args.n_expert) * ntn;
-    auto unit_coords = [&](int u) {
+    // Work cursor: the grouped mode walks units blockIdx.x, +gridDim.x, ...; stream-K walks this
+    // CTA's granule range [g_beg, g_end) from its end backwards, so the pieces other CTAs finish
+    // (at the end of the range) come first and the piece this CTA finishes, whose partials come
+    // from lower-numbered CTAs, comes last.
+    int64_t num_units = 0, g_beg = 0, g_end = 0;
+    if constexpr (GROUPED) {
+        num_units = (int64_t)__ldg(args.g_tile_start + args.n_expert) * ntn;
+    } else {
+        g_beg = (int64_t)blockIdx.x * args.total_g / gridDim.x;
+        g_end = (int64_t)(blockIdx.x + 1) * args.total_g / gridDim.x;
+    }
+    const int64_t cursor0 = GROUPED ? (int64_t)blockIdx.x : g_end;
+    auto cursor_ok = [&](int64_t c) { return GROUPED ? c < num_units : c > g_beg; };
+    auto unit_coords = [&](int64_t cur) {
         UnitCoords c;
         if constexpr (GROUPED) {
-            const int tg = u / ntn;
-            const int nt = u % ntn;
+            const int tg = (int)(cur / ntn);
+            const int nt = (int)(cur % ntn);
             int lo = 0, hi = args.n_expert;            // last e with tile_start[e] <= tg
             while (hi - lo > 1) {
                 const int mid = (lo + hi) >> 1;
@@ -186,20 +221,27 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             c.t_end = __ldg(args.g_off + e + 1);
             c.n0 = nt * GEMM_BN;
             c.wrow0 = e * args.N + c.n0;
-            c.ks = 0;
             c.kb0 = 0;
             c.kb1 = args.nkb;
+            c.finishes = true;
+            c.c_first = blockIdx.x;
+            c.next = cur + gridDim.x;
         } else {
-            const int tt = u % ntt;
-            const int rest = u / ntt;
-            const int nt = rest % ntn;
-            c.ks = rest / ntn;
+            const int64_t tile = (cur - 1) / args.tile_g;
+            const int64_t tstart = tile * args.tile_g;
+            const int64_t s0 = tstart > g_beg ? tstart : g_beg;
+            const int tt = (int)(tile % ntt);          // neighbouring tiles share a weight tile
+            const int nt = (int)(tile / ntt);
             c.t0 = tt * BT;
             c.t_end = args.M;
             c.n0 = nt * GEMM_BN;
             c.wrow0 = c.n0;
-            c.kb0 = c.ks * args.kb_per_split;
-            c.kb1 = min(args.nkb, c.kb0 + args.kb_per_split);
+            c.kb0 = (int)(s0 - tstart) * args.gran;
+            c.kb1 = min(args.nkb, (int)(cur - tstart) * args.gran);
+            c.finishes = cur - tstart == args.tile_g;
+            // the CTA whose range holds granule tstart: largest c with c*total/grid <= tstart
+            c.c_first = (int)(((tstart + 1) * (int64_t)gridDim.x - 1) / args.total_g);
+            c.next = s0;
         }
         return c;
     };
@@ -211,8 +253,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         int issued = -1;                                 // phase of the last issue per stage, packed
         uint32_t issued_mask = 0, issued_par = 0;
         bool ok = true;
-        for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-            const UnitCoords uc = unit_coords(u);
+        for (int64_t cur = cursor0; cursor_ok(cur) && ok;) {
+            const UnitCoords uc = unit_coords(cur);
+            cur = uc.next;
             for (int kb = uc.kb0; kb < uc.kb1; kb++) {
                 if (!mbar_wait(empty_bar(stage), phase ^ 1u, args.err, ERR_WAIT_PRODUCER, abort_flag)) { ok = false; break; }
                 const uint32_t sa = sbase + stage * C::STAGE_BYTES;
@@ -248,8 +291,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                 uint32_t rph = 0;
                 uint32_t issued_mask = 0, issued_par = 0;
                 bool ok = true;
-                for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-                    const UnitCoords uc = unit_coords(u);
+                for (int64_t cur = cursor0; cursor_ok(cur) && ok;) {
+                    const UnitCoords uc = unit_coords(cur);
+                    cur = uc.next;
                     const int sb0 = uc.kb0 >> 2, sb_end = (uc.kb1 + 3) >> 2;
                     for (int pf = sb0; pf < sb0 + RC::PREFETCH && pf < sb_end; pf++)
                         tma_prefetch_l2_2d(&tmW, pf * RC::X_ELEMS, uc.wrow0);
@@ -282,8 +326,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             // descriptors of stage 0; a stage adds STAGE_BYTES, a 16-element K step 32 bytes (>> 4)
             const uint64_t wdesc0 = sdesc_k_sw128(sbase + C::A_BYTES);
             const uint64_t adesc0 = sdesc_k_sw128(sbase);
-            for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, lt++) {
-                const UnitCoords uc = unit_coords(u);
+            for (int64_t cur = cursor0; cursor_ok(cur) && ok; lt++) {
+                const UnitCoords uc = unit_coords(cur);
+                cur = uc.next;
                 const int kb0 = uc.kb0, kb1 = uc.kb1;
                 const int acc = lt & 1;
                 const uint32_t aphase = (uint32_t)(lt >> 1) & 1u;
@@ -314,45 +359,101 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         float* es = reinterpret_cast<float*>(smem + C::EPI_OFF) + (warp - W_EPI0) * 1024;
         const float4* es4 = reinterpret_cast<const float4*>(es);
         const int cc = lane & 7;                         // float4 column of the read-back
+        const uint32_t lane_tmem = tmem_base + ((uint32_t)(32 * q) << 16);
         int lt = 0;
-        for (int u = blockIdx.x; u < num_units; u += gridDim.x, lt++) {
-            const UnitCoords uc = unit_coords(u);
+        for (int64_t cur = cursor0; cursor_ok(cur); lt++) {
+            const UnitCoords uc = unit_coords(cur);
+            cur = uc.next;
             const int acc = lt & 1;
             const uint32_t aphase = (uint32_t)(lt >> 1) & 1u;
+            const int ntok = min(BT, uc.t_end - uc.t0);  // tokens of this tile
+            bool with_part = false;
+            if constexpr (!GROUPED) {
+                if (uc.finishes && uc.c_first < (int)blockIdx.x) {
+                    // A finisher sums the partials of the lower-numbered CTAs sharing its tile
+                    // (they computed them first) into the idle accumulator while its own K range
+                    // is still on the tensor core; this is always the CTA's last item, so the MMA
+                    // issuer no longer uses that accumulator.
+                    bool ok = true;
+                    for (int c = uc.c_first; c < (int)blockIdx.x && ok; c++)
+                        ok = wait_flag(args.flags + 4 * c + q, args.epoch, args.err, abort_flag);
+                    if (!ok) break;
+                    for (int c0 = 0; c0 < ntok; c0 += 32) {
+                        const float* p = args.partials + (size_t)uc.c_first * (BT * GEMM_BN) +
+                                         (size_t)c0 * GEMM_BN + 32 * q + lane;
+                        float sum[32];
+#pragma unroll
+                        for (int j = 0; j < 32; j++) sum[j] = __ldcg(p + j * GEMM_BN);
+                        for (int c = uc.c_first + 1; c < (int)blockIdx.x; c++) {
+                            p += BT * GEMM_BN;
+#pragma unroll
+                            for (int j = 0; j < 32; j++) sum[j] += __ldcg(p + j * GEMM_BN);
+                        }
+                        uint32_t r[32];
+#pragma unroll
+                        for (int j = 0; j < 32; j++) r[j] = __float_as_uint(sum[j]);
+                        tmem_st32(lane_tmem + (uint32_t)((acc ^ 1) * BT + c0), r);
+                    }
+                    tmem_st_wait();
+                    with_part = true;
+                }
+            }
             if (!mbar_wait(tfull_bar(acc), aphase, args.err, ERR_WAIT_EPILOGUE, abort_flag)) break;
             tc_fence_after();
-            const int nb = uc.n0 + 32 * q + 4 * cc;      // this lane's 4 output columns
-            float* obase = args.out + (size_t)uc.ks * args.split_stride;
-            const bool scaled = args.splits == 1;
-            for (int c0 = 0; c0 < BT; c0 += 32) {
-                if (uc.t0 + c0 >= uc.t_end) break;
-                uint32_t r[32];
-                tmem_ld32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BT + c0), r);
-                tmem_ld_wait();
+            if (!uc.finishes) {
+                // A piece another CTA finishes: this warp's 32 weight rows of the unscaled
+                // partial, stored [token][128] f32 straight from TMEM (coalesced per token).
+                float* p = args.partials + (size_t)blockIdx.x * (BT * GEMM_BN) + 32 * q + lane;
+                for (int c0 = 0; c0 < ntok; c0 += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(lane_tmem + (uint32_t)(acc * BT + c0), r);
+                    tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 32; j++) es[j * 32 + lane] = __uint_as_float(r[j]);
-                __syncwarp();
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const int jr = (lane >> 3) + 4 * i;
-                    const int t = uc.t0 + c0 + jr;
-                    if (t < uc.t_end && nb < args.N) {
-                        float4 v = es4[jr * 8 + cc];
-                        if (scaled) {
-                            const float sc = __ldg(args.scales + t);
-                            v.x *= sc; v.y *= sc; v.z *= sc; v.w *= sc;
-                        }
-                        float* dp;
-                        if constexpr (GROUPED)
-                            dp = reinterpret_cast<float*>(reinterpret_cast<char*>(args.out) +
-                                                          (int64_t)__ldg(args.g_tok + t) * args.d_nb2 +
-                                                          (int64_t)__ldg(args.g_slot + t) * args.d_nb1) + nb;
-                        else
-                            dp = obase + (size_t)t * args.ldo + nb;
-                        *reinterpret_cast<float4*>(dp) = v;
-                    }
+                    for (int j = 0; j < 32; j++) __stcg(p + (size_t)(c0 + j) * GEMM_BN, __uint_as_float(r[j]));
                 }
+                __threadfence();
                 __syncwarp();
+                if (lane == 0) st_release_gpu(args.flags + 4 * blockIdx.x + q, args.epoch);
+            } else {
+                const int nb = uc.n0 + 32 * q + 4 * cc;  // this lane's 4 output columns
+                for (int c0 = 0; c0 < ntok; c0 += 32) {
+                    // the scale of token c0 + lane, handed to the storing lanes by shuffle
+                    const int tl = uc.t0 + c0 + lane;
+                    const float sc_lane = tl < uc.t_end ? __ldg(args.scales + tl) : 0.0f;
+                    uint32_t r[32];
+                    tmem_ld32(lane_tmem + (uint32_t)(acc * BT + c0), r);
+                    if (with_part) {
+                        uint32_t r2[32];
+                        tmem_ld32(lane_tmem + (uint32_t)((acc ^ 1) * BT + c0), r2);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 32; j++) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(r2[j]));
+                    } else {
+                        tmem_ld_wait();
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; j++) es[j * 32 + lane] = __uint_as_float(r[j]);
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int jr = (lane >> 3) + 4 * i;
+                        const int t = uc.t0 + c0 + jr;
+                        const float sc = __shfl_sync(0xffffffffu, sc_lane, jr);
+                        if (t < uc.t_end && nb < args.N) {
+                            float4 v = es4[jr * 8 + cc];
+                            v.x *= sc; v.y *= sc; v.z *= sc; v.w *= sc;
+                            float* dp;
+                            if constexpr (GROUPED)
+                                dp = reinterpret_cast<float*>(reinterpret_cast<char*>(args.out) +
+                                                              (int64_t)__ldg(args.g_tok + t) * args.d_nb2 +
+                                                              (int64_t)__ldg(args.g_slot + t) * args.d_nb1) + nb;
+                            else
+                                dp = args.out + (size_t)t * args.ldo + nb;
+                            *reinterpret_cast<float4*>(dp) = v;
+                        }
+                    }
+                    __syncwarp();
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -367,8 +468,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             int stage = 0, rs = 0;
             uint32_t phase = 0, rph = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-                const UnitCoords uc = unit_coords(u);
+            for (int64_t cur = cursor0; cursor_ok(cur) && ok;) {
+                const UnitCoords uc = unit_coords(cur);
+                cur = uc.next;
                 for (int sb = uc.kb0 >> 2; sb * 4 < uc.kb1 && ok; sb++) {
                     if (!mbar_wait(rfull_bar(rs), rph, args.err, ERR_WAIT_DEQUANT, abort_flag)) { ok = false; break; }
                     const uint8_t* raw = smem + C::RAW_OFF + rs * RC::STAGE;

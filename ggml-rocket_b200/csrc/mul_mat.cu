@@ -1,9 +1,10 @@
 // MUL_MAT on sm_100a: the activation pre-pass, the weight decode / re-layout kernels, the
-// tcgen05 GEMM launches (gemm.cuh) and the split-K reduction, behind the C ABI declared in
+// tcgen05 GEMM launches (gemm.cuh, stream-K scheduled), behind the C ABI declared in
 // include/ggml-b200-kernels.h.
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include <cuda.h>
@@ -97,21 +98,6 @@ static cudaError_t launch_act_pack(const float* A, int64_t lda, int64_t M, int64
     else if (per <= 8) act_pack_kernel<8><<<grid, ACT_THREADS, 0, st>>>(A, lda, (int)K, a16, scales);
     else act_pack_kernel<16><<<grid, ACT_THREADS, 0, st>>>(A, lda, (int)K, a16, scales);
     return cudaGetLastError();
-}
-
-// ------------------------------------------------------------------------------------------
-// Split-K reduction: out[t, n] = s[t] * sum_s P[s][t, n].
-// ------------------------------------------------------------------------------------------
-__global__ void splitk_reduce_kernel(const float* __restrict__ P, int splits, int64_t split_stride,
-                                     const float* __restrict__ scales, float* __restrict__ out,
-                                     int64_t ldo, int M, int N) {
-    const int64_t total = (int64_t)M * N;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int t = (int)(i / N), n = (int)(i % N);
-        float acc = 0.0f;
-        for (int s = 0; s < splits; s++) acc += P[(size_t)s * split_stride + i];
-        out[(size_t)t * ldo + n] = acc * __ldg(scales + t);
-    }
 }
 
 // ------------------------------------------------------------------------------------------
@@ -241,19 +227,23 @@ static bool make_tmap_2d_u16(CUtensorMap* map, const void* base, uint64_t rows, 
 
 static inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-// The launch plan for one MUL_MAT: token tile, split-K factor and unit count.
+// The launch plan for one MUL_MAT: token tile and the stream-K granule split.
 struct GemmPlan {
-    int bt, splits, kb_per_split, nkb, ntn, ntt, units, grid;
+    int bt, gran, tile_g, nkb, ntn, ntt, grid, pieces;
+    int64_t tiles, total_g;
 };
 
-// Choose the token tile and the split-K factor from a cost model (SM clocks): a unit of
-// kb_per_split K-chunks costs per chunk the slowest of the tensor core (128 x BT x 64 MACs at
-// 4096 MAC/clk), the decode of 8192 quantized weights by 8 warps, and the L2 feed of its
-// operand tiles; units run in waves over the SMs; a split adds its partial-sum round trip.
+// Choose the token tile from a cost model (SM clocks). Per 64-wide K block a tile costs the
+// slowest of the tensor core (128 x BT x 64 MACs at 4096 MAC/clk), the decode of 8192 quantized
+// weights by the dequant warps, and the L2 feed of its operand tiles. Stream-K spreads the
+// tiles' K blocks evenly over the grid, so the time is the total over the grid plus a fixed
+// cost per work item and, where tiles are shared, the partial-tile round trip.
 static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms, int wtype) {
     const bool quant = wtype != WT_F16;
     const int nkb = (int)((K + GEMM_BK - 1) / GEMM_BK);
     const int ntn = (int)((N + GEMM_BN - 1) / GEMM_BN);
+    const int gran = quant ? 4 : 1;
+    const int tile_g = (nkb + gran - 1) / gran;
     GemmPlan best{};
     double best_t = 1e30;
     const int bts[4] = {32, 64, 128, 256};
@@ -261,36 +251,50 @@ static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms, int wtype) {
         const int bt = bts[bi];
         if (bi > 0 && bts[bi - 1] >= M) break;          // a smaller tile already covers M
         const int ntt = (int)((M + bt - 1) / bt);
-        const int tiles = ntn * ntt;
+        const int64_t tiles = (int64_t)ntn * ntt;
+        const int64_t total_g = tiles * tile_g;
+        const int grid = (int)(total_g < sms ? total_g : sms);
         const double mma = bt < 64 ? 128.0 : 2.0 * bt;
-        const double decode = quant ? 300.0 : 0.0;
+        const double decode = quant ? 400.0 : 0.0;
         const double feed = (bt * 128.0 + (quant ? 4600.0 : 16384.0)) / 96.0;
         const double per_kb = (mma > decode ? (mma > feed ? mma : feed) : (decode > feed ? decode : feed)) + 16.0;
-        for (int splits = 1; splits <= 16; splits++) {
-            int kbs = (nkb + splits - 1) / splits;
-            if (quant) kbs = (kbs + 3) / 4 * 4;
-            const int sp = (nkb + kbs - 1) / kbs;
-            if (sp != splits && splits > 1) continue;
-            const int units = tiles * sp;
-            const int grid = units < sms ? units : sms;
-            const int waves = (units + grid - 1) / grid;
-            double t = waves * (kbs * per_kb + 800.0);
-            if (sp > 1) t += 3000.0 + (double)(sp + 1) * M * N * 4.0 / 3200.0;
-            if (t < best_t * 0.97) {
-                best_t = t;
-                best.bt = bt;
-                best.splits = sp;
-                best.kb_per_split = kbs;
-                best.nkb = nkb;
-                best.ntn = ntn;
-                best.ntt = ntt;
-                best.units = units;
-                best.grid = grid;
-            }
-            if (units >= 4 * sms) break;
+        const double items = 1.0 + (double)tiles / grid;
+        const bool shared = total_g % grid != 0 || tiles % grid != 0;
+        double t = (double)tiles * nkb * per_kb / grid + 800.0 * items;
+        if (shared) t += 16.0 * bt;
+        if (t < best_t * 0.97) {
+            best_t = t;
+            best.bt = bt;
+            best.gran = gran;
+            best.tile_g = tile_g;
+            best.nkb = nkb;
+            best.ntn = ntn;
+            best.ntt = ntt;
+            best.grid = grid;
+            best.tiles = tiles;
+            best.total_g = total_g;
+            const int64_t run = total_g / grid;           // shortest granule run of a CTA
+            best.pieces = (int)((tile_g - 1) / run + 2 < tile_g ? (tile_g - 1) / run + 2 : tile_g);
+            if (!shared) best.pieces = 1;
         }
     }
     return best;
+}
+
+// Stream-K scratch: one partial tile per CTA, then four flags per CTA; none when every CTA
+// owns whole tiles.
+static size_t streamk_partials_bytes(const GemmPlan& p) { return (size_t)p.grid * p.bt * GEMM_BN * 4; }
+static size_t streamk_bytes(const GemmPlan& p) {
+    return p.pieces > 1 ? streamk_partials_bytes(p) + (size_t)p.grid * 16 : 0;
+}
+
+// A value no earlier launch has published in the flags (0 is skipped, so zeroed memory never
+// reads as published).
+static uint32_t next_epoch() {
+    static std::atomic<uint32_t> ctr{0x9e3779b9u};
+    uint32_t e;
+    do { e = ctr.fetch_add(1, std::memory_order_relaxed) + 1; } while (e == 0);
+    return e;
 }
 
 struct MulMatWorkspace {
@@ -302,7 +306,7 @@ static MulMatWorkspace mm_workspace_layout(int64_t M, int64_t N, int64_t K, cons
     w.a16_off = 0;
     w.scales_off = align_up((size_t)M * K * 2, 256);
     w.part_off = align_up(w.scales_off + (size_t)M * 4, 256);
-    w.total = w.part_off + (p.splits > 1 ? (size_t)p.splits * M * N * 4 : 0);
+    w.total = w.part_off + streamk_bytes(p);
     return w;
 }
 
@@ -319,8 +323,18 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW,
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
-    gemm_kernel<BT, WT, GROUPED><<<grid, C::THREADS, C::SMEM, st>>>(tmA, tmW, tmD, a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    // stream-K finishers wait on other CTAs of the grid: ask for a grid that is all resident
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = GROUPED ? 0 : 1;
+    return cudaLaunchKernelEx(&cfg, gemm_kernel<BT, WT, GROUPED>, tmA, tmW, tmD, a);
 }
 
 template <int WT, bool GROUPED>
@@ -394,10 +408,7 @@ int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int6
     a.K = (int)K;
     a.n_tiles_n = (int)((N + GEMM_BN - 1) / GEMM_BN);
     a.n_tiles_t = 1;
-    a.splits = 1;
     a.nkb = (int)((K + GEMM_BK - 1) / GEMM_BK);
-    a.kb_per_split = a.nkb;
-    a.num_units = 0;
     a.err = dev_err;
     a.g_off = off;
     a.g_tile_start = tile_start;
@@ -453,45 +464,33 @@ int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, cons
     if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return B200_E_UNSUPPORTED;
     const int sms = device_sm_count();
     const GemmPlan p = plan_gemm(M, N, K, sms, wtype);
-    const size_t part_bytes = p.splits > 1 ? (size_t)p.splits * M * N * 4 : 0;
-    if (part_bytes && (!workspace || workspace_bytes < part_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
+    const size_t sk_bytes = streamk_bytes(p);
+    if (sk_bytes && (!workspace || workspace_bytes < sk_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
         return B200_E_WORKSPACE;
-    float* part = static_cast<float*>(workspace);
     CUtensorMap tmA, tmW, tmD;
     if (!make_tmap_2d_f16(&tmA, a16, (uint64_t)M, (uint64_t)K, (uint64_t)K, (uint32_t)p.bt, GEMM_BK))
         return B200_E_CUDA;
     GemmArgs a{};
     if (!setup_weight_maps(wtype, w_packed, N, K, tmW, tmD, tmA)) return B200_E_CUDA;
     a.scales = scales;
+    a.out = dst;
+    a.ldo = ldd;
     a.M = (int)M;
     a.N = (int)N;
     a.K = (int)K;
     a.n_tiles_n = p.ntn;
     a.n_tiles_t = p.ntt;
-    a.splits = p.splits;
-    a.kb_per_split = p.kb_per_split;
     a.nkb = p.nkb;
-    a.num_units = p.units;
     a.err = dev_err;
-    if (p.splits > 1) {
-        a.out = part;
-        a.ldo = N;
-        a.split_stride = (int64_t)M * N;
-    } else {
-        a.out = dst;
-        a.ldo = ldd;
-        a.split_stride = 0;
-    }
+    a.partials = sk_bytes ? static_cast<float*>(workspace) : nullptr;
+    a.flags = sk_bytes ? reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + streamk_partials_bytes(p))
+                       : nullptr;
+    a.epoch = next_epoch();
+    a.gran = p.gran;
+    a.tile_g = p.tile_g;
+    a.total_g = p.total_g;
     const cudaError_t e = launch_gemm_typed<false>(wtype, p.bt, tmA, tmW, tmD, a, p.grid, st);
-    if (e != cudaSuccess) return B200_E_CUDA;
-    if (p.splits > 1) {
-        const int64_t total = M * N;
-        int blocks = (int)((total + 255) / 256);
-        if (blocks > sms * 8) blocks = sms * 8;
-        splitk_reduce_kernel<<<blocks, 256, 0, st>>>(part, p.splits, (int64_t)M * N, scales, dst, ldd, (int)M, (int)N);
-        if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
-    }
-    return B200_OK;
+    return e == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 
 int act_pack_impl(const float* src1, int64_t lda, int64_t M, int64_t K, __half* a16, float* scales, cudaStream_t st) {
@@ -597,8 +596,7 @@ int b200_act_pack(const float* src1, int64_t lda, int64_t M, int64_t K, void* a1
 
 size_t b200_gemm_packed_workspace_size(int wtype, int64_t M, int64_t N, int64_t K) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
-    const b200::GemmPlan p = b200::plan_gemm(M, N, K, b200::device_sm_count(), wtype);
-    return p.splits > 1 ? (size_t)p.splits * M * N * 4 : 0;
+    return b200::streamk_bytes(b200::plan_gemm(M, N, K, b200::device_sm_count(), wtype));
 }
 
 int b200_gemm_packed(int wtype, const void* w_packed, int64_t N, int64_t K, const void* a16, const float* scales,
@@ -613,9 +611,9 @@ int b200_mul_mat_plan(int wtype, int64_t M, int64_t N, int64_t K, int* token_til
     if (M <= 0 || N <= 0 || K <= 0) return B200_E_INVALID;
     const b200::GemmPlan p = b200::plan_gemm(M, N, K, b200::device_sm_count(), wtype);
     if (token_tile) *token_tile = p.bt;
-    if (splits) *splits = p.splits;
+    if (splits) *splits = p.pieces;
     if (grid) *grid = p.grid;
-    if (launches) *launches = 2 + (p.splits > 1 ? 1 : 0);
+    if (launches) *launches = 2;
     return B200_OK;
 }
 

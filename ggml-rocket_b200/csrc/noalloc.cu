@@ -3,8 +3,8 @@
 // Some hosts cannot call cudaMalloc on the path that runs an op: a plugin loaded into a
 // process whose allocator owns the device and forbids side allocations, code running inside a
 // region that must not change the device memory map, or a caller whose memory budget was fixed
-// up front. b200_mul_mat needs a workspace (the fp16 activations, their row scales and, when K
-// is split, the partial sums); this entry point takes that workspace from a file-scope device
+// up front. b200_mul_mat needs a workspace (the fp16 activations, their row scales and, when
+// CTAs share an output tile, their partial tiles); this entry point takes that workspace from a file-scope device
 // array instead, so the caller passes only its inputs and outputs.
 //
 // The array is NOALLOC_SCRATCH_BYTES (32 MiB); every GPU that loads this library holds it until

@@ -26,6 +26,7 @@ enum : int {
     ERR_WAIT_DEQUANT = 4,    // a dequant warp gave up waiting for a free stage
     ERR_WAIT_DRAIN = 5,      // the drain after an abort gave up
     ERR_BAD_INDEX = 6,       // a bounds check failed
+    ERR_WAIT_PEER = 7,       // a stream-K finisher gave up waiting for another CTA's partial tile
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -113,6 +114,36 @@ __device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity) {
         if (globaltimer() - t0 > B200_WAIT_LIMIT_NS) return false;
     }
     return true;
+}
+
+// ---- flags between CTAs of one grid (global memory, gpu scope) ---------------------------
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Wait until *flag == want (another CTA of the same grid publishes it), bounded like mbar_wait.
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t want, int* err, volatile int* abort_flag) {
+    if (ld_acquire_gpu(flag) == want) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        __nanosleep(128);
+        if (ld_acquire_gpu(flag) == want) return true;
+        if ((i & 63u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer() - t0 > B200_WAIT_LIMIT_NS) {
+                atomicCAS(err, 0, ERR_WAIT_PEER);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
 }
 
 // ---- async-proxy fences and TMA ------------------------------------------------------------
@@ -229,6 +260,19 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
         ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
           "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]),
           "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+// 32 lanes x 32 bits x 32 columns store (the inverse of tmem_ld32).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+          "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+          "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]),
+          "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]),
+          "r"(r[31])
         : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() {

@@ -75,8 +75,9 @@ int    b200_mul_mat(int wtype, const void * w_packed, int64_t N, int64_t K,
  * several weights (the reference's fused QKV / gate-up group shares one pack,
  * ggml-rocket.cpp:4956-5020) or times them apart:
  *   b200_act_pack     src1 F32 [M, lda] -> a16 fp16 [M, K] (dense) + scales F32 [M]
- *   b200_gemm_packed  dst = scales[m] * (a16 . W^T); the workspace is only needed when the
- *                     plan splits K (b200_gemm_packed_workspace_size > 0). */
+ *   b200_gemm_packed  dst = scales[m] * (a16 . W^T); the workspace (256-byte aligned) holds
+ *                     the partial tiles of output tiles whose K range several CTAs share
+ *                     (b200_gemm_packed_workspace_size bytes; 0 when no tile is shared). */
 int    b200_act_pack(const float * src1, int64_t lda, int64_t M, int64_t K, void * a16, float * scales, void * stream);
 size_t b200_gemm_packed_workspace_size(int wtype, int64_t M, int64_t N, int64_t K);
 int    b200_gemm_packed(int wtype, const void * w_packed, int64_t N, int64_t K, const void * a16, const float * scales,
@@ -84,7 +85,8 @@ int    b200_gemm_packed(int wtype, const void * w_packed, int64_t N, int64_t K, 
                         void * stream);
 
 /* The launch plan b200_mul_mat uses on the current device: the token tile (tcgen05 N), the
- * split-K factor, the persistent grid and the number of kernel launches one call makes. */
+ * most CTAs that share one output tile's K range (1 = every CTA owns whole tiles), the
+ * persistent grid and the number of kernel launches one call makes. */
 int    b200_mul_mat_plan(int wtype, int64_t M, int64_t N, int64_t K, int * token_tile, int * splits, int * grid,
                          int * launches);
 
