@@ -22,5 +22,10 @@ int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int6
                       const float* scales, int64_t rows, int bt, const int32_t* off, const int32_t* tile_start,
                       const int32_t* slot, const int32_t* tok, float* dst, int64_t d_nb1, int64_t d_nb2, int* dev_err,
                       cudaStream_t st);
+// Gather b[:, slot[r] % ne11, tok[r]] for r < *n_rows (device count; max_rows bounds the grid)
+// and pack each row to fp16 with its per-row scale (moe.cu).
+int launch_gather_pack(const float* b, int64_t b_nb1, int64_t b_nb2, int64_t ne11, int64_t K, const int32_t* slot,
+                       const int32_t* tok, const int32_t* n_rows, int64_t max_rows, __half* a16, float* scales,
+                       cudaStream_t st);
 
 }  // namespace b200

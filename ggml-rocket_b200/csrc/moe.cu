@@ -142,6 +142,24 @@ __global__ void __launch_bounds__(256) moe_gather_pack_kernel(const float* __res
     }
 }
 
+int launch_gather_pack(const float* b, int64_t b_nb1, int64_t b_nb2, int64_t ne11, int64_t K, const int32_t* slot,
+                       const int32_t* tok, const int32_t* n_rows, int64_t max_rows, __half* a16, float* scales,
+                       cudaStream_t st) {
+    if (max_rows <= 0) return B200_OK;
+    const int64_t per = (K / 4 + 255) / 256;
+    const dim3 grid((unsigned)max_rows);
+#define B200_GATHER(V) \
+    moe_gather_pack_kernel<V><<<grid, 256, 0, st>>>(b, b_nb1, b_nb2, (int)ne11, (int)K, slot, tok, n_rows, a16, scales)
+    if (per <= 1) B200_GATHER(1);
+    else if (per <= 2) B200_GATHER(2);
+    else if (per <= 4) B200_GATHER(4);
+    else if (per <= 8) B200_GATHER(8);
+    else if (per <= 16) B200_GATHER(16);
+    else return B200_E_UNSUPPORTED;
+#undef B200_GATHER
+    return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
 struct MoeLayout {
     size_t off, tiles, slot, tok, a16, scales, total;
 };
@@ -197,18 +215,8 @@ int mul_mat_id_impl(int wtype, const void* as_packed, int64_t K, int64_t N, int6
                                                            (int)n_expert, bt, off, tiles, slot, tok, dev_err);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
 
-    const int64_t per = (K / 4 + 255) / 256;
-    const dim3 grid((unsigned)R);
-#define B200_GATHER(V) \
-    moe_gather_pack_kernel<V><<<grid, 256, 0, st>>>(b, b_nb1, b_nb2, (int)ne11, (int)K, slot, tok, off + n_expert, a16, scales)
-    if (per <= 1) B200_GATHER(1);
-    else if (per <= 2) B200_GATHER(2);
-    else if (per <= 4) B200_GATHER(4);
-    else if (per <= 8) B200_GATHER(8);
-    else if (per <= 16) B200_GATHER(16);
-    else return B200_E_UNSUPPORTED;
-#undef B200_GATHER
-    if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
+    const int rc = launch_gather_pack(b, b_nb1, b_nb2, ne11, K, slot, tok, off + n_expert, R, a16, scales, st);
+    if (rc != B200_OK) return rc;
 
     return gemm_grouped_impl(wtype, as_packed, N, K, n_expert, a16, scales, R, bt, off, tiles, slot, tok, dst, d_nb1,
                              d_nb2, dev_err, st);

@@ -192,6 +192,14 @@ _BACKEND_SIGS = {
 }
 _SIGS.update(_BACKEND_SIGS)
 _SIGS.update({
+    "b200_moe_ep_dispatch": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
+                                    _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "b200_moe_ep_expert_workspace_size": (_sz, [_i64] * 4),
+    "b200_moe_ep_expert": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i64,
+                                  _vp, _vp, _sz, _vp, _vp]),
+    "b200_moe_ep_combine": (_int, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _vp]),
+})
+_SIGS.update({
     "b200_mul_mat_noalloc_max_workspace": (_sz, []),
     "b200_mul_mat_noalloc": (_int, [_int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp]),
     "b200_mul_mat_noalloc_error": (_int, [_vp, _c.POINTER(_int)]),

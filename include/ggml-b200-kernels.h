@@ -159,6 +159,42 @@ int    b200_mul_mat_id(int wtype, const void * as_packed, int64_t K, int64_t N, 
 int    b200_mul_mat_id_route_view(int64_t K, int64_t n_expert, int64_t n_used, int64_t n_tokens,
                                   size_t * off_offset, size_t * slot_offset, size_t * tok_offset);
 
+/* ---- MUL_MAT_ID with the experts split across GPUs (expert parallelism) -------------------
+ * No counterpart in the reference, whose MUL_MAT_ID (ggml-rocket.cpp:6692-6944) runs on one
+ * device; these are its per-rank halves around two all-to-all exchanges the caller runs
+ * (ggml_b200.ep does them with NCCL). Rank r of n_ranks owns experts
+ * [r*E/n_ranks, (r+1)*E/n_ranks) as one packed stack and its own tokens. Per op:
+ *
+ *  1. b200_moe_ep_dispatch (home rank): one send row per (token, b row j, destination rank),
+ *     grouped by destination; its header is {slot mask, ids[0..n_used-1] of the token} (int32
+ *     [n_used+1]); rows are packed fp16 with a per-row scale like MUL_MAT's activations.
+ *     Buffers hold up to n_tokens*n_used rows. counts (device int32 [2*n_ranks+2]) receives
+ *     rows per destination, return rows (slot-mask bits) per destination, total rows, total
+ *     return rows. row_tok / row_slot / row_ret are the home rank's bookkeeping for step 3.
+ *  2. b200_moe_ep_expert (owner rank): over the n_rows received rows (any number of sources,
+ *     concatenated), writes one f32 row of N per (row, slot in its mask) into ret, in received
+ *     order with each row's slots ascending -- the order the home rank expects back.
+ *     n_pairs_hint (host, may be 0) sizes the token tile.
+ *  3. b200_moe_ep_combine (home rank): the returned rows (in destination order, as step 1
+ *     laid them out) -> dst[:, slot, token] with dst strides d_nb1 / d_nb2 in bytes.
+ * An id outside [0, n_expert) (dispatch) or a header naming an expert this rank does not own
+ * (expert) sets *dev_err to B200_DEV_BAD_IDS and produces no rows. */
+int    b200_moe_ep_dispatch(const int32_t * ids, int64_t ids_nb0, int64_t ids_nb1, int64_t n_used,
+                            int64_t n_tokens, int64_t n_expert, int64_t n_ranks,
+                            const float * b, int64_t b_nb1, int64_t b_nb2, int64_t ne11, int64_t K,
+                            void * send_a16, float * send_scale, int32_t * send_hdr,
+                            int32_t * row_tok, int32_t * row_slot, int32_t * row_ret, int32_t * counts,
+                            int * dev_err, void * stream);
+size_t b200_moe_ep_expert_workspace_size(int64_t K, int64_t n_local, int64_t n_used, int64_t n_rows);
+int    b200_moe_ep_expert(int wtype, const void * local_stack, int64_t K, int64_t N, int64_t n_local,
+                          int64_t expert0, const void * recv_a16, const float * recv_scale,
+                          const int32_t * recv_hdr, int64_t n_rows, int64_t n_used, int64_t n_pairs_hint,
+                          float * ret, void * workspace, size_t workspace_bytes, int * dev_err, void * stream);
+int    b200_moe_ep_combine(const float * ret, int64_t N, const int32_t * send_hdr, int64_t n_used,
+                           const int32_t * row_tok, const int32_t * row_ret, const int32_t * counts,
+                           int64_t n_ranks, int64_t max_rows, float * dst, int64_t d_nb1, int64_t d_nb2,
+                           void * stream);
+
 #ifdef __cplusplus
 }
 #endif

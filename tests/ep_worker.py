@@ -1,0 +1,67 @@
+"""One rank of the two-GPU expert-parallel MUL_MAT_ID check (launched by test_gpu_moe_ep.py
+through torchrun): the NCCL path of ggml_b200.ep must reproduce, bit for bit, the single-GPU
+b200_mul_mat_id result for this rank's tokens over the full expert stack."""
+import datetime
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "ggml-rocket_b200"), os.path.join(ROOT, "tests")]
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+import ggml_b200 as g  # noqa: E402
+from ggml_b200 import quants  # noqa: E402
+from ggml_b200.ep import ExpertParallelMulMatId  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    ok = True
+    for (wtype, K, N, E, n_used, ne11, T) in [(12, 2048, 768, 32, 8, 1, 256), (12, 768, 256, 32, 8, 8, 96 + 31 * rank)]:
+        rng = np.random.default_rng(7)
+        w = (rng.standard_normal((E * N, K)) * 0.02).astype(np.float32)
+        native = quants.quantize(wtype, w)
+        e_loc = E // world
+        rpe = native.shape[0] // E
+
+        def pack(nat, rows):
+            raw = torch.from_numpy(np.ascontiguousarray(nat).reshape(-1)).cuda()
+            out = torch.empty(g.weight_packed_size(wtype, rows, K), dtype=torch.uint8, device="cuda")
+            g.weight_pack(wtype, raw, rows, K, out)
+            return out
+
+        local_stack = pack(native[rank * e_loc * rpe:(rank + 1) * e_loc * rpe], e_loc * N)
+        rng = np.random.default_rng(100 + rank)
+        b = torch.from_numpy(rng.standard_normal((T, ne11, K)).astype(np.float32)).cuda()
+        ids = torch.from_numpy(np.stack([rng.permutation(E)[:n_used] for _ in range(T)]).astype(np.int32)).cuda()
+        dst = torch.full((T, n_used, N), float("nan"), device="cuda")
+        ep = ExpertParallelMulMatId()
+        ep(wtype, local_stack, K, N, E, b, ne11, ids, dst)
+        full = pack(native, E * N)
+        want = torch.full_like(dst, float("nan"))
+        ws = torch.zeros(g.mul_mat_id_workspace_size(K, N, E, n_used, T), dtype=torch.uint8, device="cuda")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        rc = g.mul_mat_id(wtype, full, K, N, E, b, K * 4, ne11 * K * 4, ne11, ids, 4, n_used * 4, n_used, T,
+                          want, N * 4, n_used * N * 4, ws, err)
+        torch.cuda.synchronize()
+        same = rc == 0 and int(err.item()) == 0 and bool(torch.equal(dst, want))
+        if not same:
+            print(f"rank {rank} case {(wtype, K, N, E, n_used, ne11, T)} mismatch: "
+                  f"{float((dst - want).abs().max())}", flush=True)
+        ok = ok and same
+    dist.barrier()
+    dist.destroy_process_group()
+    if ok:
+        print("EP_OK", flush=True)
+    return 0 if ok else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
