@@ -55,6 +55,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["gemm", "moe", "fa"], default="gemm",
+                    help="gemm: the headline MUL_MAT sweep (default); moe: the MUL_MAT_ID layer of "
+                         "BASELINE configs[3], expert-parallel over the ranks; fa: the FLASH_ATTN_EXT "
+                         "prefill of configs[2]")
     return ap.parse_args()
 
 
@@ -362,10 +366,192 @@ def run_ours(args):
     return 0
 
 
+# ------------------------------------------------------------------------------------------------
+# secondary workloads (not the headline): MoE layer and flash attention
+# ------------------------------------------------------------------------------------------------
+
+MOE = dict(E=128, top=8, hidden=2048, ffn=768, tokens=2048, wtype=12)
+
+
+def moe_flops_per_rank():
+    m = MOE
+    return 3 * 2.0 * m["tokens"] * m["top"] * m["hidden"] * m["ffn"]
+
+
+def run_moe(args):
+    import numpy as np
+    import torch
+    import ggml_b200 as g
+    from ggml_b200 import quants
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    g.lib()
+    E, top, H, F, T, wt = (MOE[k] for k in ("E", "top", "hidden", "ffn", "tokens", "wtype"))
+    e_loc = E // world
+    rng = np.random.default_rng(0xB200)                 # the same expert stacks on every rank
+
+    def stack(K, N):
+        # 16 distinct quantized experts repeated to 128 (the host quantizer is the slow part;
+        # the device work does not depend on the values)
+        pool = 16
+        w = (rng.standard_normal((pool * N, K), dtype=np.float32) * np.float32(0.02))
+        nat = np.tile(quants.quantize(wt, w).reshape(pool, N, -1), (E // pool, 1, 1)).reshape(E * N, -1)
+        rows = nat[rank * e_loc * N:(rank + 1) * e_loc * N] if world > 1 else nat
+        raw = torch.from_numpy(np.ascontiguousarray(rows).reshape(-1)).to(dev)
+        out = torch.empty(g.weight_packed_size(wt, rows.shape[0], K), dtype=torch.uint8, device=dev)
+        g.weight_pack(wt, raw, rows.shape[0], K, out)
+        return out
+
+    w_gate, w_up, w_down = stack(H, F), stack(H, F), stack(F, H)
+    rng = np.random.default_rng(0xB200 + 17 * rank)     # this rank's tokens
+    x = torch.from_numpy(rng.standard_normal((T, 1, H), dtype=np.float32)).to(dev)
+    h = torch.from_numpy(rng.standard_normal((T, top, F), dtype=np.float32)).to(dev)
+    logits = torch.from_numpy(rng.standard_normal((T, E), dtype=np.float32))
+    ids = torch.topk(torch.softmax(logits, -1), top, dim=-1).indices.to(torch.int32).to(dev)
+    y_gate = torch.empty((T, top, F), device=dev)
+    y_up = torch.empty((T, top, F), device=dev)
+    y_down = torch.empty((T, top, H), device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    if world > 1:
+        from ggml_b200.ep import DeviceOps, ExpertParallelMulMatId
+        ep = ExpertParallelMulMatId(ops=DeviceOps(err))
+
+        def layer():
+            ep(wt, w_gate, H, F, E, x, 1, ids, y_gate)
+            ep(wt, w_up, H, F, E, x, 1, ids, y_up)
+            ep(wt, w_down, F, H, E, h, top, ids, y_down)
+    else:
+        ws = torch.empty(max(g.mul_mat_id_workspace_size(H, F, E, top, T), g.mul_mat_id_workspace_size(F, H, E, top, T)),
+                         dtype=torch.uint8, device=dev)
+
+        def one(wst, K, N, b, ne11, y):
+            rc = g.mul_mat_id(wt, wst, K, N, E, b, K * 4, ne11 * K * 4, ne11, ids, 4, top * 4, top, T, y, N * 4,
+                              top * N * 4, ws, err)
+            g.check(rc, "mul_mat_id")
+
+        def layer():
+            one(w_gate, H, F, x, 1, y_gate)
+            one(w_up, H, F, x, 1, y_up)
+            one(w_down, F, H, h, top, y_down)
+
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        flush.zero_()
+        layer()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda._sleep(400000)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        layer()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    if int(err.item()) != 0:
+        raise SystemExit(f"device error {int(err.item())}")
+    ms_local = sorted(times)[len(times) // 2]
+    t = torch.tensor([ms_local], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    if rank == 0:
+        peaks, src = measured_peaks()
+        tf = moe_flops_per_rank() * world / (ms / 1e3) / 1e12
+        line = {"metric": "MoE MUL_MAT_ID layer prompt tokens/sec (gate+up+down, Q4_K, 128 experts top-8)",
+                "value": T * world / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
+                "config": {"workload": "BASELINE configs[3] MoE layer, 2048 tokens per rank, experts split "
+                                       f"{E}/{world} per rank" + (" (NCCL all-to-all)" if world > 1 else ""),
+                           "weights": "16 distinct N(0,0.02) Q4_K experts per stack, repeated to 128",
+                           "median_of_steps": True},
+                "tflops": tf,
+                "roofline": {"bound": "tensor", "achieved": tf / world, "peak": float(peaks["bf16_tflops"]),
+                             "unit": "TFLOP/s", "frac": tf / world / float(peaks["bf16_tflops"]),
+                             "peak_source": f"{src} bf16_tflops (burst)"}}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def run_fa(args):
+    import numpy as np
+    import torch
+    import ggml_b200 as g
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    g.lib()
+    D, T, Hq, HK = 128, 512, 32, 8
+    res = {}
+    for KV in (1024, 4096, 16384):
+        gen = torch.Generator(device="cpu").manual_seed(KV)
+        q = torch.randn((Hq, T, D), generator=gen).to(dev)
+        k = torch.randn((HK, KV, D), generator=gen).to(torch.float16).to(dev)
+        v = torch.randn((HK, KV, D), generator=gen).to(torch.float16).to(dev)
+        pos = torch.arange(KV - T, KV).view(T, 1)
+        m = torch.where(torch.arange(KV).view(1, KV) <= pos, 0.0, float("-inf")).to(torch.float16).to(dev)
+        dst = torch.empty((T, Hq, D), device=dev)
+        ws = torch.empty(g.flash_attn_workspace_size(D, D, T, Hq, KV, HK), dtype=torch.uint8, device=dev)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+        def call():
+            g.flash_attn_ext(q, D * 4, T * D * 4, k, D * 2, KV * D * 2, v, D * 2, KV * D * 2, m, KV * 2, dst, D, D,
+                             T, Hq, KV, HK, 1.0 / np.sqrt(D), 0.0, ws, err)
+
+        for _ in range(args.warmup):
+            call()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(args.steps):
+            torch.cuda._sleep(200000)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            call()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        if int(err.item()) != 0:
+            raise SystemExit(f"device error {int(err.item())}")
+        ms = sorted(ts)[len(ts) // 2]
+        causal = 4.0 * Hq * D * (T * (KV - T) + T * (T + 1) / 2)    # causal-effective FLOPs
+        res[KV] = {"ms": ms, "tflops_causal": causal / (ms / 1e3) / 1e12,
+                   "tflops_dense": 4.0 * Hq * T * KV * D / (ms / 1e3) / 1e12}
+    if rank == 0:
+        peaks, src = measured_peaks()
+        best = res[16384]["tflops_causal"]
+        line = {"metric": "FLASH_ATTN_EXT prefill TFLOP/s (causal-effective), 32/8 heads, D 128, n_q 512",
+                "value": best, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": res[16384]["ms"], "higher_is_better": True, "scaling": "replicas only",
+                "vs_baseline": None, "dtype": "f16 (fp32 softmax/accumulate)", "data": "synthetic",
+                "config": {"workload": "BASELINE configs[2], value at n_kv=16384", "per_n_kv": res},
+                "roofline": {"bound": "tensor", "achieved": best, "peak": float(peaks["bf16_tflops"]),
+                             "unit": "TFLOP/s", "frac": best / float(peaks["bf16_tflops"]),
+                             "peak_source": f"{src} bf16_tflops (burst)"}}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "moe":
+        return run_moe(args)
+    if args.workload == "fa":
+        return run_fa(args)
     return run_ours(args)
 
 
