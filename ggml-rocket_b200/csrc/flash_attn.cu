@@ -8,11 +8,13 @@
 //   mask_flags per (token block, 128-key block) of the F16 mask: all -inf (skipped), all zero
 //              (no mask loads), or mixed. Causal prefill skips ~half the key blocks.
 //   fa_kernel  one CTA per (group of GP query heads that share a KV head, TQ tokens) = 128 query
-//              rows. Per key block: S = Q.K^T by tcgen05 into one of two TMEM buffers; the 128
-//              softmax threads (one per row) read S from TMEM, keep the online max / sum in
-//              fp32, write P (fp16) to shared memory; O_blk = P.V by tcgen05 into TMEM, which
-//              the same threads fold into their fp32 output registers. K and V tiles arrive by
-//              TMA straight from the op's strided cache views, two stages deep.
+//              rows. Per key block: S = Q.K^T by tcgen05 into one of two TMEM buffers; 256
+//              softmax threads (two per row, 64 keys each, the row max exchanged through shared
+//              memory) read S from TMEM once, keep the online max / sum in fp32 (log2 units),
+//              write P (fp16) to shared memory; O += P.V by tcgen05 accumulates in TMEM for the
+//              whole key range, rescaled in place only when a row max grows by more than 2^8.
+//              K and V tiles arrive by TMA straight from the op's strided cache views, two
+//              stages deep.
 #include <cstdint>
 #include <cstring>
 
@@ -28,7 +30,9 @@ namespace b200 {
 
 constexpr int FA_ROWS = 128;      // query rows per CTA (tcgen05 M)
 constexpr int FA_KB = 128;        // keys per block (tcgen05 N of Q.K^T, K of P.V)
-constexpr int FA_THREADS = 192;   // warp 0 TMA, warp 1 MMA, warps 2..5 softmax
+constexpr int FA_THREADS = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 softmax
+constexpr int FA_SOFTMAX_WARPS = 8;
+constexpr float FA_RESCALE_LOG2 = 8.0f;   // rescale O only when the row max grows by more than 2^8
 enum : uint8_t { MF_MIXED = 0, MF_ZERO = 1, MF_MASKED = 2 };
 
 struct FaArgs {
@@ -165,7 +169,9 @@ struct FaCfg {
     static constexpr int OFF_K = OFF_Q + Q_BYTES;
     static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
     static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
-    static constexpr int OFF_BAR = OFF_P + P_BYTES;
+    // row-pair exchange: maxima [2][256] f32, their sequence numbers [2][256], sums [256] + seq [256]
+    static constexpr int OFF_XCH = OFF_P + P_BYTES;
+    static constexpr int OFF_BAR = OFF_XCH + 6144;
     static constexpr int SMEM = OFF_BAR + 256 + 1024;
     static constexpr uint32_t TMEM_COLS = 512;      // S0 | S1 | O
     static constexpr uint32_t IDESC_S = idesc_f16_f32(FA_ROWS, FA_KB);
@@ -191,7 +197,6 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
     auto s_empty = [&](int s) { return bar + 8u * (11 + s); };
     const uint32_t p_full = bar + 8u * 13;
     const uint32_t o_full = bar + 8u * 14;
-    const uint32_t o_empty = bar + 8u * 15;
     const uint32_t drain = bar + 8u * 16;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 8 * 17);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 8 * 17 + 4);
@@ -212,11 +217,10 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
             mbar_init(v_full(s), 1);
             mbar_init(v_empty(s), 1);
             mbar_init(s_full(s), 1);
-            mbar_init(s_empty(s), 4);
+            mbar_init(s_empty(s), FA_SOFTMAX_WARPS);
         }
-        mbar_init(p_full, 4);
+        mbar_init(p_full, FA_SOFTMAX_WARPS);
         mbar_init(o_full, 1);
-        mbar_init(o_empty, 4);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -227,6 +231,12 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
         tmem_relinquish();
+    }
+    {
+        int* seqs = reinterpret_cast<int*>(smem + C::OFF_XCH + 2048);
+        for (int k = threadIdx.x; k < 512; k += FA_THREADS) seqs[k] = 0;
+        int* seql = reinterpret_cast<int*>(smem + C::OFF_XCH + 5120);
+        for (int k = threadIdx.x; k < 256; k += FA_THREADS) seql[k] = 0;
     }
     tc_fence_before();
     __syncthreads();
@@ -276,14 +286,13 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
                 const uint32_t ph = (uint32_t)(i >> 1) & 1u;
                 if (!mbar_wait(p_full, (uint32_t)i & 1u, args.err, ERR_WAIT_MMA, abort_flag)) return false;
                 if (!mbar_wait(v_full(s), ph, args.err, ERR_WAIT_MMA, abort_flag)) return false;
-                if (i > 0 && !mbar_wait(o_empty, (uint32_t)(i - 1) & 1u, args.err, ERR_WAIT_MMA, abort_flag)) return false;
                 tc_fence_after();
                 const uint32_t vb = sb + C::OFF_V + s * C::V_BYTES;
 #pragma unroll
                 for (int ks = 0; ks < FA_KB / 16; ks++) {
                     const uint64_t a = sdesc_k_sw128(sb + C::OFF_P + (ks >> 2) * (FA_ROWS * 128) + (ks & 3) * 32);
                     const uint64_t bdesc = sdesc_mn_sw128(vb + ks * 2048, FA_KB * 128);
-                    mma_f16(tmem + 256, a, bdesc, C::IDESC_O, ks > 0 ? 1u : 0u);
+                    mma_f16(tmem + 256, a, bdesc, C::IDESC_O, (i > 0 || ks > 0) ? 1u : 0u);   // O stays in TMEM
                 }
                 mma_commit(o_full);
                 mma_commit(v_empty(s));
@@ -314,8 +323,14 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
             if (!mbar_drain(drain, 0)) atomicCAS(args.err, 0, ERR_WAIT_DRAIN);
         }
     } else {
-        // ---------------- softmax / output (128 threads, one query row each) ----------------
+        // ---------------- softmax / output: 8 warps, two threads per query row ----------------
+        // Warps w and w+4 share TMEM lane quarter (w & 3); thread (row r, half hf) owns keys
+        // [64*hf, 64*hf + 64) of every block and O columns [hf*DV/2, (hf+1)*DV/2). Scores are kept
+        // in log2 units. O accumulates in TMEM across blocks (P.V MMAs with accumulate); it is
+        // rescaled only when a row's max grows by more than 2^FA_RESCALE_LOG2 over the max the
+        // exponentials were taken against (which keeps P <= 2^8 and the sums exact up to rounding).
         const int quad = warp & 3;
+        const int hf = (warp - 2) >> 2;
         const int r = quad * 32 + lane;
         const int g = r / args.TQ, tq = r % args.TQ;
         const int h = hg * args.GP + g;
@@ -324,128 +339,182 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
         const float qs = row_valid ? __ldg(args.qscale + (int64_t)h * args.T + t) : 1.0f;
         const uint16_t* mrow = (args.mask && row_valid) ? args.mask + (int64_t)t * args.m_stride : nullptr;
         const float LOG2E = 1.4426950408889634f;
+        const float c2 = qs * LOG2E;                     // raw score -> log2 units
         const float softcap = args.softcap;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-        float o[DV];
-#pragma unroll
-        for (int c = 0; c < DV; c++) o[c] = 0.0f;
-        float m = -INFINITY, l = 0.0f;
+        const uint32_t o_tmem = tmem + lane_base + 256u + (uint32_t)(hf * (DV / 2));
+        volatile float* xv = reinterpret_cast<volatile float*>(smem + C::OFF_XCH);
+        volatile int* xs = reinterpret_cast<volatile int*>(smem + C::OFF_XCH + 2048);
+        volatile float* xl = reinterpret_cast<volatile float*>(smem + C::OFF_XCH + 4096);
+        volatile int* xls = reinterpret_cast<volatile int*>(smem + C::OFF_XCH + 5120);
+        const uint32_t pchunk = sb + C::OFF_P + (uint32_t)hf * (FA_ROWS * 128);
+        // Hand a value to the other thread of this row and take its value: a bounded spin on a
+        // sequence number in shared memory (the two threads are in different warps).
+        auto exchange = [&](volatile float* v, volatile int* sq, float mine, int seq, float& theirs) -> bool {
+            v[hf * 128 + r] = mine;
+            __threadfence_block();
+            sq[hf * 128 + r] = seq;
+            const int other = (hf ^ 1) * 128 + r;
+            if (sq[other] != seq) {
+                const uint64_t t0 = globaltimer();
+                for (uint32_t n = 1; sq[other] != seq; ++n) {
+                    if ((n & 255u) == 0) {
+                        if (*abort_flag) return false;
+                        if (globaltimer() - t0 > B200_WAIT_LIMIT_NS) {
+                            atomicCAS(args.err, 0, ERR_WAIT_EPILOGUE);
+                            *abort_flag = 1;
+                            return false;
+                        }
+                    }
+                }
+            }
+            __threadfence_block();
+            theirs = v[other];
+            return true;
+        };
+        float m = -INFINITY;                             // running max (log2 units)
+        float l = 0.0f;                                  // this thread's partial row sum
         int i = 0;
         bool ok = true;
-        auto score = [&](float raw, int key, uint16_t mbits, bool use_mask) -> float {
-            float s = raw * qs;
-            if (softcap != 0.0f) s = softcap * tanhf(s / softcap);
-            if (key >= args.KV) return -INFINITY;
-            if (use_mask) s += __half2float(__ushort_as_half(mbits));
-            return s;
-        };
         for (int j = 0; j < args.n_kvb && ok; j++) {
             const uint8_t fl = flags[j];
             if (fl == MF_MASKED) continue;
             const bool use_mask = (fl == MF_MIXED) && (mrow != nullptr);
+            const bool general = use_mask || softcap != 0.0f || (j + 1) * FA_KB > args.KV;
             const int s = i & 1;
             const uint32_t ph = (uint32_t)(i >> 1) & 1u;
             if (!mbar_wait(s_full(s), ph, args.err, ERR_WAIT_EPILOGUE, abort_flag)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t sbase = tmem + lane_base + (uint32_t)(s * FA_KB);
-            // pass 1: the block's row max
-            float bmax = -INFINITY;
-#pragma unroll 1
-            for (int c0 = 0; c0 < FA_KB; c0 += 32) {
-                uint32_t rv[32];
-                tmem_ld32(sbase + c0, rv);
+            float x[64];
+            {
+                const uint32_t sbase = tmem + lane_base + (uint32_t)(s * FA_KB + hf * 64);
+                uint32_t rv[32], rv2[32];
+                tmem_ld32(sbase, rv);
+                tmem_ld32(sbase + 32u, rv2);
                 tmem_ld_wait();
-                uint4 mv[4];
-                if (use_mask) load_mask32(mrow, j * FA_KB + c0, args.KV, args.mask_vec, mv);
 #pragma unroll
                 for (int e = 0; e < 32; e++) {
-                    const uint32_t mw = use_mask ? (&mv[e >> 3].x)[(e & 7) >> 1] : 0u;
-                    const uint16_t mb = (uint16_t)((e & 1) ? (mw >> 16) : (mw & 0xFFFFu));
-                    bmax = fmaxf(bmax, score(__uint_as_float(rv[e]), j * FA_KB + c0 + e, mb, use_mask));
+                    x[e] = __uint_as_float(rv[e]);
+                    x[32 + e] = __uint_as_float(rv2[e]);
                 }
             }
-            const float m_new = fmaxf(m, bmax);
-            const float m_use = (m_new == -INFINITY) ? 0.0f : m_new;
-            const float alpha = (m == -INFINITY) ? 0.0f : ex2_approx((m - m_use) * LOG2E);
-            // fold the previous block's P.V into the registers, then rescale
+            // S is in registers: the buffer may take the next Q.K^T
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_empty(s));
+            const int k0 = j * FA_KB + hf * 64;
+            float bmax = -INFINITY;
+            if (!general) {
+#pragma unroll
+                for (int e = 0; e < 64; e++) bmax = fmaxf(bmax, x[e]);
+                bmax *= c2;
+            } else {
+#pragma unroll
+                for (int c0 = 0; c0 < 64; c0 += 32) {
+                    uint4 mv[4];
+                    if (use_mask) load_mask32(mrow, k0 + c0, args.KV, args.mask_vec, mv);
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        const int ee = c0 + e;
+                        float sv = x[ee] * qs;
+                        if (softcap != 0.0f) sv = softcap * tanhf(sv / softcap);
+                        sv *= LOG2E;
+                        if (use_mask) {
+                            const uint32_t mw = (&mv[e >> 3].x)[(e & 7) >> 1];
+                            const uint16_t mb = (uint16_t)((e & 1) ? (mw >> 16) : (mw & 0xFFFFu));
+                            sv = fmaf(__half2float(__ushort_as_half(mb)), LOG2E, sv);
+                        }
+                        if (k0 + ee >= args.KV) sv = -INFINITY;
+                        x[ee] = sv;
+                        bmax = fmaxf(bmax, sv);
+                    }
+                }
+            }
+            // the row max over both halves (double-buffered by block parity)
+            float other_max;
+            if (!exchange(xv + (i & 1) * 256, xs + (i & 1) * 256, bmax, i + 1, other_max)) { ok = false; break; }
+            bmax = fmaxf(bmax, other_max);
+            const bool grow = bmax > m + FA_RESCALE_LOG2;
+            const float m_new = grow ? bmax : m;
+            const float alpha = (grow && m != -INFINITY) ? ex2_approx(m - m_new) : 1.0f;
+            // P.V of the previous block must be done before P is overwritten and O rescaled
             if (i > 0) {
                 if (!mbar_wait(o_full, (uint32_t)(i - 1) & 1u, args.err, ERR_WAIT_EPILOGUE, abort_flag)) { ok = false; break; }
                 tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll
-                for (int c0 = 0; c0 < DV; c0 += 32) {
-                    uint32_t ov[32];
-                    tmem_ld32(tmem + lane_base + 256u + (uint32_t)c0, ov);
-                    tmem_ld_wait();
+                    for (int c0 = 0; c0 < DV / 2; c0 += 32) {
+                        uint32_t ov[32];
+                        tmem_ld32(o_tmem + (uint32_t)c0, ov);
+                        tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 32; e++) o[c0 + e] += __uint_as_float(ov[e]);
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(o_empty);
-            }
-#pragma unroll
-            for (int c = 0; c < DV; c++) o[c] *= alpha;
-            l *= alpha;
-            // pass 2: P = exp(S - m) to shared memory (fp16, 128-byte swizzled, K-major)
-            const float mb2 = m_use * LOG2E;
-#pragma unroll 1
-            for (int c0 = 0; c0 < FA_KB; c0 += 32) {
-                uint32_t rv[32];
-                tmem_ld32(sbase + c0, rv);
-                tmem_ld_wait();
-                uint4 mv[4];
-                if (use_mask) load_mask32(mrow, j * FA_KB + c0, args.KV, args.mask_vec, mv);
-                uint32_t pw[16];
-#pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    float p2[2];
-#pragma unroll
-                    for (int u = 0; u < 2; u++) {
-                        const int ee = e + u;
-                        const uint32_t mw = use_mask ? (&mv[ee >> 3].x)[(ee & 7) >> 1] : 0u;
-                        const uint16_t mbits = (uint16_t)((ee & 1) ? (mw >> 16) : (mw & 0xFFFFu));
-                        const float sc = score(__uint_as_float(rv[ee]), j * FA_KB + c0 + ee, mbits, use_mask);
-                        p2[u] = (sc == -INFINITY) ? 0.0f : ex2_approx(fmaf(sc, LOG2E, -mb2));
-                        l += p2[u];
+                        for (int e = 0; e < 32; e++) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+                        tmem_st32(o_tmem + (uint32_t)c0, ov);
                     }
-                    pw[e >> 1] = pack_half2(p2[0], p2[1]);
+                    tmem_st_wait();
                 }
-                // keys c0..c0+31 -> P chunk (c0 / 64), 16-byte units ((c0 % 64) / 8) .. +3
-                const uint32_t pchunk = sb + C::OFF_P + (uint32_t)(c0 >> 6) * (FA_ROWS * 128);
-                const uint32_t u0 = (uint32_t)((c0 & 63) >> 3);
-#pragma unroll
-                for (int u = 0; u < 4; u++)
-                    st_shared_v4(pchunk + sw128_offset((uint32_t)r, u0 + u), pw[4 * u], pw[4 * u + 1], pw[4 * u + 2],
-                                 pw[4 * u + 3]);
             }
+            l *= alpha;
+            m = m_new;
+            const float mu = (m == -INFINITY) ? 0.0f : m;
+            uint32_t pw[32];
+            if (!general) {
+#pragma unroll
+                for (int e = 0; e < 64; e += 2) {
+                    const float p0 = ex2_approx(fmaf(x[e], c2, -mu));
+                    const float p1 = ex2_approx(fmaf(x[e + 1], c2, -mu));
+                    l += p0 + p1;
+                    pw[e >> 1] = pack_half2(p0, p1);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 64; e += 2) {
+                    const float p0 = ex2_approx(x[e] - mu);
+                    const float p1 = ex2_approx(x[e + 1] - mu);
+                    l += p0 + p1;
+                    pw[e >> 1] = pack_half2(p0, p1);
+                }
+            }
+            // keys 64*hf .. +63 of this row -> P chunk hf (128-byte swizzled, K-major)
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                st_shared_v4(pchunk + sw128_offset((uint32_t)r, (uint32_t)u), pw[4 * u], pw[4 * u + 1], pw[4 * u + 2],
+                             pw[4 * u + 3]);
             tc_fence_before();
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(s_empty(s));
-                mbar_arrive(p_full);
-            }
-            m = m_new;
+            if (lane == 0) mbar_arrive(p_full);
             i++;
         }
+        bool have_o = false;
         if (ok && i > 0) {
-            if (mbar_wait(o_full, (uint32_t)(i - 1) & 1u, args.err, ERR_WAIT_EPILOGUE, abort_flag)) {
-                tc_fence_after();
+            have_o = mbar_wait(o_full, (uint32_t)(i - 1) & 1u, args.err, ERR_WAIT_EPILOGUE, abort_flag);
+            tc_fence_after();
+        }
+        // row sum over both halves, added in a fixed order so both threads agree
+        float l_other = 0.0f;
+        if (ok && !exchange(xl, xls, l, 1, l_other)) ok = false;
+        const float l_tot = hf == 0 ? l + l_other : l_other + l;
+        if (ok && have_o) {
+            const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
+            float* out = args.dst + ((int64_t)t * args.H + h) * DV + hf * (DV / 2);
 #pragma unroll
-                for (int c0 = 0; c0 < DV; c0 += 32) {
-                    uint32_t ov[32];
-                    tmem_ld32(tmem + lane_base + 256u + (uint32_t)c0, ov);
-                    tmem_ld_wait();
+            for (int c0 = 0; c0 < DV / 2; c0 += 32) {
+                uint32_t ov[32];
+                tmem_ld32(o_tmem + (uint32_t)c0, ov);
+                tmem_ld_wait();
+                if (row_valid) {
 #pragma unroll
-                    for (int e = 0; e < 32; e++) o[c0 + e] += __uint_as_float(ov[e]);
+                    for (int e = 0; e < 32; e += 4)
+                        *reinterpret_cast<float4*>(out + c0 + e) =
+                            make_float4(__uint_as_float(ov[e]) * inv, __uint_as_float(ov[e + 1]) * inv,
+                                        __uint_as_float(ov[e + 2]) * inv, __uint_as_float(ov[e + 3]) * inv);
                 }
             }
-        }
-        if (row_valid) {
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-            float4* out = reinterpret_cast<float4*>(args.dst + ((int64_t)t * args.H + h) * DV);
-#pragma unroll
-            for (int c = 0; c < DV; c += 4) out[c >> 2] = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+        } else if (ok && row_valid) {
+            // no key block survived the mask: the row is all zeros
+            float* out = args.dst + ((int64_t)t * args.H + h) * DV + hf * (DV / 2);
+            for (int c = 0; c < DV / 2; c += 4) *reinterpret_cast<float4*>(out + c) = make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
 
