@@ -30,8 +30,9 @@ namespace b200 {
 
 constexpr int FA_ROWS = 128;      // query rows per CTA (tcgen05 M)
 constexpr int FA_KB = 128;        // keys per block (tcgen05 N of Q.K^T, K of P.V)
-constexpr int FA_THREADS = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 softmax
-constexpr int FA_SOFTMAX_WARPS = 8;
+constexpr int FA_SPLIT = 2;                          // softmax threads per query row
+constexpr int FA_SOFTMAX_WARPS = 4 * FA_SPLIT;
+constexpr int FA_THREADS = 64 + 32 * FA_SOFTMAX_WARPS;   // warp 0 TMA, warp 1 MMA, then softmax
 constexpr float FA_RESCALE_LOG2 = 8.0f;   // rescale O only when the row max grows by more than 2^8
 enum : uint8_t { MF_MIXED = 0, MF_ZERO = 1, MF_MASKED = 2 };
 
@@ -156,6 +157,20 @@ __global__ void fa_mask_flags_kernel(const uint16_t* __restrict__ mask, int64_t 
     if (threadIdx.x == 0) flags[(int64_t)tb * n_kvb + j] = am ? MF_MASKED : (az ? MF_ZERO : MF_MIXED);
 }
 
+// A P row segment of N 32-bit columns (2N fp16 keys) into TMEM.
+template <int N>
+__device__ __forceinline__ void tmem_st_p(uint32_t taddr, const uint32_t (&w)[N]) {
+    if constexpr (N == 64) {
+        tmem_st32(taddr, reinterpret_cast<const uint32_t(&)[32]>(w[0]));
+        tmem_st32(taddr + 32u, reinterpret_cast<const uint32_t(&)[32]>(w[32]));
+    } else if constexpr (N == 32) {
+        tmem_st32(taddr, w);
+    } else {
+        static_assert(N == 16, "P segments are 16, 32 or 64 columns");
+        tmem_st16(taddr, w);
+    }
+}
+
 // ---------------------------------------------------------------------------------------------
 // The attention kernel.
 // ---------------------------------------------------------------------------------------------
@@ -164,16 +179,20 @@ struct FaCfg {
     static constexpr int Q_BYTES = FA_ROWS * D * 2;
     static constexpr int K_BYTES = FA_KB * D * 2;
     static constexpr int V_BYTES = FA_KB * DV * 2;
-    static constexpr int P_BYTES = FA_ROWS * FA_KB * 2;
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = OFF_Q + Q_BYTES;
     static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
-    static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
-    // row-pair exchange: maxima [2][256] f32, their sequence numbers [2][256], sums [256] + seq [256]
-    static constexpr int OFF_XCH = OFF_P + P_BYTES;
-    static constexpr int OFF_BAR = OFF_XCH + 6144;
+    // exchange between the FA_SPLIT threads of a row: maxima [2][SPLIT][128] f32 and their
+    // sequence numbers (same shape, int), then sums [SPLIT][128] + sequence numbers
+    static constexpr int XCH_MAX = 2 * FA_SPLIT * 128 * 4;
+    static constexpr int XCH_SUM = FA_SPLIT * 128 * 4;
+    static constexpr int OFF_XCH = OFF_V + 2 * V_BYTES;
+    static constexpr int OFF_BAR = OFF_XCH + 2 * XCH_MAX + 2 * XCH_SUM;
     static constexpr int SMEM = OFF_BAR + 256 + 1024;
-    static constexpr uint32_t TMEM_COLS = 512;      // S0 | S1 | O
+    // TMEM columns: S0 [0,128) | S1 [128,256) | O [256, 256+DV) | P0 [384,448) | P1 [448,512)
+    // (P is fp16, two keys per 32-bit column, read by the P.V MMA as its A operand)
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr uint32_t P_TMEM0 = 384;
     static constexpr uint32_t IDESC_S = idesc_f16_f32(FA_ROWS, FA_KB);
     static constexpr uint32_t IDESC_O = idesc_f16_f32_bmn(FA_ROWS, DV);
 };
@@ -195,11 +214,13 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
     auto v_empty = [&](int s) { return bar + 8u * (7 + s); };
     auto s_full = [&](int s) { return bar + 8u * (9 + s); };
     auto s_empty = [&](int s) { return bar + 8u * (11 + s); };
-    const uint32_t p_full = bar + 8u * 13;
-    const uint32_t o_full = bar + 8u * 14;
+    // P of blocks b, b+2, ... written (per parity: a softmax warp may run one block ahead of
+    // another, never two, because P buffer b is reused only after the P.V two blocks back)
+    auto p_full = [&](int b) { return bar + 8u * (17 + b); };
+    auto pv_done = [&](int b) { return bar + 8u * (14 + b); };   // P.V of blocks b, b+2, ... completed
     const uint32_t drain = bar + 8u * 16;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 8 * 17);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 8 * 17 + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 8 * 19);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_BAR + 8 * 19 + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // heavier (later) token blocks first
@@ -219,8 +240,10 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
             mbar_init(s_full(s), 1);
             mbar_init(s_empty(s), FA_SOFTMAX_WARPS);
         }
-        mbar_init(p_full, FA_SOFTMAX_WARPS);
-        mbar_init(o_full, 1);
+        mbar_init(p_full(0), FA_SOFTMAX_WARPS);
+        mbar_init(p_full(1), FA_SOFTMAX_WARPS);
+        mbar_init(pv_done(0), 1);
+        mbar_init(pv_done(1), 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -233,10 +256,10 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
         tmem_relinquish();
     }
     {
-        int* seqs = reinterpret_cast<int*>(smem + C::OFF_XCH + 2048);
-        for (int k = threadIdx.x; k < 512; k += FA_THREADS) seqs[k] = 0;
-        int* seql = reinterpret_cast<int*>(smem + C::OFF_XCH + 5120);
-        for (int k = threadIdx.x; k < 256; k += FA_THREADS) seql[k] = 0;
+        int* seqs = reinterpret_cast<int*>(smem + C::OFF_XCH + C::XCH_MAX);
+        for (int k = threadIdx.x; k < 2 * FA_SPLIT * 128; k += FA_THREADS) seqs[k] = 0;
+        int* seql = reinterpret_cast<int*>(smem + C::OFF_XCH + 2 * C::XCH_MAX + C::XCH_SUM);
+        for (int k = threadIdx.x; k < FA_SPLIT * 128; k += FA_THREADS) seql[k] = 0;
     }
     tc_fence_before();
     __syncthreads();
@@ -284,17 +307,17 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
             auto issue_pv = [&](int i) -> bool {
                 const int s = i & 1;
                 const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-                if (!mbar_wait(p_full, (uint32_t)i & 1u, args.err, ERR_WAIT_MMA, abort_flag)) return false;
+                if (!mbar_wait(p_full(i & 1), (uint32_t)(i >> 1) & 1u, args.err, ERR_WAIT_MMA, abort_flag)) return false;
                 if (!mbar_wait(v_full(s), ph, args.err, ERR_WAIT_MMA, abort_flag)) return false;
                 tc_fence_after();
                 const uint32_t vb = sb + C::OFF_V + s * C::V_BYTES;
+                const uint32_t p_tmem = tmem + C::P_TMEM0 + (uint32_t)(64 * (i & 1));
 #pragma unroll
                 for (int ks = 0; ks < FA_KB / 16; ks++) {
-                    const uint64_t a = sdesc_k_sw128(sb + C::OFF_P + (ks >> 2) * (FA_ROWS * 128) + (ks & 3) * 32);
                     const uint64_t bdesc = sdesc_mn_sw128(vb + ks * 2048, FA_KB * 128);
-                    mma_f16(tmem + 256, a, bdesc, C::IDESC_O, (i > 0 || ks > 0) ? 1u : 0u);   // O stays in TMEM
+                    mma_f16_ts(tmem + 256, p_tmem + 8u * ks, bdesc, C::IDESC_O, (i > 0 || ks > 0) ? 1u : 0u);
                 }
-                mma_commit(o_full);
+                mma_commit(pv_done(i & 1));
                 mma_commit(v_empty(s));
                 return true;
             };
@@ -323,14 +346,16 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
             if (!mbar_drain(drain, 0)) atomicCAS(args.err, 0, ERR_WAIT_DRAIN);
         }
     } else {
-        // ---------------- softmax / output: 8 warps, two threads per query row ----------------
-        // Warps w and w+4 share TMEM lane quarter (w & 3); thread (row r, half hf) owns keys
-        // [64*hf, 64*hf + 64) of every block and O columns [hf*DV/2, (hf+1)*DV/2). Scores are kept
+        // ---------------- softmax / output: FA_SPLIT threads per query row ----------------
+        // Warps w, w+4, ... share TMEM lane quarter (w & 3); thread (row r, part pt) owns keys
+        // [KPT*pt, KPT*(pt+1)) of every block and O columns [OPT*pt, OPT*(pt+1)). Scores are kept
         // in log2 units. O accumulates in TMEM across blocks (P.V MMAs with accumulate); it is
         // rescaled only when a row's max grows by more than 2^FA_RESCALE_LOG2 over the max the
-        // exponentials were taken against (which keeps P <= 2^8 and the sums exact up to rounding).
+        // exponentials were taken against (so P <= 2^8 and nothing overflows).
+        constexpr int KPT = FA_KB / FA_SPLIT;            // keys per thread per block
+        constexpr int OPT = DV / FA_SPLIT;               // O columns per thread
         const int quad = warp & 3;
-        const int hf = (warp - 2) >> 2;
+        const int pt = (warp - 2) >> 2;
         const int r = quad * 32 + lane;
         const int g = r / args.TQ, tq = r % args.TQ;
         const int h = hg * args.GP + g;
@@ -342,23 +367,30 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
         const float c2 = qs * LOG2E;                     // raw score -> log2 units
         const float softcap = args.softcap;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-        const uint32_t o_tmem = tmem + lane_base + 256u + (uint32_t)(hf * (DV / 2));
+        const uint32_t o_tmem = tmem + lane_base + 256u + (uint32_t)(pt * OPT);
         volatile float* xv = reinterpret_cast<volatile float*>(smem + C::OFF_XCH);
-        volatile int* xs = reinterpret_cast<volatile int*>(smem + C::OFF_XCH + 2048);
-        volatile float* xl = reinterpret_cast<volatile float*>(smem + C::OFF_XCH + 4096);
-        volatile int* xls = reinterpret_cast<volatile int*>(smem + C::OFF_XCH + 5120);
-        const uint32_t pchunk = sb + C::OFF_P + (uint32_t)hf * (FA_ROWS * 128);
-        // Hand a value to the other thread of this row and take its value: a bounded spin on a
-        // sequence number in shared memory (the two threads are in different warps).
-        auto exchange = [&](volatile float* v, volatile int* sq, float mine, int seq, float& theirs) -> bool {
-            v[hf * 128 + r] = mine;
+        volatile int* xs = reinterpret_cast<volatile int*>(smem + C::OFF_XCH + C::XCH_MAX);
+        volatile float* xl = reinterpret_cast<volatile float*>(smem + C::OFF_XCH + 2 * C::XCH_MAX);
+        volatile int* xls = reinterpret_cast<volatile int*>(smem + C::OFF_XCH + 2 * C::XCH_MAX + C::XCH_SUM);
+        // this thread's keys of a block are P columns [KPT/2*pt, KPT/2*(pt+1)) of the P buffer
+        const uint32_t p_lane = tmem + lane_base + C::P_TMEM0 + (uint32_t)(pt * (KPT / 2));
+        // wait until the P.V MMA of block k has completed (pv_done[k & 1], completion k >> 1)
+        auto wait_pv = [&](int k) {
+            return mbar_wait(pv_done(k & 1), (uint32_t)(k >> 1) & 1u, args.err, ERR_WAIT_EPILOGUE, abort_flag);
+        };
+        // Publish a value to the other threads of this row and wait for theirs: a bounded spin on
+        // sequence numbers in shared memory (the threads are in different warps). vals[k] gets
+        // part k's value.
+        auto exchange = [&](volatile float* v, volatile int* sq, float mine, int seq, float (&vals)[FA_SPLIT]) -> bool {
+            v[pt * 128 + r] = mine;
             __threadfence_block();
-            sq[hf * 128 + r] = seq;
-            const int other = (hf ^ 1) * 128 + r;
-            if (sq[other] != seq) {
-                const uint64_t t0 = globaltimer();
-                for (uint32_t n = 1; sq[other] != seq; ++n) {
-                    if ((n & 255u) == 0) {
+            sq[pt * 128 + r] = seq;
+            const uint64_t t0 = globaltimer();
+            uint32_t n = 0;
+#pragma unroll
+            for (int k = 0; k < FA_SPLIT; k++) {
+                while (sq[k * 128 + r] != seq) {
+                    if ((++n & 255u) == 0) {
                         if (*abort_flag) return false;
                         if (globaltimer() - t0 > B200_WAIT_LIMIT_NS) {
                             atomicCAS(args.err, 0, ERR_WAIT_EPILOGUE);
@@ -369,7 +401,8 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
                 }
             }
             __threadfence_block();
-            theirs = v[other];
+#pragma unroll
+            for (int k = 0; k < FA_SPLIT; k++) vals[k] = v[k * 128 + r];
             return true;
         };
         float m = -INFINITY;                             // running max (log2 units)
@@ -385,38 +418,33 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
             const uint32_t ph = (uint32_t)(i >> 1) & 1u;
             if (!mbar_wait(s_full(s), ph, args.err, ERR_WAIT_EPILOGUE, abort_flag)) { ok = false; break; }
             tc_fence_after();
-            float x[64];
-            {
-                const uint32_t sbase = tmem + lane_base + (uint32_t)(s * FA_KB + hf * 64);
-                uint32_t rv[32], rv2[32];
-                tmem_ld32(sbase, rv);
-                tmem_ld32(sbase + 32u, rv2);
+            float x[KPT];
+#pragma unroll
+            for (int c0 = 0; c0 < KPT; c0 += 32) {
+                uint32_t rv[32];
+                tmem_ld32(tmem + lane_base + (uint32_t)(s * FA_KB + pt * KPT + c0), rv);
                 tmem_ld_wait();
 #pragma unroll
-                for (int e = 0; e < 32; e++) {
-                    x[e] = __uint_as_float(rv[e]);
-                    x[32 + e] = __uint_as_float(rv2[e]);
-                }
+                for (int e = 0; e < 32; e++) x[c0 + e] = __uint_as_float(rv[e]);
             }
             // S is in registers: the buffer may take the next Q.K^T
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(s_empty(s));
-            const int k0 = j * FA_KB + hf * 64;
+            const int k0 = j * FA_KB + pt * KPT;
             float bmax = -INFINITY;
             if (!general) {
 #pragma unroll
-                for (int e = 0; e < 64; e++) bmax = fmaxf(bmax, x[e]);
+                for (int e = 0; e < KPT; e++) bmax = fmaxf(bmax, x[e]);
                 bmax *= c2;
             } else {
 #pragma unroll
-                for (int c0 = 0; c0 < 64; c0 += 32) {
+                for (int c0 = 0; c0 < KPT; c0 += 32) {
                     uint4 mv[4];
                     if (use_mask) load_mask32(mrow, k0 + c0, args.KV, args.mask_vec, mv);
 #pragma unroll
                     for (int e = 0; e < 32; e++) {
-                        const int ee = c0 + e;
-                        float sv = x[ee] * qs;
+                        float sv = x[c0 + e] * qs;
                         if (softcap != 0.0f) sv = softcap * tanhf(sv / softcap);
                         sv *= LOG2E;
                         if (use_mask) {
@@ -424,32 +452,36 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
                             const uint16_t mb = (uint16_t)((e & 1) ? (mw >> 16) : (mw & 0xFFFFu));
                             sv = fmaf(__half2float(__ushort_as_half(mb)), LOG2E, sv);
                         }
-                        if (k0 + ee >= args.KV) sv = -INFINITY;
-                        x[ee] = sv;
+                        if (k0 + c0 + e >= args.KV) sv = -INFINITY;
+                        x[c0 + e] = sv;
                         bmax = fmaxf(bmax, sv);
                     }
                 }
             }
-            // the row max over both halves (double-buffered by block parity)
-            float other_max;
-            if (!exchange(xv + (i & 1) * 256, xs + (i & 1) * 256, bmax, i + 1, other_max)) { ok = false; break; }
-            bmax = fmaxf(bmax, other_max);
+            // the row max over all parts (double-buffered by block parity)
+            float maxes[FA_SPLIT];
+            if (!exchange(xv + (i & 1) * (FA_SPLIT * 128), xs + (i & 1) * (FA_SPLIT * 128), bmax, i + 1, maxes)) {
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int k = 0; k < FA_SPLIT; k++) bmax = fmaxf(bmax, maxes[k]);
             const bool grow = bmax > m + FA_RESCALE_LOG2;
             const float m_new = grow ? bmax : m;
             const float alpha = (grow && m != -INFINITY) ? ex2_approx(m - m_new) : 1.0f;
-            // P.V of the previous block must be done before P is overwritten and O rescaled
-            if (i > 0) {
-                if (!mbar_wait(o_full, (uint32_t)(i - 1) & 1u, args.err, ERR_WAIT_EPILOGUE, abort_flag)) { ok = false; break; }
+            // O is rescaled in place only after the previous block's P.V has landed in it
+            if (i > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+                if (!wait_pv(i - 1)) { ok = false; break; }
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+                {
 #pragma unroll
-                    for (int c0 = 0; c0 < DV / 2; c0 += 32) {
-                        uint32_t ov[32];
-                        tmem_ld32(o_tmem + (uint32_t)c0, ov);
+                    for (int c0 = 0; c0 < OPT; c0 += 16) {
+                        uint32_t ov[16];
+                        tmem_ld16(o_tmem + (uint32_t)c0, ov);
                         tmem_ld_wait();
 #pragma unroll
-                        for (int e = 0; e < 32; e++) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-                        tmem_st32(o_tmem + (uint32_t)c0, ov);
+                        for (int e = 0; e < 16; e++) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+                        tmem_st16(o_tmem + (uint32_t)c0, ov);
                     }
                     tmem_st_wait();
                 }
@@ -457,10 +489,10 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
             l *= alpha;
             m = m_new;
             const float mu = (m == -INFINITY) ? 0.0f : m;
-            uint32_t pw[32];
+            uint32_t pw[KPT / 2];
             if (!general) {
 #pragma unroll
-                for (int e = 0; e < 64; e += 2) {
+                for (int e = 0; e < KPT; e += 2) {
                     const float p0 = ex2_approx(fmaf(x[e], c2, -mu));
                     const float p1 = ex2_approx(fmaf(x[e + 1], c2, -mu));
                     l += p0 + p1;
@@ -468,44 +500,47 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
                 }
             } else {
 #pragma unroll
-                for (int e = 0; e < 64; e += 2) {
+                for (int e = 0; e < KPT; e += 2) {
                     const float p0 = ex2_approx(x[e] - mu);
                     const float p1 = ex2_approx(x[e + 1] - mu);
                     l += p0 + p1;
                     pw[e >> 1] = pack_half2(p0, p1);
                 }
             }
-            // keys 64*hf .. +63 of this row -> P chunk hf (128-byte swizzled, K-major)
-#pragma unroll
-            for (int u = 0; u < 8; u++)
-                st_shared_v4(pchunk + sw128_offset((uint32_t)r, (uint32_t)u), pw[4 * u], pw[4 * u + 1], pw[4 * u + 2],
-                             pw[4 * u + 3]);
+            // P buffer (i & 1) is free once the P.V of block i-2 has completed
+            if (i >= 2) {
+                if (!wait_pv(i - 2)) { ok = false; break; }
+                tc_fence_after();
+            }
+            tmem_st_p<KPT / 2>(p_lane + (uint32_t)(64 * (i & 1)), pw);
+            tmem_st_wait();
             tc_fence_before();
-            fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(p_full(i & 1));
             i++;
         }
         bool have_o = false;
         if (ok && i > 0) {
-            have_o = mbar_wait(o_full, (uint32_t)(i - 1) & 1u, args.err, ERR_WAIT_EPILOGUE, abort_flag);
+            have_o = wait_pv(i - 1);
             tc_fence_after();
         }
-        // row sum over both halves, added in a fixed order so both threads agree
-        float l_other = 0.0f;
-        if (ok && !exchange(xl, xls, l, 1, l_other)) ok = false;
-        const float l_tot = hf == 0 ? l + l_other : l_other + l;
+        // row sum over all parts, added in part order so every thread of the row agrees
+        float sums[FA_SPLIT];
+        if (ok && !exchange(xl, xls, l, 1, sums)) ok = false;
+        float l_tot = 0.0f;
+#pragma unroll
+        for (int k = 0; k < FA_SPLIT; k++) l_tot += sums[k];
         if (ok && have_o) {
             const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
-            float* out = args.dst + ((int64_t)t * args.H + h) * DV + hf * (DV / 2);
+            float* out = args.dst + ((int64_t)t * args.H + h) * DV + pt * OPT;
 #pragma unroll
-            for (int c0 = 0; c0 < DV / 2; c0 += 32) {
-                uint32_t ov[32];
-                tmem_ld32(o_tmem + (uint32_t)c0, ov);
+            for (int c0 = 0; c0 < OPT; c0 += 16) {
+                uint32_t ov[16];
+                tmem_ld16(o_tmem + (uint32_t)c0, ov);
                 tmem_ld_wait();
                 if (row_valid) {
 #pragma unroll
-                    for (int e = 0; e < 32; e += 4)
+                    for (int e = 0; e < 16; e += 4)
                         *reinterpret_cast<float4*>(out + c0 + e) =
                             make_float4(__uint_as_float(ov[e]) * inv, __uint_as_float(ov[e + 1]) * inv,
                                         __uint_as_float(ov[e + 2]) * inv, __uint_as_float(ov[e + 3]) * inv);
@@ -513,8 +548,8 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
             }
         } else if (ok && row_valid) {
             // no key block survived the mask: the row is all zeros
-            float* out = args.dst + ((int64_t)t * args.H + h) * DV + hf * (DV / 2);
-            for (int c = 0; c < DV / 2; c += 4) *reinterpret_cast<float4*>(out + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+            float* out = args.dst + ((int64_t)t * args.H + h) * DV + pt * OPT;
+            for (int c = 0; c < OPT; c += 4) *reinterpret_cast<float4*>(out + c) = make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
 
