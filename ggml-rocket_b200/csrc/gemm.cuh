@@ -114,10 +114,12 @@ __device__ __forceinline__ int dequant_slot(int warp) {
     }
 }
 
-template <int BT, int WT>
+template <int BT, int WT, bool PAIR = false>
 struct GemmCfg {
     static constexpr bool QUANT = (WT != WT_F16);
-    static constexpr int A_BYTES = BT * GEMM_BK * 2;
+    // A CTA pair splits the token tile: each CTA stages BT/2 activation rows.
+    static constexpr int A_ROWS = PAIR ? BT / 2 : BT;
+    static constexpr int A_BYTES = A_ROWS * GEMM_BK * 2;
     static constexpr int W_BYTES = GEMM_BN * GEMM_BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + W_BYTES;
     static constexpr int RAW_TOTAL = RawCfg<WT>::STAGE * RawCfg<WT>::STAGES;
@@ -132,15 +134,17 @@ struct GemmCfg {
     static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
     static constexpr int SMEM = BAR_OFF + BAR_BYTES + 1024;
     static constexpr uint32_t TMEM_COLS = 2 * BT;
-    static constexpr uint32_t IDESC = idesc_f16_f32(GEMM_BN, BT);
+    static constexpr uint32_t IDESC = idesc_f16_f32(PAIR ? 2 * GEMM_BN : GEMM_BN, BT);
+    static constexpr int TILE_N = PAIR ? 2 * GEMM_BN : GEMM_BN;   // weight rows per work tile
     static_assert(STAGES >= 2, "pipeline too shallow");
 };
 
-template <int BT, int WT, bool GROUPED>
-__global__ void __launch_bounds__(GemmCfg<BT, WT>::THREADS, 1)
+template <int BT, int WT, bool GROUPED, bool PAIR>
+__global__ void __launch_bounds__(GemmCfg<BT, WT, PAIR>::THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
             const __grid_constant__ CUtensorMap tmD, const GemmArgs args) {
-    using C = GemmCfg<BT, WT>;
+    static_assert(!(GROUPED && PAIR), "the grouped GEMM runs one CTA per tile");
+    using C = GemmCfg<BT, WT, PAIR>;
     using RC = RawCfg<WT>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -161,15 +165,27 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // CTA pair (2-SM MMA): the even CTA (leader) issues the MMAs and owns the full / tempty
+    // barriers both CTAs feed; the MMA commits arrive in both CTAs.
+    const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+    const bool leader = crank == 0;
+    const int unit_id = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int n_units_grid = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    auto leader_addr = [&](uint32_t a) { return PAIR ? mapa_shared(a, 0) : a; };
+    // arrive on the leader's copy of a barrier (a local arrive in the leader itself)
+    auto arrive_leader = [&](uint32_t a) {
+        if (!PAIR || leader) mbar_arrive(a);
+        else mbar_arrive_cluster(mapa_shared(a, 0));
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            mbar_init(full_bar(s), C::QUANT ? 1 + DEQ_WARPS : 2);
+            mbar_init(full_bar(s), C::QUANT ? 1 + (PAIR ? 2 : 1) * DEQ_WARPS : 2);
             mbar_init(empty_bar(s), 1);
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(tfull_bar(a), 1);
-            mbar_init(tempty_bar(a), 4);
+            mbar_init(tempty_bar(a), PAIR ? 8 : 4);
         }
         for (int s = 0; s < RC::STAGES; s++) {
             mbar_init(rfull_bar(s), 1);
@@ -183,13 +199,24 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         if (WT == WT_Q6_K) tma_prefetch_desc(&tmD);
     }
     if (warp == W_MMA) {
-        tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(smem_u32(tmem_slot), C::TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync();   // the peer's barriers exist before anything arrives on them
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Everything above overlapped the previous kernel of the stream (programmatic launch); from
+    // here on this grid reads and writes global memory, so it waits for that kernel to finish,
+    // then lets the next kernel begin its own launch.
+    grid_dep_wait();
+    grid_dep_launch();
 
     const int ntt = args.n_tiles_t, ntn = args.n_tiles_n;
     // Work cursor: the grouped mode walks units blockIdx.x, +gridDim.x, ...; stream-K walks this
@@ -200,8 +227,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     if constexpr (GROUPED) {
         num_units = (int64_t)__ldg(args.g_tile_start + args.n_expert) * ntn;
     } else {
-        g_beg = (int64_t)blockIdx.x * args.total_g / gridDim.x;
-        g_end = (int64_t)(blockIdx.x + 1) * args.total_g / gridDim.x;
+        g_beg = (int64_t)unit_id * args.total_g / n_units_grid;
+        g_end = (int64_t)(unit_id + 1) * args.total_g / n_units_grid;
     }
     const int64_t cursor0 = GROUPED ? (int64_t)blockIdx.x : g_end;
     auto cursor_ok = [&](int64_t c) { return GROUPED ? c < num_units : c > g_beg; };
@@ -224,7 +251,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             c.kb0 = 0;
             c.kb1 = args.nkb;
             c.finishes = true;
-            c.c_first = blockIdx.x;
+            c.c_first = unit_id;
             c.next = cur + gridDim.x;
         } else {
             const int64_t tile = (cur - 1) / args.tile_g;
@@ -234,13 +261,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             const int nt = (int)(tile / ntt);
             c.t0 = tt * BT;
             c.t_end = args.M;
-            c.n0 = nt * GEMM_BN;
+            c.n0 = nt * C::TILE_N + (int)crank * GEMM_BN;   // this CTA's 128 weight rows
             c.wrow0 = c.n0;
             c.kb0 = (int)(s0 - tstart) * args.gran;
             c.kb1 = min(args.nkb, (int)(cur - tstart) * args.gran);
             c.finishes = cur - tstart == args.tile_g;
             // the CTA whose range holds granule tstart: largest c with c*total/grid <= tstart
-            c.c_first = (int)(((tstart + 1) * (int64_t)gridDim.x - 1) / args.total_g);
+            c.c_first = (int)(((tstart + 1) * (int64_t)n_units_grid - 1) / args.total_g);
             c.next = s0;
         }
         return c;
@@ -259,7 +286,17 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             for (int kb = uc.kb0; kb < uc.kb1; kb++) {
                 if (!mbar_wait(empty_bar(stage), phase ^ 1u, args.err, ERR_WAIT_PRODUCER, abort_flag)) { ok = false; break; }
                 const uint32_t sa = sbase + stage * C::STAGE_BYTES;
-                if (is_w) {
+                if constexpr (PAIR) {
+                    // both CTAs' tiles complete on the leader's barrier; the leader expects both
+                    const uint32_t fb = leader_addr(full_bar(stage));
+                    if (is_w) {
+                        if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * C::W_BYTES);
+                        tma_load_2d_pair(sa + C::A_BYTES, &tmW, fb, kb * GEMM_BK, uc.wrow0);
+                    } else {
+                        if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * C::A_BYTES);
+                        tma_load_2d_pair(sa, &tmA, fb, kb * GEMM_BK, uc.t0 + (int)crank * C::A_ROWS);
+                    }
+                } else if (is_w) {
                     mbar_arrive_expect_tx(full_bar(stage), C::W_BYTES);
                     tma_load_2d(sa + C::A_BYTES, &tmW, full_bar(stage), kb * GEMM_BK, uc.wrow0);
                 } else {
@@ -272,7 +309,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             }
         }
         (void)issued;
-        if (!ok) {   // let every copy already issued land before the CTA exits
+        if (!ok && (!PAIR || leader)) {   // let every copy already issued land before the CTA exits
             for (int s = 0; s < STAGES; s++)
                 if (((issued_mask >> s) & 1u) && !mbar_drain(full_bar(s), (issued_par >> s) & 1u))
                     atomicCAS(args.err, 0, ERR_WAIT_DRAIN);
@@ -317,8 +354,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             }
         }
     } else if (warp == W_MMA) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
+        // ---------------- MMA issuer (the leader's, for a pair) ----------------
+        if (lane == 0 && (!PAIR || leader)) {
             int stage = 0;
             uint32_t phase = 0;
             int lt = 0;
@@ -332,25 +369,33 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                 const int kb0 = uc.kb0, kb1 = uc.kb1;
                 const int acc = lt & 1;
                 const uint32_t aphase = (uint32_t)(lt >> 1) & 1u;
-                if (!mbar_wait(tempty_bar(acc), aphase ^ 1u, args.err, ERR_WAIT_MMA, abort_flag)) { ok = false; break; }
+                if (!mbar_wait<PAIR>(tempty_bar(acc), aphase ^ 1u, args.err, ERR_WAIT_MMA, abort_flag)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BT);
                 for (int kb = kb0; kb < kb1; kb++) {
-                    if (!mbar_wait(full_bar(stage), phase, args.err, ERR_WAIT_MMA, abort_flag)) { ok = false; break; }
+                    if (!mbar_wait<PAIR>(full_bar(stage), phase, args.err, ERR_WAIT_MMA, abort_flag)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t soff = (uint64_t)((stage * C::STAGE_BYTES) >> 4);
 #pragma unroll
-                    for (int k = 0; k < GEMM_BK / 16; k++)
-                        mma_f16(d_tmem, wdesc0 + soff + 2 * k, adesc0 + soff + 2 * k, C::IDESC,
-                                (kb > kb0 || k > 0) ? 1u : 0u);
-                    mma_commit(empty_bar(stage));
+                    for (int k = 0; k < GEMM_BK / 16; k++) {
+                        if constexpr (PAIR)
+                            mma_f16_pair(d_tmem, wdesc0 + soff + 2 * k, adesc0 + soff + 2 * k, C::IDESC,
+                                         (kb > kb0 || k > 0) ? 1u : 0u);
+                        else
+                            mma_f16(d_tmem, wdesc0 + soff + 2 * k, adesc0 + soff + 2 * k, C::IDESC,
+                                    (kb > kb0 || k > 0) ? 1u : 0u);
+                    }
+                    if constexpr (PAIR) mma_commit_pair(empty_bar(stage));
+                    else mma_commit(empty_bar(stage));
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
                 if (!ok) break;
-                mma_commit(tfull_bar(acc));
+                if constexpr (PAIR) mma_commit_pair(tfull_bar(acc));
+                else mma_commit(tfull_bar(acc));
             }
             // Every MMA this thread issued has completed once drain_bar fires.
-            mma_commit(drain_bar);
+            if constexpr (PAIR) mma_commit_pair(drain_bar);
+            else mma_commit(drain_bar);
             if (!mbar_drain(drain_bar, 0)) atomicCAS(args.err, 0, ERR_WAIT_DRAIN);
         }
     } else if (warp >= W_EPI0 && warp < W_EPI0 + 4) {
@@ -369,23 +414,26 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             const int ntok = min(BT, uc.t_end - uc.t0);  // tokens of this tile
             bool with_part = false;
             if constexpr (!GROUPED) {
-                if (uc.finishes && uc.c_first < (int)blockIdx.x) {
+                if (uc.finishes && uc.c_first < unit_id) {
                     // A finisher sums the partials of the lower-numbered CTAs sharing its tile
                     // (they computed them first) into the idle accumulator while its own K range
                     // is still on the tensor core; this is always the CTA's last item, so the MMA
                     // issuer no longer uses that accumulator.
                     bool ok = true;
-                    for (int c = uc.c_first; c < (int)blockIdx.x && ok; c++)
-                        ok = wait_flag(args.flags + 4 * c + q, args.epoch, args.err, abort_flag);
+                    // partial slot of work unit c for this CTA's rows: 2c + rank for a pair
+                    for (int c = uc.c_first; c < unit_id && ok; c++)
+                        ok = wait_flag(args.flags + 4 * (PAIR ? 2 * c + (int)crank : c) + q, args.epoch, args.err,
+                                       abort_flag);
                     if (!ok) break;
                     for (int c0 = 0; c0 < ntok; c0 += 32) {
-                        const float* p = args.partials + (size_t)uc.c_first * (BT * GEMM_BN) +
+                        const int slot0 = PAIR ? 2 * uc.c_first + (int)crank : uc.c_first;
+                        const float* p = args.partials + (size_t)slot0 * (BT * GEMM_BN) +
                                          (size_t)c0 * GEMM_BN + 32 * q + lane;
                         float sum[32];
 #pragma unroll
                         for (int j = 0; j < 32; j++) sum[j] = __ldcg(p + j * GEMM_BN);
-                        for (int c = uc.c_first + 1; c < (int)blockIdx.x; c++) {
-                            p += BT * GEMM_BN;
+                        for (int c = uc.c_first + 1; c < unit_id; c++) {
+                            p += (PAIR ? 2 : 1) * BT * GEMM_BN;
 #pragma unroll
                             for (int j = 0; j < 32; j++) sum[j] += __ldcg(p + j * GEMM_BN);
                         }
@@ -457,7 +505,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(tempty_bar(acc));
+            if (lane == 0) arrive_leader(tempty_bar(acc));
         }
     } else if (C::QUANT && dequant_slot(warp) >= 0) {
         // ---------------- dequant (quantized weights) ----------------
@@ -491,7 +539,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                                          o[4 * c + 2], o[4 * c + 3]);
                         fence_proxy_async_smem();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(full_bar(stage));
+                        if (lane == 0) arrive_leader(full_bar(stage));
                         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                     }
                     __syncwarp();
@@ -503,10 +551,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
 
     tc_fence_before();
-    __syncthreads();
+    // a pair: neither CTA leaves while the leader's MMAs may still read the peer's shared memory
+    // or write its TMEM (the leader's MMA thread passes here only after its drain)
+    if constexpr (PAIR) cluster_sync();
+    else __syncthreads();
     if (warp == W_MMA) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, C::TMEM_COLS);
+        if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+        else tmem_dealloc(tmem_base, C::TMEM_COLS);
     }
 }
 

@@ -5,7 +5,9 @@
 #include <cstdio>
 #include <cstring>
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
+#include <utility>
 
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -31,6 +33,8 @@ template <int V>
 __global__ void __launch_bounds__(ACT_THREADS) act_pack_kernel(const float* __restrict__ A, int64_t lda, int K,
                                                                __half* __restrict__ A16, float* __restrict__ scales) {
     __shared__ float red[ACT_THREADS / 32];
+    grid_dep_wait();     // the previous kernel may still read A16 / write A (programmatic launch)
+    grid_dep_launch();
     const int m = blockIdx.x;
     const float4* row = reinterpret_cast<const float4*>(A + (size_t)m * lda);
     uint2* out = reinterpret_cast<uint2*>(A16 + (size_t)m * K);
@@ -69,6 +73,8 @@ __global__ void __launch_bounds__(ACT_THREADS) act_pack_kernel(const float* __re
 __global__ void __launch_bounds__(ACT_THREADS) act_pack_loop_kernel(const float* __restrict__ A, int64_t lda, int K,
                                                                     __half* __restrict__ A16, float* __restrict__ scales) {
     __shared__ float red[ACT_THREADS / 32];
+    grid_dep_wait();
+    grid_dep_launch();
     const int m = blockIdx.x;
     const float* row = A + (size_t)m * lda;
     __half* out = A16 + (size_t)m * K;
@@ -86,18 +92,36 @@ __global__ void __launch_bounds__(ACT_THREADS) act_pack_loop_kernel(const float*
     for (int i = threadIdx.x; i < K; i += ACT_THREADS) out[i] = __float2half_rn(__fmul_rn(__ldg(row + i), inv));
 }
 
+// Launch with programmatic stream serialization: the kernel may be scheduled while the previous
+// kernel of the stream drains (its prologue overlaps that tail; it waits with grid_dep_wait()).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 static cudaError_t launch_act_pack(const float* A, int64_t lda, int64_t M, int64_t K, __half* a16, float* scales,
                                    cudaStream_t st) {
     const bool vec = ((reinterpret_cast<uintptr_t>(A) & 15u) == 0) && (lda % 4 == 0) && (K % 4 == 0);
     const int64_t per = (K / 4 + ACT_THREADS - 1) / ACT_THREADS;   // float4 per thread
-    const dim3 grid((unsigned)M);
-    if (!vec || per > 16) act_pack_loop_kernel<<<grid, ACT_THREADS, 0, st>>>(A, lda, (int)K, a16, scales);
-    else if (per <= 1) act_pack_kernel<1><<<grid, ACT_THREADS, 0, st>>>(A, lda, (int)K, a16, scales);
-    else if (per <= 2) act_pack_kernel<2><<<grid, ACT_THREADS, 0, st>>>(A, lda, (int)K, a16, scales);
-    else if (per <= 4) act_pack_kernel<4><<<grid, ACT_THREADS, 0, st>>>(A, lda, (int)K, a16, scales);
-    else if (per <= 8) act_pack_kernel<8><<<grid, ACT_THREADS, 0, st>>>(A, lda, (int)K, a16, scales);
-    else act_pack_kernel<16><<<grid, ACT_THREADS, 0, st>>>(A, lda, (int)K, a16, scales);
-    return cudaGetLastError();
+    const dim3 grid((unsigned)M), block(ACT_THREADS);
+    const int k = (int)K;
+    if (!vec || per > 16) return launch_pdl(act_pack_loop_kernel, grid, block, 0, st, A, lda, k, a16, scales);
+    if (per <= 1) return launch_pdl(act_pack_kernel<1>, grid, block, 0, st, A, lda, k, a16, scales);
+    if (per <= 2) return launch_pdl(act_pack_kernel<2>, grid, block, 0, st, A, lda, k, a16, scales);
+    if (per <= 4) return launch_pdl(act_pack_kernel<4>, grid, block, 0, st, A, lda, k, a16, scales);
+    if (per <= 8) return launch_pdl(act_pack_kernel<8>, grid, block, 0, st, A, lda, k, a16, scales);
+    return launch_pdl(act_pack_kernel<16>, grid, block, 0, st, A, lda, k, a16, scales);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -230,8 +254,21 @@ static inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; 
 // The launch plan for one MUL_MAT: token tile and the stream-K granule split.
 struct GemmPlan {
     int bt, gran, tile_g, nkb, ntn, ntt, grid, pieces;
+    bool pair;                 // 2-SM MMA: CTA pairs over 256 weight rows (grid counts CTAs)
     int64_t tiles, total_g;
 };
+
+// CTA pairs (the 2-SM MMA) halve each SM's activation traffic. Measured on B200 they pay a few
+// per cent for F16 weights at large M and cost the quantized path (whose decoded-weight hand-off
+// then crosses the pair) a third of its speed, so by default only F16 with M >= 1024 uses them.
+// B200_GEMM_PAIR: unset = that rule, 0 = never, 1 = whenever the token tile allows.
+static int pair_knob() {
+    static const int v = [] {
+        const char* e = getenv("B200_GEMM_PAIR");
+        return (e && *e) ? atoi(e) : -1;
+    }();
+    return v;
+}
 
 // Choose the token tile from a cost model (SM clocks). Per 64-wide K block a tile costs the
 // slowest of the tensor core (128 x BT x 64 MACs at 4096 MAC/clk), the decode of 8192 quantized
@@ -241,41 +278,57 @@ struct GemmPlan {
 static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms, int wtype) {
     const bool quant = wtype != WT_F16;
     const int nkb = (int)((K + GEMM_BK - 1) / GEMM_BK);
-    const int ntn = (int)((N + GEMM_BN - 1) / GEMM_BN);
     const int gran = quant ? 4 : 1;
     const int tile_g = (nkb + gran - 1) / gran;
     GemmPlan best{};
     double best_t = 1e30;
     const int bts[4] = {32, 64, 128, 256};
-    for (int bi = 0; bi < 4; bi++) {
-        const int bt = bts[bi];
-        if (bi > 0 && bts[bi - 1] >= M) break;          // a smaller tile already covers M
-        const int ntt = (int)((M + bt - 1) / bt);
-        const int64_t tiles = (int64_t)ntn * ntt;
-        const int64_t total_g = tiles * tile_g;
-        const int grid = (int)(total_g < sms ? total_g : sms);
-        const double mma = bt < 64 ? 128.0 : 2.0 * bt;
-        const double decode = quant ? 400.0 : 0.0;
-        const double feed = (bt * 128.0 + (quant ? 4600.0 : 16384.0)) / 96.0;
-        const double per_kb = (mma > decode ? (mma > feed ? mma : feed) : (decode > feed ? decode : feed)) + 16.0;
-        const double items = 1.0 + (double)tiles / grid;
-        const bool shared = total_g % grid != 0 || tiles % grid != 0;
-        double t = (double)tiles * nkb * per_kb / grid + 800.0 * items;
-        if (shared) t += 16.0 * bt;
-        if (t < best_t * 0.97) {
-            best_t = t;
-            best.bt = bt;
-            best.gran = gran;
-            best.tile_g = tile_g;
-            best.nkb = nkb;
-            best.ntn = ntn;
-            best.ntt = ntt;
-            best.grid = grid;
-            best.tiles = tiles;
-            best.total_g = total_g;
-            const int64_t run = total_g / grid;           // shortest granule run of a CTA
-            best.pieces = (int)((tile_g - 1) / run + 2 < tile_g ? (tile_g - 1) / run + 2 : tile_g);
-            if (!shared) best.pieces = 1;
+    const bool pair_default = !quant && M >= 1024;
+    for (int pair = 0; pair < 2; pair++) {
+        if (pair && (pair_knob() == 0 || (pair_knob() < 0 && !pair_default))) continue;
+        if (!pair && (pair_knob() == 1 || (pair_knob() < 0 && pair_default)) && M > 64) continue;
+        const int tile_n = pair ? 2 * GEMM_BN : GEMM_BN;
+        const int ntn = (int)((N + tile_n - 1) / tile_n);
+        for (int bi = 0; bi < 4; bi++) {
+            const int bt = bts[bi];
+            if (bi > 0 && bts[bi - 1] >= M) break;      // a smaller tile already covers M
+            if (pair && bt < 128) continue;              // each CTA of a pair stages >= 64 tokens
+            const int ntt = (int)((M + bt - 1) / bt);
+            const int64_t tiles = (int64_t)ntn * ntt;
+            const int64_t total_g = tiles * tile_g;
+            const int per_unit = pair ? 2 : 1;           // CTAs per work unit
+            const int units = (int)(total_g < sms / per_unit ? total_g : sms / per_unit);
+            // per SM and 64-wide K block: tensor-core clocks (128 x BT x 64 MACs at 4096 MAC/clk),
+            // the decode of 8192 quantized weights, and shared-memory bytes (TMA writes + MMA
+            // reads, 128 B/clk): the activation tile is halved in a pair
+            const double mma = bt < 64 ? 128.0 : 2.0 * bt;
+            const double decode = quant ? 400.0 : 0.0;
+            const double a_bytes = (pair ? bt / 2 : bt) * 128.0 * 2.0;
+            const double w_bytes = quant ? 41984.0 : 32768.0;
+            const double feed = (a_bytes + w_bytes) / 128.0;
+            double per_kb = mma > decode ? mma : decode;
+            if (feed > per_kb) per_kb = feed;
+            per_kb += 16.0;
+            const double items = 1.0 + (double)tiles / units;
+            const bool shared = total_g % units != 0 || tiles % units != 0;
+            double t = (double)tiles * nkb * per_kb / units + 800.0 * items;
+            if (shared) t += 16.0 * bt;
+            if (t < best_t * 0.97) {
+                best_t = t;
+                best.bt = bt;
+                best.pair = pair != 0;
+                best.gran = gran;
+                best.tile_g = tile_g;
+                best.nkb = nkb;
+                best.ntn = ntn;
+                best.ntt = ntt;
+                best.grid = units * per_unit;
+                best.tiles = tiles;
+                best.total_g = total_g;
+                const int64_t run = total_g / units;      // shortest granule run of a unit
+                best.pieces = (int)((tile_g - 1) / run + 2 < tile_g ? (tile_g - 1) / run + 2 : tile_g);
+                if (!shared) best.pieces = 1;
+            }
         }
     }
     return best;
@@ -310,16 +363,16 @@ static MulMatWorkspace mm_workspace_layout(int64_t M, int64_t N, int64_t K, cons
     return w;
 }
 
-template <int BT, int WT, bool GROUPED>
+template <int BT, int WT, bool GROUPED, bool PAIR>
 static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmD,
                                  const GemmArgs& a, int grid, cudaStream_t st) {
-    using C = GemmCfg<BT, WT>;
+    using C = GemmCfg<BT, WT, PAIR>;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BT, WT, GROUPED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             C::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BT, WT, GROUPED, PAIR>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
@@ -328,23 +381,43 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW,
     cfg.blockDim = dim3(C::THREADS);
     cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = st;
-    // stream-K finishers wait on other CTAs of the grid: ask for a grid that is all resident
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
+    // Programmatic launch: the prologue (barriers, TMEM, descriptor prefetch) overlaps the tail of
+    // the previous kernel. Stream-K finishers only ever wait for lower-numbered CTAs, which are
+    // scheduled no later than themselves, so the grid needs no co-residency guarantee.
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    int na = 1;
+    if (PAIR) {
+        // CTA pairs: clusters of two (the 2-SM MMA's peers)
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 2;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        na = 2;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = GROUPED ? 0 : 1;
-    return cudaLaunchKernelEx(&cfg, gemm_kernel<BT, WT, GROUPED>, tmA, tmW, tmD, a);
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, gemm_kernel<BT, WT, GROUPED, PAIR>, tmA, tmW, tmD, a);
 }
 
 template <int WT, bool GROUPED>
-static cudaError_t launch_gemm_bt(int bt, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmD,
-                                  const GemmArgs& a, int grid, cudaStream_t st) {
+static cudaError_t launch_gemm_bt(int bt, bool pair, const CUtensorMap& tmA, const CUtensorMap& tmW,
+                                  const CUtensorMap& tmD, const GemmArgs& a, int grid, cudaStream_t st) {
+    if constexpr (!GROUPED) {
+        if (pair) {
+            switch (bt) {
+                case 128: return launch_gemm_t<128, WT, false, true>(tmA, tmW, tmD, a, grid, st);
+                case 256: return launch_gemm_t<256, WT, false, true>(tmA, tmW, tmD, a, grid, st);
+                default: return cudaErrorInvalidValue;
+            }
+        }
+    }
     switch (bt) {
-        case 32: return launch_gemm_t<32, WT, GROUPED>(tmA, tmW, tmD, a, grid, st);
-        case 64: return launch_gemm_t<64, WT, GROUPED>(tmA, tmW, tmD, a, grid, st);
-        case 128: return launch_gemm_t<128, WT, GROUPED>(tmA, tmW, tmD, a, grid, st);
-        default: return launch_gemm_t<256, WT, GROUPED>(tmA, tmW, tmD, a, grid, st);
+        case 32: return launch_gemm_t<32, WT, GROUPED, false>(tmA, tmW, tmD, a, grid, st);
+        case 64: return launch_gemm_t<64, WT, GROUPED, false>(tmA, tmW, tmD, a, grid, st);
+        case 128: return launch_gemm_t<128, WT, GROUPED, false>(tmA, tmW, tmD, a, grid, st);
+        default: return launch_gemm_t<256, WT, GROUPED, false>(tmA, tmW, tmD, a, grid, st);
     }
 }
 
@@ -379,13 +452,13 @@ static bool setup_weight_maps(int wtype, const void* w_packed, int64_t wrows, in
 }
 
 template <bool GROUPED>
-cudaError_t launch_gemm_typed(int wtype, int bt, const CUtensorMap& tmA, const CUtensorMap& tmW,
+cudaError_t launch_gemm_typed(int wtype, int bt, bool pair, const CUtensorMap& tmA, const CUtensorMap& tmW,
                               const CUtensorMap& tmD, const GemmArgs& a, int grid, cudaStream_t st) {
     switch (wtype) {
-        case WT_F16: return launch_gemm_bt<WT_F16, GROUPED>(bt, tmA, tmW, tmD, a, grid, st);
-        case WT_Q4_K: return launch_gemm_bt<WT_Q4_K, GROUPED>(bt, tmA, tmW, tmD, a, grid, st);
-        case WT_Q6_K: return launch_gemm_bt<WT_Q6_K, GROUPED>(bt, tmA, tmW, tmD, a, grid, st);
-        case WT_Q8_0: return launch_gemm_bt<WT_Q8_0, GROUPED>(bt, tmA, tmW, tmD, a, grid, st);
+        case WT_F16: return launch_gemm_bt<WT_F16, GROUPED>(bt, pair, tmA, tmW, tmD, a, grid, st);
+        case WT_Q4_K: return launch_gemm_bt<WT_Q4_K, GROUPED>(bt, pair, tmA, tmW, tmD, a, grid, st);
+        case WT_Q6_K: return launch_gemm_bt<WT_Q6_K, GROUPED>(bt, pair, tmA, tmW, tmD, a, grid, st);
+        case WT_Q8_0: return launch_gemm_bt<WT_Q8_0, GROUPED>(bt, pair, tmA, tmW, tmD, a, grid, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -422,7 +495,7 @@ int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int6
     const int64_t max_units = max_tiles * a.n_tiles_n;
     const int grid = (int)(max_units < sms ? max_units : sms);
     if (grid <= 0) return B200_OK;
-    return launch_gemm_typed<true>(wtype, bt, tmA, tmW, tmD, a, grid, st) == cudaSuccess ? B200_OK : B200_E_CUDA;
+    return launch_gemm_typed<true>(wtype, bt, false, tmA, tmW, tmD, a, grid, st) == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 
 size_t packed_weight_bytes(int type, int64_t N, int64_t K, size_t* plane_d_off) {
@@ -468,7 +541,8 @@ int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, cons
     if (sk_bytes && (!workspace || workspace_bytes < sk_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
         return B200_E_WORKSPACE;
     CUtensorMap tmA, tmW, tmD;
-    if (!make_tmap_2d_f16(&tmA, a16, (uint64_t)M, (uint64_t)K, (uint64_t)K, (uint32_t)p.bt, GEMM_BK))
+    // a CTA of a pair stages half of the token tile
+    if (!make_tmap_2d_f16(&tmA, a16, (uint64_t)M, (uint64_t)K, (uint64_t)K, (uint32_t)(p.pair ? p.bt / 2 : p.bt), GEMM_BK))
         return B200_E_CUDA;
     GemmArgs a{};
     if (!setup_weight_maps(wtype, w_packed, N, K, tmW, tmD, tmA)) return B200_E_CUDA;
@@ -489,7 +563,7 @@ int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, cons
     a.gran = p.gran;
     a.tile_g = p.tile_g;
     a.total_g = p.total_g;
-    const cudaError_t e = launch_gemm_typed<false>(wtype, p.bt, tmA, tmW, tmD, a, p.grid, st);
+    const cudaError_t e = launch_gemm_typed<false>(wtype, p.bt, p.pair, tmA, tmW, tmD, a, p.grid, st);
     return e == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 

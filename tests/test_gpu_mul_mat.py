@@ -172,3 +172,37 @@ def test_mul_mat_quant_equals_dequant_then_f16(cuda, K, N, M, wtype):
         assert np.array_equal(got_q.view(np.uint32), got_f.view(np.uint32))
     else:   # different tilings only reorder the fp32 sums
         assert rel_err(got_q, got_f) <= 1e-5
+
+
+_PAIR_CHILD = r"""
+import sys, numpy as np, torch
+sys.path[:0] = [sys.argv[1], sys.argv[1] + '/ggml-rocket_b200', sys.argv[1] + '/tests']
+import oracle
+from conftest import rel_err
+from test_gpu_mul_mat import run_mul_mat, _weights
+worst = 0.0
+for (K, N, M, wtype) in [(1024, 384, 256, 1), (3840, 256, 128, 12), (512, 512, 300, 14), (2048, 256, 256, 8),
+                         (4096, 128, 512, 12)]:
+    rng = np.random.default_rng(K + N + M + wtype)
+    w = _weights(rng, N, K, wtype)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    got = run_mul_mat(torch, wtype, w, N, K, a)
+    assert np.all(np.isfinite(got)), (K, N, M, wtype)
+    worst = max(worst, rel_err(got, oracle.mul_mat(wtype, w, N, K, a)))
+print("PAIR_WORST", worst)
+"""
+
+
+def test_mul_mat_cta_pairs_forced(cuda):
+    """The 2-SM (CTA pair) GEMM, forced on for every format with B200_GEMM_PAIR=1 in a child
+    process (the knob is read once per process), against the oracle."""
+    import os
+    import subprocess
+    import sys
+    from conftest import ROOT
+    env = dict(os.environ, B200_GEMM_PAIR="1")
+    p = subprocess.run([sys.executable, "-c", _PAIR_CHILD, ROOT], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
+    worst = float(p.stdout.split("PAIR_WORST")[1].split()[0])
+    assert worst <= TOL
