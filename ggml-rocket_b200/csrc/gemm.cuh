@@ -16,7 +16,7 @@
 //                 quantized super-block tile: 128 rows x 256 weights into a 2-3 deep ring,
 //                 with the TMA's L2 prefetch running 4 super-blocks further ahead
 //   (quantized weights only)
-//   8 dequant warps (7, 8, 10, 11, 12, 14, 15, 16 -- none shares a scheduler with warp 1):
+//   warps 7..14   dequant, two per scheduler:
 //                 thread (row r, half h) decodes 32 weights of row r's 64-weight chunk from
 //                 the ring to fp16 and writes them, 128-byte swizzled, straight into the
 //                 stage the MMA reads -- no fp16 weight copy in HBM.
@@ -97,21 +97,14 @@ struct RawCfg {
     static constexpr int X_ELEMS = ROW / 2;                              // uint16 box width
 };
 
-// Warp roles. The dequant warps never share a scheduler (warp % 4) with the MMA warp.
-constexpr int W_APROD = 0, W_MMA = 1, W_EPI0 = 2, W_WPROD = 6;
+// Warp roles: producers 0 and 6, MMA 1, epilogue 2-5, dequant 7-14. The eight dequant warps
+// sit two per scheduler (warp % 4), the MMA warp's included: the decode is ALU-heavy, and three
+// on one scheduler (beside an epilogue warp) made that scheduler the straggler every stage
+// waits for (measured: 5-10 % slower).
+constexpr int W_APROD = 0, W_MMA = 1, W_EPI0 = 2, W_WPROD = 6, W_DEQ0 = 7;
 constexpr int DEQ_WARPS = 8;
 __device__ __forceinline__ int dequant_slot(int warp) {
-    switch (warp) {
-        case 7: return 0;
-        case 8: return 1;
-        case 10: return 2;
-        case 11: return 3;
-        case 12: return 4;
-        case 14: return 5;
-        case 15: return 6;
-        case 16: return 7;
-        default: return -1;
-    }
+    return (warp >= W_DEQ0 && warp < W_DEQ0 + DEQ_WARPS) ? warp - W_DEQ0 : -1;
 }
 
 template <int BT, int WT, bool PAIR = false>
@@ -126,7 +119,7 @@ struct GemmCfg {
     static constexpr int EPI_BYTES = 4 * 32 * 32 * 4;          // a 32 x 32 f32 transpose tile per epilogue warp
     static constexpr int BUDGET = 232448 - 1024 - 256 - RAW_TOTAL - EPI_BYTES;
     static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
-    static constexpr int THREADS = QUANT ? 17 * 32 : 7 * 32;
+    static constexpr int THREADS = QUANT ? (W_DEQ0 + DEQ_WARPS) * 32 : 7 * 32;
     static constexpr int DEQ_THREADS = DEQ_WARPS * 32;
     static constexpr int BAR_BYTES = 256;
     static constexpr int RAW_OFF = STAGES * STAGE_BYTES;
@@ -527,11 +520,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     if constexpr (WT == WT_Q6_K) d6 = __half2float(reinterpret_cast<const __half*>(raw + RC::A_BYTES)[r]);
                     const int k_lo = max(uc.kb0, 4 * sb), k_hi = min(uc.kb1, 4 * sb + 4);
                     for (int kb = k_lo; kb < k_hi; kb++) {
-                        if (!mbar_wait(empty_bar(stage), phase ^ 1u, args.err, ERR_WAIT_DEQUANT, abort_flag)) { ok = false; break; }
+                        // decode first: the arithmetic overlaps the wait for the stage to free up
                         uint32_t o[16];
                         if constexpr (WT == WT_Q4_K) decode_q4k_half(rrow, kb & 3, h, o);
                         else if constexpr (WT == WT_Q6_K) decode_q6k_half(rrow, d6, kb & 3, h, o);
                         else decode_q8_0_half(rrow, kb & 3, h, o);
+                        if (!mbar_wait(empty_bar(stage), phase ^ 1u, args.err, ERR_WAIT_DEQUANT, abort_flag)) { ok = false; break; }
                         const uint32_t sw = sbase + stage * C::STAGE_BYTES + C::A_BYTES;
 #pragma unroll
                         for (int c = 0; c < 4; c++)
