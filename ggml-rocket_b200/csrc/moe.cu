@@ -19,35 +19,51 @@
 namespace b200 {
 
 constexpr int ROUTE_THREADS = 1024;
+constexpr int ROUTE_CHUNK = 1024;   // rows per CTA of the histogram / placement passes
 
-// One CTA. Dynamic shared memory: cnt[E], base[E], wcnt[32][E] (ints).
-__global__ void __launch_bounds__(ROUTE_THREADS) moe_route_kernel(const int32_t* __restrict__ ids, int64_t ids_nb0,
-                                                                 int64_t ids_nb1, int n_used, int n_tokens, int E,
-                                                                 int bt, int32_t* __restrict__ off,
-                                                                 int32_t* __restrict__ tile_start,
-                                                                 int32_t* __restrict__ slot, int32_t* __restrict__ tok,
-                                                                 int* err) {
-    extern __shared__ int sm[];
-    int* cnt = sm;
-    int* base = sm + E;
-    int* wcnt = sm + 2 * E;
-    const int R = n_used * n_tokens;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// The route is a stable counting sort over the token-major row order r = t * n_used + s, split
+// over CTAs that each own ROUTE_CHUNK consecutive rows:
+//   moe_hist_kernel    per-CTA histogram of the experts of its rows (and a bad-id flag)
+//   moe_scan_kernel    one CTA: per-expert offsets, the tile table, and every CTA's first
+//                      position per expert (CTA-major within an expert, which keeps the order)
+//   moe_place_kernel   per CTA: its rows in order, each to its expert's next position
+__device__ __forceinline__ int moe_id_at(const int32_t* ids, int64_t ids_nb0, int64_t ids_nb1, int n_used, int r) {
+    const int t = r / n_used, e = r % n_used;
+    return __ldg(reinterpret_cast<const int32_t*>(reinterpret_cast<const char*>(ids) + (int64_t)t * ids_nb1 +
+                                                  (int64_t)e * ids_nb0));
+}
+
+// Dynamic shared memory: cnt[E].
+__global__ void __launch_bounds__(ROUTE_THREADS) moe_hist_kernel(const int32_t* __restrict__ ids, int64_t ids_nb0,
+                                                                int64_t ids_nb1, int n_used, int R, int E,
+                                                                int32_t* __restrict__ counts, int32_t* __restrict__ bad) {
+    extern __shared__ int cnt[];
     for (int e = threadIdx.x; e < E; e += ROUTE_THREADS) cnt[e] = 0;
-    for (int i = threadIdx.x; i < 32 * E; i += ROUTE_THREADS) wcnt[i] = 0;
     __syncthreads();
-    auto id_at = [&](int r) {
-        const int t = r / n_used, e = r % n_used;
-        return __ldg(reinterpret_cast<const int32_t*>(reinterpret_cast<const char*>(ids) + (int64_t)t * ids_nb1 +
-                                                      (int64_t)e * ids_nb0));
-    };
-    int bad = 0;
-    for (int r = threadIdx.x; r < R; r += ROUTE_THREADS) {
-        const int x = id_at(r);
-        if (x < 0 || x >= E) bad = 1;
+    const int r0 = blockIdx.x * ROUTE_CHUNK, r1 = min(R, r0 + ROUTE_CHUNK);
+    int b = 0;
+    for (int r = r0 + threadIdx.x; r < r1; r += ROUTE_THREADS) {
+        const int x = moe_id_at(ids, ids_nb0, ids_nb1, n_used, r);
+        if (x < 0 || x >= E) b = 1;
         else atomicAdd(&cnt[x], 1);
     }
-    if (__syncthreads_or(bad)) {
+    b = __syncthreads_or(b);
+    for (int e = threadIdx.x; e < E; e += ROUTE_THREADS) counts[(int64_t)blockIdx.x * E + e] = cnt[e];
+    if (threadIdx.x == 0) bad[blockIdx.x] = b;
+}
+
+// One CTA. counts[nb][E] becomes each CTA's first position per expert (relative to the expert's
+// start); off / tile_start are exclusive scans over the experts. Dynamic shared memory: E ints.
+__global__ void __launch_bounds__(ROUTE_THREADS) moe_scan_kernel(int32_t* __restrict__ counts,
+                                                                const int32_t* __restrict__ bad, int nb, int E, int bt,
+                                                                int32_t* __restrict__ off,
+                                                                int32_t* __restrict__ tile_start, int* err) {
+    extern __shared__ int tot[];
+    __shared__ int wsum[2][32];
+    __shared__ int carry[2];
+    int any = 0;
+    for (int b = threadIdx.x; b < nb; b += ROUTE_THREADS) any |= __ldg(bad + b);
+    if (__syncthreads_or(any)) {
         if (threadIdx.x == 0) atomicCAS(err, 0, B200_DEV_BAD_IDS);
         for (int e = threadIdx.x; e <= E; e += ROUTE_THREADS) {
             off[e] = 0;
@@ -55,23 +71,92 @@ __global__ void __launch_bounds__(ROUTE_THREADS) moe_route_kernel(const int32_t*
         }
         return;
     }
-    if (threadIdx.x == 0) {
-        int acc = 0, tacc = 0;
-        for (int e = 0; e < E; e++) {
-            off[e] = acc;
-            base[e] = acc;
-            tile_start[e] = tacc;
-            acc += cnt[e];
-            tacc += (cnt[e] + bt - 1) / bt;
+    for (int e = threadIdx.x; e < E; e += ROUTE_THREADS) {
+        int acc = 0;
+        for (int b0 = 0; b0 < nb; b0 += 8) {       // eight independent loads per round trip
+            int c[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) c[k] = b0 + k < nb ? counts[(int64_t)(b0 + k) * E + e] : 0;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                if (b0 + k < nb) counts[(int64_t)(b0 + k) * E + e] = acc;
+                acc += c[k];
+            }
         }
-        off[E] = acc;
-        tile_start[E] = tacc;
+        tot[e] = acc;
     }
+    if (threadIdx.x < 2) carry[threadIdx.x] = 0;
     __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // exclusive scans of the row counts and of the tile counts, ROUTE_THREADS experts at a time
+    for (int e0 = 0; e0 < E; e0 += ROUTE_THREADS) {
+        const int e = e0 + threadIdx.x;
+        const int c = e < E ? tot[e] : 0;
+        int v[2] = {c, (c + bt - 1) / bt};
+        int incl[2];
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            int x = v[k];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
+            }
+            incl[k] = x;
+            if (lane == 31) wsum[k][warp] = x;
+        }
+        __syncthreads();
+        if (warp == 0) {
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+                int x = wsum[k][lane];
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, x, o);
+                    if (lane >= o) x += y;
+                }
+                wsum[k][lane] = x;
+            }
+        }
+        __syncthreads();
+        const int before0 = carry[0] + (warp > 0 ? wsum[0][warp - 1] : 0) + incl[0] - v[0];
+        const int before1 = carry[1] + (warp > 0 ? wsum[1][warp - 1] : 0) + incl[1] - v[1];
+        if (e < E) {
+            off[e] = before0;
+            tile_start[e] = before1;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            carry[0] += wsum[0][31];
+            carry[1] += wsum[1][31];
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        off[E] = carry[0];
+        tile_start[E] = carry[1];
+    }
+}
+
+// Dynamic shared memory: base[E], wcnt[32][E] (ints).
+__global__ void __launch_bounds__(ROUTE_THREADS) moe_place_kernel(const int32_t* __restrict__ ids, int64_t ids_nb0,
+                                                                 int64_t ids_nb1, int n_used, int R, int E,
+                                                                 const int32_t* __restrict__ counts,
+                                                                 const int32_t* __restrict__ off,
+                                                                 int32_t* __restrict__ slot, int32_t* __restrict__ tok) {
+    extern __shared__ int sm[];
+    int* base = sm;
+    int* wcnt = sm + E;
+    if (__ldg(off + E) != R) return;      // a bad-id op: the scan wrote an empty table
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int e = threadIdx.x; e < E; e += ROUTE_THREADS) base[e] = __ldg(off + e) + counts[(int64_t)blockIdx.x * E + e];
+    for (int i = threadIdx.x; i < 32 * E; i += ROUTE_THREADS) wcnt[i] = 0;
+    __syncthreads();
+    const int r0 = blockIdx.x * ROUTE_CHUNK, r1 = min(R, r0 + ROUTE_CHUNK);
     const unsigned lt_mask = (1u << lane) - 1u;
-    for (int r0 = 0; r0 < R; r0 += ROUTE_THREADS) {
-        const int r = r0 + threadIdx.x;
-        const int x = r < R ? id_at(r) : -1;
+    for (int rb = r0; rb < r1; rb += ROUTE_THREADS) {
+        const int r = rb + threadIdx.x;
+        const int x = r < r1 ? moe_id_at(ids, ids_nb0, ids_nb1, n_used, r) : -1;
         const unsigned same = __match_any_sync(0xffffffffu, x);
         const int rank = __popc(same & lt_mask);
         if (x >= 0 && rank == 0) wcnt[warp * E + x] = __popc(same);
@@ -161,7 +246,7 @@ int launch_gather_pack(const float* b, int64_t b_nb1, int64_t b_nb2, int64_t ne1
 }
 
 struct MoeLayout {
-    size_t off, tiles, slot, tok, a16, scales, total;
+    size_t off, tiles, slot, tok, a16, scales, counts, bad, total;
 };
 
 static MoeLayout moe_layout(int64_t K, int64_t n_expert, int64_t n_used, int64_t n_tokens) {
@@ -174,13 +259,18 @@ static MoeLayout moe_layout(int64_t K, int64_t n_expert, int64_t n_used, int64_t
     L.tok = L.slot + al(R * 4);
     L.a16 = L.tok + al(R * 4);
     L.scales = L.a16 + al(R * (size_t)K * 2);
-    L.total = L.scales + al(R * 4);
+    const size_t nb = (R + ROUTE_CHUNK - 1) / ROUTE_CHUNK;
+    L.counts = L.scales + al(R * 4);
+    L.bad = L.counts + al(nb * (size_t)n_expert * 4);
+    L.total = L.bad + al(nb * 4);
     return L;
 }
 
+// The grouped GEMM decodes an expert's weight tile once per token tile; at ~100+ rows per expert
+// one 256-token tile (tensor-core work on its padding is cheaper than a second decode) wins.
 static int moe_token_tile(int64_t R, int64_t n_expert) {
     const int64_t avg = n_expert > 0 ? R / n_expert : R;
-    return avg <= 32 ? 32 : avg <= 64 ? 64 : 128;
+    return avg <= 32 ? 32 : avg <= 64 ? 64 : avg < 96 ? 128 : 256;
 }
 
 int mul_mat_id_impl(int wtype, const void* as_packed, int64_t K, int64_t N, int64_t n_expert, const float* b,
@@ -205,16 +295,21 @@ int mul_mat_id_impl(int wtype, const void* as_packed, int64_t K, int64_t N, int6
     const int64_t R = n_used * n_tokens;
     const int bt = moe_token_tile(R, n_expert);
 
-    const size_t route_smem = (size_t)(2 + 32) * n_expert * sizeof(int);
-    if (route_smem > 48 * 1024) {
-        if (cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)route_smem) !=
+    int32_t* counts = reinterpret_cast<int32_t*>(ws + L.counts);
+    int32_t* bad = reinterpret_cast<int32_t*>(ws + L.bad);
+    const int nb = (int)((R + ROUTE_CHUNK - 1) / ROUTE_CHUNK);
+    const size_t hist_smem = (size_t)n_expert * sizeof(int);
+    const size_t place_smem = (size_t)33 * n_expert * sizeof(int);
+    if (place_smem > 48 * 1024 &&
+        cudaFuncSetAttribute(moe_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)place_smem) !=
             cudaSuccess)
-            return B200_E_UNSUPPORTED;
-    }
-    moe_route_kernel<<<1, ROUTE_THREADS, route_smem, st>>>(ids, ids_nb0, ids_nb1, (int)n_used, (int)n_tokens,
-                                                           (int)n_expert, bt, off, tiles, slot, tok, dev_err);
+        return B200_E_UNSUPPORTED;
+    moe_hist_kernel<<<nb, ROUTE_THREADS, hist_smem, st>>>(ids, ids_nb0, ids_nb1, (int)n_used, (int)R, (int)n_expert,
+                                                          counts, bad);
+    moe_scan_kernel<<<1, ROUTE_THREADS, hist_smem, st>>>(counts, bad, nb, (int)n_expert, bt, off, tiles, dev_err);
+    moe_place_kernel<<<nb, ROUTE_THREADS, place_smem, st>>>(ids, ids_nb0, ids_nb1, (int)n_used, (int)R,
+                                                            (int)n_expert, counts, off, slot, tok);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
-
     const int rc = launch_gather_pack(b, b_nb1, b_nb2, ne11, K, slot, tok, off + n_expert, R, a16, scales, st);
     if (rc != B200_OK) return rc;
 

@@ -64,6 +64,8 @@ def make_case(rng, wtype, K, N, n_expert, n_tokens, n_used, ne11, skew=False):
     (1, 256, 96, 8, 48, 2, 1, False),
     (12, 2048, 768, 32, 256, 8, 1, False),
     (12, 768, 2048, 32, 256, 8, 8, False),
+    (12, 512, 256, 8, 200, 4, 1, False),     # ~100 rows per expert: the 256-token tile
+    (14, 512, 128, 8, 300, 4, 4, True),
 ])
 def test_moe_matches_oracle(cuda, wtype, K, N, n_expert, n_tokens, n_used, ne11, skew):
     import torch
