@@ -31,9 +31,9 @@ constexpr int EP_THREADS = 1024;
 constexpr int EP_MAX_RANKS = 64;
 constexpr int EP_MAX_SLOTS = 32;   // slot masks are 32-bit
 
-// Exclusive scan of one int over the CTA (EP_THREADS threads); also returns the total.
+// Exclusive scan of one int over the CTA (any multiple of 32 threads); also returns the total.
 __device__ __forceinline__ int block_excl_scan(int v, int* total, int* sh /* [32] */) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     int x = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -43,7 +43,7 @@ __device__ __forceinline__ int block_excl_scan(int v, int* total, int* sh /* [32
     if (lane == 31) sh[warp] = x;
     __syncthreads();
     if (warp == 0) {
-        int w = sh[lane];
+        int w = lane < nw ? sh[lane] : 0;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const int y = __shfl_up_sync(0xffffffffu, w, o);
@@ -53,190 +53,290 @@ __device__ __forceinline__ int block_excl_scan(int v, int* total, int* sh /* [32
     }
     __syncthreads();
     const int before = (warp > 0 ? sh[warp - 1] : 0) + x - v;
-    *total = sh[31];
+    *total = sh[nw - 1];
     __syncthreads();                                    // sh is reused by the next call
     return before;
 }
 
+constexpr int EPC = 256;   // candidates / rows per CTA of the multi-CTA passes
+
 // Home side. Candidate c = t * ne11 + j is token t's b row j (serving slots s with s % ne11 == j).
 // For destination rank d its slot mask is {s : s % ne11 == j, ids[s, t] / E_loc == d}. Send rows
 // are ordered by destination, then token, then b row; their return rows by the same order with
-// each row's slots ascending.
-__global__ void __launch_bounds__(EP_THREADS) ep_dispatch_kernel(
-    const int32_t* __restrict__ ids, int64_t ids_nb0, int64_t ids_nb1, int n_used, int n_tokens, int ne11, int E,
-    int G, int32_t* __restrict__ hdr, int32_t* __restrict__ row_tok, int32_t* __restrict__ row_slot,
-    int32_t* __restrict__ row_ret, int32_t* __restrict__ counts, int* err) {
-    __shared__ int sh[32];
-    const int e_loc = E / G;
-    const int C = n_tokens * ne11;
-    const int chunk = (C + EP_THREADS - 1) / EP_THREADS;
-    const int c_beg = min(C, (int)threadIdx.x * chunk), c_end = min(C, c_beg + chunk);
-    auto id_at = [&](int s, int t) {
-        return __ldg(reinterpret_cast<const int32_t*>(reinterpret_cast<const char*>(ids) + (int64_t)t * ids_nb1 +
-                                                      (int64_t)s * ids_nb0));
-    };
-    int bad = 0;
-    for (int c = c_beg; c < c_end; c++) {
-        const int t = c / ne11, j = c % ne11;
-        for (int s = j; s < n_used; s += ne11) {
-            const int x = id_at(s, t);
-            if (x < 0 || x >= E) bad = 1;
-        }
+// each row's slots ascending. Three passes over CTAs of EPC candidates: count per destination,
+// one-CTA scan (destination-major, CTA order inside), write.
+struct EpIds {
+    const int32_t* ids;
+    int64_t nb0, nb1;
+    int n_used, ne11, e_loc;
+    __device__ __forceinline__ int at(int s, int t) const {
+        return __ldg(reinterpret_cast<const int32_t*>(reinterpret_cast<const char*>(ids) + (int64_t)t * nb1 +
+                                                      (int64_t)s * nb0));
     }
-    if (__syncthreads_or(bad)) {
-        if (threadIdx.x == 0) atomicCAS(err, 0, B200_DEV_BAD_IDS);
-        for (int i = threadIdx.x; i < 2 * G + 2; i += EP_THREADS) counts[i] = 0;
-        return;
-    }
-    auto mask_of = [&](int c, int d) {
+    __device__ __forceinline__ uint32_t mask(int c, int d) const {
         const int t = c / ne11, j = c % ne11;
         uint32_t m = 0;
         for (int s = j; s < n_used; s += ne11)
-            if (id_at(s, t) / e_loc == d) m |= 1u << s;
+            if (at(s, t) / e_loc == d) m |= 1u << s;
         return m;
-    };
+    }
+};
+
+// bcounts[b][d] = {rows, return rows} of CTA b for destination d; bad[b] = a bad id seen.
+__global__ void __launch_bounds__(EPC) ep_dispatch_count_kernel(EpIds I, int C, int E, int G,
+                                                                int32_t* __restrict__ bcounts, int32_t* __restrict__ bad) {
+    __shared__ int cnt[2 * EP_MAX_RANKS];
+    for (int k = threadIdx.x; k < 2 * G; k += EPC) cnt[k] = 0;
+    __syncthreads();
+    const int c = blockIdx.x * EPC + threadIdx.x;
+    int b = 0;
+    if (c < C) {
+        const int t = c / I.ne11, j = c % I.ne11;
+        for (int s = j; s < I.n_used; s += I.ne11) {
+            const int x = I.at(s, t);
+            if (x < 0 || x >= E) b = 1;
+        }
+        if (!b) {
+            for (int d = 0; d < G; d++) {
+                const uint32_t m = I.mask(c, d);
+                if (m) {
+                    atomicAdd(&cnt[2 * d], 1);
+                    atomicAdd(&cnt[2 * d + 1], __popc(m));
+                }
+            }
+        }
+    }
+    b = __syncthreads_or(b);
+    for (int k = threadIdx.x; k < 2 * G; k += EPC) bcounts[(int64_t)blockIdx.x * 2 * G + k] = cnt[k];
+    if (threadIdx.x == 0) bad[blockIdx.x] = b;
+}
+
+// One thread: bcounts becomes each CTA's first {row, return row} per destination; counts[] gets
+// the per-destination totals and the grand totals; bad[nb] = any bad id.
+__global__ void ep_dispatch_scan_kernel(int32_t* __restrict__ bcounts, int32_t* __restrict__ bad, int nb, int G,
+                                        int32_t* __restrict__ counts, int* err) {
+    if (threadIdx.x != 0) return;
+    int any = 0;
+    for (int b = 0; b < nb; b++) any |= bad[b];
+    bad[nb] = any;
+    if (any) {
+        atomicCAS(err, 0, B200_DEV_BAD_IDS);
+        for (int k = 0; k < 2 * G + 2; k++) counts[k] = 0;
+        return;
+    }
     int row_base = 0, pair_base = 0;
     for (int d = 0; d < G; d++) {
-        int nrow = 0, npair = 0;
-        for (int c = c_beg; c < c_end; c++) {
-            const uint32_t m = mask_of(c, d);
-            if (m) { nrow++; npair += __popc(m); }
+        int rr = 0, pp = 0;
+        for (int b = 0; b < nb; b++) {
+            int32_t* e = bcounts + (int64_t)b * 2 * G + 2 * d;
+            const int r = e[0], p = e[1];
+            e[0] = row_base + rr;
+            e[1] = pair_base + pp;
+            rr += r;
+            pp += p;
         }
-        int tot_row, tot_pair;
-        int p = row_base + block_excl_scan(nrow, &tot_row, sh);
-        int q = pair_base + block_excl_scan(npair, &tot_pair, sh);
-        for (int c = c_beg; c < c_end; c++) {
-            const uint32_t m = mask_of(c, d);
-            if (!m) continue;
-            const int t = c / ne11;
-            int32_t* h = hdr + (int64_t)p * (n_used + 1);
+        counts[d] = rr;
+        counts[G + d] = pp;
+        row_base += rr;
+        pair_base += pp;
+    }
+    counts[2 * G] = row_base;
+    counts[2 * G + 1] = pair_base;
+}
+
+__global__ void __launch_bounds__(EPC) ep_dispatch_write_kernel(EpIds I, int C, int G,
+                                                                const int32_t* __restrict__ bcounts,
+                                                                const int32_t* __restrict__ bad_any,
+                                                                int32_t* __restrict__ hdr, int32_t* __restrict__ row_tok,
+                                                                int32_t* __restrict__ row_slot,
+                                                                int32_t* __restrict__ row_ret) {
+    __shared__ int sh[32];
+    if (__ldg(bad_any)) return;
+    const int c = blockIdx.x * EPC + threadIdx.x;
+    for (int d = 0; d < G; d++) {
+        const uint32_t m = c < C ? I.mask(c, d) : 0u;
+        int tot;
+        const int pr = block_excl_scan(m ? 1 : 0, &tot, sh);
+        const int pq = block_excl_scan(__popc(m), &tot, sh);
+        if (m) {
+            const int32_t* base = bcounts + (int64_t)blockIdx.x * 2 * G + 2 * d;
+            const int p = __ldg(base) + pr;
+            const int t = c / I.ne11;
+            int32_t* h = hdr + (int64_t)p * (I.n_used + 1);
             h[0] = (int32_t)m;
-            for (int s = 0; s < n_used; s++) h[1 + s] = id_at(s, t);
+            for (int s = 0; s < I.n_used; s++) h[1 + s] = I.at(s, t);
             row_tok[p] = t;
             row_slot[p] = __ffs(m) - 1;
-            row_ret[p] = q;
-            p++;
-            q += __popc(m);
+            row_ret[p] = __ldg(base + 1) + pq;
         }
-        if (threadIdx.x == 0) {
-            counts[d] = tot_row;
-            counts[G + d] = tot_pair;
-        }
-        row_base += tot_row;
-        pair_base += tot_pair;
-    }
-    if (threadIdx.x == 0) {
-        counts[2 * G] = row_base;
-        counts[2 * G + 1] = pair_base;
     }
 }
 
 // Owner side: the received rows' (row, slot) pairs, counted per local expert, placed per expert
 // (any order inside an expert: a row's output does not depend on its neighbours in a tile), with
-// the return index rowpref[r] + (rank of slot s among row r's slots). off/tile_start as in
-// moe_route_kernel. Dynamic shared memory: cnt[E_loc], cur[E_loc] ints.
-__global__ void __launch_bounds__(EP_THREADS) ep_expert_route_kernel(
-    const int32_t* __restrict__ hdr, int n_rows, int n_used, int expert0, int e_loc, int bt,
-    int32_t* __restrict__ off, int32_t* __restrict__ tile_start, int32_t* __restrict__ pair_src,
-    int32_t* __restrict__ pair_ret, int32_t* __restrict__ pair_zero, int* err) {
-    extern __shared__ int smx[];
+// the return index rowpref[r] + (rank of slot s among row r's slots). Three passes over CTAs of
+// EPC rows: expert histogram (into zeroed ecnt) and per-CTA pair sums; one-CTA scans (off /
+// tile_start / placement cursors over experts, pair bases over CTAs); placement.
+__global__ void __launch_bounds__(EPC) ep_route_count_kernel(const int32_t* __restrict__ hdr, int n_rows, int n_used,
+                                                             int expert0, int e_loc, int32_t* __restrict__ ecnt,
+                                                             int32_t* __restrict__ bsum, int32_t* __restrict__ bad) {
+    extern __shared__ int hist[];
     __shared__ int sh[32];
-    int* cnt = smx;
-    int* cur = smx + e_loc;
-    for (int e = threadIdx.x; e < e_loc; e += EP_THREADS) cnt[e] = 0;
+    for (int e = threadIdx.x; e < e_loc; e += EPC) hist[e] = 0;
     __syncthreads();
-    const int chunk = (n_rows + EP_THREADS - 1) / EP_THREADS;
-    const int r_beg = min(n_rows, (int)threadIdx.x * chunk), r_end = min(n_rows, r_beg + chunk);
-    int bad = 0, npair = 0;
-    for (int r = r_beg; r < r_end; r++) {
+    const int r = blockIdx.x * EPC + threadIdx.x;
+    int b = 0, pc = 0;
+    if (r < n_rows) {
         const int32_t* h = hdr + (int64_t)r * (n_used + 1);
         uint32_t m = (uint32_t)h[0];
-        if (n_used < 32 && (m >> n_used)) bad = 1;
-        npair += __popc(m);
+        if (n_used < 32 && (m >> n_used)) b = 1;
+        pc = __popc(m);
         while (m) {
             const int s = __ffs(m) - 1;
             m &= m - 1;
             const int x = h[1 + s] - expert0;
-            if (x < 0 || x >= e_loc) bad = 1;
-            else atomicAdd(&cnt[x], 1);
+            if (x < 0 || x >= e_loc) b = 1;
+            else atomicAdd(&hist[x], 1);
         }
     }
-    if (__syncthreads_or(bad)) {
-        if (threadIdx.x == 0) atomicCAS(err, 0, B200_DEV_BAD_IDS);
+    int tot;
+    block_excl_scan(pc, &tot, sh);
+    b = __syncthreads_or(b);
+    for (int e = threadIdx.x; e < e_loc; e += EPC)
+        if (hist[e]) atomicAdd(&ecnt[e], hist[e]);
+    if (threadIdx.x == 0) {
+        bsum[blockIdx.x] = tot;
+        bad[blockIdx.x] = b;
+    }
+}
+
+// One CTA of EP_THREADS. Dynamic shared memory: none.
+__global__ void __launch_bounds__(EP_THREADS) ep_route_scan_kernel(const int32_t* __restrict__ ecnt,
+                                                                  int32_t* __restrict__ bsum, int32_t* __restrict__ bad,
+                                                                  int nb, int e_loc, int bt, int32_t* __restrict__ off,
+                                                                  int32_t* __restrict__ tile_start,
+                                                                  int32_t* __restrict__ cursor, int* err) {
+    __shared__ int sh[32];
+    __shared__ int carry[3];
+    int any = 0;
+    for (int b = threadIdx.x; b < nb; b += EP_THREADS) any |= bad[b];
+    if (__syncthreads_or(any)) {
+        if (threadIdx.x == 0) {
+            atomicCAS(err, 0, B200_DEV_BAD_IDS);
+            bad[nb] = 1;
+        }
         for (int e = threadIdx.x; e <= e_loc; e += EP_THREADS) {
             off[e] = 0;
             tile_start[e] = 0;
         }
         return;
     }
-    int total;
-    int q = block_excl_scan(npair, &total, sh);
     if (threadIdx.x == 0) {
-        int acc = 0, tacc = 0;
-        for (int e = 0; e < e_loc; e++) {
-            off[e] = acc;
-            cur[e] = acc;
-            tile_start[e] = tacc;
-            acc += cnt[e];
-            tacc += (cnt[e] + bt - 1) / bt;
-        }
-        off[e_loc] = acc;
-        tile_start[e_loc] = tacc;
+        bad[nb] = 0;
+        carry[0] = carry[1] = carry[2] = 0;
     }
     __syncthreads();
-    for (int r = r_beg; r < r_end; r++) {
-        const int32_t* h = hdr + (int64_t)r * (n_used + 1);
-        uint32_t m = (uint32_t)h[0];
-        while (m) {
-            const int s = __ffs(m) - 1;
-            m &= m - 1;
-            const int x = h[1 + s] - expert0;
-            const int p = atomicAdd(&cur[x], 1);
-            pair_src[p] = r;
-            pair_ret[p] = q++;
-            pair_zero[p] = 0;
+    for (int e0 = 0; e0 < e_loc; e0 += EP_THREADS) {
+        const int e = e0 + threadIdx.x;
+        const int c = e < e_loc ? ecnt[e] : 0;
+        int t1, t2;
+        const int x1 = block_excl_scan(c, &t1, sh);
+        const int x2 = block_excl_scan((c + bt - 1) / bt, &t2, sh);
+        if (e < e_loc) {
+            off[e] = carry[0] + x1;
+            cursor[e] = carry[0] + x1;
+            tile_start[e] = carry[1] + x2;
         }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            carry[0] += t1;
+            carry[1] += t2;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        off[e_loc] = carry[0];
+        tile_start[e_loc] = carry[1];
+    }
+    for (int b0 = 0; b0 < nb; b0 += EP_THREADS) {            // pair bases of the row CTAs
+        const int b = b0 + threadIdx.x;
+        const int v = b < nb ? bsum[b] : 0;
+        int t;
+        const int x = block_excl_scan(v, &t, sh);
+        if (b < nb) bsum[b] = carry[2] + x;
+        __syncthreads();
+        if (threadIdx.x == 0) carry[2] += t;
+        __syncthreads();
     }
 }
 
-// Sorted pair p <- received row pair_src[p] (fp16 row and its scale).
+__global__ void __launch_bounds__(EPC) ep_route_place_kernel(const int32_t* __restrict__ hdr, int n_rows, int n_used,
+                                                             int expert0, const int32_t* __restrict__ bsum,
+                                                             const int32_t* __restrict__ bad_any,
+                                                             int32_t* __restrict__ cursor,
+                                                             int32_t* __restrict__ pair_src,
+                                                             int32_t* __restrict__ pair_ret,
+                                                             int32_t* __restrict__ pair_zero) {
+    __shared__ int sh[32];
+    if (__ldg(bad_any)) return;
+    const int r = blockIdx.x * EPC + threadIdx.x;
+    uint32_t m = 0;
+    const int32_t* h = hdr + (int64_t)r * (n_used + 1);
+    if (r < n_rows) m = (uint32_t)h[0];
+    int tot;
+    int q = __ldg(bsum + blockIdx.x) + block_excl_scan(__popc(m), &tot, sh);
+    while (m) {
+        const int s = __ffs(m) - 1;
+        m &= m - 1;
+        const int x = h[1 + s] - expert0;
+        const int p = atomicAdd(&cursor[x], 1);
+        pair_src[p] = r;
+        pair_ret[p] = q++;
+        pair_zero[p] = 0;
+    }
+}
+
+// Sorted pair p <- received row pair_src[p] (fp16 row and its scale); grid-stride over pairs.
 __global__ void __launch_bounds__(256) ep_gather_rows_kernel(const __half* __restrict__ src, const float* __restrict__ src_scale,
                                                              const int32_t* __restrict__ pair_src,
                                                              const int32_t* __restrict__ n_pairs, int K,
                                                              __half* __restrict__ dst, float* __restrict__ dst_scale) {
-    const int p = blockIdx.x;
-    if (p >= __ldg(n_pairs)) return;
-    const int r = __ldg(pair_src + p);
-    const uint4* s = reinterpret_cast<const uint4*>(src + (int64_t)r * K);
-    uint4* d = reinterpret_cast<uint4*>(dst + (int64_t)p * K);
-    for (int i = threadIdx.x; i < K / 8; i += 256) d[i] = __ldg(s + i);
-    if (threadIdx.x == 0) dst_scale[p] = __ldg(src_scale + r);
+    const int n = __ldg(n_pairs);
+    for (int p = blockIdx.x; p < n; p += gridDim.x) {
+        const int r = __ldg(pair_src + p);
+        const uint4* s = reinterpret_cast<const uint4*>(src + (int64_t)r * K);
+        uint4* d = reinterpret_cast<uint4*>(dst + (int64_t)p * K);
+        for (int i = threadIdx.x; i < K / 8; i += 256) d[i] = __ldg(s + i);
+        if (threadIdx.x == 0) dst_scale[p] = __ldg(src_scale + r);
+    }
 }
 
-// Home side: send row p's returned rows (one per slot in its mask, ascending) -> dst[:, s, t].
+// Home side: send row p's returned rows (one per slot in its mask, ascending) -> dst[:, s, t];
+// grid-stride over send rows.
 __global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict__ ret, int N,
                                                          const int32_t* __restrict__ hdr, int n_used,
                                                          const int32_t* __restrict__ row_tok,
                                                          const int32_t* __restrict__ row_ret,
                                                          const int32_t* __restrict__ n_rows, float* __restrict__ dst,
                                                          int64_t d_nb1, int64_t d_nb2) {
-    const int p = blockIdx.x;
-    if (p >= __ldg(n_rows)) return;
-    const int t = __ldg(row_tok + p);
-    uint32_t m = (uint32_t)__ldg(hdr + (int64_t)p * (n_used + 1));
-    int k = __ldg(row_ret + p);
-    while (m) {
-        const int s = __ffs(m) - 1;
-        m &= m - 1;
-        const float4* src = reinterpret_cast<const float4*>(ret + (int64_t)k * N);
-        float4* out = reinterpret_cast<float4*>(reinterpret_cast<char*>(dst) + (int64_t)t * d_nb2 + (int64_t)s * d_nb1);
-        for (int i = threadIdx.x; i < N / 4; i += 256) out[i] = __ldg(src + i);
-        k++;
+    const int n = __ldg(n_rows);
+    for (int p = blockIdx.x; p < n; p += gridDim.x) {
+        const int t = __ldg(row_tok + p);
+        uint32_t m = (uint32_t)__ldg(hdr + (int64_t)p * (n_used + 1));
+        int k = __ldg(row_ret + p);
+        while (m) {
+            const int s = __ffs(m) - 1;
+            m &= m - 1;
+            const float4* src = reinterpret_cast<const float4*>(ret + (int64_t)k * N);
+            float4* out = reinterpret_cast<float4*>(reinterpret_cast<char*>(dst) + (int64_t)t * d_nb2 + (int64_t)s * d_nb1);
+            for (int i = threadIdx.x; i < N / 4; i += 256) out[i] = __ldg(src + i);
+            k++;
+        }
     }
 }
 
 struct EpExpertLayout {
-    size_t off, tiles, src, ret, zero, a16, scales, total;
+    size_t off, tiles, src, ret, zero, a16, scales, ecnt, cursor, bsum, bad, total;
 };
 
 static EpExpertLayout ep_expert_layout(int64_t K, int64_t e_loc, int64_t n_used, int64_t n_rows) {
@@ -250,27 +350,47 @@ static EpExpertLayout ep_expert_layout(int64_t K, int64_t e_loc, int64_t n_used,
     L.zero = L.ret + al(P * 4);
     L.a16 = L.zero + al(P * 4);
     L.scales = L.a16 + al(P * (size_t)K * 2);
-    L.total = L.scales + al(P * 4);
+    const size_t nb = (size_t)((n_rows + EPC - 1) / EPC);
+    L.ecnt = L.scales + al(P * 4);
+    L.cursor = L.ecnt + al((size_t)e_loc * 4);
+    L.bsum = L.cursor + al((size_t)e_loc * 4);
+    L.bad = L.bsum + al(nb * 4);
+    L.total = L.bad + al((nb + 1) * 4);
     return L;
 }
 
+// as moe_token_tile: one 256-token tile once an expert averages ~100+ rows
 static int ep_token_tile(int64_t pairs, int64_t e_loc) {
     const int64_t avg = e_loc > 0 ? pairs / e_loc : pairs;
-    return avg <= 32 ? 32 : avg <= 64 ? 64 : 128;
+    return avg <= 32 ? 32 : avg <= 64 ? 64 : avg < 96 ? 128 : 256;
+}
+
+static size_t ep_dispatch_scratch(int64_t n_tokens, int64_t ne11, int64_t n_ranks) {
+    const size_t nb = (size_t)((n_tokens * ne11 + EPC - 1) / EPC);
+    return ((nb * 2 * n_ranks * 4 + 255) & ~(size_t)255) + (nb + 1) * 4;
 }
 
 }  // namespace b200
 
 extern "C" {
 
+size_t b200_moe_ep_dispatch_scratch_size(int64_t n_tokens, int64_t ne11, int64_t n_ranks) {
+    if (n_tokens <= 0 || ne11 <= 0 || n_ranks <= 0) return 0;
+    return b200::ep_dispatch_scratch(n_tokens, ne11, n_ranks);
+}
+
 int b200_moe_ep_dispatch(const int32_t* ids, int64_t ids_nb0, int64_t ids_nb1, int64_t n_used, int64_t n_tokens,
                          int64_t n_expert, int64_t n_ranks, const float* b, int64_t b_nb1, int64_t b_nb2, int64_t ne11,
                          int64_t K, void* send_a16, float* send_scale, int32_t* send_hdr, int32_t* row_tok,
-                         int32_t* row_slot, int32_t* row_ret, int32_t* counts, int* dev_err, void* stream) {
+                         int32_t* row_slot, int32_t* row_ret, int32_t* counts, void* scratch, size_t scratch_bytes,
+                         int* dev_err, void* stream) {
     using namespace b200;
     if (!ids || !b || !send_a16 || !send_scale || !send_hdr || !row_tok || !row_slot || !row_ret || !counts ||
         !dev_err || n_used <= 0 || n_tokens <= 0 || n_expert <= 0 || n_ranks <= 0 || ne11 <= 0 || K <= 0)
         return B200_E_INVALID;
+    if (!scratch || scratch_bytes < ep_dispatch_scratch(n_tokens, ne11, n_ranks) ||
+        (reinterpret_cast<uintptr_t>(scratch) & 255u))
+        return B200_E_WORKSPACE;
     if (n_used > EP_MAX_SLOTS || n_ranks > EP_MAX_RANKS || n_expert % n_ranks != 0 || n_used % ne11 != 0 ||
         K % 8 != 0 || n_tokens * n_used > (1 << 28))
         return B200_E_UNSUPPORTED;
@@ -278,9 +398,16 @@ int b200_moe_ep_dispatch(const int32_t* ids, int64_t ids_nb0, int64_t ids_nb1, i
         (reinterpret_cast<uintptr_t>(send_a16) & 15u))
         return B200_E_UNSUPPORTED;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    ep_dispatch_kernel<<<1, EP_THREADS, 0, st>>>(ids, ids_nb0, ids_nb1, (int)n_used, (int)n_tokens, (int)ne11,
-                                                 (int)n_expert, (int)n_ranks, send_hdr, row_tok, row_slot, row_ret,
-                                                 counts, dev_err);
+    const int C = (int)(n_tokens * ne11);
+    const int nb = (C + EPC - 1) / EPC;
+    int32_t* bcounts = static_cast<int32_t*>(scratch);
+    int32_t* bad = reinterpret_cast<int32_t*>(static_cast<char*>(scratch) +
+                                              (((size_t)nb * 2 * n_ranks * 4 + 255) & ~(size_t)255));
+    const EpIds I{ids, ids_nb0, ids_nb1, (int)n_used, (int)ne11, (int)(n_expert / n_ranks)};
+    ep_dispatch_count_kernel<<<nb, EPC, 0, st>>>(I, C, (int)n_expert, (int)n_ranks, bcounts, bad);
+    ep_dispatch_scan_kernel<<<1, 32, 0, st>>>(bcounts, bad, nb, (int)n_ranks, counts, dev_err);
+    ep_dispatch_write_kernel<<<nb, EPC, 0, st>>>(I, C, (int)n_ranks, bcounts, bad + nb, send_hdr, row_tok, row_slot,
+                                                 row_ret);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
     const int rc = launch_gather_pack(b, b_nb1, b_nb2, ne11, K, row_slot, row_tok, counts + 2 * n_ranks,
                                       n_tokens * n_used, static_cast<__half*>(send_a16), send_scale, st);
@@ -318,18 +445,29 @@ int b200_moe_ep_expert(int wtype, const void* local_stack, int64_t K, int64_t N,
     int32_t* zero = reinterpret_cast<int32_t*>(ws + L.zero);
     __half* a16 = reinterpret_cast<__half*>(ws + L.a16);
     float* scales = reinterpret_cast<float*>(ws + L.scales);
+    int32_t* ecnt = reinterpret_cast<int32_t*>(ws + L.ecnt);
+    int32_t* cursor = reinterpret_cast<int32_t*>(ws + L.cursor);
+    int32_t* bsum = reinterpret_cast<int32_t*>(ws + L.bsum);
+    int32_t* bad = reinterpret_cast<int32_t*>(ws + L.bad);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int64_t pmax = n_rows * n_used;
     const int bt = ep_token_tile(n_pairs_hint > 0 ? n_pairs_hint : n_rows, n_local);
-    const size_t smem = (size_t)2 * n_local * sizeof(int);
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(ep_expert_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    const int nb = (int)((n_rows + EPC - 1) / EPC);
+    const size_t hist_smem = (size_t)n_local * sizeof(int);
+    if (hist_smem > 48 * 1024 &&
+        cudaFuncSetAttribute(ep_route_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hist_smem) !=
+            cudaSuccess)
         return B200_E_UNSUPPORTED;
-    ep_expert_route_kernel<<<1, EP_THREADS, smem, st>>>(recv_hdr, (int)n_rows, (int)n_used, (int)expert0,
-                                                        (int)n_local, bt, off, tiles, src, rix, zero, dev_err);
+    if (cudaMemsetAsync(ecnt, 0, (size_t)n_local * 4, st) != cudaSuccess) return B200_E_CUDA;
+    ep_route_count_kernel<<<nb, EPC, hist_smem, st>>>(recv_hdr, (int)n_rows, (int)n_used, (int)expert0,
+                                                      (int)n_local, ecnt, bsum, bad);
+    ep_route_scan_kernel<<<1, EP_THREADS, 0, st>>>(ecnt, bsum, bad, nb, (int)n_local, bt, off, tiles, cursor, dev_err);
+    ep_route_place_kernel<<<nb, EPC, 0, st>>>(recv_hdr, (int)n_rows, (int)n_used, (int)expert0, bsum, bad + nb,
+                                              cursor, src, rix, zero);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
-    ep_gather_rows_kernel<<<(unsigned)pmax, 256, 0, st>>>(static_cast<const __half*>(recv_a16), recv_scale, src,
-                                                          off + n_local, (int)K, a16, scales);
+    const int64_t gcap = (int64_t)device_sm_count() * 8;
+    ep_gather_rows_kernel<<<(unsigned)(pmax < gcap ? pmax : gcap), 256, 0, st>>>(
+        static_cast<const __half*>(recv_a16), recv_scale, src, off + n_local, (int)K, a16, scales);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
     return gemm_grouped_impl(wtype, local_stack, N, K, n_local, a16, scales, pmax, bt, off, tiles, zero, rix, ret, 0,
                              N * 4, dev_err, st);
@@ -346,7 +484,8 @@ int b200_moe_ep_combine(const float* ret, int64_t N, const int32_t* send_hdr, in
     if (N % 4 || (d_nb1 % 16) || (d_nb2 % 16) || (reinterpret_cast<uintptr_t>(dst) & 15u) ||
         (reinterpret_cast<uintptr_t>(ret) & 15u))
         return B200_E_UNSUPPORTED;
-    ep_combine_kernel<<<(unsigned)max_rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+    const int64_t gcap = (int64_t)device_sm_count() * 8;
+    ep_combine_kernel<<<(unsigned)(max_rows < gcap ? max_rows : gcap), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         ret, (int)N, send_hdr, (int)n_used, row_tok, row_ret, counts + 2 * n_ranks, dst, d_nb1, d_nb2);
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }

@@ -192,8 +192,9 @@ _BACKEND_SIGS = {
 }
 _SIGS.update(_BACKEND_SIGS)
 _SIGS.update({
+    "b200_moe_ep_dispatch_scratch_size": (_sz, [_i64, _i64, _i64]),
     "b200_moe_ep_dispatch": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
-                                    _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+                                    _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp]),
     "b200_moe_ep_expert_workspace_size": (_sz, [_i64] * 4),
     "b200_moe_ep_expert": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i64,
                                   _vp, _vp, _sz, _vp, _vp]),

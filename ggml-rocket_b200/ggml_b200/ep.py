@@ -59,12 +59,15 @@ class DeviceOps:
             row_slot=torch.empty(max_rows, dtype=torch.int32, device=dev),
             row_ret=torch.empty(max_rows, dtype=torch.int32, device=dev),
             counts=torch.zeros(2 * n_ranks + 2, dtype=torch.int32, device=dev))
+        scratch = torch.empty(max(256, g.lib().b200_moe_ep_dispatch_scratch_size(n_tokens, ne11, n_ranks)),
+                              dtype=torch.uint8, device=dev)
         # ids [n_tokens, n_used] as ggml stores it: the slot stride is ids_nb0, the token stride ids_nb1
         g.check(g.lib().b200_moe_ep_dispatch(
             g._ptr(ids), ids.stride(1) * 4, ids.stride(0) * 4, n_used, n_tokens, n_expert, n_ranks,
             g._ptr(b), b.stride(1) * 4, b.stride(0) * 4, ne11, K,
             g._ptr(d.a16), g._ptr(d.scale), g._ptr(d.hdr), g._ptr(d.row_tok), g._ptr(d.row_slot),
-            g._ptr(d.row_ret), g._ptr(d.counts), g._ptr(self._err(dev)), g._stream(stream)), "moe_ep_dispatch")
+            g._ptr(d.row_ret), g._ptr(d.counts), g._ptr(scratch), scratch.numel(), g._ptr(self._err(dev)),
+            g._stream(stream)), "moe_ep_dispatch")
         return d
 
     def expert(self, wtype, local_stack, K, N, n_local, expert0, a16, scale, hdr, n_pairs, stream=None):

@@ -171,6 +171,7 @@ int    b200_mul_mat_id_route_view(int64_t K, int64_t n_expert, int64_t n_used, i
  *     Buffers hold up to n_tokens*n_used rows. counts (device int32 [2*n_ranks+2]) receives
  *     rows per destination, return rows (slot-mask bits) per destination, total rows, total
  *     return rows. row_tok / row_slot / row_ret are the home rank's bookkeeping for step 3.
+ *     scratch: b200_moe_ep_dispatch_scratch_size bytes of device memory, 256-byte aligned.
  *  2. b200_moe_ep_expert (owner rank): over the n_rows received rows (any number of sources,
  *     concatenated), writes one f32 row of N per (row, slot in its mask) into ret, in received
  *     order with each row's slots ascending -- the order the home rank expects back.
@@ -179,12 +180,13 @@ int    b200_mul_mat_id_route_view(int64_t K, int64_t n_expert, int64_t n_used, i
  *     laid them out) -> dst[:, slot, token] with dst strides d_nb1 / d_nb2 in bytes.
  * An id outside [0, n_expert) (dispatch) or a header naming an expert this rank does not own
  * (expert) sets *dev_err to B200_DEV_BAD_IDS and produces no rows. */
+size_t b200_moe_ep_dispatch_scratch_size(int64_t n_tokens, int64_t ne11, int64_t n_ranks);
 int    b200_moe_ep_dispatch(const int32_t * ids, int64_t ids_nb0, int64_t ids_nb1, int64_t n_used,
                             int64_t n_tokens, int64_t n_expert, int64_t n_ranks,
                             const float * b, int64_t b_nb1, int64_t b_nb2, int64_t ne11, int64_t K,
                             void * send_a16, float * send_scale, int32_t * send_hdr,
                             int32_t * row_tok, int32_t * row_slot, int32_t * row_ret, int32_t * counts,
-                            int * dev_err, void * stream);
+                            void * scratch, size_t scratch_bytes, int * dev_err, void * stream);
 size_t b200_moe_ep_expert_workspace_size(int64_t K, int64_t n_local, int64_t n_used, int64_t n_rows);
 int    b200_moe_ep_expert(int wtype, const void * local_stack, int64_t K, int64_t N, int64_t n_local,
                           int64_t expert0, const void * recv_a16, const float * recv_scale,
