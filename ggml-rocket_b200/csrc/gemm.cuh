@@ -74,6 +74,10 @@ struct GemmArgs {
     const int32_t* g_tok;          // sorted row -> token
     int n_expert;
     int64_t d_nb1, d_nb2;          // dst strides over (slot, token), bytes
+    // optional (expert parallelism over peer memory): sorted row -> index into out_bases, the
+    // destination of that row (another GPU's buffer, reached by plain stores over NVLink)
+    const int32_t* g_src;
+    float* const* out_bases;
 };
 
 // One work item of a CTA: a tile (or, in stream-K, the piece of a tile's K range this CTA owns).
@@ -484,10 +488,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                             float4 v = es4[jr * 8 + cc];
                             v.x *= sc; v.y *= sc; v.z *= sc; v.w *= sc;
                             float* dp;
-                            if constexpr (GROUPED)
-                                dp = reinterpret_cast<float*>(reinterpret_cast<char*>(args.out) +
+                            if constexpr (GROUPED) {
+                                float* ob = args.g_src ? args.out_bases[__ldg(args.g_src + t)] : args.out;
+                                dp = reinterpret_cast<float*>(reinterpret_cast<char*>(ob) +
                                                               (int64_t)__ldg(args.g_tok + t) * args.d_nb2 +
                                                               (int64_t)__ldg(args.g_slot + t) * args.d_nb1) + nb;
+                            }
                             else
                                 dp = args.out + (size_t)t * args.ldo + nb;
                             *reinterpret_cast<float4*>(dp) = v;
@@ -495,6 +501,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     }
                     __syncwarp();
                 }
+            }
+            if constexpr (GROUPED) {
+                // rows stored into other GPUs' memory must be visible there before the kernel
+                // that follows signals their owners
+                if (args.g_src) __threadfence_system();
             }
             tc_fence_before();
             __syncwarp();

@@ -21,11 +21,16 @@ int act_pack_impl(const float* src1, int64_t lda, int64_t M, int64_t K, __half* 
 int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int64_t n_expert, const __half* a16,
                       const float* scales, int64_t rows, int bt, const int32_t* off, const int32_t* tile_start,
                       const int32_t* slot, const int32_t* tok, float* dst, int64_t d_nb1, int64_t d_nb2, int* dev_err,
-                      cudaStream_t st);
+                      cudaStream_t st, const int32_t* src = nullptr, float* const* dst_bases = nullptr);
 // Gather b[:, slot[r] % ne11, tok[r]] for r < *n_rows (device count; max_rows bounds the grid)
 // and pack each row to fp16 with its per-row scale (moe.cu).
 int launch_gather_pack(const float* b, int64_t b_nb1, int64_t b_nb2, int64_t ne11, int64_t K, const int32_t* slot,
                        const int32_t* tok, const int32_t* n_rows, int64_t max_rows, __half* a16, float* scales,
                        cudaStream_t st);
+
+// expert parallelism helpers shared by the NCCL and peer-memory paths (moe_ep.cu)
+int ep_token_tile_public(int64_t pairs, int64_t e_loc);
+void ep_route_scan_public(const int32_t* ecnt, int32_t* bsum, int32_t* bad, int nb, int e_loc, int bt, int32_t* off,
+                          int32_t* tile_start, int32_t* cursor, int* err, cudaStream_t st);
 
 }  // namespace b200

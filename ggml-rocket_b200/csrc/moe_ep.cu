@@ -31,33 +31,6 @@ constexpr int EP_THREADS = 1024;
 constexpr int EP_MAX_RANKS = 64;
 constexpr int EP_MAX_SLOTS = 32;   // slot masks are 32-bit
 
-// Exclusive scan of one int over the CTA (any multiple of 32 threads); also returns the total.
-__device__ __forceinline__ int block_excl_scan(int v, int* total, int* sh /* [32] */) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    int x = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-    }
-    if (lane == 31) sh[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-        int w = lane < nw ? sh[lane] : 0;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, w, o);
-            if (lane >= o) w += y;
-        }
-        sh[lane] = w;                                   // inclusive over warps
-    }
-    __syncthreads();
-    const int before = (warp > 0 ? sh[warp - 1] : 0) + x - v;
-    *total = sh[nw - 1];
-    __syncthreads();                                    // sh is reused by the next call
-    return before;
-}
-
 constexpr int EPC = 256;   // candidates / rows per CTA of the multi-CTA passes
 
 // Home side. Candidate c = t * ne11 + j is token t's b row j (serving slots s with s % ne11 == j).
@@ -368,6 +341,13 @@ static int ep_token_tile(int64_t pairs, int64_t e_loc) {
 static size_t ep_dispatch_scratch(int64_t n_tokens, int64_t ne11, int64_t n_ranks) {
     const size_t nb = (size_t)((n_tokens * ne11 + EPC - 1) / EPC);
     return ((nb * 2 * n_ranks * 4 + 255) & ~(size_t)255) + (nb + 1) * 4;
+}
+
+int ep_token_tile_public(int64_t pairs, int64_t e_loc) { return ep_token_tile(pairs, e_loc); }
+
+void ep_route_scan_public(const int32_t* ecnt, int32_t* bsum, int32_t* bad, int nb, int e_loc, int bt, int32_t* off,
+                          int32_t* tile_start, int32_t* cursor, int* err, cudaStream_t st) {
+    ep_route_scan_kernel<<<1, EP_THREADS, 0, st>>>(ecnt, bsum, bad, nb, e_loc, bt, off, tile_start, cursor, err);
 }
 
 }  // namespace b200

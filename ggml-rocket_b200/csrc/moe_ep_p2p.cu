@@ -1,0 +1,384 @@
+// Expert-parallel MUL_MAT_ID over NVLink peer memory: the exchange steps are the kernels' own
+// stores into other GPUs' buffers, ordered by flags, with no collective library call and no
+// host round trip on the data path.
+//
+// Every rank allocates the same "shared" buffers (cudaMalloc, exported with an IPC handle and
+// mapped by every other rank once, at set-up):
+//   recv_a16  [G][cap][K_max] fp16   rows pushed to this rank (as owner), one region per source
+//   recv_meta [G][cap][n_used + 3]   per row {scale bits, slot mask, home token, ids...}
+//   ret       [T_max][n_used][N_max] f32, this rank's (as home) outputs, dst's own layout
+//   flags     [2][G][4] int32        {epoch, rows, pairs} from each source; done epoch per owner
+// (the caller allocates them; b200_ep_shared_export / _open map them between processes)
+// One op (epoch e, every rank in the same order, all on the caller's stream):
+//   home   dispatch (moe_ep.cu kernels: rows per owner with slot masks, fp16 pack), then
+//          ep_push_kernel stores each row straight into its owner's recv region for this rank
+//          and ep_signal_kernel publishes {e, rows, pairs} in every owner's flags
+//   owner  ep_wait_kernel waits for all sources' flags (bounded), the route / gather kernels
+//          sort the received (row, slot) pairs by local expert, and the grouped tcgen05 GEMM's
+//          epilogue stores every output row straight into its home rank's ret (NVLink stores,
+//          no return exchange); ep_signal_kernel then publishes e in every home's done flags
+//   home   ep_wait_kernel waits for every owner's done flag; ret holds dst.
+// A rank reuses recv / ret only after the previous op's flags complete, so one set suffices.
+#include <cstdint>
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "ggml-b200-kernels.h"
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace b200 {
+
+constexpr int P2P_THREADS = 256;
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Home: send row p (rows grouped by destination, counts[d] per destination) -> owner d's recv
+// region for source `me`. Grid-stride over rows; one warp copies one row.
+__global__ void __launch_bounds__(P2P_THREADS) ep_push_kernel(const __half* __restrict__ a16, const float* __restrict__ scale,
+                                                              const int32_t* __restrict__ hdr,
+                                                              const int32_t* __restrict__ row_tok,
+                                                              const int32_t* __restrict__ counts, int G, int me,
+                                                              int n_used, int K, int64_t cap,
+                                                              __half* const* __restrict__ peer_a16,
+                                                              int32_t* const* __restrict__ peer_meta) {
+    const int n = __ldg(counts + 2 * G);
+    const int lane = threadIdx.x & 31;
+    const int wpb = P2P_THREADS / 32;
+    const int MW = n_used + 3;
+    for (int p = blockIdx.x * wpb + (threadIdx.x >> 5); p < n; p += gridDim.x * wpb) {
+        int d = 0, base = 0;
+        while (d < G - 1 && p >= base + __ldg(counts + d)) base += __ldg(counts + d++);
+        const int64_t slot = (int64_t)me * cap + (p - base);
+        const uint4* src = reinterpret_cast<const uint4*>(a16 + (int64_t)p * K);
+        uint4* dst = reinterpret_cast<uint4*>(peer_a16[d] + slot * K);
+        for (int i = lane; i < K / 8; i += 32) dst[i] = __ldg(src + i);
+        int32_t* meta = peer_meta[d] + slot * MW;
+        const int32_t* h = hdr + (int64_t)p * (n_used + 1);
+        for (int i = lane; i < MW; i += 32) {
+            int32_t v;
+            if (i == 0) v = __float_as_int(__ldg(scale + p));
+            else if (i == 1) v = __ldg(h);                    // slot mask
+            else if (i == 2) v = __ldg(row_tok + p);          // the home's token index
+            else v = __ldg(h + i - 2);                        // ids
+            meta[i] = v;
+        }
+    }
+    __threadfence_system();
+}
+
+// Publish epoch e (and, with rows/pairs, this rank's counts per destination) in every peer's
+// flag slot for this rank: flags[slot_base + me][0..3] on rank d.
+__global__ void ep_signal_kernel(int* const* __restrict__ peer_flags, int slot_base, int me, int G, int epoch,
+                                 const int32_t* __restrict__ counts) {
+    __threadfence_system();
+    const int d = threadIdx.x;
+    if (d >= G) return;
+    int* f = peer_flags[d] + 4 * (slot_base + me);
+    if (counts) {
+        f[1] = __ldg(counts + d);
+        f[2] = __ldg(counts + G + d);
+    }
+    __threadfence_system();
+    st_release_sys(f, epoch);
+}
+
+// Wait (bounded) until every rank's flag in this rank's slots [slot_base, slot_base + G) holds
+// the epoch; copy their row counts and prefix into region (region[G] rows, region[G+1] pairs
+// total; region[G+2..] row prefixes) when `region` is given.
+__global__ void ep_wait_kernel(const int* __restrict__ flags, int slot_base, int G, int epoch, int32_t* __restrict__ region,
+                               int* err) {
+    const int s = threadIdx.x;
+    bool ok = true;
+    if (s < G) {
+        const int* f = flags + 4 * (slot_base + s);
+        const uint64_t t0 = globaltimer();
+        while (ld_acquire_sys(f) != epoch) {
+            __nanosleep(256);
+            if (globaltimer() - t0 > B200_WAIT_LIMIT_NS) {
+                atomicCAS(err, 0, ERR_WAIT_PEER);
+                ok = false;
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (region && threadIdx.x == 0) {
+        int rows = 0, pairs = 0;
+        for (int k = 0; k < G; k++) {
+            const int rk = ok ? flags[4 * (slot_base + k) + 1] : 0;
+            region[G + 2 + k] = rows;
+            region[k] = rk;
+            rows += rk;
+            pairs += ok ? flags[4 * (slot_base + k) + 2] : 0;
+        }
+        region[G] = rows;
+        region[G + 1] = pairs;
+    }
+}
+
+// Received row r (over the G source regions, concatenated) -> (source, index in its region).
+__device__ __forceinline__ bool p2p_row(const int32_t* region, int G, int r, int& src, int& idx) {
+    if (r >= __ldg(region + G)) return false;
+    src = 0;
+    while (src < G - 1 && r >= __ldg(region + G + 2 + src + 1)) src++;
+    idx = r - __ldg(region + G + 2 + src);
+    return true;
+}
+
+constexpr int P2PC = 256;   // rows per CTA of the route passes
+
+__global__ void __launch_bounds__(P2PC) p2p_route_count_kernel(const int32_t* __restrict__ meta, const int32_t* __restrict__ region,
+                                                               int G, int64_t cap, int n_used, int expert0, int e_loc,
+                                                               int32_t* __restrict__ ecnt, int32_t* __restrict__ bsum,
+                                                               int32_t* __restrict__ bad) {
+    extern __shared__ int hist[];
+    __shared__ int sh[32];
+    for (int e = threadIdx.x; e < e_loc; e += P2PC) hist[e] = 0;
+    __syncthreads();
+    const int MW = n_used + 3;
+    const int r = blockIdx.x * P2PC + threadIdx.x;
+    int src, idx, b = 0, pc = 0;
+    if (p2p_row(region, G, r, src, idx)) {
+        const int32_t* mrow = meta + ((int64_t)src * cap + idx) * MW;
+        uint32_t m = (uint32_t)mrow[1];
+        if (n_used < 32 && (m >> n_used)) b = 1;
+        pc = __popc(m);
+        while (m) {
+            const int s = __ffs(m) - 1;
+            m &= m - 1;
+            const int x = mrow[3 + s] - expert0;
+            if (x < 0 || x >= e_loc) b = 1;
+            else atomicAdd(&hist[x], 1);
+        }
+    }
+    int tot;
+    block_excl_scan(pc, &tot, sh);
+    b = __syncthreads_or(b);
+    for (int e = threadIdx.x; e < e_loc; e += P2PC)
+        if (hist[e]) atomicAdd(&ecnt[e], hist[e]);
+    if (threadIdx.x == 0) {
+        bsum[blockIdx.x] = tot;
+        bad[blockIdx.x] = b;
+    }
+}
+
+// Pairs of the received rows -> per-expert order (any order inside an expert), with the pair's
+// home rank, home token and slot for the GEMM epilogue.
+__global__ void __launch_bounds__(P2PC) p2p_route_place_kernel(const int32_t* __restrict__ meta, const int32_t* __restrict__ region,
+                                                               int G, int64_t cap, int n_used, int expert0,
+                                                               const int32_t* __restrict__ bad_any,
+                                                               int32_t* __restrict__ cursor,
+                                                               int32_t* __restrict__ pair_row,
+                                                               int32_t* __restrict__ pair_src,
+                                                               int32_t* __restrict__ pair_tok,
+                                                               int32_t* __restrict__ pair_slot) {
+    if (__ldg(bad_any)) return;
+    const int MW = n_used + 3;
+    const int r = blockIdx.x * P2PC + threadIdx.x;
+    int src, idx;
+    if (!p2p_row(region, G, r, src, idx)) return;
+    const int32_t* mrow = meta + ((int64_t)src * cap + idx) * MW;
+    uint32_t m = (uint32_t)mrow[1];
+    const int tok = mrow[2];
+    while (m) {
+        const int s = __ffs(m) - 1;
+        m &= m - 1;
+        const int x = mrow[3 + s] - expert0;
+        const int p = atomicAdd(&cursor[x], 1);
+        pair_row[p] = (int)((int64_t)src * cap + idx);
+        pair_src[p] = src;
+        pair_tok[p] = tok;
+        pair_slot[p] = s;
+    }
+}
+
+// Sorted pair p <- its received row (fp16 row, scale from the meta record); grid-stride.
+__global__ void __launch_bounds__(256) p2p_gather_kernel(const __half* __restrict__ recv, const int32_t* __restrict__ meta,
+                                                         const int32_t* __restrict__ pair_row,
+                                                         const int32_t* __restrict__ n_pairs, int n_used, int K,
+                                                         __half* __restrict__ dst, float* __restrict__ dst_scale) {
+    const int n = __ldg(n_pairs);
+    const int MW = n_used + 3;
+    for (int p = blockIdx.x; p < n; p += gridDim.x) {
+        const int64_t rr = __ldg(pair_row + p);
+        const uint4* s = reinterpret_cast<const uint4*>(recv + rr * K);
+        uint4* d = reinterpret_cast<uint4*>(dst + (int64_t)p * K);
+        for (int i = threadIdx.x; i < K / 8; i += 256) d[i] = __ldg(s + i);
+        if (threadIdx.x == 0) dst_scale[p] = __int_as_float(__ldg(meta + rr * MW));
+    }
+}
+
+struct P2pLayout {
+    size_t region, ecnt, cursor, bsum, bad, off, tiles, prow, psrc, ptok, pslot, a16, scales, total;
+};
+
+static P2pLayout p2p_layout(int64_t G, int64_t cap, int64_t K, int64_t e_loc, int64_t n_used) {
+    auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    const size_t rows = (size_t)(G * cap);
+    const size_t P = rows;                          // every (token, slot) pair goes to one owner
+    const size_t nb = (rows + P2PC - 1) / P2PC;
+    (void)n_used;
+    P2pLayout L{};
+    L.region = 0;
+    L.ecnt = al((size_t)(2 * G + 2) * 4);
+    L.cursor = L.ecnt + al((size_t)e_loc * 4);
+    L.bsum = L.cursor + al((size_t)e_loc * 4);
+    L.bad = L.bsum + al(nb * 4);
+    L.off = L.bad + al((nb + 1) * 4);
+    L.tiles = L.off + al((size_t)(e_loc + 1) * 4);
+    L.prow = L.tiles + al((size_t)(e_loc + 1) * 4);
+    L.psrc = L.prow + al(P * 4);
+    L.ptok = L.psrc + al(P * 4);
+    L.pslot = L.ptok + al(P * 4);
+    L.a16 = L.pslot + al(P * 4);
+    L.scales = L.a16 + al(P * (size_t)K * 2);
+    L.total = L.scales + al(P * 4);
+    return L;
+}
+
+}  // namespace b200
+
+extern "C" {
+
+// Export a device buffer for the other ranks: the IPC handle of the allocation that holds it and
+// the buffer's offset inside that allocation (allocators hand out pieces of larger blocks).
+int b200_ep_shared_export(const void* ptr, void* handle, size_t* offset) {
+    if (!ptr || !handle || !offset) return B200_E_INVALID;
+    using GetRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+    static GetRangeFn range = nullptr;
+    if (!range) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn)
+            return B200_E_CUDA;
+        range = reinterpret_cast<GetRangeFn>(fn);
+    }
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return B200_E_CUDA;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return B200_E_CUDA;
+    static_assert(sizeof(h) == B200_IPC_HANDLE_BYTES, "IPC handle size");
+    __builtin_memcpy(handle, &h, sizeof(h));
+    *offset = (size_t)(reinterpret_cast<CUdeviceptr>(ptr) - base);
+    return B200_OK;
+}
+
+// Map another rank's exported allocation; *base is its start in this process (add the offset).
+int b200_ep_shared_open(const void* handle, void** base) {
+    if (!handle || !base) return B200_E_INVALID;
+    cudaIpcMemHandle_t h;
+    __builtin_memcpy(&h, handle, sizeof(h));
+    return cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
+int b200_ep_shared_close(void* base) { return cudaIpcCloseMemHandle(base) == cudaSuccess ? B200_OK : B200_E_CUDA; }
+
+int b200_moe_ep_p2p_push(const void* send_a16, const float* send_scale, const int32_t* send_hdr, const int32_t* row_tok,
+                         const int32_t* counts, int64_t n_ranks, int64_t rank, int64_t n_used, int64_t K, int64_t cap,
+                         void* const* peer_recv_a16, int32_t* const* peer_recv_meta, int* const* peer_flags,
+                         int epoch, int64_t max_rows, void* stream) {
+    using namespace b200;
+    if (!send_a16 || !send_scale || !send_hdr || !row_tok || !counts || !peer_recv_a16 || !peer_recv_meta ||
+        !peer_flags || n_ranks <= 0 || rank < 0 || rank >= n_ranks || n_used <= 0 || K <= 0 || cap <= 0)
+        return B200_E_INVALID;
+    if (K % 8 || n_ranks > 64) return B200_E_UNSUPPORTED;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t gcap = (int64_t)device_sm_count() * 4;
+    const int64_t blocks = (max_rows + 7) / 8 < gcap ? (max_rows + 7) / 8 : gcap;
+    if (blocks > 0)
+        ep_push_kernel<<<(unsigned)blocks, P2P_THREADS, 0, st>>>(
+            static_cast<const __half*>(send_a16), send_scale, send_hdr, row_tok, counts, (int)n_ranks, (int)rank,
+            (int)n_used, (int)K, cap, reinterpret_cast<__half* const*>(peer_recv_a16), peer_recv_meta);
+    ep_signal_kernel<<<1, 64, 0, st>>>(peer_flags, 0, (int)rank, (int)n_ranks, epoch, counts);
+    return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
+size_t b200_moe_ep_p2p_expert_workspace_size(int64_t n_ranks, int64_t cap, int64_t K, int64_t n_local, int64_t n_used) {
+    if (n_ranks <= 0 || cap <= 0 || K <= 0 || n_local <= 0 || n_used <= 0) return 0;
+    return b200::p2p_layout(n_ranks, cap, K, n_local, n_used).total;
+}
+
+int b200_moe_ep_p2p_expert(int wtype, const void* local_stack, int64_t K, int64_t N, int64_t n_local, int64_t expert0,
+                           const void* recv_a16, const int32_t* recv_meta, const int* flags, int64_t n_ranks,
+                           int64_t rank, int64_t n_used, int64_t cap, int64_t pairs_hint, float* const* peer_ret,
+                           int64_t ret_nb1, int64_t ret_nb2, int* const* peer_flags, int epoch, void* workspace,
+                           size_t workspace_bytes, int* dev_err, void* stream) {
+    using namespace b200;
+    if (!local_stack || !recv_a16 || !recv_meta || !flags || !peer_ret || !peer_flags || !dev_err || K <= 0 ||
+        N <= 0 || n_local <= 0 || expert0 < 0 || n_ranks <= 0 || rank < 0 || rank >= n_ranks || n_used <= 0 ||
+        cap <= 0)
+        return B200_E_INVALID;
+    if (!weight_type_supported(wtype, K) || K % 32 != 0 || N % 16 != 0 || n_used > 32 || n_local > 4096 ||
+        n_ranks > 64 || (ret_nb1 % 16) || (ret_nb2 % 16))
+        return B200_E_UNSUPPORTED;
+    const P2pLayout L = p2p_layout(n_ranks, cap, K, n_local, n_used);
+    if (!workspace || workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+        return B200_E_WORKSPACE;
+    char* ws = static_cast<char*>(workspace);
+    int32_t* region = reinterpret_cast<int32_t*>(ws + L.region);
+    int32_t* ecnt = reinterpret_cast<int32_t*>(ws + L.ecnt);
+    int32_t* cursor = reinterpret_cast<int32_t*>(ws + L.cursor);
+    int32_t* bsum = reinterpret_cast<int32_t*>(ws + L.bsum);
+    int32_t* bad = reinterpret_cast<int32_t*>(ws + L.bad);
+    int32_t* off = reinterpret_cast<int32_t*>(ws + L.off);
+    int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
+    int32_t* prow = reinterpret_cast<int32_t*>(ws + L.prow);
+    int32_t* psrc = reinterpret_cast<int32_t*>(ws + L.psrc);
+    int32_t* ptok = reinterpret_cast<int32_t*>(ws + L.ptok);
+    int32_t* pslot = reinterpret_cast<int32_t*>(ws + L.pslot);
+    __half* a16 = reinterpret_cast<__half*>(ws + L.a16);
+    float* scales = reinterpret_cast<float*>(ws + L.scales);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int G = (int)n_ranks;
+    const int64_t rows_max = n_ranks * cap;
+    const int nb = (int)((rows_max + P2PC - 1) / P2PC);
+    const int bt = ep_token_tile_public(pairs_hint > 0 ? pairs_hint : rows_max / 2, n_local);
+    // 1. every source's rows have landed (their flags carry the counts)
+    ep_wait_kernel<<<1, 64, 0, st>>>(flags, 0, G, epoch, region, dev_err);
+    // 2. route the (row, slot) pairs by local expert
+    const size_t hist_smem = (size_t)n_local * sizeof(int);
+    if (hist_smem > 48 * 1024 &&
+        cudaFuncSetAttribute(p2p_route_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hist_smem) !=
+            cudaSuccess)
+        return B200_E_UNSUPPORTED;
+    if (cudaMemsetAsync(ecnt, 0, (size_t)n_local * 4, st) != cudaSuccess) return B200_E_CUDA;
+    p2p_route_count_kernel<<<nb, P2PC, hist_smem, st>>>(recv_meta, region, G, cap, (int)n_used, (int)expert0,
+                                                        (int)n_local, ecnt, bsum, bad);
+    ep_route_scan_public(ecnt, bsum, bad, nb, (int)n_local, bt, off, tiles, cursor, dev_err, st);
+    p2p_route_place_kernel<<<nb, P2PC, 0, st>>>(recv_meta, region, G, cap, (int)n_used, (int)expert0, bad + nb,
+                                                cursor, prow, psrc, ptok, pslot);
+    // 3. gather the fp16 rows in expert order
+    const int64_t gcap = (int64_t)device_sm_count() * 8;
+    p2p_gather_kernel<<<(unsigned)(rows_max < gcap ? rows_max : gcap), 256, 0, st>>>(
+        static_cast<const __half*>(recv_a16), recv_meta, prow, off + n_local, (int)n_used, (int)K, a16, scales);
+    if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
+    // 4. the grouped GEMM stores each output row into its home rank's ret over NVLink
+    const int rc = gemm_grouped_impl(wtype, local_stack, N, K, n_local, a16, scales, rows_max, bt, off, tiles, pslot,
+                                     ptok, nullptr, ret_nb1, ret_nb2, dev_err, st, psrc, peer_ret);
+    if (rc != B200_OK) return rc;
+    // 5. tell every home rank its rows are in place
+    ep_signal_kernel<<<1, 64, 0, st>>>(peer_flags, G, (int)rank, G, epoch, nullptr);
+    return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
+int b200_moe_ep_p2p_finish(const int* flags, int64_t n_ranks, int epoch, int* dev_err, void* stream) {
+    using namespace b200;
+    if (!flags || !dev_err || n_ranks <= 0 || n_ranks > 64) return B200_E_INVALID;
+    ep_wait_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(flags, (int)n_ranks, (int)n_ranks, epoch, nullptr,
+                                                                    dev_err);
+    return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
+}  // extern "C"

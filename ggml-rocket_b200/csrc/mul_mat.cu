@@ -468,8 +468,10 @@ cudaError_t launch_gemm_typed(int wtype, int bt, bool pair, const CUtensorMap& t
 int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int64_t n_expert, const __half* a16,
                       const float* scales, int64_t rows, int bt, const int32_t* off, const int32_t* tile_start,
                       const int32_t* slot, const int32_t* tok, float* dst, int64_t d_nb1, int64_t d_nb2, int* dev_err,
-                      cudaStream_t st) {
-    if ((d_nb1 % 16) || (d_nb2 % 16) || (reinterpret_cast<uintptr_t>(dst) & 15u)) return B200_E_UNSUPPORTED;
+                      cudaStream_t st, const int32_t* src, float* const* dst_bases) {
+    // dst_bases (a device array) replaces dst when rows go to several buffers
+    if ((d_nb1 % 16) || (d_nb2 % 16) || (!dst_bases && (!dst || (reinterpret_cast<uintptr_t>(dst) & 15u))))
+        return B200_E_UNSUPPORTED;
     CUtensorMap tmA, tmW, tmD;
     if (!make_tmap_2d_f16(&tmA, a16, (uint64_t)rows, (uint64_t)K, (uint64_t)K, (uint32_t)bt, GEMM_BK)) return B200_E_CUDA;
     GemmArgs a{};
@@ -490,6 +492,8 @@ int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int6
     a.n_expert = (int)n_expert;
     a.d_nb1 = d_nb1;
     a.d_nb2 = d_nb2;
+    a.g_src = src;
+    a.out_bases = dst_bases;
     const int sms = device_sm_count();
     const int64_t max_tiles = (rows + bt - 1) / bt + n_expert;
     const int64_t max_units = max_tiles * a.n_tiles_n;

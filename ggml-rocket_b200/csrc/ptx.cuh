@@ -214,6 +214,34 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
+// Exclusive scan of one int over the CTA (any multiple of 32 threads, all of them calling);
+// also returns the total. sh: 32 ints of shared memory, free again on return.
+__device__ __forceinline__ int block_excl_scan(int v, int* total, int* sh) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) sh[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < nw ? sh[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        sh[lane] = w;                                   // inclusive over warps
+    }
+    __syncthreads();
+    const int before = (warp > 0 ? sh[warp - 1] : 0) + x - v;
+    *total = sh[nw - 1];
+    __syncthreads();
+    return before;
+}
+
 // ---- programmatic dependent launch ----------------------------------------------------------
 // A kernel launched with programmatic stream serialization may start while the previous kernel
 // of the stream is still running; grid_dep_wait() blocks until that kernel has completed and its

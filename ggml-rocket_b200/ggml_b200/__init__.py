@@ -201,6 +201,17 @@ _SIGS.update({
     "b200_moe_ep_combine": (_int, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _vp]),
 })
 _SIGS.update({
+    "b200_ep_shared_export": (_int, [_vp, _vp, _c.POINTER(_sz)]),
+    "b200_ep_shared_open": (_int, [_vp, _c.POINTER(_vp)]),
+    "b200_ep_shared_close": (_int, [_vp]),
+    "b200_moe_ep_p2p_push": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _int,
+                                    _i64, _vp]),
+    "b200_moe_ep_p2p_expert_workspace_size": (_sz, [_i64] * 5),
+    "b200_moe_ep_p2p_expert": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                                      _i64, _vp, _i64, _i64, _vp, _int, _vp, _sz, _vp, _vp]),
+    "b200_moe_ep_p2p_finish": (_int, [_vp, _i64, _int, _vp, _vp]),
+})
+_SIGS.update({
     "b200_mul_mat_noalloc_max_workspace": (_sz, []),
     "b200_mul_mat_noalloc": (_int, [_int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp]),
     "b200_mul_mat_noalloc_error": (_int, [_vp, _c.POINTER(_int)]),

@@ -143,3 +143,96 @@ class ExpertParallelMulMatId:
                            "wire_bytes_out": S * (d.a16.shape[1] * d.a16.element_size() + 4 + 4 * d.hdr.shape[1])
                            + P_in * N * 4}
         return dst
+
+
+class PeerExpertParallelMulMatId:
+    """The same op as ExpertParallelMulMatId with both exchanges done by the library's kernels
+    over NVLink peer memory (b200_moe_ep_p2p_*): the dispatch pushes every packed row into its
+    owner's receive buffer, the owner's grouped GEMM stores every output row into its home rank's
+    return buffer, and flags with a per-op epoch order the steps -- no collective call and no
+    host synchronisation per op. torch.distributed is used once, at construction, to exchange
+    the buffers' IPC handles.
+
+    Sizes are fixed at construction: at most n_tokens_max tokens per rank, n_used slots, K_max
+    input and N_max output columns over the ops it will run. __call__ returns a view of the
+    return buffer holding dst [n_tokens, n_used, N] (valid until the next call), and copies it
+    into dst when one is given."""
+
+    def __init__(self, n_tokens_max, n_used, K_max, N_max, group=None, device=None, ops=None):
+        self.group = group
+        self.G = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.ops = ops if ops is not None else DeviceOps()
+        self.n_used, self.K_max, self.N_max = n_used, K_max, N_max
+        self.cap = n_tokens_max * n_used
+        G, dev = self.G, self.dev
+        self.recv_a16 = torch.zeros((G, self.cap, K_max), dtype=torch.float16, device=dev)
+        self.recv_meta = torch.zeros((G, self.cap, n_used + 3), dtype=torch.int32, device=dev)
+        self.ret = torch.zeros((n_tokens_max, n_used, N_max), dtype=torch.float32, device=dev)
+        self.flags = torch.zeros((2 * G, 4), dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        mine = [self._export(t) for t in (self.recv_a16, self.recv_meta, self.ret, self.flags)]
+        allh = [None] * G
+        dist.all_gather_object(allh, mine, group=group)
+        self._opened = []
+        ptrs = [[0] * G for _ in range(4)]
+        for q in range(G):
+            for b, t in enumerate((self.recv_a16, self.recv_meta, self.ret, self.flags)):
+                if q == self.rank:
+                    ptrs[b][q] = t.data_ptr()
+                else:
+                    handle, off = allh[q][b]
+                    base = g._c.c_void_p(0)
+                    hb = g._c.create_string_buffer(handle, len(handle))
+                    g.check(g.lib().b200_ep_shared_open(hb, g._c.byref(base)), "ep_shared_open")
+                    self._opened.append(base.value)
+                    ptrs[b][q] = base.value + off
+        self.peer = [torch.tensor(p, dtype=torch.int64, device=dev) for p in ptrs]
+        self.epoch = 0
+        self.last_stats = {}
+        dist.barrier(group=group)
+
+    @staticmethod
+    def _export(t):
+        h = g._c.create_string_buffer(64)
+        off = g._c.c_size_t(0)
+        g.check(g.lib().b200_ep_shared_export(g._ptr(t), h, g._c.byref(off)), "ep_shared_export")
+        return (h.raw, off.value)
+
+    def close(self):
+        """Unmap the other ranks' buffers (collective: every rank calls it)."""
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)
+        for base in self._opened:
+            g.lib().b200_ep_shared_close(g._c.c_void_p(base))
+        self._opened = []
+
+    def __call__(self, wtype, local_stack, K, N, n_expert, b, ne11, ids, dst=None, stream=None):
+        G, ops = self.G, self.ops
+        n_tokens, n_used = ids.shape
+        if n_expert % G or n_used != self.n_used or K > self.K_max or N > self.N_max or \
+                n_tokens * n_used > self.cap:
+            raise ValueError("op outside the sizes this exchange was built for")
+        n_local = n_expert // G
+        self.epoch += 1
+        d = ops.dispatch(ids, b, ne11, n_expert, G, K, stream=stream)
+        err = ops._err(self.dev)
+        lib = g.lib()
+        g.check(lib.b200_moe_ep_p2p_push(
+            g._ptr(d.a16), g._ptr(d.scale), g._ptr(d.hdr), g._ptr(d.row_tok), g._ptr(d.counts), G, self.rank,
+            n_used, K, self.cap, g._ptr(self.peer[0]), g._ptr(self.peer[1]), g._ptr(self.peer[3]), self.epoch,
+            n_tokens * n_used, g._stream(stream)), "moe_ep_p2p_push")
+        ws_bytes = lib.b200_moe_ep_p2p_expert_workspace_size(G, self.cap, K, n_local, n_used)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=self.dev)
+        g.check(lib.b200_moe_ep_p2p_expert(
+            wtype, g._ptr(local_stack), K, N, n_local, self.rank * n_local, g._ptr(self.recv_a16),
+            g._ptr(self.recv_meta), g._ptr(self.flags), G, self.rank, n_used, self.cap, n_tokens * n_used,
+            g._ptr(self.peer[2]), self.N_max * 4, n_used * self.N_max * 4, g._ptr(self.peer[3]), self.epoch,
+            g._ptr(ws), ws_bytes, g._ptr(err), g._stream(stream)), "moe_ep_p2p_expert")
+        g.check(lib.b200_moe_ep_p2p_finish(g._ptr(self.flags), G, self.epoch, g._ptr(err), g._stream(stream)),
+                "moe_ep_p2p_finish")
+        out = self.ret[:n_tokens, :, :N]
+        if dst is not None:
+            dst.copy_(out)
+        return out

@@ -197,6 +197,43 @@ int    b200_moe_ep_combine(const float * ret, int64_t N, const int32_t * send_hd
                            int64_t n_ranks, int64_t max_rows, float * dst, int64_t d_nb1, int64_t d_nb2,
                            void * stream);
 
+/* ---- MUL_MAT_ID expert parallelism over NVLink peer memory ----------------------------------
+ * No counterpart in the reference. The same op as the per-rank halves above, with the two
+ * exchanges done by the kernels' own stores into the other GPUs' buffers (no collective call, no
+ * host synchronisation). Each rank allocates, with the same sizes on every rank:
+ *   recv_a16  fp16 [n_ranks][cap][K]            rows other ranks push to it (cap = max rows one
+ *                                                source sends one owner, e.g. n_tokens*n_used)
+ *   recv_meta int32 [n_ranks][cap][n_used + 3]   {scale bits, slot mask, home token, ids}
+ *   ret       f32 [n_tokens][n_used][N]          its own op output (dst's layout, strides given)
+ *   flags     int32 [2 * n_ranks][4], zeroed once
+ * and maps the other ranks' ones (b200_ep_shared_export on the owner, _open on the others).
+ * peer_* arguments are device arrays of n_ranks device pointers (entry r = rank r's buffer as
+ * mapped in this process). Per op, with an epoch that grows by one per op on every rank:
+ *   home   b200_moe_ep_dispatch, then b200_moe_ep_p2p_push (rows into their owners' recv_a16 /
+ *          recv_meta, counts into their flags)
+ *   owner  b200_moe_ep_p2p_expert (waits for every source, runs the grouped GEMM whose
+ *          epilogue stores each output row into its home rank's ret, then flags every home)
+ *   home   b200_moe_ep_p2p_finish (waits for every owner): ret holds the op's dst.
+ * Every wait is bounded (a rank that never arrives ends the op with a device error). */
+#define B200_IPC_HANDLE_BYTES 64
+int    b200_ep_shared_export(const void * ptr, void * handle, size_t * offset);
+int    b200_ep_shared_open(const void * handle, void ** base);
+int    b200_ep_shared_close(void * base);
+int    b200_moe_ep_p2p_push(const void * send_a16, const float * send_scale, const int32_t * send_hdr,
+                            const int32_t * row_tok, const int32_t * counts, int64_t n_ranks, int64_t rank,
+                            int64_t n_used, int64_t K, int64_t cap, void * const * peer_recv_a16,
+                            int32_t * const * peer_recv_meta, int * const * peer_flags, int epoch,
+                            int64_t max_rows, void * stream);
+size_t b200_moe_ep_p2p_expert_workspace_size(int64_t n_ranks, int64_t cap, int64_t K, int64_t n_local,
+                                             int64_t n_used);
+int    b200_moe_ep_p2p_expert(int wtype, const void * local_stack, int64_t K, int64_t N, int64_t n_local,
+                              int64_t expert0, const void * recv_a16, const int32_t * recv_meta,
+                              const int * flags, int64_t n_ranks, int64_t rank, int64_t n_used, int64_t cap,
+                              int64_t pairs_hint, float * const * peer_ret, int64_t ret_nb1, int64_t ret_nb2,
+                              int * const * peer_flags, int epoch, void * workspace, size_t workspace_bytes,
+                              int * dev_err, void * stream);
+int    b200_moe_ep_p2p_finish(const int * flags, int64_t n_ranks, int epoch, int * dev_err, void * stream);
+
 #ifdef __cplusplus
 }
 #endif

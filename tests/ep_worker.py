@@ -1,6 +1,7 @@
-"""One rank of the two-GPU expert-parallel MUL_MAT_ID check (launched by test_gpu_moe_ep.py
-through torchrun): the NCCL path of ggml_b200.ep must reproduce, bit for bit, the single-GPU
-b200_mul_mat_id result for this rank's tokens over the full expert stack."""
+"""One rank of the expert-parallel MUL_MAT_ID check (launched by test_gpu_moe_ep.py through
+torchrun, one or two GPUs): the NCCL path and the peer-memory path of ggml_b200.ep must both
+reproduce, bit for bit, the single-GPU b200_mul_mat_id result for this rank's tokens over the
+full expert stack."""
 import datetime
 import os
 import sys
@@ -24,6 +25,8 @@ def main():
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     ok = True
+    from ggml_b200.ep import PeerExpertParallelMulMatId
+    p2p = PeerExpertParallelMulMatId(n_tokens_max=256, n_used=8, K_max=2048, N_max=768)
     for (wtype, K, N, E, n_used, ne11, T) in [(12, 2048, 768, 32, 8, 1, 256), (12, 768, 256, 32, 8, 8, 96 + 31 * rank)]:
         rng = np.random.default_rng(7)
         w = (rng.standard_normal((E * N, K)) * 0.02).astype(np.float32)
@@ -55,7 +58,19 @@ def main():
         if not same:
             print(f"rank {rank} case {(wtype, K, N, E, n_used, ne11, T)} mismatch: "
                   f"{float((dst - want).abs().max())}", flush=True)
+        # the same op with both exchanges over peer memory (twice: the buffers are reused)
+        for rep in range(2):
+            perr = torch.zeros(1, dtype=torch.int32, device="cuda")
+            p2p.ops.dev_err = perr
+            got = p2p(wtype, local_stack, K, N, E, b, ne11, ids)
+            torch.cuda.synchronize()
+            p_same = int(perr.item()) == 0 and bool(torch.equal(got, want))
+            if not p_same:
+                print(f"rank {rank} p2p case {(wtype, K, N, E, n_used, ne11, T)} rep {rep} mismatch: err "
+                      f"{int(perr.item())} max {float((got - want).abs().max())}", flush=True)
+            same = same and p_same
         ok = ok and same
+    p2p.close()
     dist.barrier()
     dist.destroy_process_group()
     if ok:

@@ -3,8 +3,9 @@
 The exchanges are emulated inside one process (rank r's send rows for rank q are handed to q
 by slicing), so the G-rank kernel contract is checked on a single B200: every rank's dst must
 equal the single-GPU b200_mul_mat_id result for its tokens over the full expert stack, and the
-CPU oracle within the MUL_MAT tolerance. With two or more GPUs the same op also runs for real as
-torchrun ranks over NCCL (ep_worker.py).
+CPU oracle within the MUL_MAT tolerance. The op also runs as torchrun ranks (ep_worker.py)
+through both exchange paths -- NCCL all-to-all and the kernels' own stores into peer memory --
+with one rank always and with two when two GPUs are present.
 """
 import os
 import socket
@@ -129,18 +130,28 @@ def test_ep_bad_expert_id_sets_error(cuda):
     assert int(d.counts[-2].item()) == 0
 
 
-def test_ep_nccl_two_gpus(cuda):
-    import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+def _run_worker(nproc):
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "10", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
+           f"--nproc-per-node={nproc}", "--master-addr=127.0.0.1", f"--master-port={port}",
            os.path.join(ROOT, "tests", "ep_worker.py")]
     p = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=360)
     assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
-    assert p.stdout.count("EP_OK") == 2, p.stdout[-2000:]
+    assert p.stdout.count("EP_OK") == nproc, p.stdout[-2000:]
+
+
+def test_ep_one_rank_nccl_and_peer_paths(cuda):
+    """Both exchange paths with a single rank (every expert local): the push, flag, route and
+    epilogue-store kernels of the peer-memory path run on one GPU."""
+    _run_worker(1)
+
+
+def test_ep_two_gpus_nccl_and_peer_paths(cuda):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    _run_worker(2)
