@@ -60,6 +60,9 @@ def parse():
                     help="gemm: the headline MUL_MAT sweep (default); moe: the MUL_MAT_ID layer of "
                          "BASELINE configs[3], expert-parallel over the ranks; fa: the FLASH_ATTN_EXT "
                          "prefill of configs[2]")
+    ap.add_argument("--ep", choices=["peer", "nccl"], default="peer",
+                    help="moe workload on several GPUs: exchanges by the kernels' own stores into peer "
+                         "memory (default) or by NCCL all-to-all")
     return ap.parse_args()
 
 
@@ -439,7 +442,7 @@ def run_moe(args):
     y_down = torch.empty((T, top, H), device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    if world > 1:
+    if world > 1 and args.ep == "nccl":
         from ggml_b200.ep import DeviceOps, ExpertParallelMulMatId
         ep = ExpertParallelMulMatId(ops=DeviceOps(err))
 
@@ -447,6 +450,16 @@ def run_moe(args):
             ep(wt, w_gate, H, F, E, x, 1, ids, y_gate)
             ep(wt, w_up, H, F, E, x, 1, ids, y_up)
             ep(wt, w_down, F, H, E, h, top, ids, y_down)
+    elif world > 1:
+        from ggml_b200.ep import DeviceOps, PeerExpertParallelMulMatId
+        ep = PeerExpertParallelMulMatId(T, top, max(H, F), max(H, F), ops=DeviceOps(err))
+
+        def layer():
+            # each op's result is a view of the exchange's return buffer; consume it (copy into
+            # the layer's tensor) before the next op reuses that buffer
+            y_gate.copy_(ep(wt, w_gate, H, F, E, x, 1, ids))
+            y_up.copy_(ep(wt, w_up, H, F, E, x, 1, ids))
+            y_down.copy_(ep(wt, w_down, F, H, E, h, top, ids))
     else:
         ws = torch.empty(max(g.mul_mat_id_workspace_size(H, F, E, top, T), g.mul_mat_id_workspace_size(F, H, E, top, T)),
                          dtype=torch.uint8, device=dev)
@@ -493,7 +506,9 @@ def run_moe(args):
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
                 "config": {"workload": "BASELINE configs[3] MoE layer, 2048 tokens per rank, experts split "
-                                       f"{E}/{world} per rank" + (" (NCCL all-to-all)" if world > 1 else ""),
+                                       f"{E}/{world} per rank" +
+                                       ((" (NCCL all-to-all)" if args.ep == "nccl" else
+                                         " (exchanges by kernel stores into NVLink peer memory)") if world > 1 else ""),
                            "weights": "16 distinct N(0,0.02) Q4_K experts per stack, repeated to 128",
                            "median_of_steps": True},
                 "tflops": tf,
