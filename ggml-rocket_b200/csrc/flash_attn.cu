@@ -262,7 +262,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
         for (int k = threadIdx.x; k < FA_SPLIT * 128; k += FA_THREADS) seql[k] = 0;
     }
     tc_fence_before();
-    __syncthreads();
+    cta_sync();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -554,7 +554,7 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
     }
 
     tc_fence_before();
-    __syncthreads();
+    cta_sync();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);

@@ -10,8 +10,9 @@
 // Warp roles in one CTA (persistent over work units):
 //   warp 0        TMA producer of the activation tile [BT x 64]
 //   warp 1        TMEM allocator and the single-thread tcgen05.mma issuer
-//   warps 2..5    epilogue: TMEM -> registers -> a 32x32 shared-memory transpose -> scaled
-//                 16-byte stores of whole 128-byte output lines (or of a stream-K partial)
+//   warps 2..5    epilogue: TMEM -> registers -> scaled into a 32 x 32 shared-memory box ->
+//                 one TMA store per box (grouped mode: 16-byte stores of whole 128-byte lines
+//                 of the scattered rows); a stream-K partial goes straight from registers
 //   warp 6        TMA producer of the F16 weight tile, or (quantized weights) of the raw
 //                 quantized super-block tile: 128 rows x 256 weights into a 2-3 deep ring,
 //                 with the TMA's L2 prefetch running 4 super-blocks further ahead
@@ -139,7 +140,7 @@ struct GemmCfg {
 template <int BT, int WT, bool GROUPED, bool PAIR>
 __global__ void __launch_bounds__(GemmCfg<BT, WT, PAIR>::THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-            const __grid_constant__ CUtensorMap tmD, const GemmArgs args) {
+            const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmO, const GemmArgs args) {
     static_assert(!(GROUPED && PAIR), "the grouped GEMM runs one CTA per tile");
     using C = GemmCfg<BT, WT, PAIR>;
     using RC = RawCfg<WT>;
@@ -206,24 +207,17 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
     tc_fence_before();
     if constexpr (PAIR) cluster_sync();   // the peer's barriers exist before anything arrives on them
-    else __syncthreads();
+    else cta_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    // Everything above overlapped the previous kernel of the stream (programmatic launch); from
-    // here on this grid reads and writes global memory, so it waits for that kernel to finish,
-    // then lets the next kernel begin its own launch.
-    grid_dep_wait();
-    grid_dep_launch();
 
     const int ntt = args.n_tiles_t, ntn = args.n_tiles_n;
     // Work cursor: the grouped mode walks units blockIdx.x, +gridDim.x, ...; stream-K walks this
     // CTA's granule range [g_beg, g_end) from its end backwards, so the pieces other CTAs finish
     // (at the end of the range) come first and the piece this CTA finishes, whose partials come
     // from lower-numbered CTAs, comes last.
-    int64_t num_units = 0, g_beg = 0, g_end = 0;
-    if constexpr (GROUPED) {
-        num_units = (int64_t)__ldg(args.g_tile_start + args.n_expert) * ntn;
-    } else {
+    int64_t num_units = 0, g_beg = 0, g_end = 0;   // num_units (grouped): set after the wait below
+    if constexpr (!GROUPED) {
         g_beg = (int64_t)unit_id * args.total_g / n_units_grid;
         g_end = (int64_t)(unit_id + 1) * args.total_g / n_units_grid;
     }
@@ -269,6 +263,28 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         }
         return c;
     };
+
+    // Everything above overlapped the previous kernel of the stream (programmatic launch). The
+    // weights are not that kernel's output, so the weight producer first starts its first
+    // tile's weights on their way into L2 (a prefetch only warms L2, the point of coherence, so
+    // it cannot return stale data). From here on the grid reads and writes global memory: it
+    // waits for the previous kernel to finish, then lets the next one begin its launch.
+    if constexpr (!GROUPED) {
+        if (warp == W_WPROD && lane == 0 && cursor_ok(cursor0)) {
+            const UnitCoords uc = unit_coords(cursor0);
+            if constexpr (C::QUANT) {
+                const int sb0 = uc.kb0 >> 2, sb_end = (uc.kb1 + 3) >> 2;
+                for (int pf = sb0; pf < sb0 + RC::PREFETCH && pf < sb_end; pf++)
+                    tma_prefetch_l2_2d(&tmW, pf * RC::X_ELEMS, uc.wrow0);
+            } else {
+                for (int kb = uc.kb0; kb < uc.kb0 + 2 * STAGES && kb < uc.kb1; kb++)
+                    tma_prefetch_l2_2d(&tmW, kb * GEMM_BK, uc.wrow0);
+            }
+        }
+    }
+    grid_dep_wait();
+    grid_dep_launch();
+    if constexpr (GROUPED) num_units = (int64_t)__ldg(args.g_tile_start + args.n_expert) * ntn;
 
     // One operand's TMA producer over the A/W stage ring (W only for F16 weights).
     auto produce_stages = [&](bool is_w) {
@@ -397,10 +413,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         }
     } else if (warp >= W_EPI0 && warp < W_EPI0 + 4) {
         // ---------------- epilogue ----------------
+        // Thread i of warp q owns TMEM lane (weight row) 32q + i and reads its tokens 16 at a time
+        // (tcgen05.ld 32x32b.x16), the next 16 already in flight while the current ones are
+        // stored. Every store is one token's 32 consecutive rows: 128 contiguous bytes per warp.
+        constexpr int NG = BT / 32;                      // 32-token groups (one value per lane)
         const int q = warp & 3;                          // TMEM lane quadrant this warp may read
-        float* es = reinterpret_cast<float*>(smem + C::EPI_OFF) + (warp - W_EPI0) * 1024;
-        const float4* es4 = reinterpret_cast<const float4*>(es);
-        const int cc = lane & 7;                         // float4 column of the read-back
         const uint32_t lane_tmem = tmem_base + ((uint32_t)(32 * q) << 16);
         int lt = 0;
         for (int64_t cur = cursor0; cursor_ok(cur); lt++) {
@@ -443,9 +460,29 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     with_part = true;
                 }
             }
+            // Per-token values of a finished tile, fetched before the accumulator is ready: lane
+            // i holds those of tokens 32g + i and hands them to the storing lanes by shuffle.
+            float scl[NG];
+            uint64_t rowp[GROUPED ? NG : 1];
+            if (uc.finishes) {
+#pragma unroll
+                for (int g = 0; g < NG; g++) {
+                    const int t = uc.t0 + 32 * g + lane;
+                    const bool live = 32 * g < ntok && t < uc.t_end;
+                    scl[g] = live ? __ldg(args.scales + t) : 0.0f;
+                    if constexpr (GROUPED) {
+                        const char* ob = reinterpret_cast<const char*>(
+                            args.g_src && live ? args.out_bases[__ldg(args.g_src + t)] : args.out);
+                        rowp[g] = live ? reinterpret_cast<uint64_t>(ob + (int64_t)__ldg(args.g_tok + t) * args.d_nb2 +
+                                                                   (int64_t)__ldg(args.g_slot + t) * args.d_nb1)
+                                       : 0ull;
+                    }
+                }
+            }
             if (!mbar_wait(tfull_bar(acc), aphase, args.err, ERR_WAIT_EPILOGUE, abort_flag)) break;
             tc_fence_after();
-            if (!uc.finishes) {
+            const bool fin = uc.finishes;
+            if (!fin) {
                 // A piece another CTA finishes: this warp's 32 weight rows of the unscaled
                 // partial, stored [token][128] f32 straight from TMEM (coalesced per token).
                 float* p = args.partials + (size_t)blockIdx.x * (BT * GEMM_BN) + 32 * q + lane;
@@ -456,15 +493,24 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 #pragma unroll
                     for (int j = 0; j < 32; j++) __stcg(p + (size_t)(c0 + j) * GEMM_BN, __uint_as_float(r[j]));
                 }
-                __threadfence();
-                __syncwarp();
-                if (lane == 0) st_release_gpu(args.flags + 4 * blockIdx.x + q, args.epoch);
             } else {
-                const int nb = uc.n0 + 32 * q + 4 * cc;  // this lane's 4 output columns
+                // 32 tokens at a time, through this warp's 32 x 32 f32 box of shared memory
+                float* es = reinterpret_cast<float*>(smem + C::EPI_OFF) + (warp - W_EPI0) * 1024;
+                const float4* es4 = reinterpret_cast<const float4*>(es);
+                const int cc = lane & 7;                 // float4 column of the read-back (grouped)
+                const int nb = uc.n0 + 32 * q + 4 * cc;  // this lane's 4 output columns (grouped)
+                const uint32_t es_addr = smem_u32(es);
                 for (int c0 = 0; c0 < ntok; c0 += 32) {
-                    // the scale of token c0 + lane, handed to the storing lanes by shuffle
-                    const int tl = uc.t0 + c0 + lane;
-                    const float sc_lane = tl < uc.t_end ? __ldg(args.scales + tl) : 0.0f;
+                    const int g = c0 >> 5;
+                    float sg = scl[0];
+                    uint64_t rg = GROUPED ? rowp[0] : 0ull;
+#pragma unroll
+                    for (int i = 1; i < NG; i++) {
+                        if (g == i) {
+                            sg = scl[i];
+                            if constexpr (GROUPED) rg = rowp[i];
+                        }
+                    }
                     uint32_t r[32];
                     tmem_ld32(lane_tmem + (uint32_t)(acc * BT + c0), r);
                     if (with_part) {
@@ -476,31 +522,45 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     } else {
                         tmem_ld_wait();
                     }
+                    if constexpr (!GROUPED) {
+                        // the scaled [token][32 rows] box, then one TMA store of it (rows past
+                        // M and columns past N are clipped by the tensor map)
+                        if (lane == 0) bulk_wait_read_all();     // the previous box has been read
+                        __syncwarp();
 #pragma unroll
-                    for (int j = 0; j < 32; j++) es[j * 32 + lane] = __uint_as_float(r[j]);
-                    __syncwarp();
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        const int jr = (lane >> 3) + 4 * i;
-                        const int t = uc.t0 + c0 + jr;
-                        const float sc = __shfl_sync(0xffffffffu, sc_lane, jr);
-                        if (t < uc.t_end && nb < args.N) {
-                            float4 v = es4[jr * 8 + cc];
-                            v.x *= sc; v.y *= sc; v.z *= sc; v.w *= sc;
-                            float* dp;
-                            if constexpr (GROUPED) {
-                                float* ob = args.g_src ? args.out_bases[__ldg(args.g_src + t)] : args.out;
-                                dp = reinterpret_cast<float*>(reinterpret_cast<char*>(ob) +
-                                                              (int64_t)__ldg(args.g_tok + t) * args.d_nb2 +
-                                                              (int64_t)__ldg(args.g_slot + t) * args.d_nb1) + nb;
-                            }
-                            else
-                                dp = args.out + (size_t)t * args.ldo + nb;
-                            *reinterpret_cast<float4*>(dp) = v;
+                        for (int j = 0; j < 32; j++)
+                            es[j * 32 + lane] = __uint_as_float(r[j]) * __shfl_sync(0xffffffffu, sg, j);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&tmO, es_addr, uc.n0 + 32 * q, uc.t0 + c0);
+                            bulk_commit();
                         }
+                    } else {
+                        // scattered rows: a transpose, then 16-byte stores, each instruction
+                        // four whole 128-byte output lines
+#pragma unroll
+                        for (int j = 0; j < 32; j++) es[j * 32 + lane] = __uint_as_float(r[j]);
+                        __syncwarp();
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const int jr = (lane >> 3) + 4 * i;
+                            const float sc = __shfl_sync(0xffffffffu, sg, jr);
+                            const uint64_t rp = __shfl_sync(0xffffffffu, rg, jr);
+                            if (rp && nb < args.N) {
+                                float4 v = es4[jr * 8 + cc];
+                                v.x *= sc; v.y *= sc; v.z *= sc; v.w *= sc;
+                                *reinterpret_cast<float4*>(reinterpret_cast<float*>(rp) + nb) = v;
+                            }
+                        }
+                        __syncwarp();
                     }
-                    __syncwarp();
                 }
+            }
+            if (!fin) {
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) st_release_gpu(args.flags + 4 * blockIdx.x + q, args.epoch);
             }
             if constexpr (GROUPED) {
                 // rows stored into other GPUs' memory must be visible there before the kernel
@@ -511,6 +571,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             __syncwarp();
             if (lane == 0) arrive_leader(tempty_bar(acc));
         }
+        if (lane == 0) bulk_wait_all();   // this warp's output stores are complete before it exits
     } else if (C::QUANT && dequant_slot(warp) >= 0) {
         // ---------------- dequant (quantized weights) ----------------
         if constexpr (C::QUANT) {
@@ -559,7 +620,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     // a pair: neither CTA leaves while the leader's MMAs may still read the peer's shared memory
     // or write its TMEM (the leader's MMA thread passes here only after its drain)
     if constexpr (PAIR) cluster_sync();
-    else __syncthreads();
+    else cta_sync();
     if (warp == W_MMA) {
         tc_fence_after();
         if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);

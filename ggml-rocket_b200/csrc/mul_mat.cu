@@ -249,6 +249,18 @@ static bool make_tmap_2d_u16(CUtensorMap* map, const void* base, uint64_t rows, 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The f32 output [rows, cols] (cols innermost, row pitch in bytes) as 32 x 32 store boxes.
+static bool make_tmap_2d_f32_out(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols, uint64_t pitch_bytes) {
+    EncodeTiledFn fn = get_encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {pitch_bytes};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // The launch plan for one MUL_MAT: token tile and the stream-K granule split.
@@ -270,12 +282,31 @@ static int pair_knob() {
     return v;
 }
 
+// B200_GEMM_TILE: unset = the cost model's token tile; 32 / 64 / 128 / 256 = that tile.
+static int tile_knob() {
+    static const int v = [] {
+        const char* e = getenv("B200_GEMM_TILE");
+        return (e && *e) ? atoi(e) : 0;
+    }();
+    return v;
+}
+
+// B200_GEMM_STREAMK: unset / 1 = stream-K over every SM; 0 = one whole tile per CTA whenever the
+// tiles fit in one wave (no partials, idle SMs allowed).
+static int streamk_knob() {
+    static const int v = [] {
+        const char* e = getenv("B200_GEMM_STREAMK");
+        return (e && *e) ? atoi(e) : 1;
+    }();
+    return v;
+}
+
 // Choose the token tile from a cost model (SM clocks). Per 64-wide K block a tile costs the
 // slowest of the tensor core (128 x BT x 64 MACs at 4096 MAC/clk), the decode of 8192 quantized
 // weights by the dequant warps, and the L2 feed of its operand tiles. Stream-K spreads the
 // tiles' K blocks evenly over the grid, so the time is the total over the grid plus a fixed
 // cost per work item and, where tiles are shared, the partial-tile round trip.
-static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms, int wtype) {
+static GemmPlan plan_gemm_knobs(int64_t M, int64_t N, int64_t K, int sms, int wtype, int tile) {
     const bool quant = wtype != WT_F16;
     const int nkb = (int)((K + GEMM_BK - 1) / GEMM_BK);
     const int gran = quant ? 4 : 1;
@@ -293,11 +324,13 @@ static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms, int wtype) {
             const int bt = bts[bi];
             if (bi > 0 && bts[bi - 1] >= M) break;      // a smaller tile already covers M
             if (pair && bt < 128) continue;              // each CTA of a pair stages >= 64 tokens
+            if (tile > 0 && bt != tile) continue;
             const int ntt = (int)((M + bt - 1) / bt);
             const int64_t tiles = (int64_t)ntn * ntt;
             const int64_t total_g = tiles * tile_g;
             const int per_unit = pair ? 2 : 1;           // CTAs per work unit
-            const int units = (int)(total_g < sms / per_unit ? total_g : sms / per_unit);
+            int units = (int)(total_g < sms / per_unit ? total_g : sms / per_unit);
+            if (streamk_knob() == 0 && tiles <= units) units = (int)tiles;
             // per SM and 64-wide K block: tensor-core clocks (128 x BT x 64 MACs at 4096 MAC/clk),
             // the decode of 8192 quantized weights, and shared-memory bytes (TMA writes + MMA
             // reads, 128 B/clk): the activation tile is halved in a pair
@@ -334,6 +367,12 @@ static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms, int wtype) {
     return best;
 }
 
+static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms, int wtype) {
+    GemmPlan p = plan_gemm_knobs(M, N, K, sms, wtype, tile_knob());
+    if (p.bt == 0) p = plan_gemm_knobs(M, N, K, sms, wtype, 0);   // the forced tile does not apply
+    return p;
+}
+
 // Stream-K scratch: one partial tile per CTA, then four flags per CTA; none when every CTA
 // owns whole tiles.
 static size_t streamk_partials_bytes(const GemmPlan& p) { return (size_t)p.grid * p.bt * GEMM_BN * 4; }
@@ -365,7 +404,7 @@ static MulMatWorkspace mm_workspace_layout(int64_t M, int64_t N, int64_t K, cons
 
 template <int BT, int WT, bool GROUPED, bool PAIR>
 static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmD,
-                                 const GemmArgs& a, int grid, cudaStream_t st) {
+                                 const CUtensorMap& tmO, const GemmArgs& a, int grid, cudaStream_t st) {
     using C = GemmCfg<BT, WT, PAIR>;
     static bool attr_set[64] = {false};
     int dev = 0;
@@ -398,26 +437,26 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW,
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    return cudaLaunchKernelEx(&cfg, gemm_kernel<BT, WT, GROUPED, PAIR>, tmA, tmW, tmD, a);
+    return cudaLaunchKernelEx(&cfg, gemm_kernel<BT, WT, GROUPED, PAIR>, tmA, tmW, tmD, tmO, a);
 }
 
 template <int WT, bool GROUPED>
 static cudaError_t launch_gemm_bt(int bt, bool pair, const CUtensorMap& tmA, const CUtensorMap& tmW,
-                                  const CUtensorMap& tmD, const GemmArgs& a, int grid, cudaStream_t st) {
+                                  const CUtensorMap& tmD, const CUtensorMap& tmO, const GemmArgs& a, int grid, cudaStream_t st) {
     if constexpr (!GROUPED) {
         if (pair) {
             switch (bt) {
-                case 128: return launch_gemm_t<128, WT, false, true>(tmA, tmW, tmD, a, grid, st);
-                case 256: return launch_gemm_t<256, WT, false, true>(tmA, tmW, tmD, a, grid, st);
+                case 128: return launch_gemm_t<128, WT, false, true>(tmA, tmW, tmD, tmO, a, grid, st);
+                case 256: return launch_gemm_t<256, WT, false, true>(tmA, tmW, tmD, tmO, a, grid, st);
                 default: return cudaErrorInvalidValue;
             }
         }
     }
     switch (bt) {
-        case 32: return launch_gemm_t<32, WT, GROUPED, false>(tmA, tmW, tmD, a, grid, st);
-        case 64: return launch_gemm_t<64, WT, GROUPED, false>(tmA, tmW, tmD, a, grid, st);
-        case 128: return launch_gemm_t<128, WT, GROUPED, false>(tmA, tmW, tmD, a, grid, st);
-        default: return launch_gemm_t<256, WT, GROUPED, false>(tmA, tmW, tmD, a, grid, st);
+        case 32: return launch_gemm_t<32, WT, GROUPED, false>(tmA, tmW, tmD, tmO, a, grid, st);
+        case 64: return launch_gemm_t<64, WT, GROUPED, false>(tmA, tmW, tmD, tmO, a, grid, st);
+        case 128: return launch_gemm_t<128, WT, GROUPED, false>(tmA, tmW, tmD, tmO, a, grid, st);
+        default: return launch_gemm_t<256, WT, GROUPED, false>(tmA, tmW, tmD, tmO, a, grid, st);
     }
 }
 
@@ -453,12 +492,12 @@ static bool setup_weight_maps(int wtype, const void* w_packed, int64_t wrows, in
 
 template <bool GROUPED>
 cudaError_t launch_gemm_typed(int wtype, int bt, bool pair, const CUtensorMap& tmA, const CUtensorMap& tmW,
-                              const CUtensorMap& tmD, const GemmArgs& a, int grid, cudaStream_t st) {
+                              const CUtensorMap& tmD, const CUtensorMap& tmO, const GemmArgs& a, int grid, cudaStream_t st) {
     switch (wtype) {
-        case WT_F16: return launch_gemm_bt<WT_F16, GROUPED>(bt, pair, tmA, tmW, tmD, a, grid, st);
-        case WT_Q4_K: return launch_gemm_bt<WT_Q4_K, GROUPED>(bt, pair, tmA, tmW, tmD, a, grid, st);
-        case WT_Q6_K: return launch_gemm_bt<WT_Q6_K, GROUPED>(bt, pair, tmA, tmW, tmD, a, grid, st);
-        case WT_Q8_0: return launch_gemm_bt<WT_Q8_0, GROUPED>(bt, pair, tmA, tmW, tmD, a, grid, st);
+        case WT_F16: return launch_gemm_bt<WT_F16, GROUPED>(bt, pair, tmA, tmW, tmD, tmO, a, grid, st);
+        case WT_Q4_K: return launch_gemm_bt<WT_Q4_K, GROUPED>(bt, pair, tmA, tmW, tmD, tmO, a, grid, st);
+        case WT_Q6_K: return launch_gemm_bt<WT_Q6_K, GROUPED>(bt, pair, tmA, tmW, tmD, tmO, a, grid, st);
+        case WT_Q8_0: return launch_gemm_bt<WT_Q8_0, GROUPED>(bt, pair, tmA, tmW, tmD, tmO, a, grid, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -499,7 +538,7 @@ int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int6
     const int64_t max_units = max_tiles * a.n_tiles_n;
     const int grid = (int)(max_units < sms ? max_units : sms);
     if (grid <= 0) return B200_OK;
-    return launch_gemm_typed<true>(wtype, bt, false, tmA, tmW, tmD, a, grid, st) == cudaSuccess ? B200_OK : B200_E_CUDA;
+    return launch_gemm_typed<true>(wtype, bt, false, tmA, tmW, tmD, tmA, a, grid, st) == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 
 size_t packed_weight_bytes(int type, int64_t N, int64_t K, size_t* plane_d_off) {
@@ -567,7 +606,9 @@ int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, cons
     a.gran = p.gran;
     a.tile_g = p.tile_g;
     a.total_g = p.total_g;
-    const cudaError_t e = launch_gemm_typed<false>(wtype, p.bt, p.pair, tmA, tmW, tmD, a, p.grid, st);
+    CUtensorMap tmO;
+    if (!make_tmap_2d_f32_out(&tmO, dst, (uint64_t)M, (uint64_t)N, (uint64_t)ldd * 4)) return B200_E_CUDA;
+    const cudaError_t e = launch_gemm_typed<false>(wtype, p.bt, p.pair, tmA, tmW, tmD, tmO, a, p.grid, st);
     return e == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 

@@ -183,6 +183,18 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 }
 
 // Prefetch the 2-D box at (x, y) into L2 (no shared-memory destination, no completion).
+// 2-D tiled TMA store of a shared-memory box (bulk group; the caller commits and waits).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the stores committed so far have read their shared-memory source
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// ... and have completed
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t x, int32_t y) {
     asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
                  ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y)
@@ -258,9 +270,18 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
     return r;
 }
 
-// All threads of both CTAs of the cluster (release / acquire at cluster scope).
+// All threads of both CTAs of the cluster (release / acquire at cluster scope). The non-aligned
+// form: the threads of a warp may arrive at different times (a role run by lane 0 alone).
 __device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Every thread of the CTA, counted one by one. Warp-specialised kernels reach their closing
+// barrier with divergent warps (lane 0 still in a producer or MMA loop while lanes 1-31 are
+// already there); the aligned barrier behind __syncthreads() may count such a warp as arrived
+// when its first lanes get there, releasing the CTA before the warp's lane 0 is done.
+__device__ __forceinline__ void cta_sync() {
+    asm volatile("barrier.sync 0;" ::: "memory");
 }
 
 // The shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster.
