@@ -53,7 +53,7 @@ def step_flops(m=M_TOKENS):
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["gemm", "moe", "fa"], default="gemm",
@@ -94,7 +94,7 @@ def profile_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms during the timed region."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -108,7 +108,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=self.out, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -116,7 +116,6 @@ class ClockSampler:
     def stop(self):
         if self.proc is None:
             return None
-        time.sleep(0.25)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -172,22 +171,28 @@ def run_reference(args):
     import oracle
     oracle.build()
     ws, acts = make_host_inputs(0xB200, CPU_SAMPLE_ROWS)
+    tw = time.perf_counter()
     for _ in range(args.warmup):
         cpu_oracle_step(ws, acts)
+    t_step = (time.perf_counter() - tw) / max(args.warmup, 1)
+    # a CPU step takes ~0.3 s: time as many of the requested steps as fit in ~30 s
+    steps = max(1, min(args.steps, int(30.0 / max(t_step, 1e-3))))
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(steps):
         cpu_oracle_step(ws, acts)
-    dt = (time.perf_counter() - t0) / args.steps
+    dt = (time.perf_counter() - t0) / steps
     val = step_flops(CPU_SAMPLE_ROWS) / dt / 1e12
     cores = os.cpu_count()
     line = {
         "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "steps": steps, "steps_requested": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
         "config": {"workload": WORKLOAD, "sample": f"{CPU_SAMPLE_ROWS} of the 512 tokens per step",
                    "global_batch": M_TOKENS, "parallelism": "host threads"},
         "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                         "sample": f"{CPU_SAMPLE_ROWS} token rows x 3 shapes per step"},
+                         "sample": f"{CPU_SAMPLE_ROWS} token rows x 3 shapes per step, {steps} steps "
+                                   f"(the requested steps that fit in ~30 s)"},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -231,18 +236,21 @@ def run_ours(args):
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     launches_per_step = sum(g.mul_mat_plan(M_TOKENS, n, k, WTYPE)["launches"] for (k, n) in SHAPES)
 
-    def step(ev):
-        # ev: list of events [start, after pack0, after gemm0, after pack1, ...]
-        ev[0].record(stream)
+    def step(ev=None):
+        # ev (the kernel-timing pass only): [after pack0, after gemm0, after pack1, ...]. The timed
+        # pass records no event between the kernels, so each launch may begin (programmatic
+        # dependent launch) while the one before it drains.
         for i, (k, n) in enumerate(SHAPES):
             g.act_pack(acts[i], M_TOKENS, k, a16s[i], scales[i], stream=stream)
-            ev[1 + 2 * i].record(stream)
+            if ev:
+                ev[2 * i].record(stream)
             g.gemm_packed(WTYPE, weights[i], n, k, a16s[i], scales[i], M_TOKENS, outs[i], gws[i], err,
                           stream=stream)
-            ev[2 + 2 * i].record(stream)
+            if ev:
+                ev[2 * i + 1].record(stream)
 
-    def new_events():
-        return [torch.cuda.Event(enable_timing=True) for _ in range(1 + 2 * len(SHAPES))]
+    def new_events(n):
+        return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
 
     # A GPU-side delay after each flush lets the host enqueue the whole step before the device
     # reaches it, so the events bracket device work only (no host launch gaps).
@@ -250,7 +258,7 @@ def run_ours(args):
     for _ in range(args.warmup):
         flush.zero_()
         torch.cuda._sleep(slack_cycles)
-        step(new_events())
+        step()
     torch.cuda.synchronize()
     if int(err.item()) != 0:
         raise SystemExit(f"device error {int(err.item())} during warm-up")
@@ -265,8 +273,10 @@ def run_ours(args):
     for _ in range(args.steps):
         flush.zero_()
         torch.cuda._sleep(slack_cycles)
-        e = new_events()
-        step(e)
+        e = new_events(2)
+        e[0].record(stream)
+        step()
+        e[1].record(stream)
         evs.append(e)
     torch.cuda.synchronize()
     if world > 1:
@@ -274,11 +284,22 @@ def run_ours(args):
     clocks = sampler.stop() if sampler else None
     if int(err.item()) != 0:
         raise SystemExit(f"device error {int(err.item())} in the timed region")
+    step_ms = [e[0].elapsed_time(e[1]) for e in evs]
 
-    step_ms = [e[0].elapsed_time(e[-1]) for e in evs]
-    gemm_ms = [sum(e[1 + 2 * i].elapsed_time(e[2 + 2 * i]) for i in range(len(SHAPES))) for e in evs]
+    # The roofline's kernel time: the same steps again with an event pair around every GEMM
+    # launch (on its stream), averaged over the steps.
+    kevs = []
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda._sleep(slack_cycles)
+        e = new_events(2 * len(SHAPES))
+        step(e)
+        kevs.append(e)
+    torch.cuda.synchronize()
+    gemm_ms = [sum(e[2 * i].elapsed_time(e[2 * i + 1]) for i in range(len(SHAPES))) for e in kevs]
     ms_local = sum(step_ms) / len(step_ms)
     gemm_local = sum(gemm_ms) / len(gemm_ms)
+
 
     # ---- e2e: host buffers through the public C ABI ----
     # Every step copies each op's activations in from pinned host memory, runs b200_mul_mat and

@@ -291,8 +291,8 @@ static int tile_knob() {
     return v;
 }
 
-// B200_GEMM_STREAMK: unset / 1 = stream-K over every SM; 0 = one whole tile per CTA whenever the
-// tiles fit in one wave (no partials, idle SMs allowed).
+// B200_GEMM_STREAMK: unset / 1 = the cost model's choice; 0 = one whole tile per CTA whenever the
+// tiles fit in one wave (no partials, idle SMs allowed); 2 = always stream-K over every SM.
 static int streamk_knob() {
     static const int v = [] {
         const char* e = getenv("B200_GEMM_STREAMK");
@@ -330,22 +330,28 @@ static GemmPlan plan_gemm_knobs(int64_t M, int64_t N, int64_t K, int sms, int wt
             const int64_t total_g = tiles * tile_g;
             const int per_unit = pair ? 2 : 1;           // CTAs per work unit
             int units = (int)(total_g < sms / per_unit ? total_g : sms / per_unit);
-            if (streamk_knob() == 0 && tiles <= units) units = (int)tiles;
             // per SM and 64-wide K block: tensor-core clocks (128 x BT x 64 MACs at 4096 MAC/clk),
-            // the decode of 8192 quantized weights, and shared-memory bytes (TMA writes + MMA
-            // reads, 128 B/clk): the activation tile is halved in a pair
+            // the dequant warps' hand-off of 8192 decoded weights (measured: ~800 clocks a block
+            // whatever the token tile), and shared-memory bytes (TMA writes + MMA reads,
+            // 128 B/clk): the activation tile is halved in a pair
             const double mma = bt < 64 ? 128.0 : 2.0 * bt;
-            const double decode = quant ? 400.0 : 0.0;
+            const double decode = quant ? 800.0 : 0.0;
             const double a_bytes = (pair ? bt / 2 : bt) * 128.0 * 2.0;
             const double w_bytes = quant ? 41984.0 : 32768.0;
             const double feed = (a_bytes + w_bytes) / 128.0;
             double per_kb = mma > decode ? mma : decode;
             if (feed > per_kb) per_kb = feed;
             per_kb += 16.0;
+            // whole tiles, one per CTA, when they fit in one wave: no partials
+            const bool whole = tiles <= units && streamk_knob() != 2 && (streamk_knob() == 0 || (double)nkb * per_kb + 800.0 <
+                (double)tiles * nkb * per_kb / units + 800.0 * (1.0 + (double)tiles / units) + 51.2 * bt);
+            if (whole) units = (int)tiles;
             const double items = 1.0 + (double)tiles / units;
             const bool shared = total_g % units != 0 || tiles % units != 0;
             double t = (double)tiles * nkb * per_kb / units + 800.0 * items;
-            if (shared) t += 16.0 * bt;
+            // a shared tile's partials: written by one CTA, read back by its finisher (128 x BT
+            // f32 each way at ~20 B/clk per SM, measured)
+            if (shared) t += 51.2 * bt;
             if (t < best_t * 0.97) {
                 best_t = t;
                 best.bt = bt;
