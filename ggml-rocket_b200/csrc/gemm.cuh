@@ -589,14 +589,22 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     const uint8_t* raw = smem + C::RAW_OFF + rs * RC::STAGE;
                     const uint8_t* rrow = raw + r * RC::ROW;
                     float d6 = 0.0f;
+                    Q4kFactors f4{};
                     if constexpr (WT == WT_Q6_K) d6 = __half2float(reinterpret_cast<const __half*>(raw + RC::A_BYTES)[r]);
+                    if constexpr (WT == WT_Q4_K) f4 = q4k_factors(rrow, h);
                     const int k_lo = max(uc.kb0, 4 * sb), k_hi = min(uc.kb1, 4 * sb + 4);
                     for (int kb = k_lo; kb < k_hi; kb++) {
-                        // decode first: the arithmetic overlaps the wait for the stage to free up
                         uint32_t o[16];
-                        if constexpr (WT == WT_Q4_K) decode_q4k_half(rrow, kb & 3, h, o);
-                        else if constexpr (WT == WT_Q6_K) decode_q6k_half(rrow, d6, kb & 3, h, o);
-                        else decode_q8_0_half(rrow, kb & 3, h, o);
+                        if constexpr (WT == WT_Q4_K) {
+                            float dj, mj;
+                            f4.pick(kb & 3, dj, mj);
+                            decode_q4k_half(rrow, kb & 3, h, dj, mj, o);
+                        } else if constexpr (WT == WT_Q6_K) {
+                            decode_q6k_half(rrow, d6, kb & 3, h, o);
+                        } else {
+                            decode_q8_0_half(rrow, kb & 3, h, o);
+                        }
+                        // decoded first: the arithmetic overlaps the wait for the stage to free up
                         if (!mbar_wait(empty_bar(stage), phase ^ 1u, args.err, ERR_WAIT_DEQUANT, abort_flag)) { ok = false; break; }
                         const uint32_t sw = sbase + stage * C::STAGE_BYTES + C::A_BYTES;
 #pragma unroll

@@ -108,14 +108,32 @@ __device__ __forceinline__ uint32_t f2_to_half2(uint64_t v) {
 
 // Q4_K: raw row = native 144-byte super-blocks. Chunk j of super-block sb, half h: the low (h=0)
 // or high (h=1) nibbles of qs[32j .. 32j+31], sub-block 2j+h: y = (d*sc)*q - dmin*m.
-__device__ __forceinline__ void decode_q4k_half(const uint8_t* blk, int j, int h, uint32_t (&o)[16]) {
+// The factors d*sc and dmin*m of the four sub-blocks 2j+h (j = 0..3) one thread decodes from a
+// super-block, taken once per super-block; pick(j) selects chunk j's pair.
+struct Q4kFactors {
+    float d0, d1, d2, d3, m0, m1, m2, m3;
+    __device__ __forceinline__ void pick(int j, float& d, float& m) const {
+        d = j == 0 ? d0 : j == 1 ? d1 : j == 2 ? d2 : d3;
+        m = j == 0 ? m0 : j == 1 ? m1 : j == 2 ? m2 : m3;
+    }
+};
+__device__ __forceinline__ Q4kFactors q4k_factors(const uint8_t* blk, int h) {
     const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+    const float d = h2f_bits(hdr.x), dmin = h2f_bits(hdr.x >> 16);
+    uint32_t sc[4], m[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) q4k_sm(2 * j + h, hdr.y, hdr.z, hdr.w, sc[j], m[j]);
+    Q4kFactors f;
+    f.d0 = __fmul_rn(d, (float)sc[0]); f.m0 = __fmul_rn(dmin, (float)m[0]);
+    f.d1 = __fmul_rn(d, (float)sc[1]); f.m1 = __fmul_rn(dmin, (float)m[1]);
+    f.d2 = __fmul_rn(d, (float)sc[2]); f.m2 = __fmul_rn(dmin, (float)m[2]);
+    f.d3 = __fmul_rn(d, (float)sc[3]); f.m3 = __fmul_rn(dmin, (float)m[3]);
+    return f;
+}
+__device__ __forceinline__ void decode_q4k_half(const uint8_t* blk, int j, int h, float d1, float m1,
+                                                uint32_t (&o)[16]) {
     const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * j);
     const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * j);
-    uint32_t sc, m;
-    q4k_sm(2 * j + h, hdr.y, hdr.z, hdr.w, sc, m);
-    const float d1 = __fmul_rn(h2f_bits(hdr.x), (float)sc);
-    const float m1 = __fmul_rn(h2f_bits(hdr.x >> 16), (float)m);
     const uint64_t D1 = f2_pack(d1, d1), NM1 = f2_pack(-m1, -m1);
     const uint64_t MAG = f2_pack(-8388608.0f, -8388608.0f);
     const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
