@@ -91,13 +91,14 @@ __device__ __forceinline__ void load_mask32(const uint16_t* mrow, int k0, int KV
 }
 
 // ---------------------------------------------------------------------------------------------
-// Q pre-pass: one warp per (h, t) row.
+// Set-up pass, one launch: CTAs [0, q_ctas) pack Q, one warp per (h, t) row; the rest classify
+// the mask, one CTA per (token block, key block). Launched programmatically; the attention
+// kernel that follows starts its prologue while this pass drains.
 // ---------------------------------------------------------------------------------------------
 template <int D>
-__global__ void fa_q_pack_kernel(const float* __restrict__ q, int64_t q_nb1, int64_t q_nb2, int T, int H,
-                                 float scale, __half* __restrict__ q16, float* __restrict__ qscale) {
-    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
+__device__ __forceinline__ void fa_q_pack_row(const float* __restrict__ q, int64_t q_nb1, int64_t q_nb2, int T,
+                                              int H, float scale, __half* __restrict__ q16,
+                                              float* __restrict__ qscale, int row, int lane) {
     if (row >= H * T) return;
     const int h = row / T, t = row % T;
     const float* src = reinterpret_cast<const float*>(reinterpret_cast<const char*>(q) + (int64_t)t * q_nb1 +
@@ -128,33 +129,63 @@ __global__ void fa_q_pack_kernel(const float* __restrict__ q, int64_t q_nb1, int
     if (lane == 0) qscale[row] = div;
 }
 
-// ---------------------------------------------------------------------------------------------
-// Mask flags: one 256-thread CTA per (token block, key block).
-// ---------------------------------------------------------------------------------------------
-__global__ void fa_mask_flags_kernel(const uint16_t* __restrict__ mask, int64_t m_stride, int T, int KV, int TQ,
-                                     int n_kvb, uint8_t* __restrict__ flags) {
-    const int tb = blockIdx.y, j = blockIdx.x;
+// 256 threads: thread (token row trow of every 32, 16-key segment key_seg) of one 128-key block.
+// With 16-byte aligned mask rows a segment is two 16-byte loads.
+__device__ __forceinline__ void fa_mask_block(const uint16_t* __restrict__ mask, int64_t m_stride, bool vec, int T,
+                                              int KV, int TQ, int tb, int j, int n_kvb, uint8_t* __restrict__ flags) {
     const int key_seg = threadIdx.x & 7;          // 16 keys each
     const int trow = threadIdx.x >> 3;            // 32 token rows per pass
-    bool all_masked = true, all_zero = true;
+    const int key0 = j * FA_KB + key_seg * 16;
+    const bool full_seg = key0 + 16 <= KV;
+    bool all_masked = true, all_zero = key0 < KV && full_seg;
     for (int tr = trow; tr < TQ; tr += 32) {
         const int t = tb * TQ + tr;
         if (t >= T) continue;
-        const uint16_t* mrow = mask + (int64_t)t * m_stride + (int64_t)j * FA_KB + key_seg * 16;
-        for (int i = 0; i < 16; i++) {
-            const int key = j * FA_KB + key_seg * 16 + i;
-            if (key >= KV) {
-                all_zero = false;
-                continue;
+        const uint16_t* mrow = mask + (int64_t)t * m_stride + key0;
+        if (vec && full_seg) {
+            const uint4 a = __ldg(reinterpret_cast<const uint4*>(mrow));
+            const uint4 b = __ldg(reinterpret_cast<const uint4*>(mrow) + 1);
+            const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                if (w[i] != 0xFC00FC00u) all_masked = false;         // two -inf
+                if ((w[i] & 0x7FFF7FFFu) != 0) all_zero = false;     // two +-0
             }
-            const uint16_t v = __ldg(mrow + i);
-            if (v != 0xFC00u) all_masked = false;                 // -inf
-            if ((v & 0x7FFFu) != 0) all_zero = false;            // +-0
+        } else {
+            for (int i = 0; i < 16; i++) {
+                if (key0 + i >= KV) break;
+                const uint16_t v = __ldg(mrow + i);
+                if (v != 0xFC00u) all_masked = false;
+                if ((v & 0x7FFFu) != 0) all_zero = false;
+            }
         }
     }
     const int am = __syncthreads_and(all_masked ? 1 : 0);
     const int az = __syncthreads_and(all_zero ? 1 : 0);
     if (threadIdx.x == 0) flags[(int64_t)tb * n_kvb + j] = am ? MF_MASKED : (az ? MF_ZERO : MF_MIXED);
+}
+
+template <int D>
+__global__ void __launch_bounds__(256) fa_prep_kernel(const float* __restrict__ q, int64_t q_nb1, int64_t q_nb2,
+                                                      int T, int H, float scale, __half* __restrict__ q16,
+                                                      float* __restrict__ qscale, int q_ctas,
+                                                      const uint16_t* __restrict__ mask, int64_t m_stride,
+                                                      bool mask_vec, int KV, int TQ, int n_kvb, int n_tb,
+                                                      uint8_t* __restrict__ flags) {
+    grid_dep_wait();          // q and the mask may be the previous kernel's output
+    grid_dep_launch();
+    if ((int)blockIdx.x < q_ctas) {
+        fa_q_pack_row<D>(q, q_nb1, q_nb2, T, H, scale, q16, qscale, (int)(blockIdx.x * 8 + (threadIdx.x >> 5)),
+                         (int)(threadIdx.x & 31));
+        return;
+    }
+    const int mi = (int)blockIdx.x - q_ctas;
+    if (!mask) {              // no mask: every block is all zero (one CTA writes them)
+        if (mi == 0)
+            for (int i = threadIdx.x; i < n_tb * n_kvb; i += blockDim.x) flags[i] = MF_ZERO;
+        return;
+    }
+    fa_mask_block(mask, m_stride, mask_vec, T, KV, TQ, mi / n_kvb, mi % n_kvb, n_kvb, flags);
 }
 
 // A P row segment of N 32-bit columns (2N fp16 keys) into TMEM.
@@ -265,6 +296,10 @@ fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUten
     cta_sync();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // The prologue above overlapped the set-up pass (programmatic launch): Q16, its row divisors
+    // and the mask flags are that pass's output, so wait for it before the first read.
+    grid_dep_wait();
+    grid_dep_launch();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -603,8 +638,7 @@ static cudaError_t launch_fa(const CUtensorMap& tq, const CUtensorMap& tk, const
         if (e != cudaSuccess) return e;
         set[dev] = true;
     }
-    fa_kernel<D, DV><<<grid, FA_THREADS, C::SMEM, st>>>(tq, tk, tv, a);
-    return cudaGetLastError();
+    return launch_pdl(fa_kernel<D, DV>, dim3((unsigned)grid), dim3(FA_THREADS), C::SMEM, st, tq, tk, tv, a);
 }
 
 int flash_attn_impl(const float* q, int64_t q_nb1, int64_t q_nb2, const void* k, int64_t k_nb1, int64_t k_nb2,
@@ -626,20 +660,18 @@ int flash_attn_impl(const float* q, int64_t q_nb1, int64_t q_nb2, const void* k,
     uint8_t* flags = reinterpret_cast<uint8_t*>(ws + L.flags_off);
 
     {
-        const int rows = H * T;
-        const int blocks = (rows * 32 + 255) / 256;
-        if (D == 64) fa_q_pack_kernel<64><<<blocks, 256, 0, st>>>(q, q_nb1, q_nb2, T, H, scale, q16, qs);
-        else fa_q_pack_kernel<128><<<blocks, 256, 0, st>>>(q, q_nb1, q_nb2, T, H, scale, q16, qs);
-        if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
+        const int q_ctas = (H * T + 7) / 8;
+        const int m_ctas = mask ? L.n_tb * L.n_kvb : 1;
+        const bool mvec = mask && (m_nb1 % 16) == 0 && (reinterpret_cast<uintptr_t>(mask) & 15u) == 0;
+        const dim3 grid((unsigned)(q_ctas + m_ctas)), block(256);
+        const uint16_t* m16 = static_cast<const uint16_t*>(mask);
+        const cudaError_t e = D == 64
+            ? launch_pdl(fa_prep_kernel<64>, grid, block, 0, st, q, q_nb1, q_nb2, T, H, scale, q16, qs, q_ctas, m16,
+                         (int64_t)(m_nb1 / 2), mvec, KV, L.TQ, L.n_kvb, L.n_tb, flags)
+            : launch_pdl(fa_prep_kernel<128>, grid, block, 0, st, q, q_nb1, q_nb2, T, H, scale, q16, qs, q_ctas, m16,
+                         (int64_t)(m_nb1 / 2), mvec, KV, L.TQ, L.n_kvb, L.n_tb, flags);
+        if (e != cudaSuccess) return B200_E_CUDA;
     }
-    if (mask) {
-        dim3 grid(L.n_kvb, L.n_tb);
-        fa_mask_flags_kernel<<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(mask), m_nb1 / 2, T, KV, L.TQ, L.n_kvb,
-                                                   flags);
-    } else {
-        cudaMemsetAsync(flags, MF_ZERO, (size_t)L.n_tb * L.n_kvb, st);
-    }
-    if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
 
     CUtensorMap tq, tk, tv;
     if (!make_tmap_3d_f16(&tq, q16, D, T, H, (uint64_t)D * 2, (uint64_t)T * D * 2, 64, L.TQ, L.GP)) return B200_E_CUDA;

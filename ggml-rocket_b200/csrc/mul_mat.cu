@@ -92,24 +92,6 @@ __global__ void __launch_bounds__(ACT_THREADS) act_pack_loop_kernel(const float*
     for (int i = threadIdx.x; i < K; i += ACT_THREADS) out[i] = __float2half_rn(__fmul_rn(__ldg(row + i), inv));
 }
 
-// Launch with programmatic stream serialization: the kernel may be scheduled while the previous
-// kernel of the stream drains (its prologue overlaps that tail; it waits with grid_dep_wait()).
-template <typename... KArgs, typename... Args>
-static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                              Args&&... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
-
 static cudaError_t launch_act_pack(const float* A, int64_t lda, int64_t M, int64_t K, __half* a16, float* scales,
                                    cudaStream_t st) {
     const bool vec = ((reinterpret_cast<uintptr_t>(A) & 15u) == 0) && (lda % 4 == 0) && (K % 4 == 0);
