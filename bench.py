@@ -23,6 +23,7 @@ ggml-decoded weight, rocket_cpu_matmul_slice) on all host cores, on a bounded to
 the same workload per step.
 """
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -60,6 +61,10 @@ def parse():
                     help="gemm: the headline MUL_MAT sweep (default); moe: the MUL_MAT_ID layer of "
                          "BASELINE configs[3], expert-parallel over the ranks; fa: the FLASH_ATTN_EXT "
                          "prefill of configs[2]")
+    ap.add_argument("--shard", action="store_true",
+                    help="gemm workload on several GPUs: split every weight's rows across the ranks "
+                         "(strong scaling), the output all-gathered by the GEMM epilogue's stores into "
+                         "peer memory, instead of one replica per rank")
     ap.add_argument("--ep", choices=["peer", "nccl"], default="peer",
                     help="moe workload on several GPUs: exchanges by the kernels' own stores into peer "
                          "memory (default) or by NCCL all-to-all")
@@ -603,6 +608,92 @@ def run_fa(args):
     return 0
 
 
+def run_gemm_sharded(args):
+    """The headline sweep with every weight's rows split across the ranks (ggml_b200.tp): each
+    rank packs its row block of each shape's weight, runs the N-sharded MUL_MAT on the shared
+    activation, and ends holding the full dst. value = the sweep's FLOPs / max-over-ranks time."""
+    import numpy as np
+    import torch
+    import ggml_b200 as g
+    from ggml_b200 import quants
+    from ggml_b200.tp import PeerShardedMulMat, shard_rows
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+    else:
+        torch.distributed.init_process_group("gloo", init_method="tcp://127.0.0.1:29581", rank=0, world_size=1)
+    g.lib()
+    rng = np.random.default_rng(0xB200)
+    shards, acts = [], []
+    for (k, n) in SHAPES:
+        w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02))
+        lo, hi = shard_rows(n, world, rank)
+        raw = torch.from_numpy(quants.quantize(WTYPE, w[lo:hi]).reshape(-1)).to(dev)
+        packed = torch.empty(g.weight_packed_size(WTYPE, hi - lo, k), dtype=torch.uint8, device=dev)
+        g.weight_pack(WTYPE, raw, hi - lo, k, packed)
+        shards.append(packed)
+        acts.append(torch.from_numpy(rng.standard_normal((M_TOKENS, k)).astype(np.float32)).to(dev))
+    tp = PeerShardedMulMat(M_TOKENS, max(n for (_, n) in SHAPES))
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def step():
+        for i, (k, n) in enumerate(SHAPES):
+            tp(WTYPE, shards[i], n, k, acts[i], M_TOKENS, stream=stream)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        torch.cuda._sleep(1000000)
+        step()
+    torch.cuda.synchronize()
+    if int(tp.err.item()) != 0:
+        raise SystemExit(f"device error {int(tp.err.item())} during warm-up")
+    sampler = ClockSampler(local) if rank == 0 else None
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+    evs = []
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda._sleep(1000000)
+        e = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+        e[0].record(stream)
+        step()
+        e[1].record(stream)
+        evs.append(e)
+    torch.cuda.synchronize()
+    torch.distributed.barrier()
+    clocks = sampler.stop() if sampler else None
+    if int(tp.err.item()) != 0:
+        raise SystemExit(f"device error {int(tp.err.item())} in the timed region")
+    ms_local = sum(e[0].elapsed_time(e[1]) for e in evs) / len(evs)
+    vals = torch.tensor([ms_local], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+    ms = float(vals.item())
+    tp.close()
+    if rank == 0:
+        flops = step_flops()
+        line = {"metric": METRIC, "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
+                "config": {"workload": WORKLOAD + "; every weight's rows split across the ranks, the output "
+                                                  "all-gathered by the GEMM epilogue's stores into peer memory",
+                           "weight_type": "Q4_K", "global_batch": M_TOKENS, "seq_len": M_TOKENS,
+                           "parallelism": f"N-sharded x{world}",
+                           "l2": "flushed before every timed step (256 MiB memset), outside the timed events",
+                           "tokens_per_s": M_TOKENS / (ms / 1e3)},
+                "clocks": clocks, "gpu_launches": 4 * len(SHAPES) * args.steps}
+        print(json.dumps(line), flush=True)
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -611,6 +702,8 @@ def main():
         return run_moe(args)
     if args.workload == "fa":
         return run_fa(args)
+    if args.shard:
+        return run_gemm_sharded(args)
     return run_ours(args)
 
 

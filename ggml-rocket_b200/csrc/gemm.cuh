@@ -79,6 +79,11 @@ struct GemmArgs {
     // destination of that row (another GPU's buffer, reached by plain stores over NVLink)
     const int32_t* g_src;
     float* const* out_bases;
+    // plain MUL_MAT with its weight rows split across GPUs: when n_dst > 0 every finished box
+    // goes to all n_dst buffers out_bases[d] (this GPU's dst and the other GPUs', [M][ldo] f32),
+    // at column col0 + n -- the all-gather done by the epilogue's own stores over NVLink
+    int n_dst;
+    int col0;
 };
 
 // One work item of a CTA: a tile (or, in stream-K, the piece of a tile's K range this CTA owns).
@@ -522,7 +527,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     } else {
                         tmem_ld_wait();
                     }
-                    if constexpr (!GROUPED) {
+                    if (!GROUPED && args.n_dst == 0) {
                         // the scaled [token][32 rows] box, then one TMA store of it (rows past
                         // M and columns past N are clipped by the tensor map)
                         if (lane == 0) bulk_wait_read_all();     // the previous box has been read
@@ -537,8 +542,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                             bulk_commit();
                         }
                     } else {
-                        // scattered rows: a transpose, then 16-byte stores, each instruction
-                        // four whole 128-byte output lines
+                        // scattered rows (grouped) or several destinations (split weight rows): a
+                        // transpose, then 16-byte stores, each instruction four whole 128-byte
+                        // output lines (plain stores: the destinations may be other GPUs')
 #pragma unroll
                         for (int j = 0; j < 32; j++) es[j * 32 + lane] = __uint_as_float(r[j]);
                         __syncwarp();
@@ -546,11 +552,18 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                         for (int i = 0; i < 8; i++) {
                             const int jr = (lane >> 3) + 4 * i;
                             const float sc = __shfl_sync(0xffffffffu, sg, jr);
-                            const uint64_t rp = __shfl_sync(0xffffffffu, rg, jr);
-                            if (rp && nb < args.N) {
-                                float4 v = es4[jr * 8 + cc];
-                                v.x *= sc; v.y *= sc; v.z *= sc; v.w *= sc;
-                                *reinterpret_cast<float4*>(reinterpret_cast<float*>(rp) + nb) = v;
+                            float4 v = es4[jr * 8 + cc];
+                            v.x *= sc; v.y *= sc; v.z *= sc; v.w *= sc;
+                            if constexpr (GROUPED) {
+                                const uint64_t rp = __shfl_sync(0xffffffffu, rg, jr);
+                                if (rp && nb < args.N) *reinterpret_cast<float4*>(reinterpret_cast<float*>(rp) + nb) = v;
+                            } else {
+                                const int t = uc.t0 + c0 + jr;
+                                if (t < uc.t_end && nb < args.N) {
+                                    const size_t o = (size_t)t * args.ldo + args.col0 + nb;
+                                    for (int d = 0; d < args.n_dst; d++)
+                                        *reinterpret_cast<float4*>(args.out_bases[d] + o) = v;
+                                }
                             }
                         }
                         __syncwarp();
@@ -562,16 +575,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                 __syncwarp();
                 if (lane == 0) st_release_gpu(args.flags + 4 * blockIdx.x + q, args.epoch);
             }
-            if constexpr (GROUPED) {
-                // rows stored into other GPUs' memory must be visible there before the kernel
-                // that follows signals their owners
-                if (args.g_src) __threadfence_system();
-            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) arrive_leader(tempty_bar(acc));
         }
         if (lane == 0) bulk_wait_all();   // this warp's output stores are complete before it exits
+        // rows stored into other GPUs' memory must be visible there before the kernel that follows
+        // signals their owners: one system fence per thread after its last store (a fence per
+        // tile would hold the accumulator until every store of the tile had crossed NVLink)
+        if (GROUPED ? args.g_src != nullptr : args.n_dst > 0) __threadfence_system();
     } else if (C::QUANT && dequant_slot(warp) >= 0) {
         // ---------------- dequant (quantized weights) ----------------
         if constexpr (C::QUANT) {

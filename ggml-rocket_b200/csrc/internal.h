@@ -33,8 +33,14 @@ bool make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_
                       uint32_t box_rows, uint32_t box_cols);
 size_t packed_weight_bytes(int type, int64_t N, int64_t K, size_t* plane_d_off);
 bool weight_type_supported(int type, int64_t K);
+// dst_bases / n_dst / col0: the output columns [col0, col0 + N) of every one of n_dst [M][ldd]
+// buffers (a device array of pointers, other GPUs' included) instead of dst
 int mul_mat_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const float* src1, int64_t lda, int64_t M,
-                 float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t st);
+                 float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t st,
+                 float* const* dst_bases = nullptr, int n_dst = 0, int64_t col0 = 0);
+int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const __half* a16, const float* scales,
+                     int64_t M, float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err,
+                     cudaStream_t st, float* const* dst_bases = nullptr, int n_dst = 0, int64_t col0 = 0);
 size_t mul_mat_workspace(int wtype, int64_t M, int64_t N, int64_t K);
 int act_pack_impl(const float* src1, int64_t lda, int64_t M, int64_t K, __half* a16, float* scales, cudaStream_t st);
 int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int64_t n_expert, const __half* a16,

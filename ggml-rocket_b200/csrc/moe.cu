@@ -37,6 +37,8 @@ __device__ __forceinline__ int moe_id_at(const int32_t* ids, int64_t ids_nb0, in
 __global__ void __launch_bounds__(ROUTE_THREADS) moe_hist_kernel(const int32_t* __restrict__ ids, int64_t ids_nb0,
                                                                 int64_t ids_nb1, int n_used, int R, int E,
                                                                 int32_t* __restrict__ counts, int32_t* __restrict__ bad) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     extern __shared__ int cnt[];
     for (int e = threadIdx.x; e < E; e += ROUTE_THREADS) cnt[e] = 0;
     __syncthreads();
@@ -58,6 +60,8 @@ __global__ void __launch_bounds__(ROUTE_THREADS) moe_scan_kernel(int32_t* __rest
                                                                 const int32_t* __restrict__ bad, int nb, int E, int bt,
                                                                 int32_t* __restrict__ off,
                                                                 int32_t* __restrict__ tile_start, int* err) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     extern __shared__ int tot[];
     __shared__ int wsum[2][32];
     __shared__ int carry[2];
@@ -144,6 +148,8 @@ __global__ void __launch_bounds__(ROUTE_THREADS) moe_place_kernel(const int32_t*
                                                                  const int32_t* __restrict__ counts,
                                                                  const int32_t* __restrict__ off,
                                                                  int32_t* __restrict__ slot, int32_t* __restrict__ tok) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     extern __shared__ int sm[];
     int* base = sm;
     int* wcnt = sm + E;
@@ -189,6 +195,8 @@ __global__ void __launch_bounds__(256) moe_gather_pack_kernel(const float* __res
                                                               const int32_t* __restrict__ tok,
                                                               const int32_t* __restrict__ off_total,
                                                               __half* __restrict__ a16, float* __restrict__ scales) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     __shared__ float red[8];
     const int r = blockIdx.x;
     if (r >= __ldg(off_total)) return;   // a bad-id op has no rows
@@ -234,7 +242,7 @@ int launch_gather_pack(const float* b, int64_t b_nb1, int64_t b_nb2, int64_t ne1
     const int64_t per = (K / 4 + 255) / 256;
     const dim3 grid((unsigned)max_rows);
 #define B200_GATHER(V) \
-    moe_gather_pack_kernel<V><<<grid, 256, 0, st>>>(b, b_nb1, b_nb2, (int)ne11, (int)K, slot, tok, n_rows, a16, scales)
+    launch_pdl(moe_gather_pack_kernel<V>, dim3(grid), dim3(256), 0, st, b, b_nb1, b_nb2, (int)ne11, (int)K, slot, tok, n_rows, a16, scales)
     if (per <= 1) B200_GATHER(1);
     else if (per <= 2) B200_GATHER(2);
     else if (per <= 4) B200_GATHER(4);
@@ -304,10 +312,10 @@ int mul_mat_id_impl(int wtype, const void* as_packed, int64_t K, int64_t N, int6
         cudaFuncSetAttribute(moe_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)place_smem) !=
             cudaSuccess)
         return B200_E_UNSUPPORTED;
-    moe_hist_kernel<<<nb, ROUTE_THREADS, hist_smem, st>>>(ids, ids_nb0, ids_nb1, (int)n_used, (int)R, (int)n_expert,
+    launch_pdl(moe_hist_kernel, dim3(nb), dim3(ROUTE_THREADS), hist_smem, st, ids, ids_nb0, ids_nb1, (int)n_used, (int)R, (int)n_expert,
                                                           counts, bad);
-    moe_scan_kernel<<<1, ROUTE_THREADS, hist_smem, st>>>(counts, bad, nb, (int)n_expert, bt, off, tiles, dev_err);
-    moe_place_kernel<<<nb, ROUTE_THREADS, place_smem, st>>>(ids, ids_nb0, ids_nb1, (int)n_used, (int)R,
+    launch_pdl(moe_scan_kernel, dim3(1), dim3(ROUTE_THREADS), hist_smem, st, counts, bad, nb, (int)n_expert, bt, off, tiles, dev_err);
+    launch_pdl(moe_place_kernel, dim3(nb), dim3(ROUTE_THREADS), place_smem, st, ids, ids_nb0, ids_nb1, (int)n_used, (int)R,
                                                             (int)n_expert, counts, off, slot, tok);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
     const int rc = launch_gather_pack(b, b_nb1, b_nb2, ne11, K, slot, tok, off + n_expert, R, a16, scales, st);

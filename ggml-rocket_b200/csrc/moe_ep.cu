@@ -58,6 +58,8 @@ struct EpIds {
 // bcounts[b][d] = {rows, return rows} of CTA b for destination d; bad[b] = a bad id seen.
 __global__ void __launch_bounds__(EPC) ep_dispatch_count_kernel(EpIds I, int C, int E, int G,
                                                                 int32_t* __restrict__ bcounts, int32_t* __restrict__ bad) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     __shared__ int cnt[2 * EP_MAX_RANKS];
     for (int k = threadIdx.x; k < 2 * G; k += EPC) cnt[k] = 0;
     __syncthreads();
@@ -88,6 +90,8 @@ __global__ void __launch_bounds__(EPC) ep_dispatch_count_kernel(EpIds I, int C, 
 // the per-destination totals and the grand totals; bad[nb] = any bad id.
 __global__ void ep_dispatch_scan_kernel(int32_t* __restrict__ bcounts, int32_t* __restrict__ bad, int nb, int G,
                                         int32_t* __restrict__ counts, int* err) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     if (threadIdx.x != 0) return;
     int any = 0;
     for (int b = 0; b < nb; b++) any |= bad[b];
@@ -123,6 +127,8 @@ __global__ void __launch_bounds__(EPC) ep_dispatch_write_kernel(EpIds I, int C, 
                                                                 int32_t* __restrict__ hdr, int32_t* __restrict__ row_tok,
                                                                 int32_t* __restrict__ row_slot,
                                                                 int32_t* __restrict__ row_ret) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     __shared__ int sh[32];
     if (__ldg(bad_any)) return;
     const int c = blockIdx.x * EPC + threadIdx.x;
@@ -153,6 +159,8 @@ __global__ void __launch_bounds__(EPC) ep_dispatch_write_kernel(EpIds I, int C, 
 __global__ void __launch_bounds__(EPC) ep_route_count_kernel(const int32_t* __restrict__ hdr, int n_rows, int n_used,
                                                              int expert0, int e_loc, int32_t* __restrict__ ecnt,
                                                              int32_t* __restrict__ bsum, int32_t* __restrict__ bad) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     extern __shared__ int hist[];
     __shared__ int sh[32];
     for (int e = threadIdx.x; e < e_loc; e += EPC) hist[e] = 0;
@@ -189,6 +197,8 @@ __global__ void __launch_bounds__(EP_THREADS) ep_route_scan_kernel(const int32_t
                                                                   int nb, int e_loc, int bt, int32_t* __restrict__ off,
                                                                   int32_t* __restrict__ tile_start,
                                                                   int32_t* __restrict__ cursor, int* err) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     __shared__ int sh[32];
     __shared__ int carry[3];
     int any = 0;
@@ -250,6 +260,8 @@ __global__ void __launch_bounds__(EPC) ep_route_place_kernel(const int32_t* __re
                                                              int32_t* __restrict__ pair_src,
                                                              int32_t* __restrict__ pair_ret,
                                                              int32_t* __restrict__ pair_zero) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     __shared__ int sh[32];
     if (__ldg(bad_any)) return;
     const int r = blockIdx.x * EPC + threadIdx.x;
@@ -274,6 +286,8 @@ __global__ void __launch_bounds__(256) ep_gather_rows_kernel(const __half* __res
                                                              const int32_t* __restrict__ pair_src,
                                                              const int32_t* __restrict__ n_pairs, int K,
                                                              __half* __restrict__ dst, float* __restrict__ dst_scale) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     const int n = __ldg(n_pairs);
     for (int p = blockIdx.x; p < n; p += gridDim.x) {
         const int r = __ldg(pair_src + p);
@@ -292,6 +306,8 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const float* __restrict
                                                          const int32_t* __restrict__ row_ret,
                                                          const int32_t* __restrict__ n_rows, float* __restrict__ dst,
                                                          int64_t d_nb1, int64_t d_nb2) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     const int n = __ldg(n_rows);
     for (int p = blockIdx.x; p < n; p += gridDim.x) {
         const int t = __ldg(row_tok + p);
@@ -347,7 +363,7 @@ int ep_token_tile_public(int64_t pairs, int64_t e_loc) { return ep_token_tile(pa
 
 void ep_route_scan_public(const int32_t* ecnt, int32_t* bsum, int32_t* bad, int nb, int e_loc, int bt, int32_t* off,
                           int32_t* tile_start, int32_t* cursor, int* err, cudaStream_t st) {
-    ep_route_scan_kernel<<<1, EP_THREADS, 0, st>>>(ecnt, bsum, bad, nb, e_loc, bt, off, tile_start, cursor, err);
+    launch_pdl(ep_route_scan_kernel, dim3(1), dim3(EP_THREADS), 0, st, ecnt, bsum, bad, nb, e_loc, bt, off, tile_start, cursor, err);
 }
 
 }  // namespace b200
@@ -384,9 +400,9 @@ int b200_moe_ep_dispatch(const int32_t* ids, int64_t ids_nb0, int64_t ids_nb1, i
     int32_t* bad = reinterpret_cast<int32_t*>(static_cast<char*>(scratch) +
                                               (((size_t)nb * 2 * n_ranks * 4 + 255) & ~(size_t)255));
     const EpIds I{ids, ids_nb0, ids_nb1, (int)n_used, (int)ne11, (int)(n_expert / n_ranks)};
-    ep_dispatch_count_kernel<<<nb, EPC, 0, st>>>(I, C, (int)n_expert, (int)n_ranks, bcounts, bad);
-    ep_dispatch_scan_kernel<<<1, 32, 0, st>>>(bcounts, bad, nb, (int)n_ranks, counts, dev_err);
-    ep_dispatch_write_kernel<<<nb, EPC, 0, st>>>(I, C, (int)n_ranks, bcounts, bad + nb, send_hdr, row_tok, row_slot,
+    launch_pdl(ep_dispatch_count_kernel, dim3(nb), dim3(EPC), 0, st, I, C, (int)n_expert, (int)n_ranks, bcounts, bad);
+    launch_pdl(ep_dispatch_scan_kernel, dim3(1), dim3(32), 0, st, bcounts, bad, nb, (int)n_ranks, counts, dev_err);
+    launch_pdl(ep_dispatch_write_kernel, dim3(nb), dim3(EPC), 0, st, I, C, (int)n_ranks, bcounts, bad + nb, send_hdr, row_tok, row_slot,
                                                  row_ret);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
     const int rc = launch_gather_pack(b, b_nb1, b_nb2, ne11, K, row_slot, row_tok, counts + 2 * n_ranks,
@@ -439,14 +455,14 @@ int b200_moe_ep_expert(int wtype, const void* local_stack, int64_t K, int64_t N,
             cudaSuccess)
         return B200_E_UNSUPPORTED;
     if (cudaMemsetAsync(ecnt, 0, (size_t)n_local * 4, st) != cudaSuccess) return B200_E_CUDA;
-    ep_route_count_kernel<<<nb, EPC, hist_smem, st>>>(recv_hdr, (int)n_rows, (int)n_used, (int)expert0,
+    launch_pdl(ep_route_count_kernel, dim3(nb), dim3(EPC), hist_smem, st, recv_hdr, (int)n_rows, (int)n_used, (int)expert0,
                                                       (int)n_local, ecnt, bsum, bad);
-    ep_route_scan_kernel<<<1, EP_THREADS, 0, st>>>(ecnt, bsum, bad, nb, (int)n_local, bt, off, tiles, cursor, dev_err);
-    ep_route_place_kernel<<<nb, EPC, 0, st>>>(recv_hdr, (int)n_rows, (int)n_used, (int)expert0, bsum, bad + nb,
+    launch_pdl(ep_route_scan_kernel, dim3(1), dim3(EP_THREADS), 0, st, ecnt, bsum, bad, nb, (int)n_local, bt, off, tiles, cursor, dev_err);
+    launch_pdl(ep_route_place_kernel, dim3(nb), dim3(EPC), 0, st, recv_hdr, (int)n_rows, (int)n_used, (int)expert0, bsum, bad + nb,
                                               cursor, src, rix, zero);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
     const int64_t gcap = (int64_t)device_sm_count() * 8;
-    ep_gather_rows_kernel<<<(unsigned)(pmax < gcap ? pmax : gcap), 256, 0, st>>>(
+    launch_pdl(ep_gather_rows_kernel, dim3((unsigned)(pmax < gcap ? pmax : gcap)), dim3(256), 0, st, 
         static_cast<const __half*>(recv_a16), recv_scale, src, off + n_local, (int)K, a16, scales);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
     return gemm_grouped_impl(wtype, local_stack, N, K, n_local, a16, scales, pmax, bt, off, tiles, zero, rix, ret, 0,
@@ -465,7 +481,7 @@ int b200_moe_ep_combine(const float* ret, int64_t N, const int32_t* send_hdr, in
         (reinterpret_cast<uintptr_t>(ret) & 15u))
         return B200_E_UNSUPPORTED;
     const int64_t gcap = (int64_t)device_sm_count() * 8;
-    ep_combine_kernel<<<(unsigned)(max_rows < gcap ? max_rows : gcap), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+    launch_pdl(ep_combine_kernel, dim3((unsigned)(max_rows < gcap ? max_rows : gcap)), dim3(256), 0, static_cast<cudaStream_t>(stream), 
         ret, (int)N, send_hdr, (int)n_used, row_tok, row_ret, counts + 2 * n_ranks, dst, d_nb1, d_nb2);
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }

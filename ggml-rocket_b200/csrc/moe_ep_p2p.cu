@@ -51,6 +51,8 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_push_kernel(const __half* __re
                                                               int n_used, int K, int64_t cap,
                                                               __half* const* __restrict__ peer_a16,
                                                               int32_t* const* __restrict__ peer_meta) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     const int n = __ldg(counts + 2 * G);
     const int lane = threadIdx.x & 31;
     const int wpb = P2P_THREADS / 32;
@@ -80,6 +82,8 @@ __global__ void __launch_bounds__(P2P_THREADS) ep_push_kernel(const __half* __re
 // flag slot for this rank: flags[slot_base + me][0..3] on rank d.
 __global__ void ep_signal_kernel(int* const* __restrict__ peer_flags, int slot_base, int me, int G, int epoch,
                                  const int32_t* __restrict__ counts) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     __threadfence_system();
     const int d = threadIdx.x;
     if (d >= G) return;
@@ -97,6 +101,8 @@ __global__ void ep_signal_kernel(int* const* __restrict__ peer_flags, int slot_b
 // total; region[G+2..] row prefixes) when `region` is given.
 __global__ void ep_wait_kernel(const int* __restrict__ flags, int slot_base, int G, int epoch, int32_t* __restrict__ region,
                                int* err) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     const int s = threadIdx.x;
     bool ok = true;
     if (s < G) {
@@ -141,6 +147,8 @@ __global__ void __launch_bounds__(P2PC) p2p_route_count_kernel(const int32_t* __
                                                                int G, int64_t cap, int n_used, int expert0, int e_loc,
                                                                int32_t* __restrict__ ecnt, int32_t* __restrict__ bsum,
                                                                int32_t* __restrict__ bad) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     extern __shared__ int hist[];
     __shared__ int sh[32];
     for (int e = threadIdx.x; e < e_loc; e += P2PC) hist[e] = 0;
@@ -182,6 +190,8 @@ __global__ void __launch_bounds__(P2PC) p2p_route_place_kernel(const int32_t* __
                                                                int32_t* __restrict__ pair_src,
                                                                int32_t* __restrict__ pair_tok,
                                                                int32_t* __restrict__ pair_slot) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     if (__ldg(bad_any)) return;
     const int MW = n_used + 3;
     const int r = blockIdx.x * P2PC + threadIdx.x;
@@ -207,6 +217,8 @@ __global__ void __launch_bounds__(256) p2p_gather_kernel(const __half* __restric
                                                          const int32_t* __restrict__ pair_row,
                                                          const int32_t* __restrict__ n_pairs, int n_used, int K,
                                                          __half* __restrict__ dst, float* __restrict__ dst_scale) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
     const int n = __ldg(n_pairs);
     const int MW = n_used + 3;
     for (int p = blockIdx.x; p < n; p += gridDim.x) {
@@ -298,10 +310,10 @@ int b200_moe_ep_p2p_push(const void* send_a16, const float* send_scale, const in
     const int64_t gcap = (int64_t)device_sm_count() * 4;
     const int64_t blocks = (max_rows + 7) / 8 < gcap ? (max_rows + 7) / 8 : gcap;
     if (blocks > 0)
-        ep_push_kernel<<<(unsigned)blocks, P2P_THREADS, 0, st>>>(
+        launch_pdl(ep_push_kernel, dim3((unsigned)blocks), dim3(P2P_THREADS), 0, st, 
             static_cast<const __half*>(send_a16), send_scale, send_hdr, row_tok, counts, (int)n_ranks, (int)rank,
             (int)n_used, (int)K, cap, reinterpret_cast<__half* const*>(peer_recv_a16), peer_recv_meta);
-    ep_signal_kernel<<<1, 64, 0, st>>>(peer_flags, 0, (int)rank, (int)n_ranks, epoch, counts);
+    launch_pdl(ep_signal_kernel, dim3(1), dim3(64), 0, st, peer_flags, 0, (int)rank, (int)n_ranks, epoch, counts);
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 
@@ -346,7 +358,7 @@ int b200_moe_ep_p2p_expert(int wtype, const void* local_stack, int64_t K, int64_
     const int nb = (int)((rows_max + P2PC - 1) / P2PC);
     const int bt = ep_token_tile_public(pairs_hint > 0 ? pairs_hint : rows_max / 2, n_local);
     // 1. every source's rows have landed (their flags carry the counts)
-    ep_wait_kernel<<<1, 64, 0, st>>>(flags, 0, G, epoch, region, dev_err);
+    launch_pdl(ep_wait_kernel, dim3(1), dim3(64), 0, st, flags, 0, G, epoch, region, dev_err);
     // 2. route the (row, slot) pairs by local expert
     const size_t hist_smem = (size_t)n_local * sizeof(int);
     if (hist_smem > 48 * 1024 &&
@@ -354,14 +366,14 @@ int b200_moe_ep_p2p_expert(int wtype, const void* local_stack, int64_t K, int64_
             cudaSuccess)
         return B200_E_UNSUPPORTED;
     if (cudaMemsetAsync(ecnt, 0, (size_t)n_local * 4, st) != cudaSuccess) return B200_E_CUDA;
-    p2p_route_count_kernel<<<nb, P2PC, hist_smem, st>>>(recv_meta, region, G, cap, (int)n_used, (int)expert0,
+    launch_pdl(p2p_route_count_kernel, dim3(nb), dim3(P2PC), hist_smem, st, recv_meta, region, G, cap, (int)n_used, (int)expert0,
                                                         (int)n_local, ecnt, bsum, bad);
     ep_route_scan_public(ecnt, bsum, bad, nb, (int)n_local, bt, off, tiles, cursor, dev_err, st);
-    p2p_route_place_kernel<<<nb, P2PC, 0, st>>>(recv_meta, region, G, cap, (int)n_used, (int)expert0, bad + nb,
+    launch_pdl(p2p_route_place_kernel, dim3(nb), dim3(P2PC), 0, st, recv_meta, region, G, cap, (int)n_used, (int)expert0, bad + nb,
                                                 cursor, prow, psrc, ptok, pslot);
     // 3. gather the fp16 rows in expert order
     const int64_t gcap = (int64_t)device_sm_count() * 8;
-    p2p_gather_kernel<<<(unsigned)(rows_max < gcap ? rows_max : gcap), 256, 0, st>>>(
+    launch_pdl(p2p_gather_kernel, dim3((unsigned)(rows_max < gcap ? rows_max : gcap)), dim3(256), 0, st, 
         static_cast<const __half*>(recv_a16), recv_meta, prow, off + n_local, (int)n_used, (int)K, a16, scales);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
     // 4. the grouped GEMM stores each output row into its home rank's ret over NVLink
@@ -369,14 +381,14 @@ int b200_moe_ep_p2p_expert(int wtype, const void* local_stack, int64_t K, int64_
                                      ptok, nullptr, ret_nb1, ret_nb2, dev_err, st, psrc, peer_ret);
     if (rc != B200_OK) return rc;
     // 5. tell every home rank its rows are in place
-    ep_signal_kernel<<<1, 64, 0, st>>>(peer_flags, G, (int)rank, G, epoch, nullptr);
+    launch_pdl(ep_signal_kernel, dim3(1), dim3(64), 0, st, peer_flags, G, (int)rank, G, epoch, nullptr);
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 
 int b200_moe_ep_p2p_finish(const int* flags, int64_t n_ranks, int epoch, int* dev_err, void* stream) {
     using namespace b200;
     if (!flags || !dev_err || n_ranks <= 0 || n_ranks > 64) return B200_E_INVALID;
-    ep_wait_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(flags, (int)n_ranks, (int)n_ranks, epoch, nullptr,
+    launch_pdl(ep_wait_kernel, dim3(1), dim3(64), 0, static_cast<cudaStream_t>(stream), flags, (int)n_ranks, (int)n_ranks, epoch, nullptr,
                                                                     dev_err);
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }

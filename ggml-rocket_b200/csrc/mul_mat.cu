@@ -557,14 +557,18 @@ bool weight_type_supported(int type, int64_t K) {
     }
 }
 
-// The tcgen05 GEMM over an already packed activation (A16 [M,K] fp16 + per-row scales).
+// The tcgen05 GEMM over an already packed activation (A16 [M,K] fp16 + per-row scales). With
+// dst_bases (a device array of n_dst pointers) the output columns [col0, col0 + N) go to every
+// one of those [M][ldd] buffers instead of dst (the weight rows split across GPUs).
 int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const __half* a16, const float* scales,
                      int64_t M, float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err,
-                     cudaStream_t st) {
-    if (!w_packed || !a16 || !scales || !dst || !dev_err || M <= 0 || N <= 0 || K <= 0) return B200_E_INVALID;
+                     cudaStream_t st, float* const* dst_bases, int n_dst, int64_t col0) {
+    if (!w_packed || !a16 || !scales || !(dst || (dst_bases && n_dst > 0)) || !dev_err || M <= 0 || N <= 0 || K <= 0)
+        return B200_E_INVALID;
     if (!weight_type_supported(wtype, K) || K % 32 != 0 || N % 16 != 0) return B200_E_UNSUPPORTED;
     // the epilogue writes 16-byte vectors of dst rows
-    if (ldd % 4 != 0 || (reinterpret_cast<uintptr_t>(dst) & 15u)) return B200_E_UNSUPPORTED;
+    if (ldd % 4 != 0 || (dst && (reinterpret_cast<uintptr_t>(dst) & 15u)) || col0 % 16 != 0 || n_dst > 64)
+        return B200_E_UNSUPPORTED;
     if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return B200_E_UNSUPPORTED;
     const int sms = device_sm_count();
     const GemmPlan p = plan_gemm(M, N, K, sms, wtype);
@@ -594,8 +598,11 @@ int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, cons
     a.gran = p.gran;
     a.tile_g = p.tile_g;
     a.total_g = p.total_g;
-    CUtensorMap tmO;
-    if (!make_tmap_2d_f32_out(&tmO, dst, (uint64_t)M, (uint64_t)N, (uint64_t)ldd * 4)) return B200_E_CUDA;
+    a.out_bases = n_dst > 0 ? dst_bases : nullptr;
+    a.n_dst = n_dst > 0 ? n_dst : 0;
+    a.col0 = (int)col0;
+    CUtensorMap tmO = tmA;   // unused with several destinations
+    if (n_dst <= 0 && !make_tmap_2d_f32_out(&tmO, dst, (uint64_t)M, (uint64_t)N, (uint64_t)ldd * 4)) return B200_E_CUDA;
     const cudaError_t e = launch_gemm_typed<false>(wtype, p.bt, p.pair, tmA, tmW, tmD, tmO, a, p.grid, st);
     return e == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
@@ -606,8 +613,10 @@ int act_pack_impl(const float* src1, int64_t lda, int64_t M, int64_t K, __half* 
 }
 
 int mul_mat_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const float* src1, int64_t lda, int64_t M,
-                 float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t st) {
-    if (!w_packed || !src1 || !dst || !dev_err || M <= 0 || N <= 0 || K <= 0) return B200_E_INVALID;
+                 float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t st,
+                 float* const* dst_bases, int n_dst, int64_t col0) {
+    if (!w_packed || !src1 || !(dst || (dst_bases && n_dst > 0)) || !dev_err || M <= 0 || N <= 0 || K <= 0)
+        return B200_E_INVALID;
     const GemmPlan p = plan_gemm(M, N, K, device_sm_count(), wtype);
     const MulMatWorkspace wl = mm_workspace_layout(M, N, K, p);
     if (!workspace || workspace_bytes < wl.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
@@ -618,7 +627,7 @@ int mul_mat_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const fl
     int rc = act_pack_impl(src1, lda, M, K, a16, scales, st);
     if (rc != B200_OK) return rc;
     return gemm_packed_impl(wtype, w_packed, N, K, a16, scales, M, dst, ldd, ws + wl.part_off, wl.total - wl.part_off,
-                            dev_err, st);
+                            dev_err, st, dst_bases, n_dst, col0);
 }
 
 size_t mul_mat_workspace(int wtype, int64_t M, int64_t N, int64_t K) {

@@ -19,7 +19,7 @@ BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144
 B200_OK = 0
 STATUS = {0: "ok", -1: "invalid", -2: "unsupported", -3: "cuda", -4: "device", -5: "workspace",
           -6: "bad_ids", -7: "no_device", -8: "too_large"}
-B200_E_TOO_LARGE = -8
+B200_E_INVALID, B200_E_UNSUPPORTED, B200_E_TOO_LARGE = -1, -2, -8
 
 
 class B200Error(RuntimeError):
@@ -210,6 +210,10 @@ _SIGS.update({
     "b200_moe_ep_p2p_expert": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                       _i64, _vp, _i64, _i64, _vp, _int, _vp, _sz, _vp, _vp]),
     "b200_moe_ep_p2p_finish": (_int, [_vp, _i64, _int, _vp, _vp]),
+    "b200_mul_mat_tp_workspace_size": (_sz, [_int, _i64, _i64, _i64]),
+    "b200_mul_mat_tp": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _int, _vp,
+                               _sz, _vp, _vp]),
+    "b200_mul_mat_tp_finish": (_int, [_vp, _i64, _int, _vp, _vp]),
 })
 _SIGS.update({
     "b200_mul_mat_noalloc_max_workspace": (_sz, []),

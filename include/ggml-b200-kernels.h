@@ -234,6 +234,25 @@ int    b200_moe_ep_p2p_expert(int wtype, const void * local_stack, int64_t K, in
                               int * dev_err, void * stream);
 int    b200_moe_ep_p2p_finish(const int * flags, int64_t n_ranks, int epoch, int * dev_err, void * stream);
 
+/* ---- MUL_MAT with the weight rows split across GPUs (N-sharded), all-gather by the epilogue ----
+ * No counterpart in the reference (its MUL_MAT, ggml-rocket.cpp:4548-4871, runs on one device):
+ * the same op with an [N, K] weight cut into n_ranks row blocks, one per GPU. Rank r calls
+ *   b200_mul_mat_tp       its GEMM over w_shard (packed rows [col0, col0 + N_shard)) writes
+ *                         every output box into every rank's dst (peer_dst: a DEVICE array of
+ *                         n_ranks pointers to [M][ldd] f32 buffers, this rank's own included,
+ *                         the others mapped with b200_ep_shared_open) at column col0, then puts
+ *                         epoch into slot `rank` of every rank's flags (peer_flags, device array)
+ *   b200_mul_mat_tp_finish waits (bounded) until every slot of this rank's flags ([n_ranks][4]
+ *                         int32) holds epoch: then this rank's dst holds all N columns.
+ * epoch must differ from the flags' previous contents (count calls from 1). col0 % 16 == 0,
+ * N_shard % 16 == 0, ldd % 4 == 0; the workspace is b200_mul_mat_tp_workspace_size bytes. */
+size_t b200_mul_mat_tp_workspace_size(int wtype, int64_t M, int64_t N_shard, int64_t K);
+int    b200_mul_mat_tp(int wtype, const void * w_shard, int64_t N_shard, int64_t col0, int64_t K,
+                       const float * src1, int64_t lda, int64_t M, float * const * peer_dst, int64_t ldd,
+                       int64_t n_ranks, int64_t rank, int * const * peer_flags, int epoch, void * workspace,
+                       size_t workspace_bytes, int * dev_err, void * stream);
+int    b200_mul_mat_tp_finish(const int * flags, int64_t n_ranks, int epoch, int * dev_err, void * stream);
+
 #ifdef __cplusplus
 }
 #endif
