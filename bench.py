@@ -498,8 +498,11 @@ def run_moe(args):
             g.check(rc, "mul_mat_id")
 
         def layer():
-            one(w_gate, H, F, x, 1, y_gate)
-            one(w_up, H, F, x, 1, y_up)
+            # gate and up read the same x and ids: one route and gather-pack for both (the group
+            # graph_compute forms from the two MUL_MAT_ID nodes)
+            rc = g.mul_mat_id_group(wt, [w_gate, w_up], [F, F], H, E, x, H * 4, H * 4, 1, ids, 4, top * 4, top, T,
+                                    [y_gate, y_up], [F * 4, F * 4], [top * F * 4, top * F * 4], ws, err)
+            g.check(rc, "mul_mat_id_group")
             one(w_down, F, H, h, top, y_down)
 
     stream = torch.cuda.current_stream()

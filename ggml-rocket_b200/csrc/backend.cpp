@@ -694,24 +694,42 @@ bool node_fusable(const b200_tensor* op) {
     return a->ne[2] == 1 && a->ne[3] == 1 && bb->ne[2] == 1 && bb->ne[3] == 1 && ggml_backend_b200_supports_op(op);
 }
 
-int do_mul_mat_id(b200_backend* b, b200_tensor* op) {
-    const b200_tensor* as = op->src[0];
-    const b200_tensor* bb = op->src[1];
-    const b200_tensor* ids = op->src[2];
-    const int64_t K = as->ne[0], N = as->ne[1], n_expert = as->ne[2];
+// MUL_MAT_ID, and a group of MUL_MAT_IDs reading the same b and ids (a MoE layer's gate and up
+// projections): the route and the packed rows are made once for the group (b200_mul_mat_id_group).
+int do_mul_mat_id_group(b200_backend* b, b200_tensor* const* ops, int ng) {
+    const b200_tensor* op0 = ops[0];
+    const b200_tensor* bb = op0->src[1];
+    const b200_tensor* ids = op0->src[2];
+    const int64_t K = op0->src[0]->ne[0], n_expert = op0->src[0]->ne[2];
     const int64_t ne11 = bb->ne[1], n_used = ids->ne[0], n_tokens = ids->ne[1];
+    std::vector<const void*> w(ng);
+    std::vector<int64_t> Ns(ng), nb1(ng), nb2(ng);
+    std::vector<float*> dsts(ng);
     int kt = 0;
-    const std::string key = weight_key(as);
-    void* w = pack_weight(b, key, as->type, as->data, as->on_device != 0, N * n_expert, K, &kt);
-    if (!w) return B200_E_CUDA;
-    if (!key.empty() && !b->moe_seen[key]) {
-        b->moe_seen[key] = true;
-        b->moe_resident++;
-    } else if (key.empty()) {
-        b->moe_streamed++;
+    for (int g = 0; g < ng; g++) {
+        const b200_tensor* as = ops[g]->src[0];
+        const std::string key = weight_key(as);
+        int ktg = 0;
+        w[g] = pack_weight(b, key, as->type, as->data, as->on_device != 0, as->ne[1] * n_expert, K, &ktg);
+        if (!w[g]) return B200_E_CUDA;
+        if (g == 0) kt = ktg;
+        else if (ktg != kt) return B200_E_UNSUPPORTED;
+        if (!key.empty() && !b->moe_seen[key]) {
+            b->moe_seen[key] = true;
+            b->moe_resident++;
+        } else if (key.empty()) {
+            b->moe_streamed++;
+        }
+        Ns[g] = as->ne[1];
+        nb1[g] = (int64_t)ops[g]->nb[1];
+        nb2[g] = (int64_t)ops[g]->nb[2];
     }
-    const size_t need_ws = b200_mul_mat_id_workspace_size(K, N, n_expert, n_used, n_tokens);
-    size_t need_io = staged_size(bb) + staged_size(ids) + (op->on_device ? 0 : ((nbytes(op) + 255) & ~(size_t)255));
+    size_t need_ws = 0;
+    for (int g = 0; g < ng; g++)
+        need_ws = std::max(need_ws, b200_mul_mat_id_workspace_size(K, Ns[g], n_expert, n_used, n_tokens));
+    size_t need_io = staged_size(bb) + staged_size(ids);
+    for (int g = 0; g < ng; g++)
+        if (!ops[g]->on_device) need_io += (nbytes(ops[g]) + 255) & ~(size_t)255;
     if (!grow(&b->io, &b->io_bytes, need_io, b->stream)) return B200_E_CUDA;
     if (!grow(&b->ws, &b->ws_bytes, need_ws, b->stream)) return B200_E_CUDA;
     size_t io_off = 0;
@@ -719,20 +737,25 @@ int do_mul_mat_id(b200_backend* b, b200_tensor* op) {
     const void* bd = stage_in(b, bb, &io_off, &ok);
     const void* idd = stage_in(b, ids, &io_off, &ok);
     if (!ok) return B200_E_CUDA;
-    char* dd;
-    if (op->on_device) {
-        dd = static_cast<char*>(op->data);
-    } else {
-        io_off = (io_off + 255) & ~(size_t)255;
-        dd = static_cast<char*>(b->io) + io_off;
+    for (int g = 0; g < ng; g++) {
+        if (ops[g]->on_device) {
+            dsts[g] = static_cast<float*>(ops[g]->data);
+        } else {
+            io_off = (io_off + 255) & ~(size_t)255;
+            dsts[g] = reinterpret_cast<float*>(static_cast<char*>(b->io) + io_off);
+            io_off += nbytes(ops[g]);
+        }
     }
-    int rc = b200_mul_mat_id(kt, w, K, N, n_expert, static_cast<const float*>(bd), (int64_t)bb->nb[1],
-                             (int64_t)bb->nb[2], ne11, static_cast<const int32_t*>(idd), (int64_t)ids->nb[0],
-                             (int64_t)ids->nb[1], n_used, n_tokens, reinterpret_cast<float*>(dd), (int64_t)op->nb[1],
-                             (int64_t)op->nb[2], b->ws, b->ws_bytes, b->dev_err, b->stream);
+    int rc = b200_mul_mat_id_group(ng, kt, w.data(), Ns.data(), K, n_expert, static_cast<const float*>(bd),
+                                   (int64_t)bb->nb[1], (int64_t)bb->nb[2], ne11, static_cast<const int32_t*>(idd),
+                                   (int64_t)ids->nb[0], (int64_t)ids->nb[1], n_used, n_tokens, dsts.data(), nb1.data(),
+                                   nb2.data(), b->ws, b->ws_bytes, b->dev_err, b->stream);
     if (rc != B200_OK) return rc;
-    if (!op->on_device && cudaMemcpyAsync(op->data, dd, nbytes(op), cudaMemcpyDeviceToHost, b->stream) != cudaSuccess)
-        return B200_E_CUDA;
+    for (int g = 0; g < ng; g++) {
+        if (!ops[g]->on_device &&
+            cudaMemcpyAsync(ops[g]->data, dsts[g], nbytes(ops[g]), cudaMemcpyDeviceToHost, b->stream) != cudaSuccess)
+            return B200_E_CUDA;
+    }
     int h = 0;
     cudaMemcpyAsync(&h, b->dev_err, sizeof(int), cudaMemcpyDeviceToHost, b->stream);
     if (cudaStreamSynchronize(b->stream) != cudaSuccess) {
@@ -750,8 +773,19 @@ int do_mul_mat_id(b200_backend* b, b200_tensor* op) {
         logf("E", "MUL_MAT_ID: device error word %d\n", h);
         return B200_E_DEVICE;
     }
-    b->route_ops["moe"]++;
+    b->route_ops["moe"] += ng;
+    if (ng > 1) b->route_ops["moe_grouped"] += ng;
     return B200_OK;
+}
+
+int do_mul_mat_id(b200_backend* b, b200_tensor* op) { return do_mul_mat_id_group(b, &op, 1); }
+
+// Members of one MUL_MAT_ID group: the same b and ids tensors, the same K, expert count and weight
+// type (each member's stack is a leaf, so hoisting a later member cannot skip a dependency).
+static bool mmid_groupable(const b200_tensor* a, const b200_tensor* c) {
+    return c->op == B200_OP_MUL_MAT_ID && c->src[1] == a->src[1] && c->src[2] == a->src[2] &&
+           c->src[0]->ne[0] == a->src[0]->ne[0] && c->src[0]->ne[2] == a->src[0]->ne[2] &&
+           c->src[0]->type == a->src[0]->type && ggml_backend_b200_supports_op(c);
 }
 
 int do_flash_attn(b200_backend* b, b200_tensor* op) {
@@ -981,11 +1015,28 @@ int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes,
                     status = B200_STATUS_FAILED;
                     break;
                 }
-                const int rc = do_mul_mat_id(b, node);
+                std::vector<b200_tensor*> group{node};
+                std::vector<int> gidx{i};
+                if (fuse && breaker_allow(b->brk_fused)) {
+                    for (int j = i + 1; j < n && group.size() < 4; j++) {
+                        if (!done[j] && mmid_groupable(node, nodes[j])) {
+                            group.push_back(nodes[j]);
+                            gidx.push_back(j);
+                        }
+                    }
+                }
+                int rc = do_mul_mat_id_group(b, group.data(), (int)group.size());
+                if (group.size() > 1) breaker_note(b->brk_fused, rc, "grouped MUL_MAT_ID");
+                if (rc != B200_OK && rc != B200_E_BAD_IDS && group.size() > 1) {
+                    // the group's optional route failed: run the members one by one
+                    rc = B200_OK;
+                    for (size_t g = 0; g < group.size() && rc == B200_OK; g++) rc = do_mul_mat_id(b, group[g]);
+                }
                 if (rc != B200_OK) {
                     logf("E", "graph_compute: MUL_MAT_ID handler failed (%d)\n", rc);
                     status = B200_STATUS_FAILED;
                 }
+                for (int g : gidx) done[g] = true;
                 break;
             }
             case B200_OP_FLASH_ATTN_EXT: {

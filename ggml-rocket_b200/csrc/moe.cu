@@ -281,14 +281,22 @@ static int moe_token_tile(int64_t R, int64_t n_expert) {
     return avg <= 32 ? 32 : avg <= 64 ? 64 : avg < 96 ? 128 : 256;
 }
 
-int mul_mat_id_impl(int wtype, const void* as_packed, int64_t K, int64_t N, int64_t n_expert, const float* b,
-                    int64_t b_nb1, int64_t b_nb2, int64_t ne11, const int32_t* ids, int64_t ids_nb0, int64_t ids_nb1,
-                    int64_t n_used, int64_t n_tokens, float* dst, int64_t d_nb1, int64_t d_nb2, void* workspace,
-                    size_t ws_bytes, int* dev_err, cudaStream_t st) {
-    if (!as_packed || !b || !ids || !dst || !dev_err || K <= 0 || N <= 0 || n_expert <= 0 || n_used <= 0 ||
-        n_tokens <= 0 || ne11 <= 0)
+// MUL_MAT_ID over n_members expert stacks that share the input rows b and the routing ids (a
+// layer's gate and up projections): the route and the gather-pack run once, then one grouped
+// GEMM per member reads the same sorted fp16 rows. n_members = 1 is the plain op.
+int mul_mat_id_group_impl(int n_members, int wtype, const void* const* as_packed, const int64_t* Ns, int64_t K,
+                          int64_t n_expert, const float* b, int64_t b_nb1, int64_t b_nb2, int64_t ne11,
+                          const int32_t* ids, int64_t ids_nb0, int64_t ids_nb1, int64_t n_used, int64_t n_tokens,
+                          float* const* dsts, const int64_t* d_nb1s, const int64_t* d_nb2s, void* workspace,
+                          size_t ws_bytes, int* dev_err, cudaStream_t st) {
+    if (n_members <= 0 || !as_packed || !Ns || !dsts || !d_nb1s || !d_nb2s || !b || !ids || !dev_err || K <= 0 ||
+        n_expert <= 0 || n_used <= 0 || n_tokens <= 0 || ne11 <= 0)
         return B200_E_INVALID;
-    if (!weight_type_supported(wtype, K) || K % 32 != 0 || N % 16 != 0 || K % 4 != 0) return B200_E_UNSUPPORTED;
+    for (int m = 0; m < n_members; m++)
+        if (!as_packed[m] || !dsts[m] || Ns[m] <= 0) return B200_E_INVALID;
+    if (!weight_type_supported(wtype, K) || K % 32 != 0 || K % 4 != 0) return B200_E_UNSUPPORTED;
+    for (int m = 0; m < n_members; m++)
+        if (Ns[m] % 16 != 0) return B200_E_UNSUPPORTED;
     if (n_expert > 4096 || n_used * n_tokens > (1 << 28)) return B200_E_UNSUPPORTED;
     if ((b_nb1 % 16) || (b_nb2 % 16) || (reinterpret_cast<uintptr_t>(b) & 15u)) return B200_E_UNSUPPORTED;
     const MoeLayout L = moe_layout(K, n_expert, n_used, n_tokens);
@@ -312,17 +320,30 @@ int mul_mat_id_impl(int wtype, const void* as_packed, int64_t K, int64_t N, int6
         cudaFuncSetAttribute(moe_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)place_smem) !=
             cudaSuccess)
         return B200_E_UNSUPPORTED;
-    launch_pdl(moe_hist_kernel, dim3(nb), dim3(ROUTE_THREADS), hist_smem, st, ids, ids_nb0, ids_nb1, (int)n_used, (int)R, (int)n_expert,
-                                                          counts, bad);
-    launch_pdl(moe_scan_kernel, dim3(1), dim3(ROUTE_THREADS), hist_smem, st, counts, bad, nb, (int)n_expert, bt, off, tiles, dev_err);
-    launch_pdl(moe_place_kernel, dim3(nb), dim3(ROUTE_THREADS), place_smem, st, ids, ids_nb0, ids_nb1, (int)n_used, (int)R,
-                                                            (int)n_expert, counts, off, slot, tok);
+    launch_pdl(moe_hist_kernel, dim3(nb), dim3(ROUTE_THREADS), hist_smem, st, ids, ids_nb0, ids_nb1, (int)n_used,
+               (int)R, (int)n_expert, counts, bad);
+    launch_pdl(moe_scan_kernel, dim3(1), dim3(ROUTE_THREADS), hist_smem, st, counts, bad, nb, (int)n_expert, bt, off,
+               tiles, dev_err);
+    launch_pdl(moe_place_kernel, dim3(nb), dim3(ROUTE_THREADS), place_smem, st, ids, ids_nb0, ids_nb1, (int)n_used,
+               (int)R, (int)n_expert, counts, off, slot, tok);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
     const int rc = launch_gather_pack(b, b_nb1, b_nb2, ne11, K, slot, tok, off + n_expert, R, a16, scales, st);
     if (rc != B200_OK) return rc;
+    for (int m = 0; m < n_members; m++) {
+        const int r2 = gemm_grouped_impl(wtype, as_packed[m], Ns[m], K, n_expert, a16, scales, R, bt, off, tiles, slot,
+                                         tok, dsts[m], d_nb1s[m], d_nb2s[m], dev_err, st);
+        if (r2 != B200_OK) return r2;
+    }
+    return B200_OK;
+}
 
-    return gemm_grouped_impl(wtype, as_packed, N, K, n_expert, a16, scales, R, bt, off, tiles, slot, tok, dst, d_nb1,
-                             d_nb2, dev_err, st);
+int mul_mat_id_impl(int wtype, const void* as_packed, int64_t K, int64_t N, int64_t n_expert, const float* b,
+                    int64_t b_nb1, int64_t b_nb2, int64_t ne11, const int32_t* ids, int64_t ids_nb0, int64_t ids_nb1,
+                    int64_t n_used, int64_t n_tokens, float* dst, int64_t d_nb1, int64_t d_nb2, void* workspace,
+                    size_t ws_bytes, int* dev_err, cudaStream_t st) {
+    if (!as_packed || !dst) return B200_E_INVALID;
+    return mul_mat_id_group_impl(1, wtype, &as_packed, &N, K, n_expert, b, b_nb1, b_nb2, ne11, ids, ids_nb0, ids_nb1,
+                                 n_used, n_tokens, &dst, &d_nb1, &d_nb2, workspace, ws_bytes, dev_err, st);
 }
 
 }  // namespace b200
@@ -342,6 +363,17 @@ int b200_mul_mat_id(int wtype, const void* as_packed, int64_t K, int64_t N, int6
     return b200::mul_mat_id_impl(wtype, as_packed, K, N, n_expert, b, b_nb1, b_nb2, ne11, ids, ids_nb0, ids_nb1, n_used,
                                  n_tokens, dst, d_nb1, d_nb2, workspace, workspace_bytes, dev_err,
                                  static_cast<cudaStream_t>(stream));
+}
+
+int b200_mul_mat_id_group(int n_members, int wtype, const void* const* as_packed, const int64_t* N, int64_t K,
+                          int64_t n_expert, const float* b, int64_t b_nb1, int64_t b_nb2, int64_t ne11,
+                          const int32_t* ids, int64_t ids_nb0, int64_t ids_nb1, int64_t n_used, int64_t n_tokens,
+                          float* const* dst, const int64_t* d_nb1, const int64_t* d_nb2, void* workspace,
+                          size_t workspace_bytes, int* dev_err, void* stream) {
+    if (n_members > 16) return B200_E_UNSUPPORTED;
+    return b200::mul_mat_id_group_impl(n_members, wtype, as_packed, N, K, n_expert, b, b_nb1, b_nb2, ne11, ids, ids_nb0,
+                                       ids_nb1, n_used, n_tokens, dst, d_nb1, d_nb2, workspace, workspace_bytes,
+                                       dev_err, static_cast<cudaStream_t>(stream));
 }
 
 int b200_mul_mat_id_route_view(int64_t K, int64_t n_expert, int64_t n_used, int64_t n_tokens, size_t* off_offset,

@@ -187,6 +187,8 @@ _BACKEND_SIGS = {
     "b200_mul_mat_id_workspace_size": (_sz, [_i64] * 5),
     "b200_mul_mat_id": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
                                _vp, _i64, _i64, _vp, _sz, _vp, _vp]),
+    "b200_mul_mat_id_group": (_int, [_int, _int, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64,
+                                     _i64, _i64, _vp, _vp, _vp, _vp, _sz, _vp, _vp]),
     "b200_mul_mat_id_route_view": (_int, [_i64, _i64, _i64, _i64, _c.POINTER(_sz), _c.POINTER(_sz),
                                           _c.POINTER(_sz)]),
 }
@@ -346,6 +348,19 @@ def mul_mat_id(wtype, as_packed, K, N, n_expert, b, b_nb1, b_nb2, ne11, ids, ids
     return lib().b200_mul_mat_id(wtype, _ptr(as_packed), K, N, n_expert, _ptr(b), b_nb1, b_nb2, ne11, _ptr(ids),
                                  ids_nb0, ids_nb1, n_used, n_tokens, _ptr(dst), d_nb1, d_nb2, _ptr(workspace),
                                  workspace.numel() * workspace.element_size(), _ptr(dev_err), _stream(stream))
+
+
+def mul_mat_id_group(wtype, stacks, Ns, K, n_expert, b, b_nb1, b_nb2, ne11, ids, ids_nb0, ids_nb1, n_used, n_tokens,
+                     dsts, d_nb1s, d_nb2s, workspace, dev_err, stream=None):
+    """MUL_MAT_IDs over several expert stacks sharing b and ids: one route and gather-pack, one
+    grouped GEMM per stack (b200_mul_mat_id_group)."""
+    n = len(stacks)
+    P = ctypes.c_void_p * n
+    I = ctypes.c_int64 * n
+    return lib().b200_mul_mat_id_group(n, wtype, P(*[_ptr(t) for t in stacks]), I(*Ns), K, n_expert, _ptr(b), b_nb1,
+                                       b_nb2, ne11, _ptr(ids), ids_nb0, ids_nb1, n_used, n_tokens,
+                                       P(*[_ptr(t) for t in dsts]), I(*d_nb1s), I(*d_nb2s), _ptr(workspace),
+                                       workspace.numel() * workspace.element_size(), _ptr(dev_err), _stream(stream))
 
 
 def mul_mat_id_route_view(K, n_expert, n_used, n_tokens):

@@ -154,6 +154,16 @@ int    b200_mul_mat_id(int wtype, const void * as_packed, int64_t K, int64_t N, 
                        const int32_t * ids, int64_t ids_nb0, int64_t ids_nb1, int64_t n_used, int64_t n_tokens,
                        float * dst, int64_t d_nb1, int64_t d_nb2,
                        void * workspace, size_t workspace_bytes, int * dev_err, void * stream);
+/* n_members MUL_MAT_IDs that read the same b and the same ids (a MoE layer's gate and up
+ * projections, ggml nodes sharing src1 and src2): the route and the gather-pack run once, then
+ * one grouped GEMM per member (its stack as_packed[m], N[m] output rows, dst[m] with strides
+ * d_nb1[m], d_nb2[m]). Host arrays of n_members entries (at most 16); the workspace is
+ * b200_mul_mat_id_workspace_size's. Each dst equals the member's own b200_mul_mat_id. */
+int    b200_mul_mat_id_group(int n_members, int wtype, const void * const * as_packed, const int64_t * N,
+                             int64_t K, int64_t n_expert, const float * b, int64_t b_nb1, int64_t b_nb2,
+                             int64_t ne11, const int32_t * ids, int64_t ids_nb0, int64_t ids_nb1, int64_t n_used,
+                             int64_t n_tokens, float * const * dst, const int64_t * d_nb1, const int64_t * d_nb2,
+                             void * workspace, size_t workspace_bytes, int * dev_err, void * stream);
 /* Byte offsets, inside the workspace, of the route arrays the last b200_mul_mat_id call wrote:
  * off int32 [n_expert + 1], row_slot int32 [n_used*n_tokens], row_tok int32 [n_used*n_tokens]. */
 int    b200_mul_mat_id_route_view(int64_t K, int64_t n_expert, int64_t n_used, int64_t n_tokens,

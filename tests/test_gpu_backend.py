@@ -155,3 +155,29 @@ def test_backend_mul_mat_id_and_bad_ids(cuda):
     assert be.graph_compute([d]) == g.STATUS_SUCCESS
     assert rel_err(out, want) <= 1e-2
     be.close()
+
+
+def test_backend_groups_mul_mat_ids_sharing_inputs(cuda):
+    """A MoE layer's gate and up (two MUL_MAT_ID nodes on the same b and ids) run as one group:
+    one route and gather-pack, one grouped GEMM per stack; each result matches the oracle."""
+    be = g.Backend()
+    rng = np.random.default_rng(8)
+    K, N, n_expert, n_tokens, n_used = 512, 128, 16, 96, 4
+    b = rng.standard_normal((n_tokens, 1, K)).astype(np.float32)
+    bt = g.make_tensor(g.F32, [K, 1, n_tokens], b)
+    ids = np.stack([rng.permutation(n_expert)[:n_used] for _ in range(n_tokens)]).astype(np.int32)
+    it = g.make_tensor(g.I32, [n_used, n_tokens], ids)
+    nodes, outs, raws = [], [], []
+    for name in ("blk.0.ffn_gate_exps.weight", "blk.0.ffn_up_exps.weight"):
+        raw = quants.quantize(g.Q4_K, (rng.standard_normal((n_expert * N, K)) * 0.02).astype(np.float32))
+        as_t = g.make_tensor(g.Q4_K, [K, N, n_expert], raw, name=name)
+        out = np.full((n_tokens, n_used, N), np.nan, np.float32)
+        nodes.append(g.make_tensor(g.F32, [N, n_used, n_tokens], out, op=g.OP_MUL_MAT_ID, srcs=[as_t, bt, it]))
+        outs.append(out)
+        raws.append(raw)
+    assert be.graph_compute(nodes) == g.STATUS_SUCCESS
+    for out, raw in zip(outs, raws):
+        want = oracle.mul_mat_id(g.Q4_K, raw.reshape(n_expert, N, -1), K, N, n_expert, b, ids)
+        assert rel_err(out, want) <= 1e-2
+    assert be.route_ops("moe") == 2 and be.route_ops("moe_grouped") == 2
+    be.close()

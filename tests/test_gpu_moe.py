@@ -90,3 +90,41 @@ def test_moe_bad_id_is_reported(cuda):
     got, err, route = run_moe(torch, 12, ws_native, 256, 64, 8, b, ids)
     assert err == 100                     # B200_DEV_BAD_IDS
     assert np.all(np.isnan(got))          # nothing written
+
+
+@pytest.mark.parametrize("wtype,K,Ns,n_expert,n_tokens,n_used,ne11", [
+    (12, 2048, (768, 768), 32, 256, 8, 1),      # a MoE layer's gate and up
+    (12, 512, (256, 128, 64), 16, 100, 4, 4),   # three members, different N, per-slot b rows
+    (14, 512, (128,), 8, 70, 3, 1),             # one member: the plain op
+])
+def test_moe_group_equals_members(cuda, wtype, K, Ns, n_expert, n_tokens, n_used, ne11):
+    """b200_mul_mat_id_group (one route and gather-pack for stacks sharing b and ids) gives every
+    member exactly its own b200_mul_mat_id result: the same sorted rows, the same kernels."""
+    import torch
+    import ggml_b200 as g
+    rng = np.random.default_rng(5 + wtype + len(Ns))
+    _, b, ids = make_case(rng, wtype, K, Ns[0], n_expert, n_tokens, n_used, ne11)
+    bd = torch.from_numpy(np.ascontiguousarray(b)).cuda()
+    idd = torch.from_numpy(np.ascontiguousarray(ids)).cuda()
+    stacks, dsts, wants = [], [], []
+    for m, N in enumerate(Ns):
+        w = (rng.standard_normal((n_expert * N, K)) * 0.02).astype(np.float32)
+        native = quants.quantize(wtype, w)
+        raw = torch.from_numpy(np.ascontiguousarray(native).reshape(-1)).cuda()
+        packed = torch.empty(g.weight_packed_size(wtype, N * n_expert, K), dtype=torch.uint8, device="cuda")
+        g.weight_pack(wtype, raw, N * n_expert, K, packed)
+        stacks.append(packed)
+        dsts.append(torch.full((n_tokens, n_used, N), float("nan"), dtype=torch.float32, device="cuda"))
+        want, err, _ = run_moe(torch, wtype, native, K, N, n_expert, b, ids)
+        assert err == 0
+        wants.append(want)
+    ws = torch.zeros(max(g.mul_mat_id_workspace_size(K, N, n_expert, n_used, n_tokens) for N in Ns),
+                     dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc = g.mul_mat_id_group(wtype, stacks, list(Ns), K, n_expert, bd, K * 4, ne11 * K * 4, ne11, idd, 4, n_used * 4,
+                            n_used, n_tokens, dsts, [N * 4 for N in Ns], [n_used * N * 4 for N in Ns], ws, err)
+    torch.cuda.synchronize()
+    assert rc == 0 and int(err.item()) == 0
+    for d, want in zip(dsts, wants):
+        got = d.cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
