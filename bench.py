@@ -483,10 +483,12 @@ def run_moe(args):
         ep = PeerExpertParallelMulMatId(T, top, max(H, F), max(H, F), ops=DeviceOps(err))
 
         def layer():
-            # each op's result is a view of the exchange's return buffer; consume it (copy into
-            # the layer's tensor) before the next op reuses that buffer
-            y_gate.copy_(ep(wt, w_gate, H, F, E, x, 1, ids))
-            y_up.copy_(ep(wt, w_up, H, F, E, x, 1, ids))
+            # each op's result is a view of the exchange's return buffers; consume it (copy into
+            # the layer's tensor) before the next op reuses them. Gate and up read the same x and
+            # ids: one push, route and gather for both.
+            g_out, u_out = ep.grouped(wt, [w_gate, w_up], H, [F, F], E, x, 1, ids)
+            y_gate.copy_(g_out)
+            y_up.copy_(u_out)
             y_down.copy_(ep(wt, w_down, F, H, E, h, top, ids))
     else:
         ws = torch.empty(max(g.mul_mat_id_workspace_size(H, F, E, top, T), g.mul_mat_id_workspace_size(F, H, E, top, T)),

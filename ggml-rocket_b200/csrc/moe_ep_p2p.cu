@@ -322,19 +322,24 @@ size_t b200_moe_ep_p2p_expert_workspace_size(int64_t n_ranks, int64_t cap, int64
     return b200::p2p_layout(n_ranks, cap, K, n_local, n_used).total;
 }
 
-int b200_moe_ep_p2p_expert(int wtype, const void* local_stack, int64_t K, int64_t N, int64_t n_local, int64_t expert0,
-                           const void* recv_a16, const int32_t* recv_meta, const int* flags, int64_t n_ranks,
-                           int64_t rank, int64_t n_used, int64_t cap, int64_t pairs_hint, float* const* peer_ret,
-                           int64_t ret_nb1, int64_t ret_nb2, int* const* peer_flags, int epoch, void* workspace,
-                           size_t workspace_bytes, int* dev_err, void* stream) {
+int b200_moe_ep_p2p_expert_group(int n_members, int wtype, const void* const* local_stacks, const int64_t* Ns,
+                                 int64_t K, int64_t n_local, int64_t expert0, const void* recv_a16,
+                                 const int32_t* recv_meta, const int* flags, int64_t n_ranks, int64_t rank,
+                                 int64_t n_used, int64_t cap, int64_t pairs_hint, float* const* const* peer_rets,
+                                 const int64_t* ret_nb1, const int64_t* ret_nb2, int* const* peer_flags, int epoch,
+                                 void* workspace, size_t workspace_bytes, int* dev_err, void* stream) {
     using namespace b200;
-    if (!local_stack || !recv_a16 || !recv_meta || !flags || !peer_ret || !peer_flags || !dev_err || K <= 0 ||
-        N <= 0 || n_local <= 0 || expert0 < 0 || n_ranks <= 0 || rank < 0 || rank >= n_ranks || n_used <= 0 ||
-        cap <= 0)
+    if (n_members <= 0 || !local_stacks || !Ns || !peer_rets || !ret_nb1 || !ret_nb2 || !recv_a16 || !recv_meta ||
+        !flags || !peer_flags || !dev_err || K <= 0 || n_local <= 0 || expert0 < 0 || n_ranks <= 0 || rank < 0 ||
+        rank >= n_ranks || n_used <= 0 || cap <= 0)
         return B200_E_INVALID;
-    if (!weight_type_supported(wtype, K) || K % 32 != 0 || N % 16 != 0 || n_used > 32 || n_local > 4096 ||
-        n_ranks > 64 || (ret_nb1 % 16) || (ret_nb2 % 16))
+    if (n_members > 16 || !weight_type_supported(wtype, K) || K % 32 != 0 || n_used > 32 || n_local > 4096 ||
+        n_ranks > 64)
         return B200_E_UNSUPPORTED;
+    for (int m = 0; m < n_members; m++) {
+        if (!local_stacks[m] || !peer_rets[m] || Ns[m] <= 0) return B200_E_INVALID;
+        if (Ns[m] % 16 != 0 || (ret_nb1[m] % 16) || (ret_nb2[m] % 16)) return B200_E_UNSUPPORTED;
+    }
     const P2pLayout L = p2p_layout(n_ranks, cap, K, n_local, n_used);
     if (!workspace || workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
         return B200_E_WORKSPACE;
@@ -366,23 +371,36 @@ int b200_moe_ep_p2p_expert(int wtype, const void* local_stack, int64_t K, int64_
             cudaSuccess)
         return B200_E_UNSUPPORTED;
     if (cudaMemsetAsync(ecnt, 0, (size_t)n_local * 4, st) != cudaSuccess) return B200_E_CUDA;
-    launch_pdl(p2p_route_count_kernel, dim3(nb), dim3(P2PC), hist_smem, st, recv_meta, region, G, cap, (int)n_used, (int)expert0,
-                                                        (int)n_local, ecnt, bsum, bad);
+    launch_pdl(p2p_route_count_kernel, dim3(nb), dim3(P2PC), hist_smem, st, recv_meta, region, G, cap, (int)n_used,
+               (int)expert0, (int)n_local, ecnt, bsum, bad);
     ep_route_scan_public(ecnt, bsum, bad, nb, (int)n_local, bt, off, tiles, cursor, dev_err, st);
-    launch_pdl(p2p_route_place_kernel, dim3(nb), dim3(P2PC), 0, st, recv_meta, region, G, cap, (int)n_used, (int)expert0, bad + nb,
-                                                cursor, prow, psrc, ptok, pslot);
-    // 3. gather the fp16 rows in expert order
+    launch_pdl(p2p_route_place_kernel, dim3(nb), dim3(P2PC), 0, st, recv_meta, region, G, cap, (int)n_used,
+               (int)expert0, bad + nb, cursor, prow, psrc, ptok, pslot);
+    // 3. gather the fp16 rows in expert order (once for every member)
     const int64_t gcap = (int64_t)device_sm_count() * 8;
-    launch_pdl(p2p_gather_kernel, dim3((unsigned)(rows_max < gcap ? rows_max : gcap)), dim3(256), 0, st, 
-        static_cast<const __half*>(recv_a16), recv_meta, prow, off + n_local, (int)n_used, (int)K, a16, scales);
+    launch_pdl(p2p_gather_kernel, dim3((unsigned)(rows_max < gcap ? rows_max : gcap)), dim3(256), 0, st,
+               static_cast<const __half*>(recv_a16), recv_meta, prow, off + n_local, (int)n_used, (int)K, a16, scales);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
-    // 4. the grouped GEMM stores each output row into its home rank's ret over NVLink
-    const int rc = gemm_grouped_impl(wtype, local_stack, N, K, n_local, a16, scales, rows_max, bt, off, tiles, pslot,
-                                     ptok, nullptr, ret_nb1, ret_nb2, dev_err, st, psrc, peer_ret);
-    if (rc != B200_OK) return rc;
+    // 4. per member, the grouped GEMM stores each output row into its home rank's ret over NVLink
+    for (int m = 0; m < n_members; m++) {
+        const int rc = gemm_grouped_impl(wtype, local_stacks[m], Ns[m], K, n_local, a16, scales, rows_max, bt, off,
+                                         tiles, pslot, ptok, nullptr, ret_nb1[m], ret_nb2[m], dev_err, st, psrc,
+                                         peer_rets[m]);
+        if (rc != B200_OK) return rc;
+    }
     // 5. tell every home rank its rows are in place
     launch_pdl(ep_signal_kernel, dim3(1), dim3(64), 0, st, peer_flags, G, (int)rank, G, epoch, nullptr);
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
+int b200_moe_ep_p2p_expert(int wtype, const void* local_stack, int64_t K, int64_t N, int64_t n_local, int64_t expert0,
+                           const void* recv_a16, const int32_t* recv_meta, const int* flags, int64_t n_ranks,
+                           int64_t rank, int64_t n_used, int64_t cap, int64_t pairs_hint, float* const* peer_ret,
+                           int64_t ret_nb1, int64_t ret_nb2, int* const* peer_flags, int epoch, void* workspace,
+                           size_t workspace_bytes, int* dev_err, void* stream) {
+    return b200_moe_ep_p2p_expert_group(1, wtype, &local_stack, &N, K, n_local, expert0, recv_a16, recv_meta, flags,
+                                        n_ranks, rank, n_used, cap, pairs_hint, &peer_ret, &ret_nb1, &ret_nb2,
+                                        peer_flags, epoch, workspace, workspace_bytes, dev_err, stream);
 }
 
 int b200_moe_ep_p2p_finish(const int* flags, int64_t n_ranks, int epoch, int* dev_err, void* stream) {

@@ -212,6 +212,8 @@ _SIGS.update({
     "b200_moe_ep_p2p_expert": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                       _i64, _vp, _i64, _i64, _vp, _int, _vp, _sz, _vp, _vp]),
     "b200_moe_ep_p2p_finish": (_int, [_vp, _i64, _int, _vp, _vp]),
+    "b200_moe_ep_p2p_expert_group": (_int, [_int, _int, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i64,
+                                            _i64, _i64, _vp, _vp, _vp, _vp, _int, _vp, _sz, _vp, _vp]),
     "b200_mul_mat_tp_workspace_size": (_sz, [_int, _i64, _i64, _i64]),
     "b200_mul_mat_tp": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _int, _vp,
                                _sz, _vp, _vp]),

@@ -158,7 +158,7 @@ class PeerExpertParallelMulMatId:
     return buffer holding dst [n_tokens, n_used, N] (valid until the next call), and copies it
     into dst when one is given."""
 
-    def __init__(self, n_tokens_max, n_used, K_max, N_max, group=None, device=None, ops=None):
+    def __init__(self, n_tokens_max, n_used, K_max, N_max, group=None, device=None, ops=None, n_members_max=2):
         self.group = group
         self.G = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -169,16 +169,19 @@ class PeerExpertParallelMulMatId:
         G, dev = self.G, self.dev
         self.recv_a16 = torch.zeros((G, self.cap, K_max), dtype=torch.float16, device=dev)
         self.recv_meta = torch.zeros((G, self.cap, n_used + 3), dtype=torch.int32, device=dev)
-        self.ret = torch.zeros((n_tokens_max, n_used, N_max), dtype=torch.float32, device=dev)
+        # one return buffer per member of a group op (gate and up share their rows)
+        self.n_members_max = n_members_max
+        self.rets = torch.zeros((n_members_max, n_tokens_max, n_used, N_max), dtype=torch.float32, device=dev)
+        self.ret = self.rets[0]
         self.flags = torch.zeros((2 * G, 4), dtype=torch.int32, device=dev)
         torch.cuda.synchronize(dev)
-        mine = [self._export(t) for t in (self.recv_a16, self.recv_meta, self.ret, self.flags)]
+        mine = [self._export(t) for t in (self.recv_a16, self.recv_meta, self.rets, self.flags)]
         allh = [None] * G
         dist.all_gather_object(allh, mine, group=group)
         self._opened = []
         ptrs = [[0] * G for _ in range(4)]
         for q in range(G):
-            for b, t in enumerate((self.recv_a16, self.recv_meta, self.ret, self.flags)):
+            for b, t in enumerate((self.recv_a16, self.recv_meta, self.rets, self.flags)):
                 if q == self.rank:
                     ptrs[b][q] = t.data_ptr()
                 else:
@@ -189,6 +192,9 @@ class PeerExpertParallelMulMatId:
                     self._opened.append(base.value)
                     ptrs[b][q] = base.value + off
         self.peer = [torch.tensor(p, dtype=torch.int64, device=dev) for p in ptrs]
+        member_bytes = self.rets[0].numel() * 4
+        self.peer_rets = [torch.tensor([p + m * member_bytes for p in ptrs[2]], dtype=torch.int64, device=dev)
+                          for m in range(n_members_max)]
         self.epoch = 0
         self.last_stats = {}
         dist.barrier(group=group)
@@ -209,10 +215,20 @@ class PeerExpertParallelMulMatId:
         self._opened = []
 
     def __call__(self, wtype, local_stack, K, N, n_expert, b, ne11, ids, dst=None, stream=None):
+        out = self.grouped(wtype, [local_stack], K, [N], n_expert, b, ne11, ids, stream=stream)[0]
+        if dst is not None:
+            dst.copy_(out)
+        return out
+
+    def grouped(self, wtype, local_stacks, K, Ns, n_expert, b, ne11, ids, stream=None):
+        """Several MUL_MAT_IDs over the same b and ids (a layer's gate and up): the rows are
+        dispatched and pushed once, each owner routes and gathers them once and runs one grouped
+        GEMM per stack. Returns one view of the return buffers per member, [n_tokens, n_used, N]."""
         G, ops = self.G, self.ops
         n_tokens, n_used = ids.shape
-        if n_expert % G or n_used != self.n_used or K > self.K_max or N > self.N_max or \
-                n_tokens * n_used > self.cap:
+        nm = len(local_stacks)
+        if n_expert % G or n_used != self.n_used or K > self.K_max or max(Ns) > self.N_max or \
+                n_tokens * n_used > self.cap or nm > self.n_members_max:
             raise ValueError("op outside the sizes this exchange was built for")
         n_local = n_expert // G
         self.epoch += 1
@@ -225,14 +241,14 @@ class PeerExpertParallelMulMatId:
             n_tokens * n_used, g._stream(stream)), "moe_ep_p2p_push")
         ws_bytes = lib.b200_moe_ep_p2p_expert_workspace_size(G, self.cap, K, n_local, n_used)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=self.dev)
-        g.check(lib.b200_moe_ep_p2p_expert(
-            wtype, g._ptr(local_stack), K, N, n_local, self.rank * n_local, g._ptr(self.recv_a16),
-            g._ptr(self.recv_meta), g._ptr(self.flags), G, self.rank, n_used, self.cap, n_tokens * n_used,
-            g._ptr(self.peer[2]), self.N_max * 4, n_used * self.N_max * 4, g._ptr(self.peer[3]), self.epoch,
-            g._ptr(ws), ws_bytes, g._ptr(err), g._stream(stream)), "moe_ep_p2p_expert")
+        P = g._c.c_void_p * nm
+        I = g._c.c_int64 * nm
+        g.check(lib.b200_moe_ep_p2p_expert_group(
+            nm, wtype, P(*[g._ptr(t) for t in local_stacks]), I(*Ns), K, n_local, self.rank * n_local,
+            g._ptr(self.recv_a16), g._ptr(self.recv_meta), g._ptr(self.flags), G, self.rank, n_used, self.cap,
+            n_tokens * n_used, P(*[g._ptr(self.peer_rets[m]) for m in range(nm)]), I(*([self.N_max * 4] * nm)),
+            I(*([n_used * self.N_max * 4] * nm)), g._ptr(self.peer[3]), self.epoch, g._ptr(ws), ws_bytes,
+            g._ptr(err), g._stream(stream)), "moe_ep_p2p_expert_group")
         g.check(lib.b200_moe_ep_p2p_finish(g._ptr(self.flags), G, self.epoch, g._ptr(err), g._stream(stream)),
                 "moe_ep_p2p_finish")
-        out = self.ret[:n_tokens, :, :N]
-        if dst is not None:
-            dst.copy_(out)
-        return out
+        return [self.rets[m][:n_tokens, :, :Ns[m]] for m in range(nm)]

@@ -243,6 +243,17 @@ int    b200_moe_ep_p2p_expert(int wtype, const void * local_stack, int64_t K, in
                               int * const * peer_flags, int epoch, void * workspace, size_t workspace_bytes,
                               int * dev_err, void * stream);
 int    b200_moe_ep_p2p_finish(const int * flags, int64_t n_ranks, int epoch, int * dev_err, void * stream);
+/* The owner step for n_members expert stacks that read the same pushed rows (a layer's gate and
+ * up): one wait, route and gather, then one grouped GEMM per member storing into its own return
+ * buffers (peer_rets[m]: a host array of n_members DEVICE arrays of n_ranks pointers), then one
+ * flag to every home. b200_moe_ep_p2p_expert is the one-member case. */
+int    b200_moe_ep_p2p_expert_group(int n_members, int wtype, const void * const * local_stacks,
+                                    const int64_t * N, int64_t K, int64_t n_local, int64_t expert0,
+                                    const void * recv_a16, const int32_t * recv_meta, const int * flags,
+                                    int64_t n_ranks, int64_t rank, int64_t n_used, int64_t cap, int64_t pairs_hint,
+                                    float * const * const * peer_rets, const int64_t * ret_nb1,
+                                    const int64_t * ret_nb2, int * const * peer_flags, int epoch, void * workspace,
+                                    size_t workspace_bytes, int * dev_err, void * stream);
 
 /* ---- MUL_MAT with the weight rows split across GPUs (N-sharded), all-gather by the epilogue ----
  * No counterpart in the reference (its MUL_MAT, ggml-rocket.cpp:4548-4871, runs on one device):

@@ -69,7 +69,23 @@ def main():
                 print(f"rank {rank} p2p case {(wtype, K, N, E, n_used, ne11, T)} rep {rep} mismatch: err "
                       f"{int(perr.item())} max {float((got - want).abs().max())}", flush=True)
             same = same and p_same
-        ok = ok and same
+        # a two-member group (gate and up over the same rows): the second stack is this rank's
+        # experts of a second weight; each member must equal its own single-GPU op
+        w2 = (np.random.default_rng(8).standard_normal((E * N, K)) * 0.02).astype(np.float32)
+        native2 = quants.quantize(wtype, w2)
+        local2 = pack(native2[rank * e_loc * rpe:(rank + 1) * e_loc * rpe], e_loc * N)
+        want2 = torch.full_like(dst, float("nan"))
+        rc = g.mul_mat_id(wtype, pack(native2, E * N), K, N, E, b, K * 4, ne11 * K * 4, ne11, ids, 4, n_used * 4,
+                          n_used, T, want2, N * 4, n_used * N * 4, ws, err)
+        perr = torch.zeros(1, dtype=torch.int32, device="cuda")
+        p2p.ops.dev_err = perr
+        g1, g2 = p2p.grouped(wtype, [local_stack, local2], K, [N, N], E, b, ne11, ids)
+        torch.cuda.synchronize()
+        g_same = rc == 0 and int(perr.item()) == 0 and bool(torch.equal(g1, want)) and bool(torch.equal(g2, want2))
+        if not g_same:
+            print(f"rank {rank} p2p group case {(wtype, K, N, E, n_used, ne11, T)} mismatch: err {int(perr.item())}",
+                  flush=True)
+        ok = ok and same and g_same
     p2p.close()
     dist.barrier()
     dist.destroy_process_group()
