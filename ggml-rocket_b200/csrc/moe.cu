@@ -242,7 +242,8 @@ int launch_gather_pack(const float* b, int64_t b_nb1, int64_t b_nb2, int64_t ne1
     const int64_t per = (K / 4 + 255) / 256;
     const dim3 grid((unsigned)max_rows);
 #define B200_GATHER(V) \
-    launch_pdl(moe_gather_pack_kernel<V>, dim3(grid), dim3(256), 0, st, b, b_nb1, b_nb2, (int)ne11, (int)K, slot, tok, n_rows, a16, scales)
+    launch_pdl(moe_gather_pack_kernel<V>, dim3(grid), dim3(256), 0, st, b, b_nb1, b_nb2, (int)ne11, (int)K, slot, tok, \
+               n_rows, a16, scales)
     if (per <= 1) B200_GATHER(1);
     else if (per <= 2) B200_GATHER(2);
     else if (per <= 4) B200_GATHER(4);

@@ -363,7 +363,8 @@ int ep_token_tile_public(int64_t pairs, int64_t e_loc) { return ep_token_tile(pa
 
 void ep_route_scan_public(const int32_t* ecnt, int32_t* bsum, int32_t* bad, int nb, int e_loc, int bt, int32_t* off,
                           int32_t* tile_start, int32_t* cursor, int* err, cudaStream_t st) {
-    launch_pdl(ep_route_scan_kernel, dim3(1), dim3(EP_THREADS), 0, st, ecnt, bsum, bad, nb, e_loc, bt, off, tile_start, cursor, err);
+    launch_pdl(ep_route_scan_kernel, dim3(1), dim3(EP_THREADS), 0, st, ecnt, bsum, bad, nb, e_loc, bt, off,
+               tile_start, cursor, err);
 }
 
 }  // namespace b200
@@ -400,10 +401,11 @@ int b200_moe_ep_dispatch(const int32_t* ids, int64_t ids_nb0, int64_t ids_nb1, i
     int32_t* bad = reinterpret_cast<int32_t*>(static_cast<char*>(scratch) +
                                               (((size_t)nb * 2 * n_ranks * 4 + 255) & ~(size_t)255));
     const EpIds I{ids, ids_nb0, ids_nb1, (int)n_used, (int)ne11, (int)(n_expert / n_ranks)};
-    launch_pdl(ep_dispatch_count_kernel, dim3(nb), dim3(EPC), 0, st, I, C, (int)n_expert, (int)n_ranks, bcounts, bad);
+    launch_pdl(ep_dispatch_count_kernel, dim3(nb), dim3(EPC), 0, st, I, C, (int)n_expert, (int)n_ranks, bcounts,
+               bad);
     launch_pdl(ep_dispatch_scan_kernel, dim3(1), dim3(32), 0, st, bcounts, bad, nb, (int)n_ranks, counts, dev_err);
-    launch_pdl(ep_dispatch_write_kernel, dim3(nb), dim3(EPC), 0, st, I, C, (int)n_ranks, bcounts, bad + nb, send_hdr, row_tok, row_slot,
-                                                 row_ret);
+    launch_pdl(ep_dispatch_write_kernel, dim3(nb), dim3(EPC), 0, st, I, C, (int)n_ranks, bcounts, bad + nb, send_hdr,
+               row_tok, row_slot, row_ret);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
     const int rc = launch_gather_pack(b, b_nb1, b_nb2, ne11, K, row_slot, row_tok, counts + 2 * n_ranks,
                                       n_tokens * n_used, static_cast<__half*>(send_a16), send_scale, st);
@@ -455,15 +457,16 @@ int b200_moe_ep_expert(int wtype, const void* local_stack, int64_t K, int64_t N,
             cudaSuccess)
         return B200_E_UNSUPPORTED;
     if (cudaMemsetAsync(ecnt, 0, (size_t)n_local * 4, st) != cudaSuccess) return B200_E_CUDA;
-    launch_pdl(ep_route_count_kernel, dim3(nb), dim3(EPC), hist_smem, st, recv_hdr, (int)n_rows, (int)n_used, (int)expert0,
-                                                      (int)n_local, ecnt, bsum, bad);
-    launch_pdl(ep_route_scan_kernel, dim3(1), dim3(EP_THREADS), 0, st, ecnt, bsum, bad, nb, (int)n_local, bt, off, tiles, cursor, dev_err);
-    launch_pdl(ep_route_place_kernel, dim3(nb), dim3(EPC), 0, st, recv_hdr, (int)n_rows, (int)n_used, (int)expert0, bsum, bad + nb,
-                                              cursor, src, rix, zero);
+    launch_pdl(ep_route_count_kernel, dim3(nb), dim3(EPC), hist_smem, st, recv_hdr, (int)n_rows, (int)n_used,
+               (int)expert0, (int)n_local, ecnt, bsum, bad);
+    launch_pdl(ep_route_scan_kernel, dim3(1), dim3(EP_THREADS), 0, st, ecnt, bsum, bad, nb, (int)n_local, bt, off, tiles,
+               cursor, dev_err);
+    launch_pdl(ep_route_place_kernel, dim3(nb), dim3(EPC), 0, st, recv_hdr, (int)n_rows, (int)n_used, (int)expert0,
+               bsum, bad + nb, cursor, src, rix, zero);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
     const int64_t gcap = (int64_t)device_sm_count() * 8;
-    launch_pdl(ep_gather_rows_kernel, dim3((unsigned)(pmax < gcap ? pmax : gcap)), dim3(256), 0, st, 
-        static_cast<const __half*>(recv_a16), recv_scale, src, off + n_local, (int)K, a16, scales);
+    launch_pdl(ep_gather_rows_kernel, dim3((unsigned)(pmax < gcap ? pmax : gcap)), dim3(256), 0, st,
+               static_cast<const __half*>(recv_a16), recv_scale, src, off + n_local, (int)K, a16, scales);
     if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
     return gemm_grouped_impl(wtype, local_stack, N, K, n_local, a16, scales, pmax, bt, off, tiles, zero, rix, ret, 0,
                              N * 4, dev_err, st);
@@ -481,8 +484,9 @@ int b200_moe_ep_combine(const float* ret, int64_t N, const int32_t* send_hdr, in
         (reinterpret_cast<uintptr_t>(ret) & 15u))
         return B200_E_UNSUPPORTED;
     const int64_t gcap = (int64_t)device_sm_count() * 8;
-    launch_pdl(ep_combine_kernel, dim3((unsigned)(max_rows < gcap ? max_rows : gcap)), dim3(256), 0, static_cast<cudaStream_t>(stream), 
-        ret, (int)N, send_hdr, (int)n_used, row_tok, row_ret, counts + 2 * n_ranks, dst, d_nb1, d_nb2);
+    launch_pdl(ep_combine_kernel, dim3((unsigned)(max_rows < gcap ? max_rows : gcap)), dim3(256), 0,
+               static_cast<cudaStream_t>(stream), ret, (int)N, send_hdr, (int)n_used, row_tok, row_ret,
+               counts + 2 * n_ranks, dst, d_nb1, d_nb2);
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 

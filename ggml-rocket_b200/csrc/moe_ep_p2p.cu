@@ -310,9 +310,10 @@ int b200_moe_ep_p2p_push(const void* send_a16, const float* send_scale, const in
     const int64_t gcap = (int64_t)device_sm_count() * 4;
     const int64_t blocks = (max_rows + 7) / 8 < gcap ? (max_rows + 7) / 8 : gcap;
     if (blocks > 0)
-        launch_pdl(ep_push_kernel, dim3((unsigned)blocks), dim3(P2P_THREADS), 0, st, 
-            static_cast<const __half*>(send_a16), send_scale, send_hdr, row_tok, counts, (int)n_ranks, (int)rank,
-            (int)n_used, (int)K, cap, reinterpret_cast<__half* const*>(peer_recv_a16), peer_recv_meta);
+        launch_pdl(ep_push_kernel, dim3((unsigned)blocks), dim3(P2P_THREADS), 0, st,
+                   static_cast<const __half*>(send_a16), send_scale, send_hdr, row_tok, counts, (int)n_ranks,
+                   (int)rank, (int)n_used, (int)K, cap, reinterpret_cast<__half* const*>(peer_recv_a16),
+                   peer_recv_meta);
     launch_pdl(ep_signal_kernel, dim3(1), dim3(64), 0, st, peer_flags, 0, (int)rank, (int)n_ranks, epoch, counts);
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
@@ -406,8 +407,8 @@ int b200_moe_ep_p2p_expert(int wtype, const void* local_stack, int64_t K, int64_
 int b200_moe_ep_p2p_finish(const int* flags, int64_t n_ranks, int epoch, int* dev_err, void* stream) {
     using namespace b200;
     if (!flags || !dev_err || n_ranks <= 0 || n_ranks > 64) return B200_E_INVALID;
-    launch_pdl(ep_wait_kernel, dim3(1), dim3(64), 0, static_cast<cudaStream_t>(stream), flags, (int)n_ranks, (int)n_ranks, epoch, nullptr,
-                                                                    dev_err);
+    launch_pdl(ep_wait_kernel, dim3(1), dim3(64), 0, static_cast<cudaStream_t>(stream), flags, (int)n_ranks,
+               (int)n_ranks, epoch, nullptr, dev_err);
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 

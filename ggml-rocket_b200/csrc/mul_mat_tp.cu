@@ -89,7 +89,8 @@ int b200_mul_mat_tp_finish(const int* flags, int64_t n_ranks, int epoch, int* de
     using namespace b200;
     if (!flags || !dev_err || n_ranks <= 0) return B200_E_INVALID;
     if (n_ranks > 64) return B200_E_UNSUPPORTED;
-    launch_pdl(tp_wait_kernel, dim3(1), dim3(64), 0, static_cast<cudaStream_t>(stream), flags, (int)n_ranks, epoch, dev_err);
+    launch_pdl(tp_wait_kernel, dim3(1), dim3(64), 0, static_cast<cudaStream_t>(stream), flags, (int)n_ranks, epoch,
+               dev_err);
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 

@@ -38,3 +38,28 @@ def test_library_answers_without_a_gpu():
     assert lib.ggml_backend_b200_op_from_name(b"ADD") == g.OP_OTHER
     assert g.weight_packed_size(g.Q4_K, 4096, 4096) == 4096 * 16 * 144
     assert g.weight_packed_size(g.Q4_K, 4096, 4000) == 0       # K % 256 != 0
+
+
+def test_multi_gpu_and_group_entry_points_reject_bad_arguments_without_a_gpu():
+    """The N-sharded, grouped MUL_MAT_ID and grouped expert-parallel entry points check their
+    arguments before any CUDA call, so malformed calls fail with a status even on a host with
+    no GPU."""
+    lib = g.lib()
+    p = ctypes.c_void_p(16)
+    # b200_mul_mat_tp: null weight, rank out of range, column offset not a multiple of 16
+    assert lib.b200_mul_mat_tp(12, None, 16, 0, 256, p, 256, 4, p, 64, 1, 0, p, 1, p, 0, p, None) == \
+        g.B200_E_INVALID
+    assert lib.b200_mul_mat_tp(12, p, 16, 0, 256, p, 256, 4, p, 64, 2, 2, p, 1, p, 0, p, None) == g.B200_E_INVALID
+    assert lib.b200_mul_mat_tp(12, p, 16, 8, 256, p, 256, 4, p, 64, 1, 0, p, 1, p, 0, p, None) == \
+        g.B200_E_UNSUPPORTED
+    assert lib.b200_mul_mat_tp_finish(None, 1, 1, p, None) == g.B200_E_INVALID
+    assert lib.b200_mul_mat_tp_finish(p, 65, 1, p, None) == g.B200_E_UNSUPPORTED
+    assert lib.b200_mul_mat_tp_workspace_size(12, 0, 16, 256) == 0
+    # b200_mul_mat_id_group: no members, too many members
+    assert lib.b200_mul_mat_id_group(0, 12, p, p, 256, 8, p, 1024, 1024, 1, p, 4, 16, 4, 8, p, p, p, p, 0, p,
+                                     None) == g.B200_E_INVALID
+    assert lib.b200_mul_mat_id_group(17, 12, p, p, 256, 8, p, 1024, 1024, 1, p, 4, 16, 4, 8, p, p, p, p, 0, p,
+                                     None) == g.B200_E_UNSUPPORTED
+    # b200_moe_ep_p2p_expert_group: no members
+    assert lib.b200_moe_ep_p2p_expert_group(0, 12, p, p, 256, 4, 0, p, p, p, 2, 0, 4, 64, 0, p, p, p, p, 1, p, 0, p,
+                                            None) == g.B200_E_INVALID
