@@ -350,10 +350,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     const UnitCoords uc = unit_coords(cur);
                     cur = uc.next;
                     const int sb0 = uc.kb0 >> 2, sb_end = (uc.kb1 + 3) >> 2;
+                    // the L2 prefetch runs PREFETCH super-blocks ahead, on into the next work
+                    // unit's first ones, so a unit (an expert's tile in the grouped mode) does not
+                    // start on cold weights
+                    const bool has_next = cursor_ok(cur);
+                    const UnitCoords un = has_next ? unit_coords(cur) : uc;
+                    const int nsb0 = un.kb0 >> 2, nsb_end = (un.kb1 + 3) >> 2;
                     for (int pf = sb0; pf < sb0 + RC::PREFETCH && pf < sb_end; pf++)
                         tma_prefetch_l2_2d(&tmW, pf * RC::X_ELEMS, uc.wrow0);
                     for (int sb = sb0; sb < sb_end; sb++) {
-                        if (sb + RC::PREFETCH < sb_end) tma_prefetch_l2_2d(&tmW, (sb + RC::PREFETCH) * RC::X_ELEMS, uc.wrow0);
+                        const int ahead = sb + RC::PREFETCH;
+                        if (ahead < sb_end) tma_prefetch_l2_2d(&tmW, ahead * RC::X_ELEMS, uc.wrow0);
+                        else if (has_next && nsb0 + (ahead - sb_end) < nsb_end)
+                            tma_prefetch_l2_2d(&tmW, (nsb0 + (ahead - sb_end)) * RC::X_ELEMS, un.wrow0);
                         if (!mbar_wait(rempty_bar(rs), rph ^ 1u, args.err, ERR_WAIT_PRODUCER, abort_flag)) { ok = false; break; }
                         const uint32_t dst = sbase + C::RAW_OFF + rs * RC::STAGE;
                         mbar_arrive_expect_tx(rfull_bar(rs), RC::A_BYTES + RC::D_BYTES);
