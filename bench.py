@@ -57,10 +57,13 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemm", "moe", "fa"], default="gemm",
-                    help="gemm: the headline MUL_MAT sweep (default); moe: the MUL_MAT_ID layer of "
+    ap.add_argument("--workload", choices=["gemm", "gemv", "moe", "fa"], default="gemm",
+                    help="gemm: the headline MUL_MAT sweep (default); gemv: the sweep's Q4_K weights at decode "
+                         "size (M = --decode-m, b200_mul_mat_vec); moe: the MUL_MAT_ID layer of "
                          "BASELINE configs[3], expert-parallel over the ranks; fa: the FLASH_ATTN_EXT "
                          "prefill of configs[2]")
+    ap.add_argument("--decode-m", type=int, default=1,
+                    help="gemv workload: token rows per step (1..8)")
     ap.add_argument("--shard", action="store_true",
                     help="gemm workload on several GPUs: split every weight's rows across the ranks "
                          "(strong scaling), the output all-gathered by the GEMM epilogue's stores into "
@@ -613,6 +616,82 @@ def run_fa(args):
     return 0
 
 
+def run_gemv(args):
+    """Decode-size MUL_MAT (b200_mul_mat_vec): the three Q4_K weights of the headline sweep against
+    M = --decode-m token rows, L2 flushed before every step. value = Q4_K weight bytes streamed per
+    second (the kernel's roofline is HBM: each weight byte is read once)."""
+    import numpy as np
+    import torch
+    import ggml_b200 as g
+    from ggml_b200 import quants
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    g.lib()
+    M = args.decode_m
+    rng = np.random.default_rng(0xB200)
+    packed, acts, outs, wss = [], [], [], []
+    wbytes = 0
+    for (k, n) in SHAPES:
+        w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02))
+        raw = torch.from_numpy(quants.quantize(WTYPE, w).reshape(-1)).to(dev)
+        p = torch.empty(g.weight_packed_size(WTYPE, n, k), dtype=torch.uint8, device=dev)
+        g.weight_pack(WTYPE, raw, n, k, p)
+        packed.append(p)
+        wbytes += p.numel()
+        acts.append(torch.from_numpy(rng.standard_normal((M, k)).astype(np.float32)).to(dev))
+        outs.append(torch.empty((M, n), dtype=torch.float32, device=dev))
+        wss.append(torch.empty(max(256, g.lib().b200_mul_mat_vec_workspace_size(M, k)), dtype=torch.uint8, device=dev))
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for i, (k, n) in enumerate(SHAPES):
+            g.check(g.mul_mat_vec(WTYPE, packed[i], n, k, acts[i], M, outs[i], wss[i], err, stream=stream),
+                    "mul_mat_vec")
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ts = []
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda._sleep(1000000)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step()
+        e1.record(stream)
+        ts.append((e0, e1))
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    if int(err.item()) != 0:
+        raise SystemExit(f"device error {int(err.item())}")
+    ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in ts)
+    if rank == 0:
+        peaks, src = measured_peaks()
+        gbs = wbytes / (ms / 1e3) / 1e9
+        peak = float(peaks.get("hbm_gbs", 6650.0))
+        line = {"metric": "decode MUL_MAT GB/s of Q4_K weight streamed (b200_mul_mat_vec)", "value": gbs,
+                "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "replicas only", "vs_baseline": None,
+                "dtype": "f32 (Q4_K weights)", "data": "synthetic",
+                "config": {"workload": f"the Q4_K weights of BASELINE configs[1] at M={M} token rows, one op per "
+                                       "shape per step", "weight_bytes_per_step": wbytes,
+                           "tokens_per_s": M / (ms / 1e3),
+                           "l2": "flushed before every timed step (256 MiB memset), outside the timed events",
+                           "median_of_steps": True},
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                             "peak_source": f"{src} hbm_gbs"},
+                "clocks": clocks, "gpu_launches": 2 * len(SHAPES) * args.steps}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_gemm_sharded(args):
     """The headline sweep with every weight's rows split across the ranks (ggml_b200.tp): each
     rank packs its row block of each shape's weight, runs the N-sharded MUL_MAT on the shared
@@ -707,6 +786,8 @@ def main():
         return run_moe(args)
     if args.workload == "fa":
         return run_fa(args)
+    if args.workload == "gemv":
+        return run_gemv(args)
     if args.shard:
         return run_gemm_sharded(args)
     return run_ours(args)

@@ -122,6 +122,13 @@ bool flash_attn_unmasked() {
     static const bool v = knob_int("B200_FLASH_ATTN_UNMASKED", 0) > 0;
     return v;
 }
+// Decode-size MUL_MAT (M <= 8) over Q4_K weights on the GPU (b200_mul_mat_vec). Off by default:
+// the reference leaves M below its offload threshold on the CPU; B200_DECODE=1 claims it.
+bool decode_on() {
+    static const bool v = knob_on("B200_DECODE", false);
+    return v;
+}
+
 bool fuse_on() {
     static const bool v = knob_on("B200_FUSE", true);
     return v;
@@ -499,10 +506,14 @@ extern "C" bool ggml_backend_b200_supports_op(const b200_tensor* op) {
             if (prec_declines(op)) return false;
             const int64_t K = a->ne[0], N = a->ne[1], M = bb->ne[1];
             const bool aq = is_quantized(a->type);
-            return a->op == B200_OP_NONE && weight_type_ok(a->type) && bb->type == T_F32 && op->type == T_F32 &&
-                   is_contiguous(a) && is_contiguous(bb) && is_contiguous(op) && a->ne[0] == bb->ne[0] &&
-                   a->ne[2] == 1 && a->ne[3] == 1 && (!aq || K % blck_size(a->type) == 0) && K % 32 == 0 &&
-                   N % 16 == 0 && K >= 64 && N >= 64 && M >= (aq ? min_m_quant() : min_m());
+            const bool base = a->op == B200_OP_NONE && weight_type_ok(a->type) && bb->type == T_F32 &&
+                              op->type == T_F32 && is_contiguous(a) && is_contiguous(bb) && is_contiguous(op) &&
+                              a->ne[0] == bb->ne[0] && a->ne[2] == 1 && a->ne[3] == 1 &&
+                              (!aq || K % blck_size(a->type) == 0) && K % 32 == 0 && N % 16 == 0 && K >= 64 &&
+                              N >= 64;
+            if (base && M >= (aq ? min_m_quant() : min_m())) return true;
+            // decode (opt-in): Q4_K weights against 1..8 token rows, one 2-D activation
+            return base && decode_on() && a->type == T_Q4_K && M >= 1 && M <= 8 && bb->ne[2] == 1 && bb->ne[3] == 1;
         }
         case B200_OP_MUL_MAT_ID: {
             const int mode = moe_mode();
@@ -655,9 +666,23 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
     float* scales = reinterpret_cast<float*>(ws + a16_bytes);
     void* gws = ws + a16_bytes + sc_bytes;
     const size_t gws_bytes = b->ws_bytes - a16_bytes - sc_bytes;
+    // decode-size M (claimed only under B200_DECODE, Q4_K): the weight-streaming kernel per member,
+    // straight from the f32 activations
+    const bool decode = M < min_m_quant() && M <= 8;
     for (int64_t i3 = 0; i3 < ne13; i3++) {
         for (int64_t i2 = 0; i2 < ne12; i2++) {
             const float* A = reinterpret_cast<const float*>(a_base + i3 * src1->nb[3] + i2 * src1->nb[2]);
+            if (decode) {
+                for (int g = 0; g < ng; g++) {
+                    const b200_tensor* d = nodes[g];
+                    const int64_t N = d->src[0]->ne[1];
+                    float* C = reinterpret_cast<float*>(d_base[g] + i3 * d->nb[3] + i2 * d->nb[2]);
+                    const int rc = b200_mul_mat_vec(kt[g], wdev[g], N, K, A, (int64_t)(src1->nb[1] / 4), M, C,
+                                                    (int64_t)(d->nb[1] / 4), nullptr, 0, b->dev_err, b->stream);
+                    if (rc != B200_OK) return rc;
+                }
+                continue;
+            }
             int rc = b200_act_pack(A, (int64_t)(src1->nb[1] / 4), M, K, a16, scales, b->stream);
             if (rc != B200_OK) return rc;
             for (int g = 0; g < ng; g++) {
@@ -680,7 +705,8 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
             return B200_E_CUDA;
     }
     if (!check_dev_err(b, "MUL_MAT")) return B200_E_DEVICE;
-    if (ng > 1) b->route_ops["fused"]++;
+    if (decode) b->route_ops["decode"] += ng;
+    else if (ng > 1) b->route_ops["fused"]++;
     else b->route_ops[route_name(kt[0])]++;
     return B200_OK;
 }

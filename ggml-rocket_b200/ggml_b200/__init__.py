@@ -187,6 +187,8 @@ _BACKEND_SIGS = {
     "b200_mul_mat_id_workspace_size": (_sz, [_i64] * 5),
     "b200_mul_mat_id": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
                                _vp, _i64, _i64, _vp, _sz, _vp, _vp]),
+    "b200_mul_mat_vec_workspace_size": (_sz, [_i64, _i64]),
+    "b200_mul_mat_vec": (_int, [_int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _sz, _vp, _vp]),
     "b200_mul_mat_id_group": (_int, [_int, _int, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64,
                                      _i64, _i64, _vp, _vp, _vp, _vp, _sz, _vp, _vp]),
     "b200_mul_mat_id_route_view": (_int, [_i64, _i64, _i64, _i64, _c.POINTER(_sz), _c.POINTER(_sz),
@@ -350,6 +352,13 @@ def mul_mat_id(wtype, as_packed, K, N, n_expert, b, b_nb1, b_nb2, ne11, ids, ids
     return lib().b200_mul_mat_id(wtype, _ptr(as_packed), K, N, n_expert, _ptr(b), b_nb1, b_nb2, ne11, _ptr(ids),
                                  ids_nb0, ids_nb1, n_used, n_tokens, _ptr(dst), d_nb1, d_nb2, _ptr(workspace),
                                  workspace.numel() * workspace.element_size(), _ptr(dev_err), _stream(stream))
+
+
+def mul_mat_vec(wtype, w_packed, N, K, a, M, out, workspace, dev_err, lda=None, ldd=None, stream=None):
+    """Decode-size MUL_MAT (M <= 8, Q4_K): out[M, N] = a[M, K] . W^T (b200_mul_mat_vec)."""
+    return lib().b200_mul_mat_vec(wtype, _ptr(w_packed), N, K, _ptr(a), lda if lda else K, M, _ptr(out),
+                                  ldd if ldd else N, _ptr(workspace), workspace.numel() * workspace.element_size(),
+                                  _ptr(dev_err), _stream(stream))
 
 
 def mul_mat_id_group(wtype, stacks, Ns, K, n_expert, b, b_nb1, b_nb2, ne11, ids, ids_nb0, ids_nb1, n_used, n_tokens,

@@ -132,6 +132,18 @@ int    b200_flash_attn_ext(const float * q, int64_t q_nb1, int64_t q_nb2,
                            float scale, float max_bias, float softcap,
                            void * workspace, size_t workspace_bytes, int * dev_err, void * stream);
 
+/* ---- decode-size MUL_MAT (M = 1..8) over Q4_K weights ---------------------------------------
+ * The reference leaves decode (M below its ROCKET_MIN_M) on the CPU (ggml-rocket.cpp:7424-7496);
+ * this is MUL_MAT for those M on the GPU: dst[m, n] = sum_k src1[m, k] * W[n, k] with W the
+ * weight as b200_weight_pack packs it (Q4_K only), src1 f32 [M][lda], dst f32 [M][ldd]. A
+ * weight-streaming kernel on the CUDA cores: the exact ggml decode in the factored per-sub-block
+ * form d*sc*sum(q*a) - dmin*m*sum(a), fp32 sums (no activation pack, no fp16 rounding), fixed
+ * summation order. No scratch is needed (the workspace arguments are accepted and unused). */
+size_t b200_mul_mat_vec_workspace_size(int64_t M, int64_t K);
+int    b200_mul_mat_vec(int wtype, const void * w_packed, int64_t N, int64_t K, const float * src1, int64_t lda,
+                        int64_t M, float * dst, int64_t ldd, void * workspace, size_t workspace_bytes,
+                        int * dev_err, void * stream);
+
 /* ---- MUL_MAT_ID ----------------------------------------------------------------------------
  * Replaces ggml_backend_rocket_mul_mat_id (ggml-rocket.cpp:6692-6944): the counting sort of
  * (slot, token) rows by expert (:6706-6732), the per-expert gather (:6790-6800), the expert

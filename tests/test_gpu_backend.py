@@ -181,3 +181,53 @@ def test_backend_groups_mul_mat_ids_sharing_inputs(cuda):
         assert rel_err(out, want) <= 1e-2
     assert be.route_ops("moe") == 2 and be.route_ops("moe_grouped") == 2
     be.close()
+
+
+_DECODE_CHILD = r"""
+import sys
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/ggml-rocket_b200"); sys.path.insert(0, sys.argv[1] + "/tests")
+import numpy as np
+import ggml_b200 as g
+import oracle
+from conftest import rel_err
+from ggml_b200 import quants
+be = g.Backend()
+rng = np.random.default_rng(7)
+K = 4096
+worst, n = 0.0, 0
+for M, Ns in ((1, (4096,)), (4, (4096, 1024, 1024)), (8, (14336, 14336))):
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    x = g.make_tensor(g.F32, [K, M], a, name="x")
+    keep, nodes = [], []
+    for i, N in enumerate(Ns):
+        raw = quants.quantize(g.Q4_K, (rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+        w = g.make_tensor(g.Q4_K, [K, N], raw, name=f"blk.{M}.w{i}")
+        out = np.full((M, N), np.nan, np.float32)
+        d = g.make_tensor(g.F32, [N, M], out, op=g.OP_MUL_MAT, srcs=[w, x])
+        assert g.supports_op(d)
+        keep.append((raw, w, out, d, N))
+        nodes.append(d)
+    assert be.graph_compute(nodes) == g.STATUS_SUCCESS
+    for raw, w, out, d, N in keep:
+        worst = max(worst, rel_err(out, oracle.mul_mat(g.Q4_K, raw, N, K, a)))
+    n += len(Ns)
+assert be.route_ops("decode") == n, be.route_ops("decode")
+assert be.cpu_fallbacks() == 0 and be.device_errors() == 0
+be.close()
+print("DECODE_WORST", worst)
+"""
+
+
+def test_backend_decode_route(cuda):
+    """B200_DECODE=1 (read once per process, so in a child): Q4_K MUL_MATs with M = 1..8 --
+    one op, and shared-src1 groups -- run on the weight-streaming kernel through graph_compute,
+    matching the oracle to fp32-sum accuracy."""
+    import os
+    import subprocess
+    import sys
+    from conftest import ROOT
+    env = dict(os.environ, B200_DECODE="1")
+    p = subprocess.run([sys.executable, "-c", _DECODE_CHILD, ROOT], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
+    assert float(p.stdout.split("DECODE_WORST")[1].split()[0]) <= 1e-5

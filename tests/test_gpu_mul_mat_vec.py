@@ -1,0 +1,71 @@
+"""Decode-size MUL_MAT (b200_mul_mat_vec, M = 1..8, Q4_K) on the GPU against the CPU oracle.
+
+The kernel takes the exact ggml decode in the factored per-sub-block form with f32 activations
+and fp32 sums, so it must match the fp64 oracle far inside the MUL_MAT tolerance (the fp32 sums
+of K products: a relative error of a few 1e-6); shapes include N not a multiple of the 8-row
+block, K of one super-block, strided src1 / dst rows and unaligned activations (the scalar
+load path)."""
+import numpy as np
+import pytest
+
+import oracle
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(torch, w_raw, N, K, a, lda=None, ldd=None, offset=0):
+    import ggml_b200 as g
+    M = a.shape[0]
+    lda = lda or K
+    ldd = ldd or N
+    raw = torch.from_numpy(np.ascontiguousarray(w_raw).reshape(-1)).cuda()
+    packed = torch.empty(g.weight_packed_size(g.Q4_K, N, K), dtype=torch.uint8, device="cuda")
+    g.weight_pack(g.Q4_K, raw, N, K, packed)
+    abuf = torch.zeros(offset + M * lda, dtype=torch.float32, device="cuda")
+    av = abuf[offset:offset + M * lda].view(M, lda)
+    av[:, :K] = torch.from_numpy(a)
+    out = torch.full((M * ldd,), float("nan"), dtype=torch.float32, device="cuda")
+    ws = torch.empty(max(256, g.lib().b200_mul_mat_vec_workspace_size(M, K)), dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc = g.mul_mat_vec(g.Q4_K, packed, N, K, av, M, out, ws, err, lda=lda, ldd=ldd)
+    torch.cuda.synchronize()
+    assert rc == 0 and int(err.item()) == 0
+    return out.view(M, ldd)[:, :N].cpu().numpy()
+
+
+@pytest.mark.parametrize("N,K,M", [(4096, 4096, 1), (14336, 4096, 2), (4096, 14336, 3), (1000, 512, 4),
+                                   (200, 256, 7), (4104, 4096, 8), (64, 2048, 5)])
+def test_mul_mat_vec_matches_oracle(cuda, N, K, M):
+    import torch
+    rng = np.random.default_rng(N + K + M)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    raw = oracle.quantize(12, w)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    got = _run(torch, raw, N, K, a)
+    want = oracle.mul_mat(12, raw, N, K, a)
+    assert np.all(np.isfinite(got))
+    assert rel_err(got, want) <= 1e-5, rel_err(got, want)
+
+
+def test_mul_mat_vec_strided_and_unaligned(cuda):
+    import torch
+    rng = np.random.default_rng(3)
+    N, K, M = 520, 1024, 3
+    raw = oracle.quantize(12, (rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    want = oracle.mul_mat(12, raw, N, K, a)
+    # padded rows on both sides, then activations that start 4 bytes past a 16-byte boundary
+    assert rel_err(_run(torch, raw, N, K, a, lda=K + 8, ldd=N + 24), want) <= 1e-5
+    assert rel_err(_run(torch, raw, N, K, a, lda=K + 1, offset=1), want) <= 1e-5
+
+
+def test_mul_mat_vec_declines_what_it_does_not_tile(cuda):
+    import torch
+    import ggml_b200 as g
+    x = torch.zeros(1 << 16, dtype=torch.uint8, device="cuda")
+    f = torch.zeros(1 << 14, dtype=torch.float32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert g.mul_mat_vec(g.F16, x, 64, 256, f, 1, f, x, err) == g.B200_E_UNSUPPORTED      # not Q4_K
+    assert g.mul_mat_vec(g.Q4_K, x, 64, 256, f, 9, f, x, err) == g.B200_E_UNSUPPORTED     # M > 8
+    assert g.mul_mat_vec(g.Q4_K, x, 64, 200, f, 1, f, x, err) == g.B200_E_UNSUPPORTED     # K % 256

@@ -130,6 +130,8 @@ sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/ggml-rocket_
 import test_placement as t
 print(json.dumps({"q4k_m256": t.supported(256, 128, 256, 12), "q4k_m512": t.supported(256, 128, 512, 12),
                   "f16_m16": t.supported(256, 128, 16, 1), "f16_m3": t.supported(256, 128, 3, 1),
+                  "q4k_m1": t.supported(256, 128, 1, 12), "q4k_m8": t.supported(256, 128, 8, 12),
+                  "q4k_m9": t.supported(256, 128, 9, 12), "q8_m1": t.supported(256, 128, 1, 8),
                   "moe": t.moe(2048, 8, 128), "fa_unmasked": t.fa(64, 256, 8, 1024, 2, masked=False),
                   "fa": t.fa(64, 256, 8, 1024, 2)}))
 """
@@ -167,6 +169,10 @@ def test_knobs_in_children():
     assert not r["fa"]
     r = child({"B200_FLASH_ATTN_MIN_KV": "2048"})
     assert not r["fa"]
+    r = child({})                                  # decode-size MUL_MAT stays on the host by default
+    assert not r["q4k_m1"] and not r["q4k_m8"]
+    r = child({"B200_DECODE": "1"})                # Q4_K at M = 1..8 only
+    assert r["q4k_m1"] and r["q4k_m8"] and not r["q4k_m9"] and not r["q8_m1"]
 
 
 def test_moe_ledger_budget_in_child():
