@@ -679,7 +679,7 @@ def run_gemv(args):
         line = {"metric": "decode MUL_MAT GB/s of Q4_K weight streamed (b200_mul_mat_vec)", "value": gbs,
                 "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
                 "higher_is_better": True, "scaling": "replicas only", "vs_baseline": None,
-                "dtype": "f32 (Q4_K weights)", "data": "synthetic",
+                "dtype": "f16 activations x Q4_K weights, fp32 accumulate", "data": "synthetic",
                 "config": {"workload": f"the Q4_K weights of BASELINE configs[1] at M={M} token rows, one op per "
                                        "shape per step", "weight_bytes_per_step": wbytes,
                            "tokens_per_s": M / (ms / 1e3),

@@ -642,6 +642,9 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
         if (!d->on_device) need_out += (nbytes(d) + 255) & ~(size_t)255;
         need_ws = std::max(need_ws, b200_gemm_packed_workspace_size(kernel_wtype(d->src[0]->type), M, d->src[0]->ne[1], K));
     }
+    // decode-size M (claimed only under B200_DECODE, Q4_K): the weight-streaming kernel per member
+    const bool decode = M < min_m_quant() && M <= 8;
+    if (decode) need_ws = std::max(need_ws, b200_mul_mat_vec_workspace_size(M, K));
     const size_t a16_bytes = ((size_t)M * K * 2 + 255) & ~(size_t)255;
     const size_t sc_bytes = ((size_t)M * 4 + 255) & ~(size_t)255;
     need_ws = ((need_ws + 255) & ~(size_t)255) + a16_bytes + sc_bytes;
@@ -666,9 +669,6 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
     float* scales = reinterpret_cast<float*>(ws + a16_bytes);
     void* gws = ws + a16_bytes + sc_bytes;
     const size_t gws_bytes = b->ws_bytes - a16_bytes - sc_bytes;
-    // decode-size M (claimed only under B200_DECODE, Q4_K): the weight-streaming kernel per member,
-    // straight from the f32 activations
-    const bool decode = M < min_m_quant() && M <= 8;
     for (int64_t i3 = 0; i3 < ne13; i3++) {
         for (int64_t i2 = 0; i2 < ne12; i2++) {
             const float* A = reinterpret_cast<const float*>(a_base + i3 * src1->nb[3] + i2 * src1->nb[2]);
@@ -678,7 +678,7 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
                     const int64_t N = d->src[0]->ne[1];
                     float* C = reinterpret_cast<float*>(d_base[g] + i3 * d->nb[3] + i2 * d->nb[2]);
                     const int rc = b200_mul_mat_vec(kt[g], wdev[g], N, K, A, (int64_t)(src1->nb[1] / 4), M, C,
-                                                    (int64_t)(d->nb[1] / 4), nullptr, 0, b->dev_err, b->stream);
+                                                    (int64_t)(d->nb[1] / 4), gws, gws_bytes, b->dev_err, b->stream);
                     if (rc != B200_OK) return rc;
                 }
                 continue;

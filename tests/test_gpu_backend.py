@@ -221,7 +221,7 @@ print("DECODE_WORST", worst)
 def test_backend_decode_route(cuda):
     """B200_DECODE=1 (read once per process, so in a child): Q4_K MUL_MATs with M = 1..8 --
     one op, and shared-src1 groups -- run on the weight-streaming kernel through graph_compute,
-    matching the oracle to fp32-sum accuracy."""
+    within the decode kernel's bound against the oracle (fp16 activations, exact weights)."""
     import os
     import subprocess
     import sys
@@ -230,4 +230,4 @@ def test_backend_decode_route(cuda):
     p = subprocess.run([sys.executable, "-c", _DECODE_CHILD, ROOT], env=env, capture_output=True, text=True,
                        timeout=300)
     assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
-    assert float(p.stdout.split("DECODE_WORST")[1].split()[0]) <= 1e-5
+    assert float(p.stdout.split("DECODE_WORST")[1].split()[0]) <= 2e-3   # the decode kernel's bound

@@ -1,10 +1,11 @@
 """Decode-size MUL_MAT (b200_mul_mat_vec, M = 1..8, Q4_K) on the GPU against the CPU oracle.
 
-The kernel takes the exact ggml decode in the factored per-sub-block form with f32 activations
-and fp32 sums, so it must match the fp64 oracle far inside the MUL_MAT tolerance (the fp32 sums
-of K products: a relative error of a few 1e-6); shapes include N not a multiple of the 8-row
-block, K of one super-block, strided src1 / dst rows and unaligned activations (the scalar
-load path)."""
+The weights enter the MMA as exact integers q*sc with fp32 scales, the activations as fp16 of
+a / s per 256-value block (s the block's absmax), products are exact and summed in fp32; so the
+only error beyond fp32 sums is the activations' fp16 rounding (~2^-12 relative), and the bound
+here, DECODE_TOL = 2e-3 max relative error, is five times tighter than the prefill MUL_MAT's
+1e-2. Shapes include N not a multiple of the 16-row block, K of one super-block, strided src1 /
+dst rows and unaligned activations (the scalar load path); repeated calls are bit-identical."""
 import numpy as np
 import pytest
 
@@ -12,6 +13,8 @@ import oracle
 from conftest import rel_err
 
 pytestmark = pytest.mark.gpu
+
+DECODE_TOL = 2e-3
 
 
 def _run(torch, w_raw, N, K, a, lda=None, ldd=None, offset=0):
@@ -45,7 +48,7 @@ def test_mul_mat_vec_matches_oracle(cuda, N, K, M):
     got = _run(torch, raw, N, K, a)
     want = oracle.mul_mat(12, raw, N, K, a)
     assert np.all(np.isfinite(got))
-    assert rel_err(got, want) <= 1e-5, rel_err(got, want)
+    assert rel_err(got, want) <= DECODE_TOL, rel_err(got, want)
 
 
 def test_mul_mat_vec_strided_and_unaligned(cuda):
@@ -56,8 +59,10 @@ def test_mul_mat_vec_strided_and_unaligned(cuda):
     a = rng.standard_normal((M, K)).astype(np.float32)
     want = oracle.mul_mat(12, raw, N, K, a)
     # padded rows on both sides, then activations that start 4 bytes past a 16-byte boundary
-    assert rel_err(_run(torch, raw, N, K, a, lda=K + 8, ldd=N + 24), want) <= 1e-5
-    assert rel_err(_run(torch, raw, N, K, a, lda=K + 1, offset=1), want) <= 1e-5
+    first = _run(torch, raw, N, K, a, lda=K + 8, ldd=N + 24)
+    assert rel_err(first, want) <= DECODE_TOL
+    assert np.array_equal(first, _run(torch, raw, N, K, a, lda=K + 8, ldd=N + 24))   # deterministic
+    assert rel_err(_run(torch, raw, N, K, a, lda=K + 1, offset=1), want) <= DECODE_TOL
 
 
 def test_mul_mat_vec_declines_what_it_does_not_tile(cuda):
@@ -69,3 +74,5 @@ def test_mul_mat_vec_declines_what_it_does_not_tile(cuda):
     assert g.mul_mat_vec(g.F16, x, 64, 256, f, 1, f, x, err) == g.B200_E_UNSUPPORTED      # not Q4_K
     assert g.mul_mat_vec(g.Q4_K, x, 64, 256, f, 9, f, x, err) == g.B200_E_UNSUPPORTED     # M > 8
     assert g.mul_mat_vec(g.Q4_K, x, 64, 200, f, 1, f, x, err) == g.B200_E_UNSUPPORTED     # K % 256
+    small = x[:g.lib().b200_mul_mat_vec_workspace_size(1, 256) - 1]
+    assert g.mul_mat_vec(g.Q4_K, x, 64, 256, f, 1, f, small, err) == g.B200_E_INVALID      # workspace too small
