@@ -641,7 +641,7 @@ def run_gemv(args):
         wbytes += p.numel()
         acts.append(torch.from_numpy(rng.standard_normal((M, k)).astype(np.float32)).to(dev))
         outs.append(torch.empty((M, n), dtype=torch.float32, device=dev))
-        wss.append(torch.empty(max(256, g.lib().b200_mul_mat_vec_workspace_size(M, k)), dtype=torch.uint8, device=dev))
+        wss.append(torch.empty(max(256, g.lib().b200_mul_mat_vec_workspace_size(M, n, k)), dtype=torch.uint8, device=dev))
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)

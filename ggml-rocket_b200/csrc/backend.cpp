@@ -644,7 +644,9 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
     }
     // decode-size M (claimed only under B200_DECODE, Q4_K): the weight-streaming kernel per member
     const bool decode = M < min_m_quant() && M <= 8;
-    if (decode) need_ws = std::max(need_ws, b200_mul_mat_vec_workspace_size(M, K));
+    if (decode)
+        for (int g = 0; g < ng; g++)
+            need_ws = std::max(need_ws, b200_mul_mat_vec_workspace_size(M, nodes[g]->src[0]->ne[1], K));
     const size_t a16_bytes = ((size_t)M * K * 2 + 255) & ~(size_t)255;
     const size_t sc_bytes = ((size_t)M * 4 + 255) & ~(size_t)255;
     need_ws = ((need_ws + 255) & ~(size_t)255) + a16_bytes + sc_bytes;

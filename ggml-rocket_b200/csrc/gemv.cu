@@ -24,7 +24,10 @@
 // fp32 scales); products with the fp16 activations are exact in the MMA and summed in fp32. The
 // only rounding beyond fp32 sums is the activations' fp16 rounding, as in the prefill GEMM.
 // The decode is ggml's dequantize_row_q4_K (ggml-rocket.cpp:3894-3907 calls it through to_float).
+#include <algorithm>
 #include <cstdint>
+#include <cstdlib>
+#include <cstring>
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -36,13 +39,15 @@
 
 namespace b200 {
 
-constexpr int GV_WARPS = 8;                      // warps per CTA, splitting the super-blocks
+constexpr int GV_WARPS = 8;                      // warps per CTA
 constexpr int GV_ROWS = 16;                      // weight rows per CTA (the MMA's M)
-constexpr int GV_STAGES = 4;                     // super-block columns in flight per warp
-constexpr int GV_STAGE = GV_ROWS * 144;          // one super-block of 16 rows, bytes
-constexpr int GV_PIECES = GV_STAGE / 16;         // 16-byte copies per stage (144)
-constexpr int GV_SMEM = GV_WARPS * GV_STAGES * GV_STAGE + GV_WARPS * GV_ROWS * 8 * 4;
+constexpr int GV_STAGES = 4;                     // TMA stages (units) in flight per warp
+constexpr int GV_STAGE = GV_ROWS * 144;          // one unit: a super-block column of 16 rows, bytes
+constexpr int GV_PIECES = GV_STAGE / 16;         // 16-byte cp.async copies per stage (rows schedule)
+constexpr int GV_SMEM = GV_WARPS * GV_STAGES * GV_STAGE;                              // stream schedule
+constexpr int GV_SMEM_ROWS = GV_WARPS * GV_STAGES * GV_STAGE + GV_WARPS * GV_ROWS * 8 * 4;   // + reduction
 constexpr int GV_MMAX = 8;                       // token rows per call (the MMA's N)
+constexpr bool GV_DEFAULT_STREAM = false;        // default schedule: rows
 
 // ---- small PTX helpers ---------------------------------------------------------------------
 
@@ -99,12 +104,17 @@ __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_
 //                                    k slots
 //   asum2[m * K/32 + 8 sb + j]       fp16 pair (hi, lo), hi + lo = the fp32 sum of sub-block j's
 //                                    32 fp16 values to ~22 bits
+// and zeroes the n_cnt arrival counters of the weight-streaming kernel that follows.
 template <bool VEC>
 __global__ void __launch_bounds__(256) gemv_act_kernel(const float* __restrict__ a, int64_t lda, int M, int K,
                                                        __half* __restrict__ a16p, uint32_t* __restrict__ asum2,
-                                                       float* __restrict__ scl) {
+                                                       float* __restrict__ scl, uint32_t* __restrict__ cnt,
+                                                       int64_t n_cnt) {
     grid_dep_wait();   // the previous kernel may still read this workspace (programmatic launch)
     grid_dep_launch();
+    // the weight-streaming kernel's arrival counters start at zero
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_cnt; i += (int64_t)gridDim.x * blockDim.x)
+        cnt[i] = 0u;
     const int nsb = K / 256;
     const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= M * nsb) return;
@@ -180,12 +190,15 @@ __device__ __forceinline__ GvRowScales gv_row_scales(const uint4 h, bool upper, 
     return r;
 }
 
-// CTA = 16 weight rows n0 .. n0+15; warp w takes super-block columns [w nsb / 8, (w+1) nsb / 8).
+
+// The "rows" schedule: CTA = 16 weight rows n0 .. n0+15, one CTA per row block (several waves);
+// warp w takes super-block columns [w nsb / 8, (w+1) nsb / 8), streamed through a 4-deep cp.async
+// ring of its own, and the warps' partials are added in warp order in shared memory.
 // Lane (g, t) = (lane / 4, lane % 4) is the MMA's thread group g, thread t: it decodes qs chunk t
 // (bytes 32t .. 32t+31) of rows n0+g and n0+g+8 and feeds token row g's activations; its
 // accumulators are rows n0+g, n0+g+8 x token rows 2t, 2t+1.
 __global__ void __launch_bounds__(32 * GV_WARPS, 2)
-    gemv_q4k_kernel(const uint8_t* __restrict__ w, int64_t N, int K, const __half* __restrict__ a16p,
+    gemv_q4k_rows_kernel(const uint8_t* __restrict__ w, int64_t N, int K, const __half* __restrict__ a16p,
                     const uint32_t* __restrict__ asum2, const float* __restrict__ scl, int M, float* __restrict__ dst,
                     int64_t ldd) {
     extern __shared__ __align__(128) uint8_t gv_smem[];
@@ -244,16 +257,16 @@ __global__ void __launch_bounds__(32 * GV_WARPS, 2)
             const uint4* ap = reinterpret_cast<const uint4*>(arow + (int64_t)sb * 256);
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                const uint4 l = __ldg(ap + j), h = __ldg(ap + 4 + j);
+                const uint4 l = __ldca(ap + j), h = __ldca(ap + 4 + j);
                 awl[4 * j] = l.x, awl[4 * j + 1] = l.y, awl[4 * j + 2] = l.z, awl[4 * j + 3] = l.w;
                 awh[4 * j] = h.x, awh[4 * j + 1] = h.y, awh[4 * j + 2] = h.z, awh[4 * j + 3] = h.w;
             }
-            as2 = __ldg(reinterpret_cast<const uint2*>(srow + (int64_t)sb * 8));
+            as2 = __ldca(reinterpret_cast<const uint2*>(srow + (int64_t)sb * 8));
         } else {
 #pragma unroll
             for (int j = 0; j < 16; j++) awl[j] = awh[j] = 0u;
         }
-        const float2 s2 = __ldg(reinterpret_cast<const float2*>(scl + (int64_t)sb * GV_MMAX + 2 * t));
+        const float2 s2 = __ldca(reinterpret_cast<const float2*>(scl + (int64_t)sb * GV_MMAX + 2 * t));
         cp_async_wait<GV_STAGES - 1>();   // this lane's copies of the stage have landed
         __syncwarp();                     // ... and every lane's
         const uint8_t* r0 = ring + (it % GV_STAGES) * GV_STAGE + g * 144;
@@ -307,26 +320,236 @@ __global__ void __launch_bounds__(32 * GV_WARPS, 2)
     }
 }
 
-struct GvWorkspace {
-    size_t a16_off, asum_off, scl_off, total;
+
+// The "stream" schedule.
+// Work split. A unit is one super-block column (256 weights) of one 16-row block: 16 x 144 bytes,
+// one TMA box. The n_rb * nsb units, row block major, are cut into equal contiguous ranges, one
+// per warp of a one-wave persistent grid, so every SM streams the same number of bytes. A row
+// block covered by one warp is stored directly; one shared by several warps (at most at the two
+// ends of each range) is finished by the last of them to arrive: each writes its 16 x 8 partial,
+// fences and counts in; the last adds all partials in warp order (so the result does not depend
+// on timing) and stores. Nothing waits on another warp.
+struct GvSplit {
+    int64_t units, warps;
+    __device__ __forceinline__ int64_t start(int64_t w) const { return w * units / warps; }
+    __device__ __forceinline__ int64_t owner(int64_t u) const { return ((u + 1) * warps - 1) / units; }
 };
-static GvWorkspace gv_workspace(int64_t M, int64_t K) {
+
+// Lane (g, t) = (lane / 4, lane % 4) is the MMA's thread group g, thread t: it decodes qs chunk t
+// (bytes 32t .. 32t+31) of the block's rows g and g+8 and feeds token row g's activations; its
+// accumulators are rows g, g+8 x token rows 2t, 2t+1.
+__global__ void __launch_bounds__(32 * GV_WARPS, 2)
+    gemv_q4k_kernel(const __grid_constant__ CUtensorMap tmW, int64_t N, int K, const __half* __restrict__ a16p,
+                    const uint32_t* __restrict__ asum2, const float* __restrict__ scl, int M, float* __restrict__ dst,
+                    int64_t ldd, uint32_t* __restrict__ cnt, float* __restrict__ part, int* __restrict__ err) {
+    extern __shared__ __align__(128) uint8_t gv_smem[];
+    __shared__ __align__(8) uint64_t bars[GV_WARPS][GV_STAGES];     // stage landed (TMA bytes)
+    __shared__ __align__(8) uint64_t empty[GV_WARPS][GV_STAGES];    // stage read by all 32 lanes
+    __shared__ int abort_flag;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int nsb = K / 256;
+    const int64_t n_rb = (N + GV_ROWS - 1) / GV_ROWS;
+    // never more working warps than units, so that every working warp's range is non-empty
+    const GvSplit split{n_rb * nsb, std::min<int64_t>((int64_t)gridDim.x * GV_WARPS, n_rb * nsb)};
+    const int64_t wid = (int64_t)blockIdx.x * GV_WARPS + warp;
+    const int64_t u0 = wid < split.warps ? split.start(wid) : 0, u1 = wid < split.warps ? split.start(wid + 1) : 0;
+    const uint32_t ring_s = smem_u32(gv_smem + warp * (GV_STAGES * GV_STAGE));
+    const uint32_t bar0 = smem_u32(&bars[warp][0]), ebar0 = smem_u32(&empty[warp][0]);
+    if (threadIdx.x == 0) abort_flag = 0;
+    if (lane == 0) {
+        for (int s = 0; s < GV_STAGES; s++) {
+            mbar_init(bar0 + 8 * s, 1);
+            mbar_init(ebar0 + 8 * s, 32);
+        }
+        fence_barrier_init();
+        tma_prefetch_desc(&tmW);
+    }
+    __syncthreads();
+    // the weights do not depend on the previous kernel: start streaming them before waiting on it
+    auto issue = [&](int64_t u, int slot) {
+        mbar_arrive_expect_tx(bar0 + 8 * slot, GV_STAGE);
+        tma_load_2d(ring_s + slot * GV_STAGE, &tmW, bar0 + 8 * slot, (int32_t)(u % nsb) * 72,
+                    (int32_t)(u / nsb) * GV_ROWS);
+    };
+    if (lane == 0)
+        for (int s = 0; s < GV_STAGES && u0 + s < u1; s++) issue(u0 + s, s);
+    grid_dep_wait();   // programmatic launch: the activation prep has finished
+    grid_dep_launch();
+
+    const bool upper = t >= 2;
+    const uint32_t j0 = (2u * t) & 3u;
+    const uint32_t sel0 = 0x4040u | (j0 * 0x101u), sel1 = 0x4040u | ((j0 + 1u) * 0x101u);
+    const bool has = g < M;   // token rows past M feed zeros
+    const __half* arow = a16p + (int64_t)(has ? g : 0) * K + 64 * t;
+    const uint32_t* srow = asum2 + (int64_t)(has ? g : 0) * (K / 32) + 2 * t;
+    const uint32_t H1024 = 0x64006400u;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int64_t rb = u0 / nsb, seg0 = u0;
+    int sb = (int)(u0 % nsb);
+    for (int64_t u = u0; u < u1; ++u) {
+        const int i = (int)(u - u0), slot = i % GV_STAGES;
+        uint32_t awl[16], awh[16];
+        uint2 as2 = make_uint2(0u, 0u);
+        // the prep kernel wrote these while this grid was already resident (programmatic launch):
+        // coherent L1-cached loads (ld.global.ca) after the grid dependency wait, never the
+        // non-coherent path
+        if (has) {
+            const uint4* ap = reinterpret_cast<const uint4*>(arow + (int64_t)sb * 256);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const uint4 l = __ldca(ap + j), h = __ldca(ap + 4 + j);
+                awl[4 * j] = l.x, awl[4 * j + 1] = l.y, awl[4 * j + 2] = l.z, awl[4 * j + 3] = l.w;
+                awh[4 * j] = h.x, awh[4 * j + 1] = h.y, awh[4 * j + 2] = h.z, awh[4 * j + 3] = h.w;
+            }
+            as2 = __ldca(reinterpret_cast<const uint2*>(srow + (int64_t)sb * 8));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) awl[j] = awh[j] = 0u;
+        }
+        const float2 s2 = __ldca(reinterpret_cast<const float2*>(scl + (int64_t)sb * GV_MMAX + 2 * t));
+        if (!mbar_wait(bar0 + 8 * slot, (uint32_t)(i / GV_STAGES) & 1u, err, ERR_WAIT_STREAM, &abort_flag)) {
+            // let the copies this warp issued land before the CTA's shared memory is released
+            if (lane == 0)
+                for (int64_t v = u; v < u1 && v < u0 + i + GV_STAGES; ++v) {
+                    const int vi = (int)(v - u0);
+                    if (!mbar_drain(bar0 + 8 * (vi % GV_STAGES), (uint32_t)(vi / GV_STAGES) & 1u))
+                        atomicCAS(err, 0, ERR_WAIT_DRAIN);
+                }
+            return;
+        }
+        const uint8_t* r0 = gv_smem + warp * (GV_STAGES * GV_STAGE) + slot * GV_STAGE + g * 144;
+        const uint8_t* r1 = r0 + 8 * 144;
+        const GvRowScales f0 = gv_row_scales(lds128(r0), upper, sel0, sel1);
+        const GvRowScales f1 = gv_row_scales(lds128(r1), upper, sel0, sel1);
+        const uint4 q0a = lds128(r0 + 16 + 32 * t), q0b = lds128(r0 + 32 + 32 * t);
+        const uint4 q1a = lds128(r1 + 16 + 32 * t), q1b = lds128(r1 + 32 + 32 * t);
+        // release the slot; the refill's TMA (async proxy) write is issued only once all 32 lanes'
+        // reads of it are known complete through the slot's empty barrier
+        mbar_arrive(ebar0 + 8 * slot);
+        if (lane == 0 && u + GV_STAGES < u1) {
+            if (mbar_wait(ebar0 + 8 * slot, (uint32_t)(i / GV_STAGES) & 1u, err, ERR_WAIT_STREAM, &abort_flag))
+                issue(u + GV_STAGES, slot);
+        }
+        __syncwarp();
+        const uint32_t w0[8] = {q0a.x, q0a.y, q0a.z, q0a.w, q0b.x, q0b.y, q0b.z, q0b.w};
+        const uint32_t w1[8] = {q1a.x, q1a.y, q1a.z, q1a.w, q1b.x, q1b.y, q1b.z, q1b.w};
+        float clo[4] = {0.0f, 0.0f, 0.0f, 0.0f}, chi[4] = {0.0f, 0.0f, 0.0f, 0.0f}, cm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            // word k = qs bytes 4k..4k+3 of the chunk: low nibbles are weights 4k..4k+3 of sub-block
+            // 2t, high nibbles the same of 2t+1; a0/a1 take bytes (0, 2), a2/a3 bytes (1, 3)
+            const uint32_t x0 = w0[k], x1 = w1[k], y0 = x0 >> 8, y1 = x1 >> 8;
+            mma16816(clo, hfma2(lop_and_or(x0, 0x000F000Fu, H1024), f0.mul_lo, f0.add_lo),
+                     hfma2(lop_and_or(x1, 0x000F000Fu, H1024), f1.mul_lo, f1.add_lo),
+                     hfma2(lop_and_or(y0, 0x000F000Fu, H1024), f0.mul_lo, f0.add_lo),
+                     hfma2(lop_and_or(y1, 0x000F000Fu, H1024), f1.mul_lo, f1.add_lo), awl[2 * k], awl[2 * k + 1]);
+            mma16816(chi, hfma2(lop_and_or(x0, 0x00F000F0u, H1024), f0.mul_hi, f0.add_hi),
+                     hfma2(lop_and_or(x1, 0x00F000F0u, H1024), f1.mul_hi, f1.add_hi),
+                     hfma2(lop_and_or(y0, 0x00F000F0u, H1024), f0.mul_hi, f0.add_hi),
+                     hfma2(lop_and_or(y1, 0x00F000F0u, H1024), f1.mul_hi, f1.add_hi), awh[2 * k], awh[2 * k + 1]);
+        }
+        // sum_j m_j * (sum of sub-block j's activations), the sums as (hi, lo) fp16 pairs
+        mma16816(cm, f0.m_lo, f1.m_lo, f0.m_hi, f1.m_hi, as2.x, as2.y);
+        acc[0] = fmaf(s2.x, fmaf(f0.d, clo[0] + chi[0], -f0.dmin * cm[0]), acc[0]);   // row g,   token 2t
+        acc[1] = fmaf(s2.y, fmaf(f0.d, clo[1] + chi[1], -f0.dmin * cm[1]), acc[1]);   // row g,   token 2t+1
+        acc[2] = fmaf(s2.x, fmaf(f1.d, clo[2] + chi[2], -f1.dmin * cm[2]), acc[2]);   // row g+8, token 2t
+        acc[3] = fmaf(s2.y, fmaf(f1.d, clo[3] + chi[3], -f1.dmin * cm[3]), acc[3]);   // row g+8, token 2t+1
+        if (sb == nsb - 1 || u + 1 == u1) {
+            // the end of this warp's part of row block rb
+            const int64_t n0 = rb * GV_ROWS;
+            float v[4] = {acc[0], acc[1], acc[2], acc[3]};
+            bool store = seg0 == rb * nsb && u + 1 == (rb + 1) * nsb;   // the whole row block is ours
+            if (!store) {
+                const int slot_out = seg0 == u0 ? 0 : 1;                  // first or last block of the range
+                *reinterpret_cast<float4*>(part + (wid * 2 + slot_out) * 128 + 4 * lane) =
+                    make_float4(acc[0], acc[1], acc[2], acc[3]);
+                __threadfence();
+                __syncwarp();
+                const int64_t w_lo = split.owner(rb * nsb), w_hi = split.owner((rb + 1) * nsb - 1);
+                uint32_t old = 0;
+                if (lane == 0) old = atomicAdd(cnt + rb, 1u);
+                old = __shfl_sync(0xffffffffu, old, 0);
+                if (old == (uint32_t)(w_hi - w_lo)) {
+                    __threadfence();
+                    v[0] = v[1] = v[2] = v[3] = 0.0f;
+                    for (int64_t q = w_lo; q <= w_hi; ++q) {
+                        const int sq = (q == w_lo && split.start(q) / nsb != rb) ? 1 : 0;
+                        const float4 p = __ldcg(reinterpret_cast<const float4*>(part + (q * 2 + sq) * 128 + 4 * lane));
+                        v[0] += p.x, v[1] += p.y, v[2] += p.z, v[3] += p.w;
+                    }
+                    store = true;
+                }
+            }
+            if (store) {
+                const int64_t ra = n0 + g, rc = n0 + g + 8;
+                const int ta = 2 * t, tb = 2 * t + 1;
+                if (ra < N && ta < M) dst[(int64_t)ta * ldd + ra] = v[0];
+                if (ra < N && tb < M) dst[(int64_t)tb * ldd + ra] = v[1];
+                if (rc < N && ta < M) dst[(int64_t)ta * ldd + rc] = v[2];
+                if (rc < N && tb < M) dst[(int64_t)tb * ldd + rc] = v[3];
+            }
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
+            seg0 = u + 1;
+        }
+        if (++sb == nsb) sb = 0, ++rb;
+    }
+}
+
+struct GvWorkspace {
+    size_t a16_off, asum_off, scl_off, cnt_off, part_off, total;
+};
+// warps = the weight-streaming grid's warp count (its partial slots)
+static GvWorkspace gv_workspace(int64_t M, int64_t N, int64_t K, int64_t warps) {
     auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
     GvWorkspace l{};
     l.a16_off = 0;
     l.asum_off = al((size_t)M * K * 2);
     l.scl_off = l.asum_off + al((size_t)M * (K / 32) * 4);
-    l.total = l.scl_off + al((size_t)(K / 256) * GV_MMAX * 4);
+    l.cnt_off = l.scl_off + al((size_t)(K / 256) * GV_MMAX * 4);
+    l.part_off = l.cnt_off + al((size_t)((N + GV_ROWS - 1) / GV_ROWS) * 4);
+    l.total = l.part_off + al((size_t)warps * 2 * 128 * 4);
     return l;
+}
+
+static int gv_sm_count() {
+    static int sms[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (sms[dev] == 0) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        sms[dev] = v;
+    }
+    return sms[dev];
+}
+
+// Which schedule runs: B200_GEMV_SCHEDULE = rows | stream (read once per process).
+static bool gv_stream_schedule() {
+    static const bool v = [] {
+        const char* e = getenv("B200_GEMV_SCHEDULE");
+        if (e && strcmp(e, "stream") == 0) return true;
+        if (e && strcmp(e, "rows") == 0) return false;
+        return GV_DEFAULT_STREAM;
+    }();
+    return v;
+}
+
+// CTAs of the one-wave grid (two per SM), never more warps than units.
+static int64_t gv_grid(int64_t N, int64_t K) {
+    const int64_t units = ((N + GV_ROWS - 1) / GV_ROWS) * (K / 256);
+    return std::max<int64_t>(1, std::min<int64_t>(2 * gv_sm_count(), units / GV_WARPS));
 }
 
 }  // namespace b200
 
 extern "C" {
 
-size_t b200_mul_mat_vec_workspace_size(int64_t M, int64_t K) {
-    if (M <= 0 || K <= 0) return 0;
-    return b200::gv_workspace(M, K).total;
+size_t b200_mul_mat_vec_workspace_size(int64_t M, int64_t N, int64_t K) {
+    using namespace b200;
+    if (M <= 0 || N <= 0 || K <= 0 || K % 256 != 0) return 0;
+    return gv_workspace(M, N, K, gv_grid(N, K) * GV_WARPS).total;
 }
 
 int b200_mul_mat_vec(int wtype, const void* w_packed, int64_t N, int64_t K, const float* src1, int64_t lda, int64_t M,
@@ -334,36 +557,54 @@ int b200_mul_mat_vec(int wtype, const void* w_packed, int64_t N, int64_t K, cons
     using namespace b200;
     if (!w_packed || !src1 || !dst || !dev_err || N <= 0 || K <= 0 || M <= 0 || lda < K || ldd < N)
         return B200_E_INVALID;
-    if (wtype != WT_Q4_K || K % 256 != 0 || M > GV_MMAX || N > (1ll << 30) || K > (1 << 28))
+    if (wtype != WT_Q4_K || K % 256 != 0 || M > GV_MMAX || N > (1ll << 30) || K > (1 << 28) ||
+        (reinterpret_cast<uintptr_t>(w_packed) & 15u) != 0)
         return B200_E_UNSUPPORTED;
-    const GvWorkspace l = gv_workspace(M, K);
+    const int64_t grid = gv_grid(N, K);
+    const GvWorkspace l = gv_workspace(M, N, K, grid * GV_WARPS);
     if (!workspace || workspace_bytes < l.total || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
         return B200_E_INVALID;
-    (void)dev_err;   // nothing in these kernels waits or can fail on the device
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(gemv_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_SMEM) != cudaSuccess)
+        if (cudaFuncSetAttribute(gemv_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_SMEM) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(gemv_q4k_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_SMEM_ROWS) !=
+                cudaSuccess)
             return B200_E_CUDA;
         attr_set[dev] = true;
     }
+    // the packed Q4_K weight as a 2-D uint16 tensor [N rows, 72 * nsb]: one unit is a 72 x 16 box
+    const int64_t row_bytes = (K / 256) * 144;
+    CUtensorMap tmW;
+    if (!make_tmap_2d_u16(&tmW, w_packed, (uint64_t)N, (uint64_t)(row_bytes / 2), (uint64_t)row_bytes, GV_ROWS, 72))
+        return B200_E_CUDA;
     char* ws = static_cast<char*>(workspace);
     __half* a16p = reinterpret_cast<__half*>(ws + l.a16_off);
     uint32_t* asum2 = reinterpret_cast<uint32_t*>(ws + l.asum_off);
     float* scl = reinterpret_cast<float*>(ws + l.scl_off);
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(ws + l.cnt_off);
+    float* part = reinterpret_cast<float*>(ws + l.part_off);
+    const int64_t n_rb = (N + GV_ROWS - 1) / GV_ROWS;
     const bool vec = (reinterpret_cast<uintptr_t>(src1) & 15u) == 0 && lda % 4 == 0;
     const int warps = (int)(M * (K / 256));
-    const dim3 pgrid((unsigned)((warps + 7) / 8)), pblock(256);
+    const dim3 pgrid((unsigned)std::max(1, (warps + 7) / 8)), pblock(256);
     cudaError_t e = vec ? launch_pdl(gemv_act_kernel<true>, pgrid, pblock, 0, st, src1, lda, (int)M, (int)K, a16p,
-                                     asum2, scl)
+                                     asum2, scl, cnt, n_rb)
                         : launch_pdl(gemv_act_kernel<false>, pgrid, pblock, 0, st, src1, lda, (int)M, (int)K, a16p,
-                                     asum2, scl);
+                                     asum2, scl, cnt, n_rb);
     if (e != cudaSuccess) return B200_E_CUDA;
-    e = launch_pdl(gemv_q4k_kernel, dim3((unsigned)((N + GV_ROWS - 1) / GV_ROWS)), dim3(32 * GV_WARPS), GV_SMEM, st,
-                   static_cast<const uint8_t*>(w_packed), N, (int)K, (const __half*)a16p, (const uint32_t*)asum2,
-                   (const float*)scl, (int)M, dst, ldd);
+    if (!gv_stream_schedule()) {
+        e = launch_pdl(gemv_q4k_rows_kernel, dim3((unsigned)n_rb), dim3(32 * GV_WARPS), GV_SMEM_ROWS, st,
+                       static_cast<const uint8_t*>(w_packed), N, (int)K, (const __half*)a16p, (const uint32_t*)asum2,
+                       (const float*)scl, (int)M, dst, ldd);
+        return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
+    }
+    e = launch_pdl(gemv_q4k_kernel, dim3((unsigned)grid), dim3(32 * GV_WARPS), GV_SMEM, st, tmW, N, (int)K,
+                   (const __half*)a16p, (const uint32_t*)asum2, (const float*)scl, (int)M, dst, ldd, cnt, part,
+                   dev_err);
     return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 

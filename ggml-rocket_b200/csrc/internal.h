@@ -31,6 +31,10 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 int device_sm_count();
 bool make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
                       uint32_t box_rows, uint32_t box_cols);
+// A 2-D uint16 tensor map [rows, cols] (cols innermost, row pitch in bytes), box [box_rows,
+// box_cols], no swizzle; rows past the end read as zero.
+bool make_tmap_2d_u16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_bytes,
+                      uint32_t box_rows, uint32_t box_cols);
 size_t packed_weight_bytes(int type, int64_t N, int64_t K, size_t* plane_d_off);
 bool weight_type_supported(int type, int64_t K);
 // dst_bases / n_dst / col0: the output columns [col0, col0 + N) of every one of n_dst [M][ldd]

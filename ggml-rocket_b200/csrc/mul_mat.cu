@@ -218,7 +218,7 @@ bool make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_
 
 // A 2-D uint16 tensor map [rows, cols] (cols innermost, row pitch in bytes), box [box_rows,
 // box_cols], no swizzle: the raw quantized tiles and the transposed d plane.
-static bool make_tmap_2d_u16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_bytes,
+bool make_tmap_2d_u16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_bytes,
                              uint32_t box_rows, uint32_t box_cols) {
     EncodeTiledFn fn = get_encode_fn();
     if (!fn) return false;

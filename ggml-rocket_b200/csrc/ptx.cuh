@@ -27,6 +27,7 @@ enum : int {
     ERR_WAIT_DRAIN = 5,      // the drain after an abort gave up
     ERR_BAD_INDEX = 6,       // a bounds check failed
     ERR_WAIT_PEER = 7,       // a stream-K finisher gave up waiting for another CTA's partial tile
+    ERR_WAIT_STREAM = 8,     // a weight-streaming warp gave up waiting for one of its TMA stages
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

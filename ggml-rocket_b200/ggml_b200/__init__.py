@@ -187,7 +187,7 @@ _BACKEND_SIGS = {
     "b200_mul_mat_id_workspace_size": (_sz, [_i64] * 5),
     "b200_mul_mat_id": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64,
                                _vp, _i64, _i64, _vp, _sz, _vp, _vp]),
-    "b200_mul_mat_vec_workspace_size": (_sz, [_i64, _i64]),
+    "b200_mul_mat_vec_workspace_size": (_sz, [_i64, _i64, _i64]),
     "b200_mul_mat_vec": (_int, [_int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _sz, _vp, _vp]),
     "b200_mul_mat_id_group": (_int, [_int, _int, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64,
                                      _i64, _i64, _vp, _vp, _vp, _vp, _sz, _vp, _vp]),

@@ -135,11 +135,16 @@ int    b200_flash_attn_ext(const float * q, int64_t q_nb1, int64_t q_nb2,
 /* ---- decode-size MUL_MAT (M = 1..8) over Q4_K weights ---------------------------------------
  * The reference leaves decode (M below its ROCKET_MIN_M) on the CPU (ggml-rocket.cpp:7424-7496);
  * this is MUL_MAT for those M on the GPU: dst[m, n] = sum_k src1[m, k] * W[n, k] with W the
- * weight as b200_weight_pack packs it (Q4_K only), src1 f32 [M][lda], dst f32 [M][ldd]. A
- * weight-streaming kernel on the CUDA cores: the exact ggml decode in the factored per-sub-block
- * form d*sc*sum(q*a) - dmin*m*sum(a), fp32 sums (no activation pack, no fp16 rounding), fixed
- * summation order. No scratch is needed (the workspace arguments are accepted and unused). */
-size_t b200_mul_mat_vec_workspace_size(int64_t M, int64_t K);
+ * weight as b200_weight_pack packs it (Q4_K only, 16-byte aligned), src1 f32 [M][lda], dst f32
+ * [M][ldd]. Two launches: an activation prep (fp16 of src1 / s per 256-value block, s the block's
+ * absmax, with the fp16 (hi, lo) sums of every 32-value sub-block) and a weight-streaming kernel
+ * that decodes the weights into warp-level tensor-core MMA fragments as exact integers q*sc and
+ * accumulates in fp32, each super-block scaled by d, dmin and s in fp32. The weight is split
+ * into equal contiguous parts, one per warp of a one-wave grid; row blocks shared by two warps are
+ * added by the last to finish, in a fixed order (results do not depend on timing). The workspace
+ * (b200_mul_mat_vec_workspace_size bytes, 256-byte aligned) holds the prepared activations, the
+ * partial sums and their counters; calls sharing one must not overlap on the GPU. */
+size_t b200_mul_mat_vec_workspace_size(int64_t M, int64_t N, int64_t K);
 int    b200_mul_mat_vec(int wtype, const void * w_packed, int64_t N, int64_t K, const float * src1, int64_t lda,
                         int64_t M, float * dst, int64_t ldd, void * workspace, size_t workspace_bytes,
                         int * dev_err, void * stream);

@@ -209,7 +209,9 @@ for M, Ns in ((1, (4096,)), (4, (4096, 1024, 1024)), (8, (14336, 14336))):
         nodes.append(d)
     assert be.graph_compute(nodes) == g.STATUS_SUCCESS
     for raw, w, out, d, N in keep:
-        worst = max(worst, rel_err(out, oracle.mul_mat(g.Q4_K, raw, N, K, a)))
+        e = rel_err(out, oracle.mul_mat(g.Q4_K, raw, N, K, a))
+        print("CASE", M, N, e)
+        worst = max(worst, e)
     n += len(Ns)
 assert be.route_ops("decode") == n, be.route_ops("decode")
 assert be.cpu_fallbacks() == 0 and be.device_errors() == 0
@@ -230,4 +232,4 @@ def test_backend_decode_route(cuda):
     p = subprocess.run([sys.executable, "-c", _DECODE_CHILD, ROOT], env=env, capture_output=True, text=True,
                        timeout=300)
     assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
-    assert float(p.stdout.split("DECODE_WORST")[1].split()[0]) <= 2e-3   # the decode kernel's bound
+    assert float(p.stdout.split("DECODE_WORST")[1].split()[0]) <= 2e-3, p.stdout   # the decode kernel's bound

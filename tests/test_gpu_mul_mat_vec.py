@@ -29,7 +29,7 @@ def _run(torch, w_raw, N, K, a, lda=None, ldd=None, offset=0):
     av = abuf[offset:offset + M * lda].view(M, lda)
     av[:, :K] = torch.from_numpy(a)
     out = torch.full((M * ldd,), float("nan"), dtype=torch.float32, device="cuda")
-    ws = torch.empty(max(256, g.lib().b200_mul_mat_vec_workspace_size(M, K)), dtype=torch.uint8, device="cuda")
+    ws = torch.empty(max(256, g.lib().b200_mul_mat_vec_workspace_size(M, N, K)), dtype=torch.uint8, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     rc = g.mul_mat_vec(g.Q4_K, packed, N, K, av, M, out, ws, err, lda=lda, ldd=ldd)
     torch.cuda.synchronize()
@@ -74,5 +74,50 @@ def test_mul_mat_vec_declines_what_it_does_not_tile(cuda):
     assert g.mul_mat_vec(g.F16, x, 64, 256, f, 1, f, x, err) == g.B200_E_UNSUPPORTED      # not Q4_K
     assert g.mul_mat_vec(g.Q4_K, x, 64, 256, f, 9, f, x, err) == g.B200_E_UNSUPPORTED     # M > 8
     assert g.mul_mat_vec(g.Q4_K, x, 64, 200, f, 1, f, x, err) == g.B200_E_UNSUPPORTED     # K % 256
-    small = x[:g.lib().b200_mul_mat_vec_workspace_size(1, 256) - 1]
+    small = x[:g.lib().b200_mul_mat_vec_workspace_size(1, 64, 256) - 1]
     assert g.mul_mat_vec(g.Q4_K, x, 64, 256, f, 1, f, small, err) == g.B200_E_INVALID      # workspace too small
+
+
+def test_mul_mat_vec_back_to_back_shared_workspace(cuda):
+    """Calls queued back to back on one stream, sharing one workspace, with different M, N and
+    activations (the backend's pattern: each call's prep rewrites the workspace the previous
+    call's kernel read), synchronised only at the end."""
+    import torch
+    import ggml_b200 as g
+    rng = np.random.default_rng(11)
+    K = 4096
+    cases = [(4096, 1), (1024, 4), (14336, 8), (1024, 4), (4096, 1), (2048, 2)]
+    need = max(g.lib().b200_mul_mat_vec_workspace_size(M, N, K) for N, M in cases)
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    runs = []
+    for N, M in cases:
+        raw = oracle.quantize(12, (rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+        a = rng.standard_normal((M, K)).astype(np.float32)
+        rawd = torch.from_numpy(np.ascontiguousarray(raw).reshape(-1)).cuda()
+        packed = torch.empty(g.weight_packed_size(g.Q4_K, N, K), dtype=torch.uint8, device="cuda")
+        g.weight_pack(g.Q4_K, rawd, N, K, packed)
+        runs.append((raw, a, packed, torch.from_numpy(a).cuda(), torch.full((M, N), float("nan"), device="cuda"), N, M))
+    torch.cuda.synchronize()
+    for raw, a, packed, ad, out, N, M in runs:
+        assert g.mul_mat_vec(g.Q4_K, packed, N, K, ad, M, out, ws, err) == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    for raw, a, packed, ad, out, N, M in runs:
+        e = rel_err(out.cpu().numpy(), oracle.mul_mat(12, raw, N, K, a))
+        assert e <= DECODE_TOL, (N, M, e)
+
+
+def test_mul_mat_vec_stream_schedule(cuda):
+    """The other work schedule (B200_GEMV_SCHEDULE, read once per process, so in a child): the
+    same parity cases and the back-to-back shared-workspace case under it."""
+    import os
+    import subprocess
+    import sys
+    from conftest import ROOT
+    other = "rows" if os.environ.get("B200_GEMV_SCHEDULE") == "stream" else "stream"
+    env = dict(os.environ, B200_GEMV_SCHEDULE=other)
+    p = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider", __file__,
+                        "-k", "matches_oracle or back_to_back or strided"], cwd=ROOT, env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-2000:]
