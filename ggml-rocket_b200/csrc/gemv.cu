@@ -12,9 +12,12 @@
 //   * the sub-block minimum term dmin * sum_j m_j * sum(a over sub-block j) is one more MMA per
 //     super-block, with the activation sums split into fp16 (hi, lo) pairs;
 //   * per super-block: acc += s * (d * C - dmin * Cmin) in fp32, s the activation block scale;
-//   * a CTA owns 16 weight rows; its 8 warps split the super-blocks into contiguous ranges, each
-//     streaming its 16 x 144-byte super-block columns through a 4-deep cp.async ring in shared
-//     memory, and add their partials in warp order (the result does not depend on timing).
+//   * two work schedules (B200_GEMV_SCHEDULE): "rows" (default), one CTA per 16 weight rows whose
+//     8 warps split the super-blocks into contiguous ranges, each streaming its 16 x 144-byte
+//     super-block columns through a 4-deep cp.async ring, partials added in warp order; and
+//     "stream", a one-wave grid whose warps each take an equal contiguous range of the whole
+//     weight through a 4-stage TMA ring, row blocks shared by two warps finished by the last to
+//     arrive. Both add partials in a fixed order: results do not depend on timing.
 // The activations are prepared once per call by gemv_act_kernel: per 256-value block, the
 // block's absmax s and fp16(a / s) (the same per-row "sandwich" rule the GEMM's activation pack
 // applies, here per block), stored in the MMA's k-slot order, plus the fp16 (hi, lo) sums of
