@@ -17,8 +17,10 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <list>
 #include <map>
+#include <set>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -276,6 +278,10 @@ std::string weight_key(const b200_tensor* t) {
     if (t->data && !t->on_device) {
         snprintf(buf, sizeof buf, "@%016llx", (unsigned long long)fingerprint(t, t->data));
         key += buf;
+    } else if (t->data) {
+        // device bytes: keyed by where they live; writes through the buffer API drop the entry
+        snprintf(buf, sizeof buf, "@d%llx", (unsigned long long)(uintptr_t)t->data);
+        key += buf;
     }
     return key;
 }
@@ -325,6 +331,7 @@ struct CachedWeight {
     size_t bytes = 0;
     int ktype = 0;            // the type the kernels read
     std::list<std::string>::iterator lru;
+    uintptr_t src_lo = 0, src_hi = 0;   // device bytes it was packed from (on-device weights)
 };
 
 struct b200_backend {
@@ -353,6 +360,21 @@ struct b200_backend {
     std::map<std::string, bool> moe_seen;
     Breaker brk_fused;
     std::mutex mu;            // graph_compute is serial per instance
+    std::set<b200_buffer*> buffers;   // live device buffers allocated through this instance
+};
+
+struct b200_buffer {
+    uint32_t magic = 0xB200BF00u;
+    b200_backend* owner = nullptr;    // nullptr once the backend is freed
+    int device = 0;
+    void* base = nullptr;
+    size_t size = 0;
+};
+
+struct b200_event {
+    uint32_t magic = 0xB200EE00u;
+    int device = 0;
+    cudaEvent_t ev = nullptr;
 };
 
 namespace {
@@ -399,6 +421,22 @@ void evict_until(b200_backend* b, size_t need) {
             cudaFree(it->second.dev);
             b->cache_bytes -= it->second.bytes;
             b->cache.erase(it);
+        }
+    }
+}
+
+// Drop the cached packed weights whose device source bytes overlap [lo, hi).
+void invalidate_range(b200_backend* b, uintptr_t lo, uintptr_t hi) {
+    for (auto it = b->cache.begin(); it != b->cache.end();) {
+        const CachedWeight& cw = it->second;
+        if (cw.src_hi > lo && cw.src_lo < hi) {
+            cudaStreamSynchronize(b->stream);
+            cudaFree(cw.dev);
+            b->cache_bytes -= cw.bytes;
+            b->lru.erase(cw.lru);
+            it = b->cache.erase(it);
+        } else {
+            ++it;
         }
     }
 }
@@ -459,6 +497,10 @@ void* pack_weight(b200_backend* b, const std::string& key, int type, const void*
         cw.bytes = packed;
         cw.ktype = kt;
         cw.lru = b->lru.begin();
+        if (src_on_device) {
+            cw.src_lo = reinterpret_cast<uintptr_t>(src);
+            cw.src_hi = cw.src_lo + native;
+        }
         b->cache[key] = cw;
         b->cache_bytes += packed;
     }
@@ -920,6 +962,7 @@ b200_backend_t ggml_backend_b200_init(void) {
 
 void ggml_backend_b200_free(b200_backend_t b) {
     if (!b) return;
+    for (b200_buffer* buf : b->buffers) buf->owner = nullptr;   // they stay valid device memory
     if (b->dev_ready) {
         cudaSetDevice(b->device);
         cudaStreamSynchronize(b->stream);
@@ -1094,6 +1137,230 @@ int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes,
     for (void* p : b->transient) cudaFree(p);
     b->transient.clear();
     return status;
+}
+
+
+// ---- device buffers, async transfers and events -------------------------------------------------
+
+static bool buf_ok(const b200_buffer* buf) { return buf && buf->magic == 0xB200BF00u && buf->base; }
+static bool range_ok(const b200_buffer* buf, size_t offset, size_t size) {
+    return offset <= buf->size && size <= buf->size - offset;
+}
+// The stream a buffer's synchronous calls are ordered on: its backend's (0 once that is freed).
+static cudaStream_t buf_stream(const b200_buffer* buf) {
+    return buf->owner && buf->owner->dev_ready ? buf->owner->stream : nullptr;
+}
+static void buf_invalidate(b200_buffer* buf, size_t offset, size_t size) {
+    if (!buf->owner) return;
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(buf->base) + offset;
+    invalidate_range(buf->owner, lo, lo + size);
+}
+
+const char* ggml_backend_b200_buffer_type_name(void) { return "B200"; }
+size_t ggml_backend_b200_buffer_type_alignment(void) { return 256; }
+size_t ggml_backend_b200_buffer_type_max_size(int device) {
+    size_t fr = 0, total = 0;
+    if (ggml_backend_b200_device_memory(device, &fr, &total) != 0) return 0;
+    return total;
+}
+size_t ggml_backend_b200_buffer_type_alloc_size(const b200_tensor* t) { return t ? nbytes(t) : 0; }
+bool ggml_backend_b200_buffer_type_is_host(void) { return false; }
+
+b200_buffer_t ggml_backend_b200_buffer_alloc(b200_backend_t b, size_t size) {
+    if (!ggml_backend_is_b200(b) || size == 0) return nullptr;
+    std::lock_guard<std::mutex> lk(b->mu);
+    if (!ensure_device(b)) return nullptr;
+    void* p = nullptr;
+    if (!cuda_ok(cudaMalloc(&p, size), "cudaMalloc(buffer)")) return nullptr;
+    auto* buf = new b200_buffer();
+    buf->owner = b;
+    buf->device = b->device;
+    buf->base = p;
+    buf->size = size;
+    b->buffers.insert(buf);
+    return buf;
+}
+
+void ggml_backend_b200_buffer_free(b200_buffer_t buf) {
+    if (!buf_ok(buf)) return;
+    cudaSetDevice(buf->device);
+    if (buf->owner) {
+        std::lock_guard<std::mutex> lk(buf->owner->mu);
+        buf_invalidate(buf, 0, buf->size);
+        if (buf->owner->dev_ready) cudaStreamSynchronize(buf->owner->stream);
+        buf->owner->buffers.erase(buf);
+    }
+    cudaFree(buf->base);
+    buf->magic = 0;
+    buf->base = nullptr;
+    delete buf;
+}
+
+void* ggml_backend_b200_buffer_base(b200_buffer_t buf) { return buf_ok(buf) ? buf->base : nullptr; }
+size_t ggml_backend_b200_buffer_size(b200_buffer_t buf) { return buf_ok(buf) ? buf->size : 0; }
+
+// One synchronous transfer into / out of / within buffers, ordered after the owner's queued work.
+static int buf_sync_op(b200_buffer* lock_buf, b200_buffer* inval_buf, size_t inval_off, size_t inval_size,
+                       const std::function<cudaError_t(cudaStream_t)>& op) {
+    cudaSetDevice(lock_buf->device);
+    std::unique_lock<std::mutex> lk;
+    if (lock_buf->owner) lk = std::unique_lock<std::mutex>(lock_buf->owner->mu);
+    if (inval_buf) buf_invalidate(inval_buf, inval_off, inval_size);
+    const cudaStream_t st = buf_stream(lock_buf);
+    if (op(st) != cudaSuccess) return B200_STATUS_FAILED;
+    return cudaStreamSynchronize(st) == cudaSuccess ? B200_STATUS_SUCCESS : B200_STATUS_FAILED;
+}
+
+int ggml_backend_b200_buffer_set(b200_buffer_t buf, size_t offset, const void* src, size_t size) {
+    if (!buf_ok(buf) || !range_ok(buf, offset, size) || (!src && size)) return B200_STATUS_FAILED;
+    if (size == 0) return B200_STATUS_SUCCESS;
+    return buf_sync_op(buf, buf, offset, size, [&](cudaStream_t st) {
+        return cudaMemcpyAsync(static_cast<char*>(buf->base) + offset, src, size, cudaMemcpyHostToDevice, st);
+    });
+}
+
+int ggml_backend_b200_buffer_get(b200_buffer_t buf, size_t offset, void* dst, size_t size) {
+    if (!buf_ok(buf) || !range_ok(buf, offset, size) || (!dst && size)) return B200_STATUS_FAILED;
+    if (size == 0) return B200_STATUS_SUCCESS;
+    return buf_sync_op(buf, nullptr, 0, 0, [&](cudaStream_t st) {
+        return cudaMemcpyAsync(dst, static_cast<const char*>(buf->base) + offset, size, cudaMemcpyDeviceToHost, st);
+    });
+}
+
+int ggml_backend_b200_buffer_memset(b200_buffer_t buf, size_t offset, uint8_t value, size_t size) {
+    if (!buf_ok(buf) || !range_ok(buf, offset, size)) return B200_STATUS_FAILED;
+    if (size == 0) return B200_STATUS_SUCCESS;
+    return buf_sync_op(buf, buf, offset, size, [&](cudaStream_t st) {
+        return cudaMemsetAsync(static_cast<char*>(buf->base) + offset, value, size, st);
+    });
+}
+
+int ggml_backend_b200_buffer_clear(b200_buffer_t buf, uint8_t value) {
+    if (!buf_ok(buf)) return B200_STATUS_FAILED;
+    return ggml_backend_b200_buffer_memset(buf, 0, value, buf->size);
+}
+
+int ggml_backend_b200_buffer_copy(b200_buffer_t src, size_t src_offset, b200_buffer_t dst, size_t dst_offset,
+                                  size_t size) {
+    if (!buf_ok(src) || !buf_ok(dst) || !range_ok(src, src_offset, size) || !range_ok(dst, dst_offset, size))
+        return B200_STATUS_FAILED;
+    if (src->owner != dst->owner && src->owner && dst->owner) return B200_STATUS_FAILED;   // one backend's buffers
+    if (size == 0) return B200_STATUS_SUCCESS;
+    return buf_sync_op(dst, dst, dst_offset, size, [&](cudaStream_t st) {
+        return cudaMemcpyAsync(static_cast<char*>(dst->base) + dst_offset,
+                               static_cast<const char*>(src->base) + src_offset, size, cudaMemcpyDeviceToDevice, st);
+    });
+}
+
+void* ggml_backend_b200_host_alloc(size_t size) {
+    if (size == 0) return nullptr;
+    void* p = nullptr;
+    return cudaMallocHost(&p, size) == cudaSuccess ? p : nullptr;
+}
+void ggml_backend_b200_host_free(void* ptr) {
+    if (ptr) cudaFreeHost(ptr);
+}
+
+// The backend's own buffer, on its device, with the device state ready; locks its mutex.
+static bool async_prologue(b200_backend_t b, const b200_buffer* buf, std::unique_lock<std::mutex>* lk) {
+    if (!ggml_backend_is_b200(b)) return false;
+    if (buf && (!buf_ok(buf) || buf->owner != b)) return false;
+    *lk = std::unique_lock<std::mutex>(b->mu);
+    if (!ensure_device(b)) return false;
+    return cudaSetDevice(b->device) == cudaSuccess;
+}
+
+int ggml_backend_b200_set_async(b200_backend_t b, b200_buffer_t buf, size_t offset, const void* src, size_t size) {
+    std::unique_lock<std::mutex> lk;
+    if (!async_prologue(b, buf, &lk) || !buf || !range_ok(buf, offset, size) || (!src && size))
+        return B200_STATUS_FAILED;
+    if (size == 0) return B200_STATUS_SUCCESS;
+    buf_invalidate(buf, offset, size);
+    return cudaMemcpyAsync(static_cast<char*>(buf->base) + offset, src, size, cudaMemcpyHostToDevice, b->stream) ==
+                   cudaSuccess
+               ? B200_STATUS_SUCCESS
+               : B200_STATUS_FAILED;
+}
+
+int ggml_backend_b200_get_async(b200_backend_t b, b200_buffer_t buf, size_t offset, void* dst, size_t size) {
+    std::unique_lock<std::mutex> lk;
+    if (!async_prologue(b, buf, &lk) || !buf || !range_ok(buf, offset, size) || (!dst && size))
+        return B200_STATUS_FAILED;
+    if (size == 0) return B200_STATUS_SUCCESS;
+    return cudaMemcpyAsync(dst, static_cast<const char*>(buf->base) + offset, size, cudaMemcpyDeviceToHost,
+                           b->stream) == cudaSuccess
+               ? B200_STATUS_SUCCESS
+               : B200_STATUS_FAILED;
+}
+
+int ggml_backend_b200_copy_async(b200_backend_t b, b200_buffer_t src, size_t src_offset, b200_buffer_t dst,
+                                 size_t dst_offset, size_t size) {
+    std::unique_lock<std::mutex> lk;
+    if (!buf_ok(src) || src->owner != b || !async_prologue(b, dst, &lk) || !dst ||
+        !range_ok(src, src_offset, size) || !range_ok(dst, dst_offset, size))
+        return B200_STATUS_FAILED;
+    if (size == 0) return B200_STATUS_SUCCESS;
+    buf_invalidate(dst, dst_offset, size);
+    return cudaMemcpyAsync(static_cast<char*>(dst->base) + dst_offset,
+                           static_cast<const char*>(src->base) + src_offset, size, cudaMemcpyDeviceToDevice,
+                           b->stream) == cudaSuccess
+               ? B200_STATUS_SUCCESS
+               : B200_STATUS_FAILED;
+}
+
+int ggml_backend_b200_synchronize(b200_backend_t b) {
+    std::unique_lock<std::mutex> lk;
+    if (!async_prologue(b, nullptr, &lk)) return B200_STATUS_FAILED;
+    return cudaStreamSynchronize(b->stream) == cudaSuccess ? B200_STATUS_SUCCESS : B200_STATUS_FAILED;
+}
+
+b200_event_t ggml_backend_b200_event_new(b200_backend_t b) {
+    std::unique_lock<std::mutex> lk;
+    if (!async_prologue(b, nullptr, &lk)) return nullptr;
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+    auto* ev = new b200_event();
+    ev->device = b->device;
+    ev->ev = e;
+    return ev;
+}
+
+static bool ev_ok(const b200_event* ev) { return ev && ev->magic == 0xB200EE00u && ev->ev; }
+
+void ggml_backend_b200_event_free(b200_event_t ev) {
+    if (!ev_ok(ev)) return;
+    cudaSetDevice(ev->device);
+    cudaEventSynchronize(ev->ev);
+    cudaEventDestroy(ev->ev);
+    ev->magic = 0;
+    delete ev;
+}
+
+int ggml_backend_b200_event_record(b200_backend_t b, b200_event_t ev) {
+    std::unique_lock<std::mutex> lk;
+    if (!ev_ok(ev) || !async_prologue(b, nullptr, &lk) || ev->device != b->device) return B200_STATUS_FAILED;
+    return cudaEventRecord(ev->ev, b->stream) == cudaSuccess ? B200_STATUS_SUCCESS : B200_STATUS_FAILED;
+}
+
+int ggml_backend_b200_event_wait(b200_backend_t b, b200_event_t ev) {
+    std::unique_lock<std::mutex> lk;
+    if (!ev_ok(ev) || !async_prologue(b, nullptr, &lk)) return B200_STATUS_FAILED;
+    return cudaStreamWaitEvent(b->stream, ev->ev, 0) == cudaSuccess ? B200_STATUS_SUCCESS : B200_STATUS_FAILED;
+}
+
+int ggml_backend_b200_event_synchronize(b200_event_t ev) {
+    if (!ev_ok(ev)) return B200_STATUS_FAILED;
+    cudaSetDevice(ev->device);
+    return cudaEventSynchronize(ev->ev) == cudaSuccess ? B200_STATUS_SUCCESS : B200_STATUS_FAILED;
+}
+
+void ggml_backend_b200_device_caps(int device, bool* async, bool* host_buffer, bool* buffer_from_host_ptr,
+                                   bool* events) {
+    const bool present = device >= 0 && device < ggml_backend_b200_reg_device_count();
+    if (async) *async = present;
+    if (host_buffer) *host_buffer = present;
+    if (buffer_from_host_ptr) *buffer_from_host_ptr = present;   // host tensors are staged per op
+    if (events) *events = present;
 }
 
 }  // extern "C"

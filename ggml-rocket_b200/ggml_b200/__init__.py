@@ -181,6 +181,33 @@ _BACKEND_SIGS = {
     "ggml_backend_b200_weight_cache_bytes": (_sz, [_vp, _c.POINTER(_c.c_long)]),
     "ggml_backend_b200_weight_key": (_sz, [_TP, ctypes.c_char_p, _sz]),
     "ggml_backend_b200_breaker_replay": (None, [_c.POINTER(_int), _int, _c.POINTER(_int)]),
+    "ggml_backend_b200_buffer_type_name": (ctypes.c_char_p, []),
+    "ggml_backend_b200_buffer_type_alignment": (_sz, []),
+    "ggml_backend_b200_buffer_type_max_size": (_sz, [_int]),
+    "ggml_backend_b200_buffer_type_alloc_size": (_sz, [_TP]),
+    "ggml_backend_b200_buffer_type_is_host": (ctypes.c_bool, []),
+    "ggml_backend_b200_buffer_alloc": (_vp, [_vp, _sz]),
+    "ggml_backend_b200_buffer_free": (None, [_vp]),
+    "ggml_backend_b200_buffer_base": (_vp, [_vp]),
+    "ggml_backend_b200_buffer_size": (_sz, [_vp]),
+    "ggml_backend_b200_buffer_set": (_int, [_vp, _sz, _vp, _sz]),
+    "ggml_backend_b200_buffer_get": (_int, [_vp, _sz, _vp, _sz]),
+    "ggml_backend_b200_buffer_memset": (_int, [_vp, _sz, _c.c_uint8, _sz]),
+    "ggml_backend_b200_buffer_clear": (_int, [_vp, _c.c_uint8]),
+    "ggml_backend_b200_buffer_copy": (_int, [_vp, _sz, _vp, _sz, _sz]),
+    "ggml_backend_b200_host_alloc": (_vp, [_sz]),
+    "ggml_backend_b200_host_free": (None, [_vp]),
+    "ggml_backend_b200_set_async": (_int, [_vp, _vp, _sz, _vp, _sz]),
+    "ggml_backend_b200_get_async": (_int, [_vp, _vp, _sz, _vp, _sz]),
+    "ggml_backend_b200_copy_async": (_int, [_vp, _vp, _sz, _vp, _sz, _sz]),
+    "ggml_backend_b200_synchronize": (_int, [_vp]),
+    "ggml_backend_b200_event_new": (_vp, [_vp]),
+    "ggml_backend_b200_event_free": (None, [_vp]),
+    "ggml_backend_b200_event_record": (_int, [_vp, _vp]),
+    "ggml_backend_b200_event_wait": (_int, [_vp, _vp]),
+    "ggml_backend_b200_event_synchronize": (_int, [_vp]),
+    "ggml_backend_b200_device_caps": (None, [_int, _c.POINTER(ctypes.c_bool), _c.POINTER(ctypes.c_bool),
+                                             _c.POINTER(ctypes.c_bool), _c.POINTER(ctypes.c_bool)]),
     "b200_flash_attn_workspace_size": (_sz, [_int] * 6),
     "b200_flash_attn_ext": (_int, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp,
                                    _int, _int, _int, _int, _int, _int, _f, _f, _f, _vp, _sz, _vp, _vp]),
@@ -315,6 +342,37 @@ class Backend:
         n = ctypes.c_long(0)
         by = lib().ggml_backend_b200_weight_cache_bytes(self.h, ctypes.byref(n))
         return by, n.value
+
+
+class DeviceBuffer:
+    """A b200 device buffer (the backend's buffer type): tensors placed in it are passed with
+    on_device = 1 and data = base + offset, and graph_compute uses them in place."""
+
+    def __init__(self, backend, size):
+        self.backend = backend
+        self.h = lib().ggml_backend_b200_buffer_alloc(backend.h, size)
+        if not self.h:
+            raise B200Error("ggml_backend_b200_buffer_alloc failed")
+        self.size = size
+        self.base = lib().ggml_backend_b200_buffer_base(self.h)
+
+    def free(self):
+        if self.h:
+            lib().ggml_backend_b200_buffer_free(self.h)
+            self.h = None
+
+    def set(self, offset, arr):
+        import numpy as np
+        a = np.ascontiguousarray(arr)
+        return lib().ggml_backend_b200_buffer_set(self.h, offset, a.ctypes.data, a.nbytes)
+
+    def get(self, offset, out):
+        return lib().ggml_backend_b200_buffer_get(self.h, offset, out.ctypes.data, out.nbytes)
+
+    def tensor(self, offset, ttype, ne, op=OP_NONE, srcs=(), name="", op_params=None):
+        """A descriptor of a contiguous tensor at `offset` in this buffer."""
+        return make_tensor(ttype, ne, self.base + offset, op=op, srcs=srcs, name=name, on_device=True,
+                           op_params=op_params)
 
 
 def weight_key(t):

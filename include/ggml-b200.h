@@ -118,6 +118,67 @@ size_t         ggml_backend_b200_weight_cache_bytes(b200_backend_t backend, long
  * (an unnamed or scheduler-generated "leaf_N" / "node_N" name). */
 size_t         ggml_backend_b200_weight_key(const b200_tensor * w, char * buf, size_t n);
 
+/* ---- device buffers, async transfers and events ----------------------------------------------
+ * The reference hands out the host CPU buffer type (get_buffer_type, ggml-rocket.cpp:7326-7328)
+ * and reports caps.async = caps.events = caps.host_buffer = false (get_props, :7310-7322): its
+ * NPU computes out of system DRAM. A B200 has its own memory, so this backend also offers what a
+ * ggml device with memory offers: a buffer type of device memory (buffer_type_i / buffer_i),
+ * async set / get / copy on the backend's stream, events, and pinned host memory. A tensor placed
+ * in a b200 buffer is passed with on_device = 1 and data = base + offset; graph_compute then
+ * reads and writes it in place, with no host staging. Host buffers stay accepted as before.
+ * Calls return B200_STATUS_SUCCESS or B200_STATUS_FAILED (bad handle, range outside the buffer,
+ * CUDA error). */
+typedef struct b200_buffer * b200_buffer_t;
+typedef struct b200_event  * b200_event_t;
+
+/* buffer type (ggml_backend_buffer_type_i): "B200", 256-byte alignment, at most the device's
+ * memory, the bytes a tensor needs, not host memory */
+const char *  ggml_backend_b200_buffer_type_name(void);
+size_t        ggml_backend_b200_buffer_type_alignment(void);
+size_t        ggml_backend_b200_buffer_type_max_size(int device);
+size_t        ggml_backend_b200_buffer_type_alloc_size(const b200_tensor * t);
+bool          ggml_backend_b200_buffer_type_is_host(void);
+
+/* buffers (ggml_backend_buffer_i) on the backend's GPU; NULL when the allocation fails. The
+ * synchronous calls are ordered after all work already queued on the backend's stream. Writing a
+ * range through these calls, or freeing the buffer, drops every packed weight the backend cached
+ * from bytes in that range (the next graph packs them again). */
+b200_buffer_t ggml_backend_b200_buffer_alloc(b200_backend_t backend, size_t size);
+void          ggml_backend_b200_buffer_free(b200_buffer_t buf);
+void *        ggml_backend_b200_buffer_base(b200_buffer_t buf);
+size_t        ggml_backend_b200_buffer_size(b200_buffer_t buf);
+int           ggml_backend_b200_buffer_set(b200_buffer_t buf, size_t offset, const void * src, size_t size);
+int           ggml_backend_b200_buffer_get(b200_buffer_t buf, size_t offset, void * dst, size_t size);
+int           ggml_backend_b200_buffer_memset(b200_buffer_t buf, size_t offset, uint8_t value, size_t size);
+int           ggml_backend_b200_buffer_clear(b200_buffer_t buf, uint8_t value);
+int           ggml_backend_b200_buffer_copy(b200_buffer_t src, size_t src_offset, b200_buffer_t dst,
+                                            size_t dst_offset, size_t size);
+
+/* pinned host memory (caps.host_buffer): transfers from and to it run asynchronously */
+void *        ggml_backend_b200_host_alloc(size_t size);
+void          ggml_backend_b200_host_free(void * ptr);
+
+/* async transfers on the backend's stream (backend set_tensor_async / get_tensor_async /
+ * cpy_tensor_async) and the wait for everything queued on it (synchronize) */
+int           ggml_backend_b200_set_async(b200_backend_t backend, b200_buffer_t buf, size_t offset,
+                                          const void * src, size_t size);
+int           ggml_backend_b200_get_async(b200_backend_t backend, b200_buffer_t buf, size_t offset,
+                                          void * dst, size_t size);
+int           ggml_backend_b200_copy_async(b200_backend_t backend, b200_buffer_t src, size_t src_offset,
+                                           b200_buffer_t dst, size_t dst_offset, size_t size);
+int           ggml_backend_b200_synchronize(b200_backend_t backend);
+
+/* events (device event_new / event_free / event_synchronize, backend event_record / event_wait) */
+b200_event_t  ggml_backend_b200_event_new(b200_backend_t backend);
+void          ggml_backend_b200_event_free(b200_event_t ev);
+int           ggml_backend_b200_event_record(b200_backend_t backend, b200_event_t ev);
+int           ggml_backend_b200_event_wait(b200_backend_t backend, b200_event_t ev);   /* the stream waits */
+int           ggml_backend_b200_event_synchronize(b200_event_t ev);                    /* the host waits */
+
+/* ggml_backend_dev_caps of a device: async, host_buffer, buffer_from_host_ptr, events */
+void          ggml_backend_b200_device_caps(int device, bool * async, bool * host_buffer,
+                                            bool * buffer_from_host_ptr, bool * events);
+
 /* ---- the device-route circuit breaker (ggml-rocket.cpp:263-307) ----------------------------- */
 /* Replays a sequence of route outcomes through one breaker and writes, per call, whether the
  * route was attempted (1) or bypassed (0); a bypassed call's rc is ignored. For tests. */

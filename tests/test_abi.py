@@ -63,3 +63,32 @@ def test_multi_gpu_and_group_entry_points_reject_bad_arguments_without_a_gpu():
     # b200_moe_ep_p2p_expert_group: no members
     assert lib.b200_moe_ep_p2p_expert_group(0, 12, p, p, 256, 4, 0, p, p, p, 2, 0, 4, 64, 0, p, p, p, p, 1, p, 0, p,
                                             None) == g.B200_E_INVALID
+
+
+def test_buffer_type_and_handles_without_a_gpu():
+    """The device buffer type answers its static queries anywhere; buffer, event and async calls
+    on null or foreign handles fail with a status instead of touching memory."""
+    lib = g.lib()
+    assert lib.ggml_backend_b200_buffer_type_name() == b"B200"
+    assert lib.ggml_backend_b200_buffer_type_alignment() == 256
+    assert not lib.ggml_backend_b200_buffer_type_is_host()
+    t = g.make_tensor(g.F32, [64, 3])
+    assert lib.ggml_backend_b200_buffer_type_alloc_size(ctypes.byref(t)) == 64 * 3 * 4
+    q = g.make_tensor(g.Q4_K, [512, 2])
+    assert lib.ggml_backend_b200_buffer_type_alloc_size(ctypes.byref(q)) == 2 * 2 * 144
+    assert not lib.ggml_backend_b200_buffer_alloc(None, 1024)
+    assert lib.ggml_backend_b200_buffer_size(None) == 0 and not lib.ggml_backend_b200_buffer_base(None)
+    buf = ctypes.create_string_buffer(64)
+    assert lib.ggml_backend_b200_buffer_set(None, 0, buf, 16) == g.STATUS_FAILED
+    assert lib.ggml_backend_b200_buffer_get(None, 0, buf, 16) == g.STATUS_FAILED
+    assert lib.ggml_backend_b200_buffer_memset(None, 0, 0, 16) == g.STATUS_FAILED
+    assert lib.ggml_backend_b200_buffer_copy(None, 0, None, 0, 16) == g.STATUS_FAILED
+    assert lib.ggml_backend_b200_set_async(None, None, 0, buf, 16) == g.STATUS_FAILED
+    assert lib.ggml_backend_b200_synchronize(None) == g.STATUS_FAILED
+    assert not lib.ggml_backend_b200_event_new(None)
+    assert lib.ggml_backend_b200_event_synchronize(None) == g.STATUS_FAILED
+    lib.ggml_backend_b200_buffer_free(None)
+    lib.ggml_backend_b200_event_free(None)
+    flags = [ctypes.c_bool(True) for _ in range(4)]
+    lib.ggml_backend_b200_device_caps(-1, *[ctypes.byref(f) for f in flags])
+    assert not any(f.value for f in flags)
