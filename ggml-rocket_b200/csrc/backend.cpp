@@ -135,6 +135,12 @@ bool fuse_on() {
     static const bool v = knob_on("B200_FUSE", true);
     return v;
 }
+// The glue ops (RMS_NORM, ADD, MUL, SILU, SWIGLU, ROPE, GET_ROWS, CPY). Off by default: the
+// reference claims none of them; B200_GLUE=1 keeps a layer's activations on the device.
+bool glue_on() {
+    static const bool v = knob_on("B200_GLUE", false);
+    return v;
+}
 size_t weight_budget_bytes(int device) {
     const int mb = knob_int("B200_WEIGHT_BUDGET_MB", 0);
     if (mb > 0) return (size_t)mb << 20;
@@ -531,6 +537,63 @@ size_t staged_size(const b200_tensor* t) { return t->on_device ? 0 : ((nbytes(t)
 // claim rules
 // ================================================================================================
 
+// The shapes, types and parameters the glue kernels (glue.cu) implement; anything else stays
+// with the host's CPU backend.
+static bool same_shape(const b200_tensor* a, const b200_tensor* b) {
+    return a->ne[0] == b->ne[0] && a->ne[1] == b->ne[1] && a->ne[2] == b->ne[2] && a->ne[3] == b->ne[3];
+}
+static bool glue_supported(const b200_tensor* op) {
+    const b200_tensor* a = op->src[0];
+    const b200_tensor* b = op->src[1];
+    if (!a) return false;
+    for (int i = 0; i < 4; i++)
+        if (op->ne[i] <= 0) return false;
+    switch (op->op) {
+        case B200_OP_RMS_NORM:
+            return a->type == T_F32 && op->type == T_F32 && is_contiguous(op) && same_shape(a, op) &&
+                   op_param_f32(op, 0) >= 0.0f;
+        case B200_OP_ADD:
+        case B200_OP_MUL: {
+            if (!b || a->type != T_F32 || b->type != T_F32 || op->type != T_F32 || !is_contiguous(op) ||
+                !same_shape(a, op))
+                return false;
+            for (int i = 0; i < 4; i++)
+                if (b->ne[i] <= 0 || a->ne[i] % b->ne[i] != 0) return false;
+            return true;
+        }
+        case B200_OP_UNARY:
+            return op->op_params[0] == B200_UNARY_SILU && a->type == T_F32 && op->type == T_F32 &&
+                   is_contiguous(op) && same_shape(a, op);
+        case B200_OP_GLU: {
+            if (op->op_params[0] != B200_GLU_SWIGLU || a->type != T_F32 || op->type != T_F32 || !is_contiguous(op))
+                return false;
+            if (b) return b->type == T_F32 && same_shape(a, op) && same_shape(b, op);
+            // one input: its two halves along ne[0]
+            return a->ne[0] == 2 * op->ne[0] && a->ne[1] == op->ne[1] && a->ne[2] == op->ne[2] &&
+                   a->ne[3] == op->ne[3];
+        }
+        case B200_OP_ROPE: {
+            const int n_dims = op->op_params[1], mode = op->op_params[2];
+            return b && !op->src[2] && a->type == T_F32 && op->type == T_F32 && b->type == T_I32 &&
+                   is_contiguous(op) && same_shape(a, op) && a->ne[3] == 1 && b->ne[0] == a->ne[2] &&
+                   a->ne[0] % 2 == 0 && n_dims > 0 && n_dims % 2 == 0 && n_dims <= a->ne[0] &&
+                   (mode == 0 || mode == 2) && op_param_f32(op, 7) == 0.0f && op_param_f32(op, 5) > 0.0f;
+        }
+        case B200_OP_GET_ROWS:
+            return b && (a->type == T_F32 || a->type == T_F16) && b->type == T_I32 && op->type == T_F32 &&
+                   is_contiguous(op) && op->ne[0] == a->ne[0] && op->ne[1] == b->ne[0] && op->ne[2] == b->ne[1] &&
+                   op->ne[3] == b->ne[2] && b->ne[3] == 1 && b->ne[1] <= a->ne[2] && b->ne[2] <= a->ne[3];
+        case B200_OP_CPY: {
+            const bool types = (a->type == T_F32 || a->type == T_F16) && (op->type == T_F32 || op->type == T_F16);
+            const int64_t na = a->ne[0] * a->ne[1] * a->ne[2] * a->ne[3];
+            const int64_t nd = op->ne[0] * op->ne[1] * op->ne[2] * op->ne[3];
+            return types && na == nd && (same_shape(a, op) || is_contiguous(op));
+        }
+        default:
+            return false;
+    }
+}
+
 extern "C" bool ggml_backend_b200_supports_op(const b200_tensor* op) {
     if (!op) return false;
     if (!sources_readable(op)) return false;
@@ -617,6 +680,15 @@ extern "C" bool ggml_backend_b200_supports_op(const b200_tensor* op) {
                    aligned16(k) && aligned16(v) && (!m || (m->ne[0] >= KV && m->ne[1] >= T)) &&
                    T >= flash_attn_min_t() && KV >= flash_attn_min_kv();
         }
+        case B200_OP_RMS_NORM:
+        case B200_OP_ADD:
+        case B200_OP_MUL:
+        case B200_OP_UNARY:
+        case B200_OP_GLU:
+        case B200_OP_ROPE:
+        case B200_OP_GET_ROWS:
+        case B200_OP_CPY:
+            return glue_on() && glue_supported(op);
         default:
             return false;
     }
@@ -897,6 +969,81 @@ int do_flash_attn(b200_backend* b, b200_tensor* op) {
     return B200_OK;
 }
 
+// One glue op (glue.cu). Host tensors are staged through the io arena (an output that is a
+// strided host view is read in first, so the bytes between its elements survive the copy back);
+// tensors in device buffers are used in place, with no host synchronisation.
+int do_glue(b200_backend* b, const b200_tensor* op) {
+    const b200_tensor* a = op->src[0];
+    const b200_tensor* c = op->src[1];
+    const bool out_host = !op->on_device;
+    const size_t need_io = staged_size(a) + (c ? staged_size(c) : 0) + 256 +
+                           (out_host ? ((nbytes(op) + 255) & ~(size_t)255) : 0);
+    if (!grow(&b->io, &b->io_bytes, need_io, b->stream)) return B200_E_CUDA;
+    size_t io_off = 0;
+    bool ok = true;
+    const char* sa = static_cast<const char*>(stage_in(b, a, &io_off, &ok));
+    const char* sc = c ? static_cast<const char*>(stage_in(b, c, &io_off, &ok)) : nullptr;
+    if (!ok) return B200_E_CUDA;
+    char* d;
+    if (!out_host) {
+        d = static_cast<char*>(op->data);
+    } else {
+        io_off = (io_off + 255) & ~(size_t)255;
+        d = static_cast<char*>(b->io) + io_off;
+        if (!is_contiguous(op) && cudaMemcpyAsync(d, op->data, nbytes(op), cudaMemcpyHostToDevice, b->stream) != cudaSuccess)
+            return B200_E_CUDA;
+    }
+    float* df = reinterpret_cast<float*>(d);
+    const cudaStream_t st = b->stream;
+    int rc = B200_E_UNSUPPORTED;
+    switch (op->op) {
+        case B200_OP_RMS_NORM:
+            rc = b200_rms_norm(reinterpret_cast<const float*>(sa), a->ne, a->nb, op_param_f32(op, 0), df, st);
+            break;
+        case B200_OP_ADD:
+        case B200_OP_MUL:
+            rc = b200_binary(op->op == B200_OP_ADD ? B200_BIN_ADD : B200_BIN_MUL, reinterpret_cast<const float*>(sa),
+                             a->ne, a->nb, reinterpret_cast<const float*>(sc), c->ne, c->nb, df, st);
+            break;
+        case B200_OP_UNARY:
+            rc = b200_silu(reinterpret_cast<const float*>(sa), a->ne, a->nb, df, st);
+            break;
+        case B200_OP_GLU: {
+            const bool swapped = op->op_params[1] != 0;
+            const char* x = sa;
+            const char* g = sc;
+            const size_t* gnb = c ? c->nb : a->nb;
+            if (!c) g = sa + (size_t)op->ne[0] * a->nb[0];   // one input: its two halves along ne[0]
+            if (swapped) std::swap(x, g);
+            const size_t* xnb = a->nb;
+            if (c && swapped) std::swap(xnb, gnb);
+            rc = b200_swiglu(reinterpret_cast<const float*>(x), xnb, reinterpret_cast<const float*>(g), gnb, op->ne,
+                             df, st);
+            break;
+        }
+        case B200_OP_ROPE:
+            rc = b200_rope(reinterpret_cast<const float*>(sa), a->ne, a->nb, reinterpret_cast<const int32_t*>(sc),
+                           op->op_params[1], op->op_params[2], op_param_f32(op, 5), op_param_f32(op, 6),
+                           op_param_f32(op, 8), df, st);
+            break;
+        case B200_OP_GET_ROWS:
+            rc = b200_get_rows(a->type == T_F16 ? 1 : 0, sa, a->ne, a->nb, reinterpret_cast<const int32_t*>(sc), c->ne,
+                               c->nb, df, b->dev_err, st);
+            break;
+        case B200_OP_CPY:
+            rc = b200_cpy(a->type == T_F16 ? 1 : 0, sa, a->ne, a->nb, op->type == T_F16 ? 1 : 0, d, op->ne, op->nb, st);
+            break;
+        default:
+            break;
+    }
+    if (rc != B200_OK) return rc;
+    if (out_host && cudaMemcpyAsync(op->data, d, nbytes(op), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return B200_E_CUDA;
+    if (op->op == B200_OP_GET_ROWS && !check_dev_err(b, "GET_ROWS")) return B200_E_DEVICE;
+    b->route_ops["glue"]++;
+    return B200_OK;
+}
+
 }  // namespace
 
 // ================================================================================================
@@ -919,10 +1066,20 @@ int ggml_backend_b200_op_from_name(const char* name) {
         {"NONE", B200_OP_NONE},         {"RESHAPE", B200_OP_RESHAPE},       {"VIEW", B200_OP_VIEW},
         {"PERMUTE", B200_OP_PERMUTE},   {"TRANSPOSE", B200_OP_TRANSPOSE},   {"MUL_MAT", B200_OP_MUL_MAT},
         {"MUL_MAT_ID", B200_OP_MUL_MAT_ID}, {"FLASH_ATTN_EXT", B200_OP_FLASH_ATTN_EXT},
+        {"RMS_NORM", B200_OP_RMS_NORM}, {"ADD", B200_OP_ADD},   {"MUL", B200_OP_MUL},
+        {"UNARY", B200_OP_UNARY},       {"GLU", B200_OP_GLU},   {"ROPE", B200_OP_ROPE},
+        {"GET_ROWS", B200_OP_GET_ROWS}, {"CPY", B200_OP_CPY},
     };
     for (const auto& e : map)
         if (strcmp(name, e.n) == 0) return e.op;
     return B200_OP_OTHER;
+}
+
+int ggml_backend_b200_subop_from_name(const char* name) {
+    if (!name) return -1;
+    if (strcmp(name, "SILU") == 0) return B200_UNARY_SILU;
+    if (strcmp(name, "SWIGLU") == 0) return B200_GLU_SWIGLU;
+    return -1;
 }
 
 const char* ggml_backend_b200_device_name(int device) {
@@ -1118,6 +1275,25 @@ int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes,
                 const int rc = do_flash_attn(b, node);
                 if (rc != B200_OK) {
                     logf("E", "graph_compute: FLASH_ATTN_EXT handler failed (%d)\n", rc);
+                    status = B200_STATUS_FAILED;
+                }
+                break;
+            }
+            case B200_OP_RMS_NORM:
+            case B200_OP_ADD:
+            case B200_OP_MUL:
+            case B200_OP_UNARY:
+            case B200_OP_GLU:
+            case B200_OP_ROPE:
+            case B200_OP_GET_ROWS:
+            case B200_OP_CPY: {
+                if (!ggml_backend_b200_supports_op(node)) {
+                    status = B200_STATUS_FAILED;
+                    break;
+                }
+                const int rc = do_glue(b, node);
+                if (rc != B200_OK) {
+                    logf("E", "graph_compute: glue op handler failed (%d) in node %s\n", rc, node->name);
                     status = B200_STATUS_FAILED;
                 }
                 break;

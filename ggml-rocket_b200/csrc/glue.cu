@@ -1,0 +1,321 @@
+// The glue ops of a transformer layer on the device: RMS_NORM, ADD / MUL (with ggml's
+// broadcast), SILU, SWIGLU, ROPE, GET_ROWS and CPY.
+//
+// The reference claims only MUL_MAT, MUL_MAT_ID and FLASH_ATTN_EXT and leaves these to the host's
+// CPU backend; every one of them then forces a device-to-host copy of its input and a
+// host-to-device copy of its output around the claimed ops. Run here, on tensors in device
+// buffers, a layer's activations stay in HBM between ops.
+//
+// Each op follows ggml's CPU definition element by element (the host's ggml-cpu ops.cpp; ggml is
+// not part of this project): the same f32 operations in the same order wherever the result can
+// depend on it (explicit __fmul_rn / __fadd_rn where a contracted FMA would round differently),
+// with two exceptions stated at the kernels: RMS_NORM sums its squares in a tree (in double, as
+// ggml does sequentially) and SILU / ROPE call the device's expf / cosf / sinf (within a few ulp
+// of the host libm's).
+//
+// All are bound by HBM (a read and a write per element, no reuse); they run as grid-stride
+// kernels sized to 4 CTAs per SM, with programmatic launch like the other kernels.
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "ggml-b200-kernels.h"
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace b200 {
+
+struct Shape4 {
+    int64_t ne[4];
+    int64_t nb[4];   // bytes
+};
+
+static Shape4 shape_of(const int64_t ne[4], const size_t nb[4]) {
+    Shape4 s;
+    for (int i = 0; i < 4; i++) s.ne[i] = ne[i], s.nb[i] = (int64_t)nb[i];
+    return s;
+}
+
+__device__ __forceinline__ void unravel(int64_t i, const int64_t ne[4], int64_t (&c)[4]) {
+    c[0] = i % ne[0];
+    i /= ne[0];
+    c[1] = i % ne[1];
+    i /= ne[1];
+    c[2] = i % ne[2];
+    c[3] = i / ne[2];
+}
+__device__ __forceinline__ int64_t offset_of(const int64_t (&c)[4], const int64_t nb[4]) {
+    return c[0] * nb[0] + c[1] * nb[1] + c[2] * nb[2] + c[3] * nb[3];
+}
+
+static int grid_for(int64_t n, int threads) {
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t want = (n + threads - 1) / threads;
+    return (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)sms * 4 * (1024 / threads)));
+}
+
+// ---- RMS_NORM: y = x * (1 / sqrtf(mean(x^2) + eps)), one CTA per row ------------------------
+// ggml sums x*x (an f32 product) into a double sequentially; here each thread sums its strided
+// share in double and the CTA adds the shares in a tree: the same terms, another order.
+constexpr int RMS_THREADS = 256;
+
+__global__ void __launch_bounds__(RMS_THREADS) rms_norm_kernel(const char* __restrict__ x, Shape4 s, float eps,
+                                                               float* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    __shared__ double red[RMS_THREADS / 32];
+    const int64_t rows = s.ne[1] * s.ne[2] * s.ne[3];
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const int64_t i1 = r % s.ne[1], i2 = (r / s.ne[1]) % s.ne[2], i3 = r / (s.ne[1] * s.ne[2]);
+        const char* row = x + i1 * s.nb[1] + i2 * s.nb[2] + i3 * s.nb[3];
+        double sum = 0.0;
+        for (int64_t i = threadIdx.x; i < s.ne[0]; i += RMS_THREADS) {
+            const float v = *reinterpret_cast<const float*>(row + i * s.nb[0]);
+            sum += (double)__fmul_rn(v, v);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+        __syncthreads();
+        double tot = 0.0;
+#pragma unroll
+        for (int w = 0; w < RMS_THREADS / 32; w++) tot += red[w];
+        const float mean = (float)(tot / (double)s.ne[0]);
+        const float scale = 1.0f / sqrtf(__fadd_rn(mean, eps));
+        float* out = dst + r * s.ne[0];
+        for (int64_t i = threadIdx.x; i < s.ne[0]; i += RMS_THREADS)
+            out[i] = __fmul_rn(*reinterpret_cast<const float*>(row + i * s.nb[0]), scale);
+        __syncthreads();   // red is reused by the next row
+    }
+}
+
+// ---- ADD / MUL: dst = a op b, b repeated over a (ggml_can_repeat) ------------------------------
+__global__ void binary_kernel(int op, const char* __restrict__ a, Shape4 sa, const char* __restrict__ b, Shape4 sb,
+                              float* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t n = sa.ne[0] * sa.ne[1] * sa.ne[2] * sa.ne[3];
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t c[4];
+        unravel(i, sa.ne, c);
+        const float x = *reinterpret_cast<const float*>(a + offset_of(c, sa.nb));
+        const int64_t cb[4] = {c[0] % sb.ne[0], c[1] % sb.ne[1], c[2] % sb.ne[2], c[3] % sb.ne[3]};
+        const float y = *reinterpret_cast<const float*>(b + offset_of(cb, sb.nb));
+        dst[i] = op == B200_BIN_ADD ? __fadd_rn(x, y) : __fmul_rn(x, y);
+    }
+}
+
+// ggml_silu_f32: x / (1 + expf(-x)), expf being the device's (within 2 ulp of the host libm's)
+__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+
+// ---- SILU and SWIGLU (dst = silu(a) * g) -------------------------------------------------------
+__global__ void silu_kernel(const char* __restrict__ x, Shape4 s, float* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t n = s.ne[0] * s.ne[1] * s.ne[2] * s.ne[3];
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t c[4];
+        unravel(i, s.ne, c);
+        dst[i] = silu(*reinterpret_cast<const float*>(x + offset_of(c, s.nb)));
+    }
+}
+
+__global__ void swiglu_kernel(const char* __restrict__ a, Shape4 sa, const char* __restrict__ g, Shape4 sg,
+                              float* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t n = sa.ne[0] * sa.ne[1] * sa.ne[2] * sa.ne[3];
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t c[4];
+        unravel(i, sa.ne, c);
+        const float x = *reinterpret_cast<const float*>(a + offset_of(c, sa.nb));
+        const float y = *reinterpret_cast<const float*>(g + offset_of(c, sg.nb));
+        dst[i] = __fmul_rn(silu(x), y);
+    }
+}
+
+// ---- ROPE, modes normal (pairs 2j, 2j+1) and neox (pairs j, j + n_dims/2) -----------------------
+// ggml's rope cache: theta_0 = p, theta_{j+1} = theta_j * theta_scale (f32, sequentially), with
+// theta_scale = powf(freq_base, -2 / n_dims) computed on the host; without YaRN extrapolation
+// (ext_factor 0) the rotation uses cosf(freq_scale * theta_j) * attn_factor and the same for sin.
+// Thread (row, j): one rotated pair (or, for j >= n_dims / 2, a copied pair).
+__global__ void rope_kernel(const char* __restrict__ x, Shape4 s, const int32_t* __restrict__ pos, int n_dims,
+                            int neox, float theta_scale, float freq_scale, float attn_factor, float* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t half = s.ne[0] / 2;
+    const int64_t n = half * s.ne[1] * s.ne[2] * s.ne[3];
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = i % half, r = i / half;
+        const int64_t i1 = r % s.ne[1], i2 = (r / s.ne[1]) % s.ne[2], i3 = r / (s.ne[1] * s.ne[2]);
+        const char* row = x + i1 * s.nb[1] + i2 * s.nb[2] + i3 * s.nb[3];
+        float* out = dst + r * s.ne[0];
+        if (2 * j >= n_dims) {   // past the rotated dimensions: copied
+            out[2 * j] = *reinterpret_cast<const float*>(row + (2 * j) * s.nb[0]);
+            out[2 * j + 1] = *reinterpret_cast<const float*>(row + (2 * j + 1) * s.nb[0]);
+            continue;
+        }
+        float theta = (float)pos[i2];
+        for (int64_t k = 0; k < j; k++) theta = __fmul_rn(theta, theta_scale);
+        const float t = __fmul_rn(freq_scale, theta);
+        const float c = __fmul_rn(cosf(t), attn_factor), sn = __fmul_rn(sinf(t), attn_factor);
+        const int64_t e0 = neox ? j : 2 * j, e1 = neox ? j + n_dims / 2 : 2 * j + 1;
+        const float x0 = *reinterpret_cast<const float*>(row + e0 * s.nb[0]);
+        const float x1 = *reinterpret_cast<const float*>(row + e1 * s.nb[0]);
+        out[e0] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+        out[e1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    }
+}
+
+// ---- GET_ROWS: dst[:, i10, i11, i12] = src[:, idx[i10, i11, i12], i11, i12] (f32 or f16 -> f32) ----
+// An index outside [0, src rows) records ERR_BAD_INDEX and writes zeros for that row.
+__global__ void get_rows_kernel(int f16, const char* __restrict__ src, Shape4 ss, const char* __restrict__ idx,
+                                Shape4 si, float* __restrict__ dst, int* err) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t n = ss.ne[0] * si.ne[0] * si.ne[1] * si.ne[2];
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i0 = i % ss.ne[0];
+        int64_t q = i / ss.ne[0];
+        const int64_t i10 = q % si.ne[0];
+        q /= si.ne[0];
+        const int64_t i11 = q % si.ne[1], i12 = q / si.ne[1];
+        const int64_t r = *reinterpret_cast<const int32_t*>(idx + i10 * si.nb[0] + i11 * si.nb[1] + i12 * si.nb[2]);
+        if (r < 0 || r >= ss.ne[1]) {
+            if (i0 == 0) atomicCAS(err, 0, ERR_BAD_INDEX);
+            dst[i] = 0.0f;
+            continue;
+        }
+        const char* p = src + r * ss.nb[1] + i11 * ss.nb[2] + i12 * ss.nb[3] + i0 * ss.nb[0];
+        dst[i] = f16 ? __half2float(*reinterpret_cast<const __half*>(p)) : *reinterpret_cast<const float*>(p);
+    }
+}
+
+// ---- CPY: element k of src (i0 fastest) -> element k of dst, f32 / f16 either side -------------
+// dst either has src's shape (any strides) or is contiguous with src's element count.
+__global__ void cpy_kernel(int src_f16, const char* __restrict__ src, Shape4 ss, int dst_f16, char* __restrict__ dst,
+                           Shape4 sd, int same_shape) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t n = ss.ne[0] * ss.ne[1] * ss.ne[2] * ss.ne[3];
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t c[4];
+        unravel(i, ss.ne, c);
+        const char* p = src + offset_of(c, ss.nb);
+        const float v = src_f16 ? __half2float(*reinterpret_cast<const __half*>(p)) : *reinterpret_cast<const float*>(p);
+        char* q;
+        if (same_shape) {
+            q = dst + offset_of(c, sd.nb);
+        } else {
+            q = dst + i * (dst_f16 ? 2 : 4);
+        }
+        if (dst_f16) *reinterpret_cast<__half*>(q) = __float2half_rn(v);
+        else *reinterpret_cast<float*>(q) = v;
+    }
+}
+
+static bool shape_ok(const int64_t ne[4], const size_t nb[4]) {
+    if (!ne || !nb) return false;
+    for (int i = 0; i < 4; i++)
+        if (ne[i] <= 0) return false;
+    return true;
+}
+static int64_t nelem(const int64_t ne[4]) { return ne[0] * ne[1] * ne[2] * ne[3]; }
+static int done(cudaError_t e) { return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA; }
+
+}  // namespace b200
+
+extern "C" {
+
+int b200_rms_norm(const float* x, const int64_t ne[4], const size_t nb[4], float eps, float* dst, void* stream) {
+    using namespace b200;
+    if (!x || !dst || !shape_ok(ne, nb) || !(eps >= 0.0f)) return B200_E_INVALID;
+    const int64_t rows = ne[1] * ne[2] * ne[3];
+    const int grid = (int)std::min<int64_t>(rows, 148 * 8);
+    return done(launch_pdl(rms_norm_kernel, dim3((unsigned)grid), dim3(RMS_THREADS), 0,
+                           static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), eps,
+                           dst));
+}
+
+int b200_binary(int op, const float* a, const int64_t ane[4], const size_t anb[4], const float* b, const int64_t bne[4],
+                const size_t bnb[4], float* dst, void* stream) {
+    using namespace b200;
+    if (!a || !b || !dst || !shape_ok(ane, anb) || !shape_ok(bne, bnb)) return B200_E_INVALID;
+    if (op != B200_BIN_ADD && op != B200_BIN_MUL) return B200_E_UNSUPPORTED;
+    for (int i = 0; i < 4; i++)
+        if (ane[i] % bne[i] != 0) return B200_E_INVALID;   // b must repeat over a
+    const int64_t n = nelem(ane);
+    return done(launch_pdl(binary_kernel, dim3((unsigned)grid_for(n, 256)), dim3(256), 0,
+                           static_cast<cudaStream_t>(stream), op, reinterpret_cast<const char*>(a), shape_of(ane, anb),
+                           reinterpret_cast<const char*>(b), shape_of(bne, bnb), dst));
+}
+
+int b200_silu(const float* x, const int64_t ne[4], const size_t nb[4], float* dst, void* stream) {
+    using namespace b200;
+    if (!x || !dst || !shape_ok(ne, nb)) return B200_E_INVALID;
+    const int64_t n = nelem(ne);
+    return done(launch_pdl(silu_kernel, dim3((unsigned)grid_for(n, 256)), dim3(256), 0,
+                           static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), dst));
+}
+
+int b200_swiglu(const float* a, const size_t anb[4], const float* g, const size_t gnb[4], const int64_t ne[4],
+                float* dst, void* stream) {
+    using namespace b200;
+    if (!a || !g || !dst || !shape_ok(ne, anb) || !shape_ok(ne, gnb)) return B200_E_INVALID;
+    const int64_t n = nelem(ne);
+    return done(launch_pdl(swiglu_kernel, dim3((unsigned)grid_for(n, 256)), dim3(256), 0,
+                           static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(a), shape_of(ne, anb),
+                           reinterpret_cast<const char*>(g), shape_of(ne, gnb), dst));
+}
+
+int b200_rope(const float* x, const int64_t ne[4], const size_t nb[4], const int32_t* pos, int n_dims, int mode,
+              float freq_base, float freq_scale, float attn_factor, float* dst, void* stream) {
+    using namespace b200;
+    if (!x || !pos || !dst || !shape_ok(ne, nb) || ne[0] % 2 != 0 || n_dims <= 0 || n_dims % 2 != 0 ||
+        n_dims > ne[0] || !(freq_base > 0.0f))
+        return B200_E_INVALID;
+    if (mode != 0 && mode != 2) return B200_E_UNSUPPORTED;
+    const float theta_scale = powf(freq_base, -2.0f / (float)n_dims);   // the host libm's, as ggml's
+    const int64_t n = (ne[0] / 2) * ne[1] * ne[2] * ne[3];
+    return done(launch_pdl(rope_kernel, dim3((unsigned)grid_for(n, 256)), dim3(256), 0,
+                           static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), pos,
+                           n_dims, mode == 2 ? 1 : 0, theta_scale, freq_scale, attn_factor, dst));
+}
+
+int b200_get_rows(int src_type, const void* src, const int64_t sne[4], const size_t snb[4], const int32_t* idx,
+                  const int64_t ine[4], const size_t inb[4], float* dst, int* dev_err, void* stream) {
+    using namespace b200;
+    if (!src || !idx || !dst || !dev_err || !shape_ok(sne, snb) || !shape_ok(ine, inb) || ine[3] != 1)
+        return B200_E_INVALID;
+    if (src_type != 0 && src_type != 1) return B200_E_UNSUPPORTED;   // F32, F16
+    if (ine[1] > sne[2] || ine[2] > sne[3]) return B200_E_INVALID;
+    const int64_t n = sne[0] * ine[0] * ine[1] * ine[2];
+    return done(launch_pdl(get_rows_kernel, dim3((unsigned)grid_for(n, 256)), dim3(256), 0,
+                           static_cast<cudaStream_t>(stream), src_type, static_cast<const char*>(src),
+                           shape_of(sne, snb), reinterpret_cast<const char*>(idx), shape_of(ine, inb), dst, dev_err));
+}
+
+int b200_cpy(int src_type, const void* src, const int64_t sne[4], const size_t snb[4], int dst_type, void* dst,
+             const int64_t dne[4], const size_t dnb[4], void* stream) {
+    using namespace b200;
+    if (!src || !dst || !shape_ok(sne, snb) || !shape_ok(dne, dnb)) return B200_E_INVALID;
+    if ((src_type != 0 && src_type != 1) || (dst_type != 0 && dst_type != 1)) return B200_E_UNSUPPORTED;
+    const bool same = sne[0] == dne[0] && sne[1] == dne[1] && sne[2] == dne[2] && sne[3] == dne[3];
+    if (!same) {
+        const size_t es = dst_type ? 2 : 4;
+        const bool contiguous = dnb[0] == es && dnb[1] == dnb[0] * (size_t)dne[0] &&
+                                dnb[2] == dnb[1] * (size_t)dne[1] && dnb[3] == dnb[2] * (size_t)dne[2];
+        if (!contiguous || nelem(sne) != nelem(dne)) return B200_E_INVALID;
+    }
+    const int64_t n = nelem(sne);
+    return done(launch_pdl(cpy_kernel, dim3((unsigned)grid_for(n, 256)), dim3(256), 0,
+                           static_cast<cudaStream_t>(stream), src_type, static_cast<const char*>(src),
+                           shape_of(sne, snb), dst_type, static_cast<char*>(dst), shape_of(dne, dnb), same ? 1 : 0));
+}
+
+}  // extern "C"

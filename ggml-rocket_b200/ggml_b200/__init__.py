@@ -137,6 +137,8 @@ def mul_mat_plan(M, N, K, wtype=F16):
 # ---- backend-level API (include/ggml-b200.h) -------------------------------------------------
 
 OP_NONE, OP_RESHAPE, OP_VIEW, OP_PERMUTE, OP_TRANSPOSE, OP_MUL_MAT, OP_MUL_MAT_ID, OP_FLASH_ATTN_EXT, OP_OTHER = range(9)
+OP_RMS_NORM, OP_ADD, OP_MUL, OP_UNARY, OP_GLU, OP_ROPE, OP_GET_ROWS, OP_CPY = range(9, 17)
+UNARY_SILU, GLU_SWIGLU = 1, 2
 STATUS_SUCCESS, STATUS_FAILED = 0, -1
 PREC_F32, PREC_BF16, PREC_F16, PREC_Q8, PREC_Q4 = 10, 15, 20, 30, 40
 HINT_SRC0_IS_HADAMARD = 1
@@ -181,6 +183,14 @@ _BACKEND_SIGS = {
     "ggml_backend_b200_weight_cache_bytes": (_sz, [_vp, _c.POINTER(_c.c_long)]),
     "ggml_backend_b200_weight_key": (_sz, [_TP, ctypes.c_char_p, _sz]),
     "ggml_backend_b200_breaker_replay": (None, [_c.POINTER(_int), _int, _c.POINTER(_int)]),
+    "ggml_backend_b200_subop_from_name": (_int, [ctypes.c_char_p]),
+    "b200_rms_norm": (_int, [_vp, _vp, _vp, _f, _vp, _vp]),
+    "b200_binary": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "b200_silu": (_int, [_vp, _vp, _vp, _vp, _vp]),
+    "b200_swiglu": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "b200_rope": (_int, [_vp, _vp, _vp, _vp, _int, _int, _f, _f, _f, _vp, _vp]),
+    "b200_get_rows": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "b200_cpy": (_int, [_int, _vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
     "ggml_backend_b200_buffer_type_name": (ctypes.c_char_p, []),
     "ggml_backend_b200_buffer_type_alignment": (_sz, []),
     "ggml_backend_b200_buffer_type_max_size": (_sz, [_int]),

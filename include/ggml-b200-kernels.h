@@ -149,6 +149,36 @@ int    b200_mul_mat_vec(int wtype, const void * w_packed, int64_t N, int64_t K, 
                         int64_t M, float * dst, int64_t ldd, void * workspace, size_t workspace_bytes,
                         int * dev_err, void * stream);
 
+/* ---- the glue ops of a layer (RMS_NORM, ADD, MUL, SILU, SWIGLU, ROPE, GET_ROWS, CPY) ----------
+ * The reference leaves these to the host's CPU backend (its supports_op claims only MUL_MAT,
+ * MUL_MAT_ID and FLASH_ATTN_EXT, ggml-rocket.cpp:7410-7772); each follows ggml's CPU definition
+ * element by element. Shapes are ggml's ne[4] (ne[0] innermost) with byte strides nb[4]; f32
+ * outputs are contiguous. All run on `stream` and return B200_OK or a B200_E_* code. */
+enum { B200_BIN_ADD = 0, B200_BIN_MUL = 1 };
+/* every row of x scaled by 1 / sqrtf(mean(x^2) + eps) (ggml rms_norm) */
+int b200_rms_norm(const float * x, const int64_t ne[4], const size_t nb[4], float eps, float * dst, void * stream);
+/* dst = a + b or a * b, b repeated over a (ggml_can_repeat: ane[i] % bne[i] == 0); dst has a's shape */
+int b200_binary(int op, const float * a, const int64_t ane[4], const size_t anb[4],
+                const float * b, const int64_t bne[4], const size_t bnb[4], float * dst, void * stream);
+/* dst = x / (1 + exp(-x)) */
+int b200_silu(const float * x, const int64_t ne[4], const size_t nb[4], float * dst, void * stream);
+/* dst = silu(a) * g, a and g of shape ne */
+int b200_swiglu(const float * a, const size_t anb[4], const float * g, const size_t gnb[4], const int64_t ne[4],
+                float * dst, void * stream);
+/* ggml ROPE of x [head_dim, n_head, n_tokens, 1] at positions pos[n_tokens], mode 0 (normal) or 2
+ * (neox), without YaRN extrapolation (ext_factor 0) and without frequency factors; dimensions
+ * past n_dims are copied */
+int b200_rope(const float * x, const int64_t ne[4], const size_t nb[4], const int32_t * pos, int n_dims, int mode,
+              float freq_base, float freq_scale, float attn_factor, float * dst, void * stream);
+/* dst[:, i, j, k] = src[:, idx[i, j, k], j, k]; src f32 (0) or f16 (1), dst f32 [sne[0], ine[0],
+ * ine[1], ine[2]]; an index outside src's rows records a device error and yields a zero row */
+int b200_get_rows(int src_type, const void * src, const int64_t sne[4], const size_t snb[4], const int32_t * idx,
+                  const int64_t ine[4], const size_t inb[4], float * dst, int * dev_err, void * stream);
+/* element k of src (ne[0] fastest) to element k of dst, converting between f32 (0) and f16 (1)
+ * (round to nearest even); dst has src's shape (any strides) or is contiguous */
+int b200_cpy(int src_type, const void * src, const int64_t sne[4], const size_t snb[4], int dst_type, void * dst,
+             const int64_t dne[4], const size_t dnb[4], void * stream);
+
 /* ---- MUL_MAT_ID ----------------------------------------------------------------------------
  * Replaces ggml_backend_rocket_mul_mat_id (ggml-rocket.cpp:6692-6944): the counting sort of
  * (slot, token) rows by expert (:6706-6732), the per-expert gather (:6790-6800), the expert

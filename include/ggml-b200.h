@@ -37,7 +37,21 @@ typedef enum {
     B200_OP_MUL_MAT_ID,
     B200_OP_FLASH_ATTN_EXT,
     B200_OP_OTHER,
+    /* the glue ops of a layer, claimed only under B200_GLUE=1 (the reference leaves them to the
+     * host's CPU backend) */
+    B200_OP_RMS_NORM,
+    B200_OP_ADD,
+    B200_OP_MUL,
+    B200_OP_UNARY,       /* op_params[0]: B200_UNARY_* */
+    B200_OP_GLU,         /* op_params[0]: B200_GLU_*, op_params[1]: swapped */
+    B200_OP_ROPE,
+    B200_OP_GET_ROWS,
+    B200_OP_CPY,
 } b200_op;
+
+/* Sub-ops of UNARY and GLU, which a ggml adapter maps by name (ggml_unary_op_name /
+ * ggml_glu_op_name) through ggml_backend_b200_subop_from_name; -1 for any other. */
+enum { B200_UNARY_SILU = 1, B200_GLU_SWIGLU = 2 };
 
 /* Precision ranks of ggml's precision contract (op_params, ggml-rocket.cpp:7334-7355). */
 enum {
@@ -79,6 +93,8 @@ const char * ggml_backend_b200_reg_name(void);                       /* "B200" *
 int          ggml_backend_b200_reg_device_count(void);               /* visible CUDA devices */
 /* Maps a ggml op name to a b200_op (B200_OP_OTHER when the backend has no use for it). */
 int          ggml_backend_b200_op_from_name(const char * ggml_op_name);
+/* Maps a ggml unary or GLU op name ("SILU", "SWIGLU") to its B200_UNARY_* / B200_GLU_* value. */
+int          ggml_backend_b200_subop_from_name(const char * name);
 
 /* ---- device (ggml-rocket.cpp:7830-7842) ---------------------------------------------------- */
 const char * ggml_backend_b200_device_name(int device);

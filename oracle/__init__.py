@@ -47,6 +47,10 @@ def lib():
         L.orc_moe_route.argtypes = [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp]
         L.orc_mul_mat_id_f64.argtypes = [_int, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64,
                                          _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _int]
+        L.orc_rms_norm.argtypes = [_vp, _i64, _i64, _f, _vp]
+        L.orc_silu.argtypes = [_vp, _i64, _vp]
+        L.orc_swiglu.argtypes = [_vp, _vp, _i64, _vp]
+        L.orc_rope.argtypes = [_vp, _i64, _i64, _i64, _vp, _int, _int, _f, _f, _f, _vp]
         _L = L
     return _L
 
@@ -154,3 +158,39 @@ def mul_mat_id(t, as_raw, K, N, n_expert, b, ids, nthreads=0):
     if rc:
         return None
     return dst
+
+
+# ---- glue ops (ggml CPU definitions; unpinned: ggml is absent) ----------------------------------
+
+def rms_norm(x, eps):
+    """x [..., n] f32 -> ggml rms_norm over the last axis."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    n = x.shape[-1]
+    lib().orc_rms_norm(_p(x), x.size // n, n, eps, _p(y))
+    return y
+
+
+def silu(x):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().orc_silu(_p(x), x.size, _p(y))
+    return y
+
+
+def swiglu(a, g):
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    y = np.empty_like(a)
+    lib().orc_swiglu(_p(a), _p(g), a.size, _p(y))
+    return y
+
+
+def rope(x, pos, n_dims, mode, freq_base, freq_scale=1.0, attn_factor=1.0):
+    """x [n_tokens, n_head, head_dim] f32, pos [n_tokens] i32 -> ggml rope (ext_factor 0)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    y = np.empty_like(x)
+    T, H, D = x.shape
+    lib().orc_rope(_p(x), D, H, T, _p(pos), n_dims, mode, freq_base, freq_scale, attn_factor, _p(y))
+    return y

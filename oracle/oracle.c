@@ -515,3 +515,58 @@ int orc_mul_mat_id_f64(int wtype, const void * as, int64_t as_nb2, int64_t K, in
     free(off); free(slot); free(tok);
     return 0;
 }
+
+/* ------------------------------------------------------------------------------------ */
+/* Glue ops, restated from ggml's CPU definitions (ggml_compute_forward_rms_norm_f32,       */
+/* ggml_silu_f32, the swiglu vec op, ggml_compute_forward_rope_f32 with its rope cache).    */
+/* ------------------------------------------------------------------------------------ */
+
+void orc_rms_norm(const float * x, int64_t rows, int64_t n, float eps, float * y) {
+    for (int64_t r = 0; r < rows; r++) {
+        const float * xr = x + r * n;
+        double sum = 0.0;
+        for (int64_t i = 0; i < n; i++) sum += (double)(xr[i] * xr[i]);
+        const float mean = (float)(sum / (double)n);
+        const float scale = 1.0f / sqrtf(mean + eps);
+        for (int64_t i = 0; i < n; i++) y[r * n + i] = xr[i] * scale;
+    }
+}
+
+static float orc_silu1(float x) { return x / (1.0f + expf(-x)); }
+
+void orc_silu(const float * x, int64_t n, float * y) {
+    for (int64_t i = 0; i < n; i++) y[i] = orc_silu1(x[i]);
+}
+
+void orc_swiglu(const float * a, const float * g, int64_t n, float * y) {
+    for (int64_t i = 0; i < n; i++) y[i] = orc_silu1(a[i]) * g[i];
+}
+
+void orc_rope(const float * x, int64_t head_dim, int64_t n_head, int64_t n_tokens, const int32_t * pos,
+              int n_dims, int mode, float freq_base, float freq_scale, float attn_factor, float * y) {
+    const float theta_scale = powf(freq_base, -2.0f / (float)n_dims);
+    float * cache = (float *)malloc((size_t)head_dim * sizeof(float));
+    for (int64_t t = 0; t < n_tokens; t++) {
+        float theta = (float)pos[t];
+        for (int64_t i0 = 0; i0 < head_dim; i0 += 2) {
+            const float th = freq_scale * theta;
+            cache[i0 + 0] = cosf(th) * attn_factor;
+            cache[i0 + 1] = sinf(th) * attn_factor;
+            theta *= theta_scale;
+        }
+        for (int64_t h = 0; h < n_head; h++) {
+            const float * src = x + (t * n_head + h) * head_dim;
+            float * dst = y + (t * n_head + h) * head_dim;
+            for (int64_t i0 = 0; i0 < n_dims; i0 += 2) {
+                const float c = cache[i0], s = cache[i0 + 1];
+                const int64_t e0 = mode == 2 ? i0 / 2 : i0;
+                const int64_t e1 = mode == 2 ? i0 / 2 + n_dims / 2 : i0 + 1;
+                const float x0 = src[e0], x1 = src[e1];
+                dst[e0] = x0 * c - x1 * s;
+                dst[e1] = x0 * s + x1 * c;
+            }
+            for (int64_t i0 = n_dims; i0 < head_dim; i0++) dst[i0] = src[i0];
+        }
+    }
+    free(cache);
+}

@@ -91,6 +91,21 @@ int orc_mul_mat_id_f64(int wtype, const void * as, int64_t as_nb2, int64_t K, in
                        const int32_t * ids, int64_t ids_nb0, int64_t ids_nb1, int64_t n_used, int64_t n_tokens,
                        float * dst, int64_t d_nb1, int64_t d_nb2, int nthreads);
 
+/* The glue ops of a layer (RMS_NORM, SILU, SWIGLU, ROPE), restated from ggml's CPU backend
+ * (ggml-cpu ops.cpp / vec.h; ggml is not in this container, so these are unpinned: the product's
+ * kernels follow the same definitions, and the tests compare the two). Contiguous f32 arrays. */
+/* per row of n: squares summed in double in index order, mean = (float)(sum / n),
+ * y = x * (1.0f / sqrtf(mean + eps)) */
+void orc_rms_norm(const float * x, int64_t rows, int64_t n, float eps, float * y);
+/* y = x / (1 + expf(-x)) and y = silu(a) * g */
+void orc_silu(const float * x, int64_t n, float * y);
+void orc_swiglu(const float * a, const float * g, int64_t n, float * y);
+/* ROPE of x [n_tokens][n_head][head_dim], mode 0 (normal) or 2 (neox), ext_factor 0, no
+ * frequency factors: theta_0 = pos, theta_{j+1} = theta_j * powf(freq_base, -2 / n_dims);
+ * cos / sin of freq_scale * theta_j, times attn_factor; dimensions past n_dims copied */
+void orc_rope(const float * x, int64_t head_dim, int64_t n_head, int64_t n_tokens, const int32_t * pos,
+              int n_dims, int mode, float freq_base, float freq_scale, float attn_factor, float * y);
+
 #ifdef __cplusplus
 }
 #endif

@@ -35,7 +35,11 @@ def test_library_answers_without_a_gpu():
     assert lib.ggml_backend_b200_reg_name() == b"B200"
     assert lib.ggml_backend_b200_op_from_name(b"MUL_MAT") == g.OP_MUL_MAT
     assert lib.ggml_backend_b200_op_from_name(b"FLASH_ATTN_EXT") == g.OP_FLASH_ATTN_EXT
-    assert lib.ggml_backend_b200_op_from_name(b"ADD") == g.OP_OTHER
+    assert lib.ggml_backend_b200_op_from_name(b"ADD") == g.OP_ADD
+    assert lib.ggml_backend_b200_op_from_name(b"CONV_2D") == g.OP_OTHER
+    assert lib.ggml_backend_b200_subop_from_name(b"SILU") == g.UNARY_SILU
+    assert lib.ggml_backend_b200_subop_from_name(b"SWIGLU") == g.GLU_SWIGLU
+    assert lib.ggml_backend_b200_subop_from_name(b"GELU") == -1
     assert g.weight_packed_size(g.Q4_K, 4096, 4096) == 4096 * 16 * 144
     assert g.weight_packed_size(g.Q4_K, 4096, 4000) == 0       # K % 256 != 0
 

@@ -1,0 +1,242 @@
+"""The glue ops of a layer (RMS_NORM, ADD, MUL, SILU, SWIGLU, ROPE, GET_ROWS, CPY) on the GPU.
+
+The kernels follow ggml's CPU definitions (restated in the oracle, unpinned since ggml is absent):
+ADD, MUL, GET_ROWS and CPY are exact, so they are compared bit for bit; RMS_NORM (tree-ordered
+double sum), SILU / SWIGLU (device expf) and ROPE (device cosf / sinf on the same f32 angles)
+within GLUE_TOL = 1e-5 max relative error. Then a chain of them runs through graph_compute
+(B200_GLUE=1, read once per process, so in a child) on tensors in a device buffer and on host
+tensors, including a strided host destination."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+GLUE_TOL = 1e-5
+
+
+def _shape(t):
+    """ggml ne / nb (bytes) of a torch tensor whose dims are listed outermost first."""
+    ne = list(reversed(t.shape)) + [1] * (4 - t.dim())
+    nb = [s * t.element_size() for s in reversed(t.stride())]
+    last = nb[-1] * ne[t.dim() - 1] if t.dim() else t.element_size()
+    nb = nb + [last] * (4 - t.dim())
+    return (ctypes.c_int64 * 4)(*ne), (ctypes.c_size_t * 4)(*nb)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def test_rms_norm_silu_swiglu(cuda):
+    import torch
+    import ggml_b200 as g
+    lib = g.lib()
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((7, 4096)).astype(np.float32) * 3
+    xd = torch.from_numpy(x).cuda()
+    y = torch.empty_like(xd)
+    ne, nb = _shape(xd)
+    assert lib.b200_rms_norm(_ptr(xd), ne, nb, 1e-5, _ptr(y), None) == 0
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), oracle.rms_norm(x, 1e-5)) <= GLUE_TOL
+    # a strided view: every other row
+    xs = xd[::2]
+    ne, nb = _shape(xs)
+    y2 = torch.empty(xs.shape, dtype=torch.float32, device="cuda")
+    assert lib.b200_rms_norm(_ptr(xs), ne, nb, 1e-6, _ptr(y2), None) == 0
+    torch.cuda.synchronize()
+    assert rel_err(y2.cpu().numpy(), oracle.rms_norm(x[::2], 1e-6)) <= GLUE_TOL
+    gt = rng.standard_normal(x.shape).astype(np.float32)
+    gd = torch.from_numpy(gt).cuda()
+    ne, nb = _shape(xd)
+    assert lib.b200_silu(_ptr(xd), ne, nb, _ptr(y), None) == 0
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), oracle.silu(x)) <= GLUE_TOL
+    _, gnb = _shape(gd)
+    assert lib.b200_swiglu(_ptr(xd), nb, _ptr(gd), gnb, ne, _ptr(y), None) == 0
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), oracle.swiglu(x, gt)) <= GLUE_TOL
+
+
+def test_add_mul_broadcast_exact(cuda):
+    import torch
+    import ggml_b200 as g
+    lib = g.lib()
+    rng = np.random.default_rng(2)
+    a = rng.standard_normal((2, 3, 6, 64)).astype(np.float32)
+    b = rng.standard_normal((1, 3, 1, 64)).astype(np.float32)
+    ad, bd = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    out = torch.empty_like(ad)
+    ane, anb = _shape(ad)
+    bne, bnb = _shape(bd)
+    for op, want in ((0, a + b), (1, a * b)):   # B200_BIN_ADD, B200_BIN_MUL
+        assert lib.b200_binary(op, _ptr(ad), ane, anb, _ptr(bd), bne, bnb, _ptr(out), None) == 0
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy(), want)
+    # a transposed (strided) first operand
+    at = ad.transpose(2, 3)
+    ane, anb = _shape(at)
+    out2 = torch.empty(at.shape, dtype=torch.float32, device="cuda")
+    b1 = torch.from_numpy(rng.standard_normal((1, 1, 64, 1)).astype(np.float32)).cuda()
+    bne, bnb = _shape(b1)
+    assert lib.b200_binary(0, _ptr(at), ane, anb, _ptr(b1), bne, bnb, _ptr(out2), None) == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(out2.cpu().numpy(), at.cpu().numpy() + b1.cpu().numpy())
+    # b that does not repeat over a is refused
+    bad = torch.zeros((1, 1, 1, 5), dtype=torch.float32, device="cuda")
+    bne, bnb = _shape(bad)
+    assert lib.b200_binary(0, _ptr(at), ane, anb, _ptr(bad), bne, bnb, _ptr(out2), None) == g.B200_E_INVALID
+
+
+@pytest.mark.parametrize("mode,n_dims,base,fscale", [(0, 128, 10000.0, 1.0), (2, 128, 500000.0, 1.0),
+                                                     (2, 64, 10000.0, 0.25), (0, 96, 1000000.0, 0.5)])
+def test_rope(cuda, mode, n_dims, base, fscale):
+    import torch
+    import ggml_b200 as g
+    lib = g.lib()
+    rng = np.random.default_rng(n_dims + mode)
+    T, H, D = 33, 8, 128
+    x = rng.standard_normal((T, H, D)).astype(np.float32)
+    pos = rng.integers(0, 8192, T).astype(np.int32)
+    xd = torch.from_numpy(x).cuda()
+    pd = torch.from_numpy(pos).cuda()
+    y = torch.empty_like(xd)
+    ne, nb = _shape(xd)
+    assert lib.b200_rope(_ptr(xd), ne, nb, _ptr(pd), n_dims, mode, base, fscale, 1.0, _ptr(y), None) == 0
+    torch.cuda.synchronize()
+    want = oracle.rope(x, pos, n_dims, mode, base, fscale, 1.0)
+    assert rel_err(y.cpu().numpy(), want) <= GLUE_TOL
+    assert np.array_equal(y.cpu().numpy()[..., n_dims:], x[..., n_dims:])
+    assert lib.b200_rope(_ptr(xd), ne, nb, _ptr(pd), n_dims, 8, base, fscale, 1.0, _ptr(y), None) == \
+        g.B200_E_UNSUPPORTED   # multi-section / vision modes stay on the host
+
+
+def test_get_rows_and_cpy(cuda):
+    import torch
+    import ggml_b200 as g
+    lib = g.lib()
+    rng = np.random.default_rng(4)
+    table = rng.standard_normal((100, 256)).astype(np.float32)
+    idx = np.array([[3, 99, 0, 3, 57]], dtype=np.int32)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for ttype, tab in ((0, table), (1, table.astype(np.float16))):
+        td = torch.from_numpy(tab).cuda()
+        idd = torch.from_numpy(idx).cuda()
+        out = torch.empty((1, 5, 256), dtype=torch.float32, device="cuda")
+        sne, snb = _shape(td)
+        ine, inb = _shape(idd)
+        assert lib.b200_get_rows(ttype, _ptr(td), sne, snb, _ptr(idd), ine, inb, _ptr(out), _ptr(err), None) == 0
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        assert np.array_equal(out.cpu().numpy()[0], tab[idx[0]].astype(np.float32))
+    # an index past the table: error word set, zero row, the others intact
+    bad = torch.from_numpy(np.array([[1, 100]], dtype=np.int32)).cuda()
+    ine, inb = _shape(bad)
+    td = torch.from_numpy(table).cuda()
+    sne, snb = _shape(td)
+    out = torch.full((1, 2, 256), 7.0, dtype=torch.float32, device="cuda")
+    assert lib.b200_get_rows(0, _ptr(td), sne, snb, _ptr(bad), ine, inb, _ptr(out), _ptr(err), None) == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) != 0
+    o = out.cpu().numpy()[0]
+    assert np.array_equal(o[0], table[1]) and np.all(o[1] == 0)
+    # CPY: f32 -> f16 (round to nearest even), f16 -> f32, a transposed source into a contiguous
+    # destination, and a same-shape strided destination
+    x = (rng.standard_normal((64, 48)) * 100).astype(np.float32)
+    xd = torch.from_numpy(x).cuda()
+    h = torch.empty((64, 48), dtype=torch.float16, device="cuda")
+    sne, snb = _shape(xd)
+    dne, dnb = _shape(h)
+    assert lib.b200_cpy(0, _ptr(xd), sne, snb, 1, _ptr(h), dne, dnb, None) == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(h.cpu().numpy(), x.astype(np.float16))
+    back = torch.empty((64, 48), dtype=torch.float32, device="cuda")
+    sne, snb = _shape(h)
+    dne, dnb = _shape(back)
+    assert lib.b200_cpy(1, _ptr(h), sne, snb, 0, _ptr(back), dne, dnb, None) == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(back.cpu().numpy(), x.astype(np.float16).astype(np.float32))
+    xt = xd.t()                                               # [48, 64] strided
+    flat = torch.empty(48 * 64, dtype=torch.float32, device="cuda")
+    sne, snb = _shape(xt)
+    dne, dnb = _shape(flat)
+    assert lib.b200_cpy(0, _ptr(xt), sne, snb, 0, _ptr(flat), dne, dnb, None) == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(flat.cpu().numpy(), np.ascontiguousarray(x.T).reshape(-1))
+    big = torch.zeros((64, 96), dtype=torch.float32, device="cuda")
+    view = big[:, ::2]                                        # same shape as x, strided
+    sne, snb = _shape(xd)
+    dne, dnb = _shape(view)
+    assert lib.b200_cpy(0, _ptr(xd), sne, snb, 0, _ptr(view), dne, dnb, None) == 0
+    torch.cuda.synchronize()
+    bb = big.cpu().numpy()
+    assert np.array_equal(bb[:, ::2], x) and np.all(bb[:, 1::2] == 0)
+
+
+_CHILD = r"""
+import ctypes, sys
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/ggml-rocket_b200"); sys.path.insert(0, sys.argv[1] + "/tests")
+import numpy as np
+import ggml_b200 as g
+import oracle
+from conftest import rel_err
+be = g.Backend()
+rng = np.random.default_rng(6)
+T, H, D, E = 40, 4, 64, 256
+x = rng.standard_normal((T, E)).astype(np.float32)
+wn = rng.standard_normal(E).astype(np.float32)
+pos = np.arange(T, dtype=np.int32) * 3
+# in a device buffer: xn = rms_norm(x) * wn; q = rope(xn viewed [D, H, T]); s = swiglu(q, q)
+buf = g.DeviceBuffer(be, 1 << 22)
+offs = [i << 18 for i in range(8)]
+assert buf.set(offs[0], x) == 0 and buf.set(offs[1], wn) == 0 and buf.set(offs[2], pos) == 0
+tx = buf.tensor(offs[0], g.F32, [E, T], name="x")
+tw = buf.tensor(offs[1], g.F32, [E], name="attn_norm.weight")
+tp = buf.tensor(offs[2], g.I32, [T], name="pos")
+n1 = buf.tensor(offs[3], g.F32, [E, T], op=g.OP_RMS_NORM, srcs=[tx], op_params=[1e-5])
+n2 = buf.tensor(offs[4], g.F32, [E, T], op=g.OP_MUL, srcs=[n1, tw])
+v = g.make_tensor(g.F32, [D, H, T], n2.data, op=g.OP_VIEW, srcs=[n2], on_device=True)
+r = buf.tensor(offs[5], g.F32, [D, H, T], op=g.OP_ROPE, srcs=[v, tp],
+               op_params=[0, D, 2, 0, 4096, 10000.0, 1.0, 0.0, 1.0, 32.0, 1.0])
+s = buf.tensor(offs[6], g.F32, [D, H, T], op=g.OP_GLU, srcs=[r, r], op_params=[g.GLU_SWIGLU, 0])
+nodes = [n1, n2, v, r, s]
+for nd in (n1, n2, r, s):
+    assert g.supports_op(nd), nd.op
+assert be.graph_compute(nodes) == g.STATUS_SUCCESS
+got = np.zeros((T, H, D), np.float32)
+assert buf.get(offs[6], got) == 0
+xn = oracle.rms_norm(x, 1e-5) * wn
+q = oracle.rope(xn.reshape(T, H, D), pos, D, 2, 10000.0, 1.0, 1.0)
+want = oracle.swiglu(q, q)
+print("CHAIN", rel_err(got, want))
+assert be.route_ops("glue") == 4
+# host tensors: CPY into a strided host destination (the bytes between its elements survive)
+a = rng.standard_normal((8, 32)).astype(np.float32)
+dst = np.full((8, 64), 5.0, np.float32)
+ta = g.make_tensor(g.F32, [32, 8], a)
+td = g.make_tensor(g.F32, [32, 8], dst, op=g.OP_CPY, srcs=[ta], nb=[4, 256, 2048, 2048])
+assert g.supports_op(td)
+assert be.graph_compute([td]) == g.STATUS_SUCCESS
+assert np.array_equal(dst[:, :32], a) and np.all(dst[:, 32:] == 5.0)
+print("HOSTCPY ok")
+assert be.cpu_fallbacks() == 0 and be.device_errors() == 0
+buf.free()
+be.close()
+"""
+
+
+def test_glue_chain_through_graph_compute(cuda):
+    import os
+    import subprocess
+    import sys
+    from conftest import ROOT
+    env = dict(os.environ, B200_GLUE="1")
+    p = subprocess.run([sys.executable, "-c", _CHILD, ROOT], env=env, capture_output=True, text=True, timeout=300)
+    assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
+    assert float(p.stdout.split("CHAIN")[1].split()[0]) <= GLUE_TOL
+    assert "HOSTCPY ok" in p.stdout

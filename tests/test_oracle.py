@@ -148,3 +148,33 @@ def test_oracle_mul_mat_id_matches_per_row(ne11):
             x = ids[t, e]
             ref = oracle.mul_mat(12, ws[x], N, K, b[t, e % ne11][None])
             assert np.array_equal(got[t, e], ref[0])
+
+
+def test_glue_oracle_matches_closed_forms():
+    """The glue-op restatements (unpinned: ggml is absent) against float64 closed forms: the
+    rope's sequential theta product and f32 rounding stay within 1e-5 of base^(-2j/n) * pos at
+    modest positions; rms_norm, silu and swiglu within f32 rounding."""
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((5, 3, 128)).astype(np.float32)
+    ref = x / np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=-1, keepdims=True) + 1e-6)
+    assert np.max(np.abs(oracle.rms_norm(x, 1e-6) - ref)) < 1e-5
+    s = x.astype(np.float64)
+    assert np.max(np.abs(oracle.silu(x) - s / (1 + np.exp(-s)))) < 1e-5
+    g = rng.standard_normal(x.shape).astype(np.float32)
+    assert np.max(np.abs(oracle.swiglu(x, g) - s / (1 + np.exp(-s)) * g)) < 1e-5
+    pos = np.array([0, 1, 7, 31, 100], dtype=np.int32)
+    for mode in (0, 2):
+        for n_dims in (128, 64):
+            y = oracle.rope(x, pos, n_dims, mode, 10000.0, 0.5, 1.0)
+            half = n_dims // 2
+            theta = 0.5 * pos[:, None].astype(np.float64) * 10000.0 ** (-2.0 * np.arange(half) / n_dims)
+            c, sn = np.cos(theta)[:, None, :], np.sin(theta)[:, None, :]
+            if mode == 2:
+                i0, i1 = np.arange(half), np.arange(half) + half
+            else:
+                i0, i1 = 2 * np.arange(half), 2 * np.arange(half) + 1
+            want = s.copy()
+            want[..., i0] = s[..., i0] * c - s[..., i1] * sn
+            want[..., i1] = s[..., i0] * sn + s[..., i1] * c
+            assert np.max(np.abs(y - want)) < 1e-4, (mode, n_dims)
+            assert np.array_equal(y[..., n_dims:], x[..., n_dims:])
