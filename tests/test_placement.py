@@ -124,6 +124,44 @@ def test_moe_auto_defaults():
     assert not moe(2048, 8, 128, K=2000)       # K % 256 != 0 for Q4_K
 
 
+def glue(kind):
+    """Descriptors of the glue ops the B200_GLUE claim rules accept or decline."""
+    x = g.make_tensor(g.F32, [128, 8, 4])
+    pos = g.make_tensor(g.I32, [4])
+    if kind == "rms":
+        d = g.make_tensor(g.F32, [128, 8, 4], op=g.OP_RMS_NORM, srcs=[x], op_params=[1e-5])
+    elif kind == "add_bcast":
+        d = g.make_tensor(g.F32, [128, 8, 4], op=g.OP_ADD, srcs=[x, g.make_tensor(g.F32, [128])])
+    elif kind == "add_norepeat":
+        d = g.make_tensor(g.F32, [128, 8, 4], op=g.OP_ADD, srcs=[x, g.make_tensor(g.F32, [100])])
+    elif kind == "silu":
+        d = g.make_tensor(g.F32, [128, 8, 4], op=g.OP_UNARY, srcs=[x], op_params=[g.UNARY_SILU])
+    elif kind == "gelu":
+        d = g.make_tensor(g.F32, [128, 8, 4], op=g.OP_UNARY, srcs=[x], op_params=[-1])
+    elif kind == "swiglu1":
+        d = g.make_tensor(g.F32, [64, 8, 4], op=g.OP_GLU, srcs=[x], op_params=[g.GLU_SWIGLU, 0])
+    elif kind in ("rope", "rope_yarn", "rope_mrope"):
+        ext = 1.0 if kind == "rope_yarn" else 0.0
+        mode = 8 if kind == "rope_mrope" else 2
+        d = g.make_tensor(g.F32, [128, 8, 4], op=g.OP_ROPE, srcs=[x, pos],
+                          op_params=[0, 128, mode, 0, 4096, 10000.0, 1.0, ext, 1.0, 32.0, 1.0])
+    elif kind == "get_rows_q4k":
+        d = g.make_tensor(g.F32, [256, 4], op=g.OP_GET_ROWS,
+                          srcs=[g.make_tensor(g.Q4_K, [256, 100]), g.make_tensor(g.I32, [4])])
+    elif kind == "get_rows_f16":
+        d = g.make_tensor(g.F32, [256, 4], op=g.OP_GET_ROWS,
+                          srcs=[g.make_tensor(g.F16, [256, 100]), g.make_tensor(g.I32, [4])])
+    elif kind == "cpy_f16":
+        d = g.make_tensor(g.F16, [128, 8, 4], op=g.OP_CPY, srcs=[x])
+    else:
+        raise ValueError(kind)
+    return g.supports_op(d)
+
+
+GLUE_KINDS = ("rms", "add_bcast", "add_norepeat", "silu", "gelu", "swiglu1", "rope", "rope_yarn", "rope_mrope",
+              "get_rows_q4k", "get_rows_f16", "cpy_f16")
+
+
 _CHILD = r"""
 import json, sys
 sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/ggml-rocket_b200"); sys.path.insert(0, sys.argv[1] + "/tests")
@@ -133,7 +171,7 @@ print(json.dumps({"q4k_m256": t.supported(256, 128, 256, 12), "q4k_m512": t.supp
                   "q4k_m1": t.supported(256, 128, 1, 12), "q4k_m8": t.supported(256, 128, 8, 12),
                   "q4k_m9": t.supported(256, 128, 9, 12), "q8_m1": t.supported(256, 128, 1, 8),
                   "moe": t.moe(2048, 8, 128), "fa_unmasked": t.fa(64, 256, 8, 1024, 2, masked=False),
-                  "fa": t.fa(64, 256, 8, 1024, 2)}))
+                  "fa": t.fa(64, 256, 8, 1024, 2), "glue": {k: t.glue(k) for k in t.GLUE_KINDS}}))
 """
 
 
@@ -171,6 +209,11 @@ def test_knobs_in_children():
     assert not r["fa"]
     r = child({})                                  # decode-size MUL_MAT stays on the host by default
     assert not r["q4k_m1"] and not r["q4k_m8"]
+    assert not any(r["glue"].values())             # glue ops stay on the host by default
+    r = child({"B200_GLUE": "1"})
+    assert r["glue"] == {"rms": True, "add_bcast": True, "add_norepeat": False, "silu": True, "gelu": False,
+                         "swiglu1": True, "rope": True, "rope_yarn": False, "rope_mrope": False,
+                         "get_rows_q4k": False, "get_rows_f16": True, "cpy_f16": True}
     r = child({"B200_DECODE": "1"})                # Q4_K at M = 1..8 only
     assert r["q4k_m1"] and r["q4k_m8"] and not r["q4k_m9"] and not r["q8_m1"]
 
