@@ -553,7 +553,8 @@ static bool glue_supported(const b200_tensor* op) {
             return a->type == T_F32 && op->type == T_F32 && is_contiguous(op) && same_shape(a, op) &&
                    op_param_f32(op, 0) >= 0.0f;
         case B200_OP_ADD:
-        case B200_OP_MUL: {
+        case B200_OP_MUL:
+        case B200_OP_DIV: {
             if (!b || a->type != T_F32 || b->type != T_F32 || op->type != T_F32 || !is_contiguous(op) ||
                 !same_shape(a, op))
                 return false;
@@ -583,6 +584,15 @@ static bool glue_supported(const b200_tensor* op) {
             return b && (a->type == T_F32 || a->type == T_F16) && b->type == T_I32 && op->type == T_F32 &&
                    is_contiguous(op) && op->ne[0] == a->ne[0] && op->ne[1] == b->ne[0] && op->ne[2] == b->ne[1] &&
                    op->ne[3] == b->ne[2] && b->ne[3] == 1 && b->ne[1] <= a->ne[2] && b->ne[2] <= a->ne[3];
+        case B200_OP_SOFT_MAX:   // no mask, no ALiBi slope, no sinks
+            return !b && !op->src[2] && a->type == T_F32 && op->type == T_F32 && is_contiguous(op) &&
+                   same_shape(a, op) && op_param_f32(op, 1) == 0.0f;
+        case B200_OP_ARGSORT:
+            return a->type == T_F32 && op->type == T_I32 && is_contiguous(op) && same_shape(a, op) &&
+                   a->ne[0] <= 1024 && (op->op_params[0] == 0 || op->op_params[0] == 1);
+        case B200_OP_SUM_ROWS:
+            return a->type == T_F32 && op->type == T_F32 && is_contiguous(op) && op->ne[0] == 1 &&
+                   op->ne[1] == a->ne[1] && op->ne[2] == a->ne[2] && op->ne[3] == a->ne[3];
         case B200_OP_CPY: {
             const bool types = (a->type == T_F32 || a->type == T_F16) && (op->type == T_F32 || op->type == T_F16);
             const int64_t na = a->ne[0] * a->ne[1] * a->ne[2] * a->ne[3];
@@ -688,6 +698,10 @@ extern "C" bool ggml_backend_b200_supports_op(const b200_tensor* op) {
         case B200_OP_ROPE:
         case B200_OP_GET_ROWS:
         case B200_OP_CPY:
+        case B200_OP_SOFT_MAX:
+        case B200_OP_ARGSORT:
+        case B200_OP_SUM_ROWS:
+        case B200_OP_DIV:
             return glue_on() && glue_supported(op);
         default:
             return false;
@@ -1002,8 +1016,20 @@ int do_glue(b200_backend* b, const b200_tensor* op) {
             break;
         case B200_OP_ADD:
         case B200_OP_MUL:
-            rc = b200_binary(op->op == B200_OP_ADD ? B200_BIN_ADD : B200_BIN_MUL, reinterpret_cast<const float*>(sa),
-                             a->ne, a->nb, reinterpret_cast<const float*>(sc), c->ne, c->nb, df, st);
+        case B200_OP_DIV:
+            rc = b200_binary(op->op == B200_OP_ADD ? B200_BIN_ADD : op->op == B200_OP_MUL ? B200_BIN_MUL : B200_BIN_DIV,
+                             reinterpret_cast<const float*>(sa), a->ne, a->nb, reinterpret_cast<const float*>(sc), c->ne,
+                             c->nb, df, st);
+            break;
+        case B200_OP_SOFT_MAX:
+            rc = b200_soft_max(reinterpret_cast<const float*>(sa), a->ne, a->nb, op_param_f32(op, 0), df, st);
+            break;
+        case B200_OP_ARGSORT:
+            rc = b200_argsort(reinterpret_cast<const float*>(sa), a->ne, a->nb, op->op_params[0],
+                              reinterpret_cast<int32_t*>(d), st);
+            break;
+        case B200_OP_SUM_ROWS:
+            rc = b200_sum_rows(reinterpret_cast<const float*>(sa), a->ne, a->nb, df, st);
             break;
         case B200_OP_UNARY:
             rc = b200_silu(reinterpret_cast<const float*>(sa), a->ne, a->nb, df, st);
@@ -1068,7 +1094,8 @@ int ggml_backend_b200_op_from_name(const char* name) {
         {"MUL_MAT_ID", B200_OP_MUL_MAT_ID}, {"FLASH_ATTN_EXT", B200_OP_FLASH_ATTN_EXT},
         {"RMS_NORM", B200_OP_RMS_NORM}, {"ADD", B200_OP_ADD},   {"MUL", B200_OP_MUL},
         {"UNARY", B200_OP_UNARY},       {"GLU", B200_OP_GLU},   {"ROPE", B200_OP_ROPE},
-        {"GET_ROWS", B200_OP_GET_ROWS}, {"CPY", B200_OP_CPY},
+        {"GET_ROWS", B200_OP_GET_ROWS}, {"CPY", B200_OP_CPY},   {"SOFT_MAX", B200_OP_SOFT_MAX},
+        {"ARGSORT", B200_OP_ARGSORT},   {"SUM_ROWS", B200_OP_SUM_ROWS}, {"DIV", B200_OP_DIV},
     };
     for (const auto& e : map)
         if (strcmp(name, e.n) == 0) return e.op;
@@ -1286,7 +1313,11 @@ int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes,
             case B200_OP_GLU:
             case B200_OP_ROPE:
             case B200_OP_GET_ROWS:
-            case B200_OP_CPY: {
+            case B200_OP_CPY:
+            case B200_OP_SOFT_MAX:
+            case B200_OP_ARGSORT:
+            case B200_OP_SUM_ROWS:
+            case B200_OP_DIV: {
                 if (!ggml_backend_b200_supports_op(node)) {
                     status = B200_STATUS_FAILED;
                     break;

@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(RMS_THREADS) rms_norm_kernel(const char* __res
     }
 }
 
-// ---- ADD / MUL: dst = a op b, b repeated over a (ggml_can_repeat) ------------------------------
+// ---- ADD / MUL / DIV: dst = a op b, b repeated over a (ggml_can_repeat) ------------------------
 __global__ void binary_kernel(int op, const char* __restrict__ a, Shape4 sa, const char* __restrict__ b, Shape4 sb,
                               float* __restrict__ dst) {
     grid_dep_wait();
@@ -106,7 +106,7 @@ __global__ void binary_kernel(int op, const char* __restrict__ a, Shape4 sa, con
         const float x = *reinterpret_cast<const float*>(a + offset_of(c, sa.nb));
         const int64_t cb[4] = {c[0] % sb.ne[0], c[1] % sb.ne[1], c[2] % sb.ne[2], c[3] % sb.ne[3]};
         const float y = *reinterpret_cast<const float*>(b + offset_of(cb, sb.nb));
-        dst[i] = op == B200_BIN_ADD ? __fadd_rn(x, y) : __fmul_rn(x, y);
+        dst[i] = op == B200_BIN_ADD ? __fadd_rn(x, y) : op == B200_BIN_MUL ? __fmul_rn(x, y) : __fdiv_rn(x, y);
     }
 }
 
@@ -219,6 +219,130 @@ __global__ void cpy_kernel(int src_f16, const char* __restrict__ src, Shape4 ss,
     }
 }
 
+// ---- SOFT_MAX (no mask, no ALiBi): w = x * scale; y = expf(w - max) / sum, sum in double ------
+// ggml: the exps summed in index order into a double, then every value times (float)(1 / sum);
+// here the CTA sums in a tree, in double.
+constexpr int SM_THREADS = 256;
+
+__global__ void __launch_bounds__(SM_THREADS) soft_max_kernel(const char* __restrict__ x, Shape4 s, float scale,
+                                                              float* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    __shared__ float fred[SM_THREADS / 32];
+    __shared__ double dred[SM_THREADS / 32];
+    const int64_t rows = s.ne[1] * s.ne[2] * s.ne[3];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const int64_t i1 = r % s.ne[1], i2 = (r / s.ne[1]) % s.ne[2], i3 = r / (s.ne[1] * s.ne[2]);
+        const char* row = x + i1 * s.nb[1] + i2 * s.nb[2] + i3 * s.nb[3];
+        float* out = dst + r * s.ne[0];
+        float mx = -INFINITY;
+        for (int64_t i = threadIdx.x; i < s.ne[0]; i += SM_THREADS)
+            mx = fmaxf(mx, __fmul_rn(*reinterpret_cast<const float*>(row + i * s.nb[0]), scale));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) fred[warp] = mx;
+        __syncthreads();
+        mx = fred[0];
+#pragma unroll
+        for (int w = 1; w < SM_THREADS / 32; w++) mx = fmaxf(mx, fred[w]);
+        double sum = 0.0;
+        for (int64_t i = threadIdx.x; i < s.ne[0]; i += SM_THREADS) {
+            const float e = expf(__fsub_rn(__fmul_rn(*reinterpret_cast<const float*>(row + i * s.nb[0]), scale), mx));
+            out[i] = e;
+            sum += (double)e;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) dred[warp] = sum;
+        __syncthreads();
+        double tot = 0.0;
+#pragma unroll
+        for (int w = 0; w < SM_THREADS / 32; w++) tot += dred[w];
+        const float inv = (float)(1.0 / tot);
+        for (int64_t i = threadIdx.x; i < s.ne[0]; i += SM_THREADS) out[i] = __fmul_rn(out[i], inv);
+        __syncthreads();   // fred / dred are reused by the next row
+    }
+}
+
+// ---- ARGSORT of every row (ne[0] <= 1024): a bitonic sort of (value, index) pairs in shared
+// memory, ties broken by the smaller index (ggml's std::sort leaves the order of ties open) -----
+constexpr int AS_MAX = 1024;
+
+__device__ __forceinline__ bool as_before(float va, int ia, float vb, int ib, bool desc) {
+    if (va != vb) return desc ? va > vb : va < vb;
+    return ia < ib;
+}
+
+__global__ void __launch_bounds__(AS_MAX / 2) argsort_kernel(const char* __restrict__ x, Shape4 s, int desc, int n2,
+                                                             int32_t* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    __shared__ float sv[AS_MAX];
+    __shared__ int si[AS_MAX];
+    const int64_t rows = s.ne[1] * s.ne[2] * s.ne[3];
+    const int n = (int)s.ne[0];
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const int64_t i1 = r % s.ne[1], i2 = (r / s.ne[1]) % s.ne[2], i3 = r / (s.ne[1] * s.ne[2]);
+        const char* row = x + i1 * s.nb[1] + i2 * s.nb[2] + i3 * s.nb[3];
+        for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+            // padding sorts last in either order
+            sv[i] = i < n ? *reinterpret_cast<const float*>(row + (int64_t)i * s.nb[0]) : (desc ? -INFINITY : INFINITY);
+            si[i] = i < n ? i : AS_MAX + i;
+        }
+        __syncthreads();
+        for (int k = 2; k <= n2; k <<= 1) {
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                for (int t = threadIdx.x; t < n2 / 2; t += blockDim.x) {
+                    // the pair (a, b = a + j) this thread compares in this step
+                    const int a = 2 * j * (t / j) + (t % j), b = a + j;
+                    const bool up = (a & k) == 0;   // this block of k sorts ascending in "before" order
+                    const bool swap = up ? as_before(sv[b], si[b], sv[a], si[a], desc != 0)
+                                         : as_before(sv[a], si[a], sv[b], si[b], desc != 0);
+                    if (swap) {
+                        const float tv = sv[a];
+                        sv[a] = sv[b];
+                        sv[b] = tv;
+                        const int ti = si[a];
+                        si[a] = si[b];
+                        si[b] = ti;
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        int32_t* out = dst + r * s.ne[0];
+        for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = si[i];
+        __syncthreads();
+    }
+}
+
+// ---- SUM_ROWS: the sum of every row, in double (ggml_vec_sum_f32 sums in ggml_float) -------
+__global__ void __launch_bounds__(RMS_THREADS) sum_rows_kernel(const char* __restrict__ x, Shape4 s,
+                                                               float* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    __shared__ double red[RMS_THREADS / 32];
+    const int64_t rows = s.ne[1] * s.ne[2] * s.ne[3];
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const int64_t i1 = r % s.ne[1], i2 = (r / s.ne[1]) % s.ne[2], i3 = r / (s.ne[1] * s.ne[2]);
+        const char* row = x + i1 * s.nb[1] + i2 * s.nb[2] + i3 * s.nb[3];
+        double sum = 0.0;
+        for (int64_t i = threadIdx.x; i < s.ne[0]; i += RMS_THREADS)
+            sum += (double)*reinterpret_cast<const float*>(row + i * s.nb[0]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double tot = 0.0;
+            for (int w = 0; w < RMS_THREADS / 32; w++) tot += red[w];
+            dst[r] = (float)tot;
+        }
+        __syncthreads();
+    }
+}
+
 static bool shape_ok(const int64_t ne[4], const size_t nb[4]) {
     if (!ne || !nb) return false;
     for (int i = 0; i < 4; i++)
@@ -246,7 +370,7 @@ int b200_binary(int op, const float* a, const int64_t ane[4], const size_t anb[4
                 const size_t bnb[4], float* dst, void* stream) {
     using namespace b200;
     if (!a || !b || !dst || !shape_ok(ane, anb) || !shape_ok(bne, bnb)) return B200_E_INVALID;
-    if (op != B200_BIN_ADD && op != B200_BIN_MUL) return B200_E_UNSUPPORTED;
+    if (op != B200_BIN_ADD && op != B200_BIN_MUL && op != B200_BIN_DIV) return B200_E_UNSUPPORTED;
     for (int i = 0; i < 4; i++)
         if (ane[i] % bne[i] != 0) return B200_E_INVALID;   // b must repeat over a
     const int64_t n = nelem(ane);
@@ -316,6 +440,36 @@ int b200_cpy(int src_type, const void* src, const int64_t sne[4], const size_t s
     return done(launch_pdl(cpy_kernel, dim3((unsigned)grid_for(n, 256)), dim3(256), 0,
                            static_cast<cudaStream_t>(stream), src_type, static_cast<const char*>(src),
                            shape_of(sne, snb), dst_type, static_cast<char*>(dst), shape_of(dne, dnb), same ? 1 : 0));
+}
+
+int b200_soft_max(const float* x, const int64_t ne[4], const size_t nb[4], float scale, float* dst, void* stream) {
+    using namespace b200;
+    if (!x || !dst || !shape_ok(ne, nb)) return B200_E_INVALID;
+    const int64_t rows = ne[1] * ne[2] * ne[3];
+    return done(launch_pdl(soft_max_kernel, dim3((unsigned)std::min<int64_t>(rows, 148 * 8)), dim3(SM_THREADS), 0,
+                           static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), scale,
+                           dst));
+}
+
+int b200_argsort(const float* x, const int64_t ne[4], const size_t nb[4], int descending, int32_t* dst, void* stream) {
+    using namespace b200;
+    if (!x || !dst || !shape_ok(ne, nb)) return B200_E_INVALID;
+    if (ne[0] > AS_MAX) return B200_E_UNSUPPORTED;
+    int n2 = 2;
+    while (n2 < ne[0]) n2 <<= 1;
+    const int64_t rows = ne[1] * ne[2] * ne[3];
+    const int threads = std::max(32, std::min(AS_MAX / 2, n2 / 2));
+    return done(launch_pdl(argsort_kernel, dim3((unsigned)std::min<int64_t>(rows, 148 * 8)), dim3(threads), 0,
+                           static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb),
+                           descending ? 1 : 0, n2, dst));
+}
+
+int b200_sum_rows(const float* x, const int64_t ne[4], const size_t nb[4], float* dst, void* stream) {
+    using namespace b200;
+    if (!x || !dst || !shape_ok(ne, nb)) return B200_E_INVALID;
+    const int64_t rows = ne[1] * ne[2] * ne[3];
+    return done(launch_pdl(sum_rows_kernel, dim3((unsigned)std::min<int64_t>(rows, 148 * 8)), dim3(RMS_THREADS), 0,
+                           static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), dst));
 }
 
 }  // extern "C"

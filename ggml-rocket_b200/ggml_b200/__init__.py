@@ -138,6 +138,7 @@ def mul_mat_plan(M, N, K, wtype=F16):
 
 OP_NONE, OP_RESHAPE, OP_VIEW, OP_PERMUTE, OP_TRANSPOSE, OP_MUL_MAT, OP_MUL_MAT_ID, OP_FLASH_ATTN_EXT, OP_OTHER = range(9)
 OP_RMS_NORM, OP_ADD, OP_MUL, OP_UNARY, OP_GLU, OP_ROPE, OP_GET_ROWS, OP_CPY = range(9, 17)
+OP_SOFT_MAX, OP_ARGSORT, OP_SUM_ROWS, OP_DIV = range(17, 21)
 UNARY_SILU, GLU_SWIGLU = 1, 2
 STATUS_SUCCESS, STATUS_FAILED = 0, -1
 PREC_F32, PREC_BF16, PREC_F16, PREC_Q8, PREC_Q4 = 10, 15, 20, 30, 40
@@ -191,6 +192,9 @@ _BACKEND_SIGS = {
     "b200_rope": (_int, [_vp, _vp, _vp, _vp, _int, _int, _f, _f, _f, _vp, _vp]),
     "b200_get_rows": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "b200_cpy": (_int, [_int, _vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
+    "b200_soft_max": (_int, [_vp, _vp, _vp, _f, _vp, _vp]),
+    "b200_argsort": (_int, [_vp, _vp, _vp, _int, _vp, _vp]),
+    "b200_sum_rows": (_int, [_vp, _vp, _vp, _vp, _vp]),
     "ggml_backend_b200_buffer_type_name": (ctypes.c_char_p, []),
     "ggml_backend_b200_buffer_type_alignment": (_sz, []),
     "ggml_backend_b200_buffer_type_max_size": (_sz, [_int]),

@@ -154,10 +154,11 @@ int    b200_mul_mat_vec(int wtype, const void * w_packed, int64_t N, int64_t K, 
  * MUL_MAT_ID and FLASH_ATTN_EXT, ggml-rocket.cpp:7410-7772); each follows ggml's CPU definition
  * element by element. Shapes are ggml's ne[4] (ne[0] innermost) with byte strides nb[4]; f32
  * outputs are contiguous. All run on `stream` and return B200_OK or a B200_E_* code. */
-enum { B200_BIN_ADD = 0, B200_BIN_MUL = 1 };
+enum { B200_BIN_ADD = 0, B200_BIN_MUL = 1, B200_BIN_DIV = 2 };
 /* every row of x scaled by 1 / sqrtf(mean(x^2) + eps) (ggml rms_norm) */
 int b200_rms_norm(const float * x, const int64_t ne[4], const size_t nb[4], float eps, float * dst, void * stream);
-/* dst = a + b or a * b, b repeated over a (ggml_can_repeat: ane[i] % bne[i] == 0); dst has a's shape */
+/* dst = a + b, a * b or a / b, b repeated over a (ggml_can_repeat: ane[i] % bne[i] == 0); dst has
+ * a's shape */
 int b200_binary(int op, const float * a, const int64_t ane[4], const size_t anb[4],
                 const float * b, const int64_t bne[4], const size_t bnb[4], float * dst, void * stream);
 /* dst = x / (1 + exp(-x)) */
@@ -178,6 +179,16 @@ int b200_get_rows(int src_type, const void * src, const int64_t sne[4], const si
  * (round to nearest even); dst has src's shape (any strides) or is contiguous */
 int b200_cpy(int src_type, const void * src, const int64_t sne[4], const size_t snb[4], int dst_type, void * dst,
              const int64_t dne[4], const size_t dnb[4], void * stream);
+
+/* The MoE router's ops. SOFT_MAX without mask, ALiBi or sinks: w = x * scale, y = expf(w - max)
+ * / sum(exp), the sum in double; dst f32 contiguous. */
+int b200_soft_max(const float * x, const int64_t ne[4], const size_t nb[4], float scale, float * dst, void * stream);
+/* ARGSORT of every row (ne[0] <= 1024): dst i32 [ne] holds the column indices in ascending or
+ * descending order of value, ties in index order */
+int b200_argsort(const float * x, const int64_t ne[4], const size_t nb[4], int descending, int32_t * dst,
+                 void * stream);
+/* SUM_ROWS: dst f32 [1, ne[1], ne[2], ne[3]] = the sum of every row, accumulated in double */
+int b200_sum_rows(const float * x, const int64_t ne[4], const size_t nb[4], float * dst, void * stream);
 
 /* ---- MUL_MAT_ID ----------------------------------------------------------------------------
  * Replaces ggml_backend_rocket_mul_mat_id (ggml-rocket.cpp:6692-6944): the counting sort of

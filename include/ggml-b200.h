@@ -47,6 +47,11 @@ typedef enum {
     B200_OP_ROPE,
     B200_OP_GET_ROWS,
     B200_OP_CPY,
+    /* the MoE router's ops, also under B200_GLUE=1 */
+    B200_OP_SOFT_MAX,
+    B200_OP_ARGSORT,     /* op_params[0]: 0 ascending, 1 descending (ggml_sort_order) */
+    B200_OP_SUM_ROWS,
+    B200_OP_DIV,
 } b200_op;
 
 /* Sub-ops of UNARY and GLU, which a ggml adapter maps by name (ggml_unary_op_name /

@@ -51,6 +51,7 @@ def lib():
         L.orc_silu.argtypes = [_vp, _i64, _vp]
         L.orc_swiglu.argtypes = [_vp, _vp, _i64, _vp]
         L.orc_rope.argtypes = [_vp, _i64, _i64, _i64, _vp, _int, _int, _f, _f, _f, _vp]
+        L.orc_soft_max.argtypes = [_vp, _i64, _i64, _f, _vp]
         _L = L
     return _L
 
@@ -193,4 +194,13 @@ def rope(x, pos, n_dims, mode, freq_base, freq_scale=1.0, attn_factor=1.0):
     y = np.empty_like(x)
     T, H, D = x.shape
     lib().orc_rope(_p(x), D, H, T, _p(pos), n_dims, mode, freq_base, freq_scale, attn_factor, _p(y))
+    return y
+
+
+def soft_max(x, scale=1.0):
+    """x [..., n] f32 -> ggml soft_max (no mask) over the last axis."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    n = x.shape[-1]
+    lib().orc_soft_max(_p(x), x.size // n, n, scale, _p(y))
     return y

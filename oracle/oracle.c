@@ -570,3 +570,23 @@ void orc_rope(const float * x, int64_t head_dim, int64_t n_head, int64_t n_token
     }
     free(cache);
 }
+
+void orc_soft_max(const float * x, int64_t rows, int64_t n, float scale, float * y) {
+    for (int64_t r = 0; r < rows; r++) {
+        const float * xr = x + r * n;
+        float * yr = y + r * n;
+        float mx = -INFINITY;
+        for (int64_t i = 0; i < n; i++) {
+            const float w = xr[i] * scale;
+            if (w > mx) mx = w;
+        }
+        double sum = 0.0;
+        for (int64_t i = 0; i < n; i++) {
+            const float e = expf(xr[i] * scale - mx);
+            yr[i] = e;
+            sum += (double)e;
+        }
+        const float inv = (float)(1.0 / sum);
+        for (int64_t i = 0; i < n; i++) yr[i] *= inv;
+    }
+}

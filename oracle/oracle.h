@@ -105,6 +105,9 @@ void orc_swiglu(const float * a, const float * g, int64_t n, float * y);
  * cos / sin of freq_scale * theta_j, times attn_factor; dimensions past n_dims copied */
 void orc_rope(const float * x, int64_t head_dim, int64_t n_head, int64_t n_tokens, const int32_t * pos,
               int n_dims, int mode, float freq_base, float freq_scale, float attn_factor, float * y);
+/* ggml soft_max without mask: per row of n, w = x * scale, e = expf(w - max(w)) summed in double
+ * in index order, y = e * (float)(1 / sum) */
+void orc_soft_max(const float * x, int64_t rows, int64_t n, float scale, float * y);
 
 #ifdef __cplusplus
 }

@@ -178,6 +178,100 @@ def test_get_rows_and_cpy(cuda):
     assert np.array_equal(bb[:, ::2], x) and np.all(bb[:, 1::2] == 0)
 
 
+def test_router_ops_soft_max_argsort_sum_rows_div(cuda):
+    import torch
+    import ggml_b200 as g
+    lib = g.lib()
+    rng = np.random.default_rng(8)
+    x = (rng.standard_normal((37, 128)) * 3).astype(np.float32)
+    xd = torch.from_numpy(x).cuda()
+    y = torch.empty_like(xd)
+    ne, nb = _shape(xd)
+    assert lib.b200_soft_max(_ptr(xd), ne, nb, 0.7, _ptr(y), None) == 0
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), oracle.soft_max(x, 0.7)) <= GLUE_TOL
+    s = torch.empty((37, 1), dtype=torch.float32, device="cuda")
+    assert lib.b200_sum_rows(_ptr(xd), ne, nb, _ptr(s), None) == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(s.cpu().numpy()[:, 0], x.astype(np.float64).sum(axis=1).astype(np.float32))
+    q = torch.empty_like(xd)
+    sne, snb = _shape(s)
+    assert lib.b200_binary(2, _ptr(xd), ne, nb, _ptr(s), sne, snb, _ptr(q), None) == 0   # B200_BIN_DIV
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy(), x / s.cpu().numpy())
+    for n in (8, 128, 1000):
+        v = rng.standard_normal((5, n)).astype(np.float32)
+        v[:, 1] = v[:, 0]                                  # a tie: index order
+        vd = torch.from_numpy(v).cuda()
+        ids = torch.empty((5, n), dtype=torch.int32, device="cuda")
+        vne, vnb = _shape(vd)
+        for desc in (0, 1):
+            assert lib.b200_argsort(_ptr(vd), vne, vnb, desc, _ptr(ids), None) == 0
+            torch.cuda.synchronize()
+            want = np.argsort(-v if desc else v, axis=1, kind="stable")
+            assert np.array_equal(ids.cpu().numpy(), want), (n, desc)
+    wide = torch.zeros((1, 2048), dtype=torch.float32, device="cuda")
+    wne, wnb = _shape(wide)
+    assert lib.b200_argsort(_ptr(wide), wne, wnb, 1, _ptr(ids), None) == g.B200_E_UNSUPPORTED
+
+
+_ROUTER_CHILD = r"""
+import sys
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/ggml-rocket_b200"); sys.path.insert(0, sys.argv[1] + "/tests")
+import numpy as np
+import ggml_b200 as g
+import oracle
+from conftest import rel_err
+be = g.Backend()
+rng = np.random.default_rng(12)
+E, T, K = 64, 48, 8
+logits = (rng.standard_normal((T, E)) * 2).astype(np.float32)
+buf = g.DeviceBuffer(be, 1 << 20)
+o = [i << 16 for i in range(8)]
+assert buf.set(o[0], logits) == 0
+tl = buf.tensor(o[0], g.F32, [E, T], name="ffn_moe_logits")
+pr = buf.tensor(o[1], g.F32, [E, T], op=g.OP_SOFT_MAX, srcs=[tl], op_params=[1.0, 0.0])
+srt = buf.tensor(o[2], g.I32, [E, T], op=g.OP_ARGSORT, srcs=[pr], op_params=[1])
+sel = g.make_tensor(g.I32, [K, T], srt.data, op=g.OP_VIEW, srcs=[srt], on_device=True, nb=[4, 4 * E, 4 * E * T, 4 * E * T])
+pv = g.make_tensor(g.F32, [1, E, T], pr.data, op=g.OP_VIEW, srcs=[pr], on_device=True)
+wts = buf.tensor(o[3], g.F32, [1, K, T], op=g.OP_GET_ROWS, srcs=[pv, sel])
+w2 = g.make_tensor(g.F32, [K, T], wts.data, op=g.OP_VIEW, srcs=[wts], on_device=True)
+sm = buf.tensor(o[4], g.F32, [1, T], op=g.OP_SUM_ROWS, srcs=[w2])
+nw = buf.tensor(o[5], g.F32, [K, T], op=g.OP_DIV, srcs=[w2, sm])
+for nd in (pr, srt, wts, sm, nw):
+    assert g.supports_op(nd), nd.op
+assert be.graph_compute([pr, srt, sel, pv, wts, w2, sm, nw]) == g.STATUS_SUCCESS
+ids = np.zeros((T, E), np.int32)
+got = np.zeros((T, K), np.float32)
+assert buf.get(o[2], ids) == 0 and buf.get(o[5], got) == 0
+p = oracle.soft_max(logits, 1.0)
+want_ids = np.argsort(-p, axis=1, kind="stable")
+print("IDS", int(np.array_equal(ids, want_ids)))
+top = np.take_along_axis(p, want_ids[:, :K], axis=1)
+want = top / top.astype(np.float64).sum(axis=1, keepdims=True).astype(np.float32)
+print("WEIGHTS", rel_err(got, want))
+assert be.route_ops("glue") == 5 and be.device_errors() == 0
+buf.free()
+be.close()
+"""
+
+
+def test_moe_router_through_graph_compute(cuda):
+    """The MoE router of a llama.cpp graph (soft_max -> argsort desc -> top-k view -> get_rows ->
+    sum_rows -> div) on a device buffer under B200_GLUE=1: the expert ids exactly, the
+    normalised weights within GLUE_TOL."""
+    import os
+    import subprocess
+    import sys
+    from conftest import ROOT
+    env = dict(os.environ, B200_GLUE="1")
+    p = subprocess.run([sys.executable, "-c", _ROUTER_CHILD, ROOT], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
+    assert p.stdout.split("IDS")[1].split()[0] == "1"
+    assert float(p.stdout.split("WEIGHTS")[1].split()[0]) <= GLUE_TOL
+
+
 _CHILD = r"""
 import ctypes, sys
 sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/ggml-rocket_b200"); sys.path.insert(0, sys.argv[1] + "/tests")

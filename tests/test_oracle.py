@@ -178,3 +178,11 @@ def test_glue_oracle_matches_closed_forms():
             want[..., i1] = s[..., i0] * sn + s[..., i1] * c
             assert np.max(np.abs(y - want)) < 1e-4, (mode, n_dims)
             assert np.array_equal(y[..., n_dims:], x[..., n_dims:])
+
+
+def test_soft_max_oracle_matches_closed_form():
+    rng = np.random.default_rng(10)
+    x = (rng.standard_normal((6, 256)) * 4).astype(np.float32)
+    w = x.astype(np.float64) * 0.5
+    e = np.exp(w - w.max(axis=-1, keepdims=True))
+    assert np.max(np.abs(oracle.soft_max(x, 0.5) - e / e.sum(axis=-1, keepdims=True))) < 1e-6

@@ -153,13 +153,27 @@ def glue(kind):
                           srcs=[g.make_tensor(g.F16, [256, 100]), g.make_tensor(g.I32, [4])])
     elif kind == "cpy_f16":
         d = g.make_tensor(g.F16, [128, 8, 4], op=g.OP_CPY, srcs=[x])
+    elif kind == "soft_max":
+        d = g.make_tensor(g.F32, [128, 8, 4], op=g.OP_SOFT_MAX, srcs=[x], op_params=[1.0, 0.0])
+    elif kind == "soft_max_mask":
+        d = g.make_tensor(g.F32, [128, 8, 4], op=g.OP_SOFT_MAX, srcs=[x, g.make_tensor(g.F32, [128, 8])],
+                          op_params=[1.0, 0.0])
+    elif kind == "argsort":
+        d = g.make_tensor(g.I32, [128, 8, 4], op=g.OP_ARGSORT, srcs=[x], op_params=[1])
+    elif kind == "argsort_wide":
+        d = g.make_tensor(g.I32, [2048, 3], op=g.OP_ARGSORT, srcs=[g.make_tensor(g.F32, [2048, 3])], op_params=[1])
+    elif kind == "sum_rows":
+        d = g.make_tensor(g.F32, [1, 8, 4], op=g.OP_SUM_ROWS, srcs=[x])
+    elif kind == "div":
+        d = g.make_tensor(g.F32, [128, 8, 4], op=g.OP_DIV, srcs=[x, g.make_tensor(g.F32, [1, 8, 4])])
     else:
         raise ValueError(kind)
     return g.supports_op(d)
 
 
 GLUE_KINDS = ("rms", "add_bcast", "add_norepeat", "silu", "gelu", "swiglu1", "rope", "rope_yarn", "rope_mrope",
-              "get_rows_q4k", "get_rows_f16", "cpy_f16")
+              "get_rows_q4k", "get_rows_f16", "cpy_f16", "soft_max", "soft_max_mask", "argsort", "argsort_wide",
+              "sum_rows", "div")
 
 
 _CHILD = r"""
@@ -213,7 +227,9 @@ def test_knobs_in_children():
     r = child({"B200_GLUE": "1"})
     assert r["glue"] == {"rms": True, "add_bcast": True, "add_norepeat": False, "silu": True, "gelu": False,
                          "swiglu1": True, "rope": True, "rope_yarn": False, "rope_mrope": False,
-                         "get_rows_q4k": False, "get_rows_f16": True, "cpy_f16": True}
+                         "get_rows_q4k": False, "get_rows_f16": True, "cpy_f16": True, "soft_max": True,
+                         "soft_max_mask": False, "argsort": True, "argsort_wide": False, "sum_rows": True,
+                         "div": True}
     r = child({"B200_DECODE": "1"})                # Q4_K at M = 1..8 only
     assert r["q4k_m1"] and r["q4k_m8"] and not r["q4k_m9"] and not r["q8_m1"]
 
