@@ -57,11 +57,12 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemm", "gemv", "moe", "fa"], default="gemm",
+    ap.add_argument("--workload", choices=["gemm", "gemv", "moe", "fa", "glue"], default="gemm",
                     help="gemm: the headline MUL_MAT sweep (default); gemv: the sweep's Q4_K weights at decode "
                          "size (M = --decode-m, b200_mul_mat_vec); moe: the MUL_MAT_ID layer of "
                          "BASELINE configs[3], expert-parallel over the ranks; fa: the FLASH_ATTN_EXT "
-                         "prefill of configs[2]")
+                         "prefill of configs[2]; glue: a layer's glue ops and the MoE router at the "
+                         "headline's prefill shapes (HBM-bound kernels, GB/s)")
     ap.add_argument("--decode-m", type=int, default=1,
                     help="gemv workload: token rows per step (1..8)")
     ap.add_argument("--shard", action="store_true",
@@ -778,6 +779,130 @@ def run_gemm_sharded(args):
     return 0
 
 
+def _ne_nb(t):
+    """ggml ne[4] / nb[4] (bytes) of a torch tensor whose dims are listed outermost first."""
+    import ctypes
+    ne = list(reversed(t.shape)) + [1] * (4 - t.dim())
+    nb = [st * t.element_size() for st in reversed(t.stride())]
+    last = nb[-1] * ne[t.dim() - 1]
+    nb = nb + [last] * (4 - t.dim())
+    return (ctypes.c_int64 * 4)(*ne), (ctypes.c_size_t * 4)(*nb)
+
+
+def run_glue(args):
+    """The glue ops of a Llama-8B-shaped layer at a 512-token ubatch (hidden 4096, FFN 14336, 32
+    query / 8 KV heads of 128) and the MoE router of configs[3] (128 experts, 2048 tokens), each
+    through its C-ABI entry point on device tensors, L2 flushed before every step. value = the
+    ops' algorithmic bytes (one read of every input element, one write of every output element)
+    per second of their summed CUDA-event time; per-op figures in config."""
+    import ctypes
+    import torch
+    import ggml_b200 as g
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lib = g.lib()
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    gen = torch.Generator(device=dev).manual_seed(0xB200)
+    T, E, F, H, HK, D = 512, 4096, 14336, 32, 8, 128
+
+    def rnd(*shape, dtype=torch.float32):
+        return torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32).to(dtype)
+
+    x, res, wn = rnd(T, E), rnd(T, E), rnd(E)
+    q, k = rnd(T, H, D), rnd(T, HK, D)
+    pos = torch.arange(T, device=dev, dtype=torch.int32)
+    gate, up = rnd(T, F), rnd(T, F)
+    table = rnd(32000, E, dtype=torch.float16)
+    ids = torch.randint(0, 32000, (T,), generator=gen, device=dev, dtype=torch.int32)
+    logits = rnd(2048, 128)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    o_e = torch.empty(T, E, device=dev)
+    o_q, o_k = torch.empty_like(q), torch.empty_like(k)
+    o_f = torch.empty(T, F, device=dev)
+    o_kh = torch.empty(T, HK, D, device=dev, dtype=torch.float16)
+    o_rows = torch.empty(T, E, device=dev)
+    o_p = torch.empty_like(logits)
+    o_ids = torch.empty(2048, 128, device=dev, dtype=torch.int32)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())   # noqa: E731
+    sh = {n: _ne_nb(t) for n, t in (("x", x), ("wn", wn), ("q", q), ("k", k), ("f", gate), ("tab", table),
+                                     ("ids", ids.view(1, T)), ("lg", logits), ("kh", o_kh))}
+    ops = [
+        ("rms_norm", 8 * T * E, lambda: lib.b200_rms_norm(P(x), *sh["x"], 1e-5, P(o_e), sp)),
+        ("mul_norm_weight", 8 * T * E + 4 * E,
+         lambda: lib.b200_binary(1, P(o_e), *sh["x"], P(wn), *sh["wn"], P(o_e), sp)),
+        ("rope_q", 8 * T * H * D, lambda: lib.b200_rope(P(q), *sh["q"], P(pos), D, 2, 500000.0, 1.0, 1.0, P(o_q), sp)),
+        ("rope_k", 8 * T * HK * D,
+         lambda: lib.b200_rope(P(k), *sh["k"], P(pos), D, 2, 500000.0, 1.0, 1.0, P(o_k), sp)),
+        ("cpy_k_f16", 6 * T * HK * D, lambda: lib.b200_cpy(0, P(o_k), *sh["k"], 1, P(o_kh), *sh["kh"], sp)),
+        ("swiglu", 12 * T * F,
+         lambda: lib.b200_swiglu(P(gate), sh["f"][1], P(up), sh["f"][1], sh["f"][0], P(o_f), sp)),
+        ("add_residual", 12 * T * E, lambda: lib.b200_binary(0, P(x), *sh["x"], P(res), *sh["x"], P(o_e), sp)),
+        ("get_rows_f16", 6 * T * E + 4 * T,
+         lambda: lib.b200_get_rows(1, P(table), *sh["tab"], P(ids), *sh["ids"], P(o_rows), P(err), sp)),
+        ("router_soft_max", 8 * 2048 * 128, lambda: lib.b200_soft_max(P(logits), *sh["lg"], 1.0, P(o_p), sp)),
+        ("router_argsort", 8 * 2048 * 128, lambda: lib.b200_argsort(P(o_p), *sh["lg"], 1, P(o_ids), sp)),
+    ]
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def step(evs=None):
+        for i, (_, _, fn) in enumerate(ops):
+            if evs:
+                evs[i][0].record(stream)
+            rc = fn()
+            if rc != 0:
+                raise SystemExit(f"glue op {ops[i][0]} failed: {rc}")
+            if evs:
+                evs[i][1].record(stream)
+
+    for _ in range(max(3, args.warmup)):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    per = [[] for _ in ops]
+    steps = []
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda._sleep(1000000)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in ops]
+        step(evs)
+        steps.append(evs)
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    if int(err.item()) != 0:
+        raise SystemExit(f"device error {int(err.item())}")
+    for evs in steps:
+        for i, (e0, e1) in enumerate(evs):
+            per[i].append(e0.elapsed_time(e1))
+    med = [statistics.median(v) for v in per]
+    total_bytes = sum(b for _, b, _ in ops)
+    total_ms = sum(med)
+    if rank == 0:
+        peaks, src = measured_peaks()
+        peak = float(peaks.get("hbm_gbs", 6650.0))
+        gbs = total_bytes / (total_ms / 1e3) / 1e9
+        table_out = {name: {"us": m * 1e3, "GB/s": b / (m / 1e3) / 1e9, "frac": b / (m / 1e3) / 1e9 / peak}
+                     for (name, b, _), m in zip(ops, med)}
+        line = {"metric": "glue-op GB/s (algorithmic bytes) at Llama-8B prefill shapes, T=512, and the configs[3] "
+                          "MoE router", "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": total_ms, "higher_is_better": True,
+                "scaling": "replicas only", "vs_baseline": None, "dtype": "f32 (f16 table / KV cache)",
+                "data": "synthetic",
+                "config": {"workload": "RMS_NORM, MUL, ROPE q/k, CPY k->f16, SWIGLU, ADD, GET_ROWS, SOFT_MAX, "
+                                       "ARGSORT via their C-ABI entry points", "ops": table_out,
+                           "l2": "flushed before every timed step (256 MiB memset), outside the timed events",
+                           "median_of_steps": True},
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                             "peak_source": f"{src} hbm_gbs"},
+                "clocks": clocks, "gpu_launches": len(ops) * args.steps}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -788,6 +913,8 @@ def main():
         return run_fa(args)
     if args.workload == "gemv":
         return run_gemv(args)
+    if args.workload == "glue":
+        return run_glue(args)
     if args.shard:
         return run_gemm_sharded(args)
     return run_ours(args)
