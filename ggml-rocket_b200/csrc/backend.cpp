@@ -988,7 +988,8 @@ int do_flash_attn(b200_backend* b, b200_tensor* op) {
 // tensors in device buffers are used in place, with no host synchronisation.
 int do_glue(b200_backend* b, const b200_tensor* op) {
     const b200_tensor* a = op->src[0];
-    const b200_tensor* c = op->src[1];
+    // ggml's CPY carries its destination as src[1]: that one is written, not read
+    const b200_tensor* c = op->op == B200_OP_CPY ? nullptr : op->src[1];
     const bool out_host = !op->on_device;
     const size_t need_io = staged_size(a) + (c ? staged_size(c) : 0) + 256 +
                            (out_host ? ((nbytes(op) + 255) & ~(size_t)255) : 0);
