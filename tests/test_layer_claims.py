@@ -19,6 +19,19 @@ out = {}
 for n_kv in (512, 1024):
     L = llama_layer(512, n_kv=n_kv)
     out[n_kv] = {x.name.decode(): [bool(g.supports_op(x)), bool(g.offload_op(x))] for x in L.nodes}
+# the same layer with storage: a bump allocator of (fake) device addresses, 256-byte aligned
+top = [1 << 40]
+spans = []
+def alloc(n):
+    a = top[0]
+    top[0] += (n + 255) // 256 * 256
+    spans.append((a, a + n))
+    return a, True
+L = llama_layer(512, n_kv=1024, alloc=alloc)
+out["alloc_claims"] = all(bool(g.supports_op(x)) for x in L.nodes)
+out["spans"] = spans
+out["views"] = [[x.name.decode(), x.data, x.src[0].contents.data] for x in L.nodes
+                if x.op in (g.OP_VIEW, g.OP_RESHAPE, g.OP_PERMUTE)]
 print(json.dumps(out))
 """
 
@@ -33,7 +46,7 @@ def claims(env):
     e.update(env)
     p = subprocess.run([sys.executable, "-c", _CHILD, ROOT], env=e, capture_output=True, text=True, timeout=120)
     assert p.returncode == 0, p.stderr[-2000:]
-    return {int(k): v for k, v in json.loads(p.stdout.strip().splitlines()[-1]).items()}
+    return {(int(k) if k.isdigit() else k): v for k, v in json.loads(p.stdout.strip().splitlines()[-1]).items()}
 
 
 def test_layer_nodes_are_all_accounted_for():
@@ -60,3 +73,15 @@ def test_glue_knob_claims_every_node():
     assert all(sup for sup, _ in r[1024].values()), [n for n, (s, _) in r[1024].items() if not s]
     assert [n for n, (s, _) in r[512].items() if not s] == ["kqv_out"]
     assert not any(off for n, (_, off) in r[1024].items() if n not in MATMULS)
+
+
+def test_layer_with_storage():
+    """With an allocator, every tensor gets its own 256-byte aligned range, views address their
+    base tensor's bytes, and the claims hold for device-resident tensors too."""
+    r = claims({"B200_GLUE": "1"})
+    assert r["alloc_claims"]
+    spans = sorted(r["spans"])
+    assert all(a % 256 == 0 for a, _ in spans)
+    assert all(spans[i][1] <= spans[i + 1][0] for i in range(len(spans) - 1))
+    for name, data, base in r["views"]:
+        assert data == base, name               # every view here starts at its source's first byte
