@@ -120,26 +120,36 @@ __device__ __forceinline__ int dequant_slot(int warp) {
 template <int BT, int WT, bool PAIR = false>
 struct GemmCfg {
     static constexpr bool QUANT = (WT != WT_F16);
+    // WIDE (BT = 512): one work unit is a 128-row weight tile against 512 tokens, two 256-token
+    // halves sharing every decoded weight stage, so each weight is decoded once per 512 tokens
+    // (twice as much tensor-core work per decoded weight as BT = 256). The two halves' fp32
+    // accumulators fill the 512 TMEM columns: there is one accumulator, not two alternating ones.
+    static constexpr bool WIDE = BT == 512;
+    static constexpr int MMA_N = WIDE ? 256 : BT;        // tcgen05 N of one MMA
+    static constexpr int N_ACC = WIDE ? 1 : 2;
     // A CTA pair splits the token tile: each CTA stages BT/2 activation rows.
     static constexpr int A_ROWS = PAIR ? BT / 2 : BT;
+    static constexpr int A_BOX = WIDE ? 256 : A_ROWS;   // rows per activation TMA box (<= 256)
     static constexpr int A_BYTES = A_ROWS * GEMM_BK * 2;
     static constexpr int W_BYTES = GEMM_BN * GEMM_BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + W_BYTES;
-    static constexpr int RAW_TOTAL = RawCfg<WT>::STAGE * RawCfg<WT>::STAGES;
+    static constexpr int RAW_STAGES = QUANT ? (WIDE ? 2 : RawCfg<WT>::STAGES) : 0;
+    static constexpr int RAW_TOTAL = RawCfg<WT>::STAGE * RAW_STAGES;
     static constexpr int EPI_BYTES = 4 * 32 * 32 * 4;          // a 32 x 32 f32 transpose tile per epilogue warp
-    static constexpr int BUDGET = 232448 - 1024 - 256 - RAW_TOTAL - EPI_BYTES;
+    static constexpr int BUDGET = 232448 - 1024 - 512 - RAW_TOTAL - EPI_BYTES;
     static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
     static constexpr int THREADS = QUANT ? (W_DEQ0 + DEQ_WARPS) * 32 : 7 * 32;
     static constexpr int DEQ_THREADS = DEQ_WARPS * 32;
-    static constexpr int BAR_BYTES = 256;
+    static constexpr int BAR_BYTES = 512;   // 3 * STAGES + 11 barriers + the TMEM slot and abort flag
     static constexpr int RAW_OFF = STAGES * STAGE_BYTES;
     static constexpr int EPI_OFF = RAW_OFF + RAW_TOTAL;
     static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
     static constexpr int SMEM = BAR_OFF + BAR_BYTES + 1024;
-    static constexpr uint32_t TMEM_COLS = 2 * BT;
-    static constexpr uint32_t IDESC = idesc_f16_f32(PAIR ? 2 * GEMM_BN : GEMM_BN, BT);
+    static constexpr uint32_t TMEM_COLS = WIDE ? 512 : 2 * BT;
+    static constexpr uint32_t IDESC = idesc_f16_f32(PAIR ? 2 * GEMM_BN : GEMM_BN, MMA_N);
     static constexpr int TILE_N = PAIR ? 2 * GEMM_BN : GEMM_BN;   // weight rows per work tile
     static_assert(STAGES >= 2, "pipeline too shallow");
+    static_assert(!(WIDE && PAIR), "the wide tile runs on one SM");
 };
 
 template <int BT, int WT, bool GROUPED, bool PAIR>
@@ -147,6 +157,7 @@ __global__ void __launch_bounds__(GemmCfg<BT, WT, PAIR>::THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
             const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmO, const GemmArgs args) {
     static_assert(!(GROUPED && PAIR), "the grouped GEMM runs one CTA per tile");
+    static_assert(!(GROUPED && BT == 512), "the grouped GEMM's tiles are at most 256 rows of one expert");
     using C = GemmCfg<BT, WT, PAIR>;
     using RC = RawCfg<WT>;
     constexpr int STAGES = C::STAGES;
@@ -162,7 +173,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     const uint32_t drain_bar = bar_base + 8u * (2 * STAGES + 4);
     auto rfull_bar = [&](int s) { return bar_base + 8u * (2 * STAGES + 5 + s); };
     auto rempty_bar = [&](int s) { return bar_base + 8u * (2 * STAGES + 8 + s); };
-    uint8_t* misc = smem + C::BAR_OFF + 8 * (2 * STAGES + 11);
+    // CTA pair, quantized weights: the peer's dequant warps arrive on a local barrier per stage and
+    // one thread of the peer ("announcer") forwards each completed stage to the leader's full barrier
+    // with a single cluster-scope arrive, so no dequant warp waits on a remote arrive
+    auto pfull_bar = [&](int s) { return bar_base + 8u * (2 * STAGES + 11 + s); };
+    uint8_t* misc = smem + C::BAR_OFF + 8 * (3 * STAGES + 11);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
 
@@ -183,14 +198,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            mbar_init(full_bar(s), C::QUANT ? 1 + (PAIR ? 2 : 1) * DEQ_WARPS : 2);
+            // quantized: the A TMA's expect_tx arrive + the local dequant warps (+ the peer's announcer)
+            mbar_init(full_bar(s), C::QUANT ? 1 + DEQ_WARPS + (PAIR ? 1 : 0) : 2);
             mbar_init(empty_bar(s), 1);
+            if (PAIR && C::QUANT) mbar_init(pfull_bar(s), DEQ_WARPS);
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(tfull_bar(a), 1);
             mbar_init(tempty_bar(a), PAIR ? 8 : 4);
         }
-        for (int s = 0; s < RC::STAGES; s++) {
+        for (int s = 0; s < C::RAW_STAGES; s++) {
             mbar_init(rfull_bar(s), 1);
             mbar_init(rempty_bar(s), DEQ_WARPS);
         }
@@ -320,6 +337,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                 } else {
                     mbar_arrive_expect_tx(full_bar(stage), C::A_BYTES);
                     tma_load_2d(sa, &tmA, full_bar(stage), kb * GEMM_BK, uc.t0);
+                    if constexpr (C::WIDE)   // the second 256-token half of the tile
+                        tma_load_2d(sa + C::A_BYTES / 2, &tmA, full_bar(stage), kb * GEMM_BK, uc.t0 + C::A_BOX);
                 }
                 issued_mask |= 1u << stage;
                 issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
@@ -370,11 +389,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                         if constexpr (WT == WT_Q6_K) tma_load_2d(dst + RC::A_BYTES, &tmD, rfull_bar(rs), uc.wrow0, sb);
                         issued_mask |= 1u << rs;
                         issued_par = (issued_par & ~(1u << rs)) | (rph << rs);
-                        if (++rs == RC::STAGES) { rs = 0; rph ^= 1u; }
+                        if (++rs == C::RAW_STAGES) { rs = 0; rph ^= 1u; }
                     }
                 }
                 if (!ok) {
-                    for (int s2 = 0; s2 < RC::STAGES; s2++)
+                    for (int s2 = 0; s2 < C::RAW_STAGES; s2++)
                         if (((issued_mask >> s2) & 1u) && !mbar_drain(rfull_bar(s2), (issued_par >> s2) & 1u))
                             atomicCAS(args.err, 0, ERR_WAIT_DRAIN);
                 }
@@ -394,8 +413,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                 const UnitCoords uc = unit_coords(cur);
                 cur = uc.next;
                 const int kb0 = uc.kb0, kb1 = uc.kb1;
-                const int acc = lt & 1;
-                const uint32_t aphase = (uint32_t)(lt >> 1) & 1u;
+                const int acc = C::N_ACC == 1 ? 0 : (lt & 1);
+                const uint32_t aphase = C::N_ACC == 1 ? (uint32_t)lt & 1u : (uint32_t)(lt >> 1) & 1u;
                 if (!mbar_wait<PAIR>(tempty_bar(acc), aphase ^ 1u, args.err, ERR_WAIT_MMA, abort_flag)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BT);
@@ -411,6 +430,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                         else
                             mma_f16(d_tmem, wdesc0 + soff + 2 * k, adesc0 + soff + 2 * k, C::IDESC,
                                     (kb > kb0 || k > 0) ? 1u : 0u);
+                        if constexpr (C::WIDE)   // the same decoded weights against tokens 256..511
+                            mma_f16(d_tmem + (uint32_t)C::MMA_N, wdesc0 + soff + 2 * k,
+                                    adesc0 + soff + (uint64_t)((C::A_BYTES / 2) >> 4) + 2 * k, C::IDESC,
+                                    (kb > kb0 || k > 0) ? 1u : 0u);
                     }
                     if constexpr (PAIR) mma_commit_pair(empty_bar(stage));
                     else mma_commit(empty_bar(stage));
@@ -425,6 +448,25 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             else mma_commit(drain_bar);
             if (!mbar_drain(drain_bar, 0)) atomicCAS(args.err, 0, ERR_WAIT_DRAIN);
         }
+        if constexpr (PAIR && C::QUANT) {
+            if (lane == 0 && !leader) {
+                // the announcer: one cluster-scope arrive on the leader's full barrier per stage, after
+                // this CTA's eight dequant warps have filled it (their release at CTA scope, acquired
+                // here, is carried to the leader by this arrive's release at cluster scope)
+                int stage = 0;
+                uint32_t phase = 0;
+                bool ok = true;
+                for (int64_t cur = cursor0; cursor_ok(cur) && ok;) {
+                    const UnitCoords uc = unit_coords(cur);
+                    cur = uc.next;
+                    for (int kb = uc.kb0; kb < uc.kb1; kb++) {
+                        if (!mbar_wait(pfull_bar(stage), phase, args.err, ERR_WAIT_DEQUANT, abort_flag)) { ok = false; break; }
+                        mbar_arrive_cluster(mapa_shared(full_bar(stage), 0));
+                        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                    }
+                }
+            }
+        }
     } else if (warp >= W_EPI0 && warp < W_EPI0 + 4) {
         // ---------------- epilogue ----------------
         // Thread i of warp q owns TMEM lane (weight row) 32q + i and reads its tokens 16 at a time
@@ -437,11 +479,22 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         for (int64_t cur = cursor0; cursor_ok(cur); lt++) {
             const UnitCoords uc = unit_coords(cur);
             cur = uc.next;
-            const int acc = lt & 1;
-            const uint32_t aphase = (uint32_t)(lt >> 1) & 1u;
+            const int acc = C::N_ACC == 1 ? 0 : (lt & 1);
+            const uint32_t aphase = C::N_ACC == 1 ? (uint32_t)lt & 1u : (uint32_t)(lt >> 1) & 1u;
             const int ntok = min(BT, uc.t_end - uc.t0);  // tokens of this tile
             bool with_part = false;
-            if constexpr (!GROUPED) {
+            // WIDE: no idle accumulator to gather the partials into; the store loop adds them from
+            // global memory instead, once the lower-numbered CTAs have published them
+            bool part_direct = false;
+            if constexpr (C::WIDE) {
+                if (uc.finishes && uc.c_first < unit_id) {
+                    bool ok = true;
+                    for (int c = uc.c_first; c < unit_id && ok; c++)
+                        ok = wait_flag(args.flags + 4 * c + q, args.epoch, args.err, abort_flag);
+                    if (!ok) break;
+                    part_direct = true;
+                }
+            } else if constexpr (!GROUPED) {
                 if (uc.finishes && uc.c_first < unit_id) {
                     // A finisher sums the partials of the lower-numbered CTAs sharing its tile
                     // (they computed them first) into the idle accumulator while its own K range
@@ -536,19 +589,36 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     } else {
                         tmem_ld_wait();
                     }
-                    if (!GROUPED && args.n_dst == 0) {
-                        // the scaled [token][32 rows] box, then one TMA store of it (rows past
-                        // M and columns past N are clipped by the tensor map)
-                        if (lane == 0) bulk_wait_read_all();     // the previous box has been read
-                        __syncwarp();
+                    if constexpr (C::WIDE) {
+                        if (part_direct) {
+                            const float* p = args.partials + (size_t)uc.c_first * (BT * GEMM_BN) +
+                                             (size_t)c0 * GEMM_BN + 32 * q + lane;
+                            for (int c = uc.c_first; c < unit_id; c++, p += BT * GEMM_BN) {
 #pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            es[j * 32 + lane] = __uint_as_float(r[j]) * __shfl_sync(0xffffffffu, sg, j);
-                        fence_proxy_async_smem();
-                        __syncwarp();
-                        if (lane == 0) {
-                            tma_store_2d(&tmO, es_addr, uc.n0 + 32 * q, uc.t0 + c0);
-                            bulk_commit();
+                                for (int j = 0; j < 32; j++)
+                                    r[j] = __float_as_uint(__uint_as_float(r[j]) + __ldcg(p + j * GEMM_BN));
+                            }
+                        }
+                    }
+                    if (!GROUPED && args.n_dst == 0) {
+                        // the scaled [token][32 rows] values as four [8 tokens][32 rows] boxes, each
+                        // written by one TMA store (rows past M and columns past N are clipped by the
+                        // tensor map); four box buffers per warp, so three stores are still reading
+                        // shared memory while the next box is written
+#pragma unroll
+                        for (int sbx = 0; sbx < 4; sbx++) {
+                            if (lane == 0) bulk_wait_read<3>();   // this buffer's previous store has read it
+                            __syncwarp();
+#pragma unroll
+                            for (int j = 0; j < 8; j++)
+                                es[sbx * 256 + j * 32 + lane] =
+                                    __uint_as_float(r[8 * sbx + j]) * __shfl_sync(0xffffffffu, sg, 8 * sbx + j);
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) {
+                                tma_store_2d(&tmO, es_addr + 1024u * sbx, uc.n0 + 32 * q, uc.t0 + c0 + 8 * sbx);
+                                bulk_commit();
+                            }
                         }
                     } else {
                         // scattered rows (grouped) or several destinations (split weight rows): a
@@ -634,12 +704,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                                          o[4 * c + 2], o[4 * c + 3]);
                         fence_proxy_async_smem();
                         __syncwarp();
-                        if (lane == 0) arrive_leader(full_bar(stage));
+                        if (lane == 0) mbar_arrive(PAIR && !leader ? pfull_bar(stage) : full_bar(stage));
                         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(rempty_bar(rs));
-                    if (++rs == RC::STAGES) { rs = 0; rph ^= 1u; }
+                    if (++rs == C::RAW_STAGES) { rs = 0; rph ^= 1u; }
                 }
             }
         }

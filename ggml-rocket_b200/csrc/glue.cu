@@ -269,8 +269,14 @@ __global__ void __launch_bounds__(SM_THREADS) soft_max_kernel(const char* __rest
 // memory, ties broken by the smaller index (ggml's std::sort leaves the order of ties open) -----
 constexpr int AS_MAX = 1024;
 
+// A total order, so the output is always a permutation of [0, n): padding entries (index >= AS_MAX)
+// after every row entry, NaNs after every number (in either direction), ties by index.
 __device__ __forceinline__ bool as_before(float va, int ia, float vb, int ib, bool desc) {
-    if (va != vb) return desc ? va > vb : va < vb;
+    const bool pa = ia >= AS_MAX, pb = ib >= AS_MAX;
+    if (pa != pb) return pb;
+    const bool na = isnan(va), nb = isnan(vb);
+    if (pa || na != nb) return pa ? ia < ib : nb;
+    if (!na && va != vb) return desc ? va > vb : va < vb;
     return ia < ib;
 }
 

@@ -46,6 +46,9 @@ int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, cons
                      int64_t M, float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err,
                      cudaStream_t st, float* const* dst_bases = nullptr, int n_dst = 0, int64_t col0 = 0);
 size_t mul_mat_workspace(int wtype, int64_t M, int64_t N, int64_t K);
+// Where, inside mul_mat_impl's workspace, the stream-K flags of that op live (byte offset and
+// length; length 0 when the plan shares no output tile between CTAs).
+void mul_mat_flags_range(int wtype, int64_t M, int64_t N, int64_t K, size_t* offset, size_t* bytes);
 int act_pack_impl(const float* src1, int64_t lda, int64_t M, int64_t K, __half* a16, float* scales, cudaStream_t st);
 int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int64_t n_expert, const __half* a16,
                       const float* scales, int64_t rows, int bt, const int32_t* off, const int32_t* tile_start,

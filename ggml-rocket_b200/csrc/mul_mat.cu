@@ -231,13 +231,14 @@ bool make_tmap_2d_u16(CUtensorMap* map, const void* base, uint64_t rows, uint64_
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// The f32 output [rows, cols] (cols innermost, row pitch in bytes) as 32 x 32 store boxes.
+// The f32 output [rows, cols] (cols innermost, row pitch in bytes) as store boxes of 8 rows
+// (tokens) x 32 columns (weight rows).
 static bool make_tmap_2d_f32_out(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols, uint64_t pitch_bytes) {
     EncodeTiledFn fn = get_encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {pitch_bytes};
-    cuuint32_t box[2] = {32, 32};
+    cuuint32_t box[2] = {32, 8};
     cuuint32_t estr[2] = {1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -264,7 +265,8 @@ static int pair_knob() {
     return v;
 }
 
-// B200_GEMM_TILE: unset = the cost model's token tile; 32 / 64 / 128 / 256 = that tile.
+// B200_GEMM_TILE: unset = the cost model's token tile; 32 / 64 / 128 / 256 = that tile; 512 = the
+// wide unit (Q4_K).
 static int tile_knob() {
     static const int v = [] {
         const char* e = getenv("B200_GEMM_TILE");
@@ -295,17 +297,19 @@ static GemmPlan plan_gemm_knobs(int64_t M, int64_t N, int64_t K, int sms, int wt
     const int tile_g = (nkb + gran - 1) / gran;
     GemmPlan best{};
     double best_t = 1e30;
-    const int bts[4] = {32, 64, 128, 256};
+    // 512: the wide unit (two 256-token halves on one decoded weight stage), Q4_K only
+    const int bts[5] = {32, 64, 128, 256, 512};
+    const int n_bts = wtype == WT_Q4_K ? 5 : 4;
     const bool pair_default = !quant && M >= 1024;
     for (int pair = 0; pair < 2; pair++) {
         if (pair && (pair_knob() == 0 || (pair_knob() < 0 && !pair_default))) continue;
         if (!pair && (pair_knob() == 1 || (pair_knob() < 0 && pair_default)) && M > 64) continue;
         const int tile_n = pair ? 2 * GEMM_BN : GEMM_BN;
         const int ntn = (int)((N + tile_n - 1) / tile_n);
-        for (int bi = 0; bi < 4; bi++) {
+        for (int bi = 0; bi < n_bts; bi++) {
             const int bt = bts[bi];
             if (bi > 0 && bts[bi - 1] >= M) break;      // a smaller tile already covers M
-            if (pair && bt < 128) continue;              // each CTA of a pair stages >= 64 tokens
+            if (pair && (bt < 128 || bt > 256)) continue;   // each CTA of a pair stages 64..128 tokens
             if (tile > 0 && bt != tile) continue;
             const int ntt = (int)((M + bt - 1) / bt);
             const int64_t tiles = (int64_t)ntn * ntt;
@@ -313,27 +317,33 @@ static GemmPlan plan_gemm_knobs(int64_t M, int64_t N, int64_t K, int sms, int wt
             const int per_unit = pair ? 2 : 1;           // CTAs per work unit
             int units = (int)(total_g < sms / per_unit ? total_g : sms / per_unit);
             // per SM and 64-wide K block: tensor-core clocks (128 x BT x 64 MACs at 4096 MAC/clk),
-            // the dequant warps' hand-off of 8192 decoded weights (measured: ~800 clocks a block
-            // whatever the token tile), and shared-memory bytes (TMA writes + MMA reads,
-            // 128 B/clk): the activation tile is halved in a pair
+            // the dequant warps' decode and hand-off of 8192 weights, and shared-memory bytes (TMA
+            // writes + MMA reads, 128 B/clk): the activation tile is halved in a pair. The quantized
+            // block times are measured on B200 at M = 512 (clock64 spans of the dequant warps, and
+            // whole-launch times where the tile's epilogue adds to them): ~820-900 clocks at
+            // BT <= 128, ~940 at 256, ~1450-1600 for the wide 512-token unit
             const double mma = bt < 64 ? 128.0 : 2.0 * bt;
-            const double decode = quant ? 800.0 : 0.0;
+            const double decode = !quant ? 0.0 : bt <= 128 ? 900.0 : bt == 256 ? 940.0 : 1600.0;
             const double a_bytes = (pair ? bt / 2 : bt) * 128.0 * 2.0;
             const double w_bytes = quant ? 41984.0 : 32768.0;
             const double feed = (a_bytes + w_bytes) / 128.0;
             double per_kb = mma > decode ? mma : decode;
             if (feed > per_kb) per_kb = feed;
             per_kb += 16.0;
+            // a shared tile's partials: each piece but the last is written by its CTA, and the
+            // finisher reads them all back after its own range (128 x BT f32 each at ~20 B/clk per
+            // SM, measured): pieces_sk is how many CTAs share a tile under stream-K
+            const int64_t run_sk = total_g / units > 0 ? total_g / units : 1;
+            const double pieces_sk = (double)((tile_g - 1) / run_sk + 2 < tile_g ? (tile_g - 1) / run_sk + 2 : tile_g);
+            const double part_sk = 25.6 * bt * pieces_sk;
             // whole tiles, one per CTA, when they fit in one wave: no partials
             const bool whole = tiles <= units && streamk_knob() != 2 && (streamk_knob() == 0 || (double)nkb * per_kb + 800.0 <
-                (double)tiles * nkb * per_kb / units + 800.0 * (1.0 + (double)tiles / units) + 51.2 * bt);
+                (double)tiles * nkb * per_kb / units + 800.0 * (1.0 + (double)tiles / units) + part_sk);
             if (whole) units = (int)tiles;
             const double items = 1.0 + (double)tiles / units;
             const bool shared = total_g % units != 0 || tiles % units != 0;
             double t = (double)tiles * nkb * per_kb / units + 800.0 * items;
-            // a shared tile's partials: written by one CTA, read back by its finisher (128 x BT
-            // f32 each way at ~20 B/clk per SM, measured)
-            if (shared) t += 51.2 * bt;
+            if (shared) t += part_sk;
             if (t < best_t * 0.97) {
                 best_t = t;
                 best.bt = bt;
@@ -439,6 +449,9 @@ static cudaError_t launch_gemm_bt(int bt, bool pair, const CUtensorMap& tmA, con
                 default: return cudaErrorInvalidValue;
             }
         }
+    }
+    if constexpr (!GROUPED && WT == WT_Q4_K) {
+        if (bt == 512) return launch_gemm_t<512, WT, false, false>(tmA, tmW, tmD, tmO, a, grid, st);
     }
     switch (bt) {
         case 32: return launch_gemm_t<32, WT, GROUPED, false>(tmA, tmW, tmD, tmO, a, grid, st);
@@ -576,8 +589,9 @@ int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, cons
     if (sk_bytes && (!workspace || workspace_bytes < sk_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
         return B200_E_WORKSPACE;
     CUtensorMap tmA, tmW, tmD;
-    // a CTA of a pair stages half of the token tile
-    if (!make_tmap_2d_f16(&tmA, a16, (uint64_t)M, (uint64_t)K, (uint64_t)K, (uint32_t)(p.pair ? p.bt / 2 : p.bt), GEMM_BK))
+    // the activation box: a CTA of a pair stages half of the token tile; the wide tile two boxes
+    const uint32_t a_box = (uint32_t)(p.pair ? p.bt / 2 : (p.bt > 256 ? 256 : p.bt));
+    if (!make_tmap_2d_f16(&tmA, a16, (uint64_t)M, (uint64_t)K, (uint64_t)K, a_box, GEMM_BK))
         return B200_E_CUDA;
     GemmArgs a{};
     if (!setup_weight_maps(wtype, w_packed, N, K, tmW, tmD, tmA)) return B200_E_CUDA;
@@ -633,6 +647,14 @@ int mul_mat_impl(int wtype, const void* w_packed, int64_t N, int64_t K, const fl
 size_t mul_mat_workspace(int wtype, int64_t M, int64_t N, int64_t K) {
     const GemmPlan p = plan_gemm(M, N, K, device_sm_count(), wtype);
     return mm_workspace_layout(M, N, K, p).total;
+}
+
+void mul_mat_flags_range(int wtype, int64_t M, int64_t N, int64_t K, size_t* offset, size_t* bytes) {
+    const GemmPlan p = plan_gemm(M, N, K, device_sm_count(), wtype);
+    const MulMatWorkspace wl = mm_workspace_layout(M, N, K, p);
+    const size_t sk = streamk_bytes(p);
+    *offset = sk ? wl.part_off + streamk_partials_bytes(p) : 0;
+    *bytes = sk ? sk - streamk_partials_bytes(p) : 0;
 }
 
 int weight_pack_impl(int type, const void* src, int64_t N, int64_t K, void* dst, cudaStream_t st) {

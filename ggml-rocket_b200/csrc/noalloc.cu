@@ -11,7 +11,11 @@
 // the process exits. Its first 256 bytes are this entry point's device error word (used when
 // the caller passes no dev_err of its own); the rest is the workspace. Calls share the array and
 // it keeps the last call's contents, so two calls that overlap on the GPU (different streams,
-// or different host threads on the same device) race: the caller must order them.
+// or different host threads on the same device) race: the caller must order them. The only
+// part of that carried-over content a call reads is the stream-K flag block (when CTAs share an
+// output tile), so every call clears it on its stream before the GEMM runs: a finisher then
+// never mistakes a flag left by an earlier call for this call's. The error word is not
+// cleared per call: the first error since the last b200_mul_mat_noalloc_error stays there.
 #include <cstdint>
 #include <mutex>
 
@@ -62,14 +66,14 @@ int b200_mul_mat_noalloc(int wtype, const void* w_packed, int64_t N, int64_t K, 
     const int rc = scratch_address(&base);
     if (rc != B200_OK) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    int* err = dev_err;
-    if (!err) {
-        err = static_cast<int*>(base);
-        if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess) return B200_E_CUDA;   // starts at zero
-    }
-    return b200::mul_mat_impl(wtype, w_packed, N, K, src1, lda, M, dst, ldd,
-                              static_cast<unsigned char*>(base) + NOALLOC_ERR_BYTES,
-                              NOALLOC_SCRATCH_BYTES - NOALLOC_ERR_BYTES, err, st);
+    // the error word lives in the array (zero at load, cleared by b200_mul_mat_noalloc_error)
+    int* err = dev_err ? dev_err : static_cast<int*>(base);
+    unsigned char* ws = static_cast<unsigned char*>(base) + NOALLOC_ERR_BYTES;
+    size_t flags_off = 0, flags_bytes = 0;
+    b200::mul_mat_flags_range(wtype, M, N, K, &flags_off, &flags_bytes);
+    if (flags_bytes && cudaMemsetAsync(ws + flags_off, 0, flags_bytes, st) != cudaSuccess) return B200_E_CUDA;
+    return b200::mul_mat_impl(wtype, w_packed, N, K, src1, lda, M, dst, ldd, ws, NOALLOC_SCRATCH_BYTES - NOALLOC_ERR_BYTES,
+                              err, st);
 }
 
 int b200_mul_mat_noalloc_error(void* stream, int* host_err) {

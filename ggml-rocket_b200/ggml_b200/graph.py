@@ -37,10 +37,11 @@ def _contig_nb(ttype, ne):
 
 
 def llama_layer(T, E=4096, F=14336, H=32, HK=8, D=128, n_kv=None, wtype=g.Q4_K, eps=1e-5, rope_base=500000.0,
-                alloc=None, il=0):
+                alloc=None, il=0, rope_mode=0):
     """One prefill layer of T tokens. n_kv: the KV cache length the attention reads (at least T,
     rounded up to 256 like llama.cpp's padded cache views); the new K/V rows are written at its
-    start. alloc: see the module docstring."""
+    start. rope_mode: 0 (normal, what llama.cpp uses for the Llama architecture) or 2 (neox).
+    alloc: see the module docstring."""
     n_kv = n_kv or max(256, (T + 255) // 256 * 256)
     L = Layer()
 
@@ -80,7 +81,7 @@ def llama_layer(T, E=4096, F=14336, H=32, HK=8, D=128, n_kv=None, wtype=g.Q4_K, 
     q = node(new(g.F32, [E, T], g.OP_MUL_MAT, [weight("attn_q", [E, E]), an], "Qcur"))
     k = node(new(g.F32, [D * HK, T], g.OP_MUL_MAT, [weight("attn_k", [E, D * HK]), an], "Kcur"))
     v = node(new(g.F32, [D * HK, T], g.OP_MUL_MAT, [weight("attn_v", [E, D * HK]), an], "Vcur"))
-    rope_params = [0, D, 2, 0, 8192, rope_base, 1.0, 0.0, 1.0, 32.0, 1.0]
+    rope_params = [0, D, rope_mode, 0, 8192, rope_base, 1.0, 0.0, 1.0, 32.0, 1.0]
     q3 = node(new(g.F32, [D, H, T], g.OP_RESHAPE, [q], "Qcur_3d", view_of=q))
     k3 = node(new(g.F32, [D, HK, T], g.OP_RESHAPE, [k], "Kcur_3d", view_of=k))
     qr = node(new(g.F32, [D, H, T], g.OP_ROPE, [q3, pos], "Qcur_rope", op_params=rope_params))

@@ -97,10 +97,13 @@ int    b200_mul_mat_plan(int wtype, int64_t M, int64_t N, int64_t K, int * token
  * file-scope device array that every GPU loading this library holds until exit. The caller
  * passes only inputs and outputs. An op whose workspace (b200_mul_mat_workspace_size) exceeds
  * b200_mul_mat_noalloc_max_workspace() returns B200_E_TOO_LARGE. The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress) and should come before any stream
- * capture. dev_err may be NULL: the device error word then lives in the array and
- * b200_mul_mat_noalloc_error() synchronises the stream, returns it and clears it. Calls share the
- * array, so calls that overlap on the GPU race; the caller must order them. */
+ * looks up the array's device address (cudaGetSymbolAddress), a set-up step, so make that first
+ * call before any stream capture begins. dev_err may be NULL: the device error word then lives in
+ * the array, keeps the first error any call records, and b200_mul_mat_noalloc_error()
+ * synchronises the stream, returns it and clears it. Every call clears the part of the array that
+ * would otherwise carry state into it (the flags CTAs use to hand partial tiles to each other)
+ * before its kernels run. Calls share the array, so calls that overlap on the GPU race; the caller
+ * must order them. */
 size_t b200_mul_mat_noalloc_max_workspace(void);
 int    b200_mul_mat_noalloc(int wtype, const void * w_packed, int64_t N, int64_t K,
                             const float * src1, int64_t lda, int64_t M, float * dst, int64_t ldd,

@@ -52,8 +52,12 @@ def _run_both(torch, g, wtype, N, K, M, seed):
 def test_noalloc_matches_mul_mat_twice(cuda):
     import torch
     import ggml_b200 as g
-    # two calls in a row with different shapes and formats
-    for wtype, N, K, M, seed in ((g.Q4_K, 1024, 4096, 512, 1), (g.F16, 768, 2048, 96, 2)):
+    # calls in a row with different shapes and formats; the first and the last share output tiles
+    # between CTAs (stream-K partials and their flags, the part of the array that carries state
+    # from one call to the next), so the last call runs on flags the first one left behind
+    cases = ((g.Q4_K, 4096, 4096, 128, 1), (g.F16, 768, 2048, 96, 2), (g.Q4_K, 4096, 4096, 128, 3))
+    assert g.mul_mat_plan(128, 4096, 4096, g.Q4_K)["splits"] > 1
+    for wtype, N, K, M, seed in cases:
         got, want = _run_both(torch, g, wtype, N, K, M, seed)
         assert np.all(np.isfinite(got))
         assert rel_err(got, want) <= TOL
