@@ -21,8 +21,10 @@
 #include <list>
 #include <map>
 #include <set>
+#include <condition_variable>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <unordered_map>
 #include <vector>
 
@@ -340,18 +342,47 @@ struct CachedWeight {
     uintptr_t src_lo = 0, src_hi = 0;   // device bytes it was packed from (on-device weights)
 };
 
+// Host bytes whose current value, written by an earlier op of the same graph, is still on the
+// device in the staging arena: a later op reading them uses the device copy directly.
+struct FwdRange {
+    uintptr_t lo, hi;
+    char* dev;
+};
+// A staged output on its way back into pageable host memory (copied out of pinned staging once
+// the device-to-host copy has completed).
+struct HostCopyBack {
+    void* dst;
+    const void* pinned;
+    size_t n;
+};
+
 struct b200_backend {
     uint32_t magic = 0xB2000B20u;
     int device = 0;
     int n_gpus = 1;
     bool dev_ready = false;
+    // compute, host-to-device and device-to-host streams: an op's input copies, its kernels and its
+    // output copies are ordered by events, so one op's copies overlap its neighbours' kernels
     cudaStream_t stream = nullptr;
+    cudaStream_t s_in = nullptr, s_out = nullptr;
     int* dev_err = nullptr;
     // grow-only device scratch arenas
     void* ws = nullptr;
     size_t ws_bytes = 0;
-    void* io = nullptr;       // staging for host activations / outputs / attention inputs
-    size_t io_bytes = 0;
+    // staging of host tensors, bump-allocated through one graph: device arena and pinned host
+    // arena (for tensors in pageable memory); both are reset when the graph's copies have drained
+    void* io = nullptr;
+    size_t io_bytes = 0, io_off = 0;
+    void* pin = nullptr;
+    size_t pin_bytes = 0, pin_off = 0;
+    bool in_pending = false;                 // input copies queued on s_in for the current op
+    std::vector<FwdRange> fwd;               // host ranges whose newest bytes sit in the device arena
+    std::vector<std::pair<uintptr_t, uintptr_t>> dirty;   // every host range an op of the graph wrote
+    std::vector<HostCopyBack> copy_back;
+    std::vector<cudaEvent_t> events;
+    size_t ev_next = 0;
+    void* wstage = nullptr;                  // native weight bytes on their way to the packer
+    size_t wstage_bytes = 0;
     // weight cache
     std::unordered_map<std::string, CachedWeight> cache;
     std::list<std::string> lru;
@@ -395,6 +426,8 @@ bool ensure_device(b200_backend* b) {
     if (b->dev_ready) return true;
     if (!cuda_ok(cudaSetDevice(b->device), "cudaSetDevice")) return false;
     if (!cuda_ok(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking), "cudaStreamCreate")) return false;
+    if (!cuda_ok(cudaStreamCreateWithFlags(&b->s_in, cudaStreamNonBlocking), "cudaStreamCreate(in)")) return false;
+    if (!cuda_ok(cudaStreamCreateWithFlags(&b->s_out, cudaStreamNonBlocking), "cudaStreamCreate(out)")) return false;
     if (!cuda_ok(cudaMalloc(&b->dev_err, 256), "cudaMalloc(err)")) return false;
     if (!cuda_ok(cudaMemsetAsync(b->dev_err, 0, 256, b->stream), "cudaMemset(err)")) return false;
     b->cache_budget = weight_budget_bytes(b->device);
@@ -468,28 +501,20 @@ void* pack_weight(b200_backend* b, const std::string& key, int type, const void*
     if (!key.empty()) evict_until(b, packed);
     void* dst = nullptr;
     if (cudaMalloc(&dst, packed) != cudaSuccess) return nullptr;
-    // stage the native bytes on the device
+    // stage the native bytes on the device, in a grow-only buffer the packer reads on the compute
+    // stream (the next upload reuses it in stream order: no allocation or synchronisation per weight)
     const void* dsrc = src;
-    void* stage = nullptr;
     if (!src_on_device) {
-        if (cudaMalloc(&stage, native) != cudaSuccess) {
+        if (!grow(&b->wstage, &b->wstage_bytes, native, b->stream) ||
+            cudaMemcpyAsync(b->wstage, src, native, cudaMemcpyHostToDevice, b->stream) != cudaSuccess) {
             cudaFree(dst);
             return nullptr;
         }
-        if (cudaMemcpyAsync(stage, src, native, cudaMemcpyHostToDevice, b->stream) != cudaSuccess) {
-            cudaFree(stage);
-            cudaFree(dst);
-            return nullptr;
-        }
-        dsrc = stage;
+        dsrc = b->wstage;
     }
     int rc;
     if (type == T_F32 || type == T_BF16) rc = b200_dequantize(type, dsrc, N, K, 1, dst, b->stream);
     else rc = b200_weight_pack(kt, dsrc, N, K, dst, b->stream);
-    if (stage) {
-        cudaStreamSynchronize(b->stream);
-        cudaFree(stage);
-    }
     if (rc != B200_OK) {
         cudaFree(dst);
         return nullptr;
@@ -513,23 +538,288 @@ void* pack_weight(b200_backend* b, const std::string& key, int type, const void*
     return dst;
 }
 
-// Device pointer holding a tensor's bytes: its own when on the device, else a staged copy in
-// the io arena at *io_off (advanced).
-const void* stage_in(b200_backend* b, const b200_tensor* t, size_t* io_off, bool* ok) {
-    if (t->on_device) return t->data;
-    const size_t n = nbytes(t);
-    const size_t off = (*io_off + 255) & ~(size_t)255;
-    if (off + n > b->io_bytes) {
-        *ok = false;
-        return nullptr;
+// ---- host copies between pageable memory and the pinned arena ----------------------------------
+// A pageable tensor of several MB copied by one thread runs at a fraction of the host link's speed,
+// so large copies are split over a small process-wide pool of threads.
+class CopyPool {
+public:
+    static CopyPool& get() {
+        static CopyPool pool;
+        return pool;
     }
-    void* d = static_cast<char*>(b->io) + off;
-    if (cudaMemcpyAsync(d, t->data, n, cudaMemcpyHostToDevice, b->stream) != cudaSuccess) *ok = false;
-    *io_off = off + n;
+    void memcpy_par(void* dst, const void* src, size_t n) {
+        const size_t CHUNK = (size_t)1 << 20;
+        if (n < 4 * CHUNK || workers_.empty()) {
+            memcpy(dst, src, n);
+            return;
+        }
+        std::lock_guard<std::mutex> serial(run_mu_);
+        const size_t parts = workers_.size() + 1;
+        const size_t per = ((n + parts - 1) / parts + 4095) & ~(size_t)4095;
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            dst_ = static_cast<char*>(dst);
+            src_ = static_cast<const char*>(src);
+            n_ = n;
+            per_ = per;
+            remaining_ = (int)workers_.size();
+            gen_++;
+        }
+        cv_.notify_all();
+        part(0);   // the caller takes the first part
+        std::unique_lock<std::mutex> lk(mu_);
+        done_.wait(lk, [&] { return remaining_ == 0; });
+    }
+    ~CopyPool() {
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            stop_ = true;
+        }
+        cv_.notify_all();
+        for (auto& t : workers_) t.join();
+    }
+
+private:
+    CopyPool() {
+        const unsigned hw = std::thread::hardware_concurrency();
+        const int n = (int)std::min(7u, hw > 1 ? hw - 1 : 0u);
+        for (int i = 0; i < n; i++) workers_.emplace_back([this, i] { loop(i + 1); });
+    }
+    void part(size_t k) {
+        const size_t lo = k * per_;
+        if (lo < n_) memcpy(dst_ + lo, src_ + lo, std::min(per_, n_ - lo));
+    }
+    void loop(size_t k) {
+        uint64_t seen = 0;
+        for (;;) {
+            {
+                std::unique_lock<std::mutex> lk(mu_);
+                cv_.wait(lk, [&] { return stop_ || gen_ != seen; });
+                if (stop_) return;
+                seen = gen_;
+            }
+            part(k);
+            std::lock_guard<std::mutex> lk(mu_);
+            if (--remaining_ == 0) done_.notify_one();
+        }
+    }
+    std::vector<std::thread> workers_;
+    std::mutex mu_, run_mu_;
+    std::condition_variable cv_, done_;
+    char* dst_ = nullptr;
+    const char* src_ = nullptr;
+    size_t n_ = 0, per_ = 0;
+    int remaining_ = 0;
+    uint64_t gen_ = 0;
+    bool stop_ = false;
+};
+
+// ---- staging of host tensors ----------------------------------------------------------------
+// A graph's host tensors are copied in on s_in and out on s_out; the op's kernels run on the
+// compute stream between an event after its inputs and an event before its outputs. Tensors in
+// pinned host memory (the backend's host buffers, or memory a host registered) are copied
+// directly; pageable ones go through the pinned arena (memcpy on the host, then the copy; outputs
+// land in pinned memory and are copied into place when the graph's copies have drained). An
+// output written by one op and read by a later op of the same graph is read from its device
+// copy, with no round trip through the host.
+
+size_t staged_size(const b200_tensor* t) { return t->on_device ? 0 : ((nbytes(t) + 255) & ~(size_t)255); }
+
+cudaEvent_t next_event(b200_backend* b) {
+    if (b->ev_next == b->events.size()) {
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+        b->events.push_back(e);
+    }
+    return b->events[b->ev_next++];
+}
+
+bool host_is_pinned(const void* p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+// Wait for every queued copy and kernel, land the pageable outputs, and start both arenas over.
+bool io_drain(b200_backend* b) {
+    bool ok = cudaStreamSynchronize(b->s_in) == cudaSuccess;
+    ok = cudaStreamSynchronize(b->stream) == cudaSuccess && ok;
+    ok = cudaStreamSynchronize(b->s_out) == cudaSuccess && ok;
+    for (const HostCopyBack& c : b->copy_back) CopyPool::get().memcpy_par(c.dst, c.pinned, c.n);
+    b->copy_back.clear();
+    b->fwd.clear();
+    b->dirty.clear();
+    b->io_off = b->pin_off = 0;
+    b->ev_next = 0;
+    b->in_pending = false;
+    return ok;
+}
+
+bool grow_pinned(b200_backend* b, size_t need) {
+    if (b->pin_bytes >= need) return true;
+    if (b->pin) cudaFreeHost(b->pin);
+    b->pin = nullptr;
+    b->pin_bytes = 0;
+    const size_t sz = (std::max(need, (size_t)1 << 22) + 4095) & ~(size_t)4095;
+    if (cudaHostAlloc(&b->pin, sz, cudaHostAllocDefault) != cudaSuccess) return false;
+    b->pin_bytes = sz;
+    return true;
+}
+
+// Room for one op's staging (device bytes, pinned bytes), drained and grown first if the arenas
+// cannot hold it after what the graph has already staged. After this, the op's own allocations
+// never drain, so no copy queued for it can race a reuse of its region.
+// An arena that runs out is grown to what the graph has used so far plus this op, so that the
+// next graph of the same shape stages every op without draining in between (a drain serialises
+// the copies and kernels that the streams would otherwise overlap).
+bool io_reserve(b200_backend* b, size_t dev_need, size_t pin_need) {
+    if (b->io_off + dev_need <= b->io_bytes && b->pin_off + pin_need <= b->pin_bytes) return true;
+    const size_t dev_want = b->io_off + dev_need, pin_want = b->pin_off + pin_need;
+    if (!io_drain(b)) return false;
+    if (dev_want > b->io_bytes) {
+        if (b->io) cudaFree(b->io);
+        b->io = nullptr;
+        b->io_bytes = 0;
+        const size_t sz = (std::max(dev_want, (size_t)1 << 24) + 4095) & ~(size_t)4095;
+        if (cudaMalloc(&b->io, sz) != cudaSuccess) return false;
+        b->io_bytes = sz;
+    }
+    return grow_pinned(b, pin_want);
+}
+
+char* io_take(b200_backend* b, size_t n) {
+    char* p = static_cast<char*>(b->io) + b->io_off;
+    b->io_off += (n + 255) & ~(size_t)255;
+    return p;
+}
+char* pin_take(b200_backend* b, size_t n) {
+    char* p = static_cast<char*>(b->pin) + b->pin_off;
+    b->pin_off += (n + 255) & ~(size_t)255;
+    return p;
+}
+
+// The staging an op needs for these host tensors (inputs that an earlier op's output does not
+// already hold on the device, and outputs); pinned bytes are counted for pageable tensors.
+const FwdRange* fwd_find(const b200_backend* b, const b200_tensor* t) {
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(t->data), hi = lo + nbytes(t);
+    for (const FwdRange& f : b->fwd)
+        if (lo >= f.lo && hi <= f.hi) return &f;
+    return nullptr;
+}
+// Host bytes an op of this graph wrote (their copy back may still be in flight or pending).
+bool dirty_overlaps(const b200_backend* b, const b200_tensor* t) {
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(t->data), hi = lo + nbytes(t);
+    for (const auto& d : b->dirty)
+        if (hi > d.first && lo < d.second) return true;
+    return false;
+}
+
+struct OpStaging {
+    std::vector<const b200_tensor*> ins, outs;
+};
+
+bool op_reserve(b200_backend* b, const OpStaging& st) {
+    // an input that touches bytes an earlier op wrote, without lying inside one device copy of
+    // them: land everything first, then read the host
+    for (const b200_tensor* t : st.ins)
+        if (t && !t->on_device && !fwd_find(b, t) && dirty_overlaps(b, t)) {
+            if (!io_drain(b)) return false;
+            break;
+        }
+    size_t dev = 0, pin = 0;
+    for (const b200_tensor* t : st.ins) {
+        if (!t || t->on_device || fwd_find(b, t)) continue;
+        dev += staged_size(t);
+        if (!host_is_pinned(t->data)) pin += staged_size(t);
+    }
+    for (const b200_tensor* t : st.outs) {
+        if (!t || t->on_device) continue;
+        dev += staged_size(t);
+        if (!host_is_pinned(t->data)) pin += staged_size(t);
+    }
+    return io_reserve(b, dev, pin);
+}
+
+// Device pointer holding a tensor's bytes for the op being set up: its own on the device, the
+// device copy an earlier op of the graph left, or a fresh copy queued on s_in.
+const void* stage_in(b200_backend* b, const b200_tensor* t, bool* ok) {
+    if (t->on_device) return t->data;
+    if (const FwdRange* f = fwd_find(b, t)) return f->dev + (reinterpret_cast<uintptr_t>(t->data) - f->lo);
+    const size_t n = nbytes(t);
+    char* d = io_take(b, n);
+    const void* src = t->data;
+    if (!host_is_pinned(src)) {
+        // pageable: through the pinned arena in chunks, each chunk's copy to the device queued as soon
+        // as it is in pinned memory, so the host copy of the next chunk overlaps it
+        char* p = pin_take(b, n);
+        const size_t CH = (size_t)8 << 20;
+        for (size_t o = 0; o < n; o += CH) {
+            const size_t c = std::min(CH, n - o);
+            CopyPool::get().memcpy_par(p + o, static_cast<const char*>(src) + o, c);
+            if (cudaMemcpyAsync(d + o, p + o, c, cudaMemcpyHostToDevice, b->s_in) != cudaSuccess) *ok = false;
+        }
+        b->in_pending = true;
+        return d;
+    }
+    if (cudaMemcpyAsync(d, src, n, cudaMemcpyHostToDevice, b->s_in) != cudaSuccess) *ok = false;
+    b->in_pending = true;
     return d;
 }
 
-size_t staged_size(const b200_tensor* t) { return t->on_device ? 0 : ((nbytes(t) + 255) & ~(size_t)255); }
+// Device region for a host output of the op; read_in: the op writes only some of its bytes (a
+// strided view), so the current host bytes are copied in first.
+char* stage_out(b200_backend* b, const b200_tensor* t, bool read_in, bool* ok) {
+    if (t->on_device) return static_cast<char*>(t->data);
+    if (read_in) return const_cast<char*>(static_cast<const char*>(stage_in(b, t, ok)));
+    return io_take(b, nbytes(t));
+}
+
+// The op's kernels may start once its input copies have landed.
+bool op_inputs_ready(b200_backend* b) {
+    if (!b->in_pending) return true;
+    b->in_pending = false;
+    cudaEvent_t e = next_event(b);
+    return e && cudaEventRecord(e, b->s_in) == cudaSuccess && cudaStreamWaitEvent(b->stream, e, 0) == cudaSuccess;
+}
+
+// Queue the copies of the op's host outputs (dev: their device regions) after its kernels, and
+// remember where their bytes live until the graph's copies drain.
+bool op_outputs_done(b200_backend* b, const std::vector<const b200_tensor*>& outs, const std::vector<char*>& dev) {
+    bool any = false;
+    for (const b200_tensor* t : outs) any = any || !t->on_device;
+    if (!any) return true;
+    cudaEvent_t e = next_event(b);
+    if (!e || cudaEventRecord(e, b->stream) != cudaSuccess || cudaStreamWaitEvent(b->s_out, e, 0) != cudaSuccess)
+        return false;
+    for (size_t i = 0; i < outs.size(); i++) {
+        const b200_tensor* t = outs[i];
+        if (t->on_device) continue;
+        const size_t n = nbytes(t);
+        void* dst = t->data;
+        if (!host_is_pinned(dst)) {
+            char* p = pin_take(b, n);
+            b->copy_back.push_back({t->data, p, n});
+            dst = p;
+        }
+        if (cudaMemcpyAsync(dst, dev[i], n, cudaMemcpyDeviceToHost, b->s_out) != cudaSuccess) return false;
+        const uintptr_t lo = reinterpret_cast<uintptr_t>(t->data), hi = lo + n;
+        b->dirty.push_back({lo, hi});
+        // written in place inside an existing device copy (a strided output read in from it): that
+        // copy stays current; otherwise the new region replaces every copy it overlaps
+        bool in_place = false;
+        for (const FwdRange& f : b->fwd)
+            if (lo >= f.lo && hi <= f.hi && dev[i] == f.dev + (lo - f.lo)) in_place = true;
+        if (in_place) continue;
+        for (auto it = b->fwd.begin(); it != b->fwd.end();)
+            it = (hi > it->lo && lo < it->hi) ? b->fwd.erase(it) : it + 1;
+        b->fwd.push_back({lo, hi, dev[i]});
+    }
+    return true;
+}
+
 
 }  // namespace
 
@@ -728,21 +1018,30 @@ const char* route_name(int ktype) {
     }
 }
 
-bool check_dev_err(b200_backend* b, const char* what) {
+// The device error word, read once per graph after everything queued has drained (kernels record
+// bounded-wait give-ups, bad expert ids and bad row indices there; the first writer wins).
+bool graph_finish(b200_backend* b) {
     int h = 0;
-    if (cudaMemcpyAsync(&h, b->dev_err, sizeof(int), cudaMemcpyDeviceToHost, b->stream) != cudaSuccess ||
-        cudaStreamSynchronize(b->stream) != cudaSuccess) {
-        logf("E", "%s: CUDA error %s\n", what, cudaGetErrorString(cudaGetLastError()));
+    bool ok = cudaMemcpyAsync(&h, b->dev_err, sizeof(int), cudaMemcpyDeviceToHost, b->stream) == cudaSuccess;
+    ok = io_drain(b) && ok;
+    if (!ok) {
+        logf("E", "graph_compute: CUDA error %s\n", cudaGetErrorString(cudaGetLastError()));
         b->device_errors++;
         return false;
     }
-    if (h != 0) {
-        logf("E", "%s: device error word %d\n", what, h);
+    if (h == 0) return true;
+    if (h == B200_DEV_BAD_IDS) {
+        logf("E", "graph_compute: a MUL_MAT_ID expert id outside [0, n_expert)\n");
+    } else if (h == 6) {   // the kernels' bounds-check code (GET_ROWS row index outside the table)
+        logf("E", "graph_compute: a GET_ROWS row index outside its table\n");
         b->device_errors++;
-        cudaMemsetAsync(b->dev_err, 0, sizeof(int), b->stream);
-        return false;
+    } else {
+        logf("E", "graph_compute: device error word %d\n", h);
+        b->device_errors++;
     }
-    return true;
+    cudaMemsetAsync(b->dev_err, 0, sizeof(int), b->stream);
+    cudaStreamSynchronize(b->stream);
+    return false;
 }
 
 // MUL_MAT, including ggml's batch broadcast over dims 2/3 (ggml-rocket.cpp:4725-4750), and a
@@ -762,12 +1061,13 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
         wdev[g] = pack_weight(b, key, a->type, a->data, a->on_device != 0, N * a->ne[2] * a->ne[3], K, &kt[g]);
         if (!wdev[g]) return B200_E_CUDA;
     }
-    // staging: src1 (if host), A16 + scales, per-member dst (if host), GEMM workspace
-    size_t need_io = staged_size(src1);
-    size_t need_out = 0, need_ws = 0;
+    // staging: src1 and the members' dst when they are host tensors; workspace: A16 + scales + GEMM
+    OpStaging stg;
+    stg.ins.push_back(src1);
+    size_t need_ws = 0;
     for (int g = 0; g < ng; g++) {
         const b200_tensor* d = nodes[g];
-        if (!d->on_device) need_out += (nbytes(d) + 255) & ~(size_t)255;
+        stg.outs.push_back(d);
         need_ws = std::max(need_ws, b200_gemm_packed_workspace_size(kernel_wtype(d->src[0]->type), M, d->src[0]->ne[1], K));
     }
     // decode-size M (claimed only under B200_DECODE, Q4_K): the weight-streaming kernel per member
@@ -778,22 +1078,13 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
     const size_t a16_bytes = ((size_t)M * K * 2 + 255) & ~(size_t)255;
     const size_t sc_bytes = ((size_t)M * 4 + 255) & ~(size_t)255;
     need_ws = ((need_ws + 255) & ~(size_t)255) + a16_bytes + sc_bytes;
-    if (!grow(&b->io, &b->io_bytes, need_io + need_out, b->stream)) return B200_E_CUDA;
+    if (!op_reserve(b, stg)) return B200_E_CUDA;
     if (!grow(&b->ws, &b->ws_bytes, need_ws, b->stream)) return B200_E_CUDA;
-    size_t io_off = 0;
     bool ok = true;
-    const char* a_base = static_cast<const char*>(stage_in(b, src1, &io_off, &ok));
-    if (!ok) return B200_E_CUDA;
+    const char* a_base = static_cast<const char*>(stage_in(b, src1, &ok));
     std::vector<char*> d_base(ng);
-    for (int g = 0; g < ng; g++) {
-        if (nodes[g]->on_device) {
-            d_base[g] = static_cast<char*>(nodes[g]->data);
-        } else {
-            io_off = (io_off + 255) & ~(size_t)255;
-            d_base[g] = static_cast<char*>(b->io) + io_off;
-            io_off += nbytes(nodes[g]);
-        }
-    }
+    for (int g = 0; g < ng; g++) d_base[g] = stage_out(b, nodes[g], false, &ok);
+    if (!ok || !op_inputs_ready(b)) return B200_E_CUDA;
     char* ws = static_cast<char*>(b->ws);
     void* a16 = ws;
     float* scales = reinterpret_cast<float*>(ws + a16_bytes);
@@ -829,12 +1120,7 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
             }
         }
     }
-    for (int g = 0; g < ng; g++) {
-        if (!nodes[g]->on_device &&
-            cudaMemcpyAsync(nodes[g]->data, d_base[g], nbytes(nodes[g]), cudaMemcpyDeviceToHost, b->stream) != cudaSuccess)
-            return B200_E_CUDA;
-    }
-    if (!check_dev_err(b, "MUL_MAT")) return B200_E_DEVICE;
+    if (!op_outputs_done(b, stg.outs, d_base)) return B200_E_CUDA;
     if (decode) b->route_ops["decode"] += ng;
     else if (ng > 1) b->route_ops["fused"]++;
     else b->route_ops[route_name(kt[0])]++;
@@ -883,52 +1169,26 @@ int do_mul_mat_id_group(b200_backend* b, b200_tensor* const* ops, int ng) {
     size_t need_ws = 0;
     for (int g = 0; g < ng; g++)
         need_ws = std::max(need_ws, b200_mul_mat_id_workspace_size(K, Ns[g], n_expert, n_used, n_tokens));
-    size_t need_io = staged_size(bb) + staged_size(ids);
-    for (int g = 0; g < ng; g++)
-        if (!ops[g]->on_device) need_io += (nbytes(ops[g]) + 255) & ~(size_t)255;
-    if (!grow(&b->io, &b->io_bytes, need_io, b->stream)) return B200_E_CUDA;
+    OpStaging stg;
+    stg.ins = {bb, ids};
+    for (int g = 0; g < ng; g++) stg.outs.push_back(ops[g]);
+    if (!op_reserve(b, stg)) return B200_E_CUDA;
     if (!grow(&b->ws, &b->ws_bytes, need_ws, b->stream)) return B200_E_CUDA;
-    size_t io_off = 0;
     bool ok = true;
-    const void* bd = stage_in(b, bb, &io_off, &ok);
-    const void* idd = stage_in(b, ids, &io_off, &ok);
-    if (!ok) return B200_E_CUDA;
+    const void* bd = stage_in(b, bb, &ok);
+    const void* idd = stage_in(b, ids, &ok);
+    std::vector<char*> d_dev(ng);
     for (int g = 0; g < ng; g++) {
-        if (ops[g]->on_device) {
-            dsts[g] = static_cast<float*>(ops[g]->data);
-        } else {
-            io_off = (io_off + 255) & ~(size_t)255;
-            dsts[g] = reinterpret_cast<float*>(static_cast<char*>(b->io) + io_off);
-            io_off += nbytes(ops[g]);
-        }
+        d_dev[g] = stage_out(b, ops[g], false, &ok);
+        dsts[g] = reinterpret_cast<float*>(d_dev[g]);
     }
+    if (!ok || !op_inputs_ready(b)) return B200_E_CUDA;
     int rc = b200_mul_mat_id_group(ng, kt, w.data(), Ns.data(), K, n_expert, static_cast<const float*>(bd),
                                    (int64_t)bb->nb[1], (int64_t)bb->nb[2], ne11, static_cast<const int32_t*>(idd),
                                    (int64_t)ids->nb[0], (int64_t)ids->nb[1], n_used, n_tokens, dsts.data(), nb1.data(),
                                    nb2.data(), b->ws, b->ws_bytes, b->dev_err, b->stream);
     if (rc != B200_OK) return rc;
-    for (int g = 0; g < ng; g++) {
-        if (!ops[g]->on_device &&
-            cudaMemcpyAsync(ops[g]->data, dsts[g], nbytes(ops[g]), cudaMemcpyDeviceToHost, b->stream) != cudaSuccess)
-            return B200_E_CUDA;
-    }
-    int h = 0;
-    cudaMemcpyAsync(&h, b->dev_err, sizeof(int), cudaMemcpyDeviceToHost, b->stream);
-    if (cudaStreamSynchronize(b->stream) != cudaSuccess) {
-        b->device_errors++;
-        return B200_E_CUDA;
-    }
-    if (h == B200_DEV_BAD_IDS) {
-        cudaMemsetAsync(b->dev_err, 0, sizeof(int), b->stream);
-        logf("E", "MUL_MAT_ID: an expert id outside [0, %lld)\n", (long long)n_expert);
-        return B200_E_BAD_IDS;
-    }
-    if (h != 0) {
-        cudaMemsetAsync(b->dev_err, 0, sizeof(int), b->stream);
-        b->device_errors++;
-        logf("E", "MUL_MAT_ID: device error word %d\n", h);
-        return B200_E_DEVICE;
-    }
+    if (!op_outputs_done(b, stg.outs, d_dev)) return B200_E_CUDA;
     b->route_ops["moe"] += ng;
     if (ng > 1) b->route_ops["moe_grouped"] += ng;
     return B200_OK;
@@ -952,33 +1212,25 @@ int do_flash_attn(b200_backend* b, b200_tensor* op) {
     const int D = (int)q->ne[0], T = (int)q->ne[1], H = (int)q->ne[2];
     const int DV = (int)v->ne[0], KV = (int)k->ne[1], HK = (int)k->ne[2];
     const float scale = op_param_f32(op, 0), max_bias = op_param_f32(op, 1), softcap = op_param_f32(op, 2);
-    size_t need_io = staged_size(q) + staged_size(k) + staged_size(v) + (m ? staged_size(m) : 0) +
-                     (op->on_device ? 0 : ((nbytes(op) + 255) & ~(size_t)255));
+    OpStaging stg;
+    stg.ins = {q, k, v, m};
+    stg.outs = {op};
     const size_t need_ws = b200_flash_attn_workspace_size(D, DV, T, H, KV, HK);
-    if (!grow(&b->io, &b->io_bytes, need_io, b->stream)) return B200_E_CUDA;
+    if (!op_reserve(b, stg)) return B200_E_CUDA;
     if (!grow(&b->ws, &b->ws_bytes, need_ws, b->stream)) return B200_E_CUDA;
-    size_t io_off = 0;
     bool ok = true;
-    const void* qd = stage_in(b, q, &io_off, &ok);
-    const void* kd = stage_in(b, k, &io_off, &ok);
-    const void* vd = stage_in(b, v, &io_off, &ok);
-    const void* md = m ? stage_in(b, m, &io_off, &ok) : nullptr;
-    if (!ok) return B200_E_CUDA;
-    char* dd;
-    if (op->on_device) {
-        dd = static_cast<char*>(op->data);
-    } else {
-        io_off = (io_off + 255) & ~(size_t)255;
-        dd = static_cast<char*>(b->io) + io_off;
-    }
+    const void* qd = stage_in(b, q, &ok);
+    const void* kd = stage_in(b, k, &ok);
+    const void* vd = stage_in(b, v, &ok);
+    const void* md = m ? stage_in(b, m, &ok) : nullptr;
+    char* dd = stage_out(b, op, false, &ok);
+    if (!ok || !op_inputs_ready(b)) return B200_E_CUDA;
     int rc = b200_flash_attn_ext(static_cast<const float*>(qd), (int64_t)q->nb[1], (int64_t)q->nb[2], kd,
                                  (int64_t)k->nb[1], (int64_t)k->nb[2], vd, (int64_t)v->nb[1], (int64_t)v->nb[2], md,
                                  m ? (int64_t)m->nb[1] : 0, reinterpret_cast<float*>(dd), D, DV, T, H, KV, HK, scale,
                                  max_bias, softcap, b->ws, b->ws_bytes, b->dev_err, b->stream);
     if (rc != B200_OK) return rc;
-    if (!op->on_device && cudaMemcpyAsync(op->data, dd, nbytes(op), cudaMemcpyDeviceToHost, b->stream) != cudaSuccess)
-        return B200_E_CUDA;
-    if (!check_dev_err(b, "FLASH_ATTN_EXT")) return B200_E_DEVICE;
+    if (!op_outputs_done(b, stg.outs, {dd})) return B200_E_CUDA;
     b->route_ops["fa"]++;
     return B200_OK;
 }
@@ -990,24 +1242,19 @@ int do_glue(b200_backend* b, const b200_tensor* op) {
     const b200_tensor* a = op->src[0];
     // ggml's CPY carries its destination as src[1]: that one is written, not read
     const b200_tensor* c = op->op == B200_OP_CPY ? nullptr : op->src[1];
-    const bool out_host = !op->on_device;
-    const size_t need_io = staged_size(a) + (c ? staged_size(c) : 0) + 256 +
-                           (out_host ? ((nbytes(op) + 255) & ~(size_t)255) : 0);
-    if (!grow(&b->io, &b->io_bytes, need_io, b->stream)) return B200_E_CUDA;
-    size_t io_off = 0;
+    // a strided host output is read in first, so the bytes between its elements survive the copy
+    // back; it is then both an input and an output of the op
+    const bool read_in = !op->on_device && !is_contiguous(op);
+    OpStaging stg;
+    stg.ins = {a, c};
+    if (read_in) stg.ins.push_back(op);
+    stg.outs = {op};
+    if (!op_reserve(b, stg)) return B200_E_CUDA;
     bool ok = true;
-    const char* sa = static_cast<const char*>(stage_in(b, a, &io_off, &ok));
-    const char* sc = c ? static_cast<const char*>(stage_in(b, c, &io_off, &ok)) : nullptr;
-    if (!ok) return B200_E_CUDA;
-    char* d;
-    if (!out_host) {
-        d = static_cast<char*>(op->data);
-    } else {
-        io_off = (io_off + 255) & ~(size_t)255;
-        d = static_cast<char*>(b->io) + io_off;
-        if (!is_contiguous(op) && cudaMemcpyAsync(d, op->data, nbytes(op), cudaMemcpyHostToDevice, b->stream) != cudaSuccess)
-            return B200_E_CUDA;
-    }
+    const char* sa = static_cast<const char*>(stage_in(b, a, &ok));
+    const char* sc = c ? static_cast<const char*>(stage_in(b, c, &ok)) : nullptr;
+    char* d = stage_out(b, op, read_in, &ok);
+    if (!ok || !op_inputs_ready(b)) return B200_E_CUDA;
     float* df = reinterpret_cast<float*>(d);
     const cudaStream_t st = b->stream;
     int rc = B200_E_UNSUPPORTED;
@@ -1064,9 +1311,7 @@ int do_glue(b200_backend* b, const b200_tensor* op) {
             break;
     }
     if (rc != B200_OK) return rc;
-    if (out_host && cudaMemcpyAsync(op->data, d, nbytes(op), cudaMemcpyDeviceToHost, st) != cudaSuccess)
-        return B200_E_CUDA;
-    if (op->op == B200_OP_GET_ROWS && !check_dev_err(b, "GET_ROWS")) return B200_E_DEVICE;
+    if (!op_outputs_done(b, stg.outs, {d})) return B200_E_CUDA;
     b->route_ops["glue"]++;
     return B200_OK;
 }
@@ -1152,11 +1397,17 @@ void ggml_backend_b200_free(b200_backend_t b) {
         cudaSetDevice(b->device);
         cudaStreamSynchronize(b->stream);
         for (auto& kv : b->cache) cudaFree(kv.second.dev);
+        io_drain(b);
         for (void* p : b->transient) cudaFree(p);
         cudaFree(b->ws);
         cudaFree(b->io);
+        cudaFree(b->wstage);
+        if (b->pin) cudaFreeHost(b->pin);
+        for (cudaEvent_t e : b->events) cudaEventDestroy(e);
         cudaFree(b->dev_err);
         cudaStreamDestroy(b->stream);
+        cudaStreamDestroy(b->s_in);
+        cudaStreamDestroy(b->s_out);
     }
     b->magic = 0;
     delete b;
@@ -1341,7 +1592,7 @@ int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes,
                 status = B200_STATUS_FAILED;
         }
     }
-    if (cudaStreamSynchronize(b->stream) != cudaSuccess) status = B200_STATUS_FAILED;
+    if (!graph_finish(b)) status = B200_STATUS_FAILED;
     for (void* p : b->transient) cudaFree(p);
     b->transient.clear();
     return status;
