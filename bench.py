@@ -59,12 +59,13 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemm", "gemv", "moe", "fa", "glue"], default="gemm",
+    ap.add_argument("--workload", choices=["gemm", "gemv", "moe", "fa", "glue", "layer"], default="gemm",
                     help="gemm: the headline MUL_MAT sweep (default); gemv: the sweep's Q4_K weights at decode "
                          "size (M = --decode-m, b200_mul_mat_vec); moe: the MUL_MAT_ID layer of "
                          "BASELINE configs[3], expert-parallel over the ranks; fa: the FLASH_ATTN_EXT "
                          "prefill of configs[2]; glue: a layer's glue ops and the MoE router at the "
-                         "headline's prefill shapes (HBM-bound kernels, GB/s)")
+                         "headline's prefill shapes (HBM-bound kernels, GB/s); layer: configs[4]'s Llama-3-8B "
+                         "layer through graph_compute, prompt tokens/s")
     ap.add_argument("--layers", type=int, default=8,
                     help="gemm workload: layers (distinct weight copies) the sweep runs through per step")
     ap.add_argument("--decode-m", type=int, default=1,
@@ -1027,6 +1028,123 @@ def run_glue(args):
     return 0
 
 
+LAYER_DIMS = dict(E=4096, F=14336, H=32, HK=8, D=128, vocab=128256, layers=32, prompt=4096, ubatch=512)
+
+
+def run_layer(args):
+    """BASELINE configs[4]'s prefill, layer by layer: one Llama-3-8B-architecture layer (hidden 4096,
+    FFN 14336, 32 query / 8 KV heads of 128, RoPE theta 500000, Q4_K weights) as llama.cpp builds its
+    graph (ggml_b200.graph.llama_layer), every node claimed (B200_GLUE=1) and computed by
+    graph_compute on tensors in the backend's device buffer. The 4096-token prompt runs as 8 ubatches
+    of 512; ubatch i attends to 512 (i + 1) keys. Each ubatch's layer is timed (wall clock of the
+    synchronous graph_compute call, L2 flushed before each); prompt tokens/s = 4096 / (32 layers x the
+    sum over the 8 ubatches). Not included: the token embedding lookup, the final norm and the output
+    head (llama.cpp computes logits for the last token only by default)."""
+    os.environ.setdefault("B200_GLUE", "1")
+    os.environ.setdefault("B200_FLASH_ATTN_MIN_KV", "512")   # the first ubatch attends to 512 keys
+    import numpy as np
+    import torch
+    import ggml_b200 as g
+    from ggml_b200 import quants
+    from ggml_b200.graph import llama_layer
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    g.lib()
+    d = LAYER_DIMS
+    E, F, H, HK, D, T = d["E"], d["F"], d["H"], d["HK"], d["D"], d["ubatch"]
+    n_ub = d["prompt"] // T
+    rng = np.random.default_rng(0xB200)
+    # N(0, 0.02) Q4_K weights: one [F, E] block (q, k, v, o are slices of its rows) and one [E, F]
+    big = quants.quantize(g.Q4_K, rng.standard_normal((F, E), dtype=np.float32) * np.float32(0.02))
+    down = quants.quantize(g.Q4_K, rng.standard_normal((E, F), dtype=np.float32) * np.float32(0.02))
+    wsrc = {"attn_q": big[:E], "attn_k": big[E:E + D * HK], "attn_v": big[E + D * HK:E + 2 * D * HK],
+            "attn_output": big[F - E:], "ffn_gate": big, "ffn_up": big, "ffn_down": down}
+    be = g.Backend()
+    graphs = []
+    for i in range(n_ub):
+        n_kv = T * (i + 1)
+        # size a buffer for this graph: a dry run of the allocator
+        sizes = []
+
+        def count(n):
+            sizes.append(n)
+            return 0, True
+        llama_layer(T, E=E, F=F, H=H, HK=HK, D=D, n_kv=n_kv, wtype=g.Q4_K, rope_base=500000.0, il=i, alloc=count)
+        size = sum((n + 255) // 256 * 256 for n in sizes) + (1 << 20)
+        buf = g.DeviceBuffer(be, size)
+        top = [0]
+
+        def alloc(n, buf=buf, top=top):
+            off = top[0]
+            top[0] += (n + 255) // 256 * 256
+            return buf.base + off, True
+        L = llama_layer(T, E=E, F=F, H=H, HK=HK, D=D, n_kv=n_kv, wtype=g.Q4_K, rope_base=500000.0, il=i, alloc=alloc)
+        off = lambda t: t.data - buf.base   # noqa: E731
+        buf.set(off(L.inputs["x"]), rng.standard_normal((T, E), dtype=np.float32))
+        buf.set(off(L.inputs["pos"]), np.arange(n_kv - T, n_kv, dtype=np.int32))
+        Tp = L.inputs["mask"].ne[1]
+        mask = np.full((Tp, n_kv), -np.inf, np.float32)
+        for t in range(T):
+            mask[t, :n_kv - T + t + 1] = 0.0
+        buf.set(off(L.inputs["mask"]), mask.astype(np.float16).view(np.uint16))
+        for c in L.caches.values():
+            buf.set(off(c), (rng.standard_normal(c.ne[0] * c.ne[1], dtype=np.float32)).astype(np.float16).view(np.uint16))
+        for name, t in L.weights.items():
+            if t.type == g.F32:
+                buf.set(off(t), np.ones(t.ne[0], np.float32))
+            else:
+                buf.set(off(t), np.ascontiguousarray(wsrc[name]))
+        for nd in L.nodes:
+            if not g.supports_op(nd):
+                raise SystemExit(f"node {nd.name.decode()} not claimed")
+        graphs.append((n_kv, L, buf))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    sampler = ClockSampler(local)
+    per = {}
+    for n_kv, L, buf in graphs:
+        for _ in range(max(3, args.warmup)):
+            if be.graph_compute(L.nodes) != g.STATUS_SUCCESS:
+                raise SystemExit("graph_compute failed")
+    sampler.start()
+    for n_kv, L, buf in graphs:
+        ts = []
+        for _ in range(args.steps):
+            flush.zero_()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            if be.graph_compute(L.nodes) != g.STATUS_SUCCESS:
+                raise SystemExit("graph_compute failed")
+            ts.append(time.perf_counter() - t0)
+        per[n_kv] = statistics.median(ts)
+    clocks = sampler.stop()
+    layer_s = sum(per.values())
+    prefill_s = layer_s * d["layers"]
+    tps = d["prompt"] / prefill_s
+    # algorithmic FLOPs of one layer at ubatch T with n_kv keys: projections + causal attention
+    proj = 2.0 * T * E * (E + 2 * D * HK + E + 3 * F)
+    attn = lambda n_kv: 4.0 * H * D * (T * (n_kv - T) + T * (T + 1) / 2)   # noqa: E731
+    flops = sum(proj + attn(n) for n in per)
+    assert be.cpu_fallbacks() == 0 and be.device_errors() == 0
+    line = {"metric": "prompt tokens/sec, Llama-3-8B-architecture prefill (32 layers x one measured layer), "
+                      "4096-token prompt in 512-token ubatches", "value": tps, "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": layer_s * 1e3, "higher_is_better": True,
+            "scaling": "replicas only", "vs_baseline": None, "dtype": "f16 x Q4_K (fp32 accumulate)",
+            "data": "synthetic",
+            "config": {"workload": "BASELINE configs[4]: one layer per ubatch through graph_compute on device "
+                                   "buffers (B200_GLUE=1), all 8 ubatches of a 4096-token prompt",
+                       "layer_ms_per_ubatch_n_kv": {str(k): v * 1e3 for k, v in per.items()},
+                       "layer_tflops": flops / layer_s / 1e12,
+                       "excluded": "token embedding, final norm, output head (last-token logits only)",
+                       "timing": "wall clock of the synchronous graph_compute call, median of steps, L2 flushed",
+                       "routes": {r: be.route_ops(r) for r in ("q4_K", "fused", "fa", "glue")}},
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+    for _, _, buf in graphs:
+        buf.free()
+    be.close()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -1039,6 +1157,8 @@ def main():
         return run_gemv(args)
     if args.workload == "glue":
         return run_glue(args)
+    if args.workload == "layer":
+        return run_layer(args)
     if args.shard:
         return run_gemm_sharded(args)
     return run_ours(args)

@@ -29,6 +29,8 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 }
 
 int device_sm_count();
+// The give-up limit of waits on another GPU's flags (b200_set_peer_wait_limit_ns), nanoseconds.
+uint64_t peer_wait_limit_ns();
 bool make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
                       uint32_t box_rows, uint32_t box_cols);
 // A 2-D uint16 tensor map [rows, cols] (cols innermost, row pitch in bytes), box [box_rows,

@@ -100,7 +100,7 @@ __global__ void ep_signal_kernel(int* const* __restrict__ peer_flags, int slot_b
 // the epoch; copy their row counts and prefix into region (region[G] rows, region[G+1] pairs
 // total; region[G+2..] row prefixes) when `region` is given.
 __global__ void ep_wait_kernel(const int* __restrict__ flags, int slot_base, int G, int epoch, int32_t* __restrict__ region,
-                               int* err) {
+                               int* err, uint64_t limit_ns) {
     grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
     grid_dep_launch();
     const int s = threadIdx.x;
@@ -110,7 +110,7 @@ __global__ void ep_wait_kernel(const int* __restrict__ flags, int slot_base, int
         const uint64_t t0 = globaltimer();
         while (ld_acquire_sys(f) != epoch) {
             __nanosleep(256);
-            if (globaltimer() - t0 > B200_WAIT_LIMIT_NS) {
+            if (globaltimer() - t0 > limit_ns) {
                 atomicCAS(err, 0, ERR_WAIT_PEER);
                 ok = false;
                 break;
@@ -364,7 +364,7 @@ int b200_moe_ep_p2p_expert_group(int n_members, int wtype, const void* const* lo
     const int nb = (int)((rows_max + P2PC - 1) / P2PC);
     const int bt = ep_token_tile_public(pairs_hint > 0 ? pairs_hint : rows_max / 2, n_local);
     // 1. every source's rows have landed (their flags carry the counts)
-    launch_pdl(ep_wait_kernel, dim3(1), dim3(64), 0, st, flags, 0, G, epoch, region, dev_err);
+    launch_pdl(ep_wait_kernel, dim3(1), dim3(64), 0, st, flags, 0, G, epoch, region, dev_err, peer_wait_limit_ns());
     // 2. route the (row, slot) pairs by local expert
     const size_t hist_smem = (size_t)n_local * sizeof(int);
     if (hist_smem > 48 * 1024 &&
@@ -408,7 +408,7 @@ int b200_moe_ep_p2p_finish(const int* flags, int64_t n_ranks, int epoch, int* de
     using namespace b200;
     if (!flags || !dev_err || n_ranks <= 0 || n_ranks > 64) return B200_E_INVALID;
     launch_pdl(ep_wait_kernel, dim3(1), dim3(64), 0, static_cast<cudaStream_t>(stream), flags, (int)n_ranks,
-               (int)n_ranks, epoch, nullptr, dev_err);
+               (int)n_ranks, epoch, nullptr, dev_err, peer_wait_limit_ns());
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 

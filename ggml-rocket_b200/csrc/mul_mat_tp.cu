@@ -13,6 +13,7 @@
 // The per-element arithmetic is the single-GPU MUL_MAT's (the same activation pack, decode and
 // fp32 accumulation); only the K split of a tile (the stream-K plan over N_shard rows) can
 // differ from the single-GPU plan, which reorders the fp32 sums.
+#include <atomic>
 #include <cstdint>
 
 #include <cuda_runtime.h>
@@ -22,6 +23,11 @@
 #include "ptx.cuh"
 
 namespace b200 {
+
+// How long a kernel waits for another GPU's flag before it gives up (records ERR_WAIT_PEER in the
+// error word and returns): process-wide, set by b200_set_peer_wait_limit_ns, 2 s by default.
+static std::atomic<uint64_t> g_peer_wait_ns{B200_WAIT_LIMIT_NS};
+uint64_t peer_wait_limit_ns() { return g_peer_wait_ns.load(std::memory_order_relaxed); }
 
 __device__ __forceinline__ int tp_ld_acquire_sys(const int* p) {
     int v;
@@ -43,7 +49,7 @@ __global__ void tp_signal_kernel(int* const* __restrict__ peer_flags, int me, in
 }
 
 // Thread s: wait (bounded) until rank s's slot of this rank's flags holds the epoch.
-__global__ void tp_wait_kernel(const int* __restrict__ flags, int G, int epoch, int* err) {
+__global__ void tp_wait_kernel(const int* __restrict__ flags, int G, int epoch, int* err, uint64_t limit_ns) {
     grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
     grid_dep_launch();
     const int s = threadIdx.x;
@@ -52,7 +58,7 @@ __global__ void tp_wait_kernel(const int* __restrict__ flags, int G, int epoch, 
     const uint64_t t0 = globaltimer();
     while (tp_ld_acquire_sys(f) != epoch) {
         __nanosleep(256);
-        if (globaltimer() - t0 > B200_WAIT_LIMIT_NS) {
+        if (globaltimer() - t0 > limit_ns) {
             atomicCAS(err, 0, ERR_WAIT_PEER);
             return;
         }
@@ -62,6 +68,9 @@ __global__ void tp_wait_kernel(const int* __restrict__ flags, int G, int epoch, 
 }  // namespace b200
 
 extern "C" {
+
+void b200_set_peer_wait_limit_ns(uint64_t ns) { b200::g_peer_wait_ns.store(ns ? ns : B200_WAIT_LIMIT_NS); }
+uint64_t b200_peer_wait_limit_ns(void) { return b200::peer_wait_limit_ns(); }
 
 size_t b200_mul_mat_tp_workspace_size(int wtype, int64_t M, int64_t N_shard, int64_t K) {
     if (M <= 0 || N_shard <= 0 || K <= 0) return 0;
@@ -90,7 +99,7 @@ int b200_mul_mat_tp_finish(const int* flags, int64_t n_ranks, int epoch, int* de
     if (!flags || !dev_err || n_ranks <= 0) return B200_E_INVALID;
     if (n_ranks > 64) return B200_E_UNSUPPORTED;
     launch_pdl(tp_wait_kernel, dim3(1), dim3(64), 0, static_cast<cudaStream_t>(stream), flags, (int)n_ranks, epoch,
-               dev_err);
+               dev_err, peer_wait_limit_ns());
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 

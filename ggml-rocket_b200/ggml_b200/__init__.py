@@ -75,6 +75,18 @@ def check(rc, what):
         raise B200Error(f"{what} failed: {STATUS.get(rc, rc)}")
 
 
+# codes kernels record in a device error word (first writer wins)
+DEVICE_ERRORS = {1: "wait_producer", 2: "wait_mma", 3: "wait_epilogue", 4: "wait_dequant", 5: "wait_drain",
+                 6: "bad_index", 7: "wait_peer", 8: "wait_stream", 100: "bad_ids"}
+
+
+def check_device(err, what):
+    """Read a device error word (synchronises with the work that wrote it) and raise on a nonzero code."""
+    code = int(err.item())
+    if code != 0:
+        raise B200Error(f"{what}: device error {DEVICE_ERRORS.get(code, code)}")
+
+
 def _ptr(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
@@ -261,6 +273,8 @@ _SIGS.update({
     "b200_mul_mat_tp": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _int, _vp,
                                _sz, _vp, _vp]),
     "b200_mul_mat_tp_finish": (_int, [_vp, _i64, _int, _vp, _vp]),
+    "b200_set_peer_wait_limit_ns": (None, [_c.c_uint64]),
+    "b200_peer_wait_limit_ns": (_c.c_uint64, []),
 })
 _SIGS.update({
     "b200_mul_mat_noalloc_max_workspace": (_sz, []),

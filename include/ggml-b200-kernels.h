@@ -316,6 +316,16 @@ int    b200_moe_ep_p2p_expert_group(int n_members, int wtype, const void * const
                                     const int64_t * ret_nb2, int * const * peer_flags, int epoch, void * workspace,
                                     size_t workspace_bytes, int * dev_err, void * stream);
 
+/* ---- the give-up limit of cross-GPU waits -------------------------------------------------------
+ * The reference's fault policy (ggml-rocket.cpp:263-307) turns a device route that fails into an
+ * error status instead of a hang. Here every kernel that waits for another GPU's flag (the
+ * N-sharded and expert-parallel finish and owner waits below) gives up after this many nanoseconds
+ * of %globaltimer, records B200_DEV_WAIT_PEER in its error word and returns, so the context stays
+ * usable and the caller sees the failure. Process-wide; 0 restores the default of 2 s. */
+#define B200_DEV_WAIT_PEER 7
+void     b200_set_peer_wait_limit_ns(uint64_t ns);
+uint64_t b200_peer_wait_limit_ns(void);
+
 /* ---- MUL_MAT with the weight rows split across GPUs (N-sharded), all-gather by the epilogue ----
  * No counterpart in the reference (its MUL_MAT, ggml-rocket.cpp:4548-4871, runs on one device):
  * the same op with an [N, K] weight cut into n_ranks row blocks, one per GPU. Rank r calls
