@@ -475,6 +475,34 @@ def run_ours(args):
         torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
     ms, gms, e2e_ms = [float(x) for x in vals.tolist()]
 
+    # On several GPUs, the two paths that really use them, beside the replicas: the configs[3] MoE layer
+    # with its experts split over the ranks (exchanges by kernel stores into peer memory; weak scaling:
+    # 2048 tokens per rank) and the headline sweep with every weight's rows split over the ranks (strong
+    # scaling), each with its one-GPU reference measured in the same run on rank 0.
+    multi = None
+    if world > 1:
+        del weights
+        torch.cuda.empty_cache()
+        moe_n = run_moe(args, inside=True)
+        torch.distributed.barrier()
+        moe_1 = run_moe(args, world_override=1, inside=True) if rank == 0 else None
+        torch.distributed.barrier()
+        shard_n = run_gemm_sharded(args, inside=True)
+        torch.distributed.barrier()
+        if rank == 0:
+            one_sweep_ms = ms / L
+            multi = {
+                "moe_expert_parallel": {
+                    "workload": "BASELINE configs[3] MoE layer (gate+up+down, Q4_K, 128 experts top-8), 2048 tokens "
+                                f"per rank, experts split {MOE['E']}/{world} per rank, peer-memory exchanges",
+                    "ms_per_layer": moe_n["ms"], "tokens_per_s": moe_n["tokens_per_s"], "tflops": moe_n["tflops"],
+                    "ms_per_layer_1gpu": moe_1["ms"], "weak_efficiency": moe_1["ms"] / moe_n["ms"]},
+                "sharded_sweep": {
+                    "workload": "the headline sweep (one layer) with every weight's rows split over the ranks, "
+                                "output all-gathered by the GEMM epilogue's peer stores",
+                    "ms": shard_n["ms"], "tflops": shard_n["tflops"], "ms_1gpu": one_sweep_ms,
+                    "strong_speedup": one_sweep_ms / shard_n["ms"]}}
+
     if rank == 0:
         peaks, peak_src = measured_peaks()
         flops = step_flops() * L
@@ -540,6 +568,8 @@ def run_ours(args):
             "clocks": clocks,
             "gpu_launches": launches_per_step * args.steps,
         }
+        if multi:
+            line["multi_gpu"] = multi
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
@@ -559,15 +589,20 @@ def moe_flops_per_rank():
     return 3 * 2.0 * m["tokens"] * m["top"] * m["hidden"] * m["ffn"]
 
 
-def run_moe(args):
+def run_moe(args, world_override=None, inside=False):
+    """The MoE layer of configs[3]. inside: called from the headline arm of an N-GPU run (the process
+    group exists; return the timing instead of printing a line); world_override=1: this rank alone runs
+    the single-GPU layer (all experts), the N = 1 reference of the expert-parallel numbers."""
     import numpy as np
     import torch
     import ggml_b200 as g
     from ggml_b200 import quants
     world, rank, local = dist_env()
+    if world_override is not None:
+        world = world_override
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
+    if world > 1 and not inside:
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
@@ -660,6 +695,9 @@ def run_moe(args):
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms = float(t.item())
+    if inside:
+        return {"ms": ms, "tokens_per_s": T * world / (ms / 1e3),
+                "tflops": moe_flops_per_rank() * world / (ms / 1e3) / 1e12}
     if rank == 0:
         peaks, src = measured_peaks()
         tf = moe_flops_per_rank() * world / (ms / 1e3) / 1e12
@@ -818,10 +856,11 @@ def run_gemv(args):
     return 0
 
 
-def run_gemm_sharded(args):
+def run_gemm_sharded(args, inside=False):
     """The headline sweep with every weight's rows split across the ranks (ggml_b200.tp): each
     rank packs its row block of each shape's weight, runs the N-sharded MUL_MAT on the shared
-    activation, and ends holding the full dst. value = the sweep's FLOPs / max-over-ranks time."""
+    activation, and ends holding the full dst. value = the sweep's FLOPs / max-over-ranks time.
+    inside: called from the headline arm (the process group exists; return the timing)."""
     import numpy as np
     import torch
     import ggml_b200 as g
@@ -830,7 +869,9 @@ def run_gemm_sharded(args):
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
+    if inside:
+        pass
+    elif world > 1:
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=dev)
     else:
@@ -886,6 +927,8 @@ def run_gemm_sharded(args):
         torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
     ms = float(vals.item())
     tp.close()
+    if inside:
+        return {"ms": ms, "tflops": step_flops() / (ms / 1e3) / 1e12}
     if rank == 0:
         flops = step_flops()
         line = {"metric": METRIC, "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,

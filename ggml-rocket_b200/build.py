@@ -2,6 +2,7 @@
 
     python ggml-rocket_b200/build.py            # incremental
     python ggml-rocket_b200/build.py --clean
+    GGML_DIR=/path/to/llama.cpp python ggml-rocket_b200/build.py   # + the ggml plugin
 
 Every .cu under csrc/ is compiled by nvcc for sm_100a only
 (-gencode arch=compute_100a,code=sm_100a), every .cpp by g++; the objects go to _build/ and
@@ -91,6 +92,30 @@ def build(verbose_ptxas=False, jobs=8):
     return LIB
 
 
+def build_plugin(ggml_dir, ggml_lib=None):
+    """The ggml plugin (csrc/ggml/ggml-b200-plugin.cpp -> lib/libggml-b200-plugin.so), compiled against a
+    host's ggml: ggml_dir is a llama.cpp or ggml checkout (its ggml/include and ggml/src, where the private
+    ggml-backend-impl.h lives), ggml_lib the directory holding libggml-base.so (default: its build/bin).
+    The plugin links libggml-b200.so beside it; a host loads it with GGML_BACKEND_PATH or
+    ggml_backend_load."""
+    lib = build()
+    root = ggml_dir
+    inc = [os.path.join(root, "ggml", "include"), os.path.join(root, "ggml", "src"), os.path.join(root, "include"),
+           os.path.join(root, "src")]
+    inc = [d for d in inc if os.path.isdir(d)]
+    if not any(os.path.exists(os.path.join(d, "ggml-backend-impl.h")) for d in inc):
+        raise SystemExit(f"{ggml_dir}: no ggml-backend-impl.h under ggml/src or src")
+    ggml_lib = ggml_lib or os.path.join(root, "build", "bin")
+    out = os.path.join(LIBDIR, "libggml-b200-plugin.so")
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall", "-I" + os.path.join(CUDA_HOME, "include")] + \
+        INCLUDES + ["-I" + d for d in inc] + [os.path.join(CSRC, "ggml", "ggml-b200-plugin.cpp"), "-o", out,
+                                             "-L" + LIBDIR, "-lggml-b200", "-L" + ggml_lib, "-lggml-base",
+                                             "-L" + os.path.join(CUDA_HOME, "lib64"), "-lcudart",
+                                             "-Wl,-rpath,$ORIGIN"]
+    run(cmd)
+    return out
+
+
 def clean():
     for d in (BUILD, LIBDIR):
         if os.path.isdir(d):
@@ -101,7 +126,13 @@ if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--clean", action="store_true")
     ap.add_argument("-v", action="store_true", help="ptxas -v")
+    ap.add_argument("--ggml", default=os.environ.get("GGML_DIR"),
+                    help="also build the ggml plugin against this llama.cpp / ggml checkout (default: $GGML_DIR)")
+    ap.add_argument("--ggml-lib", default=os.environ.get("GGML_LIB_DIR"), help="directory of libggml-base.so")
     a = ap.parse_args()
     if a.clean:
         clean()
-    sys.exit(0 if build(verbose_ptxas=a.v) else 1)
+    ok = build(verbose_ptxas=a.v)
+    if a.ggml:
+        build_plugin(a.ggml, a.ggml_lib)
+    sys.exit(0 if ok else 1)

@@ -277,6 +277,18 @@ _SIGS.update({
     "b200_peer_wait_limit_ns": (_c.c_uint64, []),
 })
 _SIGS.update({
+    "ggml_backend_b200_builder_new": (_vp, []),
+    "ggml_backend_b200_builder_free": (None, [_vp]),
+    "ggml_backend_b200_builder_reset": (None, [_vp]),
+    "ggml_backend_b200_builder_find": (_TP, [_vp, _vp]),
+    "ggml_backend_b200_builder_add": (_TP, [_vp, _vp, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int32,
+                                            _c.POINTER(_i64), _c.POINTER(_sz), _c.POINTER(ctypes.c_int32),
+                                            _c.POINTER(_vp), _vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_char_p]),
+    "ggml_backend_b200_builder_push_node": (_int, [_vp, _vp]),
+    "ggml_backend_b200_builder_nodes": (_int, [_vp, _c.POINTER(_c.POINTER(_TP))]),
+    "ggml_backend_b200_builder_compute": (_int, [_vp, _vp]),
+})
+_SIGS.update({
     "b200_mul_mat_noalloc_max_workspace": (_sz, []),
     "b200_mul_mat_noalloc": (_int, [_int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp]),
     "b200_mul_mat_noalloc_error": (_int, [_vp, _c.POINTER(_int)]),
@@ -401,6 +413,52 @@ class DeviceBuffer:
         """A descriptor of a contiguous tensor at `offset` in this buffer."""
         return make_tensor(ttype, ne, self.base + offset, op=op, srcs=srcs, name=name, on_device=True,
                            op_params=op_params)
+
+
+class GraphBuilder:
+    """The converter a ggml adapter drives (ggml_backend_b200_builder_*): host tensors declared by
+    key with ggml's op names, one descriptor per key, nodes pushed in execution order."""
+
+    def __init__(self):
+        self.h = lib().ggml_backend_b200_builder_new()
+
+    def close(self):
+        if self.h:
+            lib().ggml_backend_b200_builder_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def add(self, key, op_name, type_, ne, nb, op_params=None, src_keys=(), data=None, on_device=False,
+            readable=True, name="", subop_name=None):
+        ne4 = (ctypes.c_int64 * 4)(*(list(ne) + [1] * (4 - len(ne))))
+        nb4 = (ctypes.c_size_t * 4)(*nb)
+        opp = (ctypes.c_int32 * 16)(*(list(op_params or []) + [0] * (16 - len(op_params or []))))
+        srcs = (ctypes.c_void_p * 10)(*(list(src_keys) + [None] * (10 - len(src_keys))))
+        r = lib().ggml_backend_b200_builder_add(self.h, key, op_name.encode(),
+                                                subop_name.encode() if subop_name else None, type_, ne4, nb4, opp,
+                                                srcs, data, 1 if on_device else 0, 1 if readable else 0,
+                                                name.encode())
+        return r.contents if r else None
+
+    def find(self, key):
+        r = lib().ggml_backend_b200_builder_find(self.h, key)
+        return r.contents if r else None
+
+    def push(self, key):
+        return lib().ggml_backend_b200_builder_push_node(self.h, key)
+
+    def nodes(self):
+        arr = ctypes.POINTER(_TP)()
+        n = lib().ggml_backend_b200_builder_nodes(self.h, ctypes.byref(arr))
+        return [arr[i].contents for i in range(n)]
+
+    def compute(self, backend):
+        return lib().ggml_backend_b200_builder_compute(backend.h, self.h)
 
 
 def weight_key(t):

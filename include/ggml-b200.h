@@ -132,6 +132,33 @@ int            ggml_backend_b200_graph_compute(b200_backend_t backend, b200_tens
 /* Bytes held by the device-resident weight cache, and its entry count. */
 size_t         ggml_backend_b200_weight_cache_bytes(b200_backend_t backend, long * n_entries);
 
+/* ---- building a graph from a host's tensors (the ggml adapter's converter) ------------------
+ * Replaces the reference's direct reads of ggml_tensor in graph_compute (ggml-rocket.cpp:7088-7200)
+ * and its load-time check of the host's GGML_OP_* ordinals (:8231-8265): the adapter in the host
+ * process declares each tensor of a split with its fields, its op as ggml's op NAME (ggml_op_name)
+ * and, for UNARY / GLU nodes, the sub-op name (ggml_unary_op_name / ggml_glu_op_name). Every host
+ * tensor gets one descriptor, keyed by an opaque pointer (the ggml_tensor*), so nodes that share a
+ * source share its descriptor (graph_compute groups MUL_MATs / MUL_MAT_IDs by source identity).
+ * Sources are declared before their consumers; _add returns NULL for an undeclared source key and
+ * the existing descriptor when the key was declared before. Unknown op names map to B200_OP_OTHER
+ * (never claimed). The descriptors live until _reset or _free. */
+typedef struct b200_graph_builder * b200_graph_builder_t;
+b200_graph_builder_t ggml_backend_b200_builder_new(void);
+void                 ggml_backend_b200_builder_free(b200_graph_builder_t b);
+void                 ggml_backend_b200_builder_reset(b200_graph_builder_t b);
+b200_tensor *        ggml_backend_b200_builder_find(b200_graph_builder_t b, const void * key);
+b200_tensor *        ggml_backend_b200_builder_add(b200_graph_builder_t b, const void * key, const char * op_name,
+                                                   const char * subop_name, int32_t type, const int64_t ne[4],
+                                                   const size_t nb[4], const int32_t op_params[B200_MAX_OP_PARAMS],
+                                                   const void * const src_keys[B200_MAX_SRC], void * data,
+                                                   int32_t on_device, int32_t readable, const char * name);
+/* appends a declared tensor to the node list (the split's execution order); returns the node count
+ * or -1 for an undeclared key */
+int                  ggml_backend_b200_builder_push_node(b200_graph_builder_t b, const void * key);
+int                  ggml_backend_b200_builder_nodes(b200_graph_builder_t b, b200_tensor * const ** nodes);
+/* graph_compute over the pushed nodes */
+int                  ggml_backend_b200_builder_compute(b200_backend_t backend, b200_graph_builder_t b);
+
 /* ---- the weight identity (ggml-rocket.cpp:4124-4222) ---------------------------------------- */
 /* The cache key of a weight: its name with the scheduler's copy prefixes stripped, the type and
  * shape, and a 64-bit fingerprint of 16 evenly spaced 64-byte samples of its bytes. Writes at most
