@@ -199,9 +199,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             // quantized: the A TMA's expect_tx arrive + the local dequant warps (+ the peer's announcer)
-            mbar_init(full_bar(s), C::QUANT ? 1 + DEQ_WARPS + (PAIR ? 1 : 0) : 2);
+            mbar_init(full_bar(s), C::QUANT ? 1 + DEQ_WARPS / 2 + (PAIR ? 1 : 0) : 2);
             mbar_init(empty_bar(s), 1);
-            if (PAIR && C::QUANT) mbar_init(pfull_bar(s), DEQ_WARPS);
+            if (PAIR && C::QUANT) mbar_init(pfull_bar(s), DEQ_WARPS / 2);
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(tfull_bar(a), 1);
@@ -666,46 +666,65 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     } else if (C::QUANT && dequant_slot(warp) >= 0) {
         // ---------------- dequant (quantized weights) ----------------
         if constexpr (C::QUANT) {
+            // Two groups of four warps take alternate K blocks: in its blocks a warp group decodes all
+            // 64 weights of every row of the tile (thread: one row, both 32-weight halves of the chunk,
+            // from one read of the raw bytes) and fills the whole stage, with one proxy fence and one
+            // arrive per thread per block, while the other group fills the next stage.
             const int dq = dequant_slot(warp);
             const int r = (dq & 3) * 32 + lane;          // weight row within the tile
-            const int h = dq >> 2;                       // which 32 of the chunk's 64 weights
-            int stage = 0, rs = 0;
-            uint32_t phase = 0, rph = 0;
+            const int grp = dq >> 2;                     // this group fills the stages of blocks n with n % 2 == grp
+            int rs = 0;
+            uint32_t rph = 0, n = 0;                     // n: the CTA's running K-block count
             bool ok = true;
             for (int64_t cur = cursor0; cursor_ok(cur) && ok;) {
                 const UnitCoords uc = unit_coords(cur);
                 cur = uc.next;
                 for (int sb = uc.kb0 >> 2; sb * 4 < uc.kb1 && ok; sb++) {
+                    const int k_lo = max(uc.kb0, 4 * sb), k_hi = min(uc.kb1, 4 * sb + 4);
+                    // does this group own a block of this super-block?
+                    const bool mine = (k_hi - k_lo) > 1 || ((n & 1u) == (uint32_t)grp);
                     if (!mbar_wait(rfull_bar(rs), rph, args.err, ERR_WAIT_DEQUANT, abort_flag)) { ok = false; break; }
                     const uint8_t* raw = smem + C::RAW_OFF + rs * RC::STAGE;
                     const uint8_t* rrow = raw + r * RC::ROW;
                     float d6 = 0.0f;
-                    Q4kFactors f4{};
-                    if constexpr (WT == WT_Q6_K) d6 = __half2float(reinterpret_cast<const __half*>(raw + RC::A_BYTES)[r]);
-                    if constexpr (WT == WT_Q4_K) f4 = q4k_factors(rrow, h);
-                    const int k_lo = max(uc.kb0, 4 * sb), k_hi = min(uc.kb1, 4 * sb + 4);
-                    for (int kb = k_lo; kb < k_hi; kb++) {
-                        uint32_t o[16];
+                    Q4kFactors f0{}, f1{};
+                    if (mine) {
+                        if constexpr (WT == WT_Q6_K) d6 = __half2float(reinterpret_cast<const __half*>(raw + RC::A_BYTES)[r]);
                         if constexpr (WT == WT_Q4_K) {
-                            float dj, mj;
-                            f4.pick(kb & 3, dj, mj);
-                            decode_q4k_half(rrow, kb & 3, h, dj, mj, o);
-                        } else if constexpr (WT == WT_Q6_K) {
-                            decode_q6k_half(rrow, d6, kb & 3, h, o);
-                        } else {
-                            decode_q8_0_half(rrow, kb & 3, h, o);
+                            f0 = q4k_factors(rrow, 0);
+                            f1 = q4k_factors(rrow, 1);
                         }
+                    }
+                    for (int kb = k_lo; kb < k_hi; kb++, n++) {
+                        if ((n & 1u) != (uint32_t)grp) continue;
+                        uint32_t o0[16], o1[16];
+                        if constexpr (WT == WT_Q4_K) {
+                            float da, ma, db, mb;
+                            f0.pick(kb & 3, da, ma);
+                            f1.pick(kb & 3, db, mb);
+                            decode_q4k_both(rrow, kb & 3, da, ma, db, mb, o0, o1);
+                        } else if constexpr (WT == WT_Q6_K) {
+                            decode_q6k_half(rrow, d6, kb & 3, 0, o0);
+                            decode_q6k_half(rrow, d6, kb & 3, 1, o1);
+                        } else {
+                            decode_q8_0_half(rrow, kb & 3, 0, o0);
+                            decode_q8_0_half(rrow, kb & 3, 1, o1);
+                        }
+                        const int stage = (int)(n % (uint32_t)STAGES);
+                        const uint32_t phase = (n / (uint32_t)STAGES) & 1u;
                         // decoded first: the arithmetic overlaps the wait for the stage to free up
                         if (!mbar_wait(empty_bar(stage), phase ^ 1u, args.err, ERR_WAIT_DEQUANT, abort_flag)) { ok = false; break; }
                         const uint32_t sw = sbase + stage * C::STAGE_BYTES + C::A_BYTES;
 #pragma unroll
-                        for (int c = 0; c < 4; c++)
-                            st_shared_v4(sw + sw128_offset((uint32_t)r, (uint32_t)(4 * h + c)), o[4 * c], o[4 * c + 1],
-                                         o[4 * c + 2], o[4 * c + 3]);
+                        for (int c = 0; c < 4; c++) {
+                            st_shared_v4(sw + sw128_offset((uint32_t)r, (uint32_t)c), o0[4 * c], o0[4 * c + 1], o0[4 * c + 2],
+                                         o0[4 * c + 3]);
+                            st_shared_v4(sw + sw128_offset((uint32_t)r, (uint32_t)(4 + c)), o1[4 * c], o1[4 * c + 1],
+                                         o1[4 * c + 2], o1[4 * c + 3]);
+                        }
                         fence_proxy_async_smem();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(PAIR && !leader ? pfull_bar(stage) : full_bar(stage));
-                        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(rempty_bar(rs));

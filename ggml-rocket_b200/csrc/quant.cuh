@@ -148,6 +148,28 @@ __device__ __forceinline__ void decode_q4k_half(const uint8_t* blk, int j, int h
     }
 }
 
+// Both 32-weight halves of chunk j of a Q4_K super-block: the low nibbles of qs[32j .. 32j+31]
+// (sub-block 2j, factors d0/m0) into o0 and the high nibbles (sub-block 2j+1, d1/m1) into o1, from
+// one read of the 32 bytes.
+__device__ __forceinline__ void decode_q4k_both(const uint8_t* blk, int j, float d0, float m0, float d1, float m1,
+                                                uint32_t (&o0)[16], uint32_t (&o1)[16]) {
+    const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * j);
+    const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * j);
+    const uint64_t D0 = f2_pack(d0, d0), NM0 = f2_pack(-m0, -m0);
+    const uint64_t D1 = f2_pack(d1, d1), NM1 = f2_pack(-m1, -m1);
+    const uint64_t MAG = f2_pack(-8388608.0f, -8388608.0f);
+    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+    for (int w = 0; w < 8; w++) {
+        const uint32_t lo = q[w] & 0x0F0F0F0Fu, hi = (q[w] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            o0[2 * w + i] = f2_to_half2(f2_fma(D0, f2_add(magic_pair(lo, i), MAG), NM0));
+            o1[2 * w + i] = f2_to_half2(f2_fma(D1, f2_add(magic_pair(hi, i), MAG), NM1));
+        }
+    }
+}
+
 // Q6_K: raw row = 208-byte {ql, qh, scales} super-blocks, d from the transposed d plane.
 // Chunk j (hh = j>>1 selects the 128-weight half, s = j&1 the nibble), half h selects
 // ql[l] (h=0) or ql[l+32] (h=1); y = (d*sc) * (q - 32).
