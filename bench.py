@@ -59,13 +59,14 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemm", "gemv", "moe", "fa", "glue", "layer"], default="gemm",
+    ap.add_argument("--workload", choices=["gemm", "gemv", "moe", "fa", "glue", "layer", "crossover"], default="gemm",
                     help="gemm: the headline MUL_MAT sweep (default); gemv: the sweep's Q4_K weights at decode "
                          "size (M = --decode-m, b200_mul_mat_vec); moe: the MUL_MAT_ID layer of "
                          "BASELINE configs[3], expert-parallel over the ranks; fa: the FLASH_ATTN_EXT "
                          "prefill of configs[2]; glue: a layer's glue ops and the MoE router at the "
                          "headline's prefill shapes (HBM-bound kernels, GB/s); layer: configs[4]'s Llama-3-8B "
-                         "layer through graph_compute, prompt tokens/s")
+                         "layer through graph_compute, prompt tokens/s; crossover: the M at which a claimed "
+                         "MUL_MAT with host tensors beats the host CPU")
     ap.add_argument("--layers", type=int, default=8,
                     help="gemm workload: layers (distinct weight copies) the sweep runs through per step")
     ap.add_argument("--decode-m", type=int, default=1,
@@ -1188,6 +1189,98 @@ def run_layer(args):
     return 0
 
 
+def run_crossover(args):
+    """Where a claimed MUL_MAT stops paying: graph_compute on one MUL_MAT node with HOST tensors (the
+    reference's setting: the host keeps activations in its CPU buffers and the backend claims the op,
+    ggml-rocket.cpp:846-894) against the host CPU computing the same product, per M, for F16 and Q4_K
+    weights of two Llama-8B shapes. The device arm copies the activations in and the output out inside
+    the call (pageable memory, what an ACCEL device's host gets, and pinned memory from this backend's
+    host buffer type); its weight is already cached on the device, as it is after a model's first
+    ubatch. The CPU arm is torch's fp32 matmul over the dequantized weight on every host core (an
+    optimized BLAS standing in for ggml's CPU backend, which is absent here). M* is the smallest M
+    whose device time beats the CPU's."""
+    os.environ.setdefault("B200_MIN_M", "4")
+    os.environ.setdefault("B200_MIN_M_QUANT", "4")
+    import numpy as np
+    import torch
+    import ggml_b200 as g
+    from ggml_b200 import quants
+    world, rank, local = dist_env()
+    if rank != 0:
+        return 0
+    torch.cuda.set_device(local)
+    g.lib()
+    torch.set_num_threads(os.cpu_count())
+    rng = np.random.default_rng(0xC805)
+    Ms = (4, 8, 16, 32, 64, 128, 256, 512)
+    be = g.Backend()
+    res = {}
+    reps = max(3, min(args.steps, 10))
+    for wtype in (g.F16, g.Q4_K):
+        for (k, n) in ((4096, 4096), (4096, 14336)):
+            w = rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
+            if wtype == g.F16:
+                nat = w.astype(np.float16).view(np.uint8).reshape(n, -1)
+                wf = torch.from_numpy(w.astype(np.float16).astype(np.float32))
+            else:
+                nat = quants.quantize(wtype, w)
+                import oracle
+                oracle.build()
+                wf = torch.from_numpy(oracle.dequantize(wtype, nat, k))
+            rows = {}
+            for M in Ms:
+                a = rng.standard_normal((M, k), dtype=np.float32)
+                out = {}
+                for pinned in (False, True):
+                    if pinned:
+                        a_h, a_ptr = _pinned_array(g, a.nbytes, np.float32, a.shape)
+                        o_h, o_ptr = _pinned_array(g, M * n * 4, np.float32, (M, n))
+                    else:
+                        a_h, o_h = np.empty_like(a), np.empty((M, n), np.float32)
+                        a_ptr, o_ptr = a_h.ctypes.data, o_h.ctypes.data
+                    a_h[:] = a
+                    wt = g.make_tensor(wtype, [k, n], data=nat, name=f"xover.{wtype}.{k}x{n}.weight")
+                    at = g.make_tensor(g.F32, [k, M], data=a_ptr, name="x")
+                    dt = g.make_tensor(g.F32, [n, M], data=o_ptr, op=g.OP_MUL_MAT, srcs=[wt, at], name="y")
+                    if not g.supports_op(dt):
+                        raise SystemExit(f"MUL_MAT M={M} not claimed")
+                    for _ in range(2):
+                        be.graph_compute([dt])
+                    ts = []
+                    for _ in range(reps):
+                        t0 = time.perf_counter()
+                        if be.graph_compute([dt]) != g.STATUS_SUCCESS:
+                            raise SystemExit("graph_compute failed")
+                        ts.append(time.perf_counter() - t0)
+                    out["pinned" if pinned else "pageable"] = statistics.median(ts) * 1e6
+                    if pinned:
+                        g.lib().ggml_backend_b200_host_free(a_ptr)
+                        g.lib().ggml_backend_b200_host_free(o_ptr)
+                at_ = torch.from_numpy(a)
+                torch.matmul(at_, wf.T)
+                ts = []
+                for _ in range(reps):
+                    t0 = time.perf_counter()
+                    torch.matmul(at_, wf.T)
+                    ts.append(time.perf_counter() - t0)
+                out["cpu"] = statistics.median(ts) * 1e6
+                rows[M] = {kk: round(v, 1) for kk, v in out.items()}
+            xo = {arm: next((M for M in Ms if rows[M][arm] < rows[M]["cpu"]), None) for arm in ("pageable", "pinned")}
+            res[f"{g.TYPE_NAMES[wtype]} K={k} N={n}"] = {"us_by_M": rows, "crossover_M": xo}
+    be.close()
+    worst = max((v["crossover_M"]["pageable"] or 10 ** 9) for v in res.values())
+    line = {"metric": "MUL_MAT claim crossover: smallest M at which graph_compute (host tensors) beats the host CPU",
+            "value": worst, "unit": "rows", "n_gpus": 1, "steps": reps, "warmup": 2, "higher_is_better": False,
+            "scaling": "replicas only", "vs_baseline": None, "dtype": "f16 / Q4_K (fp32 accumulate)",
+            "data": "synthetic",
+            "config": {"workload": "one MUL_MAT node per graph_compute call, weights cached on the device, "
+                                   "activations and output in host memory",
+                       "cpu_arm": f"torch fp32 matmul over the dequantized weight, {os.cpu_count()} threads",
+                       "timing": "wall clock per synchronous call, median", "shapes": res}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -1202,6 +1295,8 @@ def main():
         return run_glue(args)
     if args.workload == "layer":
         return run_layer(args)
+    if args.workload == "crossover":
+        return run_crossover(args)
     if args.shard:
         return run_gemm_sharded(args)
     return run_ours(args)

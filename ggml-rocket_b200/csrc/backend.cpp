@@ -61,20 +61,27 @@ bool knob_on(const char* name, bool dflt) {
     return (e && *e) ? (atoi(e) > 0) : dflt;
 }
 
-// Minimum rows a dense MUL_MAT must carry to be claimed (ggml-rocket.cpp:868-876). Below it
-// the op's fixed cost -- here the host<->device copies of the activation and the result --
-// outweighs the device's throughput advantage; decode (M = 1) and batched-beam decode stay on
-// the CPU. Floor 4, as in the reference.
+// Minimum rows a dense MUL_MAT must carry to be claimed (ggml-rocket.cpp:846-876), re-derived for
+// B200 by the reference's method: the crossover where the claimed op (here graph_compute with the
+// activation and result in host memory, copied in and out every call) meets the host CPU computing
+// it. Measured on a B200 box (bench.py --workload crossover: one MUL_MAT per call, weights cached,
+// 16 host cores; the CPU arm an fp32 BLAS over the dequantized weight, standing in for ggml's CPU
+// backend), the device wins at every M >= 4 for F16 and Q4_K at K = 4096, N = 4096 / 14336: at
+// M = 16, 80-170 us (pageable host memory) against 0.9-3.6 ms; at M = 4, 58-82 us against 0.4-2.1
+// ms. A CPU that reads 4-bit weights directly (ggml's Q4_K path, memory-bound at these M) narrows
+// that by up to ~8x, so the default keeps a margin: 16 rows, where even then the device stays ahead.
+// Decode (M = 1) and batched-beam decode (M ~ 5) stay on the CPU unless B200_DECODE claims them for
+// the decode kernels. Floor 4, as in the reference.
 int min_m() {
-    static const int m = [] { const int x = knob_int("B200_MIN_M", 32); return x < 4 ? 4 : x; }();
+    static const int m = [] { const int x = knob_int("B200_MIN_M", 16); return x < 4 ? 4 : x; }();
     return m;
 }
 // The floor for quantized weights (ggml-rocket.cpp:887-894). The reference's 512 pays for a
-// per-call host dequant; the fused device dequant has no such cost, so the default equals
-// min_m(). Never below min_m().
+// per-call host dequant; the fused device dequant has no such cost and the same crossover
+// measurement puts Q4_K at the dense floor, so the default equals min_m(). Never below min_m().
 int min_m_quant() {
     static const int m = [] {
-        const int x = knob_int("B200_MIN_M_QUANT", 32);
+        const int x = knob_int("B200_MIN_M_QUANT", 16);
         return x < min_m() ? min_m() : x;
     }();
     return m;

@@ -40,7 +40,8 @@ def test_mul_mat_weight_types():
     assert supported(K, N, MQ, g.Q8_0)
     assert supported(K, N, MQ, g.Q4_K)
     assert supported(K, N, MQ, g.Q6_K)
-    # B200: the quant floor defaults to the dense one (32), so M=256 is claimed too
+    # B200: the quant floor defaults to the dense one (16, from a measured crossover), so M=256 is
+    # claimed too
     assert supported(K, N, M, g.Q4_K)
     assert not supported(K, N, MQ, 2)          # Q4_0: no device decoder -> CPU
 
@@ -52,7 +53,8 @@ def test_mul_mat_shape_gates():
     assert not supported(32, N, M, g.F16)      # K < 64
     assert not supported(K, 48, M, g.F16)      # N < 64
     assert not supported(K, N, 1, g.F16)       # decode GEMV stays on the CPU
-    assert not supported(K, N, 16, g.F16)      # below the default floor of 32
+    assert supported(K, N, 16, g.F16)          # the default floor (16)
+    assert not supported(K, N, 8, g.F16)       # below it
     assert not supported(384, N, MQ, g.Q4_K)   # K % 256 != 0 for a K-quant
 
 
@@ -203,12 +205,12 @@ def child(env):
 def test_knobs_in_children():
     r = child({"B200_MIN_M_QUANT": "512"})
     assert not r["q4k_m256"] and r["q4k_m512"]
-    r = child({"B200_MIN_M": "16"})
-    assert r["f16_m16"]
+    r = child({"B200_MIN_M": "32"})                # the reference's default
+    assert not r["f16_m16"]
     r = child({"B200_MIN_M": "1"})                 # floor of 4
     assert not r["f16_m3"]
-    r = child({"B200_MIN_M": ""})                  # set-but-empty reads as unset (32)
-    assert not r["f16_m16"]
+    r = child({"B200_MIN_M": ""})                  # set-but-empty reads as unset (16)
+    assert r["f16_m16"]
     r = child({"B200_MOE": "0"})
     assert not r["moe"]
     r = child({"B200_MOE": "1"})
