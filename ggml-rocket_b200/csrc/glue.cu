@@ -70,13 +70,27 @@ __global__ void __launch_bounds__(RMS_THREADS) rms_norm_kernel(const char* __res
     grid_dep_launch();
     __shared__ double red[RMS_THREADS / 32];
     const int64_t rows = s.ne[1] * s.ne[2] * s.ne[3];
+    // rows of 16-byte aligned, dense f32 values: read as float4
+    const bool vec = s.nb[0] == 4 && s.ne[0] % 4 == 0 && (s.nb[1] % 16) == 0 && (s.nb[2] % 16) == 0 &&
+                     (s.nb[3] % 16) == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
     for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
         const int64_t i1 = r % s.ne[1], i2 = (r / s.ne[1]) % s.ne[2], i3 = r / (s.ne[1] * s.ne[2]);
         const char* row = x + i1 * s.nb[1] + i2 * s.nb[2] + i3 * s.nb[3];
         double sum = 0.0;
-        for (int64_t i = threadIdx.x; i < s.ne[0]; i += RMS_THREADS) {
-            const float v = *reinterpret_cast<const float*>(row + i * s.nb[0]);
-            sum += (double)__fmul_rn(v, v);
+        if (vec) {
+            const float4* r4 = reinterpret_cast<const float4*>(row);
+            for (int64_t i = threadIdx.x; i < s.ne[0] / 4; i += RMS_THREADS) {
+                const float4 v = r4[i];
+                sum += (double)__fmul_rn(v.x, v.x);
+                sum += (double)__fmul_rn(v.y, v.y);
+                sum += (double)__fmul_rn(v.z, v.z);
+                sum += (double)__fmul_rn(v.w, v.w);
+            }
+        } else {
+            for (int64_t i = threadIdx.x; i < s.ne[0]; i += RMS_THREADS) {
+                const float v = *reinterpret_cast<const float*>(row + i * s.nb[0]);
+                sum += (double)__fmul_rn(v, v);
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
@@ -88,9 +102,71 @@ __global__ void __launch_bounds__(RMS_THREADS) rms_norm_kernel(const char* __res
         const float mean = (float)(tot / (double)s.ne[0]);
         const float scale = 1.0f / sqrtf(__fadd_rn(mean, eps));
         float* out = dst + r * s.ne[0];
-        for (int64_t i = threadIdx.x; i < s.ne[0]; i += RMS_THREADS)
-            out[i] = __fmul_rn(*reinterpret_cast<const float*>(row + i * s.nb[0]), scale);
+        if (vec && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+            const float4* r4 = reinterpret_cast<const float4*>(row);
+            float4* o4 = reinterpret_cast<float4*>(out);
+            for (int64_t i = threadIdx.x; i < s.ne[0] / 4; i += RMS_THREADS) {
+                const float4 v = r4[i];
+                o4[i] = make_float4(__fmul_rn(v.x, scale), __fmul_rn(v.y, scale), __fmul_rn(v.z, scale),
+                                    __fmul_rn(v.w, scale));
+            }
+        } else {
+            for (int64_t i = threadIdx.x; i < s.ne[0]; i += RMS_THREADS)
+                out[i] = __fmul_rn(*reinterpret_cast<const float*>(row + i * s.nb[0]), scale);
+        }
         __syncthreads();   // red is reused by the next row
+    }
+}
+
+// ---- contiguous fast paths ----------------------------------------------------------------------
+// Most of a layer's glue ops see dense f32 tensors. For those the per-element index arithmetic of
+// the general kernels (64-bit divisions and remainders per element) costs more than the memory
+// traffic, so dense operands take these kernels instead: 16-byte accesses, a grid-stride loop over
+// float4 groups, no index math. The arithmetic per element is the general kernels' (the same
+// __fadd_rn / __fmul_rn / silu on the same values), so results are bit-identical.
+__device__ __forceinline__ float bin_op(int op, float x, float y) {
+    return op == B200_BIN_ADD ? __fadd_rn(x, y) : op == B200_BIN_MUL ? __fmul_rn(x, y) : __fdiv_rn(x, y);
+}
+// a, dst dense [rows][ne0]; b dense [rows][ne0] (b_row = 0) or one row [ne0] repeated (b_row = 1)
+__global__ void binary_dense_kernel(int op, const float4* __restrict__ a, const float4* __restrict__ b, int b_row,
+                                    int64_t ne0_4, int64_t n4, float4* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 x = a[i];
+        const float4 y = b[b_row ? i % ne0_4 : i];
+        dst[i] = make_float4(bin_op(op, x.x, y.x), bin_op(op, x.y, y.y), bin_op(op, x.z, y.z), bin_op(op, x.w, y.w));
+    }
+}
+__device__ __forceinline__ float silu_f(float x);
+__global__ void swiglu_dense_kernel(const float4* __restrict__ a, const float4* __restrict__ g, int64_t n4,
+                                    float4* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 x = a[i], y = g[i];
+        dst[i] = make_float4(__fmul_rn(silu_f(x.x), y.x), __fmul_rn(silu_f(x.y), y.y), __fmul_rn(silu_f(x.z), y.z),
+                             __fmul_rn(silu_f(x.w), y.w));
+    }
+}
+__global__ void silu_dense_kernel(const float4* __restrict__ x, int64_t n4, float4* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 v = x[i];
+        dst[i] = make_float4(silu_f(v.x), silu_f(v.y), silu_f(v.z), silu_f(v.w));
+    }
+}
+
+// dense f32 -> dense f16 (round to nearest even), four values per thread
+__global__ void cpy_f32_f16_dense_kernel(const float4* __restrict__ src, int64_t n4, uint2* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 v = src[i];
+        const __half2 lo = __halves2half2(__float2half_rn(v.x), __float2half_rn(v.y));
+        const __half2 hi = __halves2half2(__float2half_rn(v.z), __float2half_rn(v.w));
+        dst[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
     }
 }
 
@@ -112,6 +188,7 @@ __global__ void binary_kernel(int op, const char* __restrict__ a, Shape4 sa, con
 
 // ggml_silu_f32: x / (1 + expf(-x)), expf being the device's (within 2 ulp of the host libm's)
 __device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+__device__ __forceinline__ float silu_f(float x) { return silu(x); }
 
 // ---- SILU and SWIGLU (dst = silu(a) * g) -------------------------------------------------------
 __global__ void silu_kernel(const char* __restrict__ x, Shape4 s, float* __restrict__ dst) {
@@ -169,6 +246,58 @@ __global__ void rope_kernel(const char* __restrict__ x, Shape4 s, const int32_t*
         const float x1 = *reinterpret_cast<const float*>(row + e1 * s.nb[0]);
         out[e0] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
         out[e1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    }
+}
+
+// The same ROPE with one CTA per token (i2): ggml's rope cache for that position -- the sequential
+// products theta_j and their cos / sin -- is computed once into shared memory (the general kernel
+// recomputes it for every head, an O(n_dims) product chain per element), then the CTA rotates every
+// head of the token. Same values, same order of operations, bit-identical to rope_kernel.
+constexpr int ROPE_MAX_HALF = 256;
+__global__ void __launch_bounds__(256) rope_token_kernel(const char* __restrict__ x, Shape4 s,
+                                                        const int32_t* __restrict__ pos, int n_dims, int neox,
+                                                        float theta_scale, float freq_scale, float attn_factor,
+                                                        float* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    __shared__ float cs[ROPE_MAX_HALF], sn[ROPE_MAX_HALF];
+    const int half_rot = n_dims / 2;
+    const int64_t half = s.ne[0] / 2;
+    for (int64_t tok = blockIdx.x; tok < s.ne[2] * s.ne[3]; tok += gridDim.x) {
+        const int64_t i2 = tok % s.ne[2], i3 = tok / s.ne[2];
+        // the product chain is sequential (one thread); its cos / sin are not (one thread each)
+        if (threadIdx.x == 0) {
+            float theta = (float)pos[i2];
+            for (int j = 0; j < half_rot; j++) {
+                cs[j] = theta;
+                theta = __fmul_rn(theta, theta_scale);
+            }
+        }
+        __syncthreads();
+        for (int j = threadIdx.x; j < half_rot; j += blockDim.x) {
+            const float t = __fmul_rn(freq_scale, cs[j]);
+            sn[j] = __fmul_rn(sinf(t), attn_factor);
+            cs[j] = __fmul_rn(cosf(t), attn_factor);
+        }
+        __syncthreads();
+        const int64_t n = half * s.ne[1];
+        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+            const int64_t j = i % half, i1 = i / half;
+            const char* row = x + i1 * s.nb[1] + i2 * s.nb[2] + i3 * s.nb[3];
+            float* out = dst + ((i3 * s.ne[2] + i2) * s.ne[1] + i1) * s.ne[0];
+            if (2 * j >= n_dims) {
+                out[2 * j] = *reinterpret_cast<const float*>(row + (2 * j) * s.nb[0]);
+                out[2 * j + 1] = *reinterpret_cast<const float*>(row + (2 * j + 1) * s.nb[0]);
+                continue;
+            }
+            const float c = cs[j], sv = sn[j];
+            const int64_t e0 = neox ? j : 2 * j, e1 = neox ? j + n_dims / 2 : 2 * j + 1;
+            const float x0 = *reinterpret_cast<const float*>(row + e0 * s.nb[0]);
+            const float x1 = *reinterpret_cast<const float*>(row + e1 * s.nb[0]);
+            out[e0] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sv));
+            out[e1] = __fadd_rn(__fmul_rn(x0, sv), __fmul_rn(x1, c));
+        }
+        __syncthreads();   // cs / sn are rewritten for the next token
     }
 }
 
@@ -356,6 +485,16 @@ static bool shape_ok(const int64_t ne[4], const size_t nb[4]) {
     return true;
 }
 static int64_t nelem(const int64_t ne[4]) { return ne[0] * ne[1] * ne[2] * ne[3]; }
+// dense f32: contiguous strides and a 16-byte aligned base, rows a multiple of four values
+static bool dense_f32(const void* p, const int64_t ne[4], const size_t nb[4]) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15u) || ne[0] % 4) return false;
+    size_t next = 4;
+    for (int i = 0; i < 4; i++) {
+        if (ne[i] != 1 && nb[i] != next) return false;
+        next *= (size_t)ne[i];
+    }
+    return true;
+}
 static int done(cudaError_t e) { return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA; }
 
 }  // namespace b200
@@ -380,6 +519,14 @@ int b200_binary(int op, const float* a, const int64_t ane[4], const size_t anb[4
     for (int i = 0; i < 4; i++)
         if (ane[i] % bne[i] != 0) return B200_E_INVALID;   // b must repeat over a
     const int64_t n = nelem(ane);
+    const bool b_same = bne[0] == ane[0] && bne[1] == ane[1] && bne[2] == ane[2] && bne[3] == ane[3];
+    const bool b_row = bne[0] == ane[0] && bne[1] == 1 && bne[2] == 1 && bne[3] == 1;
+    if (dense_f32(a, ane, anb) && dense_f32(b, bne, bnb) && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0 &&
+        (b_same || b_row))
+        return done(launch_pdl(binary_dense_kernel, dim3((unsigned)grid_for(n / 4, 256)), dim3(256), 0,
+                               static_cast<cudaStream_t>(stream), op, reinterpret_cast<const float4*>(a),
+                               reinterpret_cast<const float4*>(b), b_row ? 1 : 0, ane[0] / 4, n / 4,
+                               reinterpret_cast<float4*>(dst)));
     return done(launch_pdl(binary_kernel, dim3((unsigned)grid_for(n, 256)), dim3(256), 0,
                            static_cast<cudaStream_t>(stream), op, reinterpret_cast<const char*>(a), shape_of(ane, anb),
                            reinterpret_cast<const char*>(b), shape_of(bne, bnb), dst));
@@ -389,6 +536,10 @@ int b200_silu(const float* x, const int64_t ne[4], const size_t nb[4], float* ds
     using namespace b200;
     if (!x || !dst || !shape_ok(ne, nb)) return B200_E_INVALID;
     const int64_t n = nelem(ne);
+    if (dense_f32(x, ne, nb) && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0)
+        return done(launch_pdl(silu_dense_kernel, dim3((unsigned)grid_for(n / 4, 256)), dim3(256), 0,
+                               static_cast<cudaStream_t>(stream), reinterpret_cast<const float4*>(x), n / 4,
+                               reinterpret_cast<float4*>(dst)));
     return done(launch_pdl(silu_kernel, dim3((unsigned)grid_for(n, 256)), dim3(256), 0,
                            static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), dst));
 }
@@ -398,6 +549,10 @@ int b200_swiglu(const float* a, const size_t anb[4], const float* g, const size_
     using namespace b200;
     if (!a || !g || !dst || !shape_ok(ne, anb) || !shape_ok(ne, gnb)) return B200_E_INVALID;
     const int64_t n = nelem(ne);
+    if (dense_f32(a, ne, anb) && dense_f32(g, ne, gnb) && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0)
+        return done(launch_pdl(swiglu_dense_kernel, dim3((unsigned)grid_for(n / 4, 256)), dim3(256), 0,
+                               static_cast<cudaStream_t>(stream), reinterpret_cast<const float4*>(a),
+                               reinterpret_cast<const float4*>(g), n / 4, reinterpret_cast<float4*>(dst)));
     return done(launch_pdl(swiglu_kernel, dim3((unsigned)grid_for(n, 256)), dim3(256), 0,
                            static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(a), shape_of(ne, anb),
                            reinterpret_cast<const char*>(g), shape_of(ne, gnb), dst));
@@ -412,6 +567,10 @@ int b200_rope(const float* x, const int64_t ne[4], const size_t nb[4], const int
     if (mode != 0 && mode != 2) return B200_E_UNSUPPORTED;
     const float theta_scale = powf(freq_base, -2.0f / (float)n_dims);   // the host libm's, as ggml's
     const int64_t n = (ne[0] / 2) * ne[1] * ne[2] * ne[3];
+    if (n_dims / 2 <= ROPE_MAX_HALF)
+        return done(launch_pdl(rope_token_kernel, dim3((unsigned)std::min<int64_t>(ne[2] * ne[3], 148 * 8)), dim3(256), 0,
+                               static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), pos,
+                               n_dims, mode == 2 ? 1 : 0, theta_scale, freq_scale, attn_factor, dst));
     return done(launch_pdl(rope_kernel, dim3((unsigned)grid_for(n, 256)), dim3(256), 0,
                            static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), pos,
                            n_dims, mode == 2 ? 1 : 0, theta_scale, freq_scale, attn_factor, dst));
@@ -443,6 +602,19 @@ int b200_cpy(int src_type, const void* src, const int64_t sne[4], const size_t s
         if (!contiguous || nelem(sne) != nelem(dne)) return B200_E_INVALID;
     }
     const int64_t n = nelem(sne);
+    if (src_type == 0 && dst_type == 1 && dense_f32(src, sne, snb) && (reinterpret_cast<uintptr_t>(dst) & 7u) == 0) {
+        // the destination dense f16 with src's element order (same shape and contiguous, or contiguous)
+        bool d_dense = true;
+        size_t next = 2;
+        for (int i = 0; i < 4; i++) {
+            if (dne[i] != 1 && dnb[i] != next) d_dense = false;
+            next *= (size_t)dne[i];
+        }
+        if (d_dense)
+            return done(launch_pdl(cpy_f32_f16_dense_kernel, dim3((unsigned)grid_for(n / 4, 256)), dim3(256), 0,
+                                   static_cast<cudaStream_t>(stream), static_cast<const float4*>(src), n / 4,
+                                   static_cast<uint2*>(dst)));
+    }
     return done(launch_pdl(cpy_kernel, dim3((unsigned)grid_for(n, 256)), dim3(256), 0,
                            static_cast<cudaStream_t>(stream), src_type, static_cast<const char*>(src),
                            shape_of(sne, snb), dst_type, static_cast<char*>(dst), shape_of(dne, dnb), same ? 1 : 0));

@@ -334,3 +334,56 @@ def test_glue_chain_through_graph_compute(cuda):
     assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
     assert float(p.stdout.split("CHAIN")[1].split()[0]) <= GLUE_TOL
     assert "HOSTCPY ok" in p.stdout
+
+
+def test_dense_fast_paths_match_the_general_kernels(cuda):
+    """Dense f32 operands take 16-byte-access kernels without per-element index arithmetic; the same
+    values laid out with a row pitch wider than the row take the general strided kernels. Both
+    must give the same bits (the same f32 operation per element), and match ggml's definitions."""
+    import torch
+    import ggml_b200 as g
+    lib = g.lib()
+    rng = np.random.default_rng(21)
+    R, C = 96, 1024
+    x = rng.standard_normal((R, C)).astype(np.float32)
+    y = rng.standard_normal((R, C)).astype(np.float32)
+    w = rng.standard_normal(C).astype(np.float32)
+    xd, yd, wd = (torch.from_numpy(v).cuda() for v in (x, y, w))
+    wide = torch.zeros((R, 2 * C), dtype=torch.float32, device="cuda")
+    wide[:, :C] = xd
+    xs = wide[:, :C]                                   # the same values, row pitch 2C: strided
+    wide2 = torch.zeros((R, 2 * C), dtype=torch.float32, device="cuda")
+    wide2[:, :C] = yd
+    ys = wide2[:, :C]
+
+    def run(fn, *args):
+        out = torch.empty((R, C), dtype=torch.float32, device="cuda")
+        assert fn(*args, _ptr(out), None) == 0
+        torch.cuda.synchronize()
+        return out.cpu().numpy()
+
+    for op, want in ((0, x + y), (1, x * y), (2, x / y)):
+        d = run(lib.b200_binary, op, _ptr(xd), *_shape(xd), _ptr(yd), *_shape(yd))
+        st = run(lib.b200_binary, op, _ptr(xs), *_shape(xs), _ptr(ys), *_shape(ys))
+        assert np.array_equal(d.view(np.uint32), st.view(np.uint32)) and np.array_equal(d, want)
+    wne, wnb = _shape(wd)
+    for op, want in ((0, x + w), (1, x * w)):      # the norm weight: one row repeated
+        d = run(lib.b200_binary, op, _ptr(xd), *_shape(xd), _ptr(wd), wne, wnb)
+        st = run(lib.b200_binary, op, _ptr(xs), *_shape(xs), _ptr(wd), wne, wnb)
+        assert np.array_equal(d.view(np.uint32), st.view(np.uint32)) and np.array_equal(d, want)
+    d = run(lib.b200_silu, _ptr(xd), *_shape(xd))
+    st = run(lib.b200_silu, _ptr(xs), *_shape(xs))
+    assert np.array_equal(d.view(np.uint32), st.view(np.uint32)) and rel_err(d, oracle.silu(x)) <= GLUE_TOL
+    ne, nb = _shape(xd)
+    d = run(lib.b200_swiglu, _ptr(xd), nb, _ptr(yd), _shape(yd)[1], ne)
+    st = run(lib.b200_swiglu, _ptr(xs), _shape(xs)[1], _ptr(ys), _shape(ys)[1], _shape(xs)[0])
+    assert np.array_equal(d.view(np.uint32), st.view(np.uint32)) and rel_err(d, oracle.swiglu(x, y)) <= GLUE_TOL
+    d = run(lib.b200_rms_norm, _ptr(xd), *_shape(xd), ctypes.c_float(1e-5))
+    st = run(lib.b200_rms_norm, _ptr(xs), *_shape(xs), ctypes.c_float(1e-5))
+    assert rel_err(d, st) <= 1e-6 and rel_err(d, oracle.rms_norm(x, 1e-5)) <= GLUE_TOL
+    # f32 -> f16, dense and strided sources
+    for src in (xd, xs):
+        h = torch.empty((R, C), dtype=torch.float16, device="cuda")
+        assert lib.b200_cpy(0, _ptr(src), *_shape(src), 1, _ptr(h), *_shape(h), None) == 0
+        torch.cuda.synchronize()
+        assert np.array_equal(h.cpu().numpy().view(np.uint16), x.astype(np.float16).view(np.uint16))
