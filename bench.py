@@ -60,8 +60,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["gemm", "gemv", "moe", "fa", "glue", "layer", "crossover"], default="gemm",
-                    help="gemm: the headline MUL_MAT sweep (default); gemv: the sweep's Q4_K weights at decode "
-                         "size (M = --decode-m, b200_mul_mat_vec); moe: the MUL_MAT_ID layer of "
+                    help="gemm: the headline MUL_MAT sweep (default); gemv: the sweep's weights at decode "
+                         "size (M = --decode-m, --decode-type, b200_mul_mat_vec); moe: the MUL_MAT_ID layer of "
                          "BASELINE configs[3], expert-parallel over the ranks; fa: the FLASH_ATTN_EXT "
                          "prefill of configs[2]; glue: a layer's glue ops and the MoE router at the "
                          "headline's prefill shapes (HBM-bound kernels, GB/s); layer: configs[4]'s Llama-3-8B "
@@ -69,8 +69,10 @@ def parse():
                          "MUL_MAT with host tensors beats the host CPU")
     ap.add_argument("--layers", type=int, default=8,
                     help="gemm workload: layers (distinct weight copies) the sweep runs through per step")
+    ap.add_argument("--decode-type", choices=["q4_k", "q6_k", "q8_0"], default="q4_k",
+                    help="gemv workload: weight type")
     ap.add_argument("--decode-m", type=int, default=1,
-                    help="gemv workload: token rows per step (1..8)")
+                    help="gemv workload: token rows per step (1..32)")
     ap.add_argument("--shard", action="store_true",
                     help="gemm workload on several GPUs: split every weight's rows across the ranks "
                          "(strong scaling), the output all-gathered by the GEMM epilogue's stores into "
@@ -782,9 +784,10 @@ def run_fa(args):
 
 
 def run_gemv(args):
-    """Decode-size MUL_MAT (b200_mul_mat_vec): the three Q4_K weights of the headline sweep against
-    M = --decode-m token rows, L2 flushed before every step. value = Q4_K weight bytes streamed per
-    second (the kernel's roofline is HBM: each weight byte is read once)."""
+    """Decode-size MUL_MAT (b200_mul_mat_vec): the three weights of the headline sweep, quantized to
+    --decode-type, against M = --decode-m token rows, L2 flushed before every step. value = weight
+    bytes streamed per second (the kernel's roofline is HBM: each weight byte is read once); the
+    per-shape times (activation prep + weight-streaming kernel, CUDA events) are in config."""
     import numpy as np
     import torch
     import ggml_b200 as g
@@ -794,15 +797,18 @@ def run_gemv(args):
     dev = torch.device("cuda", local)
     g.lib()
     M = args.decode_m
+    wtype = {"q4_k": g.Q4_K, "q6_k": g.Q6_K, "q8_0": g.Q8_0}[args.decode_type]
+    tname = args.decode_type.upper()
     rng = np.random.default_rng(0xB200)
-    packed, acts, outs, wss = [], [], [], []
+    packed, acts, outs, wss, sizes = [], [], [], [], []
     wbytes = 0
     for (k, n) in SHAPES:
         w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02))
-        raw = torch.from_numpy(quants.quantize(WTYPE, w).reshape(-1)).to(dev)
-        p = torch.empty(g.weight_packed_size(WTYPE, n, k), dtype=torch.uint8, device=dev)
-        g.weight_pack(WTYPE, raw, n, k, p)
+        raw = torch.from_numpy(quants.quantize(wtype, w).reshape(-1)).to(dev)
+        p = torch.empty(g.weight_packed_size(wtype, n, k), dtype=torch.uint8, device=dev)
+        g.weight_pack(wtype, raw, n, k, p)
         packed.append(p)
+        sizes.append(p.numel())
         wbytes += p.numel()
         acts.append(torch.from_numpy(rng.standard_normal((M, k)).astype(np.float32)).to(dev))
         outs.append(torch.empty((M, n), dtype=torch.float32, device=dev))
@@ -811,10 +817,14 @@ def run_gemv(args):
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def step():
+    def step(evs=None):
         for i, (k, n) in enumerate(SHAPES):
-            g.check(g.mul_mat_vec(WTYPE, packed[i], n, k, acts[i], M, outs[i], wss[i], err, stream=stream),
+            if evs:
+                evs[i].record(stream)
+            g.check(g.mul_mat_vec(wtype, packed[i], n, k, acts[i], M, outs[i], wss[i], err, stream=stream),
                     "mul_mat_vec")
+        if evs:
+            evs[len(SHAPES)].record(stream)
 
     for _ in range(args.warmup):
         flush.zero_()
@@ -827,27 +837,29 @@ def run_gemv(args):
     for _ in range(args.steps):
         flush.zero_()
         torch.cuda._sleep(1000000)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        step()
-        e1.record(stream)
-        ts.append((e0, e1))
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(SHAPES) + 1)]
+        step(evs)
+        ts.append(evs)
     torch.cuda.synchronize()
     clocks = sampler.stop() if sampler else None
     if int(err.item()) != 0:
         raise SystemExit(f"device error {int(err.item())}")
-    ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in ts)
+    ms = statistics.median(evs[0].elapsed_time(evs[-1]) for evs in ts)
+    per = {}
+    for i, (k, n) in enumerate(SHAPES):
+        us = statistics.median(evs[i].elapsed_time(evs[i + 1]) for evs in ts) * 1e3
+        per[f"{k}x{n}"] = {"us": us, "GB/s": sizes[i] / (us / 1e6) / 1e9}
     if rank == 0:
         peaks, src = measured_peaks()
         gbs = wbytes / (ms / 1e3) / 1e9
         peak = float(peaks.get("hbm_gbs", 6650.0))
-        line = {"metric": "decode MUL_MAT GB/s of Q4_K weight streamed (b200_mul_mat_vec)", "value": gbs,
+        line = {"metric": f"decode MUL_MAT GB/s of {tname} weight streamed (b200_mul_mat_vec)", "value": gbs,
                 "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
                 "higher_is_better": True, "scaling": "replicas only", "vs_baseline": None,
-                "dtype": "f16 activations x Q4_K weights, fp32 accumulate", "data": "synthetic",
-                "config": {"workload": f"the Q4_K weights of BASELINE configs[1] at M={M} token rows, one op per "
-                                       "shape per step", "weight_bytes_per_step": wbytes,
-                           "tokens_per_s": M / (ms / 1e3),
+                "dtype": f"f16 activations x {tname} weights, fp32 accumulate", "data": "synthetic",
+                "config": {"workload": f"the weights of BASELINE configs[1] as {tname} at M={M} token rows, one op "
+                                       "per shape per step", "weight_bytes_per_step": wbytes,
+                           "tokens_per_s": M / (ms / 1e3), "per_shape": per,
                            "l2": "flushed before every timed step (256 MiB memset), outside the timed events",
                            "median_of_steps": True},
                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,

@@ -133,7 +133,7 @@ bool flash_attn_unmasked() {
     static const bool v = knob_int("B200_FLASH_ATTN_UNMASKED", 0) > 0;
     return v;
 }
-// Decode-size MUL_MAT (M <= 8) over Q4_K weights on the GPU (b200_mul_mat_vec). Off by default:
+// Decode-size MUL_MAT (M <= 32, Q4_K / Q6_K / Q8_0) on the GPU (b200_mul_mat_vec). Off by default:
 // the reference leaves M below its offload threshold on the CPU; B200_DECODE=1 claims it.
 bool decode_on() {
     static const bool v = knob_on("B200_DECODE", false);
@@ -924,8 +924,10 @@ extern "C" bool ggml_backend_b200_supports_op(const b200_tensor* op) {
                               (!aq || K % blck_size(a->type) == 0) && K % 32 == 0 && N % 16 == 0 && K >= 64 &&
                               N >= 64;
             if (base && M >= (aq ? min_m_quant() : min_m())) return true;
-            // decode (opt-in): Q4_K weights against 1..8 token rows, one 2-D activation
-            return base && decode_on() && a->type == T_Q4_K && M >= 1 && M <= 8 && bb->ne[2] == 1 && bb->ne[3] == 1;
+            // decode (opt-in): Q4_K / Q6_K / Q8_0 weights against 1..32 token rows below the floor, one
+            // 2-D activation (b200_mul_mat_vec)
+            return base && decode_on() && (a->type == T_Q4_K || a->type == T_Q6_K || a->type == T_Q8_0) && M >= 1 &&
+                   M <= 32 && bb->ne[2] == 1 && bb->ne[3] == 1;
         }
         case B200_OP_MUL_MAT_ID: {
             const int mode = moe_mode();
@@ -1077,11 +1079,16 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
         stg.outs.push_back(d);
         need_ws = std::max(need_ws, b200_gemm_packed_workspace_size(kernel_wtype(d->src[0]->type), M, d->src[0]->ne[1], K));
     }
-    // decode-size M (claimed only under B200_DECODE, Q4_K): the weight-streaming kernel per member
-    const bool decode = M < min_m_quant() && M <= 8;
-    if (decode)
-        for (int g = 0; g < ng; g++)
-            need_ws = std::max(need_ws, b200_mul_mat_vec_workspace_size(M, nodes[g]->src[0]->ne[1], K));
+    // decode-size M (claimed only under B200_DECODE, quantized weights): the weight-streaming kernel
+    // for those members, the GEMM (after one shared activation pack) for the rest
+    std::vector<char> dec(ng, 0);
+    bool any_dec = false, any_gemm = false;
+    for (int g = 0; g < ng; g++) {
+        dec[g] = M < min_m_quant() && M <= 32 && kt[g] != T_F16;   // F32 / BF16 weights run as F16
+        any_dec = any_dec || dec[g];
+        any_gemm = any_gemm || !dec[g];
+        if (dec[g]) need_ws = std::max(need_ws, b200_mul_mat_vec_workspace_size(M, nodes[g]->src[0]->ne[1], K));
+    }
     const size_t a16_bytes = ((size_t)M * K * 2 + 255) & ~(size_t)255;
     const size_t sc_bytes = ((size_t)M * 4 + 255) & ~(size_t)255;
     need_ws = ((need_ws + 255) & ~(size_t)255) + a16_bytes + sc_bytes;
@@ -1100,20 +1107,20 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
     for (int64_t i3 = 0; i3 < ne13; i3++) {
         for (int64_t i2 = 0; i2 < ne12; i2++) {
             const float* A = reinterpret_cast<const float*>(a_base + i3 * src1->nb[3] + i2 * src1->nb[2]);
-            if (decode) {
-                for (int g = 0; g < ng; g++) {
-                    const b200_tensor* d = nodes[g];
-                    const int64_t N = d->src[0]->ne[1];
-                    float* C = reinterpret_cast<float*>(d_base[g] + i3 * d->nb[3] + i2 * d->nb[2]);
-                    const int rc = b200_mul_mat_vec(kt[g], wdev[g], N, K, A, (int64_t)(src1->nb[1] / 4), M, C,
-                                                    (int64_t)(d->nb[1] / 4), gws, gws_bytes, b->dev_err, b->stream);
-                    if (rc != B200_OK) return rc;
-                }
-                continue;
+            for (int g = 0; g < ng; g++) {
+                if (!dec[g]) continue;
+                const b200_tensor* d = nodes[g];
+                const int64_t N = d->src[0]->ne[1];
+                float* C = reinterpret_cast<float*>(d_base[g] + i3 * d->nb[3] + i2 * d->nb[2]);
+                const int rc = b200_mul_mat_vec(kt[g], wdev[g], N, K, A, (int64_t)(src1->nb[1] / 4), M, C,
+                                                (int64_t)(d->nb[1] / 4), gws, gws_bytes, b->dev_err, b->stream);
+                if (rc != B200_OK) return rc;
             }
+            if (!any_gemm) continue;
             int rc = b200_act_pack(A, (int64_t)(src1->nb[1] / 4), M, K, a16, scales, b->stream);
             if (rc != B200_OK) return rc;
             for (int g = 0; g < ng; g++) {
+                if (dec[g]) continue;
                 const b200_tensor* d = nodes[g];
                 const b200_tensor* a = d->src[0];
                 const int64_t N = a->ne[1];
@@ -1128,8 +1135,10 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
         }
     }
     if (!op_outputs_done(b, stg.outs, d_base)) return B200_E_CUDA;
-    if (decode) b->route_ops["decode"] += ng;
-    else if (ng > 1) b->route_ops["fused"]++;
+    if (any_dec) b->route_ops["decode"] += std::count(dec.begin(), dec.end(), (char)1);
+    if (!any_gemm) {
+        // every member ran on the decode kernel
+    } else if (ng > 1) b->route_ops["fused"]++;
     else b->route_ops[route_name(kt[0])]++;
     return B200_OK;
 }

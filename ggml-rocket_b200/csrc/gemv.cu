@@ -1,6 +1,8 @@
-// Decode-size MUL_MAT (M = 1..8 token rows) over Q4_K weights: a weight-streaming kernel whose
-// dot products run on the warp-level tensor-core MMA, for the shapes the tcgen05 GEMM's 128-row
-// tiles cannot fill.
+// Decode-size MUL_MAT (b200_mul_mat_vec). This file holds the row-block kernels for Q4_K weights
+// at M = 1..8 token rows, the case they stream fastest; every other weight type (Q6_K, Q8_0) and
+// row count (up to 32) runs on the tiled kernel of gemv_tiles.cu, behind the same entry point.
+// Both are weight-streaming kernels whose dot products run on the warp-level tensor-core MMA, for
+// the shapes the tcgen05 GEMM's 128-row tiles cannot fill.
 //
 // dst[m, n] = sum_k a[m, k] * W[n, k], W the packed (native) Q4_K rows. With M this small the op
 // is bound by reading W once from HBM; on the CUDA cores alone a 4-bit weight costs more issue
@@ -12,7 +14,8 @@
 //   * the sub-block minimum term dmin * sum_j m_j * sum(a over sub-block j) is one more MMA per
 //     super-block, with the activation sums split into fp16 (hi, lo) pairs;
 //   * per super-block: acc += s * (d * C - dmin * Cmin) in fp32, s the activation block scale;
-//   * two work schedules (B200_GEMV_SCHEDULE): "rows" (default), one CTA per 16 weight rows whose
+//   * work schedules (B200_GEMV_SCHEDULE; "tiles" sends this case to gemv_tiles.cu too): "rows"
+//     (default), one CTA per 16 weight rows whose
 //     8 warps split the super-blocks into contiguous ranges, each streaming its 16 x 144-byte
 //     super-block columns through a 4-deep cp.async ring, partials added in warp order; and
 //     "stream", a one-wave grid whose warps each take an equal contiguous range of the whole
@@ -50,7 +53,6 @@ constexpr int GV_PIECES = GV_STAGE / 16;         // 16-byte cp.async copies per 
 constexpr int GV_SMEM = GV_WARPS * GV_STAGES * GV_STAGE;                              // stream schedule
 constexpr int GV_SMEM_ROWS = GV_WARPS * GV_STAGES * GV_STAGE + GV_WARPS * GV_ROWS * 8 * 4;   // + reduction
 constexpr int GV_MMAX = 8;                       // token rows per call (the MMA's N)
-constexpr bool GV_DEFAULT_STREAM = false;        // default schedule: rows
 
 // ---- small PTX helpers ---------------------------------------------------------------------
 
@@ -528,15 +530,32 @@ static int gv_sm_count() {
     return sms[dev];
 }
 
-// Which schedule runs: B200_GEMV_SCHEDULE = rows | stream (read once per process).
-static bool gv_stream_schedule() {
-    static const bool v = [] {
+// Which kernel runs Q4_K at M <= 8 (read once per process): B200_GEMV_SCHEDULE = rows | stream
+// (this file's kernels for every such M) | tiles (the tiled kernel of gemv_tiles.cu, which runs
+// every other type and row count). Unset: rows for M <= GV_ROWS_DEFAULT_MMAX, tiles above, the
+// crossover measured on B200 (bench.py --workload gemv, the headline's three Q4_K weights: rows
+// 1209 / 1068 / 957 GB/s at M = 4 / 6 / 8, tiles 1068-1069 GB/s at each).
+constexpr int GV_ROWS_DEFAULT_MMAX = 5;
+enum GvSchedule { GV_DEFAULT_SCHEDULE, GV_ROWS_SCHEDULE, GV_STREAM_SCHEDULE, GV_TILES_SCHEDULE };
+static GvSchedule gv_schedule() {
+    static const GvSchedule v = [] {
         const char* e = getenv("B200_GEMV_SCHEDULE");
-        if (e && strcmp(e, "stream") == 0) return true;
-        if (e && strcmp(e, "rows") == 0) return false;
-        return GV_DEFAULT_STREAM;
+        if (e && strcmp(e, "stream") == 0) return GV_STREAM_SCHEDULE;
+        if (e && strcmp(e, "tiles") == 0) return GV_TILES_SCHEDULE;
+        if (e && strcmp(e, "rows") == 0) return GV_ROWS_SCHEDULE;
+        return GV_DEFAULT_SCHEDULE;
     }();
     return v;
+}
+static bool gv_stream_schedule() { return gv_schedule() == GV_STREAM_SCHEDULE; }
+// Whether this file's row-block kernels take the call.
+static bool gv_row_kernels(int wtype, int64_t M) {
+    if (wtype != WT_Q4_K || M > GV_MMAX) return false;
+    switch (gv_schedule()) {
+        case GV_TILES_SCHEDULE: return false;
+        case GV_DEFAULT_SCHEDULE: return M <= GV_ROWS_DEFAULT_MMAX;
+        default: return true;
+    }
 }
 
 // CTAs of the one-wave grid (two per SM), never more warps than units.
@@ -551,8 +570,10 @@ extern "C" {
 
 size_t b200_mul_mat_vec_workspace_size(int64_t M, int64_t N, int64_t K) {
     using namespace b200;
-    if (M <= 0 || N <= 0 || K <= 0 || K % 256 != 0) return 0;
-    return gv_workspace(M, N, K, gv_grid(N, K) * GV_WARPS).total;
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    const size_t tiles = mul_mat_vec_tiles_workspace(M, N, K);   // 0 when M > 32
+    if (M > GV_MMAX || K % 256 != 0) return tiles;
+    return std::max(tiles, gv_workspace(M, N, K, gv_grid(N, K) * GV_WARPS).total);
 }
 
 int b200_mul_mat_vec(int wtype, const void* w_packed, int64_t N, int64_t K, const float* src1, int64_t lda, int64_t M,
@@ -560,6 +581,9 @@ int b200_mul_mat_vec(int wtype, const void* w_packed, int64_t N, int64_t K, cons
     using namespace b200;
     if (!w_packed || !src1 || !dst || !dev_err || N <= 0 || K <= 0 || M <= 0 || lda < K || ldd < N)
         return B200_E_INVALID;
+    if (!gv_row_kernels(wtype, M))
+        return mul_mat_vec_tiles(wtype, w_packed, N, K, src1, lda, M, dst, ldd, workspace, workspace_bytes, dev_err,
+                                 static_cast<cudaStream_t>(stream));
     if (wtype != WT_Q4_K || K % 256 != 0 || M > GV_MMAX || N > (1ll << 30) || K > (1 << 28) ||
         (reinterpret_cast<uintptr_t>(w_packed) & 15u) != 0)
         return B200_E_UNSUPPORTED;

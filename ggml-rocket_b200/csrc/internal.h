@@ -38,6 +38,17 @@ bool make_tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_
 bool make_tmap_2d_u16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_bytes,
                       uint32_t box_rows, uint32_t box_cols);
 size_t packed_weight_bytes(int type, int64_t N, int64_t K, size_t* plane_d_off);
+// The raw-tile tensor maps of a packed Q4_K / Q6_K / Q8_0 weight of `wrows` rows: boxes of 128
+// rows x one 256-weight super-block column (tmW, uint16 elements) and, for Q6_K, the transposed
+// d plane's 128-row box (tmD; unused otherwise).
+bool make_weight_tile_maps(int wtype, const void* w_packed, int64_t wrows, int64_t K, CUtensorMap* tmW,
+                           CUtensorMap* tmD);
+// Decode-size MUL_MAT on the tiled weight-streaming kernel (gemv_tiles.cu): Q4_K / Q6_K / Q8_0,
+// M <= 32. Same arguments and return codes as b200_mul_mat_vec.
+size_t mul_mat_vec_tiles_workspace(int64_t M, int64_t N, int64_t K);
+int mul_mat_vec_tiles(int wtype, const void* w_packed, int64_t N, int64_t K, const float* src1, int64_t lda,
+                      int64_t M, float* dst, int64_t ldd, void* workspace, size_t workspace_bytes, int* dev_err,
+                      cudaStream_t st);
 bool weight_type_supported(int type, int64_t K);
 // dst_bases / n_dst / col0: the output columns [col0, col0 + N) of every one of n_dst [M][ldd]
 // buffers (a device array of pointers, other GPUs' included) instead of dst

@@ -491,6 +491,13 @@ static bool setup_weight_maps(int wtype, const void* w_packed, int64_t wrows, in
     }
 }
 
+bool make_weight_tile_maps(int wtype, const void* w_packed, int64_t wrows, int64_t K, CUtensorMap* tmW,
+                           CUtensorMap* tmD) {
+    if (wtype != WT_Q4_K && wtype != WT_Q6_K && wtype != WT_Q8_0) return false;
+    const CUtensorMap none{};
+    return setup_weight_maps(wtype, w_packed, wrows, K, *tmW, *tmD, none);
+}
+
 template <bool GROUPED>
 cudaError_t launch_gemm_typed(int wtype, int bt, bool pair, const CUtensorMap& tmA, const CUtensorMap& tmW,
                               const CUtensorMap& tmD, const CUtensorMap& tmO, const GemmArgs& a, int grid, cudaStream_t st) {

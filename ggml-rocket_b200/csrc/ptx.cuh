@@ -205,6 +205,14 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32
                  : "memory");
 }
 
+// Untiled bulk copy global -> shared of `bytes` bytes (both addresses 16-byte aligned, bytes a
+// multiple of 16), completing as transaction bytes on the mbarrier (no multicast).
+__device__ __forceinline__ void bulk_load_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
 // 3-D tiled TMA load (no multicast).
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int32_t x, int32_t y, int32_t z) {

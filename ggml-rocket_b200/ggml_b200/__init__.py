@@ -499,7 +499,7 @@ def mul_mat_id(wtype, as_packed, K, N, n_expert, b, b_nb1, b_nb2, ne11, ids, ids
 
 
 def mul_mat_vec(wtype, w_packed, N, K, a, M, out, workspace, dev_err, lda=None, ldd=None, stream=None):
-    """Decode-size MUL_MAT (M <= 8, Q4_K): out[M, N] = a[M, K] . W^T (b200_mul_mat_vec)."""
+    """Decode-size MUL_MAT (M <= 32; Q4_K, Q6_K, Q8_0): out[M, N] = a[M, K] . W^T (b200_mul_mat_vec)."""
     return lib().b200_mul_mat_vec(wtype, _ptr(w_packed), N, K, _ptr(a), lda if lda else K, M, _ptr(out),
                                   ldd if ldd else N, _ptr(workspace), workspace.numel() * workspace.element_size(),
                                   _ptr(dev_err), _stream(stream))

@@ -135,18 +135,21 @@ int    b200_flash_attn_ext(const float * q, int64_t q_nb1, int64_t q_nb2,
                            float scale, float max_bias, float softcap,
                            void * workspace, size_t workspace_bytes, int * dev_err, void * stream);
 
-/* ---- decode-size MUL_MAT (M = 1..8) over Q4_K weights ---------------------------------------
+/* ---- decode-size MUL_MAT (M = 1..32) over Q4_K, Q6_K and Q8_0 weights ----------------------
  * The reference leaves decode (M below its ROCKET_MIN_M) on the CPU (ggml-rocket.cpp:7424-7496);
  * this is MUL_MAT for those M on the GPU: dst[m, n] = sum_k src1[m, k] * W[n, k] with W the
- * weight as b200_weight_pack packs it (Q4_K only, 16-byte aligned), src1 f32 [M][lda], dst f32
- * [M][ldd]. Two launches: an activation prep (fp16 of src1 / s per 256-value block, s the block's
- * absmax, with the fp16 (hi, lo) sums of every 32-value sub-block) and a weight-streaming kernel
- * that decodes the weights into warp-level tensor-core MMA fragments as exact integers q*sc and
- * accumulates in fp32, each super-block scaled by d, dmin and s in fp32. The weight is split
- * into equal contiguous parts, one per warp of a one-wave grid; row blocks shared by two warps are
- * added by the last to finish, in a fixed order (results do not depend on timing). The workspace
- * (b200_mul_mat_vec_workspace_size bytes, 256-byte aligned) holds the prepared activations, the
- * partial sums and their counters; calls sharing one must not overlap on the GPU. */
+ * weight as b200_weight_pack packs it (16-byte aligned; K a multiple of 256, of 32 for Q8_0),
+ * src1 f32 [M][lda], dst f32 [M][ldd]. Two launches: an activation prep (fp16 of src1 / s per
+ * 256-value block, s the block's absmax, with the per-block sums the arithmetic needs) and a
+ * weight-streaming kernel that decodes the weights into warp-level tensor-core MMA fragments as
+ * exact integers and accumulates in fp32. Q4_K at M <= 8 streams 16-row blocks per CTA; every
+ * other case takes 128-row x 256-weight tiles by TMA, one persistent CTA per SM over equal
+ * contiguous ranges of tiles, 8-token column tiles sharing each decoded fragment. Rows split
+ * between CTAs are added by the last to finish, in a fixed order (results do not depend on
+ * timing). The workspace (b200_mul_mat_vec_workspace_size bytes, 256-byte aligned, a bound for
+ * every weight type) holds the prepared activations, the partial sums and their counters; calls
+ * sharing one must not overlap on the GPU. Returns B200_E_UNSUPPORTED for other weight types,
+ * M > 32 or a K the type does not tile. */
 size_t b200_mul_mat_vec_workspace_size(int64_t M, int64_t N, int64_t K);
 int    b200_mul_mat_vec(int wtype, const void * w_packed, int64_t N, int64_t K, const float * src1, int64_t lda,
                         int64_t M, float * dst, int64_t ldd, void * workspace, size_t workspace_bytes,

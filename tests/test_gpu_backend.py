@@ -195,24 +195,26 @@ be = g.Backend()
 rng = np.random.default_rng(7)
 K = 4096
 worst, n = 0.0, 0
-for M, Ns in ((1, (4096,)), (4, (4096, 1024, 1024)), (8, (14336, 14336))):
+Q4, Q6, Q8 = g.Q4_K, g.Q6_K, g.Q8_0
+for M, Ws in ((1, ((Q4, 4096),)), (4, ((Q4, 4096), (Q8, 1024), (Q6, 1024))), (8, ((Q4, 14336), (Q4, 14336))),
+              (12, ((Q6, 4096), (Q8, 2048), (Q4, 1024)))):
     a = rng.standard_normal((M, K)).astype(np.float32)
     x = g.make_tensor(g.F32, [K, M], a, name="x")
     keep, nodes = [], []
-    for i, N in enumerate(Ns):
-        raw = quants.quantize(g.Q4_K, (rng.standard_normal((N, K)) * 0.02).astype(np.float32))
-        w = g.make_tensor(g.Q4_K, [K, N], raw, name=f"blk.{M}.w{i}")
+    for i, (t, N) in enumerate(Ws):
+        raw = quants.quantize(t, (rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+        w = g.make_tensor(t, [K, N], raw, name=f"blk.{M}.w{i}")
         out = np.full((M, N), np.nan, np.float32)
         d = g.make_tensor(g.F32, [N, M], out, op=g.OP_MUL_MAT, srcs=[w, x])
         assert g.supports_op(d)
-        keep.append((raw, w, out, d, N))
+        keep.append((t, raw, w, out, d, N))
         nodes.append(d)
     assert be.graph_compute(nodes) == g.STATUS_SUCCESS
-    for raw, w, out, d, N in keep:
-        e = rel_err(out, oracle.mul_mat(g.Q4_K, raw, N, K, a))
-        print("CASE", M, N, e)
+    for t, raw, w, out, d, N in keep:
+        e = rel_err(out, oracle.mul_mat(t, raw, N, K, a))
+        print("CASE", t, M, N, e)
         worst = max(worst, e)
-    n += len(Ns)
+    n += len(Ws)
 assert be.route_ops("decode") == n, be.route_ops("decode")
 assert be.cpu_fallbacks() == 0 and be.device_errors() == 0
 be.close()
@@ -221,8 +223,9 @@ print("DECODE_WORST", worst)
 
 
 def test_backend_decode_route(cuda):
-    """B200_DECODE=1 (read once per process, so in a child): Q4_K MUL_MATs with M = 1..8 --
-    one op, and shared-src1 groups -- run on the weight-streaming kernel through graph_compute,
+    """B200_DECODE=1 (read once per process, so in a child): Q4_K / Q6_K / Q8_0 MUL_MATs below the
+    floor (M = 1, 4, 8, 12) -- one op, and shared-src1 groups mixing the types -- run on the
+    weight-streaming kernels through graph_compute,
     within the decode kernel's bound against the oracle (fp16 activations, exact weights)."""
     import os
     import subprocess

@@ -186,6 +186,8 @@ print(json.dumps({"q4k_m256": t.supported(256, 128, 256, 12), "q4k_m512": t.supp
                   "f16_m16": t.supported(256, 128, 16, 1), "f16_m3": t.supported(256, 128, 3, 1),
                   "q4k_m1": t.supported(256, 128, 1, 12), "q4k_m8": t.supported(256, 128, 8, 12),
                   "q4k_m9": t.supported(256, 128, 9, 12), "q8_m1": t.supported(256, 128, 1, 8),
+                  "q6k_m12": t.supported(256, 128, 12, 14), "f16_m1": t.supported(256, 128, 1, 1),
+                  "q4k_m40": t.supported(256, 128, 40, 12),
                   "moe": t.moe(2048, 8, 128), "fa_unmasked": t.fa(64, 256, 8, 1024, 2, masked=False),
                   "fa": t.fa(64, 256, 8, 1024, 2), "glue": {k: t.glue(k) for k in t.GLUE_KINDS}}))
 """
@@ -232,8 +234,10 @@ def test_knobs_in_children():
                          "get_rows_q4k": False, "get_rows_f16": True, "cpy_f16": True, "soft_max": True,
                          "soft_max_mask": False, "argsort": True, "argsort_wide": False, "sum_rows": True,
                          "div": True}
-    r = child({"B200_DECODE": "1"})                # Q4_K at M = 1..8 only
-    assert r["q4k_m1"] and r["q4k_m8"] and not r["q4k_m9"] and not r["q8_m1"]
+    r = child({"B200_DECODE": "1"})                # quantized weights below the floor, M <= 32
+    assert r["q4k_m1"] and r["q4k_m8"] and r["q4k_m9"] and r["q8_m1"] and r["q6k_m12"] and not r["f16_m1"]
+    r = child({"B200_DECODE": "1", "B200_MIN_M_QUANT": "64"})
+    assert r["q4k_m9"] and not r["q4k_m40"]        # M = 33 .. 63: neither the decode kernel nor the GEMM
 
 
 def test_moe_ledger_budget_in_child():
