@@ -325,6 +325,47 @@ __global__ void get_rows_kernel(int f16, const char* __restrict__ src, Shape4 ss
     }
 }
 
+// One CTA per output row (i10, i11, i12): the index is read once, the row copied with 8-byte
+// (4 x f16) or 16-byte (4 x f32) loads when the source rows are contiguous and aligned (vec), else
+// element by element. Same values and error behaviour as get_rows_kernel.
+__global__ void __launch_bounds__(256) get_rows_row_kernel(int f16, int vec, const char* __restrict__ src, Shape4 ss,
+                                                           const char* __restrict__ idx, Shape4 si,
+                                                           float* __restrict__ dst, int* err) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t orow = blockIdx.x;   // i10 + ne[0] * (i11 + ne[1] * i12)
+    const int64_t i10 = orow % si.ne[0], i11 = (orow / si.ne[0]) % si.ne[1], i12 = orow / (si.ne[0] * si.ne[1]);
+    const int64_t r = *reinterpret_cast<const int32_t*>(idx + i10 * si.nb[0] + i11 * si.nb[1] + i12 * si.nb[2]);
+    const int64_t n0 = ss.ne[0];
+    float* out = dst + orow * n0;
+    if (r < 0 || r >= ss.ne[1]) {
+        if (threadIdx.x == 0) atomicCAS(err, 0, ERR_BAD_INDEX);
+        for (int64_t i = threadIdx.x; i < n0; i += blockDim.x) out[i] = 0.0f;
+        return;
+    }
+    const char* row = src + r * ss.nb[1] + i11 * ss.nb[2] + i12 * ss.nb[3];
+    if (vec) {
+        float4* o4 = reinterpret_cast<float4*>(out);
+        if (f16) {
+            const uint2* p = reinterpret_cast<const uint2*>(row);
+            for (int64_t i = threadIdx.x; i < n0 / 4; i += blockDim.x) {
+                const uint2 w = __ldg(p + i);
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+                o4[i] = make_float4(a.x, a.y, b.x, b.y);
+            }
+        } else {
+            const float4* p = reinterpret_cast<const float4*>(row);
+            for (int64_t i = threadIdx.x; i < n0 / 4; i += blockDim.x) o4[i] = __ldg(p + i);
+        }
+        return;
+    }
+    for (int64_t i = threadIdx.x; i < n0; i += blockDim.x) {
+        const char* p = row + i * ss.nb[0];
+        out[i] = f16 ? __half2float(*reinterpret_cast<const __half*>(p)) : *reinterpret_cast<const float*>(p);
+    }
+}
+
 // ---- CPY: element k of src (i0 fastest) -> element k of dst, f32 / f16 either side -------------
 // dst either has src's shape (any strides) or is contiguous with src's element count.
 __global__ void cpy_kernel(int src_f16, const char* __restrict__ src, Shape4 ss, int dst_f16, char* __restrict__ dst,
@@ -394,6 +435,50 @@ __global__ void __launch_bounds__(SM_THREADS) soft_max_kernel(const char* __rest
     }
 }
 
+// Rows of at most 32 * SMW_MAX values (the MoE router's 64-256 experts): one warp per row, the
+// row held in registers, max and the double sum reduced with shuffles; the same per-element
+// arithmetic as soft_max_kernel, the sum in another order.
+constexpr int SMW_MAX = 32;
+template <int E>
+__global__ void __launch_bounds__(256) soft_max_warp_kernel(const char* __restrict__ x, Shape4 s, float scale,
+                                                           float* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t rows = s.ne[1] * s.ne[2] * s.ne[3];
+    const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const int64_t i1 = r % s.ne[1], i2 = (r / s.ne[1]) % s.ne[2], i3 = r / (s.ne[1] * s.ne[2]);
+    const char* row = x + i1 * s.nb[1] + i2 * s.nb[2] + i3 * s.nb[3];
+    float* out = dst + r * s.ne[0];
+    const int n = (int)s.ne[0];
+    float w[E];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < E; j++) {
+        const int i = lane + 32 * j;
+        w[j] = i < n ? __fmul_rn(*reinterpret_cast<const float*>(row + (int64_t)i * s.nb[0]), scale) : -INFINITY;
+        mx = fmaxf(mx, w[j]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    double sum = 0.0;
+#pragma unroll
+    for (int j = 0; j < E; j++) {
+        const int i = lane + 32 * j;
+        w[j] = i < n ? expf(__fsub_rn(w[j], mx)) : 0.0f;
+        sum += (double)w[j];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float inv = (float)(1.0 / sum);
+#pragma unroll
+    for (int j = 0; j < E; j++) {
+        const int i = lane + 32 * j;
+        if (i < n) out[i] = __fmul_rn(w[j], inv);
+    }
+}
+
 // ---- ARGSORT of every row (ne[0] <= 1024): a bitonic sort of (value, index) pairs in shared
 // memory, ties broken by the smaller index (ggml's std::sort leaves the order of ties open) -----
 constexpr int AS_MAX = 1024;
@@ -449,6 +534,84 @@ __global__ void __launch_bounds__(AS_MAX / 2) argsort_kernel(const char* __restr
         int32_t* out = dst + r * s.ne[0];
         for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = si[i];
         __syncthreads();
+    }
+}
+
+// Rows of at most ASW_MAX entries (the MoE router's expert counts): one warp per row, the
+// bitonic network over n2w = max(32, n2) positions held in registers (position j * 32 + lane in
+// slot j of lane), exchanges across lanes by shuffles, within a lane by register swaps. Each entry
+// is one 64-bit key whose unsigned order is argsort_kernel's total order: the upper word ranks the
+// value (order-preserving bits of the float in the requested direction, -0 as +0; every NaN
+// above every number; padding above all), the lower word is the index (ties by index). Same
+// result as argsort_kernel.
+constexpr int ASW_MAX = 256;
+__device__ __forceinline__ uint64_t as_key(float v, int index, bool pad, bool desc) {
+    uint32_t hi;
+    if (pad) hi = 0xFFFFFFFFu;
+    else if (isnan(v)) hi = 0xFFFFFFFEu;
+    else {
+        const uint32_t bits = __float_as_uint(v == 0.0f ? 0.0f : v);
+        const uint32_t u = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);   // ascending order
+        hi = desc ? ~u : u;   // numbers stay below 0xFF800001 either way
+    }
+    return ((uint64_t)hi << 32) | (uint32_t)index;
+}
+template <int E>
+__global__ void __launch_bounds__(256) argsort_warp_kernel(const char* __restrict__ x, Shape4 s, int desc,
+                                                          int32_t* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t rows = s.ne[1] * s.ne[2] * s.ne[3];
+    const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const int64_t i1 = r % s.ne[1], i2 = (r / s.ne[1]) % s.ne[2], i3 = r / (s.ne[1] * s.ne[2]);
+    const char* row = x + i1 * s.nb[1] + i2 * s.nb[2] + i3 * s.nb[3];
+    const int n = (int)s.ne[0];
+    constexpr int N2 = 32 * E;
+    uint64_t key[E];
+#pragma unroll
+    for (int j = 0; j < E; j++) {
+        const int p = lane + 32 * j;
+        const float v = p < n ? *reinterpret_cast<const float*>(row + (int64_t)p * s.nb[0]) : 0.0f;
+        key[j] = as_key(v, p, p >= n, desc != 0);
+    }
+#pragma unroll
+    for (int k = 2; k <= N2; k <<= 1) {
+#pragma unroll
+        for (int d = k >> 1; d > 0; d >>= 1) {
+            if (d >= 32) {
+                // partners in the same lane: slots j and j ^ (d / 32); the lower position takes the
+                // smaller key in an ascending block, the larger in a descending one
+#pragma unroll
+                for (int j = 0; j < E; j++) {
+                    const int jj = j ^ (d >> 5);
+                    if (jj > j) {
+                        const bool up = ((lane + 32 * j) & k) == 0;
+                        const uint64_t lo = key[j] < key[jj] ? key[j] : key[jj];
+                        const uint64_t hi = key[j] < key[jj] ? key[jj] : key[j];
+                        key[j] = up ? lo : hi;
+                        key[jj] = up ? hi : lo;
+                    }
+                }
+            } else {
+                // partners in lane ^ d, same slot
+#pragma unroll
+                for (int j = 0; j < E; j++) {
+                    const uint64_t o = __shfl_xor_sync(0xffffffffu, key[j], d);
+                    const bool up = ((lane + 32 * j) & k) == 0;
+                    const bool lower = (lane & d) == 0;
+                    const bool want_small = lower == up;
+                    key[j] = want_small ? (o < key[j] ? o : key[j]) : (o < key[j] ? key[j] : o);
+                }
+            }
+        }
+    }
+    int32_t* out = dst + r * s.ne[0];
+#pragma unroll
+    for (int j = 0; j < E; j++) {
+        const int p = lane + 32 * j;
+        if (p < n) out[p] = (int32_t)(uint32_t)key[j];
     }
 }
 
@@ -584,6 +747,18 @@ int b200_get_rows(int src_type, const void* src, const int64_t sne[4], const siz
     if (src_type != 0 && src_type != 1) return B200_E_UNSUPPORTED;   // F32, F16
     if (ine[1] > sne[2] || ine[2] > sne[3]) return B200_E_INVALID;
     const int64_t n = sne[0] * ine[0] * ine[1] * ine[2];
+    const int64_t rows = ine[0] * ine[1] * ine[2];
+    if (rows > 0 && rows < (1ll << 31) && sne[0] >= 64) {
+        // rows long enough for a CTA each: the index is read once per row
+        const size_t esz = src_type == 1 ? 2 : 4;
+        const bool vec = snb[0] == esz && sne[0] % 4 == 0 && snb[1] % (4 * esz) == 0 && snb[2] % (4 * esz) == 0 &&
+                         snb[3] % (4 * esz) == 0 && (reinterpret_cast<uintptr_t>(src) & (4 * esz - 1)) == 0 &&
+                         (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+        return done(launch_pdl(get_rows_row_kernel, dim3((unsigned)rows), dim3(256), 0,
+                               static_cast<cudaStream_t>(stream), src_type, vec ? 1 : 0, static_cast<const char*>(src),
+                               shape_of(sne, snb), reinterpret_cast<const char*>(idx), shape_of(ine, inb), dst,
+                               dev_err));
+    }
     return done(launch_pdl(get_rows_kernel, dim3((unsigned)grid_for(n, 256)), dim3(256), 0,
                            static_cast<cudaStream_t>(stream), src_type, static_cast<const char*>(src),
                            shape_of(sne, snb), reinterpret_cast<const char*>(idx), shape_of(ine, inb), dst, dev_err));
@@ -624,6 +799,19 @@ int b200_soft_max(const float* x, const int64_t ne[4], const size_t nb[4], float
     using namespace b200;
     if (!x || !dst || !shape_ok(ne, nb)) return B200_E_INVALID;
     const int64_t rows = ne[1] * ne[2] * ne[3];
+    if (ne[0] <= 32 * SMW_MAX && rows < (1ll << 34)) {
+        const dim3 grid((unsigned)((rows + 7) / 8)), block(256);
+        const cudaStream_t st = static_cast<cudaStream_t>(stream);
+        const char* xp = reinterpret_cast<const char*>(x);
+        const Shape4 sh = shape_of(ne, nb);
+        const int64_t e = (ne[0] + 31) / 32;
+        if (e <= 1) return done(launch_pdl(soft_max_warp_kernel<1>, grid, block, 0, st, xp, sh, scale, dst));
+        if (e <= 2) return done(launch_pdl(soft_max_warp_kernel<2>, grid, block, 0, st, xp, sh, scale, dst));
+        if (e <= 4) return done(launch_pdl(soft_max_warp_kernel<4>, grid, block, 0, st, xp, sh, scale, dst));
+        if (e <= 8) return done(launch_pdl(soft_max_warp_kernel<8>, grid, block, 0, st, xp, sh, scale, dst));
+        if (e <= 16) return done(launch_pdl(soft_max_warp_kernel<16>, grid, block, 0, st, xp, sh, scale, dst));
+        return done(launch_pdl(soft_max_warp_kernel<32>, grid, block, 0, st, xp, sh, scale, dst));
+    }
     return done(launch_pdl(soft_max_kernel, dim3((unsigned)std::min<int64_t>(rows, 148 * 8)), dim3(SM_THREADS), 0,
                            static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), scale,
                            dst));
@@ -636,6 +824,17 @@ int b200_argsort(const float* x, const int64_t ne[4], const size_t nb[4], int de
     int n2 = 2;
     while (n2 < ne[0]) n2 <<= 1;
     const int64_t rows = ne[1] * ne[2] * ne[3];
+    if (n2 <= ASW_MAX && rows < (1ll << 34)) {
+        const dim3 grid((unsigned)((rows + 7) / 8)), block(256);
+        const cudaStream_t st = static_cast<cudaStream_t>(stream);
+        const char* xp = reinterpret_cast<const char*>(x);
+        const Shape4 sh = shape_of(ne, nb);
+        const int d = descending ? 1 : 0;
+        if (n2 <= 32) return done(launch_pdl(argsort_warp_kernel<1>, grid, block, 0, st, xp, sh, d, dst));
+        if (n2 <= 64) return done(launch_pdl(argsort_warp_kernel<2>, grid, block, 0, st, xp, sh, d, dst));
+        if (n2 <= 128) return done(launch_pdl(argsort_warp_kernel<4>, grid, block, 0, st, xp, sh, d, dst));
+        return done(launch_pdl(argsort_warp_kernel<8>, grid, block, 0, st, xp, sh, d, dst));
+    }
     const int threads = std::max(32, std::min(AS_MAX / 2, n2 / 2));
     return done(launch_pdl(argsort_kernel, dim3((unsigned)std::min<int64_t>(rows, 148 * 8)), dim3(threads), 0,
                            static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb),

@@ -199,9 +199,11 @@ def test_router_ops_soft_max_argsort_sum_rows_div(cuda):
     assert lib.b200_binary(2, _ptr(xd), ne, nb, _ptr(s), sne, snb, _ptr(q), None) == 0   # B200_BIN_DIV
     torch.cuda.synchronize()
     assert np.array_equal(q.cpu().numpy(), x / s.cpu().numpy())
-    for n in (8, 128, 1000):
+    for n in (8, 128, 200, 1000):
         v = rng.standard_normal((5, n)).astype(np.float32)
         v[:, 1] = v[:, 0]                                  # a tie: index order
+        v[1, 2], v[1, 3], v[1, 4], v[1, 5] = -0.0, 0.0, np.inf, -np.inf   # -0 ties +0; infinities
+        v[2, 3], v[2, 6] = np.nan, np.nan                  # NaNs after every number, either order
         vd = torch.from_numpy(v).cuda()
         ids = torch.empty((5, n), dtype=torch.int32, device="cuda")
         vne, vnb = _shape(vd)
