@@ -1332,6 +1332,48 @@ int do_glue(b200_backend* b, const b200_tensor* op) {
     return B200_OK;
 }
 
+// RMS_NORM `nrm` and the MUL `mul` right after it that multiplies its rows by one weight row, as
+// one launch (b200_rms_norm_mul). Fusable when the MUL reads the norm's output as src[0] and a
+// dense f32 row of ne[0] as src[1], both claimed, with the norm's shape. The norm's own output is
+// written only when something else may read it (a host tensor, or a later node's source).
+bool norm_mul_fusable(const b200_tensor* nrm, const b200_tensor* mul) {
+    if (nrm->op != B200_OP_RMS_NORM || mul->op != B200_OP_MUL || mul->src[0] != nrm) return false;
+    const b200_tensor* w = mul->src[1];
+    if (!w || w->type != T_F32 || !is_contiguous(w) || w->ne[0] != nrm->ne[0] || w->ne[1] != 1 || w->ne[2] != 1 ||
+        w->ne[3] != 1)
+        return false;
+    for (int d = 0; d < 4; d++)
+        if (mul->ne[d] != nrm->ne[d]) return false;
+    return nrm->type == T_F32 && mul->type == T_F32 && is_contiguous(nrm) && is_contiguous(mul) &&
+           ggml_backend_b200_supports_op(nrm) && ggml_backend_b200_supports_op(mul);
+}
+
+int do_rms_norm_mul(b200_backend* b, const b200_tensor* nrm, const b200_tensor* mul, bool write_norm) {
+    const b200_tensor* x = nrm->src[0];
+    const b200_tensor* w = mul->src[1];
+    OpStaging stg;
+    stg.ins = {x, w};
+    stg.outs = {mul};
+    if (write_norm) stg.outs.push_back(nrm);
+    if (!op_reserve(b, stg)) return B200_E_CUDA;
+    bool ok = true;
+    const char* sx = static_cast<const char*>(stage_in(b, x, &ok));
+    const char* sw = static_cast<const char*>(stage_in(b, w, &ok));
+    char* dm = stage_out(b, mul, false, &ok);
+    char* dn = write_norm ? stage_out(b, nrm, false, &ok) : nullptr;
+    if (!ok || !op_inputs_ready(b)) return B200_E_CUDA;
+    const int rc = b200_rms_norm_mul(reinterpret_cast<const float*>(sx), x->ne, x->nb, op_param_f32(nrm, 0),
+                                     reinterpret_cast<const float*>(sw), reinterpret_cast<float*>(dn),
+                                     reinterpret_cast<float*>(dm), b->stream);
+    if (rc != B200_OK) return rc;
+    std::vector<char*> bases{dm};
+    if (write_norm) bases.push_back(dn);
+    if (!op_outputs_done(b, stg.outs, bases)) return B200_E_CUDA;
+    b->route_ops["glue"] += 2;
+    b->route_ops["norm_mul"]++;
+    return B200_OK;
+}
+
 }  // namespace
 
 // ================================================================================================
@@ -1588,6 +1630,18 @@ int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes,
             case B200_OP_DIV: {
                 if (!ggml_backend_b200_supports_op(node)) {
                     status = B200_STATUS_FAILED;
+                    break;
+                }
+                if (fuse && i + 1 < n && !done[i + 1] && norm_mul_fusable(node, nodes[i + 1])) {
+                    bool write_norm = !node->on_device;
+                    for (int j = i + 2; j < n && !write_norm; j++)
+                        for (int k = 0; k < B200_MAX_SRC && !write_norm; k++) write_norm = nodes[j]->src[k] == node;
+                    const int rc = do_rms_norm_mul(b, node, nodes[i + 1], write_norm);
+                    if (rc != B200_OK) {
+                        logf("E", "graph_compute: fused RMS_NORM*MUL failed (%d) in node %s\n", rc, node->name);
+                        status = B200_STATUS_FAILED;
+                    }
+                    done[i + 1] = true;
                     break;
                 }
                 const int rc = do_glue(b, node);

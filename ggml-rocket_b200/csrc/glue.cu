@@ -64,8 +64,12 @@ static int grid_for(int64_t n, int threads) {
 // share in double and the CTA adds the shares in a tree: the same terms, another order.
 constexpr int RMS_THREADS = 256;
 
+// With w (a dense row of ne[0] f32, ggml's MUL of the normalised rows by one weight row fused
+// in): dst = y * w and norm_dst = y (skipped when null), each product rounded as the two
+// separate ops round it, so both outputs are bit-identical to RMS_NORM then MUL.
 __global__ void __launch_bounds__(RMS_THREADS) rms_norm_kernel(const char* __restrict__ x, Shape4 s, float eps,
-                                                               float* __restrict__ dst) {
+                                                               float* __restrict__ dst, const float* __restrict__ w,
+                                                               float* __restrict__ norm_dst) {
     grid_dep_wait();
     grid_dep_launch();
     __shared__ double red[RMS_THREADS / 32];
@@ -98,21 +102,40 @@ __global__ void __launch_bounds__(RMS_THREADS) rms_norm_kernel(const char* __res
         __syncthreads();
         double tot = 0.0;
 #pragma unroll
-        for (int w = 0; w < RMS_THREADS / 32; w++) tot += red[w];
+        for (int q = 0; q < RMS_THREADS / 32; q++) tot += red[q];
         const float mean = (float)(tot / (double)s.ne[0]);
         const float scale = 1.0f / sqrtf(__fadd_rn(mean, eps));
         float* out = dst + r * s.ne[0];
-        if (vec && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+        float* nout = norm_dst ? norm_dst + r * s.ne[0] : nullptr;
+        const bool vout = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0 &&
+                          (!w || (reinterpret_cast<uintptr_t>(w) & 15u) == 0) &&
+                          (!norm_dst || (reinterpret_cast<uintptr_t>(norm_dst) & 15u) == 0);
+        if (vec && vout) {
             const float4* r4 = reinterpret_cast<const float4*>(row);
             float4* o4 = reinterpret_cast<float4*>(out);
             for (int64_t i = threadIdx.x; i < s.ne[0] / 4; i += RMS_THREADS) {
                 const float4 v = r4[i];
-                o4[i] = make_float4(__fmul_rn(v.x, scale), __fmul_rn(v.y, scale), __fmul_rn(v.z, scale),
-                                    __fmul_rn(v.w, scale));
+                const float4 y = make_float4(__fmul_rn(v.x, scale), __fmul_rn(v.y, scale), __fmul_rn(v.z, scale),
+                                             __fmul_rn(v.w, scale));
+                if (w) {
+                    const float4 g = __ldg(reinterpret_cast<const float4*>(w) + i);
+                    o4[i] = make_float4(__fmul_rn(y.x, g.x), __fmul_rn(y.y, g.y), __fmul_rn(y.z, g.z),
+                                        __fmul_rn(y.w, g.w));
+                    if (nout) reinterpret_cast<float4*>(nout)[i] = y;
+                } else {
+                    o4[i] = y;
+                }
             }
         } else {
-            for (int64_t i = threadIdx.x; i < s.ne[0]; i += RMS_THREADS)
-                out[i] = __fmul_rn(*reinterpret_cast<const float*>(row + i * s.nb[0]), scale);
+            for (int64_t i = threadIdx.x; i < s.ne[0]; i += RMS_THREADS) {
+                const float y = __fmul_rn(*reinterpret_cast<const float*>(row + i * s.nb[0]), scale);
+                if (w) {
+                    out[i] = __fmul_rn(y, __ldg(w + i));
+                    if (nout) nout[i] = y;
+                } else {
+                    out[i] = y;
+                }
+            }
         }
         __syncthreads();   // red is reused by the next row
     }
@@ -671,7 +694,18 @@ int b200_rms_norm(const float* x, const int64_t ne[4], const size_t nb[4], float
     const int grid = (int)std::min<int64_t>(rows, 148 * 8);
     return done(launch_pdl(rms_norm_kernel, dim3((unsigned)grid), dim3(RMS_THREADS), 0,
                            static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), eps,
-                           dst));
+                           dst, static_cast<const float*>(nullptr), static_cast<float*>(nullptr)));
+}
+
+int b200_rms_norm_mul(const float* x, const int64_t ne[4], const size_t nb[4], float eps, const float* w,
+                      float* norm_dst, float* dst, void* stream) {
+    using namespace b200;
+    if (!x || !w || !dst || !shape_ok(ne, nb) || !(eps >= 0.0f)) return B200_E_INVALID;
+    const int64_t rows = ne[1] * ne[2] * ne[3];
+    const int grid = (int)std::min<int64_t>(rows, 148 * 8);
+    return done(launch_pdl(rms_norm_kernel, dim3((unsigned)grid), dim3(RMS_THREADS), 0,
+                           static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), eps,
+                           dst, w, norm_dst));
 }
 
 int b200_binary(int op, const float* a, const int64_t ane[4], const size_t anb[4], const float* b, const int64_t bne[4],

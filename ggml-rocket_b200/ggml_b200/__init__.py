@@ -198,6 +198,7 @@ _BACKEND_SIGS = {
     "ggml_backend_b200_breaker_replay": (None, [_c.POINTER(_int), _int, _c.POINTER(_int)]),
     "ggml_backend_b200_subop_from_name": (_int, [ctypes.c_char_p]),
     "b200_rms_norm": (_int, [_vp, _vp, _vp, _f, _vp, _vp]),
+    "b200_rms_norm_mul": (_int, [_vp, _vp, _vp, _f, _vp, _vp, _vp, _vp]),
     "b200_binary": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "b200_silu": (_int, [_vp, _vp, _vp, _vp, _vp]),
     "b200_swiglu": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),

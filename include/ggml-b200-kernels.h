@@ -163,6 +163,12 @@ int    b200_mul_mat_vec(int wtype, const void * w_packed, int64_t N, int64_t K, 
 enum { B200_BIN_ADD = 0, B200_BIN_MUL = 1, B200_BIN_DIV = 2 };
 /* every row of x scaled by 1 / sqrtf(mean(x^2) + eps) (ggml rms_norm) */
 int b200_rms_norm(const float * x, const int64_t ne[4], const size_t nb[4], float eps, float * dst, void * stream);
+/* RMS_NORM fused with the MUL by one weight row that follows it in a transformer graph
+ * (dst = rms_norm(x) * w, w a dense f32 row of ne[0]); norm_dst, when not null, also receives the
+ * normalised rows. Both outputs are bit-identical to b200_rms_norm then b200_binary(MUL); the fusion
+ * saves one launch and a re-read of the normalised rows. */
+int b200_rms_norm_mul(const float * x, const int64_t ne[4], const size_t nb[4], float eps, const float * w,
+                      float * norm_dst, float * dst, void * stream);
 /* dst = a + b, a * b or a / b, b repeated over a (ggml_can_repeat: ane[i] % bne[i] == 0); dst has
  * a's shape */
 int b200_binary(int op, const float * a, const int64_t ane[4], const size_t anb[4],

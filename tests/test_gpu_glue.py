@@ -310,7 +310,15 @@ xn = oracle.rms_norm(x, 1e-5) * wn
 q = oracle.rope(xn.reshape(T, H, D), pos, D, 2, 10000.0, 1.0, 1.0)
 want = oracle.swiglu(q, q)
 print("CHAIN", rel_err(got, want))
-assert be.route_ops("glue") == 4
+assert be.route_ops("glue") == 4 and be.route_ops("norm_mul") == 1   # RMS_NORM * weight fused
+# the norm's own output read again later: the fused launch writes it too
+m2 = buf.tensor(offs[7], g.F32, [E, T], op=g.OP_ADD, srcs=[n1, n2])
+assert be.graph_compute([n1, n2, m2]) == g.STATUS_SUCCESS
+got2 = np.zeros((T, E), np.float32)
+assert buf.get(offs[7], got2) == 0
+nrm = oracle.rms_norm(x, 1e-5)
+print("NORMREUSE", rel_err(got2, nrm + nrm * wn))
+assert be.route_ops("norm_mul") == 2
 # host tensors: CPY into a strided host destination (the bytes between its elements survive)
 a = rng.standard_normal((8, 32)).astype(np.float32)
 dst = np.full((8, 64), 5.0, np.float32)
@@ -335,6 +343,7 @@ def test_glue_chain_through_graph_compute(cuda):
     p = subprocess.run([sys.executable, "-c", _CHILD, ROOT], env=env, capture_output=True, text=True, timeout=300)
     assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
     assert float(p.stdout.split("CHAIN")[1].split()[0]) <= GLUE_TOL
+    assert float(p.stdout.split("NORMREUSE")[1].split()[0]) <= GLUE_TOL
     assert "HOSTCPY ok" in p.stdout
 
 
@@ -389,3 +398,33 @@ def test_dense_fast_paths_match_the_general_kernels(cuda):
         assert lib.b200_cpy(0, _ptr(src), *_shape(src), 1, _ptr(h), *_shape(h), None) == 0
         torch.cuda.synchronize()
         assert np.array_equal(h.cpu().numpy().view(np.uint16), x.astype(np.float16).view(np.uint16))
+
+
+def test_rms_norm_mul_matches_the_two_ops(cuda):
+    """b200_rms_norm_mul (RMS_NORM and the MUL by one weight row as one launch) gives the same bits
+    as b200_rms_norm then b200_binary(MUL), with and without the normalised rows written, for dense
+    and row-padded inputs."""
+    import torch
+    import ggml_b200 as g
+    lib = g.lib()
+    rng = np.random.default_rng(31)
+    E, T = 4096, 37
+    w = torch.from_numpy(rng.standard_normal(E).astype(np.float32)).cuda()
+    wne, wnb = _shape(w.view(1, E))
+    for pad in (0, 4, 3):
+        xb = torch.from_numpy(rng.standard_normal((T, E + pad)).astype(np.float32)).cuda()
+        x = xb[:, :E]
+        ne, nb = _shape(x)
+        ref_n = torch.empty((T, E), device="cuda")
+        ref = torch.empty((T, E), device="cuda")
+        cne, cnb = _shape(ref_n)
+        assert lib.b200_rms_norm(_ptr(x), ne, nb, 1e-6, _ptr(ref_n), None) == 0
+        assert lib.b200_binary(1, _ptr(ref_n), cne, cnb, _ptr(w), wne, wnb, _ptr(ref), None) == 0
+        got_n = torch.full((T, E), float("nan"), device="cuda")
+        got = torch.full((T, E), float("nan"), device="cuda")
+        assert lib.b200_rms_norm_mul(_ptr(x), ne, nb, 1e-6, _ptr(w), _ptr(got_n), _ptr(got), None) == 0
+        got2 = torch.full((T, E), float("nan"), device="cuda")
+        assert lib.b200_rms_norm_mul(_ptr(x), ne, nb, 1e-6, _ptr(w), None, _ptr(got2), None) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref) and torch.equal(got_n, ref_n) and torch.equal(got2, ref), pad
+    assert lib.b200_rms_norm_mul(_ptr(x), ne, nb, 1e-6, None, None, _ptr(got), None) == g.B200_E_INVALID
