@@ -10,6 +10,7 @@ import numpy as np
 import pytest
 
 import oracle
+from conftest import rel_err
 from ggml_b200 import quants
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
@@ -186,3 +187,27 @@ def test_soft_max_oracle_matches_closed_form():
     w = x.astype(np.float64) * 0.5
     e = np.exp(w - w.max(axis=-1, keepdims=True))
     assert np.max(np.abs(oracle.soft_max(x, 0.5) - e / e.sum(axis=-1, keepdims=True))) < 1e-6
+
+
+def test_cpu_path_restatement_matches_the_oracle():
+    """The timed CPU baseline (oracle/cpu_path.c: 8-bit activation blocks, integer Q4_K block dots)
+    stays within the 8-bit activation rounding of the fp64 oracle, its AVX2 and portable dots agree
+    exactly, and an all-zero activation row gives zeros."""
+    import ctypes
+    rng = np.random.default_rng(21)
+    N, K, M = 96, 1024, 5
+    raw = oracle.quantize(12, (rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    a[2] = 0.0
+    got = oracle.cpu_path_mul_mat_q4k(raw, N, K, a)
+    want = oracle.mul_mat(12, raw, N, K, a)
+    assert rel_err(got, want) <= 2e-2
+    assert np.all(got[2] == 0.0)
+    L = oracle.path_lib()
+    L.orc_cpu_path_scalar_dot_check.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
+    for n, m in ((0, 0), (7, 4), (95, 1)):
+        o = np.zeros(2, np.float32)
+        row = np.ascontiguousarray(raw[n])
+        assert L.orc_cpu_path_scalar_dot_check(row.ctypes.data, K, np.ascontiguousarray(a[m]).ctypes.data,
+                                               o.ctypes.data) == 0
+        assert o[0] == o[1]
