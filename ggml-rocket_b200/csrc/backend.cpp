@@ -16,6 +16,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <cmath>
 #include <cstring>
 #include <functional>
 #include <list>
@@ -129,6 +130,12 @@ int flash_attn_min_kv() {
     static const int kv = [] { const int x = knob_int("B200_FLASH_ATTN_MIN_KV", 1024); return x < 1 ? 1 : x; }();
     return kv;
 }
+// FLASH_ATTN_EXT over a quantized KV cache (Q8_0 / Q4_0 K or V): converted to fp16 tiles, then the
+// fp16 kernel (b200_kv_to_f16). Off by default: the reference declines these (F16 K / V only).
+bool fa_quant_kv_on() {
+    static const bool v = knob_on("B200_FA_QUANT_KV", false);
+    return v;
+}
 bool flash_attn_unmasked() {
     static const bool v = knob_int("B200_FLASH_ATTN_UNMASKED", 0) > 0;
     return v;
@@ -162,13 +169,14 @@ size_t weight_budget_bytes(int device) {
 // tensor helpers (ggml semantics)
 // ------------------------------------------------------------------------------------------------
 
-enum : int { T_F32 = 0, T_F16 = 1, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14, T_I32 = 26, T_BF16 = 30 };
+enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14, T_I32 = 26, T_BF16 = 30 };
 
-int64_t blck_size(int t) { return t == T_Q8_0 ? 32 : (t == T_Q4_K || t == T_Q6_K) ? 256 : 1; }
+int64_t blck_size(int t) { return (t == T_Q8_0 || t == T_Q4_0) ? 32 : (t == T_Q4_K || t == T_Q6_K) ? 256 : 1; }
 size_t type_size(int t) {
     switch (t) {
         case T_F32: case T_I32: return 4;
         case T_F16: case T_BF16: return 2;
+        case T_Q4_0: return 18;   // a KV-cache type only (FLASH_ATTN_EXT); no weight route
         case T_Q8_0: return 34;
         case T_Q4_K: return 144;
         case T_Q6_K: return 210;
@@ -218,6 +226,95 @@ bool prec_declines(const b200_tensor* op) {
     if (src1 != B200_PREC_UNDECLARED && src1 < B200_PREC_F16) return true;
     if (op->op == B200_OP_MUL_MAT && op_param_i32(op, 1) == B200_HINT_SRC0_IS_HADAMARD) return true;
     return false;
+}
+
+// A Hadamard-tagged MUL_MAT runs on the device as the fast transform (b200_hadamard) when the glue
+// ops are claimed and src0 is, exactly, c times the Sylvester-ordered Hadamard matrix of order n
+// (H[i][k] = (-1)^popcount(i & k); n a power of two from 32 to 1024; F32 or F16; host-readable):
+// then MUL_MAT's row i of dst = sum_k src0[i][k] x[k] = c (H x)[i]. Any other src0 under the hint
+// stays declined, as in the reference. The check reads every entry; its result is cached by the
+// data pointer with a fingerprint of sampled entries.
+float half_bits_to_float(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1fu, man = h & 0x3ffu, bits;
+    if (exp == 0) {
+        if (man == 0) bits = sign;
+        else {
+            exp = 113;
+            while (!(man & 0x400u)) { man <<= 1; exp--; }
+            bits = sign | (exp << 23) | ((man & 0x3ffu) << 13);
+        }
+    } else if (exp == 31) {
+        bits = sign | 0x7f800000u | (man << 13);
+    } else {
+        bits = sign | ((exp + 112) << 23) | (man << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+bool hadamard_scale(const b200_tensor* w, float* scale) {
+    if (!w || (w->type != T_F32 && w->type != T_F16) || w->on_device || !w->data || !is_contiguous(w)) return false;
+    const int64_t n = w->ne[0];
+    if (w->ne[1] != n || w->ne[2] != 1 || w->ne[3] != 1 || n < 32 || n > 1024 || (n & (n - 1)) != 0) return false;
+    auto at = [&](int64_t i, int64_t k) -> float {
+        return w->type == T_F32 ? static_cast<const float*>(w->data)[i * n + k]
+                                : half_bits_to_float(static_cast<const uint16_t*>(w->data)[i * n + k]);
+    };
+    uint64_t fp = 1469598103934665603ull;
+    for (int64_t t = 0; t < 64; t++) {
+        float v = at((t * 7919) % n, (t * 104729) % n);
+        uint32_t b;
+        std::memcpy(&b, &v, 4);
+        fp = (fp ^ b) * 1099511628211ull;
+    }
+    struct Entry {
+        int64_t n;
+        int type;
+        uint64_t fp;
+        bool ok;
+        float c;
+    };
+    static std::mutex mu;
+    static std::unordered_map<const void*, Entry> cache;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(w->data);
+        if (it != cache.end() && it->second.n == n && it->second.type == w->type && it->second.fp == fp) {
+            *scale = it->second.c;
+            return it->second.ok;
+        }
+    }
+    const float c = at(0, 0);
+    bool ok = std::isfinite(c) && c != 0.0f;
+    for (int64_t i = 0; i < n && ok; i++)
+        for (int64_t k = 0; k < n && ok; k++) ok = at(i, k) == ((__builtin_popcountll(i & k) & 1) ? -c : c);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (cache.size() > 256) cache.clear();
+        cache[w->data] = Entry{n, w->type, fp, ok, c};
+    }
+    *scale = c;
+    return ok;
+}
+
+bool is_hadamard_op(const b200_tensor* op) {
+    return op->op == B200_OP_MUL_MAT && op_param_i32(op, 1) == B200_HINT_SRC0_IS_HADAMARD;
+}
+
+// Claimable on the transform route: the glue ops are claimed, src0 passes hadamard_scale, src1 and
+// dst are f32 with src1's rows of n values (any strides; dst contiguous). The f32 transform meets
+// every precision declaration (accumulator and activation), so none declines it.
+bool hadamard_claimable(const b200_tensor* op) {
+    const b200_tensor* a = op->src[0];
+    const b200_tensor* x = op->src[1];
+    float c = 0.0f;
+    if (!glue_on() || !a || !x || x->type != T_F32 || op->type != T_F32 || !is_contiguous(op)) return false;
+    if (x->ne[0] != a->ne[0] || op->ne[0] != a->ne[1]) return false;
+    for (int d = 1; d < 4; d++)
+        if (op->ne[d] != x->ne[d]) return false;
+    return hadamard_scale(a, &c);
 }
 
 bool sources_readable(const b200_tensor* op) {
@@ -376,6 +473,8 @@ struct b200_backend {
     // grow-only device scratch arenas
     void* ws = nullptr;
     size_t ws_bytes = 0;
+    void* kv16 = nullptr;                    // a quantized KV cache's fp16 tiles (grow-only)
+    size_t kv16_bytes = 0;
     // staging of host tensors, bump-allocated through one graph: device arena and pinned host
     // arena (for tensors in pageable memory); both are reset when the graph's copies have drained
     void* io = nullptr;
@@ -915,6 +1014,7 @@ extern "C" bool ggml_backend_b200_supports_op(const b200_tensor* op) {
             const b200_tensor* a = op->src[0];
             const b200_tensor* bb = op->src[1];
             if (!a || !bb) return false;
+            if (is_hadamard_op(op)) return hadamard_claimable(op);
             if (prec_declines(op)) return false;
             const int64_t K = a->ne[0], N = a->ne[1], M = bb->ne[1];
             const bool aq = is_quantized(a->type);
@@ -981,12 +1081,19 @@ extern "C" bool ggml_backend_b200_supports_op(const b200_tensor* op) {
             auto aligned16 = [](const b200_tensor* t) {
                 return (t->nb[1] % 16 == 0) && (t->nb[2] % 16 == 0) && (t->on_device ? ((uintptr_t)t->data % 16 == 0) : true);
             };
-            return max_bias == 0.0f && q->type == T_F32 && k->type == T_F16 && v->type == T_F16 &&
+            // a quantized cache: 32-value blocks along the head dimension, read as bytes, so no
+            // 16-byte alignment is needed of its view
+            auto kv_ok = [&](const b200_tensor* t) {
+                if (t->type == T_F16) return t->nb[0] == 2 && aligned16(t);
+                return fa_quant_kv_on() && (t->type == T_Q8_0 || t->type == T_Q4_0) && t->ne[0] % 32 == 0 &&
+                       t->nb[0] == (size_t)(t->type == T_Q8_0 ? 34 : 18) && (t->on_device || is_contiguous(t));
+            };
+            return max_bias == 0.0f && q->type == T_F32 && kv_ok(k) && kv_ok(v) &&
                    (!m || (m->type == T_F16 && is_contiguous(m))) && op->type == T_F32 && is_contiguous(op) &&
                    q->ne[3] == 1 && k->ne[3] == 1 && v->ne[3] == 1 && k->ne[0] == D && op->ne[0] == DV &&
-                   v->ne[1] == KV && v->ne[2] == HK && q->nb[0] == 4 && k->nb[0] == 2 && v->nb[0] == 2 &&
+                   v->ne[1] == KV && v->ne[2] == HK && q->nb[0] == 4 &&
                    (D == 64 || D == 128) && (DV == 64 || DV == 128) && HK > 0 && H % HK == 0 &&
-                   aligned16(k) && aligned16(v) && (!m || (m->ne[0] >= KV && m->ne[1] >= T)) &&
+                   (!m || (m->ne[0] >= KV && m->ne[1] >= T)) &&
                    T >= flash_attn_min_t() && KV >= flash_attn_min_kv();
         }
         case B200_OP_RMS_NORM:
@@ -1146,7 +1253,7 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
 // Fusable: a static 2-D weight of a kernel-native type feeding off a shared src1
 // (ggml-rocket.cpp:4928-4944). Quantized weights fuse too: the shared pack is free here.
 bool node_fusable(const b200_tensor* op) {
-    if (op->op != B200_OP_MUL_MAT) return false;
+    if (op->op != B200_OP_MUL_MAT || is_hadamard_op(op)) return false;
     const b200_tensor* a = op->src[0];
     const b200_tensor* bb = op->src[1];
     return a->ne[2] == 1 && a->ne[3] == 1 && bb->ne[2] == 1 && bb->ne[3] == 1 && ggml_backend_b200_supports_op(op);
@@ -1241,8 +1348,27 @@ int do_flash_attn(b200_backend* b, b200_tensor* op) {
     const void* md = m ? stage_in(b, m, &ok) : nullptr;
     char* dd = stage_out(b, op, false, &ok);
     if (!ok || !op_inputs_ready(b)) return B200_E_CUDA;
-    int rc = b200_flash_attn_ext(static_cast<const float*>(qd), (int64_t)q->nb[1], (int64_t)q->nb[2], kd,
-                                 (int64_t)k->nb[1], (int64_t)k->nb[2], vd, (int64_t)v->nb[1], (int64_t)v->nb[2], md,
+    // a quantized cache: its fp16 tiles, contiguous [HK][KV][D], in a grow-only scratch buffer
+    int64_t k_nb1 = (int64_t)k->nb[1], k_nb2 = (int64_t)k->nb[2], v_nb1 = (int64_t)v->nb[1], v_nb2 = (int64_t)v->nb[2];
+    if (k->type != T_F16 || v->type != T_F16) {
+        const size_t kb = k->type != T_F16 ? ((size_t)HK * KV * D * 2 + 255) & ~(size_t)255 : 0;
+        const size_t vb = v->type != T_F16 ? (size_t)HK * KV * DV * 2 : 0;
+        if (!grow(&b->kv16, &b->kv16_bytes, kb + vb, b->stream)) return B200_E_CUDA;
+        char* base = static_cast<char*>(b->kv16);
+        if (k->type != T_F16) {
+            const int rc = b200_kv_to_f16(k->type, kd, D, KV, HK, k_nb1, k_nb2, base, b->stream);
+            if (rc != B200_OK) return rc;
+            kd = base, k_nb1 = (int64_t)D * 2, k_nb2 = (int64_t)KV * D * 2;
+        }
+        if (v->type != T_F16) {
+            const int rc = b200_kv_to_f16(v->type, vd, DV, KV, HK, v_nb1, v_nb2, base + kb, b->stream);
+            if (rc != B200_OK) return rc;
+            vd = base + kb, v_nb1 = (int64_t)DV * 2, v_nb2 = (int64_t)KV * DV * 2;
+        }
+        b->route_ops["fa_quant_kv"]++;
+    }
+    int rc = b200_flash_attn_ext(static_cast<const float*>(qd), (int64_t)q->nb[1], (int64_t)q->nb[2], kd, k_nb1,
+                                 k_nb2, vd, v_nb1, v_nb2, md,
                                  m ? (int64_t)m->nb[1] : 0, reinterpret_cast<float*>(dd), D, DV, T, H, KV, HK, scale,
                                  max_bias, softcap, b->ws, b->ws_bytes, b->dev_err, b->stream);
     if (rc != B200_OK) return rc;
@@ -1329,6 +1455,28 @@ int do_glue(b200_backend* b, const b200_tensor* op) {
     if (rc != B200_OK) return rc;
     if (!op_outputs_done(b, stg.outs, {d})) return B200_E_CUDA;
     b->route_ops["glue"]++;
+    return B200_OK;
+}
+
+// A Hadamard-tagged MUL_MAT on the transform route: src0 is never read on the device, only its
+// scale (hadamard_scale); dst = scale * H x per row of src1.
+int do_hadamard(b200_backend* b, const b200_tensor* op) {
+    const b200_tensor* x = op->src[1];
+    float c = 0.0f;
+    if (!hadamard_scale(op->src[0], &c)) return B200_E_UNSUPPORTED;
+    OpStaging stg;
+    stg.ins = {x};
+    stg.outs = {op};
+    if (!op_reserve(b, stg)) return B200_E_CUDA;
+    bool ok = true;
+    const char* sx = static_cast<const char*>(stage_in(b, x, &ok));
+    char* d = stage_out(b, op, false, &ok);
+    if (!ok || !op_inputs_ready(b)) return B200_E_CUDA;
+    const int rc = b200_hadamard(reinterpret_cast<const float*>(sx), x->ne, x->nb, c, reinterpret_cast<float*>(d),
+                                 b->stream);
+    if (rc != B200_OK) return rc;
+    if (!op_outputs_done(b, stg.outs, {d})) return B200_E_CUDA;
+    b->route_ops["hadamard"]++;
     return B200_OK;
 }
 
@@ -1458,6 +1606,7 @@ void ggml_backend_b200_free(b200_backend_t b) {
         io_drain(b);
         for (void* p : b->transient) cudaFree(p);
         cudaFree(b->ws);
+        cudaFree(b->kv16);
         cudaFree(b->io);
         cudaFree(b->wstage);
         if (b->pin) cudaFreeHost(b->pin);
@@ -1548,6 +1697,14 @@ int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes,
                 if (!ggml_backend_b200_supports_op(node)) {
                     logf("E", "graph_compute: MUL_MAT %s was not claimed\n", node->name);
                     status = B200_STATUS_FAILED;
+                    break;
+                }
+                if (is_hadamard_op(node)) {
+                    const int rc = do_hadamard(b, node);
+                    if (rc != B200_OK) {
+                        logf("E", "graph_compute: Hadamard MUL_MAT %s failed (%d)\n", node->name, rc);
+                        status = B200_STATUS_FAILED;
+                    }
                     break;
                 }
                 std::vector<b200_tensor*> group{node};

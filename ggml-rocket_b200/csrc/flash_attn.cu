@@ -15,6 +15,7 @@
 //              whole key range, rescaled in place only when a row max grows by more than 2^8.
 //              K and V tiles arrive by TMA straight from the op's strided cache views, two
 //              stages deep.
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 
@@ -732,7 +733,69 @@ static bool make_tmap_3d_f16(CUtensorMap* map, const void* base, uint64_t d0, ui
 }
 }  // namespace b200
 
+namespace b200 {
+
+// ---- a quantized KV cache (Q8_0 / Q4_0) as the fp16 tiles the kernel reads ----------------------
+// One thread per 32-value block of a [HK][KV][D] view (rows nb1 bytes apart, heads nb2): ggml's
+// dequantize_row_q8_0 / _q4_0 (y = q * d, resp. (nibble - 8) * d, in f32), then fp16 (nearest
+// even), written contiguous [HK][KV][D]. Blocks are 2-byte aligned only: byte loads.
+template <int TYPE>
+__global__ void kv_to_f16_kernel(const uint8_t* __restrict__ src, int64_t D, int64_t KV, int64_t HK, int64_t nb1,
+                                 int64_t nb2, __half* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t per_row = D / 32, total = HK * KV * per_row;
+    constexpr int BYTES = TYPE == 8 ? 34 : 18;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t c = i % per_row, r = (i / per_row) % KV, h = i / (per_row * KV);
+        const uint8_t* b = src + h * nb2 + r * nb1 + c * BYTES;
+        const float d = __half2float(__ushort_as_half((unsigned short)(b[0] | (b[1] << 8))));
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+            float v0, v1;
+            if constexpr (TYPE == 8) {
+                v0 = __fmul_rn((float)(int8_t)b[2 + e], d);
+                v1 = __fmul_rn((float)(int8_t)b[3 + e], d);
+            } else {   // Q4_0: element j < 16 is the low nibble of byte j, j >= 16 the high nibble of byte j - 16
+                const int j0 = e, j1 = e + 1;
+                const int q0 = j0 < 16 ? (b[2 + j0] & 0x0f) : (b[2 + j0 - 16] >> 4);
+                const int q1 = j1 < 16 ? (b[2 + j1] & 0x0f) : (b[2 + j1 - 16] >> 4);
+                v0 = __fmul_rn((float)(q0 - 8), d);
+                v1 = __fmul_rn((float)(q1 - 8), d);
+            }
+            w[e / 2] = (uint32_t)__half_as_ushort(__float2half_rn(v0)) |
+                       ((uint32_t)__half_as_ushort(__float2half_rn(v1)) << 16);
+        }
+        uint4* o = reinterpret_cast<uint4*>(dst + (h * KV + r) * D + 32 * c);
+#pragma unroll
+        for (int q = 0; q < 4; q++) o[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+    }
+}
+
+}  // namespace b200
+
 extern "C" {
+
+int b200_kv_to_f16(int type, const void* src, int64_t D, int64_t KV, int64_t HK, int64_t nb1, int64_t nb2, void* dst,
+                   void* stream) {
+    using namespace b200;
+    if (!src || !dst || D <= 0 || KV <= 0 || HK <= 0 || nb1 <= 0 || nb2 <= 0) return B200_E_INVALID;
+    if ((type != 8 && type != 2) || D % 32 != 0 || (reinterpret_cast<uintptr_t>(dst) & 15u) != 0)
+        return B200_E_UNSUPPORTED;
+    const int64_t total = HK * KV * (D / 32);
+    const int threads = 256;
+    const int64_t want = (total + threads - 1) / threads;
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)device_sm_count() * 16));
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const cudaError_t e =
+        type == 8 ? launch_pdl(kv_to_f16_kernel<8>, dim3(grid), dim3(threads), 0, st,
+                               static_cast<const uint8_t*>(src), D, KV, HK, nb1, nb2, static_cast<__half*>(dst))
+                  : launch_pdl(kv_to_f16_kernel<2>, dim3(grid), dim3(threads), 0, st,
+                               static_cast<const uint8_t*>(src), D, KV, HK, nb1, nb2, static_cast<__half*>(dst));
+    return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
 
 size_t b200_flash_attn_workspace_size(int D, int DV, int T, int H, int KV, int HK) {
     (void)DV;

@@ -638,6 +638,51 @@ __global__ void __launch_bounds__(256) argsort_warp_kernel(const char* __restric
     }
 }
 
+// ---- Hadamard-tagged MUL_MAT: y = scale * H_n x per row, H_n the Sylvester-ordered Walsh-Hadamard
+// matrix (H[i][k] = (-1)^popcount(i & k)), by the fast transform: log2(n) butterfly rounds of f32
+// additions (h = 1, 2, 4, ...: (a, b) -> (a + b, a - b)), then one multiply by scale. One warp per
+// row (n = 32 .. 1024), position j * 32 + lane in slot j of lane; exchanges across lanes by
+// shuffles, within a lane by register pairs.
+constexpr int HAD_MAX = 1024;
+template <int E>
+__global__ void __launch_bounds__(256) hadamard_kernel(const char* __restrict__ x, Shape4 s, float scale,
+                                                      float* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int64_t rows = s.ne[1] * s.ne[2] * s.ne[3];
+    const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const int64_t i1 = r % s.ne[1], i2 = (r / s.ne[1]) % s.ne[2], i3 = r / (s.ne[1] * s.ne[2]);
+    const char* row = x + i1 * s.nb[1] + i2 * s.nb[2] + i3 * s.nb[3];
+    float v[E];
+#pragma unroll
+    for (int j = 0; j < E; j++) v[j] = *reinterpret_cast<const float*>(row + (int64_t)(lane + 32 * j) * s.nb[0]);
+#pragma unroll
+    for (int h = 1; h < 32; h <<= 1) {
+        const bool lower = (lane & h) == 0;
+#pragma unroll
+        for (int j = 0; j < E; j++) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[j], h);
+            v[j] = lower ? __fadd_rn(v[j], o) : __fsub_rn(o, v[j]);
+        }
+    }
+#pragma unroll
+    for (int hj = 1; hj < E; hj <<= 1) {
+#pragma unroll
+        for (int j = 0; j < E; j++) {
+            if ((j & hj) == 0) {
+                const float a = v[j], b = v[j + hj];
+                v[j] = __fadd_rn(a, b);
+                v[j + hj] = __fsub_rn(a, b);
+            }
+        }
+    }
+    float* out = dst + r * s.ne[0];
+#pragma unroll
+    for (int j = 0; j < E; j++) out[lane + 32 * j] = __fmul_rn(v[j], scale);
+}
+
 // ---- SUM_ROWS: the sum of every row, in double (ggml_vec_sum_f32 sums in ggml_float) -------
 __global__ void __launch_bounds__(RMS_THREADS) sum_rows_kernel(const char* __restrict__ x, Shape4 s,
                                                                float* __restrict__ dst) {
@@ -873,6 +918,27 @@ int b200_argsort(const float* x, const int64_t ne[4], const size_t nb[4], int de
     return done(launch_pdl(argsort_kernel, dim3((unsigned)std::min<int64_t>(rows, 148 * 8)), dim3(threads), 0,
                            static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb),
                            descending ? 1 : 0, n2, dst));
+}
+
+int b200_hadamard(const float* x, const int64_t ne[4], const size_t nb[4], float scale, float* dst, void* stream) {
+    using namespace b200;
+    if (!x || !dst || !shape_ok(ne, nb)) return B200_E_INVALID;
+    const int64_t n = ne[0];
+    if (n < 32 || n > HAD_MAX || (n & (n - 1)) != 0) return B200_E_UNSUPPORTED;
+    const int64_t rows = ne[1] * ne[2] * ne[3];
+    if (rows >= (1ll << 34)) return B200_E_UNSUPPORTED;
+    const dim3 grid((unsigned)((rows + 7) / 8)), block(256);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const char* xp = reinterpret_cast<const char*>(x);
+    const Shape4 sh = shape_of(ne, nb);
+    switch (n) {
+        case 32: return done(launch_pdl(hadamard_kernel<1>, grid, block, 0, st, xp, sh, scale, dst));
+        case 64: return done(launch_pdl(hadamard_kernel<2>, grid, block, 0, st, xp, sh, scale, dst));
+        case 128: return done(launch_pdl(hadamard_kernel<4>, grid, block, 0, st, xp, sh, scale, dst));
+        case 256: return done(launch_pdl(hadamard_kernel<8>, grid, block, 0, st, xp, sh, scale, dst));
+        case 512: return done(launch_pdl(hadamard_kernel<16>, grid, block, 0, st, xp, sh, scale, dst));
+        default: return done(launch_pdl(hadamard_kernel<32>, grid, block, 0, st, xp, sh, scale, dst));
+    }
 }
 
 int b200_sum_rows(const float* x, const int64_t ne[4], const size_t nb[4], float* dst, void* stream) {

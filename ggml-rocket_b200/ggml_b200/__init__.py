@@ -13,8 +13,9 @@ LIB_PATH = os.path.join(PKG, "lib", "libggml-b200.so")
 
 # ggml_type numbering
 F32, F16, Q8_0, Q4_K, Q6_K, I32, BF16 = 0, 1, 8, 12, 14, 26, 30
+Q4_0 = 2
 TYPE_NAMES = {F32: "f32", F16: "f16", Q8_0: "q8_0", Q4_K: "q4_K", Q6_K: "q6_K", I32: "i32", BF16: "bf16"}
-BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
+BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
 
 B200_OK = 0
 STATUS = {0: "ok", -1: "invalid", -2: "unsupported", -3: "cuda", -4: "device", -5: "workspace",
@@ -199,6 +200,8 @@ _BACKEND_SIGS = {
     "ggml_backend_b200_subop_from_name": (_int, [ctypes.c_char_p]),
     "b200_rms_norm": (_int, [_vp, _vp, _vp, _f, _vp, _vp]),
     "b200_rms_norm_mul": (_int, [_vp, _vp, _vp, _f, _vp, _vp, _vp, _vp]),
+    "b200_hadamard": (_int, [_vp, _vp, _vp, _f, _vp, _vp]),
+    "b200_kv_to_f16": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
     "b200_binary": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "b200_silu": (_int, [_vp, _vp, _vp, _vp, _vp]),
     "b200_swiglu": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),

@@ -134,6 +134,14 @@ int    b200_flash_attn_ext(const float * q, int64_t q_nb1, int64_t q_nb2,
                            float * dst, int D, int DV, int T, int H, int KV, int HK,
                            float scale, float max_bias, float softcap,
                            void * workspace, size_t workspace_bytes, int * dev_err, void * stream);
+/* A quantized KV-cache view (ggml's -ctk / -ctv q8_0 or q4_0: type 8 or 2) as the fp16 tiles the
+ * attention kernel reads: [HK][KV][D] of the view whose rows are nb1 bytes apart and heads nb2,
+ * each value ggml's dequantized f32 rounded to fp16, written contiguous to dst (16-byte aligned,
+ * HK * KV * D * 2 bytes). The reference declines FLASH_ATTN_EXT on a quantized cache (its handler
+ * takes F16 K / V only, ggml-rocket.cpp:7654-7700); the backend runs such ops as this conversion
+ * followed by b200_flash_attn_ext when B200_FA_QUANT_KV=1. */
+int    b200_kv_to_f16(int type, const void * src, int64_t D, int64_t KV, int64_t HK, int64_t nb1, int64_t nb2,
+                      void * dst, void * stream);
 
 /* ---- decode-size MUL_MAT (M = 1..32) over Q4_K, Q6_K and Q8_0 weights ----------------------
  * The reference leaves decode (M below its ROCKET_MIN_M) on the CPU (ggml-rocket.cpp:7424-7496);
@@ -169,6 +177,12 @@ int b200_rms_norm(const float * x, const int64_t ne[4], const size_t nb[4], floa
  * saves one launch and a re-read of the normalised rows. */
 int b200_rms_norm_mul(const float * x, const int64_t ne[4], const size_t nb[4], float eps, const float * w,
                       float * norm_dst, float * dst, void * stream);
+/* A MUL_MAT whose src0 carries ggml's Walsh-Hadamard hint (GGML_HINT_SRC0_IS_HADAMARD), which the
+ * reference declines (ggml-rocket.cpp:7392-7403) because the CPU evaluates it as the fast
+ * transform: dst row = scale * H_n row for every row of x, H_n the Sylvester-ordered Hadamard
+ * matrix (H[i][k] = (-1)^popcount(i & k)), n = ne[0] a power of two from 32 to 1024, by log2(n)
+ * butterfly rounds in f32 and one multiply by scale; dst contiguous f32. */
+int b200_hadamard(const float * x, const int64_t ne[4], const size_t nb[4], float scale, float * dst, void * stream);
 /* dst = a + b, a * b or a / b, b repeated over a (ggml_can_repeat: ane[i] % bne[i] == 0); dst has
  * a's shape */
 int b200_binary(int op, const float * a, const int64_t ane[4], const size_t anb[4],

@@ -167,3 +167,99 @@ def test_fa_softcap_and_unmasked(cuda):
         got = run_fa(torch, Q, K16, V16, M16, scale, softcap=softcap)
         want = oracle.flash_attn(Q, K16, V16, M16, scale, softcap=softcap, q_mode=2)
         assert float(np.max(np.abs(got - want))) / np.max(np.abs(want)) <= 1e-2
+
+
+def _q4_0(x):
+    """x f32 [rows, n] -> Q4_0 blocks [rows, n / 32 * 18] (fp16 d, then 16 bytes: value j in the low
+    nibble of byte j, value j + 16 in the high nibble) and the values those blocks decode to."""
+    rows, n = x.shape
+    v = x.reshape(rows, n // 32, 32).astype(np.float32)
+    idx = np.argmax(np.abs(v), axis=-1)
+    vmax = np.take_along_axis(v, idx[..., None], axis=-1)[..., 0]
+    d = (vmax / -8.0).astype(np.float16)
+    df = d.astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        q = np.where(df[..., None] != 0, np.floor(v / df[..., None] + 8.5), 8).clip(0, 15).astype(np.uint8)
+    out = np.zeros((rows, n // 32, 18), np.uint8)
+    out[..., 0:2] = d.view(np.uint8).reshape(rows, n // 32, 2)
+    out[..., 2:] = q[..., :16] | (q[..., 16:] << 4)
+    dec = ((q.astype(np.float32) - 8.0) * df[..., None]).reshape(rows, n)
+    return out.reshape(rows, -1), dec
+
+
+@pytest.mark.parametrize("qtype", [8, 2])
+def test_kv_to_f16_matches_the_decoders(cuda, qtype):
+    """b200_kv_to_f16: a Q8_0 / Q4_0 KV-cache view with interleaved heads (rows nb1 apart, heads nb2)
+    decodes to exactly ggml's dequantized values rounded to fp16."""
+    import torch
+    import ggml_b200 as g
+    rng = np.random.default_rng(qtype)
+    HK, KV, D = 4, 96, 128
+    x = rng.standard_normal((KV, HK * D)).astype(np.float32)   # one cache row holds every head
+    if qtype == 8:
+        raw = oracle.quantize(8, x)
+        dec = oracle.dequantize(8, raw, HK * D)
+        bpb = 34
+    else:
+        raw, dec = _q4_0(x)
+        bpb = 18
+    src = torch.from_numpy(np.ascontiguousarray(raw).reshape(-1)).cuda()
+    out = torch.empty(HK * KV * D, dtype=torch.float16, device="cuda")
+    nb1, nb2 = raw.shape[1], D // 32 * bpb
+    assert g.lib().b200_kv_to_f16(qtype, src.data_ptr(), D, KV, HK, nb1, nb2, out.data_ptr(), None) == 0
+    torch.cuda.synchronize()
+    want = dec.reshape(KV, HK, D).transpose(1, 0, 2).astype(np.float16)
+    assert np.array_equal(out.cpu().numpy().reshape(HK, KV, D).view(np.uint16), want.view(np.uint16))
+
+
+_QKV_FA_CHILD = r"""
+import math, sys
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/ggml-rocket_b200"); sys.path.insert(0, sys.argv[1] + "/tests")
+import numpy as np
+import ggml_b200 as g
+import oracle
+from test_gpu_flash_attn import _q4_0
+be = g.Backend()
+rng = np.random.default_rng(5)
+H, HK, D, T, KV = 8, 2, 128, 64, 1024
+Q = rng.standard_normal((H, T, D)).astype(np.float32)
+kf = rng.standard_normal((HK * KV, D)).astype(np.float32)
+vf = rng.standard_normal((HK * KV, D)).astype(np.float32)
+kraw = oracle.quantize(8, kf)                      # Q8_0 K, [HK][KV] rows of D
+vraw, vdec = _q4_0(vf)                             # Q4_0 V
+kdec = oracle.dequantize(8, kraw, D)
+M = np.zeros((T, KV), np.float32)
+for t in range(T):
+    M[t, KV - T + t + 1:] = -np.inf
+M16 = M.astype(np.float16)
+out = np.full((T, H, D), np.nan, np.float32)
+qt = g.make_tensor(g.F32, [D, T, H], np.ascontiguousarray(Q.transpose(0, 1, 2)), nb=[4, 4 * D, 4 * D * T, 4 * D * T * H])
+kt = g.make_tensor(g.Q8_0, [D, KV, HK], kraw)
+vt = g.make_tensor(g.Q4_0, [D, KV, HK], vraw)
+mt = g.make_tensor(g.F16, [KV, T], M16)
+d = g.make_tensor(g.F32, [D, H, T], out, op=g.OP_FLASH_ATTN_EXT, srcs=[qt, kt, vt, mt],
+                  op_params=[1.0 / math.sqrt(D), 0.0, 0.0, 0])
+assert g.supports_op(d)
+assert be.graph_compute([d]) == g.STATUS_SUCCESS
+K16 = kdec.reshape(HK, KV, D).astype(np.float16).view(np.uint16)
+V16 = vdec.reshape(HK, KV, D).astype(np.float16).view(np.uint16)
+want = oracle.flash_attn(Q, K16, V16, M16.view(np.uint16), 1.0 / math.sqrt(D), q_mode=2)
+print("QKVFA", float(np.max(np.abs(out - want)) / np.max(np.abs(want))))
+assert be.route_ops("fa_quant_kv") == 1 and be.device_errors() == 0 and be.cpu_fallbacks() == 0
+be.close()
+"""
+
+
+def test_fa_over_a_quantized_kv_cache(cuda):
+    """B200_FA_QUANT_KV=1: FLASH_ATTN_EXT with a Q8_0 K cache and a Q4_0 V cache runs through
+    graph_compute (the cache converted to fp16 tiles, then the fp16 kernel) and matches the oracle on
+    the decoded cache within the FA bound."""
+    import os
+    import subprocess
+    import sys
+    from conftest import ROOT
+    env = dict(os.environ, B200_FA_QUANT_KV="1")
+    p = subprocess.run([sys.executable, "-c", _QKV_FA_CHILD, ROOT], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
+    assert float(p.stdout.split("QKVFA")[1].split()[0]) <= 1e-2

@@ -428,3 +428,74 @@ def test_rms_norm_mul_matches_the_two_ops(cuda):
         torch.cuda.synchronize()
         assert torch.equal(got, ref) and torch.equal(got_n, ref_n) and torch.equal(got2, ref), pad
     assert lib.b200_rms_norm_mul(_ptr(x), ne, nb, 1e-6, None, None, _ptr(got), None) == g.B200_E_INVALID
+
+
+def _sylvester(n):
+    i = np.arange(n)
+    return np.where(np.bitwise_count(i[:, None] & i[None, :]) % 2 == 1, -1.0, 1.0)
+
+
+@pytest.mark.parametrize("n", [32, 64, 128, 256, 512, 1024])
+def test_hadamard_transform_matches_the_dense_product(cuda, n):
+    """b200_hadamard (the fast transform of a Hadamard-tagged MUL_MAT) against the dense product
+    with the Sylvester-ordered matrix in fp64, within GLUE_TOL; row-padded input too."""
+    import torch
+    import ggml_b200 as g
+    lib = g.lib()
+    rng = np.random.default_rng(n)
+    T = 37
+    scale = np.float32(1.0 / np.sqrt(n))
+    for pad in (0, 8):
+        xb = torch.from_numpy(rng.standard_normal((T, n + pad)).astype(np.float32)).cuda()
+        x = xb[:, :n]
+        ne, nb = _shape(x)
+        y = torch.full((T, n), float("nan"), device="cuda")
+        assert lib.b200_hadamard(_ptr(x), ne, nb, float(scale), _ptr(y), None) == 0
+        torch.cuda.synchronize()
+        want = x.cpu().numpy().astype(np.float64) @ (_sylvester(n) * np.float64(scale)).T
+        assert rel_err(y.cpu().numpy(), want) <= GLUE_TOL, (n, pad)
+    bad = torch.zeros((2, 48), device="cuda")
+    bne, bnb = _shape(bad)
+    assert lib.b200_hadamard(_ptr(bad), bne, bnb, 1.0, _ptr(bad), None) == g.B200_E_UNSUPPORTED   # not 2^k
+
+
+_HADAMARD_CHILD = r"""
+import sys
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/ggml-rocket_b200"); sys.path.insert(0, sys.argv[1] + "/tests")
+import numpy as np
+import ggml_b200 as g
+from conftest import rel_err
+be = g.Backend()
+rng = np.random.default_rng(9)
+n, T = 128, 40
+i = np.arange(n)
+h = np.where(np.bitwise_count(i[:, None] & i[None, :]) % 2 == 1, -1.0, 1.0) / np.sqrt(n)
+worst = 0.0
+for wt, arr in ((g.F32, h.astype(np.float32)), (g.F16, h.astype(np.float16))):
+    x = rng.standard_normal((T, n)).astype(np.float32)
+    out = np.full((T, n), np.nan, np.float32)
+    w = g.make_tensor(wt, [n, n], arr, name="hadamard_%d" % wt)
+    tx = g.make_tensor(g.F32, [n, T], x)
+    d = g.make_tensor(g.F32, [n, T], out, op=g.OP_MUL_MAT, srcs=[w, tx], op_params=[0, g.HINT_SRC0_IS_HADAMARD])
+    assert g.supports_op(d)
+    assert be.graph_compute([d]) == g.STATUS_SUCCESS
+    want = x.astype(np.float64) @ arr.astype(np.float64).T
+    worst = max(worst, rel_err(out, want))
+assert be.route_ops("hadamard") == 2 and be.cpu_fallbacks() == 0 and be.device_errors() == 0
+be.close()
+print("HADAMARD", worst)
+"""
+
+
+def test_hadamard_mul_mat_through_graph_compute(cuda):
+    """With B200_GLUE=1 a Hadamard-tagged MUL_MAT (src0 the scaled Sylvester matrix, F32 and F16)
+    runs through graph_compute on the transform kernel and matches the dense product."""
+    import os
+    import subprocess
+    import sys
+    from conftest import ROOT
+    env = dict(os.environ, B200_GLUE="1")
+    p = subprocess.run([sys.executable, "-c", _HADAMARD_CHILD, ROOT], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
+    assert float(p.stdout.split("HADAMARD")[1].split()[0]) <= GLUE_TOL

@@ -104,6 +104,7 @@ def test_flash_attn_gates():
     assert not fa(48, 256, 8, 1024, 2)         # head_dim % 32 != 0
     assert not fa(96, 256, 8, 1024, 2)         # B200: head dims 64 / 128 only
     assert not fa(64, 256, 8, 1024, 2, kv_type=g.F32)
+    assert not fa(64, 256, 8, 1024, 2, kv_type=g.Q8_0)   # a quantized cache needs B200_FA_QUANT_KV=1
     assert not fa(64, 256, 8, 1024, 2, max_bias=8.0)
     assert not fa(64, 256, 8, 1024, 2, masked=False)   # unmasked needs B200_FLASH_ATTN_UNMASKED=1
     assert not fa(64, 256, 8, 1024, 2, sinks=True)     # attention sinks: a different softmax
@@ -287,3 +288,76 @@ def test_breaker_semantics():
     assert all(x == 1 for x in r)              # declines never open it
     r = g.breaker_replay([DEV, DEV, 0, DEV, DEV, 0])
     assert all(x == 1 for x in r)              # a success resets the count
+
+
+_HADAMARD_CHILD = r"""
+import json, sys
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/ggml-rocket_b200")
+import numpy as np
+import ggml_b200 as g
+
+
+def sylvester(n):
+    i = np.arange(n)
+    return np.where(np.bitwise_count(i[:, None] & i[None, :]) % 2 == 1, -1.0, 1.0)
+
+
+def claim(h, wt, n, hint=True, m=7):
+    arr = np.ascontiguousarray(h.astype(np.float16 if wt == g.F16 else np.float32))   # alive while claimed
+    w = g.make_tensor(wt, [n, n], arr)
+    x = g.make_tensor(g.F32, [n, m])
+    d = g.make_tensor(g.F32, [n, m], op=g.OP_MUL_MAT, srcs=[w, x],
+                      op_params=[0, g.HINT_SRC0_IS_HADAMARD if hint else 0])
+    return g.supports_op(d)
+
+
+out = {}
+for n in (32, 128, 1024):
+    h = sylvester(n) / np.sqrt(n)
+    out[f"f32_{n}"] = claim(h, g.F32, n)
+    out[f"f16_{n}"] = claim(h.astype(np.float16), g.F16, n)
+h = sylvester(128)
+out["unscaled"] = claim(h, g.F32, 128)
+out["permuted"] = claim(h[::-1].copy(), g.F32, 128)                   # not the Sylvester order
+bad = h.copy(); bad[5, 9] *= 0.5
+out["one_entry_off"] = claim(bad, g.F32, 128)
+out["n_16"] = claim(sylvester(16), g.F32, 16)
+print(json.dumps(out))
+"""
+
+
+@pytest.mark.parametrize("glue", ["0", "1"])
+def test_hadamard_tagged_mul_mat_claim(glue):
+    """A MUL_MAT under ggml's Walsh-Hadamard hint: declined by default, as the reference does;
+    with the glue ops claimed (B200_GLUE=1) claimed exactly when src0 is c times the
+    Sylvester-ordered Hadamard matrix of order 32..1024 (F32 or F16), for the device transform."""
+    e = dict(os.environ, B200_GLUE=glue)
+    p = subprocess.run([sys.executable, "-c", _HADAMARD_CHILD, ROOT], env=e, capture_output=True, text=True,
+                       timeout=120)
+    assert p.returncode == 0, p.stderr[-2000:]
+    r = json.loads(p.stdout.strip().splitlines()[-1])
+    on = glue == "1"
+    for n in (32, 128, 1024):
+        assert r[f"f32_{n}"] == on and r[f"f16_{n}"] == on, (n, r)
+    assert r["unscaled"] == on
+    assert not r["permuted"] and not r["one_entry_off"] and not r["n_16"]
+
+
+_QKV_CHILD = r"""
+import json, sys
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/ggml-rocket_b200"); sys.path.insert(0, sys.argv[1] + "/tests")
+import ggml_b200 as g
+import test_placement as t
+print(json.dumps({"q8": t.fa(64, 256, 8, 1024, 2, kv_type=g.Q8_0), "q4_0": t.fa(128, 512, 32, 4096, 8, kv_type=g.Q4_0),
+                  "q4k": t.fa(128, 512, 32, 4096, 8, kv_type=g.Q4_K), "f16": t.fa(64, 256, 8, 1024, 2)}))
+"""
+
+
+def test_flash_attn_quantized_kv_claim_in_child():
+    """B200_FA_QUANT_KV=1: FLASH_ATTN_EXT over a Q8_0 or Q4_0 KV cache is claimed (converted to fp16
+    tiles on the device); other quantized cache types stay declined, F16 is unchanged."""
+    e = dict(os.environ, B200_FA_QUANT_KV="1")
+    p = subprocess.run([sys.executable, "-c", _QKV_CHILD, ROOT], env=e, capture_output=True, text=True, timeout=120)
+    assert p.returncode == 0, p.stderr[-2000:]
+    r = json.loads(p.stdout.strip().splitlines()[-1])
+    assert r == {"q8": True, "q4_0": True, "q4k": False, "f16": True}, r
