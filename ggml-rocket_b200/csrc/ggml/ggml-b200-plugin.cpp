@@ -109,6 +109,12 @@ b200_tensor* declare(b200_graph_builder_t gb, const ggml_tensor* t) {
     else if (t->op == GGML_OP_GLU) sub = ggml_glu_op_name(ggml_get_glu_op(t));
     int32_t opp[B200_MAX_OP_PARAMS] = {};
     memcpy(opp, t->op_params, sizeof opp < sizeof t->op_params ? sizeof opp : sizeof t->op_params);
+#ifdef GGML_HINT_SRC0_IS_HADAMARD
+    // the Walsh-Hadamard hint in op_params[1]: the host's value becomes the library's (a host that
+    // spells it as an enumerator rather than a macro passes its value through unchanged)
+    if (t->op == GGML_OP_MUL_MAT)
+        opp[1] = opp[1] == (int32_t)GGML_HINT_SRC0_IS_HADAMARD ? B200_HINT_SRC0_IS_HADAMARD : 0;
+#endif
     return ggml_backend_b200_builder_add(gb, t, ggml_op_name(t->op), sub, (int32_t)t->type, t->ne, t->nb, opp, srcs,
                                          t->data, in_device_buffer(t) ? 1 : 0, tensor_readable(t) ? 1 : 0, t->name);
 }
