@@ -1480,6 +1480,51 @@ int do_hadamard(b200_backend* b, const b200_tensor* op) {
     return B200_OK;
 }
 
+// The residual ADD `add` right before a fusable RMS_NORM * MUL pair, as one launch
+// (b200_add_rms_norm_mul): both ADD operands dense f32 of the output's shape.
+bool add_norm_fusable(const b200_tensor* add, const b200_tensor* nrm) {
+    if (add->op != B200_OP_ADD || nrm->src[0] != add || add->type != T_F32 || !is_contiguous(add)) return false;
+    for (int i = 0; i < 2; i++) {
+        const b200_tensor* t = add->src[i];
+        if (!t || t->type != T_F32 || !is_contiguous(t)) return false;
+        for (int d = 0; d < 4; d++)
+            if (t->ne[d] != add->ne[d]) return false;
+    }
+    return add->ne[0] % 4 == 0 && ggml_backend_b200_supports_op(add);
+}
+
+int do_add_rms_norm_mul(b200_backend* b, const b200_tensor* add, const b200_tensor* nrm, const b200_tensor* mul,
+                        bool write_sum, bool write_norm) {
+    const b200_tensor* x = add->src[0];
+    const b200_tensor* r = add->src[1];
+    const b200_tensor* w = mul->src[1];
+    OpStaging stg;
+    stg.ins = {x, r, w};
+    stg.outs = {mul, add};
+    if (write_norm) stg.outs.push_back(nrm);
+    if (!op_reserve(b, stg)) return B200_E_CUDA;
+    bool ok = true;
+    const char* sx = static_cast<const char*>(stage_in(b, x, &ok));
+    const char* sr = static_cast<const char*>(stage_in(b, r, &ok));
+    const char* sw = static_cast<const char*>(stage_in(b, w, &ok));
+    char* dm = stage_out(b, mul, false, &ok);
+    char* ds = stage_out(b, add, false, &ok);
+    char* dn = write_norm ? stage_out(b, nrm, false, &ok) : nullptr;
+    if (!ok || !op_inputs_ready(b)) return B200_E_CUDA;
+    int rc = b200_add_rms_norm_mul(reinterpret_cast<const float*>(sx), reinterpret_cast<const float*>(sr), add->ne,
+                                   op_param_f32(nrm, 0), reinterpret_cast<const float*>(sw),
+                                   reinterpret_cast<float*>(ds), reinterpret_cast<float*>(dn),
+                                   reinterpret_cast<float*>(dm), b->stream);
+    if (rc != B200_OK) return rc;
+    std::vector<char*> bases{dm, ds};
+    if (write_norm) bases.push_back(dn);
+    if (!op_outputs_done(b, stg.outs, bases)) return B200_E_CUDA;
+    (void)write_sum;
+    b->route_ops["glue"] += 3;
+    b->route_ops["add_norm_mul"]++;
+    return B200_OK;
+}
+
 // RMS_NORM `nrm` and the MUL `mul` right after it that multiplies its rows by one weight row, as
 // one launch (b200_rms_norm_mul). Fusable when the MUL reads the norm's output as src[0] and a
 // dense f32 row of ne[0] as src[1], both claimed, with the norm's shape. The norm's own output is
@@ -1787,6 +1832,22 @@ int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes,
             case B200_OP_DIV: {
                 if (!ggml_backend_b200_supports_op(node)) {
                     status = B200_STATUS_FAILED;
+                    break;
+                }
+                // ADD (residual) -> RMS_NORM -> MUL (weight row): one launch; the sum is always
+                // written (it is the next residual), the norm's rows only when read later
+                if (fuse && i + 2 < n && !done[i + 1] && !done[i + 2] && add_norm_fusable(node, nodes[i + 1]) &&
+                    norm_mul_fusable(nodes[i + 1], nodes[i + 2])) {
+                    const b200_tensor* nrm = nodes[i + 1];
+                    bool write_norm = !nrm->on_device;
+                    for (int j = i + 3; j < n && !write_norm; j++)
+                        for (int k = 0; k < B200_MAX_SRC && !write_norm; k++) write_norm = nodes[j]->src[k] == nrm;
+                    const int rc = do_add_rms_norm_mul(b, node, nrm, nodes[i + 2], true, write_norm);
+                    if (rc != B200_OK) {
+                        logf("E", "graph_compute: fused ADD+RMS_NORM*MUL failed (%d) in node %s\n", rc, node->name);
+                        status = B200_STATUS_FAILED;
+                    }
+                    done[i + 1] = done[i + 2] = true;
                     break;
                 }
                 if (fuse && i + 1 < n && !done[i + 1] && norm_mul_fusable(node, nodes[i + 1])) {

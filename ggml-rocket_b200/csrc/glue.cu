@@ -59,6 +59,10 @@ static int grid_for(int64_t n, int threads) {
     return (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)sms * 4 * (1024 / threads)));
 }
 
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+
 // ---- RMS_NORM: y = x * (1 / sqrtf(mean(x^2) + eps)), one CTA per row ------------------------
 // ggml sums x*x (an f32 product) into a double sequentially; here each thread sums its strided
 // share in double and the CTA adds the shares in a tree: the same terms, another order.
@@ -69,7 +73,9 @@ constexpr int RMS_THREADS = 256;
 // separate ops round it, so both outputs are bit-identical to RMS_NORM then MUL.
 __global__ void __launch_bounds__(RMS_THREADS) rms_norm_kernel(const char* __restrict__ x, Shape4 s, float eps,
                                                                float* __restrict__ dst, const float* __restrict__ w,
-                                                               float* __restrict__ norm_dst) {
+                                                               float* __restrict__ norm_dst,
+                                                               const float* __restrict__ res = nullptr,
+                                                               float* __restrict__ sum_dst = nullptr) {
     grid_dep_wait();
     grid_dep_launch();
     __shared__ double red[RMS_THREADS / 32];
@@ -83,8 +89,9 @@ __global__ void __launch_bounds__(RMS_THREADS) rms_norm_kernel(const char* __res
         double sum = 0.0;
         if (vec) {
             const float4* r4 = reinterpret_cast<const float4*>(row);
+            const float4* q4 = res ? reinterpret_cast<const float4*>(res + r * s.ne[0]) : nullptr;
             for (int64_t i = threadIdx.x; i < s.ne[0] / 4; i += RMS_THREADS) {
-                const float4 v = r4[i];
+                const float4 v = q4 ? add4(r4[i], q4[i]) : r4[i];
                 sum += (double)__fmul_rn(v.x, v.x);
                 sum += (double)__fmul_rn(v.y, v.y);
                 sum += (double)__fmul_rn(v.z, v.z);
@@ -112,9 +119,12 @@ __global__ void __launch_bounds__(RMS_THREADS) rms_norm_kernel(const char* __res
                           (!norm_dst || (reinterpret_cast<uintptr_t>(norm_dst) & 15u) == 0);
         if (vec && vout) {
             const float4* r4 = reinterpret_cast<const float4*>(row);
+            const float4* q4 = res ? reinterpret_cast<const float4*>(res + r * s.ne[0]) : nullptr;
+            float4* s4 = sum_dst ? reinterpret_cast<float4*>(sum_dst + r * s.ne[0]) : nullptr;
             float4* o4 = reinterpret_cast<float4*>(out);
             for (int64_t i = threadIdx.x; i < s.ne[0] / 4; i += RMS_THREADS) {
-                const float4 v = r4[i];
+                const float4 v = q4 ? add4(r4[i], q4[i]) : r4[i];
+                if (s4) s4[i] = v;
                 const float4 y = make_float4(__fmul_rn(v.x, scale), __fmul_rn(v.y, scale), __fmul_rn(v.z, scale),
                                              __fmul_rn(v.w, scale));
                 if (w) {
@@ -739,7 +749,25 @@ int b200_rms_norm(const float* x, const int64_t ne[4], const size_t nb[4], float
     const int grid = (int)std::min<int64_t>(rows, 148 * 8);
     return done(launch_pdl(rms_norm_kernel, dim3((unsigned)grid), dim3(RMS_THREADS), 0,
                            static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), eps,
-                           dst, static_cast<const float*>(nullptr), static_cast<float*>(nullptr)));
+                           dst, static_cast<const float*>(nullptr), static_cast<float*>(nullptr),
+                           static_cast<const float*>(nullptr), static_cast<float*>(nullptr)));
+}
+
+int b200_add_rms_norm_mul(const float* a, const float* b, const int64_t ne[4], float eps, const float* w,
+                          float* sum_dst, float* norm_dst, float* dst, void* stream) {
+    using namespace b200;
+    if (!a || !b || !w || !sum_dst || !dst || ne[0] <= 0 || ne[1] <= 0 || ne[2] <= 0 || ne[3] <= 0 || !(eps >= 0.0f))
+        return B200_E_INVALID;
+    auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    if (ne[0] % 4 != 0 || !al16(a) || !al16(b) || !al16(w) || !al16(sum_dst) || !al16(dst) ||
+        (norm_dst && !al16(norm_dst)))
+        return B200_E_UNSUPPORTED;   // the dense float4 path only
+    const size_t nb[4] = {4, (size_t)ne[0] * 4, (size_t)(ne[0] * ne[1]) * 4, (size_t)(ne[0] * ne[1] * ne[2]) * 4};
+    const int64_t rows = ne[1] * ne[2] * ne[3];
+    const int grid = (int)std::min<int64_t>(rows, 148 * 8);
+    return done(launch_pdl(rms_norm_kernel, dim3((unsigned)grid), dim3(RMS_THREADS), 0,
+                           static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(a), shape_of(ne, nb), eps,
+                           dst, w, norm_dst, b, sum_dst));
 }
 
 int b200_rms_norm_mul(const float* x, const int64_t ne[4], const size_t nb[4], float eps, const float* w,
@@ -750,7 +778,7 @@ int b200_rms_norm_mul(const float* x, const int64_t ne[4], const size_t nb[4], f
     const int grid = (int)std::min<int64_t>(rows, 148 * 8);
     return done(launch_pdl(rms_norm_kernel, dim3((unsigned)grid), dim3(RMS_THREADS), 0,
                            static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), eps,
-                           dst, w, norm_dst));
+                           dst, w, norm_dst, static_cast<const float*>(nullptr), static_cast<float*>(nullptr)));
 }
 
 int b200_binary(int op, const float* a, const int64_t ane[4], const size_t anb[4], const float* b, const int64_t bne[4],

@@ -200,6 +200,7 @@ _BACKEND_SIGS = {
     "ggml_backend_b200_subop_from_name": (_int, [ctypes.c_char_p]),
     "b200_rms_norm": (_int, [_vp, _vp, _vp, _f, _vp, _vp]),
     "b200_rms_norm_mul": (_int, [_vp, _vp, _vp, _f, _vp, _vp, _vp, _vp]),
+    "b200_add_rms_norm_mul": (_int, [_vp, _vp, _vp, _f, _vp, _vp, _vp, _vp, _vp]),
     "b200_hadamard": (_int, [_vp, _vp, _vp, _f, _vp, _vp]),
     "b200_kv_to_f16": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
     "b200_binary": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),

@@ -177,6 +177,12 @@ int b200_rms_norm(const float * x, const int64_t ne[4], const size_t nb[4], floa
  * saves one launch and a re-read of the normalised rows. */
 int b200_rms_norm_mul(const float * x, const int64_t ne[4], const size_t nb[4], float eps, const float * w,
                       float * norm_dst, float * dst, void * stream);
+/* The residual ADD in front of such a norm fused in as well: sum_dst = a + b (dense f32 of shape
+ * ne, 16-byte aligned, as are w, norm_dst and dst), then dst = rms_norm(sum) * w and, when not
+ * null, norm_dst = rms_norm(sum). Bit-identical to b200_binary(ADD), b200_rms_norm, b200_binary(MUL);
+ * returns B200_E_UNSUPPORTED for operands that are not dense and aligned. */
+int b200_add_rms_norm_mul(const float * a, const float * b, const int64_t ne[4], float eps, const float * w,
+                          float * sum_dst, float * norm_dst, float * dst, void * stream);
 /* A MUL_MAT whose src0 carries ggml's Walsh-Hadamard hint (GGML_HINT_SRC0_IS_HADAMARD), which the
  * reference declines (ggml-rocket.cpp:7392-7403) because the CPU evaluates it as the fast
  * transform: dst row = scale * H_n row for every row of x, H_n the Sylvester-ordered Hadamard

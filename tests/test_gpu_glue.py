@@ -319,6 +319,16 @@ assert buf.get(offs[7], got2) == 0
 nrm = oracle.rms_norm(x, 1e-5)
 print("NORMREUSE", rel_err(got2, nrm + nrm * wn))
 assert be.route_ops("norm_mul") == 2
+# residual ADD -> RMS_NORM -> MUL: one launch; the sum (the next residual) is written
+ra = buf.tensor(offs[3], g.F32, [E, T], op=g.OP_ADD, srcs=[tx, n2])
+rn = buf.tensor(offs[5], g.F32, [E, T], op=g.OP_RMS_NORM, srcs=[ra], op_params=[1e-5])
+rm = buf.tensor(offs[6], g.F32, [E, T], op=g.OP_MUL, srcs=[rn, tw])
+assert be.graph_compute([n1, n2, ra, rn, rm]) == g.STATUS_SUCCESS
+got_s, got_m = np.zeros((T, E), np.float32), np.zeros((T, E), np.float32)
+assert buf.get(offs[3], got_s) == 0 and buf.get(offs[6], got_m) == 0
+hsum = x + nrm * wn
+print("ADDNORM", max(rel_err(got_s, hsum), rel_err(got_m, oracle.rms_norm(hsum, 1e-5) * wn)))
+assert be.route_ops("add_norm_mul") == 1
 # host tensors: CPY into a strided host destination (the bytes between its elements survive)
 a = rng.standard_normal((8, 32)).astype(np.float32)
 dst = np.full((8, 64), 5.0, np.float32)
@@ -344,6 +354,7 @@ def test_glue_chain_through_graph_compute(cuda):
     assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
     assert float(p.stdout.split("CHAIN")[1].split()[0]) <= GLUE_TOL
     assert float(p.stdout.split("NORMREUSE")[1].split()[0]) <= GLUE_TOL
+    assert float(p.stdout.split("ADDNORM")[1].split()[0]) <= GLUE_TOL
     assert "HOSTCPY ok" in p.stdout
 
 
@@ -499,3 +510,33 @@ def test_hadamard_mul_mat_through_graph_compute(cuda):
                        timeout=300)
     assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
     assert float(p.stdout.split("HADAMARD")[1].split()[0]) <= GLUE_TOL
+
+
+def test_add_rms_norm_mul_matches_the_three_ops(cuda):
+    """b200_add_rms_norm_mul (residual ADD, RMS_NORM and the MUL by the norm weight as one launch)
+    gives the same bits as b200_binary(ADD), b200_rms_norm and b200_binary(MUL), the sum included,
+    with and without the normalised rows written; and refuses an unaligned operand."""
+    import torch
+    import ggml_b200 as g
+    lib = g.lib()
+    rng = np.random.default_rng(41)
+    E, T = 4096, 29
+    a = torch.from_numpy(rng.standard_normal((T, E)).astype(np.float32)).cuda()
+    r = torch.from_numpy(rng.standard_normal((T, E)).astype(np.float32)).cuda()
+    w = torch.from_numpy(rng.standard_normal(E).astype(np.float32)).cuda()
+    ne, nb = _shape(a)
+    wne, wnb = _shape(w.view(1, E))
+    s_ref, n_ref, o_ref = (torch.empty((T, E), device="cuda") for _ in range(3))
+    assert lib.b200_binary(0, _ptr(a), ne, nb, _ptr(r), ne, nb, _ptr(s_ref), None) == 0
+    assert lib.b200_rms_norm(_ptr(s_ref), ne, nb, 1e-5, _ptr(n_ref), None) == 0
+    assert lib.b200_binary(1, _ptr(n_ref), ne, nb, _ptr(w), wne, wnb, _ptr(o_ref), None) == 0
+    for with_norm in (True, False):
+        s, n, o = (torch.full((T, E), float("nan"), device="cuda") for _ in range(3))
+        assert lib.b200_add_rms_norm_mul(_ptr(a), _ptr(r), ne, 1e-5, _ptr(w), _ptr(s), _ptr(n) if with_norm else None,
+                                         _ptr(o), None) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(s, s_ref) and torch.equal(o, o_ref)
+        assert torch.equal(n, n_ref) if with_norm else bool(torch.isnan(n).all())
+    odd = torch.empty(T * E + 1, device="cuda")[1:].view(T, E)
+    assert lib.b200_add_rms_norm_mul(_ptr(odd), _ptr(r), ne, 1e-5, _ptr(w), _ptr(s), None, _ptr(o), None) == \
+        g.B200_E_UNSUPPORTED
