@@ -648,7 +648,7 @@ def run_moe(args, world_override=None, inside=False):
     w_gate, w_up, w_down = stack(H, F), stack(H, F), stack(F, H)
     rng = np.random.default_rng(0xB200 + 17 * rank)     # this rank's tokens
     x = torch.from_numpy(rng.standard_normal((T, 1, H), dtype=np.float32)).to(dev)
-    h = torch.from_numpy(rng.standard_normal((T, top, F), dtype=np.float32)).to(dev)
+    h = torch.empty((T, top, F), dtype=torch.float32, device=dev)     # swiglu(gate, up)
     logits = torch.from_numpy(rng.standard_normal((T, E), dtype=np.float32))
     ids = torch.topk(torch.softmax(logits, -1), top, dim=-1).indices.to(torch.int32).to(dev)
     y_gate = torch.empty((T, top, F), device=dev)
@@ -663,19 +663,17 @@ def run_moe(args, world_override=None, inside=False):
         def layer():
             ep(wt, w_gate, H, F, E, x, 1, ids, y_gate)
             ep(wt, w_up, H, F, E, x, 1, ids, y_up)
+            g.check(g.swiglu(y_gate, y_up, h), "swiglu")
             ep(wt, w_down, F, H, E, h, top, ids, y_down)
     elif world > 1:
         from ggml_b200.ep import DeviceOps, PeerExpertParallelMulMatId
-        ep = PeerExpertParallelMulMatId(T, top, max(H, F), max(H, F), ops=DeviceOps(err))
+        ep = PeerExpertParallelMulMatId(T, top, H, H, ops=DeviceOps(err), n_members_max=1)
 
         def layer():
-            # each op's result is a view of the exchange's return buffers; consume it (copy into
-            # the layer's tensor) before the next op reuses them. Gate and up read the same x and
-            # ids: one push, route and gather for both.
-            g_out, u_out = ep.grouped(wt, [w_gate, w_up], H, [F, F], E, x, 1, ids)
-            y_gate.copy_(g_out)
-            y_up.copy_(u_out)
-            y_down.copy_(ep(wt, w_down, F, H, E, h, top, ids))
+            # the expert FFN where the experts are: x is pushed once, gate, up, swiglu and down run
+            # on the owner, and only the down projection's rows come back (the result is a view of
+            # the exchange's return buffer, [T, top, H])
+            ep.ffn(wt, w_gate, w_up, wt, w_down, H, F, E, x, ids)
     else:
         ws = torch.empty(max(g.mul_mat_id_workspace_size(H, F, E, top, T), g.mul_mat_id_workspace_size(F, H, E, top, T)),
                          dtype=torch.uint8, device=dev)
@@ -691,6 +689,7 @@ def run_moe(args, world_override=None, inside=False):
             rc = g.mul_mat_id_group(wt, [w_gate, w_up], [F, F], H, E, x, H * 4, H * 4, 1, ids, 4, top * 4, top, T,
                                     [y_gate, y_up], [F * 4, F * 4], [top * F * 4, top * F * 4], ws, err)
             g.check(rc, "mul_mat_id_group")
+            g.check(g.swiglu(y_gate, y_up, h), "swiglu")
             one(w_down, F, H, h, top, y_down)
 
     stream = torch.cuda.current_stream()
@@ -723,7 +722,7 @@ def run_moe(args, world_override=None, inside=False):
     if rank == 0:
         peaks, src = measured_peaks()
         tf = moe_flops_per_rank() * world / (ms / 1e3) / 1e12
-        line = {"metric": "MoE MUL_MAT_ID layer prompt tokens/sec (gate+up+down, Q4_K, 128 experts top-8)",
+        line = {"metric": "MoE MUL_MAT_ID layer prompt tokens/sec (expert FFN: gate+up, swiglu, down; Q4_K, 128 experts top-8)",
                 "value": T * world / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",

@@ -23,6 +23,7 @@
 #include <cuda_runtime.h>
 
 #include "ggml-b200-kernels.h"
+#include "glu.cuh"
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -171,15 +172,13 @@ __global__ void binary_dense_kernel(int op, const float4* __restrict__ a, const 
         dst[i] = make_float4(bin_op(op, x.x, y.x), bin_op(op, x.y, y.y), bin_op(op, x.z, y.z), bin_op(op, x.w, y.w));
     }
 }
-__device__ __forceinline__ float silu_f(float x);
 __global__ void swiglu_dense_kernel(const float4* __restrict__ a, const float4* __restrict__ g, int64_t n4,
                                     float4* __restrict__ dst) {
     grid_dep_wait();
     grid_dep_launch();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
         const float4 x = a[i], y = g[i];
-        dst[i] = make_float4(__fmul_rn(silu_f(x.x), y.x), __fmul_rn(silu_f(x.y), y.y), __fmul_rn(silu_f(x.z), y.z),
-                             __fmul_rn(silu_f(x.w), y.w));
+        dst[i] = make_float4(swiglu_f(x.x, y.x), swiglu_f(x.y, y.y), swiglu_f(x.z, y.z), swiglu_f(x.w, y.w));
     }
 }
 __global__ void silu_dense_kernel(const float4* __restrict__ x, int64_t n4, float4* __restrict__ dst) {
@@ -219,9 +218,6 @@ __global__ void binary_kernel(int op, const char* __restrict__ a, Shape4 sa, con
     }
 }
 
-// ggml_silu_f32: x / (1 + expf(-x)), expf being the device's (within 2 ulp of the host libm's)
-__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
-__device__ __forceinline__ float silu_f(float x) { return silu(x); }
 
 // ---- SILU and SWIGLU (dst = silu(a) * g) -------------------------------------------------------
 __global__ void silu_kernel(const char* __restrict__ x, Shape4 s, float* __restrict__ dst) {
@@ -245,7 +241,7 @@ __global__ void swiglu_kernel(const char* __restrict__ a, Shape4 sa, const char*
         unravel(i, sa.ne, c);
         const float x = *reinterpret_cast<const float*>(a + offset_of(c, sa.nb));
         const float y = *reinterpret_cast<const float*>(g + offset_of(c, sg.nb));
-        dst[i] = __fmul_rn(silu(x), y);
+        dst[i] = swiglu_f(x, y);
     }
 }
 

@@ -26,6 +26,7 @@
 #include <cuda_runtime.h>
 
 #include "ggml-b200-kernels.h"
+#include "glu.cuh"
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -189,7 +190,8 @@ __global__ void __launch_bounds__(P2PC) p2p_route_place_kernel(const int32_t* __
                                                                int32_t* __restrict__ pair_row,
                                                                int32_t* __restrict__ pair_src,
                                                                int32_t* __restrict__ pair_tok,
-                                                               int32_t* __restrict__ pair_slot) {
+                                                               int32_t* __restrict__ pair_slot,
+                                                               int32_t* __restrict__ pair_self) {
     grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
     grid_dep_launch();
     if (__ldg(bad_any)) return;
@@ -209,6 +211,7 @@ __global__ void __launch_bounds__(P2PC) p2p_route_place_kernel(const int32_t* __
         pair_src[p] = src;
         pair_tok[p] = tok;
         pair_slot[p] = s;
+        if (pair_self) pair_self[p] = p;   // the expert FFN's own rows: output row p of a [pairs][N] buffer
     }
 }
 
@@ -227,6 +230,61 @@ __global__ void __launch_bounds__(256) p2p_gather_kernel(const __half* __restric
         uint4* d = reinterpret_cast<uint4*>(dst + (int64_t)p * K);
         for (int i = threadIdx.x; i < K / 8; i += 256) d[i] = __ldg(s + i);
         if (threadIdx.x == 0) dst_scale[p] = __int_as_float(__ldg(meta + rr * MW));
+    }
+}
+
+// Expert FFN on the owner: pair p's down-projection input h = swiglu(gate[p], up[p]) (f32 rows
+// of F), packed like every activation row of the GEMMs (s = max|h| or 1, fp16(h * (1/s))). The
+// arithmetic is that of the SWIGLU glue kernel followed by the MUL_MAT_ID gather-pack, so the
+// packed rows equal, bit for bit, those the single-GPU op chain builds for the down projection.
+// One 256-thread CTA per pair row (grid-stride over the device count), V float4 per thread.
+template <int V>
+__global__ void __launch_bounds__(256) ep_swiglu_pack_kernel(const float* __restrict__ gate, const float* __restrict__ up,
+                                                             int F, const int32_t* __restrict__ n_pairs,
+                                                             __half* __restrict__ a16, float* __restrict__ scales) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
+    __shared__ float red[8];
+    const int n = __ldg(n_pairs);
+    const int n4 = F / 4;
+    for (int p = blockIdx.x; p < n; p += gridDim.x) {
+        const float4* g4 = reinterpret_cast<const float4*>(gate + (int64_t)p * F);
+        const float4* u4 = reinterpret_cast<const float4*>(up + (int64_t)p * F);
+        float4 v[V];
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < V; i++) {
+            const int idx = threadIdx.x + i * 256;
+            if (idx < n4) {
+                const float4 x = g4[idx], y = u4[idx];
+                v[i] = make_float4(swiglu_f(x.x, y.x), swiglu_f(x.y, y.y), swiglu_f(x.z, y.z), swiglu_f(x.w, y.w));
+            } else {
+                v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+        __syncthreads();
+        amax = red[0];
+#pragma unroll
+        for (int w = 1; w < 8; w++) amax = fmaxf(amax, red[w]);
+        __syncthreads();   // red is rewritten by the next row
+        const float sc = amax > 0.0f ? amax : 1.0f;
+        const float inv = __frcp_rn(sc);
+        if (threadIdx.x == 0) scales[p] = sc;
+        uint2* out = reinterpret_cast<uint2*>(a16 + (int64_t)p * F);
+#pragma unroll
+        for (int i = 0; i < V; i++) {
+            const int idx = threadIdx.x + i * 256;
+            if (idx < n4) {
+                uint2 w;
+                w.x = pack_half2(__fmul_rn(v[i].x, inv), __fmul_rn(v[i].y, inv));
+                w.y = pack_half2(__fmul_rn(v[i].z, inv), __fmul_rn(v[i].w, inv));
+                out[idx] = w;
+            }
+        }
     }
 }
 
@@ -256,6 +314,81 @@ static P2pLayout p2p_layout(int64_t G, int64_t cap, int64_t K, int64_t e_loc, in
     L.scales = L.a16 + al(P * (size_t)K * 2);
     L.total = L.scales + al(P * 4);
     return L;
+}
+
+// The expert FFN's extra workspace after the MUL_MAT_ID owner's: pair_self, the gate and up
+// outputs in pair order (f32 [P][F]) and the packed down-projection input (fp16 [P][F] + scales).
+struct P2pFfnLayout {
+    P2pLayout base;
+    size_t self, gate, up, h16, hscale, total;
+};
+
+static P2pFfnLayout p2p_ffn_layout(int64_t G, int64_t cap, int64_t H, int64_t F, int64_t e_loc, int64_t n_used) {
+    auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    const size_t P = (size_t)(G * cap);
+    P2pFfnLayout L{};
+    L.base = p2p_layout(G, cap, H, e_loc, n_used);
+    L.self = L.base.total;
+    L.gate = L.self + al(P * 4);
+    L.up = L.gate + al(P * (size_t)F * 4);
+    L.h16 = L.up + al(P * (size_t)F * 4);
+    L.hscale = L.h16 + al(P * (size_t)F * 2);
+    L.total = L.hscale + al(P * 4);
+    return L;
+}
+
+// The owner's steps in front of its GEMMs, shared by the MUL_MAT_ID step and the expert FFN:
+// wait for every source's rows, route the received (row, slot) pairs by local expert, gather
+// the fp16 rows in expert order. Fills the route arrays of the layout (pair_self too when given)
+// and returns the token tile the grouped GEMMs use.
+struct P2pRoute {
+    int32_t *off, *tiles, *psrc, *ptok, *pslot;
+    __half* a16;
+    float* scales;
+    int bt;
+};
+
+static int p2p_owner_prologue(const P2pLayout& L, char* ws, int64_t K, int64_t n_local, int64_t expert0,
+                              const void* recv_a16, const int32_t* recv_meta, const int* flags, int64_t n_ranks,
+                              int64_t n_used, int64_t cap, int64_t pairs_hint, int32_t* pair_self, int epoch,
+                              int* dev_err, cudaStream_t st, P2pRoute* R) {
+    int32_t* region = reinterpret_cast<int32_t*>(ws + L.region);
+    int32_t* ecnt = reinterpret_cast<int32_t*>(ws + L.ecnt);
+    int32_t* cursor = reinterpret_cast<int32_t*>(ws + L.cursor);
+    int32_t* bsum = reinterpret_cast<int32_t*>(ws + L.bsum);
+    int32_t* bad = reinterpret_cast<int32_t*>(ws + L.bad);
+    int32_t* prow = reinterpret_cast<int32_t*>(ws + L.prow);
+    R->off = reinterpret_cast<int32_t*>(ws + L.off);
+    R->tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
+    R->psrc = reinterpret_cast<int32_t*>(ws + L.psrc);
+    R->ptok = reinterpret_cast<int32_t*>(ws + L.ptok);
+    R->pslot = reinterpret_cast<int32_t*>(ws + L.pslot);
+    R->a16 = reinterpret_cast<__half*>(ws + L.a16);
+    R->scales = reinterpret_cast<float*>(ws + L.scales);
+    const int G = (int)n_ranks;
+    const int64_t rows_max = n_ranks * cap;
+    const int nb = (int)((rows_max + P2PC - 1) / P2PC);
+    R->bt = ep_token_tile_public(pairs_hint > 0 ? pairs_hint : rows_max / 2, n_local);
+    // 1. every source's rows have landed (their flags carry the counts)
+    launch_pdl(ep_wait_kernel, dim3(1), dim3(64), 0, st, flags, 0, G, epoch, region, dev_err, peer_wait_limit_ns());
+    // 2. route the (row, slot) pairs by local expert
+    const size_t hist_smem = (size_t)n_local * sizeof(int);
+    if (hist_smem > 48 * 1024 &&
+        cudaFuncSetAttribute(p2p_route_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hist_smem) !=
+            cudaSuccess)
+        return B200_E_UNSUPPORTED;
+    if (cudaMemsetAsync(ecnt, 0, (size_t)n_local * 4, st) != cudaSuccess) return B200_E_CUDA;
+    launch_pdl(p2p_route_count_kernel, dim3(nb), dim3(P2PC), hist_smem, st, recv_meta, region, G, cap, (int)n_used,
+               (int)expert0, (int)n_local, ecnt, bsum, bad);
+    ep_route_scan_public(ecnt, bsum, bad, nb, (int)n_local, R->bt, R->off, R->tiles, cursor, dev_err, st);
+    launch_pdl(p2p_route_place_kernel, dim3(nb), dim3(P2PC), 0, st, recv_meta, region, G, cap, (int)n_used,
+               (int)expert0, bad + nb, cursor, prow, R->psrc, R->ptok, R->pslot, pair_self);
+    // 3. gather the fp16 rows in expert order (once for every GEMM that reads them)
+    const int64_t gcap = (int64_t)device_sm_count() * 8;
+    launch_pdl(p2p_gather_kernel, dim3((unsigned)(rows_max < gcap ? rows_max : gcap)), dim3(256), 0, st,
+               static_cast<const __half*>(recv_a16), recv_meta, prow, R->off + n_local, (int)n_used, (int)K, R->a16,
+               R->scales);
+    return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 
 }  // namespace b200
@@ -344,52 +477,85 @@ int b200_moe_ep_p2p_expert_group(int n_members, int wtype, const void* const* lo
     const P2pLayout L = p2p_layout(n_ranks, cap, K, n_local, n_used);
     if (!workspace || workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
         return B200_E_WORKSPACE;
-    char* ws = static_cast<char*>(workspace);
-    int32_t* region = reinterpret_cast<int32_t*>(ws + L.region);
-    int32_t* ecnt = reinterpret_cast<int32_t*>(ws + L.ecnt);
-    int32_t* cursor = reinterpret_cast<int32_t*>(ws + L.cursor);
-    int32_t* bsum = reinterpret_cast<int32_t*>(ws + L.bsum);
-    int32_t* bad = reinterpret_cast<int32_t*>(ws + L.bad);
-    int32_t* off = reinterpret_cast<int32_t*>(ws + L.off);
-    int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
-    int32_t* prow = reinterpret_cast<int32_t*>(ws + L.prow);
-    int32_t* psrc = reinterpret_cast<int32_t*>(ws + L.psrc);
-    int32_t* ptok = reinterpret_cast<int32_t*>(ws + L.ptok);
-    int32_t* pslot = reinterpret_cast<int32_t*>(ws + L.pslot);
-    __half* a16 = reinterpret_cast<__half*>(ws + L.a16);
-    float* scales = reinterpret_cast<float*>(ws + L.scales);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int G = (int)n_ranks;
     const int64_t rows_max = n_ranks * cap;
-    const int nb = (int)((rows_max + P2PC - 1) / P2PC);
-    const int bt = ep_token_tile_public(pairs_hint > 0 ? pairs_hint : rows_max / 2, n_local);
-    // 1. every source's rows have landed (their flags carry the counts)
-    launch_pdl(ep_wait_kernel, dim3(1), dim3(64), 0, st, flags, 0, G, epoch, region, dev_err, peer_wait_limit_ns());
-    // 2. route the (row, slot) pairs by local expert
-    const size_t hist_smem = (size_t)n_local * sizeof(int);
-    if (hist_smem > 48 * 1024 &&
-        cudaFuncSetAttribute(p2p_route_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hist_smem) !=
-            cudaSuccess)
-        return B200_E_UNSUPPORTED;
-    if (cudaMemsetAsync(ecnt, 0, (size_t)n_local * 4, st) != cudaSuccess) return B200_E_CUDA;
-    launch_pdl(p2p_route_count_kernel, dim3(nb), dim3(P2PC), hist_smem, st, recv_meta, region, G, cap, (int)n_used,
-               (int)expert0, (int)n_local, ecnt, bsum, bad);
-    ep_route_scan_public(ecnt, bsum, bad, nb, (int)n_local, bt, off, tiles, cursor, dev_err, st);
-    launch_pdl(p2p_route_place_kernel, dim3(nb), dim3(P2PC), 0, st, recv_meta, region, G, cap, (int)n_used,
-               (int)expert0, bad + nb, cursor, prow, psrc, ptok, pslot);
-    // 3. gather the fp16 rows in expert order (once for every member)
-    const int64_t gcap = (int64_t)device_sm_count() * 8;
-    launch_pdl(p2p_gather_kernel, dim3((unsigned)(rows_max < gcap ? rows_max : gcap)), dim3(256), 0, st,
-               static_cast<const __half*>(recv_a16), recv_meta, prow, off + n_local, (int)n_used, (int)K, a16, scales);
-    if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
+    P2pRoute R;
+    int rc = p2p_owner_prologue(L, static_cast<char*>(workspace), K, n_local, expert0, recv_a16, recv_meta, flags,
+                                n_ranks, n_used, cap, pairs_hint, nullptr, epoch, dev_err, st, &R);
+    if (rc != B200_OK) return rc;
     // 4. per member, the grouped GEMM stores each output row into its home rank's ret over NVLink
     for (int m = 0; m < n_members; m++) {
-        const int rc = gemm_grouped_impl(wtype, local_stacks[m], Ns[m], K, n_local, a16, scales, rows_max, bt, off,
-                                         tiles, pslot, ptok, nullptr, ret_nb1[m], ret_nb2[m], dev_err, st, psrc,
-                                         peer_rets[m]);
+        rc = gemm_grouped_impl(wtype, local_stacks[m], Ns[m], K, n_local, R.a16, R.scales, rows_max, R.bt, R.off,
+                               R.tiles, R.pslot, R.ptok, nullptr, ret_nb1[m], ret_nb2[m], dev_err, st, R.psrc,
+                               peer_rets[m]);
         if (rc != B200_OK) return rc;
     }
     // 5. tell every home rank its rows are in place
+    launch_pdl(ep_signal_kernel, dim3(1), dim3(64), 0, st, peer_flags, G, (int)rank, G, epoch, nullptr);
+    return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
+size_t b200_moe_ep_p2p_ffn_workspace_size(int64_t n_ranks, int64_t cap, int64_t H, int64_t F, int64_t n_local,
+                                          int64_t n_used) {
+    if (n_ranks <= 0 || cap <= 0 || H <= 0 || F <= 0 || n_local <= 0 || n_used <= 0) return 0;
+    return b200::p2p_ffn_layout(n_ranks, cap, H, F, n_local, n_used).total;
+}
+
+int b200_moe_ep_p2p_expert_ffn(int wtype_gate_up, const void* gate_stack, const void* up_stack, int wtype_down,
+                               const void* down_stack, int64_t H, int64_t F, int64_t n_local, int64_t expert0,
+                               const void* recv_a16, const int32_t* recv_meta, const int* flags, int64_t n_ranks,
+                               int64_t rank, int64_t n_used, int64_t cap, int64_t pairs_hint, float* const* peer_ret,
+                               int64_t ret_nb1, int64_t ret_nb2, int* const* peer_flags, int epoch, void* workspace,
+                               size_t workspace_bytes, int* dev_err, void* stream) {
+    using namespace b200;
+    if (!gate_stack || !up_stack || !down_stack || !recv_a16 || !recv_meta || !flags || !peer_ret || !peer_flags ||
+        !dev_err || H <= 0 || F <= 0 || n_local <= 0 || expert0 < 0 || n_ranks <= 0 || rank < 0 || rank >= n_ranks ||
+        n_used <= 0 || cap <= 0)
+        return B200_E_INVALID;
+    if (!weight_type_supported(wtype_gate_up, H) || !weight_type_supported(wtype_down, F) || H % 32 || F % 32 ||
+        H % 16 || F > 8192 || n_used > 32 || n_local > 4096 || n_ranks > 64 || (ret_nb1 % 16) || (ret_nb2 % 16))
+        return B200_E_UNSUPPORTED;
+    const P2pFfnLayout L = p2p_ffn_layout(n_ranks, cap, H, F, n_local, n_used);
+    if (!workspace || workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+        return B200_E_WORKSPACE;
+    char* ws = static_cast<char*>(workspace);
+    int32_t* self = reinterpret_cast<int32_t*>(ws + L.self);
+    float* gate = reinterpret_cast<float*>(ws + L.gate);
+    float* up = reinterpret_cast<float*>(ws + L.up);
+    __half* h16 = reinterpret_cast<__half*>(ws + L.h16);
+    float* hscale = reinterpret_cast<float*>(ws + L.hscale);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int G = (int)n_ranks;
+    const int64_t rows_max = n_ranks * cap;
+    // 1-3. wait, route, gather the pushed x rows (pair_self: each pair's own row index)
+    P2pRoute R;
+    int rc = p2p_owner_prologue(L.base, ws, H, n_local, expert0, recv_a16, recv_meta, flags, n_ranks, n_used, cap,
+                                pairs_hint, self, epoch, dev_err, st, &R);
+    if (rc != B200_OK) return rc;
+    // 4. gate and up into this GPU's [pairs][F] buffers (row p = pair p: token and slot index both
+    //    pair_self, slot stride 0)
+    rc = gemm_grouped_impl(wtype_gate_up, gate_stack, F, H, n_local, R.a16, R.scales, rows_max, R.bt, R.off, R.tiles,
+                           self, self, gate, 0, F * 4, dev_err, st);
+    if (rc != B200_OK) return rc;
+    rc = gemm_grouped_impl(wtype_gate_up, up_stack, F, H, n_local, R.a16, R.scales, rows_max, R.bt, R.off, R.tiles,
+                           self, self, up, 0, F * 4, dev_err, st);
+    if (rc != B200_OK) return rc;
+    // 5. h = swiglu(gate, up), packed for the down projection in the same pair order
+    const int64_t gcap = (int64_t)device_sm_count() * 8;
+    const dim3 pg((unsigned)(rows_max < gcap ? rows_max : gcap));
+    const int v = (int)((F / 4 + 255) / 256);
+    const int32_t* n_pairs = R.off + n_local;
+    if (v <= 1) launch_pdl(ep_swiglu_pack_kernel<1>, pg, dim3(256), 0, st, gate, up, (int)F, n_pairs, h16, hscale);
+    else if (v <= 2) launch_pdl(ep_swiglu_pack_kernel<2>, pg, dim3(256), 0, st, gate, up, (int)F, n_pairs, h16, hscale);
+    else if (v <= 4) launch_pdl(ep_swiglu_pack_kernel<4>, pg, dim3(256), 0, st, gate, up, (int)F, n_pairs, h16, hscale);
+    else launch_pdl(ep_swiglu_pack_kernel<8>, pg, dim3(256), 0, st, gate, up, (int)F, n_pairs, h16, hscale);
+    if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
+    // 6. down over the same route; the epilogue stores each row into its home rank's ret
+    rc = gemm_grouped_impl(wtype_down, down_stack, H, F, n_local, h16, hscale, rows_max, R.bt, R.off, R.tiles, R.pslot,
+                           R.ptok, nullptr, ret_nb1, ret_nb2, dev_err, st, R.psrc, peer_ret);
+    if (rc != B200_OK) return rc;
+    // 7. tell every home rank its rows are in place
     launch_pdl(ep_signal_kernel, dim3(1), dim3(64), 0, st, peer_flags, G, (int)rank, G, epoch, nullptr);
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }

@@ -274,6 +274,9 @@ _SIGS.update({
     "b200_moe_ep_p2p_finish": (_int, [_vp, _i64, _int, _vp, _vp]),
     "b200_moe_ep_p2p_expert_group": (_int, [_int, _int, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i64,
                                             _i64, _i64, _vp, _vp, _vp, _vp, _int, _vp, _sz, _vp, _vp]),
+    "b200_moe_ep_p2p_ffn_workspace_size": (_sz, [_i64] * 6),
+    "b200_moe_ep_p2p_expert_ffn": (_int, [_int, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64,
+                                          _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _int, _vp, _sz, _vp, _vp]),
     "b200_mul_mat_tp_workspace_size": (_sz, [_int, _i64, _i64, _i64]),
     "b200_mul_mat_tp": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _int, _vp,
                                _sz, _vp, _vp]),
@@ -521,6 +524,16 @@ def mul_mat_id_group(wtype, stacks, Ns, K, n_expert, b, b_nb1, b_nb2, ne11, ids,
                                        b_nb2, ne11, _ptr(ids), ids_nb0, ids_nb1, n_used, n_tokens,
                                        P(*[_ptr(t) for t in dsts]), I(*d_nb1s), I(*d_nb2s), _ptr(workspace),
                                        workspace.numel() * workspace.element_size(), _ptr(dev_err), _stream(stream))
+
+
+def swiglu(a, gt, dst, stream=None):
+    """dst = silu(a) * gt over contiguous f32 tensors of one shape (b200_swiglu, ggml's
+    SWIGLU with separate gate and up tensors)."""
+    n = a.numel()
+    inner = a.shape[-1] if a.dim() else 1
+    ne = (ctypes.c_int64 * 4)(inner, n // inner, 1, 1)
+    nb = (ctypes.c_size_t * 4)(4, inner * 4, n * 4, n * 4)
+    return lib().b200_swiglu(_ptr(a), nb, _ptr(gt), nb, ne, _ptr(dst), _stream(stream))
 
 
 def mul_mat_id_route_view(K, n_expert, n_used, n_tokens):

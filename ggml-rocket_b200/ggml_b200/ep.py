@@ -214,21 +214,23 @@ class PeerExpertParallelMulMatId:
             g.lib().b200_ep_shared_close(g._c.c_void_p(base))
         self._opened = []
 
-    def __call__(self, wtype, local_stack, K, N, n_expert, b, ne11, ids, dst=None, stream=None):
-        out = self.grouped(wtype, [local_stack], K, [N], n_expert, b, ne11, ids, stream=stream)[0]
+    def __call__(self, wtype, local_stack, K, N, n_expert, b, ne11, ids, dst=None, stream=None, member=0):
+        out = self.grouped(wtype, [local_stack], K, [N], n_expert, b, ne11, ids, stream=stream, member0=member)[0]
         if dst is not None:
             dst.copy_(out)
         return out
 
-    def grouped(self, wtype, local_stacks, K, Ns, n_expert, b, ne11, ids, stream=None):
+    def grouped(self, wtype, local_stacks, K, Ns, n_expert, b, ne11, ids, stream=None, member0=0):
         """Several MUL_MAT_IDs over the same b and ids (a layer's gate and up): the rows are
         dispatched and pushed once, each owner routes and gathers them once and runs one grouped
-        GEMM per stack. Returns one view of the return buffers per member, [n_tokens, n_used, N]."""
+        GEMM per stack. Returns one view of the return buffers per member, [n_tokens, n_used, N]:
+        members member0, member0 + 1, ... of the exchange's return buffers, so that ops of a layer
+        given distinct members keep their results side by side without copies."""
         G, ops = self.G, self.ops
         n_tokens, n_used = ids.shape
         nm = len(local_stacks)
         if n_expert % G or n_used != self.n_used or K > self.K_max or max(Ns) > self.N_max or \
-                n_tokens * n_used > self.cap or nm > self.n_members_max:
+                n_tokens * n_used > self.cap or member0 < 0 or member0 + nm > self.n_members_max:
             raise ValueError("op outside the sizes this exchange was built for")
         n_local = n_expert // G
         self.epoch += 1
@@ -246,9 +248,47 @@ class PeerExpertParallelMulMatId:
         g.check(lib.b200_moe_ep_p2p_expert_group(
             nm, wtype, P(*[g._ptr(t) for t in local_stacks]), I(*Ns), K, n_local, self.rank * n_local,
             g._ptr(self.recv_a16), g._ptr(self.recv_meta), g._ptr(self.flags), G, self.rank, n_used, self.cap,
-            n_tokens * n_used, P(*[g._ptr(self.peer_rets[m]) for m in range(nm)]), I(*([self.N_max * 4] * nm)),
+            n_tokens * n_used, P(*[g._ptr(self.peer_rets[member0 + m]) for m in range(nm)]), I(*([self.N_max * 4] * nm)),
             I(*([n_used * self.N_max * 4] * nm)), g._ptr(self.peer[3]), self.epoch, g._ptr(ws), ws_bytes,
             g._ptr(err), g._stream(stream)), "moe_ep_p2p_expert_group")
         g.check(lib.b200_moe_ep_p2p_finish(g._ptr(self.flags), G, self.epoch, g._ptr(err), g._stream(stream)),
                 "moe_ep_p2p_finish")
-        return [self.rets[m][:n_tokens, :, :Ns[m]] for m in range(nm)]
+        return [self.rets[member0 + m][:n_tokens, :, :Ns[m]] for m in range(nm)]
+
+    def ffn(self, wtype_gate_up, gate_stack, up_stack, wtype_down, down_stack, H, F, n_expert, x, ids, stream=None,
+            member=0):
+        """A MoE block's expert FFN, down(swiglu(gate(x), up(x))) per (token, slot), with the
+        three expert projections run where the experts are (b200_moe_ep_p2p_expert_ffn): x's
+        rows are dispatched and pushed once, each owner keeps gate, up and h in its own memory,
+        and only the down projection's rows come back. x is [n_tokens, 1, H] (or [n_tokens, H]);
+        gate_stack / up_stack are this rank's experts of [F, H] weights, down_stack of [H, F].
+        Returns a view of return buffer `member`, [n_tokens, n_used, H], valid until that member
+        is written again; it equals the single-GPU chain MUL_MAT_ID, MUL_MAT_ID, SWIGLU,
+        MUL_MAT_ID bit for bit."""
+        G, ops = self.G, self.ops
+        n_tokens, n_used = ids.shape
+        if x.dim() == 2:
+            x = x.view(n_tokens, 1, H)
+        if n_expert % G or n_used != self.n_used or H > self.K_max or H > self.N_max or \
+                n_tokens * n_used > self.cap or not 0 <= member < self.n_members_max:
+            raise ValueError("op outside the sizes this exchange was built for")
+        n_local = n_expert // G
+        self.epoch += 1
+        d = ops.dispatch(ids, x, 1, n_expert, G, H, stream=stream)
+        err = ops._err(self.dev)
+        lib = g.lib()
+        g.check(lib.b200_moe_ep_p2p_push(
+            g._ptr(d.a16), g._ptr(d.scale), g._ptr(d.hdr), g._ptr(d.row_tok), g._ptr(d.counts), G, self.rank,
+            n_used, H, self.cap, g._ptr(self.peer[0]), g._ptr(self.peer[1]), g._ptr(self.peer[3]), self.epoch,
+            n_tokens * n_used, g._stream(stream)), "moe_ep_p2p_push")
+        ws_bytes = lib.b200_moe_ep_p2p_ffn_workspace_size(G, self.cap, H, F, n_local, n_used)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=self.dev)
+        g.check(lib.b200_moe_ep_p2p_expert_ffn(
+            wtype_gate_up, g._ptr(gate_stack), g._ptr(up_stack), wtype_down, g._ptr(down_stack), H, F, n_local,
+            self.rank * n_local, g._ptr(self.recv_a16), g._ptr(self.recv_meta), g._ptr(self.flags), G, self.rank,
+            n_used, self.cap, n_tokens * n_used, g._ptr(self.peer_rets[member]), self.N_max * 4,
+            n_used * self.N_max * 4, g._ptr(self.peer[3]), self.epoch, g._ptr(ws), ws_bytes, g._ptr(err),
+            g._stream(stream)), "moe_ep_p2p_expert_ffn")
+        g.check(lib.b200_moe_ep_p2p_finish(g._ptr(self.flags), G, self.epoch, g._ptr(err), g._stream(stream)),
+                "moe_ep_p2p_finish")
+        return self.rets[member][:n_tokens, :, :H]

@@ -344,6 +344,27 @@ int    b200_moe_ep_p2p_expert_group(int n_members, int wtype, const void * const
                                     float * const * const * peer_rets, const int64_t * ret_nb1,
                                     const int64_t * ret_nb2, int * const * peer_flags, int epoch, void * workspace,
                                     size_t workspace_bytes, int * dev_err, void * stream);
+/* The owner step for a whole expert FFN, the MoE block's three MUL_MAT_IDs and the GLU between
+ * them (gate = MUL_MAT_ID(gate_exps, x), up = MUL_MAT_ID(up_exps, x), h = SWIGLU(gate, up),
+ * out = MUL_MAT_ID(down_exps, h): the order llama.cpp's MoE FFN builds its graph in) run where
+ * the experts are. The home pushes x ([n_tokens][1][H], ne11 = 1) once with
+ * b200_moe_ep_p2p_push; the owner waits, routes and gathers the rows once, keeps gate and up in
+ * its own workspace, applies SWIGLU and packs h there, runs the down projection over the same
+ * route and stores each [H] output row into its home rank's ret; then flags every home
+ * (b200_moe_ep_p2p_finish on the home as for one op). Only x crosses NVLink out and only the
+ * down projection's rows come back: the gate / up results and h never leave the owner. The
+ * result equals, bit for bit, the single-GPU chain b200_mul_mat_id_group(gate, up),
+ * b200_swiglu, b200_mul_mat_id(down). H and F multiples of 32 and of the weight types' blocks;
+ * F <= 8192. */
+size_t b200_moe_ep_p2p_ffn_workspace_size(int64_t n_ranks, int64_t cap, int64_t H, int64_t F, int64_t n_local,
+                                          int64_t n_used);
+int    b200_moe_ep_p2p_expert_ffn(int wtype_gate_up, const void * gate_stack, const void * up_stack, int wtype_down,
+                                  const void * down_stack, int64_t H, int64_t F, int64_t n_local, int64_t expert0,
+                                  const void * recv_a16, const int32_t * recv_meta, const int * flags,
+                                  int64_t n_ranks, int64_t rank, int64_t n_used, int64_t cap, int64_t pairs_hint,
+                                  float * const * peer_ret, int64_t ret_nb1, int64_t ret_nb2,
+                                  int * const * peer_flags, int epoch, void * workspace, size_t workspace_bytes,
+                                  int * dev_err, void * stream);
 
 /* ---- the give-up limit of cross-GPU waits -------------------------------------------------------
  * The reference's fault policy (ggml-rocket.cpp:263-307) turns a device route that fails into an

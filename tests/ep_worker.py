@@ -19,6 +19,70 @@ from ggml_b200 import quants  # noqa: E402
 from ggml_b200.ep import ExpertParallelMulMatId  # noqa: E402
 
 
+def ffn_case(rank, world, p2p, wt_gu, wt_down):
+    """The expert FFN with its three projections run on the experts' owners
+    (PeerExpertParallelMulMatId.ffn) against the single-GPU chain MUL_MAT_ID group (gate, up),
+    SWIGLU, MUL_MAT_ID (down) over the full stacks: bit for bit, twice (the buffers are reused),
+    and against the CPU oracle composed op by op within the MUL_MAT tolerance."""
+    import oracle
+    from conftest import rel_err
+    E, n_used, H, F = 32, 8, 512, 768
+    T = 80 + 29 * rank
+    e_loc = E // world
+    rng = np.random.default_rng(21 + wt_down)
+    nat = {}
+    for name, wt, N, K in (("gate", wt_gu, F, H), ("up", wt_gu, F, H), ("down", wt_down, H, F)):
+        nat[name] = (wt, N, K, quants.quantize(wt, (rng.standard_normal((E * N, K)) * 0.02).astype(np.float32)))
+
+    def pack(wt, raw_rows, rows, K):
+        raw = torch.from_numpy(np.ascontiguousarray(raw_rows).reshape(-1)).cuda()
+        out = torch.empty(g.weight_packed_size(wt, rows, K), dtype=torch.uint8, device="cuda")
+        g.weight_pack(wt, raw, rows, K, out)
+        return out
+
+    full = {k: pack(wt, raw, E * N, K) for k, (wt, N, K, raw) in nat.items()}
+    loc = {k: pack(wt, raw[rank * e_loc * N:(rank + 1) * e_loc * N], e_loc * N, K) for k, (wt, N, K, raw) in nat.items()}
+    rng = np.random.default_rng(300 + rank)
+    x_np = rng.standard_normal((T, 1, H)).astype(np.float32)
+    ids_np = np.stack([rng.permutation(E)[:n_used] for _ in range(T)]).astype(np.int32)
+    x, ids = torch.from_numpy(x_np).cuda(), torch.from_numpy(ids_np).cuda()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    yg = torch.empty((T, n_used, F), device="cuda")
+    yu = torch.empty_like(yg)
+    hh = torch.empty_like(yg)
+    want = torch.full((T, n_used, H), float("nan"), device="cuda")
+    ws = torch.zeros(max(g.mul_mat_id_workspace_size(H, F, E, n_used, T), g.mul_mat_id_workspace_size(F, H, E, n_used, T)),
+                     dtype=torch.uint8, device="cuda")
+    rcs = [g.mul_mat_id_group(wt_gu, [full["gate"], full["up"]], [F, F], H, E, x, H * 4, H * 4, 1, ids, 4, n_used * 4,
+                              n_used, T, [yg, yu], [F * 4, F * 4], [n_used * F * 4] * 2, ws, err),
+           g.swiglu(yg, yu, hh),
+           g.mul_mat_id(wt_down, full["down"], F, H, E, hh, F * 4, n_used * F * 4, n_used, ids, 4, n_used * 4, n_used, T,
+                        want, H * 4, n_used * H * 4, ws, err)]
+    torch.cuda.synchronize()
+    ok = rcs == [0, 0, 0] and int(err.item()) == 0
+    for rep in range(2):
+        perr = torch.zeros(1, dtype=torch.int32, device="cuda")
+        p2p.ops.dev_err = perr
+        got = p2p.ffn(wt_gu, loc["gate"], loc["up"], wt_down, loc["down"], H, F, E, x, ids, member=rep % 2)
+        torch.cuda.synchronize()
+        same = int(perr.item()) == 0 and bool(torch.equal(got, want))
+        if not same:
+            print(f"rank {rank} ffn {(wt_gu, wt_down)} rep {rep} mismatch: err {int(perr.item())} "
+                  f"max {float((got - want).abs().max())}", flush=True)
+        ok = ok and same
+    # the chain itself against the oracle composed op by op (the first 24 tokens)
+    n = 24
+    og = oracle.mul_mat_id(wt_gu, nat["gate"][3].reshape(E, F, -1), H, F, E, x_np[:n], ids_np[:n])
+    ou = oracle.mul_mat_id(wt_gu, nat["up"][3].reshape(E, F, -1), H, F, E, x_np[:n], ids_np[:n])
+    oh = oracle.swiglu(og, ou).astype(np.float32)
+    od = oracle.mul_mat_id(wt_down, nat["down"][3].reshape(E, H, -1), F, H, E, oh, ids_np[:n])
+    e = rel_err(want[:n].cpu().numpy(), od)
+    if e > 1e-2:
+        print(f"rank {rank} ffn {(wt_gu, wt_down)} oracle rel err {e}", flush=True)
+        ok = False
+    return ok
+
+
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -86,6 +150,8 @@ def main():
             print(f"rank {rank} p2p group case {(wtype, K, N, E, n_used, ne11, T)} mismatch: err {int(perr.item())}",
                   flush=True)
         ok = ok and same and g_same
+    ok = ffn_case(rank, world, p2p, 12, 12) and ok
+    ok = ffn_case(rank, world, p2p, 12, 14) and ok
     p2p.close()
     dist.barrier()
     dist.destroy_process_group()
