@@ -675,43 +675,54 @@ def run_moe(args, world_override=None, inside=False):
             # the exchange's return buffer, [T, top, H])
             ep.ffn(wt, w_gate, w_up, wt, w_down, H, F, E, x, ids)
     else:
-        ws = torch.empty(max(g.mul_mat_id_workspace_size(H, F, E, top, T), g.mul_mat_id_workspace_size(F, H, E, top, T)),
-                         dtype=torch.uint8, device=dev)
+        ws = torch.empty(max(g.mul_mat_id_workspace_size(H, F, E, top, T), g.mul_mat_id_workspace_size(F, H, E, top, T),
+                             g.mul_mat_id_ffn_workspace_size(H, F, E, top, T)), dtype=torch.uint8, device=dev)
 
         def one(wst, K, N, b, ne11, y):
             rc = g.mul_mat_id(wt, wst, K, N, E, b, K * 4, ne11 * K * 4, ne11, ids, 4, top * 4, top, T, y, N * 4,
                               top * N * 4, ws, err)
             g.check(rc, "mul_mat_id")
 
-        def layer():
-            # gate and up read the same x and ids: one route and gather-pack for both (the group
-            # graph_compute forms from the two MUL_MAT_ID nodes)
+        def layer_chain():
+            # the ops one by one, as graph_compute runs them when the chain cannot fuse: gate and
+            # up as one group (one route and gather-pack), SWIGLU, down
             rc = g.mul_mat_id_group(wt, [w_gate, w_up], [F, F], H, E, x, H * 4, H * 4, 1, ids, 4, top * 4, top, T,
                                     [y_gate, y_up], [F * 4, F * 4], [top * F * 4, top * F * 4], ws, err)
             g.check(rc, "mul_mat_id_group")
             g.check(g.swiglu(y_gate, y_up, h), "swiglu")
             one(w_down, F, H, h, top, y_down)
 
+        def layer():
+            # the fused expert FFN graph_compute forms from the four nodes: one route for the
+            # three projections, SWIGLU fused into the down projection's packing
+            g.check(g.mul_mat_id_ffn(wt, w_gate, w_up, wt, w_down, H, F, E, x, H * 4, H * 4, 1, ids, 4, top * 4, top,
+                                     T, y_down, H * 4, top * H * 4, ws, err), "mul_mat_id_ffn")
+
     stream = torch.cuda.current_stream()
-    for _ in range(args.warmup):
-        flush.zero_()
-        layer()
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    times = []
-    for _ in range(args.steps):
-        flush.zero_()
-        torch.cuda._sleep(400000)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        layer()
-        e1.record(stream)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            flush.zero_()
+            fn()
         torch.cuda.synchronize()
-        times.append(e0.elapsed_time(e1))
-    if int(err.item()) != 0:
-        raise SystemExit(f"device error {int(err.item())}")
-    ms_local = sorted(times)[len(times) // 2]
+        if world > 1:
+            torch.distributed.barrier()
+        times = []
+        for _ in range(args.steps):
+            flush.zero_()
+            torch.cuda._sleep(400000)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        if int(err.item()) != 0:
+            raise SystemExit(f"device error {int(err.item())}")
+        return sorted(times)[len(times) // 2]
+
+    ms_local = timed(layer)
+    chain_ms = timed(layer_chain) if world == 1 and not inside else None
     t = torch.tensor([ms_local], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -733,6 +744,7 @@ def run_moe(args, world_override=None, inside=False):
                            "weights": "16 distinct N(0,0.02) Q4_K experts per stack, repeated to 128",
                            "median_of_steps": True},
                 "tflops": tf,
+                "op_chain_ms_per_layer": chain_ms,
                 "roofline": {"bound": "tensor", "achieved": tf / world, "peak": float(peaks["bf16_tflops"]),
                              "unit": "TFLOP/s", "frac": tf / world / float(peaks["bf16_tflops"]),
                              "peak_source": f"{src} bf16_tflops (burst)"}}

@@ -1327,6 +1327,95 @@ static bool mmid_groupable(const b200_tensor* a, const b200_tensor* c) {
            c->src[0]->type == a->src[0]->type && ggml_backend_b200_supports_op(c);
 }
 
+// A MoE block's expert FFN as ggml builds it: MUL_MAT_ID up and gate over the same x and ids
+// (nodes i and i + 1, either order), GLU SWIGLU of the two (i + 2), and the down MUL_MAT_ID of the
+// SWIGLU over the same ids (i + 3). It runs as one b200_mul_mat_id_ffn (one route, the SWIGLU fused
+// into the down projection's packing) when the three intermediate tensors are device tensors that
+// no other node reads: they are then never written. *gate / *up: the nodes silu and the product
+// take (the GLU's swapped flag exchanges them).
+static bool moe_ffn_match(b200_tensor* const* nodes, int n, int i, const std::vector<bool>& done,
+                          const b200_tensor** gate, const b200_tensor** up) {
+    if (i + 3 >= n || done[i + 1] || done[i + 2] || done[i + 3]) return false;
+    const b200_tensor* p0 = nodes[i];
+    const b200_tensor* p1 = nodes[i + 1];
+    const b200_tensor* glu = nodes[i + 2];
+    const b200_tensor* down = nodes[i + 3];
+    if (!mmid_groupable(p0, p1) || glu->op != B200_OP_GLU || glu->op_params[0] != B200_GLU_SWIGLU || !glu->src[1] ||
+        !ggml_backend_b200_supports_op(glu))
+        return false;
+    if (!((glu->src[0] == p0 && glu->src[1] == p1) || (glu->src[0] == p1 && glu->src[1] == p0))) return false;
+    const bool swapped = glu->op_params[1] != 0;
+    *gate = swapped ? glu->src[1] : glu->src[0];
+    *up = swapped ? glu->src[0] : glu->src[1];
+    if (down->op != B200_OP_MUL_MAT_ID || down->src[1] != glu || down->src[2] != p0->src[2] ||
+        !ggml_backend_b200_supports_op(down))
+        return false;
+    const b200_tensor* wg = (*gate)->src[0];
+    const b200_tensor* wd = down->src[0];
+    const int64_t H = wg->ne[0], F = wg->ne[1], E = wg->ne[2];
+    if (wd->ne[0] != F || wd->ne[1] != H || wd->ne[2] != E || (*up)->src[0]->ne[1] != F) return false;
+    // h [F, n_used, n_tokens]: the down projection reads row (slot, token) of it
+    if (glu->ne[0] != F || glu->ne[1] != p0->src[2]->ne[0] || glu->ne[2] != p0->src[2]->ne[1]) return false;
+    if (H % 32 || F % 32 || F > 8192) return false;
+    const b200_tensor* mid[3] = {p0, p1, glu};
+    for (const b200_tensor* t : mid)
+        if (!t->on_device) return false;
+    for (int j = 0; j < n; j++) {
+        if (j >= i && j <= i + 3) continue;
+        for (int k = 0; k < B200_MAX_SRC; k++)
+            for (const b200_tensor* t : mid)
+                if (nodes[j]->src[k] == t) return false;
+    }
+    return true;
+}
+
+int do_moe_ffn(b200_backend* b, const b200_tensor* gate, const b200_tensor* up, const b200_tensor* down) {
+    const b200_tensor* x = gate->src[1];
+    const b200_tensor* ids = gate->src[2];
+    const b200_tensor* st[3] = {gate->src[0], up->src[0], down->src[0]};
+    const int64_t H = st[0]->ne[0], F = st[0]->ne[1], n_expert = st[0]->ne[2];
+    const int64_t ne11 = x->ne[1], n_used = ids->ne[0], n_tokens = ids->ne[1];
+    const void* w[3];
+    int kt[3];
+    for (int m = 0; m < 3; m++) {
+        const std::string key = weight_key(st[m]);
+        const int64_t rows = st[m]->ne[1] * n_expert, K = st[m]->ne[0];
+        w[m] = pack_weight(b, key, st[m]->type, st[m]->data, st[m]->on_device != 0, rows, K, &kt[m]);
+        if (!w[m]) return B200_E_CUDA;
+        if (!key.empty() && !b->moe_seen[key]) {
+            b->moe_seen[key] = true;
+            b->moe_resident++;
+        } else if (key.empty()) {
+            b->moe_streamed++;
+        }
+    }
+    if (kt[0] != kt[1]) return B200_E_UNSUPPORTED;
+    OpStaging stg;
+    stg.ins = {x, ids};
+    stg.outs = {down};
+    if (!op_reserve(b, stg)) return B200_E_CUDA;
+    if (!grow(&b->ws, &b->ws_bytes, b200_mul_mat_id_ffn_workspace_size(H, F, n_expert, n_used, n_tokens), b->stream))
+        return B200_E_CUDA;
+    bool ok = true;
+    const void* xd = stage_in(b, x, &ok);
+    const void* idd = stage_in(b, ids, &ok);
+    char* dd = stage_out(b, down, false, &ok);
+    if (!ok || !op_inputs_ready(b)) return B200_E_CUDA;
+    const int rc = b200_mul_mat_id_ffn(kt[0], w[0], w[1], kt[2], w[2], H, F, n_expert, static_cast<const float*>(xd),
+                                       (int64_t)x->nb[1], (int64_t)x->nb[2], ne11, static_cast<const int32_t*>(idd),
+                                       (int64_t)ids->nb[0], (int64_t)ids->nb[1], n_used, n_tokens,
+                                       reinterpret_cast<float*>(dd), (int64_t)down->nb[1], (int64_t)down->nb[2], b->ws,
+                                       b->ws_bytes, b->dev_err, b->stream);
+    if (rc != B200_OK) return rc;
+    std::vector<char*> bases{dd};
+    if (!op_outputs_done(b, stg.outs, bases)) return B200_E_CUDA;
+    b->route_ops["moe"] += 3;
+    b->route_ops["moe_grouped"] += 2;
+    b->route_ops["moe_ffn"]++;
+    b->route_ops["glue"]++;
+    return B200_OK;
+}
+
 int do_flash_attn(b200_backend* b, b200_tensor* op) {
     const b200_tensor* q = op->src[0];
     const b200_tensor* k = op->src[1];
@@ -1781,6 +1870,22 @@ int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes,
                 if (!ggml_backend_b200_supports_op(node)) {
                     status = B200_STATUS_FAILED;
                     break;
+                }
+                const b200_tensor* ffn_gate = nullptr;
+                const b200_tensor* ffn_up = nullptr;
+                if (fuse && breaker_allow(b->brk_fused) && moe_ffn_match(nodes, n, i, done, &ffn_gate, &ffn_up)) {
+                    // gate, up, SWIGLU and down in one pass over one route
+                    const int rc = do_moe_ffn(b, ffn_gate, ffn_up, nodes[i + 3]);
+                    breaker_note(b->brk_fused, rc, "fused MoE FFN");
+                    if (rc == B200_OK || rc == B200_E_BAD_IDS) {
+                        if (rc != B200_OK) {
+                            logf("E", "graph_compute: MUL_MAT_ID handler failed (%d)\n", rc);
+                            status = B200_STATUS_FAILED;
+                        }
+                        done[i] = done[i + 1] = done[i + 2] = done[i + 3] = true;
+                        break;
+                    }
+                    // otherwise the four nodes run one by one below
                 }
                 std::vector<b200_tensor*> group{node};
                 std::vector<int> gidx{i};

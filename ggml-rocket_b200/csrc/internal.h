@@ -69,9 +69,14 @@ int gemm_grouped_impl(int wtype, const void* w_stack, int64_t N, int64_t K, int6
                       cudaStream_t st, const int32_t* src = nullptr, float* const* dst_bases = nullptr);
 // Gather b[:, slot[r] % ne11, tok[r]] for r < *n_rows (device count; max_rows bounds the grid)
 // and pack each row to fp16 with its per-row scale (moe.cu).
+// self (optional): self[r] = r for every row, the token / slot index of an output in row order.
 int launch_gather_pack(const float* b, int64_t b_nb1, int64_t b_nb2, int64_t ne11, int64_t K, const int32_t* slot,
                        const int32_t* tok, const int32_t* n_rows, int64_t max_rows, __half* a16, float* scales,
-                       cudaStream_t st);
+                       cudaStream_t st, int32_t* self = nullptr);
+// The expert FFN between its projections: h16[r] / hscale[r] = the packed row swiglu(gate[r],
+// up[r]) for r < *n_rows (f32 rows of F; max_rows bounds the grid), moe.cu.
+int launch_swiglu_pack(const float* gate, const float* up, int64_t F, const int32_t* n_rows, int64_t max_rows,
+                       __half* h16, float* hscale, cudaStream_t st);
 
 // expert parallelism helpers shared by the NCCL and peer-memory paths (moe_ep.cu)
 int ep_token_tile_public(int64_t pairs, int64_t e_loc);

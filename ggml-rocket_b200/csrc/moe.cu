@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 
 #include "ggml-b200-kernels.h"
+#include "glu.cuh"
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -194,12 +195,14 @@ __global__ void __launch_bounds__(256) moe_gather_pack_kernel(const float* __res
                                                               const int32_t* __restrict__ slot,
                                                               const int32_t* __restrict__ tok,
                                                               const int32_t* __restrict__ off_total,
-                                                              __half* __restrict__ a16, float* __restrict__ scales) {
+                                                              __half* __restrict__ a16, float* __restrict__ scales,
+                                                              int32_t* __restrict__ self) {
     grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
     grid_dep_launch();
     __shared__ float red[8];
     const int r = blockIdx.x;
     if (r >= __ldg(off_total)) return;   // a bad-id op has no rows
+    if (self && threadIdx.x == 0) self[r] = r;   // the expert FFN's own rows: row r of a [rows][N] buffer
     const int s = __ldg(slot + r), t = __ldg(tok + r);
     const float4* row = reinterpret_cast<const float4*>(reinterpret_cast<const char*>(b) + (int64_t)t * b_nb2 +
                                                         (int64_t)(s % ne11) * b_nb1);
@@ -237,13 +240,13 @@ __global__ void __launch_bounds__(256) moe_gather_pack_kernel(const float* __res
 
 int launch_gather_pack(const float* b, int64_t b_nb1, int64_t b_nb2, int64_t ne11, int64_t K, const int32_t* slot,
                        const int32_t* tok, const int32_t* n_rows, int64_t max_rows, __half* a16, float* scales,
-                       cudaStream_t st) {
+                       cudaStream_t st, int32_t* self) {
     if (max_rows <= 0) return B200_OK;
     const int64_t per = (K / 4 + 255) / 256;
     const dim3 grid((unsigned)max_rows);
 #define B200_GATHER(V) \
     launch_pdl(moe_gather_pack_kernel<V>, dim3(grid), dim3(256), 0, st, b, b_nb1, b_nb2, (int)ne11, (int)K, slot, tok, \
-               n_rows, a16, scales)
+               n_rows, a16, scales, self)
     if (per <= 1) B200_GATHER(1);
     else if (per <= 2) B200_GATHER(2);
     else if (per <= 4) B200_GATHER(4);
@@ -251,6 +254,76 @@ int launch_gather_pack(const float* b, int64_t b_nb1, int64_t b_nb2, int64_t ne1
     else if (per <= 16) B200_GATHER(16);
     else return B200_E_UNSUPPORTED;
 #undef B200_GATHER
+    return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
+// The expert FFN between its projections: row p's down-projection input h = swiglu(gate[p], up[p])
+// (f32 rows of F, in the route's sorted order), packed like every activation row of the GEMMs
+// (s = max|h| or 1, fp16(h * (1/s))). The arithmetic is the SWIGLU glue kernel's followed by the
+// gather-pack's, so the packed rows equal, bit for bit, those the op chain MUL_MAT_ID, SWIGLU,
+// MUL_MAT_ID builds for the down projection. One 256-thread CTA per row (grid-stride over the
+// device's row count), V float4 per thread.
+template <int V>
+__global__ void __launch_bounds__(256) swiglu_pack_kernel(const float* __restrict__ gate, const float* __restrict__ up,
+                                                             int F, const int32_t* __restrict__ n_rows,
+                                                             __half* __restrict__ a16, float* __restrict__ scales) {
+    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
+    grid_dep_launch();
+    __shared__ float red[8];
+    const int n = __ldg(n_rows);
+    const int n4 = F / 4;
+    for (int p = blockIdx.x; p < n; p += gridDim.x) {
+        const float4* g4 = reinterpret_cast<const float4*>(gate + (int64_t)p * F);
+        const float4* u4 = reinterpret_cast<const float4*>(up + (int64_t)p * F);
+        float4 v[V];
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < V; i++) {
+            const int idx = threadIdx.x + i * 256;
+            if (idx < n4) {
+                const float4 x = g4[idx], y = u4[idx];
+                v[i] = make_float4(swiglu_f(x.x, y.x), swiglu_f(x.y, y.y), swiglu_f(x.z, y.z), swiglu_f(x.w, y.w));
+            } else {
+                v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+        __syncthreads();
+        amax = red[0];
+#pragma unroll
+        for (int w = 1; w < 8; w++) amax = fmaxf(amax, red[w]);
+        __syncthreads();   // red is rewritten by the next row
+        const float sc = amax > 0.0f ? amax : 1.0f;
+        const float inv = __frcp_rn(sc);
+        if (threadIdx.x == 0) scales[p] = sc;
+        uint2* out = reinterpret_cast<uint2*>(a16 + (int64_t)p * F);
+#pragma unroll
+        for (int i = 0; i < V; i++) {
+            const int idx = threadIdx.x + i * 256;
+            if (idx < n4) {
+                uint2 w;
+                w.x = pack_half2(__fmul_rn(v[i].x, inv), __fmul_rn(v[i].y, inv));
+                w.y = pack_half2(__fmul_rn(v[i].z, inv), __fmul_rn(v[i].w, inv));
+                out[idx] = w;
+            }
+        }
+    }
+}
+
+int launch_swiglu_pack(const float* gate, const float* up, int64_t F, const int32_t* n_rows, int64_t max_rows,
+                       __half* h16, float* hscale, cudaStream_t st) {
+    if (max_rows <= 0) return B200_OK;
+    if (F % 8 || F > 8192) return B200_E_UNSUPPORTED;
+    const int64_t gcap = (int64_t)device_sm_count() * 8;
+    const dim3 grid((unsigned)(max_rows < gcap ? max_rows : gcap));
+    const int64_t v = (F / 4 + 255) / 256;
+    if (v <= 1) launch_pdl(swiglu_pack_kernel<1>, grid, dim3(256), 0, st, gate, up, (int)F, n_rows, h16, hscale);
+    else if (v <= 2) launch_pdl(swiglu_pack_kernel<2>, grid, dim3(256), 0, st, gate, up, (int)F, n_rows, h16, hscale);
+    else if (v <= 4) launch_pdl(swiglu_pack_kernel<4>, grid, dim3(256), 0, st, gate, up, (int)F, n_rows, h16, hscale);
+    else launch_pdl(swiglu_pack_kernel<8>, grid, dim3(256), 0, st, gate, up, (int)F, n_rows, h16, hscale);
     return cudaGetLastError() == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 
@@ -282,6 +355,49 @@ static int moe_token_tile(int64_t R, int64_t n_expert) {
     return avg <= 32 ? 32 : avg <= 64 ? 64 : avg < 96 ? 128 : 256;
 }
 
+// The route and the packed rows every grouped GEMM of an op reads: the histogram, scan and
+// placement of the (token, slot) pairs by expert, then the gather-pack of their b rows in that
+// order (self, when given, gets each sorted row's own index).
+struct MoeRoute {
+    int32_t *off, *tiles, *slot, *tok;
+    __half* a16;
+    float* scales;
+    int64_t R;
+    int bt;
+};
+
+static int moe_route_gather(const MoeLayout& L, char* ws, int64_t K, int64_t n_expert, const float* b, int64_t b_nb1,
+                            int64_t b_nb2, int64_t ne11, const int32_t* ids, int64_t ids_nb0, int64_t ids_nb1,
+                            int64_t n_used, int64_t n_tokens, int32_t* self, int* dev_err, cudaStream_t st,
+                            MoeRoute* out) {
+    int32_t* off = reinterpret_cast<int32_t*>(ws + L.off);
+    int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
+    int32_t* slot = reinterpret_cast<int32_t*>(ws + L.slot);
+    int32_t* tok = reinterpret_cast<int32_t*>(ws + L.tok);
+    __half* a16 = reinterpret_cast<__half*>(ws + L.a16);
+    float* scales = reinterpret_cast<float*>(ws + L.scales);
+    const int64_t R = n_used * n_tokens;
+    const int bt = moe_token_tile(R, n_expert);
+    *out = MoeRoute{off, tiles, slot, tok, a16, scales, R, bt};
+    int32_t* counts = reinterpret_cast<int32_t*>(ws + L.counts);
+    int32_t* bad = reinterpret_cast<int32_t*>(ws + L.bad);
+    const int nb = (int)((R + ROUTE_CHUNK - 1) / ROUTE_CHUNK);
+    const size_t hist_smem = (size_t)n_expert * sizeof(int);
+    const size_t place_smem = (size_t)33 * n_expert * sizeof(int);
+    if (place_smem > 48 * 1024 &&
+        cudaFuncSetAttribute(moe_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)place_smem) !=
+            cudaSuccess)
+        return B200_E_UNSUPPORTED;
+    launch_pdl(moe_hist_kernel, dim3(nb), dim3(ROUTE_THREADS), hist_smem, st, ids, ids_nb0, ids_nb1, (int)n_used,
+               (int)R, (int)n_expert, counts, bad);
+    launch_pdl(moe_scan_kernel, dim3(1), dim3(ROUTE_THREADS), hist_smem, st, counts, bad, nb, (int)n_expert, bt, off,
+               tiles, dev_err);
+    launch_pdl(moe_place_kernel, dim3(nb), dim3(ROUTE_THREADS), place_smem, st, ids, ids_nb0, ids_nb1, (int)n_used,
+               (int)R, (int)n_expert, counts, off, slot, tok);
+    if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
+    return launch_gather_pack(b, b_nb1, b_nb2, ne11, K, slot, tok, off + n_expert, R, a16, scales, st, self);
+}
+
 // MUL_MAT_ID over n_members expert stacks that share the input rows b and the routing ids (a
 // layer's gate and up projections): the route and the gather-pack run once, then one grouped
 // GEMM per member reads the same sorted fp16 rows. n_members = 1 is the plain op.
@@ -302,37 +418,13 @@ int mul_mat_id_group_impl(int n_members, int wtype, const void* const* as_packed
     if ((b_nb1 % 16) || (b_nb2 % 16) || (reinterpret_cast<uintptr_t>(b) & 15u)) return B200_E_UNSUPPORTED;
     const MoeLayout L = moe_layout(K, n_expert, n_used, n_tokens);
     if (!workspace || ws_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255u)) return B200_E_WORKSPACE;
-    char* ws = static_cast<char*>(workspace);
-    int32_t* off = reinterpret_cast<int32_t*>(ws + L.off);
-    int32_t* tiles = reinterpret_cast<int32_t*>(ws + L.tiles);
-    int32_t* slot = reinterpret_cast<int32_t*>(ws + L.slot);
-    int32_t* tok = reinterpret_cast<int32_t*>(ws + L.tok);
-    __half* a16 = reinterpret_cast<__half*>(ws + L.a16);
-    float* scales = reinterpret_cast<float*>(ws + L.scales);
-    const int64_t R = n_used * n_tokens;
-    const int bt = moe_token_tile(R, n_expert);
-
-    int32_t* counts = reinterpret_cast<int32_t*>(ws + L.counts);
-    int32_t* bad = reinterpret_cast<int32_t*>(ws + L.bad);
-    const int nb = (int)((R + ROUTE_CHUNK - 1) / ROUTE_CHUNK);
-    const size_t hist_smem = (size_t)n_expert * sizeof(int);
-    const size_t place_smem = (size_t)33 * n_expert * sizeof(int);
-    if (place_smem > 48 * 1024 &&
-        cudaFuncSetAttribute(moe_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)place_smem) !=
-            cudaSuccess)
-        return B200_E_UNSUPPORTED;
-    launch_pdl(moe_hist_kernel, dim3(nb), dim3(ROUTE_THREADS), hist_smem, st, ids, ids_nb0, ids_nb1, (int)n_used,
-               (int)R, (int)n_expert, counts, bad);
-    launch_pdl(moe_scan_kernel, dim3(1), dim3(ROUTE_THREADS), hist_smem, st, counts, bad, nb, (int)n_expert, bt, off,
-               tiles, dev_err);
-    launch_pdl(moe_place_kernel, dim3(nb), dim3(ROUTE_THREADS), place_smem, st, ids, ids_nb0, ids_nb1, (int)n_used,
-               (int)R, (int)n_expert, counts, off, slot, tok);
-    if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
-    const int rc = launch_gather_pack(b, b_nb1, b_nb2, ne11, K, slot, tok, off + n_expert, R, a16, scales, st);
+    MoeRoute R;
+    const int rc = moe_route_gather(L, static_cast<char*>(workspace), K, n_expert, b, b_nb1, b_nb2, ne11, ids, ids_nb0,
+                                    ids_nb1, n_used, n_tokens, nullptr, dev_err, st, &R);
     if (rc != B200_OK) return rc;
     for (int m = 0; m < n_members; m++) {
-        const int r2 = gemm_grouped_impl(wtype, as_packed[m], Ns[m], K, n_expert, a16, scales, R, bt, off, tiles, slot,
-                                         tok, dsts[m], d_nb1s[m], d_nb2s[m], dev_err, st);
+        const int r2 = gemm_grouped_impl(wtype, as_packed[m], Ns[m], K, n_expert, R.a16, R.scales, R.R, R.bt, R.off,
+                                         R.tiles, R.slot, R.tok, dsts[m], d_nb1s[m], d_nb2s[m], dev_err, st);
         if (r2 != B200_OK) return r2;
     }
     return B200_OK;
@@ -345,6 +437,67 @@ int mul_mat_id_impl(int wtype, const void* as_packed, int64_t K, int64_t N, int6
     if (!as_packed || !dst) return B200_E_INVALID;
     return mul_mat_id_group_impl(1, wtype, &as_packed, &N, K, n_expert, b, b_nb1, b_nb2, ne11, ids, ids_nb0, ids_nb1,
                                  n_used, n_tokens, &dst, &d_nb1, &d_nb2, workspace, ws_bytes, dev_err, st);
+}
+
+// The expert FFN of a MoE block, down(swiglu(gate(x), up(x))) per (token, slot), in one pass
+// over one route: the pairs are routed and x's rows gathered once, gate and up write [R][F]
+// buffers in the route's order (each row's token index is the row itself), the SWIGLU and the
+// down projection's packing run in one kernel over those rows, and the down GEMM reuses the
+// route to store dst. The single-GPU twin of the expert-parallel owner step; the result equals,
+// bit for bit, MUL_MAT_ID group (gate, up) -> SWIGLU -> MUL_MAT_ID (down).
+struct MoeFfnLayout {
+    MoeLayout base;
+    size_t self, gate, up, h16, hscale, total;
+};
+
+static MoeFfnLayout moe_ffn_layout(int64_t H, int64_t F, int64_t n_expert, int64_t n_used, int64_t n_tokens) {
+    auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    const size_t R = (size_t)(n_used * n_tokens);
+    MoeFfnLayout L{};
+    L.base = moe_layout(H, n_expert, n_used, n_tokens);
+    L.self = L.base.total;
+    L.gate = L.self + al(R * 4);
+    L.up = L.gate + al(R * (size_t)F * 4);
+    L.h16 = L.up + al(R * (size_t)F * 4);
+    L.hscale = L.h16 + al(R * (size_t)F * 2);
+    L.total = L.hscale + al(R * 4);
+    return L;
+}
+
+int mul_mat_id_ffn_impl(int wt_gate_up, const void* gate_packed, const void* up_packed, int wt_down,
+                        const void* down_packed, int64_t H, int64_t F, int64_t n_expert, const float* x, int64_t x_nb1,
+                        int64_t x_nb2, int64_t ne11, const int32_t* ids, int64_t ids_nb0, int64_t ids_nb1,
+                        int64_t n_used, int64_t n_tokens, float* dst, int64_t d_nb1, int64_t d_nb2, void* workspace,
+                        size_t ws_bytes, int* dev_err, cudaStream_t st) {
+    if (!gate_packed || !up_packed || !down_packed || !x || !ids || !dst || !dev_err || H <= 0 || F <= 0 ||
+        n_expert <= 0 || n_used <= 0 || n_tokens <= 0 || ne11 <= 0)
+        return B200_E_INVALID;
+    if (!weight_type_supported(wt_gate_up, H) || !weight_type_supported(wt_down, F) || H % 32 || F % 32 || F > 8192)
+        return B200_E_UNSUPPORTED;
+    if (n_expert > 4096 || n_used * n_tokens > (1 << 28)) return B200_E_UNSUPPORTED;
+    if ((x_nb1 % 16) || (x_nb2 % 16) || (reinterpret_cast<uintptr_t>(x) & 15u)) return B200_E_UNSUPPORTED;
+    const MoeFfnLayout L = moe_ffn_layout(H, F, n_expert, n_used, n_tokens);
+    if (!workspace || ws_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255u)) return B200_E_WORKSPACE;
+    char* ws = static_cast<char*>(workspace);
+    int32_t* self = reinterpret_cast<int32_t*>(ws + L.self);
+    float* gate = reinterpret_cast<float*>(ws + L.gate);
+    float* up = reinterpret_cast<float*>(ws + L.up);
+    __half* h16 = reinterpret_cast<__half*>(ws + L.h16);
+    float* hscale = reinterpret_cast<float*>(ws + L.hscale);
+    MoeRoute R;
+    int rc = moe_route_gather(L.base, ws, H, n_expert, x, x_nb1, x_nb2, ne11, ids, ids_nb0, ids_nb1, n_used, n_tokens,
+                              self, dev_err, st, &R);
+    if (rc != B200_OK) return rc;
+    rc = gemm_grouped_impl(wt_gate_up, gate_packed, F, H, n_expert, R.a16, R.scales, R.R, R.bt, R.off, R.tiles, self,
+                           self, gate, 0, F * 4, dev_err, st);
+    if (rc != B200_OK) return rc;
+    rc = gemm_grouped_impl(wt_gate_up, up_packed, F, H, n_expert, R.a16, R.scales, R.R, R.bt, R.off, R.tiles, self,
+                           self, up, 0, F * 4, dev_err, st);
+    if (rc != B200_OK) return rc;
+    rc = launch_swiglu_pack(gate, up, F, R.off + n_expert, R.R, h16, hscale, st);
+    if (rc != B200_OK) return rc;
+    return gemm_grouped_impl(wt_down, down_packed, H, F, n_expert, h16, hscale, R.R, R.bt, R.off, R.tiles, R.slot, R.tok,
+                             dst, d_nb1, d_nb2, dev_err, st);
 }
 
 }  // namespace b200
@@ -375,6 +528,21 @@ int b200_mul_mat_id_group(int n_members, int wtype, const void* const* as_packed
     return b200::mul_mat_id_group_impl(n_members, wtype, as_packed, N, K, n_expert, b, b_nb1, b_nb2, ne11, ids, ids_nb0,
                                        ids_nb1, n_used, n_tokens, dst, d_nb1, d_nb2, workspace, workspace_bytes,
                                        dev_err, static_cast<cudaStream_t>(stream));
+}
+
+size_t b200_mul_mat_id_ffn_workspace_size(int64_t H, int64_t F, int64_t n_expert, int64_t n_used, int64_t n_tokens) {
+    if (H <= 0 || F <= 0 || n_expert <= 0 || n_used <= 0 || n_tokens <= 0) return 0;
+    return b200::moe_ffn_layout(H, F, n_expert, n_used, n_tokens).total;
+}
+
+int b200_mul_mat_id_ffn(int wtype_gate_up, const void* gate_packed, const void* up_packed, int wtype_down,
+                        const void* down_packed, int64_t H, int64_t F, int64_t n_expert, const float* x, int64_t x_nb1,
+                        int64_t x_nb2, int64_t ne11, const int32_t* ids, int64_t ids_nb0, int64_t ids_nb1,
+                        int64_t n_used, int64_t n_tokens, float* dst, int64_t d_nb1, int64_t d_nb2, void* workspace,
+                        size_t workspace_bytes, int* dev_err, void* stream) {
+    return b200::mul_mat_id_ffn_impl(wtype_gate_up, gate_packed, up_packed, wtype_down, down_packed, H, F, n_expert, x,
+                                     x_nb1, x_nb2, ne11, ids, ids_nb0, ids_nb1, n_used, n_tokens, dst, d_nb1, d_nb2,
+                                     workspace, workspace_bytes, dev_err, static_cast<cudaStream_t>(stream));
 }
 
 int b200_mul_mat_id_route_view(int64_t K, int64_t n_expert, int64_t n_used, int64_t n_tokens, size_t* off_offset,

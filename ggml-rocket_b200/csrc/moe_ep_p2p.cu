@@ -26,7 +26,6 @@
 #include <cuda_runtime.h>
 
 #include "ggml-b200-kernels.h"
-#include "glu.cuh"
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -230,61 +229,6 @@ __global__ void __launch_bounds__(256) p2p_gather_kernel(const __half* __restric
         uint4* d = reinterpret_cast<uint4*>(dst + (int64_t)p * K);
         for (int i = threadIdx.x; i < K / 8; i += 256) d[i] = __ldg(s + i);
         if (threadIdx.x == 0) dst_scale[p] = __int_as_float(__ldg(meta + rr * MW));
-    }
-}
-
-// Expert FFN on the owner: pair p's down-projection input h = swiglu(gate[p], up[p]) (f32 rows
-// of F), packed like every activation row of the GEMMs (s = max|h| or 1, fp16(h * (1/s))). The
-// arithmetic is that of the SWIGLU glue kernel followed by the MUL_MAT_ID gather-pack, so the
-// packed rows equal, bit for bit, those the single-GPU op chain builds for the down projection.
-// One 256-thread CTA per pair row (grid-stride over the device count), V float4 per thread.
-template <int V>
-__global__ void __launch_bounds__(256) ep_swiglu_pack_kernel(const float* __restrict__ gate, const float* __restrict__ up,
-                                                             int F, const int32_t* __restrict__ n_pairs,
-                                                             __half* __restrict__ a16, float* __restrict__ scales) {
-    grid_dep_wait();   // programmatic launch: the previous kernel's output is complete
-    grid_dep_launch();
-    __shared__ float red[8];
-    const int n = __ldg(n_pairs);
-    const int n4 = F / 4;
-    for (int p = blockIdx.x; p < n; p += gridDim.x) {
-        const float4* g4 = reinterpret_cast<const float4*>(gate + (int64_t)p * F);
-        const float4* u4 = reinterpret_cast<const float4*>(up + (int64_t)p * F);
-        float4 v[V];
-        float amax = 0.0f;
-#pragma unroll
-        for (int i = 0; i < V; i++) {
-            const int idx = threadIdx.x + i * 256;
-            if (idx < n4) {
-                const float4 x = g4[idx], y = u4[idx];
-                v[i] = make_float4(swiglu_f(x.x, y.x), swiglu_f(x.y, y.y), swiglu_f(x.z, y.z), swiglu_f(x.w, y.w));
-            } else {
-                v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
-        __syncthreads();
-        amax = red[0];
-#pragma unroll
-        for (int w = 1; w < 8; w++) amax = fmaxf(amax, red[w]);
-        __syncthreads();   // red is rewritten by the next row
-        const float sc = amax > 0.0f ? amax : 1.0f;
-        const float inv = __frcp_rn(sc);
-        if (threadIdx.x == 0) scales[p] = sc;
-        uint2* out = reinterpret_cast<uint2*>(a16 + (int64_t)p * F);
-#pragma unroll
-        for (int i = 0; i < V; i++) {
-            const int idx = threadIdx.x + i * 256;
-            if (idx < n4) {
-                uint2 w;
-                w.x = pack_half2(__fmul_rn(v[i].x, inv), __fmul_rn(v[i].y, inv));
-                w.y = pack_half2(__fmul_rn(v[i].z, inv), __fmul_rn(v[i].w, inv));
-                out[idx] = w;
-            }
-        }
     }
 }
 
@@ -542,15 +486,8 @@ int b200_moe_ep_p2p_expert_ffn(int wtype_gate_up, const void* gate_stack, const 
                            self, self, up, 0, F * 4, dev_err, st);
     if (rc != B200_OK) return rc;
     // 5. h = swiglu(gate, up), packed for the down projection in the same pair order
-    const int64_t gcap = (int64_t)device_sm_count() * 8;
-    const dim3 pg((unsigned)(rows_max < gcap ? rows_max : gcap));
-    const int v = (int)((F / 4 + 255) / 256);
-    const int32_t* n_pairs = R.off + n_local;
-    if (v <= 1) launch_pdl(ep_swiglu_pack_kernel<1>, pg, dim3(256), 0, st, gate, up, (int)F, n_pairs, h16, hscale);
-    else if (v <= 2) launch_pdl(ep_swiglu_pack_kernel<2>, pg, dim3(256), 0, st, gate, up, (int)F, n_pairs, h16, hscale);
-    else if (v <= 4) launch_pdl(ep_swiglu_pack_kernel<4>, pg, dim3(256), 0, st, gate, up, (int)F, n_pairs, h16, hscale);
-    else launch_pdl(ep_swiglu_pack_kernel<8>, pg, dim3(256), 0, st, gate, up, (int)F, n_pairs, h16, hscale);
-    if (cudaGetLastError() != cudaSuccess) return B200_E_CUDA;
+    rc = launch_swiglu_pack(gate, up, F, R.off + n_local, rows_max, h16, hscale, st);
+    if (rc != B200_OK) return rc;
     // 6. down over the same route; the epilogue stores each row into its home rank's ret
     rc = gemm_grouped_impl(wtype_down, down_stack, H, F, n_local, h16, hscale, rows_max, R.bt, R.off, R.tiles, R.pslot,
                            R.ptok, nullptr, ret_nb1, ret_nb2, dev_err, st, R.psrc, peer_ret);

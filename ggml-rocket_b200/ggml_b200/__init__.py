@@ -20,7 +20,7 @@ BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q8_0: (32, 34),
 B200_OK = 0
 STATUS = {0: "ok", -1: "invalid", -2: "unsupported", -3: "cuda", -4: "device", -5: "workspace",
           -6: "bad_ids", -7: "no_device", -8: "too_large"}
-B200_E_INVALID, B200_E_UNSUPPORTED, B200_E_TOO_LARGE = -1, -2, -8
+B200_E_INVALID, B200_E_UNSUPPORTED, B200_E_WORKSPACE, B200_E_TOO_LARGE = -1, -2, -5, -8
 
 
 class B200Error(RuntimeError):
@@ -275,6 +275,9 @@ _SIGS.update({
     "b200_moe_ep_p2p_expert_group": (_int, [_int, _int, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i64,
                                             _i64, _i64, _vp, _vp, _vp, _vp, _int, _vp, _sz, _vp, _vp]),
     "b200_moe_ep_p2p_ffn_workspace_size": (_sz, [_i64] * 6),
+    "b200_mul_mat_id_ffn_workspace_size": (_sz, [_i64] * 5),
+    "b200_mul_mat_id_ffn": (_int, [_int, _vp, _vp, _int, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _i64,
+                                   _i64, _i64, _vp, _i64, _i64, _vp, _sz, _vp, _vp]),
     "b200_moe_ep_p2p_expert_ffn": (_int, [_int, _vp, _vp, _int, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64,
                                           _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _int, _vp, _sz, _vp, _vp]),
     "b200_mul_mat_tp_workspace_size": (_sz, [_int, _i64, _i64, _i64]),
@@ -534,6 +537,19 @@ def swiglu(a, gt, dst, stream=None):
     ne = (ctypes.c_int64 * 4)(inner, n // inner, 1, 1)
     nb = (ctypes.c_size_t * 4)(4, inner * 4, n * 4, n * 4)
     return lib().b200_swiglu(_ptr(a), nb, _ptr(gt), nb, ne, _ptr(dst), _stream(stream))
+
+
+def mul_mat_id_ffn_workspace_size(H, F, n_expert, n_used, n_tokens):
+    return lib().b200_mul_mat_id_ffn_workspace_size(H, F, n_expert, n_used, n_tokens)
+
+
+def mul_mat_id_ffn(wtype_gate_up, gate, up, wtype_down, down, H, F, n_expert, x, x_nb1, x_nb2, ne11, ids, ids_nb0,
+                   ids_nb1, n_used, n_tokens, dst, d_nb1, d_nb2, workspace, dev_err, stream=None):
+    """A MoE block's expert FFN, down(swiglu(gate(x), up(x))), over one route (b200_mul_mat_id_ffn)."""
+    return lib().b200_mul_mat_id_ffn(wtype_gate_up, _ptr(gate), _ptr(up), wtype_down, _ptr(down), H, F, n_expert,
+                                     _ptr(x), x_nb1, x_nb2, ne11, _ptr(ids), ids_nb0, ids_nb1, n_used, n_tokens,
+                                     _ptr(dst), d_nb1, d_nb2, _ptr(workspace),
+                                     workspace.numel() * workspace.element_size(), _ptr(dev_err), _stream(stream))
 
 
 def mul_mat_id_route_view(K, n_expert, n_used, n_tokens):

@@ -254,6 +254,22 @@ int    b200_mul_mat_id_group(int n_members, int wtype, const void * const * as_p
                              int64_t ne11, const int32_t * ids, int64_t ids_nb0, int64_t ids_nb1, int64_t n_used,
                              int64_t n_tokens, float * const * dst, const int64_t * d_nb1, const int64_t * d_nb2,
                              void * workspace, size_t workspace_bytes, int * dev_err, void * stream);
+/* A MoE block's expert FFN in one call: the node chain gate = MUL_MAT_ID(gate_exps, x, ids),
+ * up = MUL_MAT_ID(up_exps, x, ids), h = GLU SWIGLU(gate, up), dst = MUL_MAT_ID(down_exps, h, ids)
+ * that llama.cpp's MoE FFN builds (the reference claims each MUL_MAT_ID on its own,
+ * ggml-rocket.cpp:7497-7653, and leaves the GLU to the host). gate / up stacks: n_expert experts
+ * of [F, H] in wtype_gate_up; down: n_expert of [H, F] in wtype_down; x rows as b200_mul_mat_id's
+ * b with K = H; dst [n_tokens][n_used][H] with strides d_nb1 / d_nb2. The pairs are routed and x
+ * gathered once for all three projections, gate / up / h stay in the workspace
+ * (b200_mul_mat_id_ffn_workspace_size bytes), and SWIGLU is fused into the packing of the down
+ * projection's rows. dst equals, bit for bit, b200_mul_mat_id_group(gate, up), b200_swiglu,
+ * b200_mul_mat_id(down). H and F multiples of 32 and of the weight types' blocks; F <= 8192. */
+size_t b200_mul_mat_id_ffn_workspace_size(int64_t H, int64_t F, int64_t n_expert, int64_t n_used, int64_t n_tokens);
+int    b200_mul_mat_id_ffn(int wtype_gate_up, const void * gate_packed, const void * up_packed, int wtype_down,
+                           const void * down_packed, int64_t H, int64_t F, int64_t n_expert, const float * x,
+                           int64_t x_nb1, int64_t x_nb2, int64_t ne11, const int32_t * ids, int64_t ids_nb0,
+                           int64_t ids_nb1, int64_t n_used, int64_t n_tokens, float * dst, int64_t d_nb1,
+                           int64_t d_nb2, void * workspace, size_t workspace_bytes, int * dev_err, void * stream);
 /* Byte offsets, inside the workspace, of the route arrays the last b200_mul_mat_id call wrote:
  * off int32 [n_expert + 1], row_slot int32 [n_used*n_tokens], row_tok int32 [n_used*n_tokens]. */
 int    b200_mul_mat_id_route_view(int64_t K, int64_t n_expert, int64_t n_used, int64_t n_tokens,
