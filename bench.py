@@ -3,8 +3,8 @@
 
 Workload (one "step"): the quantized prefill GEMM sweep's three (K, N) weight shapes,
 (4096, 4096), (4096, 14336) and (14336, 4096), in Q4_K, each multiplied by a 512-token F32
-activation ubatch, through --layers (default 8) layers: distinct device copies of the weights,
-as a model's layers are. Weights are N(0, 0.02) quantized to Q4_K on the host, activations
+activation ubatch, through --layers (default 32, a Llama-3-8B's depth) layers: distinct device
+copies of the weights, as a model's layers are. Weights are N(0, 0.02) quantized to Q4_K on the host, activations
 N(0, 1), seeded; all synthetic.
 
   value     TFLOP/s of the step on the device, inputs resident in HBM, L2 flushed (a 256 MiB
@@ -56,7 +56,7 @@ def step_flops(m=M_TOKENS):
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["gemm", "gemv", "moe", "fa", "glue", "layer", "crossover"], default="gemm",
@@ -67,7 +67,7 @@ def parse():
                          "headline's prefill shapes (HBM-bound kernels, GB/s); layer: configs[4]'s Llama-3-8B "
                          "layer through graph_compute, prompt tokens/s; crossover: the M at which a claimed "
                          "MUL_MAT with host tensors beats the host CPU")
-    ap.add_argument("--layers", type=int, default=8,
+    ap.add_argument("--layers", type=int, default=32,
                     help="gemm workload: layers (distinct weight copies) the sweep runs through per step")
     ap.add_argument("--decode-type", choices=["q4_k", "q6_k", "q8_0"], default="q4_k",
                     help="gemv workload: weight type")

@@ -34,6 +34,16 @@
 // the CTA holding its last granule, which adds the other CTAs' f32 partials in CTA order:
 // deterministic, with no atomics and no second kernel. The finisher gathers those partials
 // into its idle second TMEM accumulator while its own K range is still on the tensor core.
+//
+// Cluster split (plain MUL_MAT with at most one tile per two SMs, e.g. N = 4096 at M = 512): a
+// cluster of two CTAs takes one tile, each CTA half of its K range. Stream-K would share every
+// such tile between three or four CTAs, and when every piece ends together the partial tiles make
+// three serial trips through L2 at the end of the launch (written, read back, the result
+// written). Here the two halves meet over distributed shared memory instead: CTA r finishes
+// tokens [r BT/2, (r+1) BT/2) of the tile; each epilogue warp sends the other half of its TMEM
+// rows into the peer's idle operand stages (st.shared::cluster, mbarrier arrives at cluster
+// scope), and adds what it receives to its own half. Addition of two terms commutes, so both
+// halves of the tile carry the same sums whichever CTA adds them.
 #pragma once
 
 #include <cstdint>
@@ -84,6 +94,9 @@ struct GemmArgs {
     // at column col0 + n -- the all-gather done by the epilogue's own stores over NVLink
     int n_dst;
     int col0;
+    // cluster split: 2 = the two CTAs of a cluster take the two K halves of each tile (launched in
+    // clusters of two, grid = 2 x the clusters; no partials or flags), 0 = off
+    int csplit;
 };
 
 // One work item of a CTA: a tile (or, in stream-K, the piece of a tile's K range this CTA owns).
@@ -140,7 +153,8 @@ struct GemmCfg {
     static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
     static constexpr int THREADS = QUANT ? (W_DEQ0 + DEQ_WARPS) * 32 : 7 * 32;
     static constexpr int DEQ_THREADS = DEQ_WARPS * 32;
-    static constexpr int BAR_BYTES = 512;   // 3 * STAGES + 11 barriers + the TMEM slot and abort flag
+    // 3 * STAGES + 11 barriers, the TMEM slot and abort flag, the cluster split's 16 barriers
+    static constexpr int BAR_BYTES = 512;
     static constexpr int RAW_OFF = STAGES * STAGE_BYTES;
     static constexpr int EPI_OFF = RAW_OFF + RAW_TOTAL;
     static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
@@ -149,6 +163,9 @@ struct GemmCfg {
     static constexpr uint32_t IDESC = idesc_f16_f32(PAIR ? 2 * GEMM_BN : GEMM_BN, MMA_N);
     static constexpr int TILE_N = PAIR ? 2 * GEMM_BN : GEMM_BN;   // weight rows per work tile
     static_assert(STAGES >= 2, "pipeline too shallow");
+    static_assert(8 * (3 * STAGES + 11) + 8 + 16 * 8 <= BAR_BYTES, "barrier area");
+    // the cluster split's receive and send regions (four warps x two halves' rows) in the idle stages
+    static constexpr bool CSPLIT_FITS = !WIDE && !PAIR && BT * 512 <= STAGES * STAGE_BYTES;
     static_assert(!(WIDE && PAIR), "the wide tile runs on one SM");
 };
 
@@ -180,6 +197,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     uint8_t* misc = smem + C::BAR_OFF + 8 * (3 * STAGES + 11);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 4);
+    // cluster split: per epilogue warp q, xfree(q, 0) completes when the peer's warp q has its
+    // receive region free (its main loop is over), xfull(q, 0) when the peer's bulk copy of its rows
+    // of this CTA's half has landed in this CTA's region (slots (q, 1) are unused)
+    const uint32_t xbar_base = bar_base + 8u * (3 * STAGES + 11) + 8u;
+    auto xfull_bar = [&](int q, int sl) { return xbar_base + 8u * (2 * q + sl); };
+    auto xfree_bar = [&](int q, int sl) { return xbar_base + 64u + 8u * (2 * q + sl); };
+    const bool csplit = !GROUPED && C::CSPLIT_FITS && args.csplit == 2;
+    const uint32_t xrank = csplit ? cluster_ctarank() : 0u;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -212,6 +237,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             mbar_init(rempty_bar(s), DEQ_WARPS);
         }
         mbar_init(drain_bar, 1);
+        if (csplit) {
+            for (int i = 0; i < 8; i++) {
+                mbar_init(xfull_bar(i >> 1, i & 1), 1);
+                mbar_init(xfree_bar(i >> 1, i & 1), 1);
+            }
+        }
         *abort_flag = 0;
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
@@ -228,7 +259,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         }
     }
     tc_fence_before();
-    if constexpr (PAIR) cluster_sync();   // the peer's barriers exist before anything arrives on them
+    if (PAIR || csplit) cluster_sync();   // the peer's barriers exist before anything arrives on them
     else cta_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
@@ -243,8 +274,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         g_beg = (int64_t)unit_id * args.total_g / n_units_grid;
         g_end = (int64_t)(unit_id + 1) * args.total_g / n_units_grid;
     }
-    const int64_t cursor0 = GROUPED ? (int64_t)blockIdx.x : g_end;
-    auto cursor_ok = [&](int64_t c) { return GROUPED ? c < num_units : c > g_beg; };
+    // cluster split: cluster c takes tiles c, c + clusters, ...
+    const int64_t n_tiles_all = (int64_t)ntn * ntt;
+    const int64_t cursor0 = GROUPED ? (int64_t)blockIdx.x : csplit ? (int64_t)(blockIdx.x >> 1) : g_end;
+    auto cursor_ok = [&](int64_t c) { return GROUPED ? c < num_units : csplit ? c < n_tiles_all : c > g_beg; };
     auto unit_coords = [&](int64_t cur) {
         UnitCoords c;
         if constexpr (GROUPED) {
@@ -266,6 +299,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             c.finishes = true;
             c.c_first = unit_id;
             c.next = cur + gridDim.x;
+        } else if (csplit) {
+            const int tt = (int)(cur % ntt);
+            const int nt = (int)(cur / ntt);
+            c.t0 = tt * BT;
+            c.t_end = args.M;
+            c.n0 = nt * GEMM_BN;
+            c.wrow0 = c.n0;
+            // this CTA's half of the K range, in whole granules
+            c.kb0 = (int)(((int64_t)args.tile_g * xrank) / 2) * args.gran;
+            c.kb1 = min(args.nkb, (int)(((int64_t)args.tile_g * (xrank + 1)) / 2) * args.gran);
+            c.finishes = true;
+            c.c_first = unit_id;
+            c.next = cur + (gridDim.x >> 1);
         } else {
             const int64_t tile = (cur - 1) / args.tile_g;
             const int64_t tstart = tile * args.tile_g;
@@ -476,6 +522,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         const int q = warp & 3;                          // TMEM lane quadrant this warp may read
         const uint32_t lane_tmem = tmem_base + ((uint32_t)(32 * q) << 16);
         int lt = 0;
+        uint32_t xn = 0;                                 // cluster split: tiles exchanged so far
         for (int64_t cur = cursor0; cursor_ok(cur); lt++) {
             const UnitCoords uc = unit_coords(cur);
             cur = uc.next;
@@ -559,6 +606,89 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 32; j++) __stcg(p + (size_t)(c0 + j) * GEMM_BN, __uint_as_float(r[j]));
+                }
+            } else if (csplit) {
+                // Cluster split: this CTA finishes tokens [own0, own0 + BT/2) of the tile. A cluster
+                // holds one tile, so once the accumulator is full this CTA's operand stages are idle.
+                // Each epilogue warp stages its rows of the peer's half there ([token][32 rows] f32,
+                // HALF x 128 bytes), and one bulk copy moves them into the peer's receive region (also
+                // in its idle stages) once the peer says the region is free; then the warp adds what
+                // arrived in its own region to its own half, scales it in place and stores it by TMA.
+                constexpr int HALF = BT / 2;
+                constexpr uint32_t WBYTES = HALF * 128;  // one warp's rows of one half
+                const uint32_t wi = (uint32_t)(warp - W_EPI0);
+                const uint32_t recv_addr = sbase + wi * WBYTES;
+                const uint32_t send_addr = sbase + 4 * WBYTES + wi * WBYTES;
+                float* recv = reinterpret_cast<float*>(smem + wi * WBYTES);
+                float* send = reinterpret_cast<float*>(smem + 4 * WBYTES + wi * WBYTES);
+                const float4* recv4 = reinterpret_cast<const float4*>(recv);
+                const uint32_t peer = xrank ^ 1u;
+                const int own0 = (int)xrank * HALF, oth0 = HALF - own0;
+                const int cc = lane & 7;                 // float4 column of the read-back
+                const int nb = uc.n0 + 32 * q + 4 * cc;  // this lane's 4 output columns
+                const uint32_t par = xn & 1u;
+                xn++;
+                // this warp's receive region is free (its MMAs are done): expect the peer's bytes, and
+                // tell the peer
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(xfull_bar(q, 0), WBYTES);
+                    mbar_arrive_cluster(mapa_shared(xfree_bar(q, 0), peer));
+                }
+                for (int ch = 0; ch < HALF / 16; ch++) {
+                    uint32_t r[16];
+                    tmem_ld16(lane_tmem + (uint32_t)(acc * BT + oth0 + 16 * ch), r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; j++) send[(16 * ch + j) * 32 + lane] = __uint_as_float(r[j]);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    if (mbar_wait<true>(xfree_bar(q, 0), par, args.err, ERR_WAIT_EPILOGUE, abort_flag))
+                        bulk_copy_s2cluster(mapa_shared(recv_addr, peer), send_addr, WBYTES,
+                                            mapa_shared(xfull_bar(q, 0), peer));
+                }
+                if (!mbar_wait<true>(xfull_bar(q, 0), par, args.err, ERR_WAIT_EPILOGUE, abort_flag)) break;
+                for (int ch = 0; ch < HALF / 16; ch++) {
+                    uint32_t o[16];
+                    tmem_ld16(lane_tmem + (uint32_t)(acc * BT + own0 + 16 * ch), o);
+                    tmem_ld_wait();
+                    const int tk0 = own0 + 16 * ch;      // first token (of the tile) of the chunk
+                    const int g = tk0 >> 5;
+                    float sg = scl[0];
+#pragma unroll
+                    for (int i = 1; i < NG; i++)
+                        if (g == i) sg = scl[i];
+                    float* rc = recv + 16 * ch * 32;
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        rc[j * 32 + lane] = (__uint_as_float(o[j]) + rc[j * 32 + lane]) *
+                                            __shfl_sync(0xffffffffu, sg, (tk0 & 31) + j);
+                    if (args.n_dst == 0) {
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0 && tk0 < ntok) {
+                            const uint32_t src = recv_addr + (uint32_t)(16 * ch * 128);
+                            tma_store_2d(&tmO, src, uc.n0 + 32 * q, uc.t0 + tk0);
+                            if (tk0 + 8 < ntok) tma_store_2d(&tmO, src + 1024u, uc.n0 + 32 * q, uc.t0 + tk0 + 8);
+                            bulk_commit();
+                        }
+                    } else {
+                        // several destinations (weight rows split across GPUs): 16-byte stores of whole
+                        // 128-byte output lines, four tokens per instruction
+                        __syncwarp();
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const int jr = (lane >> 3) + 4 * i;
+                            const float4 v = recv4[(16 * ch + jr) * 8 + cc];
+                            const int t = uc.t0 + tk0 + jr;
+                            if (t < uc.t_end && nb < args.N) {
+                                const size_t o4 = (size_t)t * args.ldo + args.col0 + nb;
+                                for (int d = 0; d < args.n_dst; d++)
+                                    *reinterpret_cast<float4*>(args.out_bases[d] + o4) = v;
+                            }
+                        }
+                    }
                 }
             } else {
                 // 32 tokens at a time, through this warp's 32 x 32 f32 box of shared memory
@@ -736,8 +866,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 
     tc_fence_before();
     // a pair: neither CTA leaves while the leader's MMAs may still read the peer's shared memory
-    // or write its TMEM (the leader's MMA thread passes here only after its drain)
-    if constexpr (PAIR) cluster_sync();
+    // or write its TMEM (the leader's MMA thread passes here only after its drain); a cluster
+    // split: neither leaves while the peer may still write into its shared memory or barriers
+    if (PAIR || csplit) cluster_sync();
     else cta_sync();
     if (warp == W_MMA) {
         tc_fence_after();

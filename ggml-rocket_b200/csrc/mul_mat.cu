@@ -250,6 +250,7 @@ static inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; 
 struct GemmPlan {
     int bt, gran, tile_g, nkb, ntn, ntt, grid, pieces;
     bool pair;                 // 2-SM MMA: CTA pairs over 256 weight rows (grid counts CTAs)
+    bool csplit;               // cluster split: two CTAs per tile, one K half each (grid counts CTAs)
     int64_t tiles, total_g;
 };
 
@@ -275,6 +276,16 @@ static int tile_knob() {
     return v;
 }
 
+// B200_GEMM_CSPLIT: unset = the cost model's choice; 0 = never; 1 = whenever the tiles fit on half
+// the SMs (two CTAs of a cluster per tile, each one half of its K range).
+static int csplit_knob() {
+    static const int v = [] {
+        const char* e = getenv("B200_GEMM_CSPLIT");
+        return (e && *e) ? atoi(e) : -1;
+    }();
+    return v;
+}
+
 // B200_GEMM_STREAMK: unset / 1 = the cost model's choice; 0 = one whole tile per CTA whenever the
 // tiles fit in one wave (no partials, idle SMs allowed); 2 = always stream-K over every SM.
 static int streamk_knob() {
@@ -283,6 +294,28 @@ static int streamk_knob() {
         return (e && *e) ? atoi(e) : 1;
     }();
     return v;
+}
+
+// Whether the cluster split's receive and send regions fit in the idle operand stages of the
+// kernel instance for this token tile and weight type.
+template <int WT>
+static bool csplit_fits_wt(int bt) {
+    switch (bt) {
+        case 32: return GemmCfg<32, WT, false>::CSPLIT_FITS;
+        case 64: return GemmCfg<64, WT, false>::CSPLIT_FITS;
+        case 128: return GemmCfg<128, WT, false>::CSPLIT_FITS;
+        case 256: return GemmCfg<256, WT, false>::CSPLIT_FITS;
+        default: return false;
+    }
+}
+static bool csplit_fits(int bt, int wtype) {
+    switch (wtype) {
+        case WT_F16: return csplit_fits_wt<WT_F16>(bt);
+        case WT_Q4_K: return csplit_fits_wt<WT_Q4_K>(bt);
+        case WT_Q6_K: return csplit_fits_wt<WT_Q6_K>(bt);
+        case WT_Q8_0: return csplit_fits_wt<WT_Q8_0>(bt);
+        default: return false;
+    }
 }
 
 // Choose the token tile from a cost model (SM clocks). Per 64-wide K block a tile costs the
@@ -344,9 +377,22 @@ static GemmPlan plan_gemm_knobs(int64_t M, int64_t N, int64_t K, int sms, int wt
             const bool shared = total_g % units != 0 || tiles % units != 0;
             double t = (double)tiles * nkb * per_kb / units + 800.0 * items;
             if (shared) t += part_sk;
+            // cluster split: when the tiles fit on half the SMs, two CTAs of a cluster take each tile,
+            // one K half each, and add the halves over distributed shared memory (no partial round
+            // trip through L2); measured on B200 at M = 512, N = 4096: 42 -> 27 us (K = 4096)
+            bool csplit = false;
+            if (!pair && csplit_fits(bt, wtype) && tile_g >= 2 && tiles * 2 <= sms && csplit_knob() != 0 &&
+                streamk_knob() == 1) {
+                const double t_cs = (double)((tile_g + 1) / 2) * gran * per_kb + 1600.0 + 12.8 * bt;
+                if (csplit_knob() == 1 || t_cs < t) {
+                    t = t_cs;
+                    csplit = true;
+                }
+            }
             if (t < best_t * 0.97) {
                 best_t = t;
                 best.bt = bt;
+                best.csplit = csplit;
                 best.pair = pair != 0;
                 best.gran = gran;
                 best.tile_g = tile_g;
@@ -359,6 +405,10 @@ static GemmPlan plan_gemm_knobs(int64_t M, int64_t N, int64_t K, int sms, int wt
                 const int64_t run = total_g / units;      // shortest granule run of a unit
                 best.pieces = (int)((tile_g - 1) / run + 2 < tile_g ? (tile_g - 1) / run + 2 : tile_g);
                 if (!shared) best.pieces = 1;
+                if (csplit) {
+                    best.pieces = 2;
+                    best.grid = (int)(2 * tiles);
+                }
             }
         }
     }
@@ -375,7 +425,7 @@ static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms, int wtype) {
 // owns whole tiles.
 static size_t streamk_partials_bytes(const GemmPlan& p) { return (size_t)p.grid * p.bt * GEMM_BN * 4; }
 static size_t streamk_bytes(const GemmPlan& p) {
-    return p.pieces > 1 ? streamk_partials_bytes(p) + (size_t)p.grid * 16 : 0;
+    return p.pieces > 1 && !p.csplit ? streamk_partials_bytes(p) + (size_t)p.grid * 16 : 0;
 }
 
 // A value no earlier launch has published in the flags (0 is skipped, so zeroed memory never
@@ -403,6 +453,7 @@ static MulMatWorkspace mm_workspace_layout(int64_t M, int64_t N, int64_t K, cons
 template <int BT, int WT, bool GROUPED, bool PAIR>
 static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmD,
                                  const CUtensorMap& tmO, const GemmArgs& a, int grid, cudaStream_t st) {
+    const bool cluster2 = PAIR || a.csplit == 2;
     using C = GemmCfg<BT, WT, PAIR>;
     static bool attr_set[64] = {false};
     int dev = 0;
@@ -425,8 +476,8 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW,
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     int na = 1;
-    if (PAIR) {
-        // CTA pairs: clusters of two (the 2-SM MMA's peers)
+    if (cluster2) {
+        // CTA pairs: clusters of two (the 2-SM MMA's peers, or the two K halves of a cluster split)
         attr[1].id = cudaLaunchAttributeClusterDimension;
         attr[1].val.clusterDim.x = 2;
         attr[1].val.clusterDim.y = 1;
@@ -593,6 +644,8 @@ int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, cons
     const int sms = device_sm_count();
     const GemmPlan p = plan_gemm(M, N, K, sms, wtype);
     const size_t sk_bytes = streamk_bytes(p);
+    // the cluster split receives into its CTAs' idle operand stages: one tile per cluster
+    if (p.csplit && ((int64_t)p.grid != 2 * p.tiles || !csplit_fits(p.bt, wtype))) return B200_E_INVALID;
     if (sk_bytes && (!workspace || workspace_bytes < sk_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
         return B200_E_WORKSPACE;
     CUtensorMap tmA, tmW, tmD;
@@ -622,6 +675,7 @@ int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, cons
     a.out_bases = n_dst > 0 ? dst_bases : nullptr;
     a.n_dst = n_dst > 0 ? n_dst : 0;
     a.col0 = (int)col0;
+    a.csplit = p.csplit ? 2 : 0;
     CUtensorMap tmO = tmA;   // unused with several destinations
     if (n_dst <= 0 && !make_tmap_2d_f32_out(&tmO, dst, (uint64_t)M, (uint64_t)N, (uint64_t)ldd * 4)) return B200_E_CUDA;
     const cudaError_t e = launch_gemm_typed<false>(wtype, p.bt, p.pair, tmA, tmW, tmD, tmO, a, p.grid, st);

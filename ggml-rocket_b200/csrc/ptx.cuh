@@ -303,6 +303,16 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
     return r;
 }
 
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from this CTA's shared
+// memory into another CTA's (dst and its mbarrier as shared::cluster addresses from mapa_shared);
+// the bytes complete_tx on that mbarrier.
+__device__ __forceinline__ void bulk_copy_s2cluster(uint32_t dst_cluster, uint32_t src, uint32_t bytes,
+                                                    uint32_t bar_cluster) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst_cluster), "r"(src), "r"(bytes), "r"(bar_cluster)
+                 : "memory");
+}
+
 // Arrive on an mbarrier of another CTA of the cluster (address from mapa_shared).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");

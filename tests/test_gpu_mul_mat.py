@@ -208,3 +208,47 @@ def test_mul_mat_cta_pairs_forced(cuda):
     assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
     worst = float(p.stdout.split("PAIR_WORST")[1].split()[0])
     assert worst <= TOL
+
+
+_CSPLIT_CHILD = r"""
+import sys, numpy as np, torch
+sys.path[:0] = [sys.argv[1], sys.argv[1] + '/ggml-rocket_b200', sys.argv[1] + '/tests']
+import oracle
+import ggml_b200 as g
+from conftest import rel_err
+from test_gpu_mul_mat import run_mul_mat, _weights
+worst, used = 0.0, 0
+for (K, N, M, wtype) in [(1024, 512, 300, 1), (2048, 1024, 512, 12), (1024, 768, 100, 14), (2048, 512, 64, 8),
+                         (512, 256, 33, 12), (4096, 256, 256, 1)]:
+    rng = np.random.default_rng(K + N + M + wtype)
+    w = _weights(rng, N, K, wtype)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    plan = g.mul_mat_plan(M, N, K, wtype)
+    tiles = ((N + 127) // 128) * ((M + plan["token_tile"] - 1) // plan["token_tile"])
+    used += plan["grid"] == 2 * tiles and plan["splits"] == 2
+    for rep in range(2):                     # twice: the exchange barriers carry their phases across calls
+        got = run_mul_mat(torch, wtype, w, N, K, a)
+        assert np.all(np.isfinite(got)), (K, N, M, wtype)
+        worst = max(worst, rel_err(got, oracle.mul_mat(wtype, w, N, K, a)))
+print("CSPLIT_WORST", worst, "USED", used)
+"""
+
+
+@pytest.mark.parametrize("mode", ["1", "0"])
+def test_mul_mat_cluster_split(cuda, mode):
+    """The cluster split (two CTAs per tile, one K half each, halves added over distributed shared
+    memory) forced on (B200_GEMM_CSPLIT=1) and off in child processes, every weight format, token
+    tiles 32-256 and ragged M, against the oracle."""
+    import os
+    import subprocess
+    import sys
+    from conftest import ROOT
+    env = dict(os.environ, B200_GEMM_CSPLIT=mode)
+    p = subprocess.run([sys.executable, "-c", _CSPLIT_CHILD, ROOT], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
+    out = p.stdout.split("CSPLIT_WORST")[1].split()
+    worst, used = float(out[0]), int(out[2])
+    assert worst <= TOL
+    if mode == "1":
+        assert used == 6
