@@ -53,10 +53,13 @@ def test_noalloc_matches_mul_mat_twice(cuda):
     import torch
     import ggml_b200 as g
     # calls in a row with different shapes and formats; the first and the last share output tiles
-    # between CTAs (stream-K partials and their flags, the part of the array that carries state
-    # from one call to the next), so the last call runs on flags the first one left behind
-    cases = ((g.Q4_K, 4096, 4096, 128, 1), (g.F16, 768, 2048, 96, 2), (g.Q4_K, 4096, 4096, 128, 3))
-    assert g.mul_mat_plan(128, 4096, 4096, g.Q4_K)["splits"] > 1
+    # between CTAs under stream-K (partials and their flags, the part of the array that carries
+    # state from one call to the next), so the last call runs on flags the first one left behind
+    cases = ((g.Q4_K, 14336, 4096, 512, 1), (g.F16, 768, 2048, 96, 2), (g.Q4_K, 14336, 4096, 512, 3))
+    plan = g.mul_mat_plan(512, 14336, 4096, g.Q4_K)
+    tiles = (14336 // 128) * (512 // plan["token_tile"])
+    # shared tiles, and more tiles than half the grid, so not the cluster split (which keeps no flags)
+    assert plan["splits"] > 1 and 2 * tiles > plan["grid"]
     for wtype, N, K, M, seed in cases:
         got, want = _run_both(torch, g, wtype, N, K, M, seed)
         assert np.all(np.isfinite(got))
