@@ -574,7 +574,7 @@ def run_ours(args):
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": profile_traffic(),
                          "traffic_launch": "DRAM bytes of the (K=4096, N=14336) launch, one ncu capture "
-                                           "(profiles/gemm_q4k_m512_n14336.md)",
+                                           "(profiles/gemm_q4k_m512_cluster_split.md)",
                          "kernel": "gemm_kernel<BT,Q4_K> (tcgen05, fused Q4_K dequant)",
                          "peak_source": f"{peak_src} bf16_tflops (burst)",
                          "algorithmic": "2*M*N*K FLOP per launch; per shape the mean CUDA-event time of its "
