@@ -496,10 +496,11 @@ def run_ours(args):
         torch.distributed.barrier()
         moe_1 = run_moe(args, world_override=1, inside=True) if rank == 0 else None
         torch.distributed.barrier()
-        shard_n = run_gemm_sharded(args, inside=True)
+        shard_n = {m: run_gemm_sharded(args, inside=True, m_tokens=m) for m in (M_TOKENS, 2048)}
+        torch.distributed.barrier()
+        shard_1 = {m: time_sweep_1gpu(args, m) for m in (M_TOKENS, 2048)} if rank == 0 else None
         torch.distributed.barrier()
         if rank == 0:
-            one_sweep_ms = ms / L
             multi = {
                 "moe_expert_parallel": {
                     "workload": "BASELINE configs[3] MoE layer (gate+up+down, Q4_K, 128 experts top-8), 2048 tokens "
@@ -507,10 +508,13 @@ def run_ours(args):
                     "ms_per_layer": moe_n["ms"], "tokens_per_s": moe_n["tokens_per_s"], "tflops": moe_n["tflops"],
                     "ms_per_layer_1gpu": moe_1["ms"], "weak_efficiency": moe_1["ms"] / moe_n["ms"]},
                 "sharded_sweep": {
-                    "workload": "the headline sweep (one layer) with every weight's rows split over the ranks, "
-                                "output all-gathered by the GEMM epilogue's peer stores",
-                    "ms": shard_n["ms"], "tflops": shard_n["tflops"], "ms_1gpu": one_sweep_ms,
-                    "strong_speedup": one_sweep_ms / shard_n["ms"]}}
+                    f"m{m}": {
+                        "workload": f"the sweep's three shapes (one layer) at M = {m} with every weight's rows split "
+                                    "over the ranks, output all-gathered by the GEMM epilogue's peer stores; L2 "
+                                    "flushed before every step",
+                        "ms": shard_n[m]["ms"], "tflops": shard_n[m]["tflops"], "ms_1gpu": shard_1[m],
+                        "ms_1gpu_what": "b200_mul_mat of the whole weights on rank 0's GPU, timed the same way",
+                        "strong_speedup": shard_1[m] / shard_n[m]["ms"]} for m in (M_TOKENS, 2048)}}
 
     if rank == 0:
         peaks, peak_src = measured_peaks()
@@ -899,11 +903,53 @@ def run_gemv(args):
     return 0
 
 
-def run_gemm_sharded(args, inside=False):
+def time_sweep_1gpu(args, m_tokens):
+    """One GPU's time for one layer of the sweep at m_tokens (b200_mul_mat per shape, whole
+    weights), measured the way run_gemm_sharded measures the sharded op: L2 flushed and a GPU
+    delay before every step, CUDA events around it; the reference for its strong scaling."""
+    import numpy as np
+    import torch
+    import ggml_b200 as g
+    from ggml_b200 import quants
+    dev = torch.device("cuda", torch.cuda.current_device())
+    rng = np.random.default_rng(0xB200)
+    ws, acts, outs, wss = [], [], [], []
+    for (k, n) in SHAPES:
+        w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02))
+        raw = torch.from_numpy(quants.quantize(WTYPE, w).reshape(-1)).to(dev)
+        packed = torch.empty(g.weight_packed_size(WTYPE, n, k), dtype=torch.uint8, device=dev)
+        g.weight_pack(WTYPE, raw, n, k, packed)
+        ws.append(packed)
+        acts.append(torch.from_numpy(rng.standard_normal((m_tokens, k)).astype(np.float32)).to(dev))
+        outs.append(torch.empty((m_tokens, n), dtype=torch.float32, device=dev))
+        wss.append(torch.empty(max(256, g.mul_mat_workspace_size(m_tokens, n, k, WTYPE)), dtype=torch.uint8,
+                               device=dev))
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    evs = []
+    for it in range(args.warmup + args.steps):
+        flush.zero_()
+        torch.cuda._sleep(1000000)
+        e = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+        e[0].record(stream)
+        for i, (k, n) in enumerate(SHAPES):
+            g.mul_mat(WTYPE, ws[i], n, k, acts[i], m_tokens, outs[i], wss[i], err, stream=stream)
+        e[1].record(stream)
+        if it >= args.warmup:
+            evs.append(e)
+    torch.cuda.synchronize()
+    if int(err.item()) != 0:
+        raise SystemExit(f"device error {int(err.item())} in the one-GPU sweep")
+    return sum(e[0].elapsed_time(e[1]) for e in evs) / len(evs)
+
+
+def run_gemm_sharded(args, inside=False, m_tokens=M_TOKENS):
     """The headline sweep with every weight's rows split across the ranks (ggml_b200.tp): each
     rank packs its row block of each shape's weight, runs the N-sharded MUL_MAT on the shared
     activation, and ends holding the full dst. value = the sweep's FLOPs / max-over-ranks time.
-    inside: called from the headline arm (the process group exists; return the timing)."""
+    inside: called from the headline arm (the process group exists; return the timing).
+    m_tokens: the token count (the sweep's M; 512 for the headline)."""
     import numpy as np
     import torch
     import ggml_b200 as g
@@ -929,14 +975,14 @@ def run_gemm_sharded(args, inside=False):
         packed = torch.empty(g.weight_packed_size(WTYPE, hi - lo, k), dtype=torch.uint8, device=dev)
         g.weight_pack(WTYPE, raw, hi - lo, k, packed)
         shards.append(packed)
-        acts.append(torch.from_numpy(rng.standard_normal((M_TOKENS, k)).astype(np.float32)).to(dev))
-    tp = PeerShardedMulMat(M_TOKENS, max(n for (_, n) in SHAPES))
+        acts.append(torch.from_numpy(rng.standard_normal((m_tokens, k)).astype(np.float32)).to(dev))
+    tp = PeerShardedMulMat(m_tokens, max(n for (_, n) in SHAPES))
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
 
     def step():
         for i, (k, n) in enumerate(SHAPES):
-            tp(WTYPE, shards[i], n, k, acts[i], M_TOKENS, stream=stream)
+            tp(WTYPE, shards[i], n, k, acts[i], m_tokens, stream=stream)
 
     for _ in range(args.warmup):
         flush.zero_()
@@ -971,7 +1017,7 @@ def run_gemm_sharded(args, inside=False):
     ms = float(vals.item())
     tp.close()
     if inside:
-        return {"ms": ms, "tflops": step_flops() / (ms / 1e3) / 1e12}
+        return {"ms": ms, "tflops": step_flops(m_tokens) / (ms / 1e3) / 1e12}
     if rank == 0:
         flops = step_flops()
         line = {"metric": METRIC, "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
