@@ -88,6 +88,13 @@ int min_m_quant() {
     return m;
 }
 
+// B200_GEMM_COMBINE: 1 (default) = a fused MUL_MAT group is one combined-N GEMM launch, 0 = one
+// launch per member after the shared activation pack.
+int combine_knob() {
+    static const int v = knob_int("B200_GEMM_COMBINE", 1);
+    return v;
+}
+
 enum MoeMode { MOE_OFF = 0, MOE_AUTO = 1, MOE_FORCED = 2 };
 int moe_mode() {
     static const int v = [] {
@@ -1196,6 +1203,15 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
         any_gemm = any_gemm || !dec[g];
         if (dec[g]) need_ws = std::max(need_ws, b200_mul_mat_vec_workspace_size(M, nodes[g]->src[0]->ne[1], K));
     }
+    // A group of 2-4 GEMM-sized members of one weight type runs as one combined-N launch
+    // (B200_GEMM_COMBINE=0: one launch per member, as the single-op path does).
+    bool comb = ng >= 2 && ng <= 4 && !any_dec && combine_knob() != 0;
+    for (int g = 1; g < ng && comb; g++) comb = kt[g] == kt[0];
+    if (comb) {
+        std::vector<int64_t> ns(ng);
+        for (int g = 0; g < ng; g++) ns[g] = nodes[g]->src[0]->ne[1];
+        need_ws = std::max(need_ws, b200_gemm_packed_group_workspace_size(ng, kt[0], M, ns.data(), K));
+    }
     const size_t a16_bytes = ((size_t)M * K * 2 + 255) & ~(size_t)255;
     const size_t sc_bytes = ((size_t)M * 4 + 255) & ~(size_t)255;
     need_ws = ((need_ws + 255) & ~(size_t)255) + a16_bytes + sc_bytes;
@@ -1226,6 +1242,23 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
             if (!any_gemm) continue;
             int rc = b200_act_pack(A, (int64_t)(src1->nb[1] / 4), M, K, a16, scales, b->stream);
             if (rc != B200_OK) return rc;
+            if (comb) {
+                // one combined-N launch over every member (all 2-D, one type, GEMM-sized)
+                std::vector<const void*> ws_w(ng);
+                std::vector<int64_t> ns(ng), lds(ng);
+                std::vector<float*> cs(ng);
+                for (int g = 0; g < ng; g++) {
+                    const b200_tensor* d = nodes[g];
+                    ws_w[g] = wdev[g];
+                    ns[g] = d->src[0]->ne[1];
+                    lds[g] = (int64_t)(d->nb[1] / 4);
+                    cs[g] = reinterpret_cast<float*>(d_base[g] + i3 * d->nb[3] + i2 * d->nb[2]);
+                }
+                rc = b200_gemm_packed_group(ng, kt[0], ws_w.data(), ns.data(), K, a16, scales, M, cs.data(),
+                                            lds.data(), gws, gws_bytes, b->dev_err, b->stream);
+                if (rc != B200_OK) return rc;
+                continue;
+            }
             for (int g = 0; g < ng; g++) {
                 if (dec[g]) continue;
                 const b200_tensor* d = nodes[g];
@@ -1413,6 +1446,71 @@ int do_moe_ffn(b200_backend* b, const b200_tensor* gate, const b200_tensor* up, 
     b->route_ops["moe_grouped"] += 2;
     b->route_ops["moe_ffn"]++;
     b->route_ops["glue"]++;
+    return B200_OK;
+}
+
+// A dense FFN as ggml builds it: GLU SWIGLU of the gate and up projections (node i, split form) and
+// the down MUL_MAT that reads it (i + 1). When the SWIGLU output is a device tensor no other node
+// reads, the pair runs as b200_swiglu_act_pack (the SWIGLU inside the down projection's activation
+// pack) and the down GEMM: h is never written. *gate / *up: the tensors silu and the product take.
+static bool swiglu_mm_match(b200_tensor* const* nodes, int n, int i, const std::vector<bool>& done,
+                            const b200_tensor** gate, const b200_tensor** up) {
+    if (i + 1 >= n || done[i + 1]) return false;
+    const b200_tensor* glu = nodes[i];
+    const b200_tensor* mm = nodes[i + 1];
+    if (glu->op != B200_OP_GLU || glu->op_params[0] != B200_GLU_SWIGLU || !glu->src[1] || !glu->on_device ||
+        glu->ne[2] != 1 || glu->ne[3] != 1 || !ggml_backend_b200_supports_op(glu))
+        return false;
+    if (mm->op != B200_OP_MUL_MAT || mm->src[1] != glu || !node_fusable(mm)) return false;
+    const bool swapped = glu->op_params[1] != 0;
+    *gate = swapped ? glu->src[1] : glu->src[0];
+    *up = swapped ? glu->src[0] : glu->src[1];
+    const int64_t F = glu->ne[0], M = glu->ne[1];
+    if (mm->src[0]->ne[0] != F || F % 4 != 0 || F > 16384) return false;
+    if (kernel_wtype(mm->src[0]->type) != T_F16 && M < min_m_quant() && M <= 32) return false;   // decode kernel
+    for (const b200_tensor* t : {*gate, *up}) {
+        if (t->ne[0] != F || t->ne[1] != M || t->nb[0] != 4 || t->nb[1] % 16 != 0) return false;
+        if (t->on_device && (reinterpret_cast<uintptr_t>(t->data) & 15u)) return false;
+    }
+    for (int j = 0; j < n; j++) {
+        if (j == i || j == i + 1) continue;
+        for (int k = 0; k < B200_MAX_SRC; k++)
+            if (nodes[j]->src[k] == glu) return false;
+    }
+    return true;
+}
+
+int do_swiglu_mul_mat(b200_backend* b, const b200_tensor* gate, const b200_tensor* up, const b200_tensor* mm) {
+    const b200_tensor* a = mm->src[0];
+    const int64_t F = a->ne[0], N = a->ne[1], M = gate->ne[1];
+    int kt = 0;
+    void* w = pack_weight(b, weight_key(a), a->type, a->data, a->on_device != 0, N, F, &kt);
+    if (!w) return B200_E_CUDA;
+    OpStaging stg;
+    stg.ins = {gate, up};
+    stg.outs = {mm};
+    const size_t a16_bytes = ((size_t)M * F * 2 + 255) & ~(size_t)255;
+    const size_t sc_bytes = ((size_t)M * 4 + 255) & ~(size_t)255;
+    const size_t gws_need = (b200_gemm_packed_workspace_size(kt, M, N, F) + 255) & ~(size_t)255;
+    if (!op_reserve(b, stg)) return B200_E_CUDA;
+    if (!grow(&b->ws, &b->ws_bytes, a16_bytes + sc_bytes + gws_need, b->stream)) return B200_E_CUDA;
+    bool ok = true;
+    const float* gd = static_cast<const float*>(stage_in(b, gate, &ok));
+    const float* ud = static_cast<const float*>(stage_in(b, up, &ok));
+    char* dd = stage_out(b, mm, false, &ok);
+    if (!ok || !op_inputs_ready(b)) return B200_E_CUDA;
+    char* ws = static_cast<char*>(b->ws);
+    float* scales = reinterpret_cast<float*>(ws + a16_bytes);
+    int rc = b200_swiglu_act_pack(gd, (int64_t)(gate->nb[1] / 4), ud, (int64_t)(up->nb[1] / 4), M, F, ws, scales,
+                                  b->stream);
+    if (rc != B200_OK) return rc;
+    rc = b200_gemm_packed(kt, w, N, F, ws, scales, M, reinterpret_cast<float*>(dd), (int64_t)(mm->nb[1] / 4),
+                          ws + a16_bytes + sc_bytes, b->ws_bytes - a16_bytes - sc_bytes, b->dev_err, b->stream);
+    if (rc != B200_OK) return rc;
+    if (!op_outputs_done(b, stg.outs, {dd})) return B200_E_CUDA;
+    b->route_ops["glue"]++;
+    b->route_ops[route_name(kt)]++;
+    b->route_ops["swiglu_fused"]++;
     return B200_OK;
 }
 
@@ -1937,6 +2035,20 @@ int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes,
             case B200_OP_DIV: {
                 if (!ggml_backend_b200_supports_op(node)) {
                     status = B200_STATUS_FAILED;
+                    break;
+                }
+                // GLU SWIGLU -> the down MUL_MAT reading it: the SWIGLU inside the down projection's
+                // activation pack, h never written
+                const b200_tensor* sw_gate = nullptr;
+                const b200_tensor* sw_up = nullptr;
+                if (fuse && breaker_allow(b->brk_fused) && swiglu_mm_match(nodes, n, i, done, &sw_gate, &sw_up)) {
+                    const int rc = do_swiglu_mul_mat(b, sw_gate, sw_up, nodes[i + 1]);
+                    breaker_note(b->brk_fused, rc, "fused SWIGLU + MUL_MAT");
+                    if (rc != B200_OK) {
+                        logf("E", "graph_compute: fused SWIGLU + MUL_MAT failed (%d) in node %s\n", rc, node->name);
+                        status = B200_STATUS_FAILED;
+                    }
+                    done[i + 1] = true;
                     break;
                 }
                 // ADD (residual) -> RMS_NORM -> MUL (weight row): one launch; the sum is always

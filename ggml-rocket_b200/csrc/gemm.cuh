@@ -57,6 +57,7 @@ namespace b200 {
 
 constexpr int GEMM_BN = 128;   // weight rows per tile (tcgen05 M)
 constexpr int GEMM_BK = 64;    // K per pipeline stage (one 128-byte swizzle row of fp16)
+constexpr int GEMM_MAX_MEMBERS = 4;   // weights in one combined-N launch (a fused QKV group has 3)
 
 struct GemmArgs {
     const float* scales;       // [M] per-token activation scale
@@ -97,11 +98,25 @@ struct GemmArgs {
     // cluster split: 2 = the two CTAs of a cluster take the two K halves of each tile (launched in
     // clusters of two, grid = 2 x the clusters; no partials or flags), 0 = off
     int csplit;
+    // combined-N launch (plain MUL_MAT, one CTA per tile): n_mem weights of the same type and K
+    // against one packed activation, each with its own dst. Their 128-row weight tiles are laid
+    // end to end: member m owns weight tiles [mem_t0[m], mem_t0[m + 1]) of the n_tiles_n (the
+    // last member's end is n_tiles_n), and its weight, d plane and dst tensor maps are the
+    // kernel's own maps for m = 0 and GemmMembers' entry m - 1 otherwise. n_mem = 1: one weight.
+    int n_mem;
+    int mem_t0[GEMM_MAX_MEMBERS];
+};
+
+// The tensor maps of a combined-N launch's members 1 .. n_mem - 1 (a kernel parameter, so the
+// TMA reads them from parameter memory like the kernel's own maps).
+struct GemmMembers {
+    CUtensorMap w[GEMM_MAX_MEMBERS - 1], d[GEMM_MAX_MEMBERS - 1], o[GEMM_MAX_MEMBERS - 1];
 };
 
 // One work item of a CTA: a tile (or, in stream-K, the piece of a tile's K range this CTA owns).
 struct UnitCoords {
     int t0, t_end, n0, wrow0, kb0, kb1;
+    int mem;                   // combined-N launch: the member whose weight tile this is (n0, wrow0 are its own)
     bool finishes;             // this piece completes the tile: scale and store dst
     int c_first;               // first CTA holding a piece of this tile (partials c_first..blockIdx.x-1)
     int64_t next;              // cursor of the CTA's next item
@@ -172,7 +187,8 @@ struct GemmCfg {
 template <int BT, int WT, bool GROUPED, bool PAIR>
 __global__ void __launch_bounds__(GemmCfg<BT, WT, PAIR>::THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-            const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmO, const GemmArgs args) {
+            const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmO, const GemmArgs args,
+            const __grid_constant__ GemmMembers mm) {
     static_assert(!(GROUPED && PAIR), "the grouped GEMM runs one CTA per tile");
     static_assert(!(GROUPED && BT == 512), "the grouped GEMM's tiles are at most 256 rows of one expert");
     using C = GemmCfg<BT, WT, PAIR>;
@@ -248,6 +264,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmW);
         if (WT == WT_Q6_K) tma_prefetch_desc(&tmD);
+        for (int m = 1; m < args.n_mem && !GROUPED; m++) {
+            tma_prefetch_desc(&mm.w[m - 1]);
+            if (WT == WT_Q6_K) tma_prefetch_desc(&mm.d[m - 1]);
+        }
     }
     if (warp == W_MMA) {
         if constexpr (PAIR) {
@@ -278,6 +298,24 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     const int64_t n_tiles_all = (int64_t)ntn * ntt;
     const int64_t cursor0 = GROUPED ? (int64_t)blockIdx.x : csplit ? (int64_t)(blockIdx.x >> 1) : g_end;
     auto cursor_ok = [&](int64_t c) { return GROUPED ? c < num_units : csplit ? c < n_tiles_all : c > g_beg; };
+    // combined-N launch: the member owning global weight tile nt, which becomes the member's own tile index
+    auto member_of = [&](int& nt) {
+        int m = 0, base = 0;
+        if constexpr (!GROUPED) {
+#pragma unroll
+            for (int i = 1; i < GEMM_MAX_MEMBERS; i++) {
+                if (i < args.n_mem && nt >= args.mem_t0[i]) {
+                    m = i;
+                    base = args.mem_t0[i];
+                }
+            }
+        }
+        nt -= base;
+        return m;
+    };
+    auto wmap = [&](int m) { return m == 0 ? &tmW : &mm.w[m - 1]; };
+    auto dmap = [&](int m) { return m == 0 ? &tmD : &mm.d[m - 1]; };
+    auto omap = [&](int m) { return m == 0 ? &tmO : &mm.o[m - 1]; };
     auto unit_coords = [&](int64_t cur) {
         UnitCoords c;
         if constexpr (GROUPED) {
@@ -294,6 +332,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             c.t_end = __ldg(args.g_off + e + 1);
             c.n0 = nt * GEMM_BN;
             c.wrow0 = e * args.N + c.n0;
+            c.mem = 0;
             c.kb0 = 0;
             c.kb1 = args.nkb;
             c.finishes = true;
@@ -301,7 +340,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             c.next = cur + gridDim.x;
         } else if (csplit) {
             const int tt = (int)(cur % ntt);
-            const int nt = (int)(cur / ntt);
+            int nt = (int)(cur / ntt);
+            c.mem = member_of(nt);
             c.t0 = tt * BT;
             c.t_end = args.M;
             c.n0 = nt * GEMM_BN;
@@ -317,7 +357,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             const int64_t tstart = tile * args.tile_g;
             const int64_t s0 = tstart > g_beg ? tstart : g_beg;
             const int tt = (int)(tile % ntt);          // neighbouring tiles share a weight tile
-            const int nt = (int)(tile / ntt);
+            int nt = (int)(tile / ntt);
+            c.mem = member_of(nt);
             c.t0 = tt * BT;
             c.t_end = args.M;
             c.n0 = nt * C::TILE_N + (int)crank * GEMM_BN;   // this CTA's 128 weight rows
@@ -343,10 +384,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             if constexpr (C::QUANT) {
                 const int sb0 = uc.kb0 >> 2, sb_end = (uc.kb1 + 3) >> 2;
                 for (int pf = sb0; pf < sb0 + RC::PREFETCH && pf < sb_end; pf++)
-                    tma_prefetch_l2_2d(&tmW, pf * RC::X_ELEMS, uc.wrow0);
+                    tma_prefetch_l2_2d(wmap(uc.mem), pf * RC::X_ELEMS, uc.wrow0);
             } else {
                 for (int kb = uc.kb0; kb < uc.kb0 + 2 * STAGES && kb < uc.kb1; kb++)
-                    tma_prefetch_l2_2d(&tmW, kb * GEMM_BK, uc.wrow0);
+                    tma_prefetch_l2_2d(wmap(uc.mem), kb * GEMM_BK, uc.wrow0);
             }
         }
     }
@@ -372,14 +413,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     const uint32_t fb = leader_addr(full_bar(stage));
                     if (is_w) {
                         if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * C::W_BYTES);
-                        tma_load_2d_pair(sa + C::A_BYTES, &tmW, fb, kb * GEMM_BK, uc.wrow0);
+                        tma_load_2d_pair(sa + C::A_BYTES, wmap(uc.mem), fb, kb * GEMM_BK, uc.wrow0);
                     } else {
                         if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * C::A_BYTES);
                         tma_load_2d_pair(sa, &tmA, fb, kb * GEMM_BK, uc.t0 + (int)crank * C::A_ROWS);
                     }
                 } else if (is_w) {
                     mbar_arrive_expect_tx(full_bar(stage), C::W_BYTES);
-                    tma_load_2d(sa + C::A_BYTES, &tmW, full_bar(stage), kb * GEMM_BK, uc.wrow0);
+                    tma_load_2d(sa + C::A_BYTES, wmap(uc.mem), full_bar(stage), kb * GEMM_BK, uc.wrow0);
                 } else {
                     mbar_arrive_expect_tx(full_bar(stage), C::A_BYTES);
                     tma_load_2d(sa, &tmA, full_bar(stage), kb * GEMM_BK, uc.t0);
@@ -421,18 +462,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     const bool has_next = cursor_ok(cur);
                     const UnitCoords un = has_next ? unit_coords(cur) : uc;
                     const int nsb0 = un.kb0 >> 2, nsb_end = (un.kb1 + 3) >> 2;
+                    const CUtensorMap* tw = wmap(uc.mem);
                     for (int pf = sb0; pf < sb0 + RC::PREFETCH && pf < sb_end; pf++)
-                        tma_prefetch_l2_2d(&tmW, pf * RC::X_ELEMS, uc.wrow0);
+                        tma_prefetch_l2_2d(tw, pf * RC::X_ELEMS, uc.wrow0);
                     for (int sb = sb0; sb < sb_end; sb++) {
                         const int ahead = sb + RC::PREFETCH;
-                        if (ahead < sb_end) tma_prefetch_l2_2d(&tmW, ahead * RC::X_ELEMS, uc.wrow0);
+                        if (ahead < sb_end) tma_prefetch_l2_2d(tw, ahead * RC::X_ELEMS, uc.wrow0);
                         else if (has_next && nsb0 + (ahead - sb_end) < nsb_end)
-                            tma_prefetch_l2_2d(&tmW, (nsb0 + (ahead - sb_end)) * RC::X_ELEMS, un.wrow0);
+                            tma_prefetch_l2_2d(wmap(un.mem), (nsb0 + (ahead - sb_end)) * RC::X_ELEMS, un.wrow0);
                         if (!mbar_wait(rempty_bar(rs), rph ^ 1u, args.err, ERR_WAIT_PRODUCER, abort_flag)) { ok = false; break; }
                         const uint32_t dst = sbase + C::RAW_OFF + rs * RC::STAGE;
                         mbar_arrive_expect_tx(rfull_bar(rs), RC::A_BYTES + RC::D_BYTES);
-                        tma_load_2d(dst, &tmW, rfull_bar(rs), sb * RC::X_ELEMS, uc.wrow0);
-                        if constexpr (WT == WT_Q6_K) tma_load_2d(dst + RC::A_BYTES, &tmD, rfull_bar(rs), uc.wrow0, sb);
+                        tma_load_2d(dst, tw, rfull_bar(rs), sb * RC::X_ELEMS, uc.wrow0);
+                        if constexpr (WT == WT_Q6_K) tma_load_2d(dst + RC::A_BYTES, dmap(uc.mem), rfull_bar(rs), uc.wrow0, sb);
                         issued_mask |= 1u << rs;
                         issued_par = (issued_par & ~(1u << rs)) | (rph << rs);
                         if (++rs == C::RAW_STAGES) { rs = 0; rph ^= 1u; }
@@ -669,8 +711,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                         __syncwarp();
                         if (lane == 0 && tk0 < ntok) {
                             const uint32_t src = recv_addr + (uint32_t)(16 * ch * 128);
-                            tma_store_2d(&tmO, src, uc.n0 + 32 * q, uc.t0 + tk0);
-                            if (tk0 + 8 < ntok) tma_store_2d(&tmO, src + 1024u, uc.n0 + 32 * q, uc.t0 + tk0 + 8);
+                            tma_store_2d(omap(uc.mem), src, uc.n0 + 32 * q, uc.t0 + tk0);
+                            if (tk0 + 8 < ntok) tma_store_2d(omap(uc.mem), src + 1024u, uc.n0 + 32 * q, uc.t0 + tk0 + 8);
                             bulk_commit();
                         }
                     } else {
@@ -746,7 +788,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                             fence_proxy_async_smem();
                             __syncwarp();
                             if (lane == 0) {
-                                tma_store_2d(&tmO, es_addr + 1024u * sbx, uc.n0 + 32 * q, uc.t0 + c0 + 8 * sbx);
+                                tma_store_2d(omap(uc.mem), es_addr + 1024u * sbx, uc.n0 + 32 * q, uc.t0 + c0 + 8 * sbx);
                                 bulk_commit();
                             }
                         }

@@ -15,6 +15,7 @@
 
 #include "ggml-b200-kernels.h"
 #include "gemm.cuh"
+#include "glu.cuh"
 #include "internal.h"
 #include "ptx.cuh"
 #include "quant.cuh"
@@ -45,6 +46,57 @@ __global__ void __launch_bounds__(ACT_THREADS) act_pack_kernel(const float* __re
     for (int i = 0; i < V; i++) {
         const int idx = threadIdx.x + i * ACT_THREADS;
         v[i] = idx < n4 ? __ldg(row + idx) : make_float4(0.f, 0.f, 0.f, 0.f);
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = red[0];
+#pragma unroll
+    for (int w = 1; w < ACT_THREADS / 32; w++) amax = fmaxf(amax, red[w]);
+    const float s = amax > 0.0f ? amax : 1.0f;
+    const float inv = __frcp_rn(s);
+    if (threadIdx.x == 0) scales[m] = s;
+#pragma unroll
+    for (int i = 0; i < V; i++) {
+        const int idx = threadIdx.x + i * ACT_THREADS;
+        if (idx < n4) {
+            uint2 w;
+            w.x = pack_half2(__fmul_rn(v[i].x, inv), __fmul_rn(v[i].y, inv));
+            w.y = pack_half2(__fmul_rn(v[i].z, inv), __fmul_rn(v[i].w, inv));
+            out[idx] = w;
+        }
+    }
+}
+
+// The dense FFN's SWIGLU fused into the down projection's activation pack: h = silu(gate) * up per
+// element (ggml_swiglu_split, the glue kernel's arithmetic), then the sandwich of h's row, exactly as
+// act_pack_kernel packs it -- so A16 and the scales equal SWIGLU followed by the pack, bit for bit,
+// and h itself is never written. One 256-thread CTA per row, V float4 of gate and of up per thread.
+template <int V>
+__global__ void __launch_bounds__(ACT_THREADS) swiglu_act_pack_kernel(const float* __restrict__ gate, int64_t ldg,
+                                                                      const float* __restrict__ up, int64_t ldu, int F,
+                                                                      __half* __restrict__ A16, float* __restrict__ scales) {
+    __shared__ float red[ACT_THREADS / 32];
+    grid_dep_wait();     // programmatic launch: gate and up are the previous kernel's output
+    grid_dep_launch();
+    const int m = blockIdx.x;
+    const float4* g4 = reinterpret_cast<const float4*>(gate + (size_t)m * ldg);
+    const float4* u4 = reinterpret_cast<const float4*>(up + (size_t)m * ldu);
+    uint2* out = reinterpret_cast<uint2*>(A16 + (size_t)m * F);
+    const int n4 = F / 4;
+    float4 v[V];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; i++) {
+        const int idx = threadIdx.x + i * ACT_THREADS;
+        if (idx < n4) {
+            const float4 x = __ldg(g4 + idx), y = __ldg(u4 + idx);
+            v[i] = make_float4(swiglu_f(x.x, y.x), swiglu_f(x.y, y.y), swiglu_f(x.z, y.z), swiglu_f(x.w, y.w));
+        } else {
+            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
     }
 #pragma unroll
@@ -323,7 +375,7 @@ static bool csplit_fits(int bt, int wtype) {
 // weights by the dequant warps, and the L2 feed of its operand tiles. Stream-K spreads the
 // tiles' K blocks evenly over the grid, so the time is the total over the grid plus a fixed
 // cost per work item and, where tiles are shared, the partial-tile round trip.
-static GemmPlan plan_gemm_knobs(int64_t M, int64_t N, int64_t K, int sms, int wtype, int tile) {
+static GemmPlan plan_gemm_knobs(int64_t M, int64_t N, int64_t K, int sms, int wtype, int tile, bool allow_pair) {
     const bool quant = wtype != WT_F16;
     const int nkb = (int)((K + GEMM_BK - 1) / GEMM_BK);
     const int gran = quant ? 4 : 1;
@@ -335,8 +387,8 @@ static GemmPlan plan_gemm_knobs(int64_t M, int64_t N, int64_t K, int sms, int wt
     const int n_bts = wtype == WT_Q4_K ? 5 : 4;
     const bool pair_default = !quant && M >= 1024;
     for (int pair = 0; pair < 2; pair++) {
-        if (pair && (pair_knob() == 0 || (pair_knob() < 0 && !pair_default))) continue;
-        if (!pair && (pair_knob() == 1 || (pair_knob() < 0 && pair_default)) && M > 64) continue;
+        if (pair && (!allow_pair || pair_knob() == 0 || (pair_knob() < 0 && !pair_default))) continue;
+        if (!pair && allow_pair && (pair_knob() == 1 || (pair_knob() < 0 && pair_default)) && M > 64) continue;
         const int tile_n = pair ? 2 * GEMM_BN : GEMM_BN;
         const int ntn = (int)((N + tile_n - 1) / tile_n);
         for (int bi = 0; bi < n_bts; bi++) {
@@ -415,9 +467,10 @@ static GemmPlan plan_gemm_knobs(int64_t M, int64_t N, int64_t K, int sms, int wt
     return best;
 }
 
-static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms, int wtype) {
-    GemmPlan p = plan_gemm_knobs(M, N, K, sms, wtype, tile_knob());
-    if (p.bt == 0) p = plan_gemm_knobs(M, N, K, sms, wtype, 0);   // the forced tile does not apply
+// allow_pair = false for a combined-N launch, whose members' tiles are 128 weight rows each.
+static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int sms, int wtype, bool allow_pair = true) {
+    GemmPlan p = plan_gemm_knobs(M, N, K, sms, wtype, tile_knob(), allow_pair);
+    if (p.bt == 0) p = plan_gemm_knobs(M, N, K, sms, wtype, 0, allow_pair);   // the forced tile does not apply
     return p;
 }
 
@@ -452,7 +505,8 @@ static MulMatWorkspace mm_workspace_layout(int64_t M, int64_t N, int64_t K, cons
 
 template <int BT, int WT, bool GROUPED, bool PAIR>
 static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmD,
-                                 const CUtensorMap& tmO, const GemmArgs& a, int grid, cudaStream_t st) {
+                                 const CUtensorMap& tmO, const GemmArgs& a, const GemmMembers& mm, int grid,
+                                 cudaStream_t st) {
     const bool cluster2 = PAIR || a.csplit == 2;
     using C = GemmCfg<BT, WT, PAIR>;
     static bool attr_set[64] = {false};
@@ -486,29 +540,30 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW,
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    return cudaLaunchKernelEx(&cfg, gemm_kernel<BT, WT, GROUPED, PAIR>, tmA, tmW, tmD, tmO, a);
+    return cudaLaunchKernelEx(&cfg, gemm_kernel<BT, WT, GROUPED, PAIR>, tmA, tmW, tmD, tmO, a, mm);
 }
 
 template <int WT, bool GROUPED>
 static cudaError_t launch_gemm_bt(int bt, bool pair, const CUtensorMap& tmA, const CUtensorMap& tmW,
-                                  const CUtensorMap& tmD, const CUtensorMap& tmO, const GemmArgs& a, int grid, cudaStream_t st) {
+                                  const CUtensorMap& tmD, const CUtensorMap& tmO, const GemmArgs& a,
+                                  const GemmMembers& mm, int grid, cudaStream_t st) {
     if constexpr (!GROUPED) {
         if (pair) {
             switch (bt) {
-                case 128: return launch_gemm_t<128, WT, false, true>(tmA, tmW, tmD, tmO, a, grid, st);
-                case 256: return launch_gemm_t<256, WT, false, true>(tmA, tmW, tmD, tmO, a, grid, st);
+                case 128: return launch_gemm_t<128, WT, false, true>(tmA, tmW, tmD, tmO, a, mm, grid, st);
+                case 256: return launch_gemm_t<256, WT, false, true>(tmA, tmW, tmD, tmO, a, mm, grid, st);
                 default: return cudaErrorInvalidValue;
             }
         }
     }
     if constexpr (!GROUPED && WT == WT_Q4_K) {
-        if (bt == 512) return launch_gemm_t<512, WT, false, false>(tmA, tmW, tmD, tmO, a, grid, st);
+        if (bt == 512) return launch_gemm_t<512, WT, false, false>(tmA, tmW, tmD, tmO, a, mm, grid, st);
     }
     switch (bt) {
-        case 32: return launch_gemm_t<32, WT, GROUPED, false>(tmA, tmW, tmD, tmO, a, grid, st);
-        case 64: return launch_gemm_t<64, WT, GROUPED, false>(tmA, tmW, tmD, tmO, a, grid, st);
-        case 128: return launch_gemm_t<128, WT, GROUPED, false>(tmA, tmW, tmD, tmO, a, grid, st);
-        default: return launch_gemm_t<256, WT, GROUPED, false>(tmA, tmW, tmD, tmO, a, grid, st);
+        case 32: return launch_gemm_t<32, WT, GROUPED, false>(tmA, tmW, tmD, tmO, a, mm, grid, st);
+        case 64: return launch_gemm_t<64, WT, GROUPED, false>(tmA, tmW, tmD, tmO, a, mm, grid, st);
+        case 128: return launch_gemm_t<128, WT, GROUPED, false>(tmA, tmW, tmD, tmO, a, mm, grid, st);
+        default: return launch_gemm_t<256, WT, GROUPED, false>(tmA, tmW, tmD, tmO, a, mm, grid, st);
     }
 }
 
@@ -551,12 +606,15 @@ bool make_weight_tile_maps(int wtype, const void* w_packed, int64_t wrows, int64
 
 template <bool GROUPED>
 cudaError_t launch_gemm_typed(int wtype, int bt, bool pair, const CUtensorMap& tmA, const CUtensorMap& tmW,
-                              const CUtensorMap& tmD, const CUtensorMap& tmO, const GemmArgs& a, int grid, cudaStream_t st) {
+                              const CUtensorMap& tmD, const CUtensorMap& tmO, const GemmArgs& a, int grid, cudaStream_t st,
+                              const GemmMembers* members = nullptr) {
+    static const GemmMembers none{};
+    const GemmMembers& mm = members ? *members : none;
     switch (wtype) {
-        case WT_F16: return launch_gemm_bt<WT_F16, GROUPED>(bt, pair, tmA, tmW, tmD, tmO, a, grid, st);
-        case WT_Q4_K: return launch_gemm_bt<WT_Q4_K, GROUPED>(bt, pair, tmA, tmW, tmD, tmO, a, grid, st);
-        case WT_Q6_K: return launch_gemm_bt<WT_Q6_K, GROUPED>(bt, pair, tmA, tmW, tmD, tmO, a, grid, st);
-        case WT_Q8_0: return launch_gemm_bt<WT_Q8_0, GROUPED>(bt, pair, tmA, tmW, tmD, tmO, a, grid, st);
+        case WT_F16: return launch_gemm_bt<WT_F16, GROUPED>(bt, pair, tmA, tmW, tmD, tmO, a, mm, grid, st);
+        case WT_Q4_K: return launch_gemm_bt<WT_Q4_K, GROUPED>(bt, pair, tmA, tmW, tmD, tmO, a, mm, grid, st);
+        case WT_Q6_K: return launch_gemm_bt<WT_Q6_K, GROUPED>(bt, pair, tmA, tmW, tmD, tmO, a, mm, grid, st);
+        case WT_Q8_0: return launch_gemm_bt<WT_Q8_0, GROUPED>(bt, pair, tmA, tmW, tmD, tmO, a, mm, grid, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -682,6 +740,97 @@ int gemm_packed_impl(int wtype, const void* w_packed, int64_t N, int64_t K, cons
     return e == cudaSuccess ? B200_OK : B200_E_CUDA;
 }
 
+// The combined-N GEMM of a fused group (the reference's _mul_mat_group, ggml-rocket.cpp:4956-5020:
+// one GEMM over the members' weights laid side by side, each member's columns unpacked into its
+// own dst). Here the members' 128-row weight tiles are numbered end to end and one persistent
+// launch takes them all under one schedule, so the group pays one launch's start and one tail
+// instead of one per member; every tile reads its member's weight and writes its member's dst
+// through that member's tensor maps. Weights of one type and K; no CTA pairs.
+static int64_t group_n_padded(int n, const int64_t* N) {
+    int64_t s = 0;
+    for (int m = 0; m < n; m++) s += (N[m] + GEMM_BN - 1) / GEMM_BN * GEMM_BN;
+    return s;
+}
+
+size_t gemm_packed_group_workspace(int n, int wtype, int64_t M, const int64_t* N, int64_t K) {
+    if (n <= 0 || n > GEMM_MAX_MEMBERS || !N || M <= 0 || K <= 0) return 0;
+    return streamk_bytes(plan_gemm(M, group_n_padded(n, N), K, device_sm_count(), wtype, false));
+}
+
+int gemm_packed_group_impl(int n, int wtype, const void* const* w_packed, const int64_t* N, int64_t K,
+                           const __half* a16, const float* scales, int64_t M, float* const* dst, const int64_t* ldd,
+                           void* workspace, size_t workspace_bytes, int* dev_err, cudaStream_t st) {
+    if (n <= 0 || n > GEMM_MAX_MEMBERS || !w_packed || !N || !dst || !ldd || !a16 || !scales || !dev_err || M <= 0 ||
+        K <= 0)
+        return B200_E_INVALID;
+    if (!weight_type_supported(wtype, K) || K % 32 != 0 || M > (1 << 30) || K > (1 << 30)) return B200_E_UNSUPPORTED;
+    for (int m = 0; m < n; m++) {
+        if (!w_packed[m] || !dst[m] || N[m] <= 0) return B200_E_INVALID;
+        if (N[m] % 16 != 0 || N[m] > (1 << 30) || ldd[m] % 4 != 0 || (reinterpret_cast<uintptr_t>(dst[m]) & 15u))
+            return B200_E_UNSUPPORTED;
+    }
+    const int64_t n_all = group_n_padded(n, N);
+    if (n_all > (1 << 30)) return B200_E_UNSUPPORTED;
+    const GemmPlan p = plan_gemm(M, n_all, K, device_sm_count(), wtype, false);
+    const size_t sk_bytes = streamk_bytes(p);
+    if (p.pair || (p.csplit && ((int64_t)p.grid != 2 * p.tiles || !csplit_fits(p.bt, wtype)))) return B200_E_INVALID;
+    if (sk_bytes && (!workspace || workspace_bytes < sk_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u)))
+        return B200_E_WORKSPACE;
+    CUtensorMap tmA, tmW, tmD, tmO;
+    const uint32_t a_box = (uint32_t)(p.bt > 256 ? 256 : p.bt);
+    if (!make_tmap_2d_f16(&tmA, a16, (uint64_t)M, (uint64_t)K, (uint64_t)K, a_box, GEMM_BK)) return B200_E_CUDA;
+    GemmMembers mm{};
+    GemmArgs a{};
+    int t0 = 0;
+    for (int m = 0; m < n; m++) {
+        CUtensorMap& w = m == 0 ? tmW : mm.w[m - 1];
+        CUtensorMap& d = m == 0 ? tmD : mm.d[m - 1];
+        CUtensorMap& o = m == 0 ? tmO : mm.o[m - 1];
+        if (!setup_weight_maps(wtype, w_packed[m], N[m], K, w, d, tmA)) return B200_E_CUDA;
+        if (!make_tmap_2d_f32_out(&o, dst[m], (uint64_t)M, (uint64_t)N[m], (uint64_t)ldd[m] * 4)) return B200_E_CUDA;
+        a.mem_t0[m] = t0;
+        t0 += (int)((N[m] + GEMM_BN - 1) / GEMM_BN);
+    }
+    a.n_mem = n;
+    a.scales = scales;
+    a.out = dst[0];
+    a.ldo = ldd[0];
+    a.M = (int)M;
+    a.N = (int)n_all;
+    a.K = (int)K;
+    a.n_tiles_n = p.ntn;
+    a.n_tiles_t = p.ntt;
+    a.nkb = p.nkb;
+    a.err = dev_err;
+    a.partials = sk_bytes ? static_cast<float*>(workspace) : nullptr;
+    a.flags = sk_bytes ? reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + streamk_partials_bytes(p))
+                       : nullptr;
+    a.epoch = next_epoch();
+    a.gran = p.gran;
+    a.tile_g = p.tile_g;
+    a.total_g = p.total_g;
+    a.csplit = p.csplit ? 2 : 0;
+    const cudaError_t e = launch_gemm_typed<false>(wtype, p.bt, false, tmA, tmW, tmD, tmO, a, p.grid, st, &mm);
+    return e == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
+int swiglu_act_pack_impl(const float* gate, int64_t ldg, const float* up, int64_t ldu, int64_t M, int64_t F,
+                         __half* a16, float* scales, cudaStream_t st) {
+    if (!gate || !up || !a16 || !scales || M <= 0 || F <= 0 || ldg < F || ldu < F) return B200_E_INVALID;
+    // rows of 16-byte vectors held in registers: F % 4 == 0, aligned rows, F <= 16 float4 per thread
+    const bool vec = F % 4 == 0 && ldg % 4 == 0 && ldu % 4 == 0 && (reinterpret_cast<uintptr_t>(gate) & 15u) == 0 &&
+                     (reinterpret_cast<uintptr_t>(up) & 15u) == 0;
+    const int64_t per = (F / 4 + ACT_THREADS - 1) / ACT_THREADS;
+    if (!vec || per > 16 || M > INT32_MAX) return B200_E_UNSUPPORTED;
+    const dim3 grid((unsigned)M), block(ACT_THREADS);
+    const int f = (int)F;
+    cudaError_t e;
+    if (per <= 4) e = launch_pdl(swiglu_act_pack_kernel<4>, grid, block, 0, st, gate, ldg, up, ldu, f, a16, scales);
+    else if (per <= 8) e = launch_pdl(swiglu_act_pack_kernel<8>, grid, block, 0, st, gate, ldg, up, ldu, f, a16, scales);
+    else e = launch_pdl(swiglu_act_pack_kernel<16>, grid, block, 0, st, gate, ldg, up, ldu, f, a16, scales);
+    return e == cudaSuccess ? B200_OK : B200_E_CUDA;
+}
+
 int act_pack_impl(const float* src1, int64_t lda, int64_t M, int64_t K, __half* a16, float* scales, cudaStream_t st) {
     if (!src1 || !a16 || !scales || M <= 0 || K <= 0 || lda < K) return B200_E_INVALID;
     return launch_act_pack(src1, lda, M, K, a16, scales, st) == cudaSuccess ? B200_OK : B200_E_CUDA;
@@ -793,6 +942,12 @@ int b200_act_pack(const float* src1, int64_t lda, int64_t M, int64_t K, void* a1
     return b200::act_pack_impl(src1, lda, M, K, static_cast<__half*>(a16), scales, static_cast<cudaStream_t>(stream));
 }
 
+int b200_swiglu_act_pack(const float* gate, int64_t ldg, const float* up, int64_t ldu, int64_t M, int64_t F, void* a16,
+                         float* scales, void* stream) {
+    return b200::swiglu_act_pack_impl(gate, ldg, up, ldu, M, F, static_cast<__half*>(a16), scales,
+                                      static_cast<cudaStream_t>(stream));
+}
+
 size_t b200_gemm_packed_workspace_size(int wtype, int64_t M, int64_t N, int64_t K) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
     return b200::streamk_bytes(b200::plan_gemm(M, N, K, b200::device_sm_count(), wtype));
@@ -803,6 +958,29 @@ int b200_gemm_packed(int wtype, const void* w_packed, int64_t N, int64_t K, cons
                      void* stream) {
     return b200::gemm_packed_impl(wtype, w_packed, N, K, static_cast<const __half*>(a16), scales, M, dst, ldd,
                                   workspace, workspace_bytes, dev_err, static_cast<cudaStream_t>(stream));
+}
+
+size_t b200_gemm_packed_group_workspace_size(int n_members, int wtype, int64_t M, const int64_t* N, int64_t K) {
+    return b200::gemm_packed_group_workspace(n_members, wtype, M, N, K);
+}
+
+int b200_gemm_packed_group(int n_members, int wtype, const void* const* w_packed, const int64_t* N, int64_t K,
+                           const void* a16, const float* scales, int64_t M, float* const* dst, const int64_t* ldd,
+                           void* workspace, size_t workspace_bytes, int* dev_err, void* stream) {
+    return b200::gemm_packed_group_impl(n_members, wtype, w_packed, N, K, static_cast<const __half*>(a16), scales, M,
+                                        dst, ldd, workspace, workspace_bytes, dev_err,
+                                        static_cast<cudaStream_t>(stream));
+}
+
+int b200_gemm_packed_group_plan(int n_members, int wtype, int64_t M, const int64_t* N, int64_t K, int* token_tile,
+                                int* splits, int* grid) {
+    if (n_members <= 0 || n_members > b200::GEMM_MAX_MEMBERS || !N || M <= 0 || K <= 0) return B200_E_INVALID;
+    const b200::GemmPlan p =
+        b200::plan_gemm(M, b200::group_n_padded(n_members, N), K, b200::device_sm_count(), wtype, false);
+    if (token_tile) *token_tile = p.bt;
+    if (splits) *splits = p.pieces;
+    if (grid) *grid = p.grid;
+    return B200_OK;
 }
 
 int b200_mul_mat_plan(int wtype, int64_t M, int64_t N, int64_t K, int* token_tile, int* splits, int* grid,

@@ -45,9 +45,13 @@ _SIGS = {
     "b200_mul_mat_workspace_size": (_sz, [_int, _i64, _i64, _i64]),
     "b200_mul_mat": (_int, [_int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _sz, _vp, _vp]),
     "b200_act_pack": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
+    "b200_swiglu_act_pack": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "b200_gemm_packed_workspace_size": (_sz, [_int, _i64, _i64, _i64]),
     "b200_gemm_packed": (_int, [_int, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _sz, _vp, _vp]),
     "b200_mul_mat_plan": (_int, [_int, _i64, _i64, _i64, _pint, _pint, _pint, _pint]),
+    "b200_gemm_packed_group_workspace_size": (_sz, [_int, _int, _i64, _vp, _i64]),
+    "b200_gemm_packed_group": (_int, [_int, _int, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _sz, _vp, _vp]),
+    "b200_gemm_packed_group_plan": (_int, [_int, _int, _i64, _vp, _i64, _pint, _pint, _pint]),
 }
 
 
@@ -130,6 +134,14 @@ def act_pack(a, M, K, a16, scales, lda=None, stream=None):
     check(lib().b200_act_pack(_ptr(a), lda, M, K, _ptr(a16), _ptr(scales), _stream(stream)), "act_pack")
 
 
+def swiglu_act_pack(gate, up, M, F, a16, scales, ldg=None, ldu=None, stream=None):
+    """a16 / scales = the activation pack of silu(gate) * up (b200_swiglu_act_pack)."""
+    ldg = F if ldg is None else ldg
+    ldu = F if ldu is None else ldu
+    check(lib().b200_swiglu_act_pack(_ptr(gate), ldg, _ptr(up), ldu, M, F, _ptr(a16), _ptr(scales), _stream(stream)),
+          "swiglu_act_pack")
+
+
 def gemm_packed_workspace_size(M, N, K, wtype=F16):
     return lib().b200_gemm_packed_workspace_size(wtype, M, N, K)
 
@@ -139,6 +151,34 @@ def gemm_packed(wtype, w_packed, N, K, a16, scales, M, out, workspace, dev_err, 
     wsb = 0 if workspace is None else workspace.numel() * workspace.element_size()
     check(lib().b200_gemm_packed(wtype, _ptr(w_packed), N, K, _ptr(a16), _ptr(scales), M, _ptr(out), ldd,
                                  _ptr(workspace), wsb, _ptr(dev_err), _stream(stream)), "gemm_packed")
+
+
+def _i64_array(vals):
+    return (ctypes.c_int64 * len(vals))(*[int(v) for v in vals])
+
+
+def gemm_packed_group_workspace_size(M, Ns, K, wtype=F16):
+    return lib().b200_gemm_packed_group_workspace_size(len(Ns), wtype, M, _i64_array(Ns), K)
+
+
+def gemm_packed_group(wtype, w_packed, Ns, K, a16, scales, M, outs, workspace, dev_err, ldds=None, stream=None):
+    """One combined-N GEMM launch over several weights (the fused group) against one packed
+    activation: outs[m] = scales * (a16 . W_m^T)."""
+    n = len(Ns)
+    ldds = list(Ns) if ldds is None else ldds
+    ws_arr = (ctypes.c_void_p * n)(*[_ptr(w) for w in w_packed])
+    out_arr = (ctypes.c_void_p * n)(*[_ptr(o) for o in outs])
+    wsb = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib().b200_gemm_packed_group(n, wtype, ws_arr, _i64_array(Ns), K, _ptr(a16), _ptr(scales), M, out_arr,
+                                       _i64_array(ldds), _ptr(workspace), wsb, _ptr(dev_err), _stream(stream)),
+          "gemm_packed_group")
+
+
+def gemm_packed_group_plan(M, Ns, K, wtype=F16):
+    vals = [ctypes.c_int(0) for _ in range(3)]
+    check(lib().b200_gemm_packed_group_plan(len(Ns), wtype, M, _i64_array(Ns), K, *[ctypes.byref(v) for v in vals]),
+          "gemm_packed_group_plan")
+    return dict(token_tile=vals[0].value, splits=vals[1].value, grid=vals[2].value)
 
 
 def mul_mat_plan(M, N, K, wtype=F16):

@@ -79,10 +79,34 @@ int    b200_mul_mat(int wtype, const void * w_packed, int64_t N, int64_t K,
  *                     the partial tiles of output tiles whose K range several CTAs share
  *                     (b200_gemm_packed_workspace_size bytes; 0 when no tile is shared). */
 int    b200_act_pack(const float * src1, int64_t lda, int64_t M, int64_t K, void * a16, float * scales, void * stream);
+/* A dense FFN's GLU SWIGLU fused into the pack of the down projection that reads it: h =
+ * silu(gate) * up per element (ggml_swiglu_split), then b200_act_pack of h's [M, F] rows -- a16 and
+ * scales equal b200_swiglu followed by b200_act_pack bit for bit; h is never written. The reference
+ * leaves SWIGLU to the host and packs the down projection's activations there (rk_pack_act_row,
+ * ggml-rocket.cpp:1451-1475). gate / up rows: F floats at row strides ldg / ldu, 16-byte aligned;
+ * F % 4 == 0 and F <= 16384, else B200_E_UNSUPPORTED. */
+int    b200_swiglu_act_pack(const float * gate, int64_t ldg, const float * up, int64_t ldu, int64_t M, int64_t F,
+                            void * a16, float * scales, void * stream);
 size_t b200_gemm_packed_workspace_size(int wtype, int64_t M, int64_t N, int64_t K);
 int    b200_gemm_packed(int wtype, const void * w_packed, int64_t N, int64_t K, const void * a16, const float * scales,
                         int64_t M, float * dst, int64_t ldd, void * workspace, size_t workspace_bytes, int * dev_err,
                         void * stream);
+
+/* The combined-N GEMM of a fused group (the reference's _mul_mat_group / _group_resident,
+ * ggml-rocket.cpp:4956-5020, 5040-5160: one GEMM over the members' weights side by side, each
+ * member's columns unpacked into its own dst): n_members (1..4) weights of one type and one K
+ * against the same packed activation, in ONE kernel launch whose schedule covers every member's
+ * tiles. dst[m][t * ldd[m] + n] = scales[t] * (a16 . W_m^T)[t, n] for n < N[m]. Each member's
+ * rules are b200_gemm_packed's; the workspace (256-byte aligned) holds
+ * b200_gemm_packed_group_workspace_size bytes. The plan call reports the token tile, the most CTAs
+ * sharing one tile's K range and the grid of that launch. */
+size_t b200_gemm_packed_group_workspace_size(int n_members, int wtype, int64_t M, const int64_t * N, int64_t K);
+int    b200_gemm_packed_group(int n_members, int wtype, const void * const * w_packed, const int64_t * N, int64_t K,
+                              const void * a16, const float * scales, int64_t M, float * const * dst,
+                              const int64_t * ldd, void * workspace, size_t workspace_bytes, int * dev_err,
+                              void * stream);
+int    b200_gemm_packed_group_plan(int n_members, int wtype, int64_t M, const int64_t * N, int64_t K,
+                                   int * token_tile, int * splits, int * grid);
 
 /* The launch plan b200_mul_mat uses on the current device: the token tile (tcgen05 N), the
  * most CTAs that share one output tile's K range (1 = every CTA owns whole tiles), the
