@@ -19,6 +19,7 @@
 #include <cmath>
 #include <cstring>
 #include <functional>
+#include <initializer_list>
 #include <list>
 #include <map>
 #include <set>
@@ -480,6 +481,8 @@ struct b200_backend {
     // grow-only device scratch arenas
     void* ws = nullptr;
     size_t ws_bytes = 0;
+    void* pre = nullptr;                     // a norm-fused activation pack for the MUL_MATs after it (grow-only)
+    size_t pre_bytes = 0;
     void* kv16 = nullptr;                    // a quantized KV cache's fp16 tiles (grow-only)
     size_t kv16_bytes = 0;
     // staging of host tensors, bump-allocated through one graph: device arena and pinned host
@@ -1169,7 +1172,11 @@ bool graph_finish(b200_backend* b) {
 
 // MUL_MAT, including ggml's batch broadcast over dims 2/3 (ggml-rocket.cpp:4725-4750), and a
 // group of MUL_MATs sharing src1 (fused: one activation pack, one GEMM per member).
-int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
+// pre_a16 / pre_scales (not null): src1 was packed by the kernel before it (a norm fused with the
+// pack) and its f32 rows were never written; the caller guarantees no member takes the decode kernel.
+int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng, const void* pre_a16 = nullptr,
+                     const float* pre_scales = nullptr) {
+    const bool pre = pre_a16 != nullptr;
     const b200_tensor* node0 = nodes[0];
     const b200_tensor* src1 = node0->src[1];
     const int64_t K = src1->ne[0], M = src1->ne[1];
@@ -1186,7 +1193,7 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
     }
     // staging: src1 and the members' dst when they are host tensors; workspace: A16 + scales + GEMM
     OpStaging stg;
-    stg.ins.push_back(src1);
+    if (!pre) stg.ins.push_back(src1);
     size_t need_ws = 0;
     for (int g = 0; g < ng; g++) {
         const b200_tensor* d = nodes[g];
@@ -1203,6 +1210,7 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
         any_gemm = any_gemm || !dec[g];
         if (dec[g]) need_ws = std::max(need_ws, b200_mul_mat_vec_workspace_size(M, nodes[g]->src[0]->ne[1], K));
     }
+    if (pre && any_dec) return B200_E_INVALID;
     // A group of 2-4 GEMM-sized members of one weight type runs as one combined-N launch
     // (B200_GEMM_COMBINE=0: one launch per member, as the single-op path does).
     bool comb = ng >= 2 && ng <= 4 && !any_dec && combine_knob() != 0;
@@ -1218,18 +1226,18 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
     if (!op_reserve(b, stg)) return B200_E_CUDA;
     if (!grow(&b->ws, &b->ws_bytes, need_ws, b->stream)) return B200_E_CUDA;
     bool ok = true;
-    const char* a_base = static_cast<const char*>(stage_in(b, src1, &ok));
+    const char* a_base = pre ? nullptr : static_cast<const char*>(stage_in(b, src1, &ok));
     std::vector<char*> d_base(ng);
     for (int g = 0; g < ng; g++) d_base[g] = stage_out(b, nodes[g], false, &ok);
     if (!ok || !op_inputs_ready(b)) return B200_E_CUDA;
     char* ws = static_cast<char*>(b->ws);
-    void* a16 = ws;
-    float* scales = reinterpret_cast<float*>(ws + a16_bytes);
+    void* a16 = pre ? const_cast<void*>(pre_a16) : ws;
+    float* scales = pre ? const_cast<float*>(pre_scales) : reinterpret_cast<float*>(ws + a16_bytes);
     void* gws = ws + a16_bytes + sc_bytes;
     const size_t gws_bytes = b->ws_bytes - a16_bytes - sc_bytes;
     for (int64_t i3 = 0; i3 < ne13; i3++) {
         for (int64_t i2 = 0; i2 < ne12; i2++) {
-            const float* A = reinterpret_cast<const float*>(a_base + i3 * src1->nb[3] + i2 * src1->nb[2]);
+            const float* A = pre ? nullptr : reinterpret_cast<const float*>(a_base + i3 * src1->nb[3] + i2 * src1->nb[2]);
             for (int g = 0; g < ng; g++) {
                 if (!dec[g]) continue;
                 const b200_tensor* d = nodes[g];
@@ -1240,7 +1248,7 @@ int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng) {
                 if (rc != B200_OK) return rc;
             }
             if (!any_gemm) continue;
-            int rc = b200_act_pack(A, (int64_t)(src1->nb[1] / 4), M, K, a16, scales, b->stream);
+            int rc = pre ? B200_OK : b200_act_pack(A, (int64_t)(src1->nb[1] / 4), M, K, a16, scales, b->stream);
             if (rc != B200_OK) return rc;
             if (comb) {
                 // one combined-N launch over every member (all 2-D, one type, GEMM-sized)
@@ -1754,6 +1762,79 @@ int do_rms_norm_mul(b200_backend* b, const b200_tensor* nrm, const b200_tensor* 
     return B200_OK;
 }
 
+// The MUL_MATs reading `t` (a fused norm's product) as src1, when they are all of t's readers, come
+// after node i0 and run as one group on the GEMM path: t's f32 rows are then never written, the norm
+// kernel packs them for the group instead (b200_rms_norm_mul_act_pack).
+bool pack_readers(b200_tensor* const* nodes, int n, int i0, const std::vector<bool>& done, const b200_tensor* t,
+                  std::vector<b200_tensor*>* grp, std::vector<int>* idx) {
+    if (!t->on_device || t->type != T_F32 || !is_contiguous(t) || t->ne[2] != 1 || t->ne[3] != 1) return false;
+    if (t->ne[0] % 4 != 0 || t->ne[0] > 16384) return false;
+    grp->clear();
+    idx->clear();
+    for (int j = 0; j < n; j++) {
+        for (int k = 0; k < B200_MAX_SRC; k++) {
+            if (nodes[j]->src[k] != t) continue;
+            if (j <= i0 || done[j] || k != 1 || nodes[j]->op != B200_OP_MUL_MAT || !node_fusable(nodes[j])) return false;
+            if (idx->empty() || idx->back() != j) {
+                grp->push_back(nodes[j]);
+                idx->push_back(j);
+            }
+        }
+    }
+    if (grp->empty() || grp->size() > 8) return false;
+    const int64_t M = t->ne[1];
+    for (const b200_tensor* mm : *grp)
+        if (kernel_wtype(mm->src[0]->type) != T_F16 && M < min_m_quant() && M <= 32) return false;   // decode kernel
+    return true;
+}
+
+// The fused norm kernel reads and writes 16-byte vectors: device tensors must start on 16 bytes
+// (host tensors are staged into 256-byte aligned device arenas).
+bool vec_ready(std::initializer_list<const b200_tensor*> ts) {
+    for (const b200_tensor* t : ts)
+        if (t && t->on_device && (reinterpret_cast<uintptr_t>(t->data) & 15u)) return false;
+    return true;
+}
+
+// [ADD ->] RMS_NORM -> MUL -> the MUL_MAT group reading the product: the norm (and the residual sum,
+// always written) in one launch that also packs the product for the group, then the group's GEMMs.
+int do_norm_pack_group(b200_backend* b, const b200_tensor* add, const b200_tensor* nrm, const b200_tensor* mul,
+                       bool write_norm, b200_tensor* const* grp, int ng) {
+    const b200_tensor* x = add ? add->src[0] : nrm->src[0];
+    const b200_tensor* r = add ? add->src[1] : nullptr;
+    const b200_tensor* w = mul->src[1];
+    const int64_t K = mul->ne[0], M = mul->ne[1];
+    const size_t a16_bytes = ((size_t)M * K * 2 + 255) & ~(size_t)255;
+    const size_t sc_bytes = ((size_t)M * 4 + 255) & ~(size_t)255;
+    if (!grow(&b->pre, &b->pre_bytes, a16_bytes + sc_bytes, b->stream)) return B200_E_CUDA;
+    OpStaging stg;
+    stg.ins = {x, w};
+    if (r) stg.ins.push_back(r);
+    if (add) stg.outs.push_back(add);
+    if (write_norm) stg.outs.push_back(nrm);
+    if (!op_reserve(b, stg)) return B200_E_CUDA;
+    bool ok = true;
+    const char* sx = static_cast<const char*>(stage_in(b, x, &ok));
+    const char* sr = r ? static_cast<const char*>(stage_in(b, r, &ok)) : nullptr;
+    const char* sw = static_cast<const char*>(stage_in(b, w, &ok));
+    char* ds = add ? stage_out(b, add, false, &ok) : nullptr;
+    char* dn = write_norm ? stage_out(b, nrm, false, &ok) : nullptr;
+    if (!ok || !op_inputs_ready(b)) return B200_E_CUDA;
+    float* scales = reinterpret_cast<float*>(static_cast<char*>(b->pre) + a16_bytes);
+    int rc = b200_rms_norm_mul_act_pack(reinterpret_cast<const float*>(sx), reinterpret_cast<const float*>(sr), mul->ne,
+                                        op_param_f32(nrm, 0), reinterpret_cast<const float*>(sw),
+                                        reinterpret_cast<float*>(ds), reinterpret_cast<float*>(dn), nullptr, b->pre,
+                                        scales, b->stream);
+    if (rc != B200_OK) return rc;
+    std::vector<char*> bases;
+    if (add) bases.push_back(ds);
+    if (write_norm) bases.push_back(dn);
+    if (!op_outputs_done(b, stg.outs, bases)) return B200_E_CUDA;
+    b->route_ops["glue"] += add ? 3 : 2;
+    b->route_ops["norm_pack"]++;
+    return do_mul_mat_group(b, grp, ng, b->pre, scales);
+}
+
 }  // namespace
 
 // ================================================================================================
@@ -1838,6 +1919,7 @@ void ggml_backend_b200_free(b200_backend_t b) {
         io_drain(b);
         for (void* p : b->transient) cudaFree(p);
         cudaFree(b->ws);
+        cudaFree(b->pre);
         cudaFree(b->kv16);
         cudaFree(b->io);
         cudaFree(b->wstage);
@@ -2059,6 +2141,22 @@ int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes,
                     bool write_norm = !nrm->on_device;
                     for (int j = i + 3; j < n && !write_norm; j++)
                         for (int k = 0; k < B200_MAX_SRC && !write_norm; k++) write_norm = nodes[j]->src[k] == nrm;
+                    std::vector<b200_tensor*> pg;
+                    std::vector<int> pidx;
+                    if (breaker_allow(b->brk_fused) &&
+                        vec_ready({node->src[0], node->src[1], node, nodes[i + 2]->src[1], write_norm ? nrm : nullptr}) &&
+                        pack_readers(nodes, n, i + 2, done, nodes[i + 2], &pg, &pidx)) {
+                        // ... and the activation pack of the MUL_MATs reading the product
+                        const int rc = do_norm_pack_group(b, node, nrm, nodes[i + 2], write_norm, pg.data(), (int)pg.size());
+                        breaker_note(b->brk_fused, rc, "fused norm + MUL_MAT pack");
+                        if (rc != B200_OK) {
+                            logf("E", "graph_compute: fused ADD+RMS_NORM*MUL+pack failed (%d) in node %s\n", rc, node->name);
+                            status = B200_STATUS_FAILED;
+                        }
+                        done[i + 1] = done[i + 2] = true;
+                        for (int j : pidx) done[j] = true;
+                        break;
+                    }
                     const int rc = do_add_rms_norm_mul(b, node, nrm, nodes[i + 2], true, write_norm);
                     if (rc != B200_OK) {
                         logf("E", "graph_compute: fused ADD+RMS_NORM*MUL failed (%d) in node %s\n", rc, node->name);
@@ -2071,6 +2169,23 @@ int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes,
                     bool write_norm = !node->on_device;
                     for (int j = i + 2; j < n && !write_norm; j++)
                         for (int k = 0; k < B200_MAX_SRC && !write_norm; k++) write_norm = nodes[j]->src[k] == node;
+                    std::vector<b200_tensor*> pg;
+                    std::vector<int> pidx;
+                    const b200_tensor* x0 = node->src[0];
+                    if (breaker_allow(b->brk_fused) && x0 && x0->type == T_F32 && is_contiguous(x0) &&
+                        vec_ready({x0, nodes[i + 1]->src[1], write_norm ? node : nullptr}) &&
+                        pack_readers(nodes, n, i + 1, done, nodes[i + 1], &pg, &pidx)) {
+                        const int rc = do_norm_pack_group(b, nullptr, node, nodes[i + 1], write_norm, pg.data(),
+                                                          (int)pg.size());
+                        breaker_note(b->brk_fused, rc, "fused norm + MUL_MAT pack");
+                        if (rc != B200_OK) {
+                            logf("E", "graph_compute: fused RMS_NORM*MUL+pack failed (%d) in node %s\n", rc, node->name);
+                            status = B200_STATUS_FAILED;
+                        }
+                        done[i + 1] = true;
+                        for (int j : pidx) done[j] = true;
+                        break;
+                    }
                     const int rc = do_rms_norm_mul(b, node, nodes[i + 1], write_norm);
                     if (rc != B200_OK) {
                         logf("E", "graph_compute: fused RMS_NORM*MUL failed (%d) in node %s\n", rc, node->name);

@@ -330,6 +330,150 @@ __global__ void __launch_bounds__(256) rope_token_kernel(const char* __restrict_
     }
 }
 
+// RMS_NORM times its weight row (the residual ADD in front when res is given) fused with the
+// activation pack of the product for the MUL_MATs that read it (the reference's sandwich,
+// rk_pack_act_row in ggml-rocket.cpp:1451-1475): one CTA per dense row held in registers (V float4
+// per thread); the sum of squares in the order rms_norm_kernel adds it, the products rounded as the
+// separate ops round them, then the row's max |value|, fp16(z / s) and s as act_pack_kernel makes
+// them. sum_dst / norm_dst / dst are written only when not null. Bit-identical to
+// b200_[add_]rms_norm_mul followed by b200_act_pack of its product.
+template <int V>
+__global__ void __launch_bounds__(RMS_THREADS) norm_mul_pack_kernel(const float* __restrict__ x,
+                                                                    const float* __restrict__ res, int ne0, float eps,
+                                                                    const float* __restrict__ w,
+                                                                    float* __restrict__ sum_dst,
+                                                                    float* __restrict__ norm_dst,
+                                                                    float* __restrict__ dst, __half* __restrict__ a16,
+                                                                    float* __restrict__ scales) {
+    grid_dep_wait();
+    grid_dep_launch();
+    __shared__ double red[RMS_THREADS / 32];
+    __shared__ float fred[RMS_THREADS / 32];
+    const int64_t r = blockIdx.x;
+    const float4* x4 = reinterpret_cast<const float4*>(x + r * ne0);
+    const float4* q4 = res ? reinterpret_cast<const float4*>(res + r * ne0) : nullptr;
+    const int n4 = ne0 / 4;
+    float4 v[V];
+    double sum = 0.0;
+#pragma unroll
+    for (int u = 0; u < V; u++) {
+        const int i = threadIdx.x + u * RMS_THREADS;
+        if (i < n4) {
+            v[u] = q4 ? add4(x4[i], q4[i]) : x4[i];
+            sum += (double)__fmul_rn(v[u].x, v[u].x);
+            sum += (double)__fmul_rn(v[u].y, v[u].y);
+            sum += (double)__fmul_rn(v[u].z, v[u].z);
+            sum += (double)__fmul_rn(v[u].w, v[u].w);
+        } else {
+            v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+    __syncthreads();
+    double tot = 0.0;
+#pragma unroll
+    for (int q = 0; q < RMS_THREADS / 32; q++) tot += red[q];
+    const float mean = (float)(tot / (double)ne0);
+    const float scale = 1.0f / sqrtf(__fadd_rn(mean, eps));
+    float amax = 0.0f;
+#pragma unroll
+    for (int u = 0; u < V; u++) {
+        const int i = threadIdx.x + u * RMS_THREADS;
+        if (i < n4) {
+            if (sum_dst) reinterpret_cast<float4*>(sum_dst + r * ne0)[i] = v[u];
+            const float4 y = make_float4(__fmul_rn(v[u].x, scale), __fmul_rn(v[u].y, scale), __fmul_rn(v[u].z, scale),
+                                         __fmul_rn(v[u].w, scale));
+            const float4 g = __ldg(reinterpret_cast<const float4*>(w) + i);
+            v[u] = make_float4(__fmul_rn(y.x, g.x), __fmul_rn(y.y, g.y), __fmul_rn(y.z, g.z), __fmul_rn(y.w, g.w));
+            if (norm_dst) reinterpret_cast<float4*>(norm_dst + r * ne0)[i] = y;
+            if (dst) reinterpret_cast<float4*>(dst + r * ne0)[i] = v[u];
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) fred[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = fred[0];
+#pragma unroll
+    for (int q = 1; q < RMS_THREADS / 32; q++) amax = fmaxf(amax, fred[q]);
+    const float s = amax > 0.0f ? amax : 1.0f;
+    const float inv = __frcp_rn(s);
+    if (threadIdx.x == 0) scales[r] = s;
+    uint2* out = reinterpret_cast<uint2*>(a16 + r * ne0);
+#pragma unroll
+    for (int u = 0; u < V; u++) {
+        const int i = threadIdx.x + u * RMS_THREADS;
+        if (i < n4) {
+            uint2 h;
+            h.x = pack_half2(__fmul_rn(v[u].x, inv), __fmul_rn(v[u].y, inv));
+            h.y = pack_half2(__fmul_rn(v[u].z, inv), __fmul_rn(v[u].w, inv));
+            out[i] = h;
+        }
+    }
+}
+
+// Normal-mode ROPE over rows whose pairs are 8-byte aligned (x's elements contiguous), one CTA per
+// token: the rope cache as in rope_token_kernel, then the token's (head, pair) items with 32-bit
+// indices (half = 2^half_shift pairs per row), each thread's RT pairs loaded as 8-byte vectors
+// before any is rotated, so one CTA has all its loads in flight at once. Same values and order of
+// operations as rope_kernel: bit-identical.
+constexpr int ROPE_RT = 8;
+__global__ void __launch_bounds__(256) rope_token_pairs_kernel(const char* __restrict__ x, Shape4 s,
+                                                              const int32_t* __restrict__ pos, int n_dims, int half_shift,
+                                                              float theta_scale, float freq_scale, float attn_factor,
+                                                              float* __restrict__ dst) {
+    grid_dep_wait();
+    grid_dep_launch();
+    __shared__ float cs[ROPE_MAX_HALF], sn[ROPE_MAX_HALF];
+    const int half_rot = n_dims / 2;
+    const int half_mask = (1 << half_shift) - 1;
+    const int n = (int)s.ne[1] << half_shift;     // pairs of one token
+    const int ne0 = (int)s.ne[0];
+    for (int64_t tok = blockIdx.x; tok < s.ne[2] * s.ne[3]; tok += gridDim.x) {
+        const int64_t i2 = tok % s.ne[2], i3 = tok / s.ne[2];
+        const char* tx = x + i2 * s.nb[2] + i3 * s.nb[3];
+        float* td = dst + (size_t)tok * (size_t)s.ne[1] * ne0;
+        float2 v[ROPE_RT];
+#pragma unroll
+        for (int u = 0; u < ROPE_RT; u++) {
+            const int i = threadIdx.x + 256 * u;
+            if (i < n)
+                v[u] = *reinterpret_cast<const float2*>(tx + (size_t)(i >> half_shift) * s.nb[1] + 8 * (i & half_mask));
+        }
+        if (threadIdx.x == 0) {
+            float theta = (float)pos[i2];
+            for (int j = 0; j < half_rot; j++) {
+                cs[j] = theta;
+                theta = __fmul_rn(theta, theta_scale);
+            }
+        }
+        __syncthreads();
+        for (int j = threadIdx.x; j < half_rot; j += blockDim.x) {
+            const float t = __fmul_rn(freq_scale, cs[j]);
+            sn[j] = __fmul_rn(sinf(t), attn_factor);
+            cs[j] = __fmul_rn(cosf(t), attn_factor);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int u = 0; u < ROPE_RT; u++) {
+            const int i = threadIdx.x + 256 * u;
+            if (i >= n) continue;
+            const int j = i & half_mask;
+            float2 o = v[u];
+            if (2 * j < n_dims) {
+                const float c = cs[j], sv = sn[j];
+                o.x = __fsub_rn(__fmul_rn(v[u].x, c), __fmul_rn(v[u].y, sv));
+                o.y = __fadd_rn(__fmul_rn(v[u].x, sv), __fmul_rn(v[u].y, c));
+            }
+            *reinterpret_cast<float2*>(td + (size_t)(i >> half_shift) * ne0 + 2 * j) = o;
+        }
+        __syncthreads();   // cs / sn are rewritten for the next token
+    }
+}
+
 // ---- GET_ROWS: dst[:, i10, i11, i12] = src[:, idx[i10, i11, i12], i11, i12] (f32 or f16 -> f32) ----
 // An index outside [0, src rows) records ERR_BAD_INDEX and writes zeros for that row.
 __global__ void get_rows_kernel(int f16, const char* __restrict__ src, Shape4 ss, const char* __restrict__ idx,
@@ -766,6 +910,29 @@ int b200_add_rms_norm_mul(const float* a, const float* b, const int64_t ne[4], f
                            dst, w, norm_dst, b, sum_dst));
 }
 
+int b200_rms_norm_mul_act_pack(const float* x, const float* res, const int64_t ne[4], float eps, const float* w,
+                               float* sum_dst, float* norm_dst, float* dst, void* a16, float* scales, void* stream) {
+    using namespace b200;
+    if (!x || !w || !a16 || !scales || (res && !sum_dst) || ne[0] <= 0 || ne[1] <= 0 || ne[2] <= 0 || ne[3] <= 0 ||
+        !(eps >= 0.0f))
+        return B200_E_INVALID;
+    auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    const int64_t rows = ne[1] * ne[2] * ne[3];
+    const int64_t per = (ne[0] / 4 + RMS_THREADS - 1) / RMS_THREADS;
+    if (ne[0] % 4 != 0 || per > 16 || rows > INT32_MAX || !al16(x) || !al16(w) || (res && !al16(res)) ||
+        (sum_dst && !al16(sum_dst)) || (norm_dst && !al16(norm_dst)) || (dst && !al16(dst)))
+        return B200_E_UNSUPPORTED;   // dense, aligned rows of at most 16384 values
+    const int n0 = (int)ne[0];
+    __half* h = static_cast<__half*>(a16);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const dim3 grid((unsigned)rows), block(RMS_THREADS);
+    if (per <= 1) return done(launch_pdl(norm_mul_pack_kernel<1>, grid, block, 0, st, x, res, n0, eps, w, sum_dst, norm_dst, dst, h, scales));
+    if (per <= 2) return done(launch_pdl(norm_mul_pack_kernel<2>, grid, block, 0, st, x, res, n0, eps, w, sum_dst, norm_dst, dst, h, scales));
+    if (per <= 4) return done(launch_pdl(norm_mul_pack_kernel<4>, grid, block, 0, st, x, res, n0, eps, w, sum_dst, norm_dst, dst, h, scales));
+    if (per <= 8) return done(launch_pdl(norm_mul_pack_kernel<8>, grid, block, 0, st, x, res, n0, eps, w, sum_dst, norm_dst, dst, h, scales));
+    return done(launch_pdl(norm_mul_pack_kernel<16>, grid, block, 0, st, x, res, n0, eps, w, sum_dst, norm_dst, dst, h, scales));
+}
+
 int b200_rms_norm_mul(const float* x, const int64_t ne[4], const size_t nb[4], float eps, const float* w,
                       float* norm_dst, float* dst, void* stream) {
     using namespace b200;
@@ -833,6 +1000,17 @@ int b200_rope(const float* x, const int64_t ne[4], const size_t nb[4], const int
     if (mode != 0 && mode != 2) return B200_E_UNSUPPORTED;
     const float theta_scale = powf(freq_base, -2.0f / (float)n_dims);   // the host libm's, as ggml's
     const int64_t n = (ne[0] / 2) * ne[1] * ne[2] * ne[3];
+    const int64_t half = ne[0] / 2;
+    const bool pow2 = half > 0 && (half & (half - 1)) == 0;
+    const bool pairs8 = nb[0] == 4 && ne[0] % 2 == 0 && nb[1] % 8 == 0 && nb[2] % 8 == 0 && nb[3] % 8 == 0 &&
+                        (reinterpret_cast<uintptr_t>(x) & 7u) == 0 && (reinterpret_cast<uintptr_t>(dst) & 7u) == 0;
+    if (mode == 0 && n_dims / 2 <= ROPE_MAX_HALF && pow2 && pairs8 && half * ne[1] <= 256 * ROPE_RT) {
+        int shift = 0;
+        while ((int64_t(1) << shift) < half) shift++;
+        return done(launch_pdl(rope_token_pairs_kernel, dim3((unsigned)std::min<int64_t>(ne[2] * ne[3], 148 * 8)),
+                               dim3(256), 0, static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x),
+                               shape_of(ne, nb), pos, n_dims, shift, theta_scale, freq_scale, attn_factor, dst));
+    }
     if (n_dims / 2 <= ROPE_MAX_HALF)
         return done(launch_pdl(rope_token_kernel, dim3((unsigned)std::min<int64_t>(ne[2] * ne[3], 148 * 8)), dim3(256), 0,
                                static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), pos,

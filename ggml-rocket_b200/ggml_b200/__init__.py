@@ -241,6 +241,7 @@ _BACKEND_SIGS = {
     "b200_rms_norm": (_int, [_vp, _vp, _vp, _f, _vp, _vp]),
     "b200_rms_norm_mul": (_int, [_vp, _vp, _vp, _f, _vp, _vp, _vp, _vp]),
     "b200_add_rms_norm_mul": (_int, [_vp, _vp, _vp, _f, _vp, _vp, _vp, _vp, _vp]),
+    "b200_rms_norm_mul_act_pack": (_int, [_vp, _vp, _vp, _f, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "b200_hadamard": (_int, [_vp, _vp, _vp, _f, _vp, _vp]),
     "b200_kv_to_f16": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
     "b200_binary": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),

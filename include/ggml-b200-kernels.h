@@ -207,6 +207,15 @@ int b200_rms_norm_mul(const float * x, const int64_t ne[4], const size_t nb[4], 
  * returns B200_E_UNSUPPORTED for operands that are not dense and aligned. */
 int b200_add_rms_norm_mul(const float * a, const float * b, const int64_t ne[4], float eps, const float * w,
                           float * sum_dst, float * norm_dst, float * dst, void * stream);
+/* The same norm (with the residual sum = x + res in front when res is not null) fused with the
+ * activation pack of its product for the MUL_MATs that read it: a16 [rows, ne[0]] fp16 and scales
+ * [rows] equal b200_act_pack of dst, bit for bit (the reference's rk_pack_act_row,
+ * ggml-rocket.cpp:1451-1475); sum_dst (required with res), norm_dst and dst (the f32 product) are
+ * written only when not null. Dense 16-byte aligned rows of ne[0] % 4 == 0 values, ne[0] <= 16384,
+ * else B200_E_UNSUPPORTED. */
+int b200_rms_norm_mul_act_pack(const float * x, const float * res, const int64_t ne[4], float eps, const float * w,
+                               float * sum_dst, float * norm_dst, float * dst, void * a16, float * scales,
+                               void * stream);
 /* A MUL_MAT whose src0 carries ggml's Walsh-Hadamard hint (GGML_HINT_SRC0_IS_HADAMARD), which the
  * reference declines (ggml-rocket.cpp:7392-7403) because the CPU evaluates it as the fast
  * transform: dst row = scale * H_n row for every row of x, H_n the Sylvester-ordered Hadamard

@@ -116,6 +116,31 @@ def test_rope(cuda, mode, n_dims, base, fscale):
         g.B200_E_UNSUPPORTED   # multi-section / vision modes stay on the host
 
 
+@pytest.mark.parametrize("T,H,pad,n_dims", [(512, 32, 0, 128), (512, 8, 0, 128), (65, 32, 2, 128), (40, 4, 6, 64)])
+def test_rope_normal_mode_rows(cuda, T, H, pad, n_dims):
+    """Normal-mode ROPE at Llama-3-8B's query / key shapes (the 8-byte pair kernel), on dense rows and
+    on a view whose head rows are wider than D, partial rotation included; against the oracle."""
+    import torch
+    import ggml_b200 as g
+    lib = g.lib()
+    D = 128
+    rng = np.random.default_rng(T * H + pad)
+    full = rng.standard_normal((T, H, D + pad)).astype(np.float32)
+    pos = rng.integers(0, 8192, T).astype(np.int32)
+    xd = torch.from_numpy(full).cuda()
+    view = xd[..., :D]
+    pd = torch.from_numpy(pos).cuda()
+    y = torch.empty((T, H, D), dtype=torch.float32, device="cuda")
+    ne = (ctypes.c_int64 * 4)(D, H, T, 1)
+    nb = (ctypes.c_size_t * 4)(4, (D + pad) * 4, H * (D + pad) * 4, T * H * (D + pad) * 4)
+    assert lib.b200_rope(_ptr(view), ne, nb, _ptr(pd), n_dims, 0, 500000.0, 1.0, 1.0, _ptr(y), None) == 0
+    torch.cuda.synchronize()
+    x = np.ascontiguousarray(full[..., :D])
+    want = oracle.rope(x, pos, n_dims, 0, 500000.0, 1.0, 1.0)
+    assert rel_err(y.cpu().numpy(), want) <= GLUE_TOL
+    assert np.array_equal(y.cpu().numpy()[..., n_dims:], x[..., n_dims:])
+
+
 def test_get_rows_and_cpy(cuda):
     import torch
     import ggml_b200 as g
