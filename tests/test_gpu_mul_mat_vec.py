@@ -58,7 +58,8 @@ def _case(wtype, N, K, M, seed):
 
 
 @pytest.mark.parametrize("wtype", [Q4_K, Q6_K, Q8_0])
-@pytest.mark.parametrize("N,K,M", [(4096, 4096, 1), (14336, 4096, 2), (4096, 14336, 3), (1000, 512, 4),
+@pytest.mark.parametrize("N,K,M", [(4096, 4096, 1), (4096, 14336, 1), (1001, 2816, 1), (14336, 4096, 2),
+                                   (4096, 14336, 3), (1000, 512, 4),
                                    (200, 256, 7), (4104, 4096, 8), (64, 2048, 5), (4096, 4096, 9),
                                    (1024, 2048, 16), (520, 1024, 17), (2048, 4096, 24), (1000, 768, 31),
                                    (4096, 4096, 32)])
@@ -130,7 +131,7 @@ def test_mul_mat_vec_declines_what_it_does_not_tile(cuda):
     # tiled path (M > 8), and a 255-byte workspace fails the row-block path
     small = x[:g.lib().b200_mul_mat_vec_workspace_size(20, 64, 256) - 1]
     assert g.mul_mat_vec(g.Q4_K, x, 64, 256, f, 20, f, small, err) == g.B200_E_INVALID
-    assert g.mul_mat_vec(g.Q4_K, x, 64, 256, f, 1, f, x[:255], err) == g.B200_E_INVALID
+    assert g.mul_mat_vec(g.Q4_K, x, 64, 256, f, 2, f, x[:255], err) == g.B200_E_INVALID
 
 
 def test_mul_mat_vec_back_to_back_shared_workspace(cuda):
@@ -166,7 +167,9 @@ def test_mul_mat_vec_back_to_back_shared_workspace(cuda):
 @pytest.mark.parametrize("schedule", ["rows", "stream", "tiles"])
 def test_mul_mat_vec_each_schedule(cuda, schedule):
     """Each kernel for Q4_K at M <= 8 forced for every such M (B200_GEMV_SCHEDULE, read once per
-    process, so in a child; unset, M <= 5 takes the row-block kernel and M >= 6 the tiled one): the parity cases, the strided cases and the back-to-back shared-workspace case under
+    process, so in a child; unset, M <= 5 takes the row-block kernel and M >= 6 the tiled one, and
+    Q8_0 at M = 1 the one-launch fp32 kernel): the parity cases, the strided cases and the
+    back-to-back shared-workspace case under
     each."""
     import os
     import subprocess
