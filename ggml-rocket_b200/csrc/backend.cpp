@@ -1171,7 +1171,8 @@ bool graph_finish(b200_backend* b) {
 }
 
 // MUL_MAT, including ggml's batch broadcast over dims 2/3 (ggml-rocket.cpp:4725-4750), and a
-// group of MUL_MATs sharing src1 (fused: one activation pack, one GEMM per member).
+// group of MUL_MATs sharing src1 (fused: one activation pack, then one combined-N GEMM launch over
+// every member's weight tiles, or one GEMM per member when their types differ).
 // pre_a16 / pre_scales (not null): src1 was packed by the kernel before it (a norm fused with the
 // pack) and its f32 rows were never written; the caller guarantees no member takes the decode kernel.
 int do_mul_mat_group(b200_backend* b, b200_tensor* const* nodes, int ng, const void* pre_a16 = nullptr,
