@@ -536,7 +536,7 @@ static int gv_sm_count() {
 // crossover measured on B200 (bench.py --workload gemv, the headline's three Q4_K weights: rows
 // 1209 / 1068 / 957 GB/s at M = 4 / 6 / 8, tiles 1068-1069 GB/s at each).
 // ---------------------------------------------------------------------------------------------
-// M = 1, Q8_0: one launch with no activation prep and no staging of the weights. A CTA of
+// M = 1, Q8_0 and Q6_K: one launch with no activation prep and no staging of the weights. A CTA of
 // NW = ceil(K / 2048) warps spans a row's K; lane l of warp w owns the 64 weights [2048w + 64l,
 // +64) (blocks 2c, 2c + 1 of group 8w + l / 4, c = l % 4), keeps their 64 x values in registers
 // (brought in by coalesced loads through shared memory), and walks groups of GV1_R rows with the
@@ -544,9 +544,9 @@ static int gv_sm_count() {
 // 32-weight block, acc = sum q * x (the codes exact in fp32, two at a time) times the block's d;
 // the lanes' parts are added by shuffles, the warps' in shared memory. fp32 throughout, within the
 // decode tolerance of the fp64 oracle (the sums are ordered differently from the reference's).
-// Measured on B200 against the tiled kernel at M = 1 (the headline's three weights as Q8_0):
-// 2401 against 1809 GB/s. The same scheme for Q4_K (its decode is twice the work per byte) ran at
-// 1338 GB/s against the row-block kernel's 1441, so Q4_K keeps that kernel.
+// Measured on B200 against the tiled kernel at M = 1 (the headline's three weights): Q8_0 2401
+// against 1809 GB/s, Q6_K 1678 against 1266. The same scheme for Q4_K (the most decode work per
+// byte) ran at 1338 GB/s against the row-block kernel's 1441, so Q4_K keeps that kernel.
 // ---------------------------------------------------------------------------------------------
 constexpr int GV1_R = 4;
 constexpr int GV1_MAXW = 8;                    // K <= 16384
@@ -577,12 +577,14 @@ __device__ __forceinline__ void gv1_load_x(const float* __restrict__ x, int K, i
     }
 }
 
-// the rows' parts: shuffles within the warp, then the NW warps' sums in shared memory
-__device__ __forceinline__ void gv1_store_rows(const float (&part)[GV1_R], float (*red)[GV1_MAXW][GV1_R], int par,
+// the R rows' parts: shuffles within the warp, then the NW warps' sums in shared memory
+template <int R>
+__device__ __forceinline__ void gv1_store_rows(const float (&part)[R], float (*red)[GV1_MAXW][GV1_R], int par,
                                                int warp, int lane, int nw, int64_t r0, int64_t N,
                                                float* __restrict__ dst) {
+    static_assert(R <= GV1_R, "row group");
 #pragma unroll
-    for (int r = 0; r < GV1_R; r++) {
+    for (int r = 0; r < R; r++) {
         float v = part[r];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -590,7 +592,7 @@ __device__ __forceinline__ void gv1_store_rows(const float (&part)[GV1_R], float
     }
     __syncthreads();
     // red[par] is next written two groups later, after every thread has passed the next barrier
-    if (threadIdx.x < GV1_R && r0 + threadIdx.x < N) {
+    if (threadIdx.x < R && r0 + threadIdx.x < N) {
         float s = 0.0f;
         for (int i = 0; i < nw; i++) s += red[par][i][threadIdx.x];
         dst[r0 + threadIdx.x] = s;
@@ -673,6 +675,95 @@ __global__ void __launch_bounds__(32 * GV1_MAXW) gemv1_q8_0_kernel(const uint8_t
     }
 }
 
+// Q6_K weights in the packed layout (208-byte rows {ql[128], qh[64], scales[16]} per super-block,
+// d in the transposed plane [nsb][N] after the rows): lane l of warp w owns the 64 weights of
+// quarter c = l % 4 of super-block 8w + l / 4 -- half c / 2 of the super-block, its low (c even) or
+// high (c odd) 4-bit codes: 64 ql bytes, 32 qh bytes and 4 scales. Two rows per group.
+constexpr int GV1_R6 = 2;
+struct Gv1Q6 {
+    uint4 ql[GV1_R6][4], qh[GV1_R6][2];
+    uint32_t sc[GV1_R6];
+    uint32_t d[GV1_R6];
+};
+
+__global__ void __launch_bounds__(32 * GV1_MAXW) gemv1_q6k_kernel(const uint8_t* __restrict__ w, int64_t N, int K,
+                                                                  size_t d_off, const float* __restrict__ x,
+                                                                  float* __restrict__ dst) {
+    __shared__ float red[2][GV1_MAXW][GV1_R];
+    extern __shared__ __align__(16) float gv1_smem[];   // the x staging rows of the CTA's NW warps
+    auto stage = reinterpret_cast<float (*)[32][GV1_XS]>(gv1_smem);
+    grid_dep_wait();   // programmatic launch: x may be the previous kernel's output
+    grid_dep_launch();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nw = (int)(blockDim.x >> 5);
+    const int nsb = K / 256;
+    const int sb = warp * 8 + (lane >> 2);
+    const int hh = (lane & 3) >> 1, hi4 = lane & 1;   // the half, and low / high codes
+    const bool live = sb < nsb;
+    const int64_t row_bytes = (int64_t)nsb * 208;
+    const uint16_t* dplane = reinterpret_cast<const uint16_t*>(w + d_off);
+    const int64_t stride = (int64_t)gridDim.x * GV1_R6;
+    auto load = [&](int64_t r0, Gv1Q6& b) {
+#pragma unroll
+        for (int r = 0; r < GV1_R6; r++) {
+            if (live && r0 + r < N) {
+                const uint8_t* blk = w + (r0 + r) * row_bytes + (int64_t)sb * 208;
+#pragma unroll
+                for (int j = 0; j < 4; j++) b.ql[r][j] = __ldg(reinterpret_cast<const uint4*>(blk + 64 * hh) + j);
+#pragma unroll
+                for (int j = 0; j < 2; j++) b.qh[r][j] = __ldg(reinterpret_cast<const uint4*>(blk + 128 + 32 * hh) + j);
+                b.sc[r] = __ldg(reinterpret_cast<const uint32_t*>(blk + 192 + 8 * hh + 4 * hi4));
+                b.d[r] = __ldg(dplane + (int64_t)sb * N + (r0 + r));
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; j++) b.ql[r][j] = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                for (int j = 0; j < 2; j++) b.qh[r][j] = make_uint4(0u, 0u, 0u, 0u);
+                b.sc[r] = 0u;   // zero scales: the row's part is zero whatever the codes
+                b.d[r] = 0u;
+            }
+        }
+    };
+    Gv1Q6 cur;
+    load((int64_t)blockIdx.x * GV1_R6, cur);
+    uint64_t xv[2][16];
+    gv1_load_x(x, K, warp, lane, stage, xv);
+    const uint64_t MAG = f2_pack(-8388640.0f, -8388640.0f);   // -(2^23 + 32)
+    int par = 0;
+    for (int64_t r0 = (int64_t)blockIdx.x * GV1_R6; r0 < N; r0 += stride, par ^= 1) {
+        Gv1Q6 nxt;
+        load(r0 + stride, nxt);                // in flight while this group is computed
+        float part[GV1_R6];
+#pragma unroll
+        for (int r = 0; r < GV1_R6; r++) {
+            float sum = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {         // 16 weights t = 16j .. 16j + 15 of the lane's 64, scale j
+                const uint4 l4 = cur.ql[r][j];
+                const uint4 h4 = cur.qh[r][j & 1];   // qh byte t % 32
+                const int hs = 4 * hi4 + 2 * (j >> 1);
+                const uint32_t lw[4] = {l4.x, l4.y, l4.z, l4.w}, hw[4] = {h4.x, h4.y, h4.z, h4.w};
+                uint64_t acc = f2_pack(0.0f, 0.0f);
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const uint32_t q = ((lw[k] >> (4 * hi4)) & 0x0F0F0F0Fu) | (((hw[k] >> hs) & 0x03030303u) << 4);
+#pragma unroll
+                    for (int i = 0; i < 2; i++) {
+                        const int t2 = (16 * j + 4 * k) / 2 + i;   // pair index of x within the lane's 64
+                        acc = f2_fma(f2_add(magic_pair(q, i), MAG), xv[t2 >> 4][t2 & 15], acc);
+                    }
+                }
+                float a0, a1;
+                f2_unpack(acc, a0, a1);
+                sum += (float)(int8_t)((cur.sc[r] >> (8 * j)) & 0xffu) * (a0 + a1);
+            }
+            part[r] = h2f_bits(cur.d[r]) * sum;
+        }
+        gv1_store_rows(part, red, par, warp, lane, nw, r0, N, dst);
+        cur = nxt;
+    }
+}
+
 constexpr int GV_ROWS_DEFAULT_MMAX = 5;
 enum GvSchedule { GV_DEFAULT_SCHEDULE, GV_ROWS_SCHEDULE, GV_STREAM_SCHEDULE, GV_TILES_SCHEDULE };
 static GvSchedule gv_schedule() {
@@ -719,7 +810,21 @@ int b200_mul_mat_vec(int wtype, const void* w_packed, int64_t N, int64_t K, cons
     using namespace b200;
     if (!w_packed || !src1 || !dst || !dev_err || N <= 0 || K <= 0 || M <= 0 || lda < K || ldd < N)
         return B200_E_INVALID;
-    // M = 1, Q8_0 (unless a schedule is forced): the one-launch fp32 kernel, which needs no workspace
+    // M = 1, Q6_K or Q8_0 (unless a schedule is forced): the one-launch fp32 kernels, which need no workspace
+    if (wtype == WT_Q6_K && M == 1 && gv_schedule() == GV_DEFAULT_SCHEDULE && K % 256 == 0 &&
+        K <= 256 * 8 * GV1_MAXW && N <= (1ll << 40) && (reinterpret_cast<uintptr_t>(w_packed) & 15u) == 0 &&
+        (reinterpret_cast<uintptr_t>(src1) & 15u) == 0) {
+        size_t d_off = 0;
+        packed_weight_bytes(WT_Q6_K, N, K, &d_off);
+        const int nw = (int)((K / 256 + 7) / 8);
+        const int64_t groups = (N + GV1_R6 - 1) / GV1_R6;
+        const int64_t per_sm = std::max(1, 12 / nw);
+        const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(groups, gv_sm_count() * per_sm));
+        const cudaError_t e = launch_pdl(gemv1_q6k_kernel, dim3((unsigned)grid), dim3(32 * nw),
+                                         (size_t)nw * 32 * GV1_XS * 4, static_cast<cudaStream_t>(stream),
+                                         static_cast<const uint8_t*>(w_packed), N, (int)K, d_off, src1, dst);
+        return e == cudaSuccess ? B200_OK : B200_E_CUDA;
+    }
     if (wtype == WT_Q8_0 && M == 1 && gv_schedule() == GV_DEFAULT_SCHEDULE && K % 32 == 0 && K <= 256 * 8 * GV1_MAXW &&
         N <= (1ll << 40) && (reinterpret_cast<uintptr_t>(w_packed) & 15u) == 0 &&
         (reinterpret_cast<uintptr_t>(src1) & 15u) == 0) {
