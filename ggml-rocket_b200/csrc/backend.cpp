@@ -23,6 +23,7 @@
 #include <list>
 #include <map>
 #include <set>
+#include <chrono>
 #include <condition_variable>
 #include <mutex>
 #include <string>
@@ -1999,8 +2000,18 @@ void ggml_backend_b200_breaker_replay(const int* rcs, int n, int* attempted) {
 int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes, int n) {
     if (!b || (n > 0 && !nodes)) return B200_STATUS_FAILED;
     std::lock_guard<std::mutex> lk(b->mu);
+    const auto t_enter = std::chrono::steady_clock::now();
     if (!ensure_device(b)) return B200_STATUS_FAILED;
     cudaSetDevice(b->device);
+    // B200_GRAPH_TIMING=1: report per graph the host's time to queue the work, the device span from
+    // the first queued operation to the last, and the whole call (a diagnostic; off by default)
+    static const bool timing = knob_on("B200_GRAPH_TIMING", false);
+    cudaEvent_t tev[2] = {nullptr, nullptr};
+    if (timing) {
+        cudaEventCreate(&tev[0]);
+        cudaEventCreate(&tev[1]);
+        cudaEventRecord(tev[0], b->stream);
+    }
     const bool fuse = fuse_on();
     std::vector<bool> done(n, false);
     int status = B200_STATUS_SUCCESS;
@@ -2213,9 +2224,22 @@ int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes,
                 status = B200_STATUS_FAILED;
         }
     }
+    const auto t_queued = std::chrono::steady_clock::now();
+    if (timing) cudaEventRecord(tev[1], b->stream);
     if (!graph_finish(b)) status = B200_STATUS_FAILED;
     for (void* p : b->transient) cudaFree(p);
     b->transient.clear();
+    if (timing) {
+        float dev_ms = 0.0f;
+        cudaEventSynchronize(tev[1]);
+        cudaEventElapsedTime(&dev_ms, tev[0], tev[1]);
+        const auto t_exit = std::chrono::steady_clock::now();
+        using us = std::chrono::duration<double, std::micro>;
+        fprintf(stderr, "B200_GRAPH_TIMING nodes %d queue_us %.1f device_us %.1f call_us %.1f\n", n,
+                us(t_queued - t_enter).count(), 1000.0 * dev_ms, us(t_exit - t_enter).count());
+        cudaEventDestroy(tev[0]);
+        cudaEventDestroy(tev[1]);
+    }
     return status;
 }
 
