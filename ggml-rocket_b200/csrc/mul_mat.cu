@@ -396,6 +396,11 @@ static GemmPlan plan_gemm_knobs(int64_t M, int64_t N, int64_t K, int sms, int wt
             if (bi > 0 && bts[bi - 1] >= M) break;      // a smaller tile already covers M
             if (pair && (bt < 128 || bt > 256)) continue;   // each CTA of a pair stages 64..128 tokens
             if (tile > 0 && bt != tile) continue;
+            // the wide unit holds one accumulator, so its epilogue never overlaps a main loop: measured
+            // slower than 256-token tiles at M = 512 (a single 4096 x 14336 weight, and a layer's
+            // combined gate/up launch: 37.1-37.6 k against 38.1-38.3 k prompt tokens/s), faster at
+            // M = 2048 (217 against 232 us) -- left to the model only above M = 512 unless forced
+            if (bt == 512 && M <= 512 && tile != 512) continue;
             const int ntt = (int)((M + bt - 1) / bt);
             const int64_t tiles = (int64_t)ntn * ntt;
             const int64_t total_g = tiles * tile_g;
