@@ -1524,6 +1524,68 @@ int do_swiglu_mul_mat(b200_backend* b, const b200_tensor* gate, const b200_tenso
     return B200_OK;
 }
 
+// ROPE (normal mode) whose only reader is a CPY of its result into an fp16 tensor -- llama.cpp's
+// write of the rotated K rows into the KV-cache view -- with only view nodes in between: the pair
+// runs as one b200_rope_f16 and the f32 rotated rows are never written. Device tensors only, with
+// the layouts the fp16-output kernel takes; *cpy_idx: the CPY's node index.
+static bool rope_cpy_match(b200_tensor* const* nodes, int n, int i, const std::vector<bool>& done, int* cpy_idx) {
+    const b200_tensor* r = nodes[i];
+    const b200_tensor* x = r->src[0];
+    const b200_tensor* pos = r->src[1];
+    if (r->op != B200_OP_ROPE || r->op_params[2] != 0 || !r->on_device || r->type != T_F32 || !x || !pos ||
+        !x->on_device || !pos->on_device || !ggml_backend_b200_supports_op(r))
+        return false;
+    const int64_t half = x->ne[0] / 2;
+    if (x->nb[0] != 4 || x->ne[0] % 2 || half <= 0 || (half & (half - 1)) || half * x->ne[1] > 2048 ||
+        r->op_params[1] / 2 > 256 || x->nb[1] % 8 || x->nb[2] % 8 || x->nb[3] % 8 ||
+        (reinterpret_cast<uintptr_t>(x->data) & 7u))
+        return false;
+    int j = -1;
+    for (int k = 0; k < n; k++) {
+        for (int q = 0; q < B200_MAX_SRC; q++) {
+            if (nodes[k]->src[q] != r) continue;
+            if (j >= 0 || k <= i || q != 0) return false;   // one reader, after the ROPE, as the CPY source
+            j = k;
+        }
+    }
+    if (j < 0 || done[j]) return false;
+    const b200_tensor* c = nodes[j];
+    if (c->op != B200_OP_CPY || c->type != T_F16 || !c->on_device || !ggml_backend_b200_supports_op(c)) return false;
+    for (int d = 0; d < 4; d++)
+        if (c->ne[d] != r->ne[d]) return false;
+    if (c->nb[0] != 2 || c->nb[1] % 4 || c->nb[2] % 4 || c->nb[3] % 4 || (reinterpret_cast<uintptr_t>(c->data) & 3u))
+        return false;
+    for (int k = i + 1; k < j; k++) {
+        const int op = nodes[k]->op;
+        if (op != B200_OP_NONE && op != B200_OP_RESHAPE && op != B200_OP_VIEW && op != B200_OP_PERMUTE &&
+            op != B200_OP_TRANSPOSE)
+            return false;
+    }
+    *cpy_idx = j;
+    return true;
+}
+
+int do_rope_cpy(b200_backend* b, const b200_tensor* r, const b200_tensor* c) {
+    const b200_tensor* x = r->src[0];
+    const b200_tensor* pos = r->src[1];
+    OpStaging stg;
+    stg.ins = {x, pos};
+    stg.outs = {c};
+    if (!op_reserve(b, stg)) return B200_E_CUDA;
+    bool ok = true;
+    const float* sx = static_cast<const float*>(stage_in(b, x, &ok));
+    const int32_t* sp = static_cast<const int32_t*>(stage_in(b, pos, &ok));
+    char* d = stage_out(b, c, false, &ok);
+    if (!ok || !op_inputs_ready(b)) return B200_E_CUDA;
+    const int rc = b200_rope_f16(sx, x->ne, x->nb, sp, r->op_params[1], r->op_params[2], op_param_f32(r, 5),
+                                 op_param_f32(r, 6), op_param_f32(r, 8), d, c->nb, b->stream);
+    if (rc != B200_OK) return rc;
+    if (!op_outputs_done(b, stg.outs, {d})) return B200_E_CUDA;
+    b->route_ops["glue"] += 2;
+    b->route_ops["rope_cpy"]++;
+    return B200_OK;
+}
+
 int do_flash_attn(b200_backend* b, b200_tensor* op) {
     const b200_tensor* q = op->src[0];
     const b200_tensor* k = op->src[1];
@@ -2129,6 +2191,18 @@ int ggml_backend_b200_graph_compute(b200_backend_t b, b200_tensor* const* nodes,
             case B200_OP_DIV: {
                 if (!ggml_backend_b200_supports_op(node)) {
                     status = B200_STATUS_FAILED;
+                    break;
+                }
+                // ROPE -> the CPY of its result into an fp16 KV-cache view: one pass
+                int cpy_j = -1;
+                if (fuse && breaker_allow(b->brk_fused) && rope_cpy_match(nodes, n, i, done, &cpy_j)) {
+                    const int rc = do_rope_cpy(b, node, nodes[cpy_j]);
+                    breaker_note(b->brk_fused, rc, "fused ROPE + CPY");
+                    if (rc != B200_OK) {
+                        logf("E", "graph_compute: fused ROPE + CPY failed (%d) in node %s\n", rc, node->name);
+                        status = B200_STATUS_FAILED;
+                    }
+                    done[cpy_j] = true;
                     break;
                 }
                 // GLU SWIGLU -> the down MUL_MAT reading it: the SWIGLU inside the down projection's

@@ -419,12 +419,16 @@ __global__ void __launch_bounds__(RMS_THREADS) norm_mul_pack_kernel(const float*
 // token: the rope cache as in rope_token_kernel, then the token's (head, pair) items with 32-bit
 // indices (half = 2^half_shift pairs per row), each thread's RT pairs loaded as 8-byte vectors
 // before any is rotated, so one CTA has all its loads in flight at once. Same values and order of
-// operations as rope_kernel: bit-identical.
+// operations as rope_kernel: bit-identical. F16OUT: each rotated pair is rounded to fp16 (round to
+// nearest even, as the f32 -> f16 CPY rounds) and stored at dst + i1 nb1 + i2 nb2 + i3 nb3 of the
+// fp16 destination sd (the ROPE and the CPY of its output into a KV-cache view in one pass);
+// otherwise dst is the contiguous f32 result.
 constexpr int ROPE_RT = 8;
+template <bool F16OUT>
 __global__ void __launch_bounds__(256) rope_token_pairs_kernel(const char* __restrict__ x, Shape4 s,
                                                               const int32_t* __restrict__ pos, int n_dims, int half_shift,
                                                               float theta_scale, float freq_scale, float attn_factor,
-                                                              float* __restrict__ dst) {
+                                                              char* __restrict__ dst, Shape4 sd) {
     grid_dep_wait();
     grid_dep_launch();
     __shared__ float cs[ROPE_MAX_HALF], sn[ROPE_MAX_HALF];
@@ -435,7 +439,8 @@ __global__ void __launch_bounds__(256) rope_token_pairs_kernel(const char* __res
     for (int64_t tok = blockIdx.x; tok < s.ne[2] * s.ne[3]; tok += gridDim.x) {
         const int64_t i2 = tok % s.ne[2], i3 = tok / s.ne[2];
         const char* tx = x + i2 * s.nb[2] + i3 * s.nb[3];
-        float* td = dst + (size_t)tok * (size_t)s.ne[1] * ne0;
+        float* td = reinterpret_cast<float*>(dst) + (size_t)tok * (size_t)s.ne[1] * ne0;
+        char* th = dst + i2 * sd.nb[2] + i3 * sd.nb[3];
         float2 v[ROPE_RT];
 #pragma unroll
         for (int u = 0; u < ROPE_RT; u++) {
@@ -468,7 +473,10 @@ __global__ void __launch_bounds__(256) rope_token_pairs_kernel(const char* __res
                 o.x = __fsub_rn(__fmul_rn(v[u].x, c), __fmul_rn(v[u].y, sv));
                 o.y = __fadd_rn(__fmul_rn(v[u].x, sv), __fmul_rn(v[u].y, c));
             }
-            *reinterpret_cast<float2*>(td + (size_t)(i >> half_shift) * ne0 + 2 * j) = o;
+            if constexpr (F16OUT)
+                *reinterpret_cast<__half2*>(th + (int64_t)(i >> half_shift) * sd.nb[1] + 4 * j) = __floats2half2_rn(o.x, o.y);
+            else
+                *reinterpret_cast<float2*>(td + (size_t)(i >> half_shift) * ne0 + 2 * j) = o;
         }
         __syncthreads();   // cs / sn are rewritten for the next token
     }
@@ -1007,9 +1015,10 @@ int b200_rope(const float* x, const int64_t ne[4], const size_t nb[4], const int
     if (mode == 0 && n_dims / 2 <= ROPE_MAX_HALF && pow2 && pairs8 && half * ne[1] <= 256 * ROPE_RT) {
         int shift = 0;
         while ((int64_t(1) << shift) < half) shift++;
-        return done(launch_pdl(rope_token_pairs_kernel, dim3((unsigned)std::min<int64_t>(ne[2] * ne[3], 148 * 8)),
+        return done(launch_pdl(rope_token_pairs_kernel<false>, dim3((unsigned)std::min<int64_t>(ne[2] * ne[3], 148 * 8)),
                                dim3(256), 0, static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x),
-                               shape_of(ne, nb), pos, n_dims, shift, theta_scale, freq_scale, attn_factor, dst));
+                               shape_of(ne, nb), pos, n_dims, shift, theta_scale, freq_scale, attn_factor,
+                               reinterpret_cast<char*>(dst), shape_of(ne, nb)));
     }
     if (n_dims / 2 <= ROPE_MAX_HALF)
         return done(launch_pdl(rope_token_kernel, dim3((unsigned)std::min<int64_t>(ne[2] * ne[3], 148 * 8)), dim3(256), 0,
@@ -1018,6 +1027,29 @@ int b200_rope(const float* x, const int64_t ne[4], const size_t nb[4], const int
     return done(launch_pdl(rope_kernel, dim3((unsigned)grid_for(n, 256)), dim3(256), 0,
                            static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x), shape_of(ne, nb), pos,
                            n_dims, mode == 2 ? 1 : 0, theta_scale, freq_scale, attn_factor, dst));
+}
+
+int b200_rope_f16(const float* x, const int64_t ne[4], const size_t nb[4], const int32_t* pos, int n_dims, int mode,
+                  float freq_base, float freq_scale, float attn_factor, void* dst, const size_t dnb[4], void* stream) {
+    using namespace b200;
+    if (!x || !pos || !dst || !shape_ok(ne, nb) || ne[0] % 2 != 0 || n_dims <= 0 || n_dims % 2 != 0 ||
+        n_dims > ne[0] || !(freq_base > 0.0f))
+        return B200_E_INVALID;
+    const int64_t half = ne[0] / 2;
+    const bool pow2 = half > 0 && (half & (half - 1)) == 0;
+    const bool pairs8 = nb[0] == 4 && nb[1] % 8 == 0 && nb[2] % 8 == 0 && nb[3] % 8 == 0 &&
+                        (reinterpret_cast<uintptr_t>(x) & 7u) == 0;
+    const bool out4 = dnb[0] == 2 && dnb[1] % 4 == 0 && dnb[2] % 4 == 0 && dnb[3] % 4 == 0 &&
+                      (reinterpret_cast<uintptr_t>(dst) & 3u) == 0;
+    if (mode != 0 || n_dims / 2 > ROPE_MAX_HALF || !pow2 || !pairs8 || !out4 || half * ne[1] > 256 * ROPE_RT)
+        return B200_E_UNSUPPORTED;   // the normal-mode pair kernel only
+    const float theta_scale = powf(freq_base, -2.0f / (float)n_dims);   // the host libm's, as ggml's
+    int shift = 0;
+    while ((int64_t(1) << shift) < half) shift++;
+    return done(launch_pdl(rope_token_pairs_kernel<true>, dim3((unsigned)std::min<int64_t>(ne[2] * ne[3], 148 * 8)),
+                           dim3(256), 0, static_cast<cudaStream_t>(stream), reinterpret_cast<const char*>(x),
+                           shape_of(ne, nb), pos, n_dims, shift, theta_scale, freq_scale, attn_factor,
+                           static_cast<char*>(dst), shape_of(ne, dnb)));
 }
 
 int b200_get_rows(int src_type, const void* src, const int64_t sne[4], const size_t snb[4], const int32_t* idx,

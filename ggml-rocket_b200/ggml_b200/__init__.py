@@ -248,6 +248,7 @@ _BACKEND_SIGS = {
     "b200_silu": (_int, [_vp, _vp, _vp, _vp, _vp]),
     "b200_swiglu": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "b200_rope": (_int, [_vp, _vp, _vp, _vp, _int, _int, _f, _f, _f, _vp, _vp]),
+    "b200_rope_f16": (_int, [_vp, _vp, _vp, _vp, _int, _int, _f, _f, _f, _vp, _vp, _vp]),
     "b200_get_rows": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "b200_cpy": (_int, [_int, _vp, _vp, _vp, _int, _vp, _vp, _vp, _vp]),
     "b200_soft_max": (_int, [_vp, _vp, _vp, _f, _vp, _vp]),

@@ -236,6 +236,13 @@ int b200_swiglu(const float * a, const size_t anb[4], const float * g, const siz
  * past n_dims are copied */
 int b200_rope(const float * x, const int64_t ne[4], const size_t nb[4], const int32_t * pos, int n_dims, int mode,
               float freq_base, float freq_scale, float attn_factor, float * dst, void * stream);
+/* The same ROPE (mode 0) with its output rounded to fp16 and stored at dst with byte strides dnb
+ * (dnb[0] == 2): the ROPE of K and the f32 -> f16 CPY of its result into the KV-cache view in one
+ * pass, bit-identical to b200_rope then b200_cpy. No counterpart in the reference (its host does
+ * both). Rows of 8-byte aligned pairs, head_dim a power of two, head_dim / 2 * n_head <= 2048, else
+ * B200_E_UNSUPPORTED. */
+int b200_rope_f16(const float * x, const int64_t ne[4], const size_t nb[4], const int32_t * pos, int n_dims, int mode,
+                  float freq_base, float freq_scale, float attn_factor, void * dst, const size_t dnb[4], void * stream);
 /* dst[:, i, j, k] = src[:, idx[i, j, k], j, k]; src f32 (0) or f16 (1), dst f32 [sne[0], ine[0],
  * ine[1], ine[2]]; an index outside src's rows records a device error and yields a zero row */
 int b200_get_rows(int src_type, const void * src, const int64_t sne[4], const size_t snb[4], const int32_t * idx,

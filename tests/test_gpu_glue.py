@@ -141,6 +141,38 @@ def test_rope_normal_mode_rows(cuda, T, H, pad, n_dims):
     assert np.array_equal(y.cpu().numpy()[..., n_dims:], x[..., n_dims:])
 
 
+@pytest.mark.parametrize("T,HK,n_kv,row0", [(512, 8, 1024, 512), (37, 2, 64, 3)])
+def test_rope_into_f16_cache_view(cuda, T, HK, n_kv, row0):
+    """ROPE of K written as fp16 straight into a KV-cache view (b200_rope_f16): bit-identical to
+    b200_rope followed by the f32 -> f16 CPY into the same view, and nothing outside the view
+    changes."""
+    import torch
+    import ggml_b200 as g
+    lib = g.lib()
+    D = 128
+    rng = np.random.default_rng(T + HK)
+    x = torch.from_numpy(rng.standard_normal((T, HK, D)).astype(np.float32)).cuda()
+    pos = torch.from_numpy(rng.integers(0, 8192, T).astype(np.int32)).cuda()
+    ne, nb = _shape(x)
+    # the cache: [n_kv rows of HK * D fp16]; the view: rows row0 .. row0 + T as [D, HK, T]
+    def cache():
+        return torch.from_numpy(rng.standard_normal((n_kv, HK * D)).astype(np.float16)).cuda()
+    fused = cache()
+    ref = fused.clone()
+    vnb = (ctypes.c_size_t * 4)(2, 2 * D, 2 * D * HK, 2 * D * HK * T)
+    base = lambda c: ctypes.c_void_p(c.data_ptr() + row0 * HK * D * 2)   # noqa: E731
+    assert lib.b200_rope_f16(_ptr(x), ne, nb, _ptr(pos), D, 0, 500000.0, 1.0, 1.0, base(fused), vnb, None) == 0
+    y = torch.empty_like(x)
+    assert lib.b200_rope(_ptr(x), ne, nb, _ptr(pos), D, 0, 500000.0, 1.0, 1.0, _ptr(y), None) == 0
+    vne = (ctypes.c_int64 * 4)(D, HK, T, 1)
+    assert lib.b200_cpy(0, _ptr(y), ne, nb, 1, base(ref), vne, vnb, None) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(fused.view(torch.int16), ref.view(torch.int16))
+    # neox mode is not the pair kernel's: refused, nothing written
+    assert lib.b200_rope_f16(_ptr(x), ne, nb, _ptr(pos), D, 2, 500000.0, 1.0, 1.0, base(fused), vnb, None) == \
+        g.B200_E_UNSUPPORTED
+
+
 def test_get_rows_and_cpy(cuda):
     import torch
     import ggml_b200 as g

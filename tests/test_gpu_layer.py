@@ -95,7 +95,7 @@ cos, bad = rk_compare(want, got)
 print("LAYER", rel_err(got, want), cos, bad)
 assert be.cpu_fallbacks() == 0 and be.device_errors() == 0
 print("ROUTES", be.route_ops("fa"), be.route_ops("glue"), be.route_ops(None), be.route_ops("fused"),
-      be.route_ops("swiglu_fused"), be.route_ops("norm_pack"))
+      be.route_ops("swiglu_fused"), be.route_ops("norm_pack"), be.route_ops("rope_cpy"))
 buf.free()
 be.close()
 """
@@ -110,8 +110,9 @@ def test_llama_layer_through_graph_compute(cuda):
     assert rel <= 1e-2, rel
     assert cos >= 0.999, cos
     assert bad == 0
-    fa, glue, total, groups, swiglu_fused, norm_pack = [int(v) for v in p.stdout.split("ROUTES")[1].split()[:6]]
+    fa, glue, total, groups, swiglu_fused, norm_pack, rope_cpy = [int(v) for v in
+                                                                  p.stdout.split("ROUTES")[1].split()[:7]]
     assert fa == 1 and glue >= 11
     # Q/K/V and gate/up each ran as one combined-N GEMM whose activation pack the norm in front of it
-    # made; SWIGLU ran inside the down projection's pack
-    assert groups == 2 and swiglu_fused == 1 and norm_pack == 2
+    # made; SWIGLU ran inside the down projection's pack; K's ROPE wrote the fp16 cache rows directly
+    assert groups == 2 and swiglu_fused == 1 and norm_pack == 2 and rope_cpy == 1
